@@ -1,0 +1,239 @@
+"""CPU oracle for rusty_whisper's quantized-matmul path (TEST INFRASTRUCTURE).
+
+ctypes front-end over ``oracle/_build/librwq_oracle.so`` (built from
+``oracle/rwq_oracle.cpp`` by ``oracle/build.sh``).  It restates the
+reference's Rust (``src/quant.rs``, ``src/model.rs``, ``src/tensor.rs``)
+and is pinned by the reference's own known-answer tests (see
+``tests/test_oracle_pins.py``).
+
+Only ``tests/``, ``__graft_entry__.smoke()`` and ``bench.py``'s CPU legs may
+import this package.  The product path (``rusty_whisper_b200``) never does.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "_build", "librwq_oracle.so")
+_lib = None
+
+QK = 32
+TIER_AUTO, TIER_VNNI, TIER_AVX2, TIER_F32 = 0, 1, 2, 3
+TIER_NAMES = {1: "avx512-vnni", 2: "avx2", 3: "f32-fallback"}
+
+
+def build() -> str:
+    """Compile the oracle library (g++, -ffp-contract=off)."""
+    subprocess.check_call(["sh", os.path.join(_HERE, "build.sh")])
+    return LIB_PATH
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            build()
+        L = ctypes.CDLL(LIB_PATH)
+        P = ctypes.c_void_p
+        i32, u32, sz, f32 = ctypes.c_int, ctypes.c_uint32, ctypes.c_size_t, ctypes.c_float
+        sig = {
+            "orc_f16_to_f32": (f32, [ctypes.c_uint16]),
+            "orc_f32_to_f16": (ctypes.c_uint16, [f32]),
+            "orc_block_bytes": (i32, [i32]),
+            "orc_has_avx2": (i32, []),
+            "orc_has_vnni": (i32, []),
+            "orc_default_threads": (i32, []),
+            "orc_dispatch_tier": (i32, []),
+            "orc_unpack_block": (i32, [i32, P, P, P, P]),
+            "orc_dequant_row_scalar": (i32, [i32, P, sz, P]),
+            "orc_dequant_row_avx2": (i32, [i32, P, sz, P]),
+            "orc_quantize_acts_i8": (i32, [P, i32, i32, P, P, P]),
+            "orc_block_dots": (i32, [P, i32, i32, i32, P, i32, P]),
+            "orc_int8_scalar_matmul": (i32, [P, i32, i32, i32, P, i32, P]),
+            "orc_matmul_t_q": (i32, [P, i32, i32, i32, P, i32, P, i32, i32, i32]),
+            "orc_matmul_t": (i32, [P, i32, i32, P, i32, P, i32]),
+            "orc_to_dense": (i32, [i32, P, i32, i32, P]),
+            "orc_test_matrix": (None, [i32, i32, u32, P]),
+            "orc_rand_bytes": (None, [u32, sz, P]),
+            "orc_quantize_q8_0": (None, [P, sz, P]),
+            "orc_quantize_q5_1": (None, [P, sz, P]),
+            "orc_qtensor_new": (P, [i32, P, i32, i32]),
+            "orc_qtensor_free": (None, [P]),
+            "orc_qtensor_matmul": (i32, [P, P, i32, P, i32, i32]),
+        }
+        for name, (res, args) in sig.items():
+            fn = getattr(L, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = L
+    return _lib
+
+
+def _p(a: np.ndarray):
+    assert a.flags["C_CONTIGUOUS"]
+    return a.ctypes.data_as(ctypes.c_void_p)
+
+
+def _check(rc: int, what: str):
+    if rc != 0:
+        raise RuntimeError(f"oracle {what} failed with status {rc}")
+
+
+# ------------------------------------------------------------------ scalars
+def f16_to_f32(h: int) -> float:
+    return lib().orc_f16_to_f32(h)
+
+
+def f32_to_f16(x: float) -> int:
+    return lib().orc_f32_to_f16(x)
+
+
+def block_bytes(dtype: int) -> int:
+    return lib().orc_block_bytes(dtype)
+
+
+def dispatch_tier() -> int:
+    return lib().orc_dispatch_tier()
+
+
+def default_threads() -> int:
+    return lib().orc_default_threads()
+
+
+# ------------------------------------------------------------------ blocks
+def unpack_block(dtype: int, block: bytes):
+    b = np.frombuffer(bytes(block), dtype=np.uint8).copy()
+    q = np.zeros(QK, np.int8)
+    d = np.zeros(1, np.float32)
+    m = np.zeros(1, np.float32)
+    _check(lib().orc_unpack_block(dtype, _p(b), _p(q), _p(d), _p(m)), "unpack_block")
+    return q, float(d[0]), float(m[0])
+
+
+def dequant_row_scalar(dtype: int, raw: np.ndarray) -> np.ndarray:
+    raw = np.ascontiguousarray(raw, np.uint8)
+    nbl = raw.size // block_bytes(dtype)
+    out = np.zeros(nbl * QK, np.float32)
+    _check(lib().orc_dequant_row_scalar(dtype, _p(raw), nbl, _p(out)), "dequant_row_scalar")
+    return out
+
+
+def dequant_row_avx2(dtype: int, raw: np.ndarray) -> np.ndarray:
+    raw = np.ascontiguousarray(raw, np.uint8)
+    nbl = raw.size // block_bytes(dtype)
+    out = np.zeros(nbl * QK, np.float32)
+    _check(lib().orc_dequant_row_avx2(dtype, _p(raw), nbl, _p(out)), "dequant_row_avx2")
+    return out
+
+
+def to_dense(dtype: int, raw: np.ndarray, n: int, k: int) -> np.ndarray:
+    raw = np.ascontiguousarray(raw, np.uint8)
+    out = np.zeros((n, k), np.float32)
+    _check(lib().orc_to_dense(dtype, _p(raw), n, k, _p(out)), "to_dense")
+    return out
+
+
+# ------------------------------------------------------------- activations
+def quantize_acts_i8(a: np.ndarray):
+    a = np.ascontiguousarray(a, np.float32)
+    m, k = a.shape
+    nb = k // QK
+    q = np.zeros((m, k), np.int8)
+    d = np.zeros((m, nb), np.float32)
+    s = np.zeros((m, nb), np.int32)
+    _check(lib().orc_quantize_acts_i8(_p(a), m, k, _p(q), _p(d), _p(s)), "quantize_acts_i8")
+    return q, d, s
+
+
+def block_dots(qa: np.ndarray, dtype: int, raw: np.ndarray, n: int) -> np.ndarray:
+    qa = np.ascontiguousarray(qa, np.int8)
+    raw = np.ascontiguousarray(raw, np.uint8)
+    m, k = qa.shape
+    S = np.zeros((m, n, k // QK), np.int32)
+    _check(lib().orc_block_dots(_p(qa), m, k, dtype, _p(raw), n, _p(S)), "block_dots")
+    return S
+
+
+# ---------------------------------------------------------------- matmuls
+def int8_scalar_matmul(a: np.ndarray, dtype: int, raw: np.ndarray, n: int) -> np.ndarray:
+    a = np.ascontiguousarray(a, np.float32)
+    raw = np.ascontiguousarray(raw, np.uint8)
+    m, k = a.shape
+    out = np.zeros((m, n), np.float32)
+    _check(lib().orc_int8_scalar_matmul(_p(a), m, k, dtype, _p(raw), n, _p(out)), "int8_scalar_matmul")
+    return out
+
+
+def matmul_t_q(a: np.ndarray, dtype: int, raw: np.ndarray, n: int, tier: int = TIER_AUTO,
+               threads: int = 0, packed: bool = False) -> np.ndarray:
+    a = np.ascontiguousarray(a, np.float32)
+    raw = np.ascontiguousarray(raw, np.uint8)
+    m, k = a.shape
+    out = np.zeros((m, n), np.float32)
+    _check(lib().orc_matmul_t_q(_p(a), m, k, dtype, _p(raw), n, _p(out), tier, threads, int(packed)),
+           "matmul_t_q")
+    return out
+
+
+def matmul_t(a: np.ndarray, b: np.ndarray, threads: int = 0) -> np.ndarray:
+    a = np.ascontiguousarray(a, np.float32)
+    b = np.ascontiguousarray(b, np.float32)
+    m, k = a.shape
+    n = b.shape[0]
+    out = np.zeros((m, n), np.float32)
+    _check(lib().orc_matmul_t(_p(a), m, k, _p(b), n, _p(out), threads), "matmul_t")
+    return out
+
+
+class QTensor:
+    """Persistent weight with the reference's call-count gated int8 cache."""
+
+    def __init__(self, dtype: int, raw: np.ndarray, n: int, k: int):
+        self._raw = np.ascontiguousarray(raw, np.uint8)
+        self.dtype, self.n, self.k = dtype, n, k
+        self._h = lib().orc_qtensor_new(dtype, _p(self._raw), n, k)
+        if not self._h:
+            raise ValueError("bad qtensor")
+
+    def matmul(self, a: np.ndarray, tier: int = TIER_AUTO, threads: int = 0, out=None) -> np.ndarray:
+        a = np.ascontiguousarray(a, np.float32)
+        if out is None:
+            out = np.zeros((a.shape[0], self.n), np.float32)
+        _check(lib().orc_qtensor_matmul(self._h, _p(a), a.shape[0], _p(out), tier, threads), "qtensor_matmul")
+        return out
+
+    def __del__(self):
+        if getattr(self, "_h", None):
+            lib().orc_qtensor_free(self._h)
+            self._h = None
+
+
+# ------------------------------------------------------ reference test data
+def test_matrix(n: int, k: int, seed: int) -> np.ndarray:
+    out = np.zeros(n * k, np.float32)
+    lib().orc_test_matrix(n, k, seed, _p(out))
+    return out
+
+
+def rand_bytes(seed: int, count: int) -> np.ndarray:
+    out = np.zeros(count, np.uint8)
+    lib().orc_rand_bytes(seed, count, _p(out))
+    return out
+
+
+def quantize_q8_0(x: np.ndarray) -> np.ndarray:
+    x = np.ascontiguousarray(x, np.float32).ravel()
+    out = np.zeros(x.size // QK * 34, np.uint8)
+    lib().orc_quantize_q8_0(_p(x), x.size, _p(out))
+    return out
+
+
+def quantize_q5_1(x: np.ndarray) -> np.ndarray:
+    x = np.ascontiguousarray(x, np.float32).ravel()
+    out = np.zeros(x.size // QK * 24, np.uint8)
+    lib().orc_quantize_q5_1(_p(x), x.size, _p(out))
+    return out
