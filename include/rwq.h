@@ -1,0 +1,123 @@
+/*
+ * rwq.h -- C ABI of the B200 (sm_100a) quantized-matmul path that replaces
+ * rusty_whisper's `quant::matmul_t_q` / `quant::linear_w`.
+ *
+ * Conventions (mirroring the crate's only C-ABI precedent, src/wasm.rs:25-111):
+ *   - every entry point returns an int status: RWQ_OK (0) or a negative code;
+ *   - the text of the last error is kept per host thread (rwq_last_error);
+ *   - nothing aborts: bad shapes, bad dtypes and CUDA failures are statuses.
+ * Matrices are row-major f32; a weight is ggml blocks, row-major [n][k/32]
+ * (quant.rs:493-498), passed as the raw bytes a ggml/gguf loader holds.
+ * `stream` is a cudaStream_t (NULL = the legacy default stream).  Calls on
+ * one weight from several host threads are safe; calls that share a stream
+ * are ordered by it.
+ */
+#ifndef RWQ_H
+#define RWQ_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+    RWQ_OK = 0,
+    RWQ_ERR_ARG = -1,     /* null pointer, negative size, k % 32 != 0, ... */
+    RWQ_ERR_DTYPE = -2,   /* not one of Q4_0/Q4_1/Q5_0/Q5_1/Q8_0 */
+    RWQ_ERR_SHAPE = -3,   /* inner dimensions disagree */
+    RWQ_ERR_CUDA = -4,    /* a CUDA call failed; see rwq_last_error() */
+    RWQ_ERR_NOMEM = -5,   /* device or pinned allocation failed */
+    RWQ_ERR_DEVICE = -6,  /* kernel reported a fault (bounded wait expired) */
+    RWQ_ERR_NOGPU = -7    /* no usable sm_100 device */
+};
+
+/* ggml type codes (quant.rs:43-52). */
+enum { RWQ_Q4_0 = 2, RWQ_Q4_1 = 3, RWQ_Q5_0 = 6, RWQ_Q5_1 = 7, RWQ_Q8_0 = 8 };
+
+/* Arithmetic of a matmul:
+ *   RWQ_MODE_INT8: activations quantized per 32-block to int8 and integer
+ *     block dots, the tier rusty_whisper runs on every AVX2/VNNI host
+ *     (quant.rs:763-994).
+ *   RWQ_MODE_F32: weights dequantized, f32 dot with unquantized
+ *     activations, the reference's f32 fallback (quant.rs:995-1018). */
+enum { RWQ_MODE_INT8 = 0, RWQ_MODE_F32 = 1 };
+
+typedef struct rwq_qtensor rwq_qtensor;
+
+/* Bytes per 32-element block, or RWQ_ERR_DTYPE.  Replaces
+ * `quant::block_bytes` (quant.rs:43). */
+int rwq_block_bytes(int dtype);
+
+/* Text of the last failure on this host thread ("" if none).  Mirrors the
+ * thread-local error text of wasm.rs:18-21. */
+const char* rwq_last_error(void);
+
+/* Select the CUDA device for this host thread and check it is sm_100. */
+int rwq_init(int device);
+
+/* Upload an [n, k] ggml weight to the current device.  `raw` holds
+ * n * (k/32) * rwq_block_bytes(dtype) bytes (host memory).  Replaces
+ * `QTensor::new(shape, dtype, raw)` (quant.rs:553). */
+int rwq_qtensor_new(const uint8_t* raw, size_t raw_len, int dtype, int64_t n, int64_t k, rwq_qtensor** out);
+
+/* Same, from device memory already holding the raw blocks (e.g. a loader
+ * that copied the file to the GPU). */
+int rwq_qtensor_new_device(const void* raw_dev, size_t raw_len, int dtype, int64_t n, int64_t k, void* stream,
+                           rwq_qtensor** out);
+
+int rwq_qtensor_free(rwq_qtensor* t);
+int rwq_qtensor_shape(const rwq_qtensor* t, int* dtype, int64_t* n, int64_t* k);
+
+/* Build the tensor-core operand cache now rather than on the first
+ * GEMM-sized call (the reference builds its int8 cache on the second call,
+ * quant.rs:778-786). */
+int rwq_qtensor_prepare_gemm(rwq_qtensor* t, void* stream);
+
+/* C[m, n] = A[m, k] * dequant(B)^T (+ bias), host buffers: copies in,
+ * computes, copies out, synchronizes.  Keeps the signature and ownership
+ * of `matmul_t_q(a: &Tensor, b: &QTensor) -> Tensor` (quant.rs:754) and,
+ * with `bias`, of `linear_w` (quant.rs:1054).  `bias` may be NULL. */
+int rwq_matmul_t_q(const float* a, int64_t m, int64_t k, const rwq_qtensor* b, const float* bias, float* out,
+                   int mode);
+
+/* Device-pointer variant, asynchronous on `stream`: the perf path.
+ * `a`, `bias`, `out` are device pointers.  Scratch comes from a
+ * per-(device, stream) workspace owned by the library. */
+int rwq_matmul_t_q_dev(const float* a, int64_t m, int64_t k, const rwq_qtensor* b, const float* bias, float* out,
+                       int mode, void* stream);
+
+/* Dequantize rows `rows[0..nrows)` (device int32 indices; NULL = rows
+ * 0..nrows-1) into out[nrows, k] (device), bit-identical to the
+ * reference's scalar dequant.  Replaces `QTensor::row_f32` (quant.rs:566)
+ * and, with rows = NULL and nrows = n, `to_dense` (quant.rs:572). */
+int rwq_dequant_rows_dev(const rwq_qtensor* t, const int32_t* rows, int64_t nrows, float* out, void* stream);
+
+/* Host-buffer gather of one row, `QTensor::row_f32` (quant.rs:566). */
+int rwq_row_f32(const rwq_qtensor* t, int64_t row, float* out);
+
+/* The int8 activation quantizer, `quantize_acts_i8` (quant.rs:690-716):
+ * q[m, k] int8, d[m, k/32] f32, sum[m, k/32] int32; device pointers. */
+int rwq_quantize_acts_dev(const float* a, int64_t m, int64_t k, int8_t* q, float* d, int32_t* sum, void* stream);
+
+/* Per-block integer dots S[m][n][k/32] = sum q_a * q_b (centred weight
+ * codes) from already-quantized activations (device pointers).  `path`
+ * 0 = the CUDA-core dp4a core used by the GEMV, 1 = the tensor-core GEMM
+ * (values read back from tensor memory).  For bit-exact tests of the
+ * integer core; no reference counterpart beyond quant.rs:1352-1360. */
+int rwq_block_dots_dev(const float* a, int64_t m, int64_t k, const rwq_qtensor* b, int32_t* S, int path,
+                       void* stream);
+
+/* Force the kernel family for matmuls with m > 8 (testing and
+ * benchmarking): 0 = automatic, 1 = CUDA-core GEMV kernel in row chunks,
+ * 2 = tensor-core GEMM.  Applies to this host thread. */
+int rwq_set_gemm_path(int path);
+
+/* Synchronize `stream` and report any fault a kernel recorded on it. */
+int rwq_stream_check(void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* RWQ_H */

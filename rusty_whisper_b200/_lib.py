@@ -1,0 +1,73 @@
+"""ctypes binding of ``librwq.so`` (the C ABI declared in include/rwq.h).
+
+The library is built in-tree (``python -m rusty_whisper_b200.build``).  If
+it is missing this module raises: there is no CPU or eager fallback.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+_PKG = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_PKG, "librwq.so")
+
+RWQ_OK = 0
+RWQ_ERR_ARG, RWQ_ERR_DTYPE, RWQ_ERR_SHAPE, RWQ_ERR_CUDA = -1, -2, -3, -4
+RWQ_ERR_NOMEM, RWQ_ERR_DEVICE, RWQ_ERR_NOGPU = -5, -6, -7
+MODE_INT8, MODE_F32 = 0, 1
+
+# Every symbol include/rwq.h declares, with its ctypes signature.
+_P = ctypes.c_void_p
+_I = ctypes.c_int
+_L = ctypes.c_int64
+_SZ = ctypes.c_size_t
+SIGNATURES = {
+    "rwq_block_bytes": (_I, [_I]),
+    "rwq_last_error": (ctypes.c_char_p, []),
+    "rwq_init": (_I, [_I]),
+    "rwq_qtensor_new": (_I, [_P, _SZ, _I, _L, _L, ctypes.POINTER(_P)]),
+    "rwq_qtensor_new_device": (_I, [_P, _SZ, _I, _L, _L, _P, ctypes.POINTER(_P)]),
+    "rwq_qtensor_free": (_I, [_P]),
+    "rwq_qtensor_shape": (_I, [_P, ctypes.POINTER(_I), ctypes.POINTER(_L), ctypes.POINTER(_L)]),
+    "rwq_qtensor_prepare_gemm": (_I, [_P, _P]),
+    "rwq_matmul_t_q": (_I, [_P, _L, _L, _P, _P, _P, _I]),
+    "rwq_matmul_t_q_dev": (_I, [_P, _L, _L, _P, _P, _P, _I, _P]),
+    "rwq_dequant_rows_dev": (_I, [_P, _P, _L, _P, _P]),
+    "rwq_row_f32": (_I, [_P, _L, _P]),
+    "rwq_quantize_acts_dev": (_I, [_P, _L, _L, _P, _P, _P, _P]),
+    "rwq_block_dots_dev": (_I, [_P, _L, _L, _P, _P, _I, _P]),
+    "rwq_set_gemm_path": (_I, [_I]),
+    "rwq_stream_check": (_I, [_P]),
+}
+
+_lib = None
+
+
+class RwqError(RuntimeError):
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"rwq status {code}: {msg}")
+        self.code = code
+
+
+def lib() -> ctypes.CDLL:
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise ImportError(f"{LIB_PATH} is missing: build it with `python -m rusty_whisper_b200.build`")
+        L = ctypes.CDLL(LIB_PATH)
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(L, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = L
+    return _lib
+
+
+def check(rc: int) -> None:
+    if rc != RWQ_OK:
+        msg = lib().rwq_last_error().decode(errors="replace")
+        if rc in (RWQ_ERR_ARG, RWQ_ERR_SHAPE):
+            raise ValueError(f"rwq status {rc}: {msg}")
+        if rc == RWQ_ERR_DTYPE:
+            raise ValueError(f"rwq status {rc}: {msg}")
+        raise RwqError(rc, msg)

@@ -1,0 +1,471 @@
+// rwq_api.cu -- the C ABI (include/rwq.h): weight objects, per-stream
+// scratch workspaces, argument checking and kernel dispatch.
+//
+// Dispatch of a matmul (quant.rs:754-1051 restated for the GPU):
+//   mode INT8 (the reference's tier on every x86 host):
+//     quantize activations (one launch), then
+//       m <= 8  -> GEMV kernel (decoder shapes; CUDA cores, HBM-bound)
+//       m >  8  -> tcgen05 GEMM (encoder shapes)
+//   mode F32 (the reference's f32 fallback): dequant-then-f32 GEMV kernel
+//     over row chunks of 8.
+#include <cuda_runtime.h>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <mutex>
+#include <string>
+#include <utility>
+#include "../../include/rwq.h"
+#include "rwq_common.cuh"
+#include "rwq_internal.h"
+
+struct rwq_qtensor {
+    rwq::Weight w;
+    std::mutex mu;
+};
+
+namespace {
+
+thread_local std::string t_err;
+thread_local int t_gemm_path = 0;
+
+int fail(int code, const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    t_err = buf;
+    return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+    return fail(e == cudaErrorMemoryAllocation ? RWQ_ERR_NOMEM : RWQ_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+#define RWQ_CUDA(call, what)                       \
+    do {                                           \
+        cudaError_t e_ = (call);                   \
+        if (e_ != cudaSuccess) return cuda_fail(e_, what); \
+    } while (0)
+
+bool valid_dtype(int dt) { return rwq::block_bytes(dt) > 0; }
+
+size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+// Scratch arena for one (device, stream): grown on demand, never shrunk.
+struct Workspace {
+    std::mutex mu;
+    void* buf = nullptr;
+    size_t cap = 0;
+    int* err = nullptr;  // device-side fault code written by kernels
+};
+
+std::mutex g_ws_mu;
+std::map<std::pair<int, cudaStream_t>, Workspace*> g_ws;
+
+int get_workspace(cudaStream_t s, Workspace** out) {
+    int dev = 0;
+    RWQ_CUDA(cudaGetDevice(&dev), "cudaGetDevice");
+    std::lock_guard<std::mutex> g(g_ws_mu);
+    auto& w = g_ws[{dev, s}];
+    if (!w) {
+        auto* nw = new Workspace;
+        cudaError_t e = cudaMalloc(&nw->err, sizeof(int));
+        if (e != cudaSuccess) {
+            delete nw;
+            return cuda_fail(e, "cudaMalloc(error flag)");
+        }
+        e = cudaMemset(nw->err, 0, sizeof(int));
+        if (e != cudaSuccess) return cuda_fail(e, "cudaMemset(error flag)");
+        w = nw;
+    }
+    *out = w;
+    return RWQ_OK;
+}
+
+int ensure_cap(Workspace* ws, size_t bytes) {
+    if (ws->cap >= bytes) return RWQ_OK;
+    if (ws->buf) {
+        RWQ_CUDA(cudaFree(ws->buf), "cudaFree(workspace)");  // implicit device sync
+        ws->buf = nullptr;
+        ws->cap = 0;
+    }
+    const size_t want = align_up(bytes + bytes / 4, 1 << 20);
+    RWQ_CUDA(cudaMalloc(&ws->buf, want), "cudaMalloc(workspace)");
+    ws->cap = want;
+    return RWQ_OK;
+}
+
+// Carve an activation view out of the arena starting at `base`.
+size_t acts_layout(int m, int k, bool gemm, rwq::ActsView* v, uint8_t* base) {
+    const int nb = k / rwq::QK;
+    const int m_pad = (m + 127) / 128 * 128;
+    size_t off = 0;
+    auto take = [&](size_t bytes) {
+        uint8_t* p = base ? base + off : nullptr;
+        off = align_up(off + bytes, 256);
+        return p;
+    };
+    v->m = m;
+    v->k = k;
+    v->nb = nb;
+    v->m_pad = m_pad;
+    v->q8 = reinterpret_cast<int8_t*>(take(size_t(m) * k));
+    v->d = reinterpret_cast<float*>(take(size_t(m) * nb * 4));
+    v->sum = reinterpret_cast<int32_t*>(take(size_t(m) * nb * 4));
+    v->u = reinterpret_cast<float*>(take(size_t(m) * nb * 4));
+    if (gemm) {
+        v->q16 = reinterpret_cast<uint16_t*>(take(size_t(m) * k * 2));
+        v->dT = reinterpret_cast<float*>(take(size_t(nb) * m_pad * 4));
+        v->uT = reinterpret_cast<float*>(take(size_t(nb) * m_pad * 4));
+    } else {
+        v->q16 = nullptr;
+        v->dT = v->uT = nullptr;
+    }
+    return off;
+}
+
+int weight_gemm_cache(rwq_qtensor* t, cudaStream_t s) {
+    std::lock_guard<std::mutex> g(t->mu);
+    rwq::Weight& w = t->w;
+    if (w.gemm_ready) return RWQ_OK;
+    w.n_pad = (w.n + 127) / 128 * 128;
+    RWQ_CUDA(cudaMalloc(&w.q16, size_t(w.n) * w.k * 2 + 16), "cudaMalloc(q16)");
+    RWQ_CUDA(cudaMalloc(&w.dT, size_t(w.nb) * w.n_pad * 4), "cudaMalloc(dT)");
+    if (rwq::has_min(w.dtype)) RWQ_CUDA(cudaMalloc(&w.mT, size_t(w.nb) * w.n_pad * 4), "cudaMalloc(mT)");
+    RWQ_CUDA(rwq::launch_build_gemm_cache(w, s), "build gemm cache");
+    // Other streams may use the cache next: finish building it here.
+    RWQ_CUDA(cudaStreamSynchronize(s), "cudaStreamSynchronize(gemm cache)");
+    w.gemm_ready = true;
+    return RWQ_OK;
+}
+
+int check_matmul_args(const float* a, int64_t m, int64_t k, const rwq_qtensor* b, const float* out, int mode) {
+    if (!b) return fail(RWQ_ERR_ARG, "weight is null");
+    if (m < 0 || k <= 0) return fail(RWQ_ERR_ARG, "bad shape m=%lld k=%lld", (long long)m, (long long)k);
+    if (k != b->w.k) return fail(RWQ_ERR_SHAPE, "matmul_t_q inner dims: %lld vs %d", (long long)k, b->w.k);
+    if (k % rwq::QK) return fail(RWQ_ERR_ARG, "k must be a multiple of 32 (k=%lld)", (long long)k);
+    if (m > (int64_t(1) << 31) / 2) return fail(RWQ_ERR_ARG, "m too large (%lld)", (long long)m);
+    if (mode != RWQ_MODE_INT8 && mode != RWQ_MODE_F32) return fail(RWQ_ERR_ARG, "unknown mode %d", mode);
+    if (m > 0 && (!a || (!out && b->w.n > 0))) return fail(RWQ_ERR_ARG, "null activation or output pointer");
+    return RWQ_OK;
+}
+
+int read_device_error(Workspace* ws, cudaStream_t s) {
+    int code = 0;
+    RWQ_CUDA(cudaMemcpyAsync(&code, ws->err, sizeof(int), cudaMemcpyDeviceToHost, s), "read error flag");
+    RWQ_CUDA(cudaStreamSynchronize(s), "cudaStreamSynchronize");
+    if (code) {
+        cudaMemsetAsync(ws->err, 0, sizeof(int), s);
+        return fail(RWQ_ERR_DEVICE, "GEMM kernel stopped: bounded wait expired (role %d)", code);
+    }
+    return RWQ_OK;
+}
+
+// The core device-pointer matmul.  `S_dump` (tests) routes through the
+// GEMM and makes it write the per-block integer dots.
+int matmul_dev_impl(const float* a, int64_t m, int64_t k, rwq_qtensor* b, const float* bias, float* out, int mode,
+                    cudaStream_t s, int32_t* S_dump, int force_path) {
+    int rc = check_matmul_args(a, m, k, b, out, mode);
+    if (rc) return rc;
+    if (m == 0 || b->w.n == 0) return RWQ_OK;
+    const rwq::Weight& w = b->w;
+    if (mode == RWQ_MODE_F32) {
+        for (int64_t m0 = 0; m0 < m; m0 += rwq::GEMV_MAX_M) {
+            const int mc = int(m - m0 < rwq::GEMV_MAX_M ? m - m0 : rwq::GEMV_MAX_M);
+            RWQ_CUDA(rwq::launch_gemv_f32(a + m0 * k, mc, w, bias, out + m0 * w.n, s), "gemv_f32 launch");
+        }
+        return RWQ_OK;
+    }
+    int path = force_path ? force_path : t_gemm_path;
+    if (path == 0) path = (m <= rwq::GEMV_MAX_M) ? 1 : 2;
+    const bool gemm = path == 2;
+    if (gemm && (k * 2) % 16) return fail(RWQ_ERR_ARG, "k*2 bytes must be a multiple of 16 for the GEMM");
+    Workspace* ws = nullptr;
+    if ((rc = get_workspace(s, &ws))) return rc;
+    std::lock_guard<std::mutex> g(ws->mu);
+    rwq::ActsView v;
+    const size_t need = acts_layout(int(m), int(k), gemm, &v, nullptr);
+    if ((rc = ensure_cap(ws, need))) return rc;
+    acts_layout(int(m), int(k), gemm, &v, static_cast<uint8_t*>(ws->buf));
+    RWQ_CUDA(rwq::launch_quantize_acts(a, v, gemm, s), "quantize launch");
+    if (!gemm) {
+        const size_t smem = size_t(rwq::GEMV_MAX_M) * k + size_t(rwq::GEMV_MAX_M) * (k / 32) * 12;
+        if (smem > 200 * 1024) return fail(RWQ_ERR_ARG, "k=%lld too large for the GEMV kernel", (long long)k);
+        for (int64_t m0 = 0; m0 < m; m0 += rwq::GEMV_MAX_M) {
+            rwq::ActsView c = v;
+            c.m = int(m - m0 < rwq::GEMV_MAX_M ? m - m0 : rwq::GEMV_MAX_M);
+            c.q8 = v.q8 + m0 * k;
+            c.d = v.d + m0 * v.nb;
+            c.sum = v.sum + m0 * v.nb;
+            c.u = v.u + m0 * v.nb;
+            RWQ_CUDA(rwq::launch_gemv_i8(c, w, bias, out + m0 * w.n, s), "gemv_i8 launch");
+        }
+        return RWQ_OK;
+    }
+    if ((rc = weight_gemm_cache(b, s))) return rc;
+    char why[256] = {0};
+    cudaError_t e = rwq::launch_gemm_tc(v, w, bias, out, S_dump, ws->err, s, why, sizeof why);
+    if (e != cudaSuccess) return fail(RWQ_ERR_CUDA, "gemm launch: %s %s", cudaGetErrorString(e), why);
+    return RWQ_OK;
+}
+
+cudaStream_t thread_stream() {
+    // One non-blocking stream per (host thread, device) for the
+    // host-buffer entry points.
+    thread_local std::map<int, cudaStream_t> streams;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    auto it = streams.find(dev);
+    if (it != streams.end()) return it->second;
+    cudaStream_t s = nullptr;
+    cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking);
+    streams[dev] = s;
+    return s;
+}
+
+}  // namespace
+
+extern "C" {
+
+int rwq_block_bytes(int dtype) {
+    const int bb = rwq::block_bytes(dtype);
+    return bb > 0 ? bb : fail(RWQ_ERR_DTYPE, "unsupported quantized dtype %d", dtype);
+}
+
+const char* rwq_last_error(void) { return t_err.c_str(); }
+
+int rwq_init(int device) {
+    int count = 0;
+    if (cudaGetDeviceCount(&count) != cudaSuccess || count == 0) return fail(RWQ_ERR_NOGPU, "no CUDA device");
+    if (device < 0 || device >= count) return fail(RWQ_ERR_ARG, "device %d out of range (%d devices)", device, count);
+    RWQ_CUDA(cudaSetDevice(device), "cudaSetDevice");
+    cudaDeviceProp p;
+    RWQ_CUDA(cudaGetDeviceProperties(&p, device), "cudaGetDeviceProperties");
+    if (p.major != 10) return fail(RWQ_ERR_NOGPU, "device %d is sm_%d%d, this build targets sm_100a", device, p.major, p.minor);
+    return RWQ_OK;
+}
+
+static int qtensor_new_impl(const void* raw, bool raw_on_device, size_t raw_len, int dtype, int64_t n, int64_t k,
+                            cudaStream_t s, rwq_qtensor** out) {
+    if (!out) return fail(RWQ_ERR_ARG, "out is null");
+    *out = nullptr;
+    if (!valid_dtype(dtype)) return fail(RWQ_ERR_DTYPE, "unsupported quantized dtype %d", dtype);
+    if (n < 0 || k <= 0 || k % rwq::QK) return fail(RWQ_ERR_ARG, "bad weight shape [%lld, %lld] (k %% 32 must be 0)",
+                                                   (long long)n, (long long)k);
+    if (n > INT32_MAX || k > INT32_MAX) return fail(RWQ_ERR_ARG, "weight too large");
+    const size_t nb = size_t(k) / rwq::QK, nblk = size_t(n) * nb;
+    const size_t want = nblk * size_t(rwq::block_bytes(dtype));
+    if (raw_len != want) return fail(RWQ_ERR_ARG, "raw length %zu != %zu for [%lld, %lld] dtype %d", raw_len, want,
+                                     (long long)n, (long long)k, dtype);
+    if (nblk && !raw) return fail(RWQ_ERR_ARG, "raw is null");
+    auto* t = new rwq_qtensor;
+    rwq::Weight& w = t->w;
+    w.dtype = dtype;
+    w.n = int(n);
+    w.k = int(k);
+    w.nb = int(nb);
+    cudaGetDevice(&w.device);
+    auto cleanup = [&](int rc) {
+        rwq_qtensor_free(t);
+        return rc;
+    };
+    cudaError_t e;
+    const size_t nalloc = nblk ? nblk : 1;
+    if ((e = cudaMalloc(&w.qs, nalloc * rwq::qs_bytes(dtype))) != cudaSuccess) return cleanup(cuda_fail(e, "cudaMalloc(qs)"));
+    if ((e = cudaMalloc(&w.d, nalloc * 2)) != cudaSuccess) return cleanup(cuda_fail(e, "cudaMalloc(d)"));
+    if (rwq::has_min(dtype) && (e = cudaMalloc(&w.m, nalloc * 2)) != cudaSuccess)
+        return cleanup(cuda_fail(e, "cudaMalloc(m)"));
+    if (rwq::has_qh(dtype) && (e = cudaMalloc(&w.qh, nalloc * 4)) != cudaSuccess)
+        return cleanup(cuda_fail(e, "cudaMalloc(qh)"));
+    if (nblk) {
+        const uint8_t* src = static_cast<const uint8_t*>(raw);
+        uint8_t* tmp = nullptr;
+        if (!raw_on_device) {
+            if ((e = cudaMalloc(&tmp, raw_len)) != cudaSuccess) return cleanup(cuda_fail(e, "cudaMalloc(raw)"));
+            if ((e = cudaMemcpyAsync(tmp, raw, raw_len, cudaMemcpyHostToDevice, s)) != cudaSuccess) {
+                cudaFree(tmp);
+                return cleanup(cuda_fail(e, "copy raw blocks"));
+            }
+            src = tmp;
+        }
+        e = rwq::launch_repack(src, w, s);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+        if (tmp) cudaFree(tmp);
+        if (e != cudaSuccess) return cleanup(cuda_fail(e, "repack"));
+    }
+    *out = t;
+    return RWQ_OK;
+}
+
+int rwq_qtensor_new(const uint8_t* raw, size_t raw_len, int dtype, int64_t n, int64_t k, rwq_qtensor** out) {
+    return qtensor_new_impl(raw, false, raw_len, dtype, n, k, thread_stream(), out);
+}
+
+int rwq_qtensor_new_device(const void* raw_dev, size_t raw_len, int dtype, int64_t n, int64_t k, void* stream,
+                           rwq_qtensor** out) {
+    return qtensor_new_impl(raw_dev, true, raw_len, dtype, n, k, static_cast<cudaStream_t>(stream), out);
+}
+
+int rwq_qtensor_free(rwq_qtensor* t) {
+    if (!t) return RWQ_OK;
+    rwq::Weight& w = t->w;
+    int prev = 0;
+    cudaGetDevice(&prev);
+    if (prev != w.device) cudaSetDevice(w.device);
+    cudaFree(w.qs);
+    cudaFree(w.qh);
+    cudaFree(w.d);
+    cudaFree(w.m);
+    cudaFree(w.q16);
+    cudaFree(w.dT);
+    cudaFree(w.mT);
+    if (prev != w.device) cudaSetDevice(prev);
+    delete t;
+    return RWQ_OK;
+}
+
+int rwq_qtensor_shape(const rwq_qtensor* t, int* dtype, int64_t* n, int64_t* k) {
+    if (!t) return fail(RWQ_ERR_ARG, "weight is null");
+    if (dtype) *dtype = t->w.dtype;
+    if (n) *n = t->w.n;
+    if (k) *k = t->w.k;
+    return RWQ_OK;
+}
+
+int rwq_qtensor_prepare_gemm(rwq_qtensor* t, void* stream) {
+    if (!t) return fail(RWQ_ERR_ARG, "weight is null");
+    return weight_gemm_cache(t, static_cast<cudaStream_t>(stream));
+}
+
+int rwq_matmul_t_q_dev(const float* a, int64_t m, int64_t k, const rwq_qtensor* b, const float* bias, float* out,
+                       int mode, void* stream) {
+    return matmul_dev_impl(a, m, k, const_cast<rwq_qtensor*>(b), bias, out, mode, static_cast<cudaStream_t>(stream),
+                           nullptr, 0);
+}
+
+int rwq_matmul_t_q(const float* a, int64_t m, int64_t k, const rwq_qtensor* b, const float* bias, float* out,
+                   int mode) {
+    int rc = check_matmul_args(a, m, k, b, out, mode);
+    if (rc) return rc;
+    const int64_t n = b->w.n;
+    if (m == 0 || n == 0) return RWQ_OK;
+    cudaStream_t s = thread_stream();
+    // Host-buffer compat path: device copies of A, bias and C live in a
+    // second arena keyed on this thread's stream.
+    Workspace* ws = nullptr;
+    if ((rc = get_workspace(reinterpret_cast<cudaStream_t>(reinterpret_cast<uintptr_t>(s) ^ 1), &ws))) return rc;
+    std::lock_guard<std::mutex> g(ws->mu);
+    const size_t a_b = align_up(size_t(m) * k * 4, 256), o_b = align_up(size_t(m) * n * 4, 256),
+                 b_b = align_up(size_t(n) * 4, 256);
+    if ((rc = ensure_cap(ws, a_b + o_b + b_b))) return rc;
+    float* da = static_cast<float*>(ws->buf);
+    float* dout = reinterpret_cast<float*>(static_cast<uint8_t*>(ws->buf) + a_b);
+    float* dbias = bias ? reinterpret_cast<float*>(static_cast<uint8_t*>(ws->buf) + a_b + o_b) : nullptr;
+    RWQ_CUDA(cudaMemcpyAsync(da, a, size_t(m) * k * 4, cudaMemcpyHostToDevice, s), "copy A to device");
+    if (bias) RWQ_CUDA(cudaMemcpyAsync(dbias, bias, size_t(n) * 4, cudaMemcpyHostToDevice, s), "copy bias");
+    if ((rc = matmul_dev_impl(da, m, k, const_cast<rwq_qtensor*>(b), dbias, dout, mode, s, nullptr, 0))) return rc;
+    RWQ_CUDA(cudaMemcpyAsync(out, dout, size_t(m) * n * 4, cudaMemcpyDeviceToHost, s), "copy C to host");
+    Workspace* mws = nullptr;
+    if ((rc = get_workspace(s, &mws))) return rc;
+    return read_device_error(mws, s);
+}
+
+int rwq_dequant_rows_dev(const rwq_qtensor* t, const int32_t* rows, int64_t nrows, float* out, void* stream) {
+    if (!t) return fail(RWQ_ERR_ARG, "weight is null");
+    if (nrows < 0 || (nrows > 0 && !out)) return fail(RWQ_ERR_ARG, "bad output");
+    if (!rows && nrows > t->w.n) return fail(RWQ_ERR_ARG, "nrows %lld > n %d", (long long)nrows, t->w.n);
+    RWQ_CUDA(rwq::launch_dequant_rows(t->w, rows, int(nrows), out, static_cast<cudaStream_t>(stream)), "dequant launch");
+    return RWQ_OK;
+}
+
+int rwq_row_f32(const rwq_qtensor* t, int64_t row, float* out) {
+    if (!t) return fail(RWQ_ERR_ARG, "weight is null");
+    if (row < 0 || row >= t->w.n) return fail(RWQ_ERR_ARG, "row %lld out of range [0, %d)", (long long)row, t->w.n);
+    if (!out) return fail(RWQ_ERR_ARG, "out is null");
+    cudaStream_t s = thread_stream();
+    Workspace* ws = nullptr;
+    int rc;
+    if ((rc = get_workspace(reinterpret_cast<cudaStream_t>(reinterpret_cast<uintptr_t>(s) ^ 1), &ws))) return rc;
+    std::lock_guard<std::mutex> g(ws->mu);
+    if ((rc = ensure_cap(ws, size_t(t->w.k) * 4 + 256))) return rc;
+    int32_t* drow = reinterpret_cast<int32_t*>(static_cast<uint8_t*>(ws->buf) + size_t(t->w.k) * 4);
+    const int32_t r32 = int32_t(row);
+    RWQ_CUDA(cudaMemcpyAsync(drow, &r32, 4, cudaMemcpyHostToDevice, s), "copy row index");
+    RWQ_CUDA(rwq::launch_dequant_rows(t->w, drow, 1, static_cast<float*>(ws->buf), s), "dequant launch");
+    RWQ_CUDA(cudaMemcpyAsync(out, ws->buf, size_t(t->w.k) * 4, cudaMemcpyDeviceToHost, s), "copy row");
+    RWQ_CUDA(cudaStreamSynchronize(s), "cudaStreamSynchronize");
+    return RWQ_OK;
+}
+
+int rwq_quantize_acts_dev(const float* a, int64_t m, int64_t k, int8_t* q, float* d, int32_t* sum, void* stream) {
+    if (m < 0 || k <= 0 || k % rwq::QK) return fail(RWQ_ERR_ARG, "bad shape (k %% 32 must be 0)");
+    if (m == 0) return RWQ_OK;
+    if (!a || !q || !d || !sum) return fail(RWQ_ERR_ARG, "null pointer");
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    Workspace* ws = nullptr;
+    int rc;
+    if ((rc = get_workspace(s, &ws))) return rc;
+    std::lock_guard<std::mutex> g(ws->mu);
+    const size_t ub = align_up(size_t(m) * (k / 32) * 4, 256);
+    if ((rc = ensure_cap(ws, ub))) return rc;
+    rwq::ActsView v;
+    v.m = int(m);
+    v.k = int(k);
+    v.nb = int(k / 32);
+    v.m_pad = v.m;
+    v.q8 = q;
+    v.d = d;
+    v.sum = sum;
+    v.u = static_cast<float*>(ws->buf);
+    RWQ_CUDA(rwq::launch_quantize_acts(a, v, false, s), "quantize launch");
+    return RWQ_OK;
+}
+
+int rwq_block_dots_dev(const float* a, int64_t m, int64_t k, const rwq_qtensor* b, int32_t* S, int path,
+                       void* stream) {
+    int rc = check_matmul_args(a, m, k, b, S ? reinterpret_cast<float*>(S) : nullptr, RWQ_MODE_INT8);
+    if (rc) return rc;
+    if (m == 0 || b->w.n == 0) return RWQ_OK;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (path == 1) {
+        // The GEMM writes S while computing C; C goes to scratch.
+        Workspace* ws = nullptr;
+        if ((rc = get_workspace(reinterpret_cast<cudaStream_t>(reinterpret_cast<uintptr_t>(s) ^ 2), &ws))) return rc;
+        std::lock_guard<std::mutex> g(ws->mu);
+        if ((rc = ensure_cap(ws, size_t(m) * b->w.n * 4 + 256))) return rc;
+        return matmul_dev_impl(a, m, k, const_cast<rwq_qtensor*>(b), nullptr, static_cast<float*>(ws->buf),
+                               RWQ_MODE_INT8, s, S, 2);
+    }
+    if (path != 0) return fail(RWQ_ERR_ARG, "unknown block-dot path %d", path);
+    Workspace* ws = nullptr;
+    if ((rc = get_workspace(s, &ws))) return rc;
+    std::lock_guard<std::mutex> g(ws->mu);
+    rwq::ActsView v;
+    const size_t need = acts_layout(int(m), int(k), false, &v, nullptr);
+    if ((rc = ensure_cap(ws, need))) return rc;
+    acts_layout(int(m), int(k), false, &v, static_cast<uint8_t*>(ws->buf));
+    RWQ_CUDA(rwq::launch_quantize_acts(a, v, false, s), "quantize launch");
+    RWQ_CUDA(rwq::launch_block_dots(v, b->w, S, s), "block dots launch");
+    return RWQ_OK;
+}
+
+int rwq_set_gemm_path(int path) {
+    if (path < 0 || path > 2) return fail(RWQ_ERR_ARG, "path must be 0, 1 or 2");
+    t_gemm_path = path;
+    return RWQ_OK;
+}
+
+int rwq_stream_check(void* stream) {
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    RWQ_CUDA(cudaStreamSynchronize(s), "cudaStreamSynchronize");
+    RWQ_CUDA(cudaGetLastError(), "pending CUDA error");
+    Workspace* ws = nullptr;
+    int rc;
+    if ((rc = get_workspace(s, &ws))) return rc;
+    return read_device_error(ws, s);
+}
+
+}  // extern "C"

@@ -1,0 +1,84 @@
+// rwq_common.cuh -- shared device helpers for the quantized-matmul kernels.
+//
+// Block formats (ggml, 32 elements per block; quant.rs:43-131):
+//   Q4_0 (2): d f16 | qs[16]             q = nib - 8
+//   Q4_1 (3): d f16 | m f16 | qs[16]     q = nib,           x = d*q + m
+//   Q5_0 (6): d f16 | qh u32 | qs[16]    q = (nib|h<<4) - 16
+//   Q5_1 (7): d f16 | m f16 | qh u32 | qs[16]   q = nib|h<<4, x = d*q + m
+//   Q8_0 (8): d f16 | q[32] i8
+// Element j<16 is the low nibble of qs[j], j>=16 the high nibble of
+// qs[j-16]; bit j of qh is element j's fifth bit.
+//
+// On the device a weight lives as "planes" (same bytes per block as the
+// ggml record, split so every block's code bytes start on a 16-byte
+// boundary):  qs [n][nb][QSB]  (QSB = 16, or 32 for Q8_0),
+//             qh [n][nb] u32 (Q5 only), d [n][nb] f16 bits,
+//             m [n][nb] f16 bits (Q4_1/Q5_1 only).
+#pragma once
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace rwq {
+
+constexpr int QK = 32;
+
+enum Dtype : int { Q4_0 = 2, Q4_1 = 3, Q5_0 = 6, Q5_1 = 7, Q8_0 = 8 };
+
+__host__ __device__ constexpr int block_bytes(int dt) {
+    return dt == Q4_0 ? 18 : dt == Q4_1 ? 20 : dt == Q5_0 ? 22 : dt == Q5_1 ? 24 : dt == Q8_0 ? 34 : -1;
+}
+__host__ __device__ constexpr bool has_min(int dt) { return dt == Q4_1 || dt == Q5_1; }
+__host__ __device__ constexpr bool has_qh(int dt) { return dt == Q5_0 || dt == Q5_1; }
+__host__ __device__ constexpr int qs_bytes(int dt) { return dt == Q8_0 ? 32 : 16; }
+// Unsigned code offset removed after the integer dot (Q4_0: 8, Q5_0: 16).
+__host__ __device__ constexpr int code_offset(int dt) { return dt == Q4_0 ? 8 : dt == Q5_0 ? 16 : 0; }
+
+// Byte offsets of the fields inside a raw ggml block.
+__host__ __device__ constexpr int raw_m_off(int) { return 2; }
+__host__ __device__ constexpr int raw_qh_off(int dt) { return dt == Q5_0 ? 2 : 4; }
+__host__ __device__ constexpr int raw_qs_off(int dt) {
+    return dt == Q4_0 ? 2 : dt == Q4_1 ? 4 : dt == Q5_0 ? 6 : dt == Q5_1 ? 8 : 2;
+}
+
+// Exact f16 -> f32 (model.rs:68-86 semantics; the hardware conversion is
+// exact for every f16 including subnormals, inf and NaN payloads).
+__device__ __forceinline__ float h2f(uint16_t h) {
+    float f;
+    asm("{ .reg .f16 t; mov.b16 t, %1; cvt.f32.f16 %0, t; }" : "=f"(f) : "h"(h));
+    return f;
+}
+
+// Spread 4 bits b[3:0] to bit 4 of bytes 0..3: bit i*(1+7) lands on bit
+// 4+8i and no two shifted copies overlap, so the product never carries.
+__device__ __forceinline__ uint32_t spread4_to_bit4(uint32_t b4) { return (b4 * 0x02040810u) & 0x10101010u; }
+
+// Unsigned 5-/4-bit code words for one block: word t < 4 holds elements
+// 4t..4t+3, word 4+t holds elements 16+4t..16+4t+3, one code per byte.
+template <int DT>
+__device__ __forceinline__ void codes_u8x4(const uint4 qs, uint32_t qh, uint32_t (&w)[8]) {
+    const uint32_t v[4] = {qs.x, qs.y, qs.z, qs.w};
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+        uint32_t lo = v[t] & 0x0F0F0F0Fu;
+        uint32_t hi = (v[t] >> 4) & 0x0F0F0F0Fu;
+        if (has_qh(DT)) {
+            lo |= spread4_to_bit4((qh >> (4 * t)) & 0xFu);
+            hi |= spread4_to_bit4((qh >> (16 + 4 * t)) & 0xFu);
+        }
+        w[t] = lo;
+        w[4 + t] = hi;
+    }
+}
+
+__device__ __forceinline__ int dp4a_su(uint32_t a_s8, uint32_t b_u8, int c) {
+    int d;
+    asm("dp4a.s32.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a_s8), "r"(b_u8), "r"(c));
+    return d;
+}
+__device__ __forceinline__ int dp4a_ss(uint32_t a_s8, uint32_t b_s8, int c) {
+    int d;
+    asm("dp4a.s32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a_s8), "r"(b_s8), "r"(c));
+    return d;
+}
+
+}  // namespace rwq

@@ -1,0 +1,53 @@
+// rwq_internal.h -- declarations shared by the library's translation units.
+// Not part of the public C ABI (that is include/rwq.h).
+#pragma once
+#include <cstddef>
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace rwq {
+
+// Device-resident weight: the "planes" layout of rwq_common.cuh plus the
+// lazily built tensor-core operand cache.
+struct Weight {
+    int dtype = 0, n = 0, k = 0, nb = 0, device = 0;
+    uint8_t* qs = nullptr;     // [n][nb][qs_bytes]
+    uint32_t* qh = nullptr;    // [n][nb]          (Q5_0 / Q5_1)
+    uint16_t* d = nullptr;     // [n][nb] f16 bits
+    uint16_t* m = nullptr;     // [n][nb] f16 bits (Q4_1 / Q5_1)
+    // tensor-core operand cache (built on first GEMM-sized call)
+    uint16_t* q16 = nullptr;   // [n][k] centred codes as f16
+    float* dT = nullptr;       // [nb][n_pad] d as f32, transposed
+    float* mT = nullptr;       // [nb][n_pad] m as f32, transposed (min formats)
+    int n_pad = 0;
+    bool gemm_ready = false;
+};
+
+// Scratch for one activation quantization (quantize_acts_i8 output).
+struct ActsView {
+    int m = 0, k = 0, nb = 0, m_pad = 0;
+    int8_t* q8 = nullptr;      // [m][k]        GEMV operand
+    float* d = nullptr;        // [m][nb]       d_a
+    int32_t* sum = nullptr;    // [m][nb]       sum(q_a)
+    float* u = nullptr;        // [m][nb]       d_a * sum(q_a)
+    uint16_t* q16 = nullptr;   // [m][k] f16    GEMM operand (optional)
+    float* dT = nullptr;       // [nb][m_pad]   (optional)
+    float* uT = nullptr;       // [nb][m_pad]   (optional)
+};
+
+// ---- launchers (return a cudaError_t of the launch) ----
+cudaError_t launch_repack(const uint8_t* raw, Weight& w, cudaStream_t s);
+cudaError_t launch_build_gemm_cache(Weight& w, cudaStream_t s);
+cudaError_t launch_quantize_acts(const float* a, const ActsView& v, bool want_gemm, cudaStream_t s);
+cudaError_t launch_dequant_rows(const Weight& w, const int32_t* rows, int nrows, float* out, cudaStream_t s);
+cudaError_t launch_block_dots(const ActsView& v, const Weight& w, int32_t* S, cudaStream_t s);
+cudaError_t launch_gemv_i8(const ActsView& v, const Weight& w, const float* bias, float* y, cudaStream_t s);
+cudaError_t launch_gemv_f32(const float* a, int m, const Weight& w, const float* bias, float* y, cudaStream_t s);
+// tcgen05 GEMM.  S_dump (optional, small shapes) receives the per-block
+// integer dots read back from tensor memory.
+cudaError_t launch_gemm_tc(const ActsView& v, const Weight& w, const float* bias, float* y, int32_t* S_dump,
+                           int* err_flag, cudaStream_t s, char* why, size_t why_len);
+
+constexpr int GEMV_MAX_M = 8;
+
+}  // namespace rwq

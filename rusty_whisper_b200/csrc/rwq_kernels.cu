@@ -1,0 +1,514 @@
+// rwq_kernels.cu -- CUDA-core kernels of the quantized-matmul path:
+// weight repack, activation int8 quantizer, bit-exact dequant gather,
+// per-block integer dots (debug/parity), the decoder GEMVs (int8 and
+// dequant-then-f32), and the builder of the tensor-core operand cache.
+#include <cuda_fp16.h>
+#include "rwq_common.cuh"
+#include "rwq_internal.h"
+
+namespace rwq {
+
+namespace {
+
+constexpr int TPB = 256;
+
+inline unsigned grid_for(size_t work, int per_block) {
+    size_t g = (work + per_block - 1) / per_block;
+    return unsigned(g ? g : 1);
+}
+
+// ---------------------------------------------------------------- repack
+// raw ggml records [n*nb][bb] -> planes.  One thread per block; the raw
+// records are not 16-byte aligned, so they are read bytewise, once.
+template <int DT>
+__global__ void k_repack(const uint8_t* __restrict__ raw, uint8_t* __restrict__ qs, uint32_t* __restrict__ qh,
+                         uint16_t* __restrict__ d, uint16_t* __restrict__ m, size_t nblk) {
+    size_t b = size_t(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (b >= nblk) return;
+    constexpr int BB = block_bytes(DT), QSB = qs_bytes(DT), QO = raw_qs_off(DT);
+    const uint8_t* p = raw + b * BB;
+    d[b] = uint16_t(p[0] | (p[1] << 8));
+    if (has_min(DT)) m[b] = uint16_t(p[2] | (p[3] << 8));
+    if (has_qh(DT)) {
+        const uint8_t* h = p + raw_qh_off(DT);
+        qh[b] = uint32_t(h[0]) | (uint32_t(h[1]) << 8) | (uint32_t(h[2]) << 16) | (uint32_t(h[3]) << 24);
+    }
+    uint32_t words[QSB / 4];
+#pragma unroll
+    for (int i = 0; i < QSB / 4; ++i)
+        words[i] = uint32_t(p[QO + 4 * i]) | (uint32_t(p[QO + 4 * i + 1]) << 8) |
+                   (uint32_t(p[QO + 4 * i + 2]) << 16) | (uint32_t(p[QO + 4 * i + 3]) << 24);
+    uint4* dst = reinterpret_cast<uint4*>(qs + b * QSB);
+#pragma unroll
+    for (int i = 0; i < QSB / 16; ++i) dst[i] = make_uint4(words[4 * i], words[4 * i + 1], words[4 * i + 2], words[4 * i + 3]);
+}
+
+// ------------------------------------------------------------ quantizer
+// quantize_acts_i8 (quant.rs:690-716), one warp per 32-element block:
+// d = amax/127 (IEEE division), inv = 1/d or 0, q = round(x*inv) half away
+// from zero, clamped to [-127,127]; NaN codes become 0 as Rust's `as i32`.
+// Rows m..m_pad-1 of the transposed scale planes are written as zeros.
+__global__ void k_quantize(const float* __restrict__ a, int m, int k, int nb, int m_pad, int8_t* __restrict__ q8,
+                           float* __restrict__ dd, int32_t* __restrict__ sum, float* __restrict__ uu,
+                           uint16_t* __restrict__ q16, float* __restrict__ dT, float* __restrict__ uT) {
+    const int lane = threadIdx.x & 31;
+    const size_t warp = (size_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    if (warp >= size_t(m_pad) * nb) return;
+    const int i = int(warp / nb), bl = int(warp % nb);
+    if (i >= m) {
+        if (lane == 0 && dT) {
+            dT[size_t(bl) * m_pad + i] = 0.f;
+            uT[size_t(bl) * m_pad + i] = 0.f;
+        }
+        return;
+    }
+    const size_t off = size_t(i) * k + size_t(bl) * QK + lane;
+    const float x = a[off];
+    float ax = fabsf(x);
+    if (isnan(ax)) ax = 0.f;  // f32::max ignores a NaN operand
+    // Non-negative floats order like their bit patterns.
+    const float amax = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(ax)));
+    const float d = __fdiv_rn(amax, 127.0f);
+    const float inv = d > 0.f ? __fdiv_rn(1.0f, d) : 0.f;
+    const float r = roundf(__fmul_rn(x, inv));
+    const int qi = isnan(r) ? 0 : int(fminf(127.f, fmaxf(-127.f, r)));
+    const int s = __reduce_add_sync(0xffffffffu, qi);
+    if (q8) q8[off] = int8_t(qi);
+    if (q16) q16[off] = __half_as_ushort(__int2half_rn(qi));
+    if (lane == 0) {
+        const size_t o = size_t(i) * nb + bl;
+        const float u = __fmul_rn(d, float(s));
+        dd[o] = d;
+        sum[o] = s;
+        uu[o] = u;
+        if (dT) {
+            dT[size_t(bl) * m_pad + i] = d;
+            uT[size_t(bl) * m_pad + i] = u;
+        }
+    }
+}
+
+// ------------------------------------------------------ block decoding
+// Load one block's code bytes and scales from the planes.
+template <int DT>
+struct BlockCodes {
+    uint32_t w[8];   // u8x4 codes (4/5-bit formats) or s8x4 codes (Q8_0)
+    float d, m;
+};
+
+template <int DT>
+__device__ __forceinline__ void load_block(const uint8_t* __restrict__ qs, const uint32_t* __restrict__ qh,
+                                           const uint16_t* __restrict__ dp, const uint16_t* __restrict__ mp,
+                                           size_t b, BlockCodes<DT>& bc) {
+    if (DT == Q8_0) {
+        const uint4* p = reinterpret_cast<const uint4*>(qs + b * 32);
+        uint4 v0 = __ldg(p), v1 = __ldg(p + 1);
+        bc.w[0] = v0.x; bc.w[1] = v0.y; bc.w[2] = v0.z; bc.w[3] = v0.w;
+        bc.w[4] = v1.x; bc.w[5] = v1.y; bc.w[6] = v1.z; bc.w[7] = v1.w;
+    } else {
+        uint4 v = __ldg(reinterpret_cast<const uint4*>(qs + b * 16));
+        uint32_t h = has_qh(DT) ? __ldg(qh + b) : 0u;
+        codes_u8x4<DT>(v, h, bc.w);
+    }
+    bc.d = h2f(__ldg(dp + b));
+    bc.m = has_min(DT) ? h2f(__ldg(mp + b)) : 0.f;
+}
+
+// Integer block dot S = sum(q_a * q_b) with q_b centred, exact.
+template <int DT>
+__device__ __forceinline__ int block_dot(const uint32_t (&w)[8], const int4 a0, const int4 a1, int suma) {
+    const uint32_t a[8] = {uint32_t(a0.x), uint32_t(a0.y), uint32_t(a0.z), uint32_t(a0.w),
+                           uint32_t(a1.x), uint32_t(a1.y), uint32_t(a1.z), uint32_t(a1.w)};
+    int s = 0;
+    if (DT == Q8_0) {
+#pragma unroll
+        for (int t = 0; t < 8; ++t) s = dp4a_ss(a[t], w[t], s);
+    } else {
+#pragma unroll
+        for (int t = 0; t < 8; ++t) s = dp4a_su(a[t], w[t], s);
+        if (code_offset(DT)) s -= code_offset(DT) * suma;
+    }
+    return s;
+}
+
+// Centred code of element e (0..31) from the u8x4 / s8x4 words.
+template <int DT>
+__device__ __forceinline__ int code_at(const uint32_t (&w)[8], int e) {
+    const int word = (e < 16) ? (e >> 2) : 4 + ((e - 16) >> 2);
+    const int byte = e & 3;
+    const uint32_t v = (w[word] >> (8 * byte)) & 0xFFu;
+    if (DT == Q8_0) return int(int8_t(v));
+    return int(v) - code_offset(DT);
+}
+
+// ------------------------------------------------------------- dequant
+// QTensor::row_f32 / to_dense (quant.rs:528-537, 566-576): x = d*q + m with
+// a separate rounded multiply and add, bit-identical to the reference.
+template <int DT>
+__global__ void k_dequant_rows(const uint8_t* __restrict__ qs, const uint32_t* __restrict__ qh,
+                               const uint16_t* __restrict__ dp, const uint16_t* __restrict__ mp,
+                               const int32_t* __restrict__ rows, int nrows, int n, int nb, float* __restrict__ out) {
+    size_t t = size_t(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (t >= size_t(nrows) * nb) return;
+    const int r = int(t / nb), bl = int(t % nb);
+    const int j = rows ? rows[r] : r;
+    if (j < 0 || j >= n) return;  // host validated; guard anyway
+    BlockCodes<DT> bc;
+    load_block<DT>(qs, qh, dp, mp, size_t(j) * nb + bl, bc);
+    float* o = out + size_t(r) * nb * QK + size_t(bl) * QK;
+#pragma unroll
+    for (int e = 0; e < QK; e += 4) {
+        float4 v;
+        v.x = __fadd_rn(__fmul_rn(bc.d, float(code_at<DT>(bc.w, e + 0))), bc.m);
+        v.y = __fadd_rn(__fmul_rn(bc.d, float(code_at<DT>(bc.w, e + 1))), bc.m);
+        v.z = __fadd_rn(__fmul_rn(bc.d, float(code_at<DT>(bc.w, e + 2))), bc.m);
+        v.w = __fadd_rn(__fmul_rn(bc.d, float(code_at<DT>(bc.w, e + 3))), bc.m);
+        *reinterpret_cast<float4*>(o + e) = v;
+    }
+}
+
+// ---------------------------------------------------------- block dots
+// S[i][j][kb] for parity tests of the integer core (quant.rs:1352-1360).
+template <int DT>
+__global__ void k_block_dots(const uint8_t* __restrict__ qs, const uint32_t* __restrict__ qh,
+                             const uint16_t* __restrict__ dp, const uint16_t* __restrict__ mp,
+                             const int8_t* __restrict__ q8, const int32_t* __restrict__ suma, int m, int n, int nb,
+                             int32_t* __restrict__ S) {
+    size_t t = size_t(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (t >= size_t(m) * n * nb) return;
+    const int bl = int(t % nb);
+    const int j = int((t / nb) % n);
+    const int i = int(t / (size_t(nb) * n));
+    BlockCodes<DT> bc;
+    load_block<DT>(qs, qh, dp, mp, size_t(j) * nb + bl, bc);
+    const int4* a = reinterpret_cast<const int4*>(q8 + size_t(i) * nb * QK + size_t(bl) * QK);
+    S[t] = block_dot<DT>(bc.w, a[0], a[1], suma[size_t(i) * nb + bl]);
+}
+
+// -------------------------------------------------------------- GEMV i8
+// Decoder GEMV, M <= 8 activation rows.  Each warp owns 32/L weight rows,
+// L lanes per row; a lane walks its row's blocks kb = sub, sub+L, ... with
+// 128-bit loads of the code plane, unpacks nibbles / high bits in
+// registers, forms the exact integer block dot with dp4a, and accumulates
+//     acc <- fma(d_a*d_b, S, acc);  acc <- fma(d_a*sum(q_a), m_b, acc)
+// per block in order.  The L partial sums are combined with an xor
+// butterfly.  Nothing in the order depends on M, so every output row is
+// bit-identical whatever the batch (quant.rs:1372-1384).
+template <int DT, int L, int MR>
+__global__ void __launch_bounds__(TPB) k_gemv_i8(const uint8_t* __restrict__ qs, const uint32_t* __restrict__ qh,
+                                                 const uint16_t* __restrict__ dp, const uint16_t* __restrict__ mp,
+                                                 const int8_t* __restrict__ q8, const float* __restrict__ da,
+                                                 const int32_t* __restrict__ sa, const float* __restrict__ ua, int M,
+                                                 int N, int K, const float* __restrict__ bias, float* __restrict__ y) {
+    extern __shared__ __align__(16) uint8_t smem[];
+    const int nb = K / QK;
+    int8_t* s_q = reinterpret_cast<int8_t*>(smem);
+    float* s_d = reinterpret_cast<float*>(smem + size_t(M) * K);
+    float* s_u = s_d + M * nb;
+    int32_t* s_s = reinterpret_cast<int32_t*>(s_u + M * nb);
+    {
+        const int4* src = reinterpret_cast<const int4*>(q8);
+        int4* dst = reinterpret_cast<int4*>(s_q);
+        for (int i = threadIdx.x; i < M * K / 16; i += blockDim.x) dst[i] = __ldg(src + i);
+        for (int i = threadIdx.x; i < M * nb; i += blockDim.x) {
+            s_d[i] = __ldg(da + i);
+            s_u[i] = __ldg(ua + i);
+            s_s[i] = __ldg(sa + i);
+        }
+    }
+    __syncthreads();
+    const int lane = threadIdx.x & 31, sub = lane % L, slot = lane / L;
+    constexpr int RPW = 32 / L;
+    const int warps_per_cta = blockDim.x >> 5;
+    const int gw = blockIdx.x * warps_per_cta + (threadIdx.x >> 5);
+    const int nw = gridDim.x * warps_per_cta;
+    for (int row0 = gw * RPW; row0 < N; row0 += nw * RPW) {
+        const int j = row0 + slot;
+        float acc[MR];
+#pragma unroll
+        for (int r = 0; r < MR; ++r) acc[r] = 0.f;
+        if (j < N) {
+            for (int kb = sub; kb < nb; kb += L) {
+                BlockCodes<DT> bc;
+                load_block<DT>(qs, qh, dp, mp, size_t(j) * nb + kb, bc);
+#pragma unroll
+                for (int r = 0; r < MR; ++r) {
+                    if (r < M) {
+                        const int4* a = reinterpret_cast<const int4*>(s_q + size_t(r) * K + kb * QK);
+                        const int S = block_dot<DT>(bc.w, a[0], a[1], s_s[r * nb + kb]);
+                        acc[r] = __fmaf_rn(__fmul_rn(s_d[r * nb + kb], bc.d), float(S), acc[r]);
+                        if (has_min(DT)) acc[r] = __fmaf_rn(s_u[r * nb + kb], bc.m, acc[r]);
+                    }
+                }
+            }
+        }
+#pragma unroll
+        for (int r = 0; r < MR; ++r) {
+#pragma unroll
+            for (int o = L / 2; o > 0; o >>= 1) acc[r] = __fadd_rn(acc[r], __shfl_xor_sync(0xffffffffu, acc[r], o));
+        }
+        if (j < N && sub == 0) {
+            const float b = bias ? __ldg(bias + j) : 0.f;
+#pragma unroll
+            for (int r = 0; r < MR; ++r)
+                if (r < M) y[size_t(r) * N + j] = bias ? __fadd_rn(acc[r], b) : acc[r];
+        }
+    }
+}
+
+// ------------------------------------------------------------- GEMV f32
+// Dequant-then-fp path (the f32 tier, quant.rs:995-1018): weights
+// dequantized bit-exactly, dotted with unquantized f32 activations.
+template <int DT, int L, int MR>
+__global__ void __launch_bounds__(TPB) k_gemv_f32(const uint8_t* __restrict__ qs, const uint32_t* __restrict__ qh,
+                                                  const uint16_t* __restrict__ dp, const uint16_t* __restrict__ mp,
+                                                  const float* __restrict__ a, int M, int N, int K,
+                                                  const float* __restrict__ bias, float* __restrict__ y) {
+    const int nb = K / QK;
+    const int lane = threadIdx.x & 31, sub = lane % L, slot = lane / L;
+    constexpr int RPW = 32 / L;
+    const int warps_per_cta = blockDim.x >> 5;
+    const int gw = blockIdx.x * warps_per_cta + (threadIdx.x >> 5);
+    const int nw = gridDim.x * warps_per_cta;
+    for (int row0 = gw * RPW; row0 < N; row0 += nw * RPW) {
+        const int j = row0 + slot;
+        float acc[MR];
+#pragma unroll
+        for (int r = 0; r < MR; ++r) acc[r] = 0.f;
+        if (j < N) {
+            for (int kb = sub; kb < nb; kb += L) {
+                BlockCodes<DT> bc;
+                load_block<DT>(qs, qh, dp, mp, size_t(j) * nb + kb, bc);
+                float w[QK];
+#pragma unroll
+                for (int e = 0; e < QK; ++e) w[e] = __fadd_rn(__fmul_rn(bc.d, float(code_at<DT>(bc.w, e))), bc.m);
+#pragma unroll
+                for (int r = 0; r < MR; ++r) {
+                    if (r < M) {
+                        const float4* ar = reinterpret_cast<const float4*>(a + size_t(r) * K + size_t(kb) * QK);
+#pragma unroll
+                        for (int e4 = 0; e4 < QK / 4; ++e4) {
+                            const float4 v = __ldg(ar + e4);
+                            acc[r] = __fmaf_rn(v.x, w[4 * e4 + 0], acc[r]);
+                            acc[r] = __fmaf_rn(v.y, w[4 * e4 + 1], acc[r]);
+                            acc[r] = __fmaf_rn(v.z, w[4 * e4 + 2], acc[r]);
+                            acc[r] = __fmaf_rn(v.w, w[4 * e4 + 3], acc[r]);
+                        }
+                    }
+                }
+            }
+        }
+#pragma unroll
+        for (int r = 0; r < MR; ++r) {
+#pragma unroll
+            for (int o = L / 2; o > 0; o >>= 1) acc[r] = __fadd_rn(acc[r], __shfl_xor_sync(0xffffffffu, acc[r], o));
+        }
+        if (j < N && sub == 0) {
+            const float b = bias ? __ldg(bias + j) : 0.f;
+#pragma unroll
+            for (int r = 0; r < MR; ++r)
+                if (r < M) y[size_t(r) * N + j] = bias ? __fadd_rn(acc[r], b) : acc[r];
+        }
+    }
+}
+
+// ----------------------------------------------------- GEMM operand cache
+// Planes -> f16 centred codes [n][k] + transposed f32 scales [nb][n_pad]
+// (the tensor-core GEMM's B operand; the GPU counterpart of the
+// reference's cached int8 unpack, quant.rs:589-639).  Padding columns of
+// the scale planes are zeroed.
+template <int DT>
+__global__ void k_build_gemm_cache(const uint8_t* __restrict__ qs, const uint32_t* __restrict__ qh,
+                                   const uint16_t* __restrict__ dp, const uint16_t* __restrict__ mp, int n, int nb,
+                                   int n_pad, uint16_t* __restrict__ q16, float* __restrict__ dT,
+                                   float* __restrict__ mT) {
+    size_t t = size_t(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (t >= size_t(n_pad) * nb) return;
+    const int j = int(t / nb), bl = int(t % nb);
+    if (j >= n) {
+        dT[size_t(bl) * n_pad + j] = 0.f;
+        if (mT) mT[size_t(bl) * n_pad + j] = 0.f;
+        return;
+    }
+    BlockCodes<DT> bc;
+    load_block<DT>(qs, qh, dp, mp, size_t(j) * nb + bl, bc);
+    uint4* o = reinterpret_cast<uint4*>(q16 + size_t(j) * nb * QK + size_t(bl) * QK);
+#pragma unroll
+    for (int e8 = 0; e8 < QK / 8; ++e8) {
+        uint32_t h[4];
+#pragma unroll
+        for (int p = 0; p < 4; ++p) {
+            const int e = 8 * e8 + 2 * p;
+            const uint32_t lo = __half_as_ushort(__int2half_rn(code_at<DT>(bc.w, e)));
+            const uint32_t hi = __half_as_ushort(__int2half_rn(code_at<DT>(bc.w, e + 1)));
+            h[p] = lo | (hi << 16);
+        }
+        o[e8] = make_uint4(h[0], h[1], h[2], h[3]);
+    }
+    dT[size_t(bl) * n_pad + j] = bc.d;
+    if (mT) mT[size_t(bl) * n_pad + j] = bc.m;
+}
+
+// ------------------------------------------------------------ dispatch
+template <template <int> class F, typename... Args>
+cudaError_t by_dtype(int dt, Args&&... args) {
+    switch (dt) {
+        case Q4_0: return F<Q4_0>::run(args...);
+        case Q4_1: return F<Q4_1>::run(args...);
+        case Q5_0: return F<Q5_0>::run(args...);
+        case Q5_1: return F<Q5_1>::run(args...);
+        case Q8_0: return F<Q8_0>::run(args...);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+template <int DT>
+struct RepackF {
+    static cudaError_t run(const uint8_t* raw, Weight& w, cudaStream_t s) {
+        size_t nblk = size_t(w.n) * w.nb;
+        if (!nblk) return cudaSuccess;
+        k_repack<DT><<<grid_for(nblk, TPB), TPB, 0, s>>>(raw, w.qs, w.qh, w.d, w.m, nblk);
+        return cudaGetLastError();
+    }
+};
+
+template <int DT>
+struct DequantF {
+    static cudaError_t run(const Weight& w, const int32_t* rows, int nrows, float* out, cudaStream_t s) {
+        size_t work = size_t(nrows) * w.nb;
+        if (!work) return cudaSuccess;
+        k_dequant_rows<DT><<<grid_for(work, TPB), TPB, 0, s>>>(w.qs, w.qh, w.d, w.m, rows, nrows, w.n, w.nb, out);
+        return cudaGetLastError();
+    }
+};
+
+template <int DT>
+struct BlockDotsF {
+    static cudaError_t run(const ActsView& v, const Weight& w, int32_t* S, cudaStream_t s) {
+        size_t work = size_t(v.m) * w.n * w.nb;
+        if (!work) return cudaSuccess;
+        k_block_dots<DT><<<grid_for(work, TPB), TPB, 0, s>>>(w.qs, w.qh, w.d, w.m, v.q8, v.sum, v.m, w.n, w.nb, S);
+        return cudaGetLastError();
+    }
+};
+
+template <int DT>
+struct GemmCacheF {
+    static cudaError_t run(Weight& w, cudaStream_t s) {
+        size_t work = size_t(w.n_pad) * w.nb;
+        k_build_gemm_cache<DT><<<grid_for(work, TPB), TPB, 0, s>>>(w.qs, w.qh, w.d, w.m, w.n, w.nb, w.n_pad, w.q16,
+                                                                   w.dT, w.mT);
+        return cudaGetLastError();
+    }
+};
+
+// Lanes per weight row for a row of nb blocks: the widest of 32/16/8 that
+// divides nb (all lanes busy), else 8.
+inline int lanes_for(int nb) {
+    if (nb % 32 == 0 && nb >= 64) return 32;
+    if (nb % 16 == 0) return 16;
+    if (nb % 8 == 0) return 8;
+    return nb >= 32 ? 32 : 8;
+}
+
+inline unsigned gemv_grid(int n, int L) {
+    const int rows_per_cta = (TPB / 32) * (32 / L);
+    unsigned g = unsigned((n + rows_per_cta - 1) / rows_per_cta);
+    const unsigned cap = 148u * 8u;
+    return g < 1 ? 1 : (g > cap ? cap : g);
+}
+
+template <int DT, int L, int MR>
+cudaError_t gemv_i8_launch(const ActsView& v, const Weight& w, const float* bias, float* y, cudaStream_t s) {
+    const size_t smem = size_t(v.m) * v.k + size_t(v.m) * w.nb * 12;
+    static bool attr_set = false;  // one per instantiation
+    if (!attr_set) {
+        cudaError_t e = cudaFuncSetAttribute(k_gemv_i8<DT, L, MR>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             200 * 1024);
+        if (e != cudaSuccess) return e;
+        attr_set = true;
+    }
+    k_gemv_i8<DT, L, MR><<<gemv_grid(w.n, L), TPB, smem, s>>>(w.qs, w.qh, w.d, w.m, v.q8, v.d, v.sum, v.u, v.m, w.n,
+                                                             w.k, bias, y);
+    return cudaGetLastError();
+}
+
+template <int DT, int L>
+cudaError_t gemv_i8_mr(const ActsView& v, const Weight& w, const float* bias, float* y, cudaStream_t s) {
+    if (v.m <= 1) return gemv_i8_launch<DT, L, 1>(v, w, bias, y, s);
+    if (v.m <= 2) return gemv_i8_launch<DT, L, 2>(v, w, bias, y, s);
+    if (v.m <= 4) return gemv_i8_launch<DT, L, 4>(v, w, bias, y, s);
+    return gemv_i8_launch<DT, L, 8>(v, w, bias, y, s);
+}
+
+template <int DT>
+struct GemvI8F {
+    static cudaError_t run(const ActsView& v, const Weight& w, const float* bias, float* y, cudaStream_t s) {
+        switch (lanes_for(w.nb)) {
+            case 32: return gemv_i8_mr<DT, 32>(v, w, bias, y, s);
+            case 16: return gemv_i8_mr<DT, 16>(v, w, bias, y, s);
+            default: return gemv_i8_mr<DT, 8>(v, w, bias, y, s);
+        }
+    }
+};
+
+template <int DT, int L, int MR>
+cudaError_t gemv_f32_launch(const float* a, int m, const Weight& w, const float* bias, float* y, cudaStream_t s) {
+    k_gemv_f32<DT, L, MR><<<gemv_grid(w.n, L), TPB, 0, s>>>(w.qs, w.qh, w.d, w.m, a, m, w.n, w.k, bias, y);
+    return cudaGetLastError();
+}
+
+template <int DT, int L>
+cudaError_t gemv_f32_mr(const float* a, int m, const Weight& w, const float* bias, float* y, cudaStream_t s) {
+    if (m <= 1) return gemv_f32_launch<DT, L, 1>(a, m, w, bias, y, s);
+    if (m <= 2) return gemv_f32_launch<DT, L, 2>(a, m, w, bias, y, s);
+    if (m <= 4) return gemv_f32_launch<DT, L, 4>(a, m, w, bias, y, s);
+    return gemv_f32_launch<DT, L, 8>(a, m, w, bias, y, s);
+}
+
+template <int DT>
+struct GemvF32F {
+    static cudaError_t run(const float* a, int m, const Weight& w, const float* bias, float* y, cudaStream_t s) {
+        switch (lanes_for(w.nb)) {
+            case 32: return gemv_f32_mr<DT, 32>(a, m, w, bias, y, s);
+            case 16: return gemv_f32_mr<DT, 16>(a, m, w, bias, y, s);
+            default: return gemv_f32_mr<DT, 8>(a, m, w, bias, y, s);
+        }
+    }
+};
+
+}  // namespace
+
+cudaError_t launch_repack(const uint8_t* raw, Weight& w, cudaStream_t s) { return by_dtype<RepackF>(w.dtype, raw, w, s); }
+
+cudaError_t launch_build_gemm_cache(Weight& w, cudaStream_t s) { return by_dtype<GemmCacheF>(w.dtype, w, s); }
+
+cudaError_t launch_quantize_acts(const float* a, const ActsView& v, bool want_gemm, cudaStream_t s) {
+    const int m_pad = want_gemm ? v.m_pad : v.m;
+    const size_t warps = size_t(m_pad) * v.nb;
+    if (!warps) return cudaSuccess;
+    k_quantize<<<grid_for(warps * 32, TPB), TPB, 0, s>>>(a, v.m, v.k, v.nb, m_pad, want_gemm ? nullptr : v.q8, v.d, v.sum, v.u,
+                                                        want_gemm ? v.q16 : nullptr, want_gemm ? v.dT : nullptr,
+                                                        want_gemm ? v.uT : nullptr);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_dequant_rows(const Weight& w, const int32_t* rows, int nrows, float* out, cudaStream_t s) {
+    return by_dtype<DequantF>(w.dtype, w, rows, nrows, out, s);
+}
+
+cudaError_t launch_block_dots(const ActsView& v, const Weight& w, int32_t* S, cudaStream_t s) {
+    return by_dtype<BlockDotsF>(w.dtype, v, w, S, s);
+}
+
+cudaError_t launch_gemv_i8(const ActsView& v, const Weight& w, const float* bias, float* y, cudaStream_t s) {
+    if (v.m <= 0 || w.n <= 0) return cudaSuccess;
+    return by_dtype<GemvI8F>(w.dtype, v, w, bias, y, s);
+}
+
+cudaError_t launch_gemv_f32(const float* a, int m, const Weight& w, const float* bias, float* y, cudaStream_t s) {
+    if (m <= 0 || w.n <= 0) return cudaSuccess;
+    return by_dtype<GemvF32F>(w.dtype, a, m, w, bias, y, s);
+}
+
+}  // namespace rwq

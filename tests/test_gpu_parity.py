@@ -1,0 +1,194 @@
+"""GPU parity of the B200 kernels against the CPU oracle (marked gpu).
+
+Bars (rusty_whisper's own rules, quant.rs:1125-1160, 1336-1384):
+  * dequant: bit-identical to the reference's scalar dequant;
+  * activation quantizer: bit-identical q, d, sum(q);
+  * per-block integer dots S[i,j,kb]: bit-identical, both kernel families;
+  * int8-path f32 outputs: |y - ref| <= 1e-3 * max(|ref|, 1) against the
+    scalar int8 oracle and the reference tier that runs on this host;
+  * dequant-then-f32 outputs: same rule against the oracle's f32 tier;
+  * batch invariance: a row's result does not depend on M.
+"""
+import glob
+import os
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+FORMATS = (2, 3, 6, 7, 8)
+TOL = 1e-3  # quant.rs:1365
+
+
+@pytest.fixture(scope="module")
+def rq():
+    import torch
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    from rusty_whisper_b200 import quant
+    quant.init(0)
+    return quant
+
+
+def close(got, ref, tol=TOL):
+    got = np.asarray(got, np.float64)
+    ref = np.asarray(ref, np.float64)
+    err = np.abs(got - ref) / np.maximum(np.abs(ref), 1.0)
+    return float(err.max()) if err.size else 0.0
+
+
+def cuda(x):
+    import torch
+    return torch.from_numpy(np.ascontiguousarray(x)).cuda()
+
+
+def host(t):
+    return t.detach().cpu().numpy()
+
+
+@pytest.mark.parametrize("path", sorted(glob.glob(os.path.join(ROOT, "tests", "golden", "*.npz"))))
+def test_golden_fixture_on_gpu(rq, path):
+    fx = np.load(path)
+    dtype, m, n, k = int(fx["dtype"]), int(fx["m"]), int(fx["n"]), int(fx["k"])
+    w = rq.QTensor([n, k], dtype, fx["raw"])
+    a = cuda(fx["a"])
+    assert np.array_equal(host(w.to_dense()).view(np.uint32), fx["dense"].view(np.uint32))
+    q, d, s = rq.quantize_acts_i8(a)
+    assert np.array_equal(host(q), fx["qa"])
+    assert np.array_equal(host(d).view(np.uint32), fx["da"].view(np.uint32))
+    assert np.array_equal(host(s), fx["sa"])
+    assert np.array_equal(host(rq.block_dots(a, w, path=0)), fx["S"])
+    y = host(rq.matmul_t_q(a, w))
+    assert close(y, fx["y_int8_scalar"]) < TOL
+    assert close(y, fx["y_avx2"]) < TOL
+    if "y_vnni" in fx.files:
+        assert close(y, fx["y_vnni"]) < TOL
+    yf = host(rq.matmul_t_q(a, w, mode="f32"))
+    assert close(yf, fx["y_f32"]) < TOL
+
+
+def _case(dtype, m, k, n, seed):
+    from rusty_whisper_b200 import synth
+    a = synth.normal(seed, m * k).reshape(m, k)
+    raw = synth.random_blocks(dtype, n, k, seed + 1)
+    return a, raw
+
+
+@pytest.mark.parametrize("dtype", FORMATS)
+@pytest.mark.parametrize("m,k,n", [(129, 96, 41), (200, 256, 130), (300, 768, 257)])
+def test_gemm_tensor_core_block_dots_bit_exact(rq, orc, dtype, m, k, n):
+    a, raw = _case(dtype, m, k, n, 7 * dtype + m)
+    w = rq.QTensor([n, k], dtype, raw)
+    qa, _, _ = orc.quantize_acts_i8(a)
+    S_ref = orc.block_dots(qa, dtype, raw, n)
+    S_tc = host(rq.block_dots(cuda(a), w, path=1))
+    assert np.array_equal(S_tc, S_ref)
+    S_cc = host(rq.block_dots(cuda(a), w, path=0))
+    assert np.array_equal(S_cc, S_ref)
+
+
+@pytest.mark.parametrize("dtype", FORMATS)
+@pytest.mark.parametrize("m,k,n", [(1, 768, 768), (5, 768, 3072), (8, 3072, 768), (9, 128, 200),
+                                   (37, 96, 41), (1500, 384, 1536), (333, 1024, 520)])
+def test_matmul_int8_matches_oracle(rq, orc, dtype, m, k, n):
+    a, raw = _case(dtype, m, k, n, 11 * dtype + m + k)
+    w = rq.QTensor([n, k], dtype, raw)
+    y = host(rq.matmul_t_q(cuda(a), w))
+    rq.stream_check()
+    ref = orc.matmul_t_q(a, dtype, raw, n)          # tier dispatched on this host
+    assert close(y, ref) < TOL
+    if m * n * k <= 50_000_000:
+        assert close(y, orc.int8_scalar_matmul(a, dtype, raw, n)) < TOL
+
+
+@pytest.mark.parametrize("dtype", FORMATS)
+@pytest.mark.parametrize("m,k,n", [(1, 768, 768), (5, 256, 300), (20, 96, 41)])
+def test_matmul_f32_mode_matches_dequant_then_fp(rq, orc, dtype, m, k, n):
+    a, raw = _case(dtype, m, k, n, 13 * dtype + m)
+    w = rq.QTensor([n, k], dtype, raw)
+    y = host(rq.matmul_t_q(cuda(a), w, mode="f32"))
+    ref = orc.matmul_t(a, orc.to_dense(dtype, raw, n, k))
+    assert close(y, ref) < TOL
+
+
+@pytest.mark.parametrize("dtype", FORMATS)
+def test_dequant_rows_bit_exact(rq, orc, dtype):
+    n, k = 77, 160
+    _, raw = _case(dtype, 1, k, n, 3 * dtype)
+    w = rq.QTensor([n, k], dtype, raw)
+    dense = orc.to_dense(dtype, raw, n, k)
+    assert np.array_equal(host(w.to_dense()).view(np.uint32), dense.view(np.uint32))
+    rows = [76, 0, 13, 13]
+    assert np.array_equal(host(w.rows_f32(rows)).view(np.uint32), dense[rows].view(np.uint32))
+    assert np.array_equal(host(w.row_f32(5)).view(np.uint32), dense[5].view(np.uint32))
+
+
+def test_batch_invariance(rq):
+    """Row results do not depend on M (quant.rs:1372-1384), within each
+    kernel family: the GEMV (M <= 8) and the tensor-core GEMM (M > 8)."""
+    import torch
+    from rusty_whisper_b200 import synth
+    for dtype in FORMATS:
+        k, n = 512, 1200
+        w = rq.QTensor([n, k], dtype, synth.random_blocks(dtype, n, k, 21))
+        a = cuda(synth.normal(22, 300 * k).reshape(300, k))
+        y8 = rq.matmul_t_q(a[:8], w)
+        for mm in (1, 3, 5):
+            assert torch.equal(rq.matmul_t_q(a[:mm], w), y8[:mm])
+        y300 = rq.matmul_t_q(a, w)
+        for mm in (9, 128, 129, 256):
+            assert torch.equal(rq.matmul_t_q(a[:mm], w), y300[:mm])
+
+
+def test_bias_and_host_path(rq, orc):
+    from rusty_whisper_b200 import synth
+    dtype, m, k, n = 7, 150, 256, 96
+    a, raw = _case(dtype, m, k, n, 5)
+    b = synth.normal(6, n)
+    w = rq.QTensor([n, k], dtype, raw)
+    y_dev = host(rq.linear_w(cuda(a), w, cuda(b)))
+    y_host = rq.linear_w(a, w, b)                   # host buffers in, host out
+    assert np.array_equal(y_dev, y_host)
+    ref = orc.matmul_t_q(a, dtype, raw, n) + b[None, :]
+    assert close(y_host, ref) < TOL
+    for mm in (1, 5):                               # GEMV with bias
+        y = rq.linear_w(a[:mm], w, b)
+        assert close(y, ref[:mm]) < TOL
+
+
+def test_errors_and_edges(rq):
+    import torch
+    from rusty_whisper_b200 import synth
+    w = rq.QTensor([40, 64], 8, synth.random_blocks(8, 40, 64, 1))
+    with pytest.raises(ValueError):
+        rq.matmul_t_q(torch.zeros((3, 96), device="cuda"), w)        # inner dims
+    with pytest.raises(ValueError):
+        rq.QTensor([4, 48], 8, bytes(4 * 34))                        # k % 32
+    with pytest.raises(ValueError):
+        rq.QTensor([4, 32], 4, bytes(4 * 18))                        # dtype
+    with pytest.raises(ValueError):
+        rq.QTensor([4, 32], 8, bytes(3 * 34))                        # raw length
+    y = rq.matmul_t_q(torch.zeros((0, 64), device="cuda"), w)        # empty batch
+    assert y.shape == (0, 40)
+    z = rq.matmul_t_q(torch.zeros((20, 64), device="cuda"), w)      # zero blocks: d = 0
+    assert torch.count_nonzero(z) == 0
+    empty = rq.QTensor([0, 64], 8, b"")
+    assert rq.matmul_t_q(torch.ones((3, 64), device="cuda"), empty).shape == (3, 0)
+    with pytest.raises(ValueError):
+        w.rows_f32([40])
+
+
+@pytest.mark.parametrize("dtype", FORMATS)
+def test_config2_full_shapes(rq, orc, dtype):
+    """BASELINE config 2 at full size: M=1500 GEMMs and M in {1,5} GEMVs."""
+    from rusty_whisper_b200 import synth
+    for (k, n) in synth.SWEEP_SHAPES:
+        raw = synth.sweep_weight(dtype, k, n)
+        w = rq.QTensor([n, k], dtype, raw)
+        for m in (synth.ENCODER_M,) + synth.SWEEP_GEMV_M:
+            a = synth.sweep_acts(m, k)
+            y = host(rq.matmul_t_q(cuda(a), w))
+            ref = orc.matmul_t_q(a, dtype, raw, n)
+            assert close(y, ref) < TOL, (k, n, m)
