@@ -88,6 +88,20 @@ int rwq_matmul_t_q(const float* a, int64_t m, int64_t k, const rwq_qtensor* b, c
 int rwq_matmul_t_q_dev(const float* a, int64_t m, int64_t k, const rwq_qtensor* b, const float* bias, float* out,
                        int mode, void* stream);
 
+/* Activations quantized once and reused against several weights: the
+ * reference quantizes inside every matmul_t_q call (quant.rs:766); a
+ * caller that feeds one layernormed input to the Q, K and V projections
+ * (encoder.rs:130-141) can quantize it once.  Results are identical to
+ * rwq_matmul_t_q_dev on the same activations. */
+typedef struct rwq_qacts rwq_qacts;
+/* Device buffers for up to max_m rows of width k on the current device. */
+int rwq_qacts_new(int64_t max_m, int64_t k, rwq_qacts** out);
+int rwq_qacts_free(rwq_qacts* q);
+/* Quantize a[m, k] (device f32) into q; m <= max_m. */
+int rwq_qacts_quantize(rwq_qacts* q, const float* a, int64_t m, void* stream);
+/* out[m, n] = (quantized a) * dequant(b)^T (+ bias), device pointers. */
+int rwq_matmul_t_q_qacts(const rwq_qacts* q, const rwq_qtensor* b, const float* bias, float* out, void* stream);
+
 /* Dequantize rows `rows[0..nrows)` (device int32 indices; NULL = rows
  * 0..nrows-1) into out[nrows, k] (device), bit-identical to the
  * reference's scalar dequant.  Replaces `QTensor::row_f32` (quant.rs:566)
@@ -102,7 +116,7 @@ int rwq_row_f32(const rwq_qtensor* t, int64_t row, float* out);
 int rwq_quantize_acts_dev(const float* a, int64_t m, int64_t k, int8_t* q, float* d, int32_t* sum, void* stream);
 
 /* Per-block integer dots S[m][n][k/32] = sum q_a * q_b (centred weight
- * codes) from already-quantized activations (device pointers).  `path`
+ * codes) of f32 activations a[m, k] (device pointers).  `path`
  * 0 = the CUDA-core dp4a core used by the GEMV, 1 = the tensor-core GEMM
  * (values read back from tensor memory).  For bit-exact tests of the
  * integer core; no reference counterpart beyond quant.rs:1352-1360. */

@@ -36,6 +36,10 @@ SIGNATURES = {
     "rwq_row_f32": (_I, [_P, _L, _P]),
     "rwq_quantize_acts_dev": (_I, [_P, _L, _L, _P, _P, _P, _P]),
     "rwq_block_dots_dev": (_I, [_P, _L, _L, _P, _P, _I, _P]),
+    "rwq_qacts_new": (_I, [_L, _L, ctypes.POINTER(_P)]),
+    "rwq_qacts_free": (_I, [_P]),
+    "rwq_qacts_quantize": (_I, [_P, _P, _L, _P]),
+    "rwq_matmul_t_q_qacts": (_I, [_P, _P, _P, _P, _P]),
     "rwq_set_gemm_path": (_I, [_I]),
     "rwq_stream_check": (_I, [_P]),
 }

@@ -25,6 +25,15 @@ struct rwq_qtensor {
     std::mutex mu;
 };
 
+// Quantized activations that outlive one call (rwq_qacts_*).
+struct rwq_qacts {
+    int device = 0;
+    int max_m = 0, k = 0;
+    void* buf = nullptr;
+    rwq::ActsView v;       // valid rows: v.m
+    bool gemm = false;     // which operand layout the last quantize produced
+};
+
 namespace {
 
 thread_local std::string t_err;
@@ -164,6 +173,34 @@ int read_device_error(Workspace* ws, cudaStream_t s) {
     return RWQ_OK;
 }
 
+// Second half of a matmul: quantized activations `v` (GEMV layout, plus
+// the GEMM layout when `gemm`) against weight `b`.
+int run_quantized(const rwq::ActsView& v, bool gemm, rwq_qtensor* b, const float* bias, float* out, cudaStream_t s,
+                  int32_t* S_dump, int* err_flag) {
+    const rwq::Weight& w = b->w;
+    const int64_t m = v.m, k = v.k;
+    if (!gemm) {
+        const size_t smem = size_t(rwq::GEMV_MAX_M) * k + size_t(rwq::GEMV_MAX_M) * (k / 32) * 12;
+        if (smem > 200 * 1024) return fail(RWQ_ERR_ARG, "k=%lld too large for the GEMV kernel", (long long)k);
+        for (int64_t m0 = 0; m0 < m; m0 += rwq::GEMV_MAX_M) {
+            rwq::ActsView c = v;
+            c.m = int(m - m0 < rwq::GEMV_MAX_M ? m - m0 : rwq::GEMV_MAX_M);
+            c.q8 = v.q8 + m0 * k;
+            c.d = v.d + m0 * v.nb;
+            c.sum = v.sum + m0 * v.nb;
+            c.u = v.u + m0 * v.nb;
+            RWQ_CUDA(rwq::launch_gemv_i8(c, w, bias, out + m0 * w.n, s), "gemv_i8 launch");
+        }
+        return RWQ_OK;
+    }
+    int rc;
+    if ((rc = weight_gemm_cache(b, s))) return rc;
+    char why[256] = {0};
+    cudaError_t e = rwq::launch_gemm_tc(v, w, bias, out, S_dump, err_flag, s, why, sizeof why);
+    if (e != cudaSuccess) return fail(RWQ_ERR_CUDA, "gemm launch: %s %s", cudaGetErrorString(e), why);
+    return RWQ_OK;
+}
+
 // The core device-pointer matmul.  `S_dump` (tests) routes through the
 // GEMM and makes it write the per-block integer dots.
 int matmul_dev_impl(const float* a, int64_t m, int64_t k, rwq_qtensor* b, const float* bias, float* out, int mode,
@@ -191,25 +228,7 @@ int matmul_dev_impl(const float* a, int64_t m, int64_t k, rwq_qtensor* b, const 
     if ((rc = ensure_cap(ws, need))) return rc;
     acts_layout(int(m), int(k), gemm, &v, static_cast<uint8_t*>(ws->buf));
     RWQ_CUDA(rwq::launch_quantize_acts(a, v, gemm, s), "quantize launch");
-    if (!gemm) {
-        const size_t smem = size_t(rwq::GEMV_MAX_M) * k + size_t(rwq::GEMV_MAX_M) * (k / 32) * 12;
-        if (smem > 200 * 1024) return fail(RWQ_ERR_ARG, "k=%lld too large for the GEMV kernel", (long long)k);
-        for (int64_t m0 = 0; m0 < m; m0 += rwq::GEMV_MAX_M) {
-            rwq::ActsView c = v;
-            c.m = int(m - m0 < rwq::GEMV_MAX_M ? m - m0 : rwq::GEMV_MAX_M);
-            c.q8 = v.q8 + m0 * k;
-            c.d = v.d + m0 * v.nb;
-            c.sum = v.sum + m0 * v.nb;
-            c.u = v.u + m0 * v.nb;
-            RWQ_CUDA(rwq::launch_gemv_i8(c, w, bias, out + m0 * w.n, s), "gemv_i8 launch");
-        }
-        return RWQ_OK;
-    }
-    if ((rc = weight_gemm_cache(b, s))) return rc;
-    char why[256] = {0};
-    cudaError_t e = rwq::launch_gemm_tc(v, w, bias, out, S_dump, ws->err, s, why, sizeof why);
-    if (e != cudaSuccess) return fail(RWQ_ERR_CUDA, "gemm launch: %s %s", cudaGetErrorString(e), why);
-    return RWQ_OK;
+    return run_quantized(v, gemm, b, bias, out, s, S_dump, ws->err);
 }
 
 cudaStream_t thread_stream() {
@@ -466,6 +485,64 @@ int rwq_stream_check(void* stream) {
     int rc;
     if ((rc = get_workspace(s, &ws))) return rc;
     return read_device_error(ws, s);
+}
+
+int rwq_qacts_new(int64_t max_m, int64_t k, rwq_qacts** out) {
+    if (!out) return fail(RWQ_ERR_ARG, "out is null");
+    *out = nullptr;
+    if (max_m < 0 || max_m > (int64_t(1) << 30) || k <= 0 || k % rwq::QK || k > INT32_MAX)
+        return fail(RWQ_ERR_ARG, "bad qacts shape [%lld, %lld] (k %% 32 must be 0)", (long long)max_m, (long long)k);
+    auto* q = new rwq_qacts;
+    cudaGetDevice(&q->device);
+    q->max_m = int(max_m);
+    q->k = int(k);
+    const size_t bytes = acts_layout(q->max_m, q->k, true, &q->v, nullptr);
+    cudaError_t e = cudaMalloc(&q->buf, bytes ? bytes : 256);
+    if (e != cudaSuccess) {
+        delete q;
+        return cuda_fail(e, "cudaMalloc(qacts)");
+    }
+    q->v.m = 0;
+    *out = q;
+    return RWQ_OK;
+}
+
+int rwq_qacts_free(rwq_qacts* q) {
+    if (!q) return RWQ_OK;
+    int prev = 0;
+    cudaGetDevice(&prev);
+    if (prev != q->device) cudaSetDevice(q->device);
+    cudaFree(q->buf);
+    if (prev != q->device) cudaSetDevice(prev);
+    delete q;
+    return RWQ_OK;
+}
+
+int rwq_qacts_quantize(rwq_qacts* q, const float* a, int64_t m, void* stream) {
+    if (!q) return fail(RWQ_ERR_ARG, "qacts is null");
+    if (m < 0 || m > q->max_m) return fail(RWQ_ERR_ARG, "m=%lld outside [0, %d]", (long long)m, q->max_m);
+    if (m > 0 && !a) return fail(RWQ_ERR_ARG, "activations are null");
+    int path = t_gemm_path;
+    if (path == 0) path = (m <= rwq::GEMV_MAX_M) ? 1 : 2;
+    q->gemm = path == 2;
+    // Carve for the current m (row strides depend on m); the arena was
+    // sized for max_m in the GEMM layout, which is the larger one.
+    acts_layout(int(m), q->k, q->gemm, &q->v, static_cast<uint8_t*>(q->buf));
+    if (m == 0) return RWQ_OK;
+    RWQ_CUDA(rwq::launch_quantize_acts(a, q->v, q->gemm, static_cast<cudaStream_t>(stream)), "quantize launch");
+    return RWQ_OK;
+}
+
+int rwq_matmul_t_q_qacts(const rwq_qacts* q, const rwq_qtensor* b, const float* bias, float* out, void* stream) {
+    if (!q || !b) return fail(RWQ_ERR_ARG, "null qacts or weight");
+    if (q->k != b->w.k) return fail(RWQ_ERR_SHAPE, "matmul_t_q inner dims: %d vs %d", q->k, b->w.k);
+    if (q->v.m == 0 || b->w.n == 0) return RWQ_OK;
+    if (!out) return fail(RWQ_ERR_ARG, "out is null");
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    Workspace* ws = nullptr;
+    int rc;
+    if ((rc = get_workspace(s, &ws))) return rc;
+    return run_quantized(q->v, q->gemm, const_cast<rwq_qtensor*>(b), bias, out, s, nullptr, ws->err);
 }
 
 }  // extern "C"

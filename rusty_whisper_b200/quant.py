@@ -185,6 +185,60 @@ def matmul_t_q(a, b: QTensor, mode="int8", out=None, bias=None):
     return out
 
 
+class QActs:
+    """Activations quantized once and reused against several weights (the
+    Q/K/V projections of one layernormed input).  Same results as
+    ``matmul_t_q`` on the same activations."""
+
+    def __init__(self, max_m: int, k: int, device: int | None = None):
+        torch = _torch()
+        if k % QK:
+            raise ValueError(f"k must be a multiple of {QK}")
+        self.device = torch.cuda.current_device() if device is None else device
+        self.max_m, self.k, self.m = int(max_m), int(k), 0
+        h = ctypes.c_void_p()
+        with torch.cuda.device(self.device):
+            _lib.check(_lib.lib().rwq_qacts_new(self.max_m, self.k, ctypes.byref(h)))
+        self._h = h
+
+    def quantize(self, a) -> "QActs":
+        torch = _torch()
+        if not (isinstance(a, torch.Tensor) and a.is_cuda and a.dtype == torch.float32):
+            raise TypeError("QActs.quantize takes a CUDA float32 tensor")
+        if a.dim() != 2 or a.shape[1] != self.k:
+            raise ValueError(f"expected [m, {self.k}] activations, got {tuple(a.shape)}")
+        a = a.contiguous()
+        with torch.cuda.device(self.device):
+            _lib.check(_lib.lib().rwq_qacts_quantize(self._h, _ptr(a), a.shape[0], ctypes.c_void_p(_stream_ptr())))
+        self.m = int(a.shape[0])
+        return self
+
+    def matmul(self, b: "QTensor", out=None, bias=None):
+        torch = _torch()
+        if b.shape[1] != self.k:
+            raise ValueError(f"matmul_t_q inner dims: {self.k} vs {b.shape[1]}")
+        with torch.cuda.device(self.device):
+            if out is None:
+                out = torch.empty((self.m, b.shape[0]), dtype=torch.float32, device="cuda")
+            bp = _ptr(bias.contiguous()) if bias is not None else None
+            _lib.check(_lib.lib().rwq_matmul_t_q_qacts(self._h, b.handle, bp, _ptr(out),
+                                                       ctypes.c_void_p(_stream_ptr())))
+        return out
+
+    def free(self) -> None:
+        if getattr(self, "_h", None):
+            try:
+                _lib.lib().rwq_qacts_free(self._h)
+            finally:
+                self._h = None
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass
+
+
 def linear_w(x, w, b=None, mode="int8"):
     """``y = x W^T + b`` (quant.rs:1054) for a quantized ``W``."""
     if not isinstance(w, QTensor):

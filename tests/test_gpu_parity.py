@@ -192,3 +192,20 @@ def test_config2_full_shapes(rq, orc, dtype):
             y = host(rq.matmul_t_q(cuda(a), w))
             ref = orc.matmul_t_q(a, dtype, raw, n)
             assert close(y, ref) < TOL, (k, n, m)
+
+
+def test_qacts_reuse_matches_matmul(rq):
+    """One quantization reused against several weights gives the same bits
+    as separate matmul_t_q calls (GEMV and GEMM sizes)."""
+    import torch
+    from rusty_whisper_b200 import synth
+    k = 256
+    ws = [rq.QTensor([n, k], dt, synth.random_blocks(dt, n, k, 40 + dt)) for dt, n in ((2, 130), (7, 64), (8, 300))]
+    qa = rq.QActs(400, k)
+    for m in (1, 5, 8, 9, 400):
+        a = cuda(synth.normal(50 + m, m * k).reshape(m, k))
+        qa.quantize(a)
+        for w in ws:
+            assert torch.equal(qa.matmul(w), rq.matmul_t_q(a, w))
+    with pytest.raises(ValueError):
+        qa.quantize(torch.zeros((401, k), device="cuda"))
