@@ -1,0 +1,444 @@
+"""Benchmark of the B200 quantized-matmul path (BASELINE config 2 sweep).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+A step is one pass of the config-2 encoder sweep: for each of the three
+whisper-small shapes (K, N) in {(768,768), (768,3072), (3072,768)} the
+M=1500 activations are quantized once and multiplied by the five weight
+formats (Q4_0, Q4_1, Q5_0, Q5_1, Q8_0): 3 quantizer + 15 GEMM launches.
+`value` is whole-job throughput in TOPS (2*M*N*K per GEMM, inputs resident
+in HBM, L2 flushed before every timed step).  The decoder GEMVs of the same
+config (M in {1, 5}) are timed in the `gemv` object against HBM bandwidth,
+over rotating weight copies larger than L2.  `e2e` is the same sweep
+through the reference-shaped host-buffer entry point (rwq_matmul_t_q:
+host activations in, host outputs back, copies inside the timed region).
+
+Multi-GPU (torchrun): every rank runs its own sweep on its own windows'
+activations (weak scaling, no collective on the data path); the timed
+region is bracketed by barriers and the max over ranks is reported.
+
+`--impl reference` times the reference's CPU path (the C++ restatement in
+oracle/, rusty_whisper being Rust with no toolchain here) on the host
+cores, rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+from rusty_whisper_b200 import synth  # noqa: E402
+from rusty_whisper_b200.formats import NAMES, QK, block_bytes  # noqa: E402
+
+METRIC = "config-2 encoder quant-GEMM throughput (5 formats x whisper-small shapes, M=1500)"
+UNIT = "TOPS"
+WORKLOAD = ("BASELINE config 2: Q4_0/Q4_1/Q5_0/Q5_1/Q8_0 x (K,N) in {(768,768),(768,3072),(3072,768)}, "
+            "M=1500 GEMMs (int8 activation semantics); decoder GEMVs M in {1,5} reported under gemv")
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+def profile_traffic(name: str):
+    """dram bytes per launch recorded from an ncu capture (profiles/)."""
+    p = os.path.join(ROOT, "profiles", name)
+    if not os.path.exists(p):
+        return None
+    for line in open(p):
+        if line.startswith("dram_bytes_per_launch:"):
+            try:
+                return float(line.split(":", 1)[1].split()[0])
+            except ValueError:
+                return None
+    return None
+
+
+def sweep_inputs(rank: int):
+    """Seeded config-2 inputs; each rank processes its own activations."""
+    acts = {}
+    weights = {}
+    for (k, n) in synth.SWEEP_SHAPES:
+        acts[(k, n)] = synth.sweep_acts(synth.ENCODER_M, k, seed=rank)
+        for dt in synth.SWEEP_FORMATS:
+            weights[(dt, k, n)] = synth.sweep_weight(dt, k, n)
+    return acts, weights
+
+
+def gemm_ops():
+    return sum(2.0 * synth.ENCODER_M * n * k for (k, n) in synth.SWEEP_SHAPES) * len(synth.SWEEP_FORMATS)
+
+
+class Clocks:
+    """nvidia-smi sampling during the timed region."""
+    Q = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.p = None
+
+    def __enter__(self):
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                                       "-lms", "200", "-i", str(self.index)], stdout=subprocess.PIPE,
+                                      stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.p = None
+        return self
+
+    def __exit__(self, *exc):
+        self.rows = []
+        if self.p is None:
+            return False
+        self.p.terminate()
+        try:
+            out, _ = self.p.communicate(timeout=10)
+        except subprocess.TimeoutExpired:
+            self.p.kill()
+            out, _ = self.p.communicate()
+        for line in out.splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) >= 8:
+                self.rows.append(f)
+        return False
+
+    def summary(self):
+        rows = getattr(self, "rows", [])
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[0]) for r in rows if r[0].replace(".", "").isdigit()]
+        mx = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        reasons = set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            for nm, v in zip(names, r[4:8]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(rows)}
+
+
+# --------------------------------------------------------------- our arm
+def run_ours(args, rank, world, local_rank):
+    import torch
+    import torch.distributed as dist
+    from rusty_whisper_b200 import quant
+
+    torch.cuda.set_device(local_rank)
+    quant.init(local_rank)
+    dev = torch.device("cuda", local_rank)
+    hbm_peak, tc_peak, peak_kind = peaks()
+
+    acts_np, w_np = sweep_inputs(rank)
+    acts = {s: torch.from_numpy(a).to(dev) for s, a in acts_np.items()}
+    W = {key: quant.QTensor([key[2], key[1]], key[0], raw) for key, raw in w_np.items()}
+    for w in W.values():
+        w.prepare_gemm()
+    Y = {key: torch.empty((synth.ENCODER_M, key[2]), dtype=torch.float32, device=dev) for key in W}
+    qa = {s: quant.QActs(synth.ENCODER_M, s[0]) for s in synth.SWEEP_SHAPES}
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream()
+
+    def step(per_gemm=None):
+        for s in synth.SWEEP_SHAPES:
+            qa[s].quantize(acts[s])
+            for dt in synth.SWEEP_FORMATS:
+                key = (dt, s[0], s[1])
+                if per_gemm is not None:
+                    e0 = torch.cuda.Event(enable_timing=True)
+                    e1 = torch.cuda.Event(enable_timing=True)
+                    e0.record(stream)
+                    qa[s].matmul(W[key], out=Y[key])
+                    e1.record(stream)
+                    per_gemm.append((key, e0, e1))
+                else:
+                    qa[s].matmul(W[key], out=Y[key])
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    quant.stream_check()
+
+    # ---- timed region: K steps, flush L2 before each, events around each
+    steps = []
+    per_gemm = []
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with Clocks(local_rank) as clk:
+        for _ in range(args.steps):
+            flush.zero_()
+            torch.cuda._sleep(2_000_000)   # keep the GPU busy while the step is enqueued
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            step(per_gemm)
+            e1.record(stream)
+            steps.append((e0, e1))
+        torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    quant.stream_check()
+    t_steps = sum(a.elapsed_time(b) for a, b in steps) / 1e3      # seconds
+    t_gemm = sum(a.elapsed_time(b) for _, a, b in per_gemm) / 1e3
+    tmax = t_steps
+    if world > 1:
+        t = torch.tensor([t_steps], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        tmax = float(t.item())
+    ops_step = gemm_ops()
+    value = world * ops_step * args.steps / tmax / 1e12
+    gemm_tops = ops_step * args.steps / t_gemm / 1e12   # kernel-level, this rank
+
+    # per-format kernel numbers (this rank)
+    by_fmt = {}
+    for key, a, b in per_gemm:
+        dt, k, n = key
+        by_fmt.setdefault(NAMES[dt], [0.0, 0.0])
+        by_fmt[NAMES[dt]][0] += 2.0 * synth.ENCODER_M * n * k
+        by_fmt[NAMES[dt]][1] += a.elapsed_time(b) / 1e3
+    by_fmt = {f: round(o / t / 1e12, 2) for f, (o, t) in by_fmt.items()}
+
+    gemv = run_gemv(args, dev, quant, w_np, hbm_peak, stream) if args.only == "all" else None
+    e2e = run_e2e(args, dev, quant, W, acts_np, world) if args.only == "all" else None
+
+    if rank != 0:
+        return
+    line = {
+        "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": max(args.warmup, 3), "ms_per_step": round(tmax / args.steps * 1e3, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "int8 codes (exact on f16 tensor cores), f32 scales/accumulation",
+        "data": "synthetic (seeded SplitMix64; BASELINE config 2 distributions)",
+        "config": {"workload": WORKLOAD, "M": synth.ENCODER_M, "shapes_KN": list(synth.SWEEP_SHAPES),
+                   "formats": [NAMES[d] for d in synth.SWEEP_FORMATS], "parallelism": f"replicas x{world}",
+                   "l2": "256 MiB buffer written before every timed step (L2 126 MB)"},
+        "gpu_launches": 18 * args.steps,
+        "roofline": {
+            "bound": "tensor", "kernel": "k_gemm_tc (tcgen05 kind::f16, per-block TMEM epilogue)",
+            "achieved": round(gemm_tops, 2), "peak": tc_peak, "unit": "TFLOP/s",
+            "frac": round(gemm_tops / tc_peak, 4), "peak_kind": f"{peak_kind} dense bf16 (burst)",
+            "traffic": profile_traffic("gemm_tc_config2.txt"),
+            "per_format_tops": by_fmt,
+        },
+        "gemv": gemv,
+        "e2e": e2e,
+        "clocks": clk.summary(),
+    }
+    if world == 1 and not args.no_cpu:
+        line["cpu_baseline"] = cpu_baseline(acts_np, w_np)
+    print(json.dumps(line), flush=True)
+
+
+def run_gemv(args, dev, quant, w_np, hbm_peak, stream):
+    """Decoder GEMVs of config 2 over weight copies rotated past L2."""
+    import torch
+    total_w = sum(r.nbytes for r in w_np.values())
+    copies = max(2, int(np.ceil(300e6 / total_w)))
+    Wc = [{key: quant.QTensor([key[2], key[1]], key[0], raw) for key, raw in w_np.items()} for _ in range(copies)]
+    res = {}
+    for mm in synth.SWEEP_GEMV_M:
+        xs = {s: torch.from_numpy(synth.sweep_acts(mm, s[0], seed=9)).to(dev) for s in synth.SWEEP_SHAPES}
+        qa = {s: quant.QActs(mm, s[0]) for s in synth.SWEEP_SHAPES}
+        for s in synth.SWEEP_SHAPES:
+            qa[s].quantize(xs[s])
+        ys = {key: torch.empty((mm, key[2]), device=dev) for key in w_np}
+
+        def one(c, rec=None):
+            for key in w_np:
+                s = (key[1], key[2])
+                if rec is not None:
+                    e0 = torch.cuda.Event(enable_timing=True)
+                    e1 = torch.cuda.Event(enable_timing=True)
+                    e0.record(stream)
+                qa[s].matmul(Wc[c][key], out=ys[key])
+                if rec is not None:
+                    e1.record(stream)
+                    rec.append((key, e0, e1))
+
+        for c in range(copies):
+            one(c)
+        torch.cuda.synchronize()
+        rec = []
+        torch.cuda._sleep(2_000_000)
+        reps = max(args.steps, 4)
+        for r in range(reps):
+            one(r % copies, rec)
+        torch.cuda.synchronize()
+        nbytes = 0.0
+        t = 0.0
+        per_fmt = {}
+        for key, e0, e1 in rec:
+            dt, k, n = key
+            b = n * (k // QK) * block_bytes(dt) + 4.0 * mm * k + 4.0 * mm * n
+            dtm = e0.elapsed_time(e1) / 1e3
+            nbytes += b
+            t += dtm
+            pf = per_fmt.setdefault(NAMES[dt], [0.0, 0.0])
+            pf[0] += b
+            pf[1] += dtm
+        gbs = nbytes / t / 1e9
+        res[f"M={mm}"] = {"GB/s": round(gbs, 1), "frac_of_measured_hbm": round(gbs / hbm_peak, 4),
+                          "us_per_gemv": round(t / len(rec) * 1e6, 3),
+                          "per_format_GBs": {f: round(b / x / 1e9, 1) for f, (b, x) in per_fmt.items()}}
+    res["bound"] = "hbm"
+    res["peak_GBs"] = hbm_peak
+    res["bytes"] = "N*(K/32)*block_bytes + 4*M*K + 4*M*N per GEMV (algorithmic)"
+    res["l2"] = f"{copies} rotating weight copies ({copies * total_w / 1e6:.0f} MB > 126 MB L2)"
+    return res
+
+
+def run_e2e(args, dev, quant, W, acts_np, world):
+    """The sweep through the reference-shaped host-buffer entry point."""
+    import torch
+    import torch.distributed as dist
+    pinned_a = {s: torch.from_numpy(a).pin_memory() for s, a in acts_np.items()}
+    pinned_y = {key: torch.empty((synth.ENCODER_M, key[2]), dtype=torch.float32).pin_memory() for key in W}
+    h2d = d2h = 0
+
+    def step():
+        nonlocal h2d, d2h
+        h2d = d2h = 0
+        for key, w in W.items():
+            s = (key[1], key[2])
+            quant.matmul_t_q(pinned_a[s].numpy(), w, out=pinned_y[key].numpy())
+            h2d += pinned_a[s].numel() * 4
+            d2h += pinned_y[key].numel() * 4
+
+    for _ in range(2):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    torch.cuda.synchronize()
+    t = time.perf_counter() - t0
+    if world > 1:
+        tt = torch.tensor([t], dtype=torch.float64, device=dev)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        t = float(tt.item())
+    return {"value": round(world * gemm_ops() * args.steps / t / 1e12, 3), "unit": UNIT,
+            "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
+            "api": "rwq_matmul_t_q (host buffers, pinned), one call per GEMM, synchronous"}
+
+
+# --------------------------------------------------------- CPU baselines
+def cpu_sweep(acts_np, w_np, threads, budget_s, max_sweeps):
+    import oracle
+    oracle.lib()
+    t0 = time.perf_counter()
+    ops = 0.0
+    sweeps = 0
+    while sweeps < max_sweeps:
+        for (dt, k, n), raw in w_np.items():
+            a = acts_np[(k, n)]
+            oracle.matmul_t_q(a, dt, raw, n, tier=oracle.TIER_AUTO, threads=threads, packed=False)
+            ops += 2.0 * a.shape[0] * n * k
+        sweeps += 1
+        if time.perf_counter() - t0 > budget_s:
+            break
+    return ops / (time.perf_counter() - t0) / 1e12, sweeps
+
+
+def cpu_baseline(acts_np, w_np):
+    import oracle
+    oracle.lib()
+    threads = oracle.default_threads()
+    v, sweeps = cpu_sweep(acts_np, w_np, threads, budget_s=10.0, max_sweeps=3)
+    # one-thread figure on a one-GEMM sample
+    (dt, k, n), raw = next(iter(w_np.items()))
+    a = acts_np[(k, n)]
+    t0 = time.perf_counter()
+    oracle.matmul_t_q(a, dt, raw, n, tier=oracle.TIER_AUTO, threads=1, packed=False)
+    t1 = time.perf_counter() - t0
+    return {"value": round(v, 4), "unit": UNIT, "cores": threads, "kind": "port",
+            "tier": oracle.TIER_NAMES[oracle.dispatch_tier()],
+            "sample": f"{sweeps} full config-2 GEMM sweep(s) (15 GEMMs, M=1500), reference's first-call path, "
+                      f"{threads} threads over N-chunks",
+            "one_thread_value": round(2.0 * a.shape[0] * n * k / t1 / 1e12, 4),
+            "one_thread_sample": f"{NAMES[dt]} {a.shape[0]}x{k}x{n}",
+            "what": "C++ restatement of rusty_whisper's matmul_t_q (oracle/), the Rust original cannot be built here"}
+
+
+def run_reference(args, rank):
+    if rank != 0:
+        return
+    import oracle
+    acts_np, w_np = sweep_inputs(0)
+    oracle.lib()
+    threads = oracle.default_threads()
+    for _ in range(args.warmup):
+        cpu_sweep(acts_np, w_np, threads, budget_s=0.0, max_sweeps=1)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        cpu_sweep(acts_np, w_np, threads, budget_s=0.0, max_sweeps=1)
+    t = time.perf_counter() - t0
+    v = gemm_ops() * args.steps / t / 1e12
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(v, 4), "unit": UNIT, "n_gpus": 0,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(t / args.steps * 1e3, 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "int8 codes, f32 scales (AVX-512 VNNI / AVX2 tier)",
+        "data": "synthetic (seeded SplitMix64; BASELINE config 2 distributions)",
+        "config": {"workload": WORKLOAD, "M": synth.ENCODER_M, "shapes_KN": list(synth.SWEEP_SHAPES),
+                   "formats": [NAMES[d] for d in synth.SWEEP_FORMATS], "parallelism": "host threads"},
+        "cpu_baseline": {"value": round(v, 4), "unit": UNIT, "cores": threads, "kind": "port",
+                         "tier": oracle.TIER_NAMES[oracle.dispatch_tier()],
+                         "sample": "one full config-2 GEMM sweep per step (15 GEMMs, M=1500)"},
+        "e2e": {"value": round(v, 4), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--only", default="all", choices=["all", "gemm"],
+                    help="gemm: skip the GEMV and e2e legs (short runs for profiling)")
+    args = ap.parse_args()
+    rank = int(os.environ.get("RANK", 0))
+    world = int(os.environ.get("WORLD_SIZE", 1))
+    local_rank = int(os.environ.get("LOCAL_RANK", 0))
+    if args.impl == "reference":
+        run_reference(args, rank)
+        return
+    if world > 1:
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local_rank))
+    try:
+        run_ours(args, rank, world, local_rank)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.barrier()
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()
