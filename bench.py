@@ -41,6 +41,10 @@ from rusty_whisper_b200.formats import NAMES, QK, block_bytes  # noqa: E402
 
 METRIC = "config-2 encoder quant-GEMM throughput (5 formats x whisper-small shapes, M=1500)"
 UNIT = "TOPS"
+# A spin kernel this long (~2 ms) runs before each timed step so that the
+# host enqueues the whole step before the GPU reaches it: the CUDA events
+# then bracket device work only, with no host gaps inside.
+GATE_CYCLES = 4_000_000
 WORKLOAD = ("BASELINE config 2: Q4_0/Q4_1/Q5_0/Q5_1/Q8_0 x (K,N) in {(768,768),(768,3072),(3072,768)}, "
             "M=1500 GEMMs (int8 activation semantics); decoder GEMVs M in {1,5} reported under gemv")
 
@@ -95,7 +99,7 @@ class Clocks:
     def __enter__(self):
         try:
             self.p = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
-                                       "-lms", "200", "-i", str(self.index)], stdout=subprocess.PIPE,
+                                       "-lms", "50", "-i", str(self.index)], stdout=subprocess.PIPE,
                                       stderr=subprocess.DEVNULL, text=True)
         except OSError:
             self.p = None
@@ -180,10 +184,11 @@ def run_ours(args, rank, world, local_rank):
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
-    with Clocks(local_rank) as clk:
+    clk = Clocks(local_rank).__enter__()
+    if True:
         for _ in range(args.steps):
             flush.zero_()
-            torch.cuda._sleep(2_000_000)   # keep the GPU busy while the step is enqueued
+            torch.cuda._sleep(GATE_CYCLES)   # hold the GPU until the whole step is enqueued
             e0 = torch.cuda.Event(enable_timing=True)
             e1 = torch.cuda.Event(enable_timing=True)
             e0.record(stream)
@@ -216,6 +221,7 @@ def run_ours(args, rank, world, local_rank):
 
     gemv = run_gemv(args, dev, quant, w_np, hbm_peak, stream) if args.only == "all" else None
     e2e = run_e2e(args, dev, quant, W, acts_np, world) if args.only == "all" else None
+    clk.__exit__(None, None, None)
 
     if rank != 0:
         return
@@ -275,9 +281,9 @@ def run_gemv(args, dev, quant, w_np, hbm_peak, stream):
             one(c)
         torch.cuda.synchronize()
         rec = []
-        torch.cuda._sleep(2_000_000)
         reps = max(args.steps, 4)
         for r in range(reps):
+            torch.cuda._sleep(GATE_CYCLES)
             one(r % copies, rec)
         torch.cuda.synchronize()
         nbytes = 0.0
@@ -296,11 +302,44 @@ def run_gemv(args, dev, quant, w_np, hbm_peak, stream):
         res[f"M={mm}"] = {"GB/s": round(gbs, 1), "frac_of_measured_hbm": round(gbs / hbm_peak, 4),
                           "us_per_gemv": round(t / len(rec) * 1e6, 3),
                           "per_format_GBs": {f: round(b / x / 1e9, 1) for f, (b, x) in per_fmt.items()}}
+    res["logits_Q5_0_51865x1024"] = gemv_logits(args, dev, quant, hbm_peak, stream)
     res["bound"] = "hbm"
     res["peak_GBs"] = hbm_peak
     res["bytes"] = "N*(K/32)*block_bytes + 4*M*K + 4*M*N per GEMV (algorithmic)"
     res["l2"] = f"{copies} rotating weight copies ({copies * total_w / 1e6:.0f} MB > 126 MB L2)"
     return res
+
+
+def gemv_logits(args, dev, quant, hbm_peak, stream):
+    """BASELINE config 4's largest GEMV: tied logits, vocab 51865, d=1024,
+    Q5_0, M = 1 and 5 (beam), over 4 weight copies (146 MB > L2)."""
+    import torch
+    n, k, dt = 51865, 1024, 6
+    raw = synth.random_blocks(dt, n, k, 77)
+    Wl = [quant.QTensor([n, k], dt, raw) for _ in range(4)]
+    out = {}
+    for mm in (1, 5):
+        x = torch.from_numpy(synth.normal(78 + mm, mm * k).reshape(mm, k)).to(dev)
+        qa = quant.QActs(mm, k).quantize(x)
+        y = torch.empty((mm, n), device=dev)
+        for w in Wl:
+            qa.matmul(w, out=y)
+        torch.cuda.synchronize()
+        rec = []
+        for r in range(max(args.steps, 8)):
+            torch.cuda._sleep(GATE_CYCLES // 4)
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            qa.matmul(Wl[r % 4], out=y)
+            e1.record(stream)
+            rec.append((e0, e1))
+        torch.cuda.synchronize()
+        t = sum(a.elapsed_time(b) for a, b in rec) / 1e3 / len(rec)
+        b = n * (k // QK) * block_bytes(dt) + 4.0 * mm * k + 4.0 * mm * n
+        out[f"M={mm}"] = {"GB/s": round(b / t / 1e9, 1), "frac_of_measured_hbm": round(b / t / 1e9 / hbm_peak, 4),
+                          "us": round(t * 1e6, 2)}
+    return out
 
 
 def run_e2e(args, dev, quant, W, acts_np, world):

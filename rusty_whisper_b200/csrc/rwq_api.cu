@@ -181,7 +181,8 @@ int run_quantized(const rwq::ActsView& v, bool gemm, rwq_qtensor* b, const float
     const int64_t m = v.m, k = v.k;
     if (!gemm) {
         const size_t smem = size_t(rwq::GEMV_MAX_M) * k + size_t(rwq::GEMV_MAX_M) * (k / 32) * 12;
-        if (smem > 200 * 1024) return fail(RWQ_ERR_ARG, "k=%lld too large for the GEMV kernel", (long long)k);
+        if (smem > 200 * 1024 || k > 8192)
+            return fail(RWQ_ERR_ARG, "k=%lld too large for the GEMV kernel (max 8192)", (long long)k);
         for (int64_t m0 = 0; m0 < m; m0 += rwq::GEMV_MAX_M) {
             rwq::ActsView c = v;
             c.m = int(m - m0 < rwq::GEMV_MAX_M ? m - m0 : rwq::GEMV_MAX_M);

@@ -43,7 +43,12 @@ constexpr int THREADS = (2 + EPI_WARPS) * 32;
 constexpr int A_STAGE_BYTES = BM * BK * 2;   // 16 KiB
 constexpr int B_STAGE_BYTES = BN * BK * 2;   // 16 KiB
 constexpr int TMEM_COLS = NBUF * BN;         // 512
-constexpr int SMEM_BYTES = STAGES * (A_STAGE_BYTES + B_STAGE_BYTES) + 1024 /*align*/ + 256 /*barriers*/;
+// Per-quant-block scale rows staged by the producer: d_a[128 rows],
+// d_b[128 cols], u_a = d_a*sum(q_a) [128 rows], m_b[128 cols].
+constexpr int SC_SLOTS = 8;
+constexpr int SC_FLOATS = 4 * 128;
+constexpr int SC_BYTES = SC_SLOTS * SC_FLOATS * 4;  // 16 KiB
+constexpr int SMEM_BYTES = STAGES * (A_STAGE_BYTES + B_STAGE_BYTES) + SC_BYTES + 1024 /*align*/ + 512 /*barriers*/;
 constexpr long long WAIT_CYCLES = 4000000000LL;  // ~2 s at 1.9 GHz
 
 // Instruction descriptor, kind::f16: D f32 (bits 4-5 = 1), A/B f16
@@ -51,7 +56,7 @@ constexpr long long WAIT_CYCLES = 4000000000LL;  // ~2 s at 1.9 GHz
 constexpr uint32_t IDESC = (1u << 4) | (uint32_t(BN >> 3) << 17) | (uint32_t(BM >> 4) << 24);
 
 struct Smem {
-    uint64_t full[STAGES], empty[STAGES], acc_full[NBUF], acc_empty[NBUF];
+    uint64_t full[STAGES], empty[STAGES], acc_full[NBUF], acc_empty[NBUF], sc_full[SC_SLOTS], sc_empty[SC_SLOTS];
     uint32_t tmem_base;
     int abort;
 };
@@ -96,6 +101,14 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity, volatile
             }
         }
     }
+}
+
+// 1-D bulk copy global -> shared (16-byte aligned, size a multiple of 16).
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     smem_u32(dst)),
+                 "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
+                 : "memory");
 }
 
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
@@ -158,7 +171,8 @@ __global__ void __launch_bounds__(THREADS, 1)
     uint8_t* base = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     uint8_t* sA = base;
     uint8_t* sB = base + STAGES * A_STAGE_BYTES;
-    Smem* sm = reinterpret_cast<Smem*>(sB + STAGES * B_STAGE_BYTES);
+    float* sc_ring = reinterpret_cast<float*>(sB + STAGES * B_STAGE_BYTES);
+    Smem* sm = reinterpret_cast<Smem*>(sB + STAGES * B_STAGE_BYTES + SC_BYTES);
     volatile int* abort = &sm->abort;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -173,6 +187,10 @@ __global__ void __launch_bounds__(THREADS, 1)
         for (int b = 0; b < NBUF; ++b) {
             mbar_init(&sm->acc_full[b], 1);
             mbar_init(&sm->acc_empty[b], EPI_WARPS);
+        }
+        for (int c = 0; c < SC_SLOTS; ++c) {
+            mbar_init(&sm->sc_full[c], 1);
+            mbar_init(&sm->sc_empty[c], EPI_WARPS);
         }
         sm->abort = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -200,6 +218,26 @@ __global__ void __launch_bounds__(THREADS, 1)
                 mbar_expect_tx(&sm->full[s], A_STAGE_BYTES + B_STAGE_BYTES);
                 tma_load_2d(sA + s * A_STAGE_BYTES, &tmA, kt * BK, m0, &sm->full[s]);
                 tma_load_2d(sB + s * B_STAGE_BYTES, &tmB, kt * BK, n0, &sm->full[s]);
+                bool ok = true;
+                for (int j = 0; j < 2 && ok; ++j) {
+                    const int kb = 2 * kt + j;
+                    if (kb >= nb) break;
+                    const int c = kb % SC_SLOTS;
+                    const uint32_t cu = kb / SC_SLOTS;
+                    if (!mbar_wait(&sm->sc_empty[c], (cu & 1) ^ 1, abort, err_flag, 5)) {
+                        ok = false;
+                        break;
+                    }
+                    float* slot = sc_ring + c * SC_FLOATS;
+                    mbar_expect_tx(&sm->sc_full[c], HAS_MIN ? 2048u : 1024u);
+                    bulk_load(slot, daT + size_t(kb) * m_pad + m0, 512, &sm->sc_full[c]);
+                    bulk_load(slot + 128, dbT + size_t(kb) * n_pad + n0, 512, &sm->sc_full[c]);
+                    if (HAS_MIN) {
+                        bulk_load(slot + 256, uaT + size_t(kb) * m_pad + m0, 512, &sm->sc_full[c]);
+                        bulk_load(slot + 384, mbT + size_t(kb) * n_pad + n0, 512, &sm->sc_full[c]);
+                    }
+                }
+                if (!ok) break;
             }
         }
     } else if (warp == 1) {
@@ -245,7 +283,10 @@ __global__ void __launch_bounds__(THREADS, 1)
         for (int kb = 0; kb < nb; ++kb) {
             const int buf = kb % NBUF;
             const uint32_t use = kb / NBUF;
-            const bool got = mbar_wait(&sm->acc_full[buf], use & 1, abort, err_flag, 4);
+            const int c = kb % SC_SLOTS;
+            const uint32_t cu = kb / SC_SLOTS;
+            const bool got = mbar_wait(&sm->sc_full[c], cu & 1, abort, err_flag, 6) &&
+                             mbar_wait(&sm->acc_full[buf], use & 1, abort, err_flag, 4);
             if (!__all_sync(0xffffffffu, got)) break;  // keep the warp converged for tcgen05.ld
             tc_fence_after();
             uint32_t r[64];
@@ -257,19 +298,16 @@ __global__ void __launch_bounds__(THREADS, 1)
             __syncwarp();
             if (lane == 0) mbar_arrive(&sm->acc_empty[buf]);
 
-            const float da = __ldg(daT + size_t(kb) * m_pad + row);
+            const float* slot = sc_ring + c * SC_FLOATS;
+            const float da = slot[q * 32 + lane];
             const float2 da2 = make_float2(da, da);
-            const float4* db4 = reinterpret_cast<const float4*>(dbT + size_t(kb) * n_pad + col0);
-            float ua = 0.f;
-            const float4* mb4 = nullptr;
-            if (HAS_MIN) {
-                ua = __ldg(uaT + size_t(kb) * m_pad + row);
-                mb4 = reinterpret_cast<const float4*>(mbT + size_t(kb) * n_pad + col0);
-            }
+            const float4* db4 = reinterpret_cast<const float4*>(slot + 128 + h * 64);
+            const float ua = HAS_MIN ? slot[256 + q * 32 + lane] : 0.f;
+            const float4* mb4 = reinterpret_cast<const float4*>(slot + 384 + h * 64);
             const float2 ua2 = make_float2(ua, ua);
 #pragma unroll
             for (int c4 = 0; c4 < 16; ++c4) {
-                const float4 db = __ldg(db4 + c4);
+                const float4 db = db4[c4];
                 const uint32_t* rr = &r[c4 * 4];
                 const float2 s01 = __fmul2_rn(da2, make_float2(db.x, db.y));
                 const float2 s23 = __fmul2_rn(da2, make_float2(db.z, db.w));
@@ -277,7 +315,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                 acc[2 * c4 + 1] =
                     __ffma2_rn(s23, make_float2(__uint_as_float(rr[2]), __uint_as_float(rr[3])), acc[2 * c4 + 1]);
                 if (HAS_MIN) {
-                    const float4 mb = __ldg(mb4 + c4);
+                    const float4 mb = mb4[c4];
                     acc[2 * c4] = __ffma2_rn(ua2, make_float2(mb.x, mb.y), acc[2 * c4]);
                     acc[2 * c4 + 1] = __ffma2_rn(ua2, make_float2(mb.z, mb.w), acc[2 * c4 + 1]);
                 }
@@ -289,6 +327,8 @@ __global__ void __launch_bounds__(THREADS, 1)
                     }
                 }
             }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&sm->sc_empty[c]);
         }
         if (row < M && !*abort) {
             float* yr = Y + size_t(row) * N;

@@ -186,15 +186,52 @@ __global__ void k_block_dots(const uint8_t* __restrict__ qs, const uint32_t* __r
 }
 
 // -------------------------------------------------------------- GEMV i8
-// Decoder GEMV, M <= 8 activation rows.  Each warp owns 32/L weight rows,
-// L lanes per row; a lane walks its row's blocks kb = sub, sub+L, ... with
-// 128-bit loads of the code plane, unpacks nibbles / high bits in
-// registers, forms the exact integer block dot with dp4a, and accumulates
+// Undecoded block bytes, loaded one row group ahead of their use.
+template <int DT>
+struct RawBlock {
+    uint4 v0, v1;   // code bytes (v1: Q8_0 only)
+    uint32_t qh;
+    uint16_t d, m;
+};
+
+template <int DT>
+__device__ __forceinline__ void load_raw(const uint8_t* __restrict__ qs, const uint32_t* __restrict__ qh,
+                                         const uint16_t* __restrict__ dp, const uint16_t* __restrict__ mp, size_t b,
+                                         RawBlock<DT>& rb) {
+    if (DT == Q8_0) {
+        const uint4* p = reinterpret_cast<const uint4*>(qs + b * 32);
+        rb.v0 = __ldg(p);
+        rb.v1 = __ldg(p + 1);
+    } else {
+        rb.v0 = __ldg(reinterpret_cast<const uint4*>(qs + b * 16));
+    }
+    if (has_qh(DT)) rb.qh = __ldg(qh + b);
+    rb.d = __ldg(dp + b);
+    if (has_min(DT)) rb.m = __ldg(mp + b);
+}
+
+template <int DT>
+__device__ __forceinline__ void decode(const RawBlock<DT>& rb, BlockCodes<DT>& bc) {
+    if (DT == Q8_0) {
+        bc.w[0] = rb.v0.x; bc.w[1] = rb.v0.y; bc.w[2] = rb.v0.z; bc.w[3] = rb.v0.w;
+        bc.w[4] = rb.v1.x; bc.w[5] = rb.v1.y; bc.w[6] = rb.v1.z; bc.w[7] = rb.v1.w;
+    } else {
+        codes_u8x4<DT>(rb.v0, has_qh(DT) ? rb.qh : 0u, bc.w);
+    }
+    bc.d = h2f(rb.d);
+    bc.m = has_min(DT) ? h2f(rb.m) : 0.f;
+}
+
+// Decoder GEMV, M <= 8 activation rows.  Each warp owns 32/L weight rows
+// (a "row group"), L lanes per row; lane `sub` takes blocks kb = sub +
+// L*t, t < BPL.  A row group's code planes are read with 128-bit loads
+// one group ahead of use (the first group before the activations are
+// staged), nibbles and high bits are unpacked in registers, the exact
+// integer block dot comes from dp4a, and per block in kb order
 //     acc <- fma(d_a*d_b, S, acc);  acc <- fma(d_a*sum(q_a), m_b, acc)
-// per block in order.  The L partial sums are combined with an xor
-// butterfly.  Nothing in the order depends on M, so every output row is
-// bit-identical whatever the batch (quant.rs:1372-1384).
-template <int DT, int L, int MR>
+// before an xor butterfly over the L lanes.  L and BPL depend on K only,
+// so every output row is bit-identical whatever M (quant.rs:1372-1384).
+template <int DT, int L, int BPL, int MR>
 __global__ void __launch_bounds__(TPB) k_gemv_i8(const uint8_t* __restrict__ qs, const uint32_t* __restrict__ qh,
                                                  const uint16_t* __restrict__ dp, const uint16_t* __restrict__ mp,
                                                  const int8_t* __restrict__ q8, const float* __restrict__ da,
@@ -202,6 +239,24 @@ __global__ void __launch_bounds__(TPB) k_gemv_i8(const uint8_t* __restrict__ qs,
                                                  int N, int K, const float* __restrict__ bias, float* __restrict__ y) {
     extern __shared__ __align__(16) uint8_t smem[];
     const int nb = K / QK;
+    constexpr int RPW = 32 / L;
+    const int lane = threadIdx.x & 31, sub = lane % L, slot = lane / L;
+    const int warps_per_cta = blockDim.x >> 5;
+    const int nw = gridDim.x * warps_per_cta;
+    const int groups = (N + RPW - 1) / RPW;
+    int g = blockIdx.x * warps_per_cta + (threadIdx.x >> 5);
+
+    RawBlock<DT> cur[BPL];
+    auto fetch = [&](int grp, RawBlock<DT>(&dst)[BPL]) {
+        const int j = grp * RPW + slot;
+#pragma unroll
+        for (int t = 0; t < BPL; ++t) {
+            const int kb = sub + L * t;
+            if (j < N && kb < nb) load_raw<DT>(qs, qh, dp, mp, size_t(j) * nb + kb, dst[t]);
+        }
+    };
+    if (g < groups) fetch(g, cur);
+
     int8_t* s_q = reinterpret_cast<int8_t*>(smem);
     float* s_d = reinterpret_cast<float*>(smem + size_t(M) * K);
     float* s_u = s_d + M * nb;
@@ -217,20 +272,20 @@ __global__ void __launch_bounds__(TPB) k_gemv_i8(const uint8_t* __restrict__ qs,
         }
     }
     __syncthreads();
-    const int lane = threadIdx.x & 31, sub = lane % L, slot = lane / L;
-    constexpr int RPW = 32 / L;
-    const int warps_per_cta = blockDim.x >> 5;
-    const int gw = blockIdx.x * warps_per_cta + (threadIdx.x >> 5);
-    const int nw = gridDim.x * warps_per_cta;
-    for (int row0 = gw * RPW; row0 < N; row0 += nw * RPW) {
-        const int j = row0 + slot;
+
+    for (; g < groups; g += nw) {
+        RawBlock<DT> nxt[BPL];
+        if (g + nw < groups) fetch(g + nw, nxt);
+        const int j = g * RPW + slot;
         float acc[MR];
 #pragma unroll
         for (int r = 0; r < MR; ++r) acc[r] = 0.f;
-        if (j < N) {
-            for (int kb = sub; kb < nb; kb += L) {
+#pragma unroll
+        for (int t = 0; t < BPL; ++t) {
+            const int kb = sub + L * t;
+            if (j < N && kb < nb) {
                 BlockCodes<DT> bc;
-                load_block<DT>(qs, qh, dp, mp, size_t(j) * nb + kb, bc);
+                decode<DT>(cur[t], bc);
 #pragma unroll
                 for (int r = 0; r < MR; ++r) {
                     if (r < M) {
@@ -253,6 +308,8 @@ __global__ void __launch_bounds__(TPB) k_gemv_i8(const uint8_t* __restrict__ qs,
             for (int r = 0; r < MR; ++r)
                 if (r < M) y[size_t(r) * N + j] = bias ? __fadd_rn(acc[r], b) : acc[r];
         }
+#pragma unroll
+        for (int t = 0; t < BPL; ++t) cur[t] = nxt[t];
     }
 }
 
@@ -418,37 +475,41 @@ inline unsigned gemv_grid(int n, int L) {
     return g < 1 ? 1 : (g > cap ? cap : g);
 }
 
-template <int DT, int L, int MR>
+template <int DT, int L, int BPL, int MR>
 cudaError_t gemv_i8_launch(const ActsView& v, const Weight& w, const float* bias, float* y, cudaStream_t s) {
     const size_t smem = size_t(v.m) * v.k + size_t(v.m) * w.nb * 12;
-    static bool attr_set = false;  // one per instantiation
-    if (!attr_set) {
-        cudaError_t e = cudaFuncSetAttribute(k_gemv_i8<DT, L, MR>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    static int attr_dev_mask = 0;  // one bit per device with the attribute set
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (!(attr_dev_mask & (1 << dev))) {
+        cudaError_t e = cudaFuncSetAttribute(k_gemv_i8<DT, L, BPL, MR>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              200 * 1024);
         if (e != cudaSuccess) return e;
-        attr_set = true;
+        attr_dev_mask |= 1 << dev;
     }
-    k_gemv_i8<DT, L, MR><<<gemv_grid(w.n, L), TPB, smem, s>>>(w.qs, w.qh, w.d, w.m, v.q8, v.d, v.sum, v.u, v.m, w.n,
-                                                             w.k, bias, y);
+    k_gemv_i8<DT, L, BPL, MR><<<gemv_grid(w.n, L), TPB, smem, s>>>(w.qs, w.qh, w.d, w.m, v.q8, v.d, v.sum, v.u, v.m,
+                                                                   w.n, w.k, bias, y);
     return cudaGetLastError();
 }
 
-template <int DT, int L>
+template <int DT, int L, int BPL>
 cudaError_t gemv_i8_mr(const ActsView& v, const Weight& w, const float* bias, float* y, cudaStream_t s) {
-    if (v.m <= 1) return gemv_i8_launch<DT, L, 1>(v, w, bias, y, s);
-    if (v.m <= 2) return gemv_i8_launch<DT, L, 2>(v, w, bias, y, s);
-    if (v.m <= 4) return gemv_i8_launch<DT, L, 4>(v, w, bias, y, s);
-    return gemv_i8_launch<DT, L, 8>(v, w, bias, y, s);
+    if (v.m <= 1) return gemv_i8_launch<DT, L, BPL, 1>(v, w, bias, y, s);
+    if (v.m <= 4) return gemv_i8_launch<DT, L, BPL, 4>(v, w, bias, y, s);
+    return gemv_i8_launch<DT, L, BPL, 8>(v, w, bias, y, s);
 }
 
 template <int DT>
 struct GemvI8F {
     static cudaError_t run(const ActsView& v, const Weight& w, const float* bias, float* y, cudaStream_t s) {
-        switch (lanes_for(w.nb)) {
-            case 32: return gemv_i8_mr<DT, 32>(v, w, bias, y, s);
-            case 16: return gemv_i8_mr<DT, 16>(v, w, bias, y, s);
-            default: return gemv_i8_mr<DT, 8>(v, w, bias, y, s);
-        }
+        const int nb = w.nb;
+        if (nb <= 8) return gemv_i8_mr<DT, 8, 1>(v, w, bias, y, s);
+        if (nb <= 16) return gemv_i8_mr<DT, 8, 2>(v, w, bias, y, s);
+        if (nb <= 32) return gemv_i8_mr<DT, 32, 1>(v, w, bias, y, s);
+        if (nb <= 64) return gemv_i8_mr<DT, 32, 2>(v, w, bias, y, s);
+        if (nb <= 128) return gemv_i8_mr<DT, 32, 4>(v, w, bias, y, s);
+        if (nb <= 256) return gemv_i8_mr<DT, 32, 8>(v, w, bias, y, s);
+        return cudaErrorInvalidValue;
     }
 };
 
