@@ -123,6 +123,22 @@ int rwq_quantize_acts_dev(const float* a, int64_t m, int64_t k, int8_t* q, float
 int rwq_block_dots_dev(const float* a, int64_t m, int64_t k, const rwq_qtensor* b, int32_t* S, int path,
                        void* stream);
 
+/* Decoder-shaped int8 matmul that allocates no memory: out[m, n] =
+ * A[m, k] * dequant(b)^T (+ bias) with m <= 8 and k <= 8192, device
+ * pointers, asynchronous on `stream`, same results as rwq_matmul_t_q_dev.
+ * No counterpart in the reference.  For callers that may not allocate GPU
+ * memory: a live-microphone decode loop on a latency-critical thread
+ * (cudaMalloc/cudaFree can stall on an implicit device synchronization),
+ * or an embedder whose GPU memory belongs to another allocator.  Its
+ * scratch (the quantized activations, 88 KiB) is a fixed array that every
+ * GPU loading this library holds until exit.  The first call on a device
+ * looks up that array's device address; make that first call before any
+ * stream capture.  All calls share the one array: calls that overlap on
+ * the GPU (other streams, other host threads) race and must be ordered by
+ * the caller, e.g. on one stream.  Larger m or k returns RWQ_ERR_ARG. */
+int rwq_matmul_t_q_noalloc(const float* a, int64_t m, int64_t k, const rwq_qtensor* b, const float* bias,
+                           float* out, void* stream);
+
 /* Force the kernel family for matmuls with m > 8 (testing and
  * benchmarking): 0 = automatic, 1 = CUDA-core GEMV kernel in row chunks,
  * 2 = tensor-core GEMM.  Applies to this host thread. */

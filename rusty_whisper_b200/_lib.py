@@ -40,6 +40,7 @@ SIGNATURES = {
     "rwq_qacts_free": (_I, [_P]),
     "rwq_qacts_quantize": (_I, [_P, _P, _L, _P]),
     "rwq_matmul_t_q_qacts": (_I, [_P, _P, _P, _P, _P]),
+    "rwq_matmul_t_q_noalloc": (_I, [_P, _L, _L, _P, _P, _P, _P]),
     "rwq_set_gemm_path": (_I, [_I]),
     "rwq_stream_check": (_I, [_P]),
 }

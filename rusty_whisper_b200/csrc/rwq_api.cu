@@ -34,10 +34,18 @@ struct rwq_qacts {
     bool gemm = false;     // which operand layout the last quantize produced
 };
 
+const rwq::Weight& rwq::weight_of(const rwq_qtensor* t) { return t->w; }
+
 namespace {
 
 thread_local std::string t_err;
 thread_local int t_gemm_path = 0;
+
+}  // namespace
+
+void rwq::set_last_error(const char* msg) { t_err = msg; }
+
+namespace {
 
 int fail(int code, const char* fmt, ...) {
     char buf[512];

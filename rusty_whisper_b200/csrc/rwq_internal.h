@@ -51,3 +51,11 @@ cudaError_t launch_gemm_tc(const ActsView& v, const Weight& w, const float* bias
 constexpr int GEMV_MAX_M = 8;
 
 }  // namespace rwq
+
+struct rwq_qtensor;
+namespace rwq {
+// The device weight behind a C-ABI handle (defined in rwq_api.cu).
+const Weight& weight_of(const rwq_qtensor* t);
+// Set the text rwq_last_error() returns on this host thread.
+void set_last_error(const char* msg);
+}  // namespace rwq
