@@ -83,8 +83,9 @@ int rwq_matmul_t_q(const float* a, int64_t m, int64_t k, const rwq_qtensor* b, c
                    int mode);
 
 /* Device-pointer variant, asynchronous on `stream`: the perf path.
- * `a`, `bias`, `out` are device pointers.  Scratch comes from a
- * per-(device, stream) workspace owned by the library. */
+ * `a`, `bias`, `out` are device pointers (RWQ_MODE_F32 needs `a` 16-byte
+ * aligned).  Scratch comes from a per-(device, stream) workspace owned by
+ * the library. */
 int rwq_matmul_t_q_dev(const float* a, int64_t m, int64_t k, const rwq_qtensor* b, const float* bias, float* out,
                        int mode, void* stream);
 
@@ -103,7 +104,7 @@ int rwq_qacts_quantize(rwq_qacts* q, const float* a, int64_t m, void* stream);
 int rwq_matmul_t_q_qacts(const rwq_qacts* q, const rwq_qtensor* b, const float* bias, float* out, void* stream);
 
 /* Dequantize rows `rows[0..nrows)` (device int32 indices; NULL = rows
- * 0..nrows-1) into out[nrows, k] (device), bit-identical to the
+ * 0..nrows-1) into out[nrows, k] (device, 16-byte aligned), bit-identical to the
  * reference's scalar dequant.  Replaces `QTensor::row_f32` (quant.rs:566)
  * and, with rows = NULL and nrows = n, `to_dense` (quant.rs:572). */
 int rwq_dequant_rows_dev(const rwq_qtensor* t, const int32_t* rows, int64_t nrows, float* out, void* stream);
@@ -141,7 +142,10 @@ int rwq_matmul_t_q_noalloc(const float* a, int64_t m, int64_t k, const rwq_qtens
 
 /* Force the kernel family for matmuls with m > 8 (testing and
  * benchmarking): 0 = automatic, 1 = CUDA-core GEMV kernel in row chunks,
- * 2 = tensor-core GEMM.  Applies to this host thread. */
+ * 2 = tensor-core GEMM with the weight scales folded into the operand
+ * (the automatic choice), 3 = tensor-core GEMM that forms each block's
+ * integer dot exactly and scales it on the CUDA cores.  Applies to this
+ * host thread. */
 int rwq_set_gemm_path(int path);
 
 /* Synchronize `stream` and report any fault a kernel recorded on it. */

@@ -159,6 +159,18 @@ int weight_gemm_cache(rwq_qtensor* t, cudaStream_t s) {
     return RWQ_OK;
 }
 
+int weight_fold_cache(rwq_qtensor* t, cudaStream_t s) {
+    std::lock_guard<std::mutex> g(t->mu);
+    rwq::Weight& w = t->w;
+    if (w.fold_ready) return RWQ_OK;
+    RWQ_CUDA(cudaMalloc(&w.bhl, size_t(w.n) * w.nb * 64 * 2 + 16), "cudaMalloc(bhl)");
+    RWQ_CUDA(cudaMalloc(&w.colscale, size_t((w.n + 255) / 256 * 256) * 4), "cudaMalloc(colscale)");
+    RWQ_CUDA(rwq::launch_build_fold_cache(w, s), "build fold cache");
+    RWQ_CUDA(cudaStreamSynchronize(s), "cudaStreamSynchronize(fold cache)");
+    w.fold_ready = true;
+    return RWQ_OK;
+}
+
 int check_matmul_args(const float* a, int64_t m, int64_t k, const rwq_qtensor* b, const float* out, int mode) {
     if (!b) return fail(RWQ_ERR_ARG, "weight is null");
     if (m < 0 || k <= 0) return fail(RWQ_ERR_ARG, "bad shape m=%lld k=%lld", (long long)m, (long long)k);
@@ -203,8 +215,14 @@ int run_quantized(const rwq::ActsView& v, bool gemm, rwq_qtensor* b, const float
         return RWQ_OK;
     }
     int rc;
-    if ((rc = weight_gemm_cache(b, s))) return rc;
     char why[256] = {0};
+    if (!S_dump && t_gemm_path != 3) {
+        if ((rc = weight_fold_cache(b, s))) return rc;
+        cudaError_t e = rwq::launch_gemm_fold(v, w, bias, out, err_flag, s, why, sizeof why);
+        if (e != cudaSuccess) return fail(RWQ_ERR_CUDA, "gemm launch: %s %s", cudaGetErrorString(e), why);
+        return RWQ_OK;
+    }
+    if ((rc = weight_gemm_cache(b, s))) return rc;
     cudaError_t e = rwq::launch_gemm_tc(v, w, bias, out, S_dump, err_flag, s, why, sizeof why);
     if (e != cudaSuccess) return fail(RWQ_ERR_CUDA, "gemm launch: %s %s", cudaGetErrorString(e), why);
     return RWQ_OK;
@@ -219,6 +237,8 @@ int matmul_dev_impl(const float* a, int64_t m, int64_t k, rwq_qtensor* b, const 
     if (m == 0 || b->w.n == 0) return RWQ_OK;
     const rwq::Weight& w = b->w;
     if (mode == RWQ_MODE_F32) {
+        if (reinterpret_cast<uintptr_t>(a) & 15)
+            return fail(RWQ_ERR_ARG, "f32 mode needs 16-byte aligned device activations");
         for (int64_t m0 = 0; m0 < m; m0 += rwq::GEMV_MAX_M) {
             const int mc = int(m - m0 < rwq::GEMV_MAX_M ? m - m0 : rwq::GEMV_MAX_M);
             RWQ_CUDA(rwq::launch_gemv_f32(a + m0 * k, mc, w, bias, out + m0 * w.n, s), "gemv_f32 launch");
@@ -227,7 +247,7 @@ int matmul_dev_impl(const float* a, int64_t m, int64_t k, rwq_qtensor* b, const 
     }
     int path = force_path ? force_path : t_gemm_path;
     if (path == 0) path = (m <= rwq::GEMV_MAX_M) ? 1 : 2;
-    const bool gemm = path == 2;
+    const bool gemm = path >= 2;
     if (gemm && (k * 2) % 16) return fail(RWQ_ERR_ARG, "k*2 bytes must be a multiple of 16 for the GEMM");
     Workspace* ws = nullptr;
     if ((rc = get_workspace(s, &ws))) return rc;
@@ -350,6 +370,8 @@ int rwq_qtensor_free(rwq_qtensor* t) {
     cudaFree(w.q16);
     cudaFree(w.dT);
     cudaFree(w.mT);
+    cudaFree(w.bhl);
+    cudaFree(w.colscale);
     if (prev != w.device) cudaSetDevice(prev);
     delete t;
     return RWQ_OK;
@@ -405,6 +427,7 @@ int rwq_dequant_rows_dev(const rwq_qtensor* t, const int32_t* rows, int64_t nrow
     if (!t) return fail(RWQ_ERR_ARG, "weight is null");
     if (nrows < 0 || (nrows > 0 && !out)) return fail(RWQ_ERR_ARG, "bad output");
     if (!rows && nrows > t->w.n) return fail(RWQ_ERR_ARG, "nrows %lld > n %d", (long long)nrows, t->w.n);
+    if (reinterpret_cast<uintptr_t>(out) & 15) return fail(RWQ_ERR_ARG, "dequant output must be 16-byte aligned");
     RWQ_CUDA(rwq::launch_dequant_rows(t->w, rows, int(nrows), out, static_cast<cudaStream_t>(stream)), "dequant launch");
     return RWQ_OK;
 }
@@ -481,7 +504,7 @@ int rwq_block_dots_dev(const float* a, int64_t m, int64_t k, const rwq_qtensor* 
 }
 
 int rwq_set_gemm_path(int path) {
-    if (path < 0 || path > 2) return fail(RWQ_ERR_ARG, "path must be 0, 1 or 2");
+    if (path < 0 || path > 3) return fail(RWQ_ERR_ARG, "path must be 0, 1, 2 or 3");
     t_gemm_path = path;
     return RWQ_OK;
 }
@@ -533,7 +556,7 @@ int rwq_qacts_quantize(rwq_qacts* q, const float* a, int64_t m, void* stream) {
     if (m > 0 && !a) return fail(RWQ_ERR_ARG, "activations are null");
     int path = t_gemm_path;
     if (path == 0) path = (m <= rwq::GEMV_MAX_M) ? 1 : 2;
-    q->gemm = path == 2;
+    q->gemm = path >= 2;
     // Carve for the current m (row strides depend on m); the arena was
     // sized for max_m in the GEMM layout, which is the larger one.
     acts_layout(int(m), q->k, q->gemm, &q->v, static_cast<uint8_t*>(q->buf));

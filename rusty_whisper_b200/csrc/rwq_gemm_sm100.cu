@@ -32,9 +32,12 @@
 #include <mutex>
 #include "rwq_common.cuh"
 #include "rwq_internal.h"
+#include "rwq_sm100.cuh"
 
 namespace rwq {
 namespace {
+
+using namespace tc;
 
 constexpr int BM = 128, BN = 128, BK = 64;  // BK f16 elements = 128 bytes per row per stage
 constexpr int STAGES = 4, NBUF = 4;
@@ -49,7 +52,6 @@ constexpr int SC_SLOTS = 8;
 constexpr int SC_FLOATS = 4 * 128;
 constexpr int SC_BYTES = SC_SLOTS * SC_FLOATS * 4;  // 16 KiB
 constexpr int SMEM_BYTES = STAGES * (A_STAGE_BYTES + B_STAGE_BYTES) + SC_BYTES + 1024 /*align*/ + 512 /*barriers*/;
-constexpr long long WAIT_CYCLES = 4000000000LL;  // ~2 s at 1.9 GHz
 
 // Instruction descriptor, kind::f16: D f32 (bits 4-5 = 1), A/B f16
 // (bits 7-12 = 0), both K-major, N>>3 at bits 17-22, M>>4 at bits 24-28.
@@ -61,76 +63,6 @@ struct Smem {
     int abort;
 };
 
-__device__ __forceinline__ uint32_t smem_u32(const void* p) { return uint32_t(__cvta_generic_to_shared(p)); }
-
-__device__ __forceinline__ void mbar_init(uint64_t* b, uint32_t count) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(b)), "r"(count) : "memory");
-}
-
-__device__ __forceinline__ void mbar_arrive(uint64_t* b) {
-    asm volatile("{ .reg .b64 st; mbarrier.arrive.shared::cta.b64 st, [%0]; }" ::"r"(smem_u32(b)) : "memory");
-}
-
-__device__ __forceinline__ void mbar_expect_tx(uint64_t* b, uint32_t bytes) {
-    asm volatile("{ .reg .b64 st; mbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1; }" ::"r"(smem_u32(b)),
-                 "r"(bytes)
-                 : "memory");
-}
-
-// Bounded parity wait.  Returns false if the kernel is aborting.
-__device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity, volatile int* abort, int* err_flag,
-                                          int code) {
-    const uint32_t addr = smem_u32(b);
-    long long t0 = 0;
-    for (uint32_t it = 0;; ++it) {
-        uint32_t ok;
-        asm volatile(
-            "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
-            : "=r"(ok)
-            : "r"(addr), "r"(parity)
-            : "memory");
-        if (ok) return true;
-        if ((it & 255u) == 0) {
-            if (*abort) return false;
-            const long long now = clock64();
-            if (it == 0) t0 = now;
-            else if (now - t0 > WAIT_CYCLES) {
-                *abort = 1;
-                if (err_flag) atomicCAS(err_flag, 0, code);
-                return false;
-            }
-        }
-    }
-}
-
-// 1-D bulk copy global -> shared (16-byte aligned, size a multiple of 16).
-__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
-    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-                     smem_u32(dst)),
-                 "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
-                 : "memory");
-}
-
-__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
-            "r"(smem_u32(dst)),
-        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
-        : "memory");
-}
-
-// Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row core
-// groups 1024 bytes apart (SBO), LBO 16 bytes (unused by this layout),
-// descriptor version 1 (bits 46-47), layout type 2 = SWIZZLE_128B.
-__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
-    uint64_t d = uint64_t((saddr & 0x3FFFFu) >> 4);
-    d |= uint64_t(16 >> 4) << 16;
-    d |= uint64_t(1024 >> 4) << 32;
-    d |= uint64_t(1) << 46;
-    d |= uint64_t(2) << 61;
-    return d;
-}
-
 __device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
     asm volatile(
         "{ .reg .pred p; setp.ne.b32 p, %4, 0; tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p; }" ::"r"(
@@ -138,27 +70,6 @@ __device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t adesc, uint64_
         "l"(adesc), "l"(bdesc), "r"(IDESC), "r"(accumulate)
         : "memory");
 }
-
-__device__ __forceinline__ void mma_commit(uint64_t* bar) {
-    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
-                 : "memory");
-}
-
-__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t* r) {
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
-          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
-          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-        : "r"(taddr));
-}
-
-__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
 template <bool HAS_MIN, bool DUMP>
 __global__ void __launch_bounds__(THREADS, 1)
@@ -332,7 +243,8 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
         if (row < M && !*abort) {
             float* yr = Y + size_t(row) * N;
-            const bool vec = (N % 4 == 0) && (col0 + 64 <= N);
+            const bool vec = (N % 4 == 0) && (col0 + 64 <= N) && (reinterpret_cast<uintptr_t>(Y) & 15) == 0 &&
+                             (reinterpret_cast<uintptr_t>(bias) & 15) == 0;
             if (vec) {
 #pragma unroll
                 for (int c4 = 0; c4 < 16; ++c4) {

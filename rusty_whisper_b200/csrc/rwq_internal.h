@@ -21,6 +21,12 @@ struct Weight {
     float* mT = nullptr;       // [nb][n_pad] m as f32, transposed (min formats)
     int n_pad = 0;
     bool gemm_ready = false;
+    // folded-scale tensor-core operand (built on first use): per row and
+    // block, 32 f16 "hi" then 32 f16 "lo" of x*2^e_j (x = d*q + m), and
+    // colscale[j] = 2^-e_j ([n_pad], zero padded).
+    uint16_t* bhl = nullptr;   // [n][nb][64]
+    float* colscale = nullptr;
+    bool fold_ready = false;
 };
 
 // Scratch for one activation quantization (quantize_acts_i8 output).
@@ -38,6 +44,7 @@ struct ActsView {
 // ---- launchers (return a cudaError_t of the launch) ----
 cudaError_t launch_repack(const uint8_t* raw, Weight& w, cudaStream_t s);
 cudaError_t launch_build_gemm_cache(Weight& w, cudaStream_t s);
+cudaError_t launch_build_fold_cache(Weight& w, cudaStream_t s);
 cudaError_t launch_quantize_acts(const float* a, const ActsView& v, bool want_gemm, cudaStream_t s);
 cudaError_t launch_dequant_rows(const Weight& w, const int32_t* rows, int nrows, float* out, cudaStream_t s);
 cudaError_t launch_block_dots(const ActsView& v, const Weight& w, int32_t* S, cudaStream_t s);
@@ -47,6 +54,10 @@ cudaError_t launch_gemv_f32(const float* a, int m, const Weight& w, const float*
 // integer dots read back from tensor memory.
 cudaError_t launch_gemm_tc(const ActsView& v, const Weight& w, const float* bias, float* y, int32_t* S_dump,
                            int* err_flag, cudaStream_t s, char* why, size_t why_len);
+
+// tcgen05 GEMM with the weight scales folded into the B operand.
+cudaError_t launch_gemm_fold(const ActsView& v, const Weight& w, const float* bias, float* y, int* err_flag,
+                             cudaStream_t s, char* why, size_t why_len);
 
 constexpr int GEMV_MAX_M = 8;
 

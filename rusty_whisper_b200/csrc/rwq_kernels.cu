@@ -406,6 +406,65 @@ __global__ void k_build_gemm_cache(const uint8_t* __restrict__ qs, const uint32_
     if (mT) mT[size_t(bl) * n_pad + j] = bc.m;
 }
 
+// ------------------------------------------------- folded-scale operand
+// One warp per weight row j: x = d*q + m for every element (the
+// reference's dequant, bit-exact), e_j so that max|x|*2^e_j lies in
+// [2^10, 2^11), then x*2^e_j (exact) = hi + lo in f16.  Rows n..n_pad-1
+// get colscale 0.
+template <int DT>
+__global__ void k_build_fold_cache(const uint8_t* __restrict__ qs, const uint32_t* __restrict__ qh,
+                                   const uint16_t* __restrict__ dp, const uint16_t* __restrict__ mp, int n, int nb,
+                                   int n_pad, uint16_t* __restrict__ bhl, float* __restrict__ colscale) {
+    const int lane = threadIdx.x & 31;
+    const int j = int((size_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5);
+    if (j >= n_pad) return;
+    if (j >= n) {
+        if (lane == 0) colscale[j] = 0.f;
+        return;
+    }
+    float mx = 0.f;
+    for (int kb = lane; kb < nb; kb += 32) {
+        BlockCodes<DT> bc;
+        load_block<DT>(qs, qh, dp, mp, size_t(j) * nb + kb, bc);
+#pragma unroll
+        for (int e = 0; e < QK; ++e) {
+            const float x = __fadd_rn(__fmul_rn(bc.d, float(code_at<DT>(bc.w, e))), bc.m);
+            mx = fmaxf(mx, fabsf(x));
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    int ex = 0;
+    if (mx > 0.f && isfinite(mx)) {
+        int E;
+        frexpf(mx, &E);          // mx = f * 2^E, f in [0.5, 1)
+        ex = 11 - E;             // mx * 2^ex in [2^10, 2^11)
+        ex = max(-120, min(120, ex));
+    }
+    const float up = ldexpf(1.0f, ex);
+    for (int kb = lane; kb < nb; kb += 32) {
+        BlockCodes<DT> bc;
+        load_block<DT>(qs, qh, dp, mp, size_t(j) * nb + kb, bc);
+        uint32_t hi2[16], lo2[16];
+#pragma unroll
+        for (int e = 0; e < QK; e += 2) {
+            const float x0 = __fmul_rn(__fadd_rn(__fmul_rn(bc.d, float(code_at<DT>(bc.w, e))), bc.m), up);
+            const float x1 = __fmul_rn(__fadd_rn(__fmul_rn(bc.d, float(code_at<DT>(bc.w, e + 1))), bc.m), up);
+            const __half h0 = __float2half_rn(x0), h1 = __float2half_rn(x1);
+            const __half l0 = __float2half_rn(__fsub_rn(x0, __half2float(h0)));
+            const __half l1 = __float2half_rn(__fsub_rn(x1, __half2float(h1)));
+            hi2[e / 2] = uint32_t(__half_as_ushort(h0)) | (uint32_t(__half_as_ushort(h1)) << 16);
+            lo2[e / 2] = uint32_t(__half_as_ushort(l0)) | (uint32_t(__half_as_ushort(l1)) << 16);
+        }
+        uint4* o = reinterpret_cast<uint4*>(bhl + (size_t(j) * nb + kb) * 64);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) o[i] = make_uint4(hi2[4 * i], hi2[4 * i + 1], hi2[4 * i + 2], hi2[4 * i + 3]);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) o[4 + i] = make_uint4(lo2[4 * i], lo2[4 * i + 1], lo2[4 * i + 2], lo2[4 * i + 3]);
+    }
+    if (lane == 0) colscale[j] = ldexpf(1.0f, -ex);
+}
+
 // ------------------------------------------------------------ dispatch
 template <template <int> class F, typename... Args>
 cudaError_t by_dtype(int dt, Args&&... args) {
@@ -445,6 +504,17 @@ struct BlockDotsF {
         size_t work = size_t(v.m) * w.n * w.nb;
         if (!work) return cudaSuccess;
         k_block_dots<DT><<<grid_for(work, TPB), TPB, 0, s>>>(w.qs, w.qh, w.d, w.m, v.q8, v.sum, v.m, w.n, w.nb, S);
+        return cudaGetLastError();
+    }
+};
+
+template <int DT>
+struct FoldCacheF {
+    static cudaError_t run(Weight& w, cudaStream_t s) {
+        const int np = (w.n + 255) / 256 * 256;  // colscale is allocated to this length
+        const size_t threads = size_t(np) * 32;
+        k_build_fold_cache<DT><<<grid_for(threads, TPB), TPB, 0, s>>>(w.qs, w.qh, w.d, w.m, w.n, w.nb, np, w.bhl,
+                                                                      w.colscale);
         return cudaGetLastError();
     }
 };
@@ -543,6 +613,8 @@ struct GemvF32F {
 cudaError_t launch_repack(const uint8_t* raw, Weight& w, cudaStream_t s) { return by_dtype<RepackF>(w.dtype, raw, w, s); }
 
 cudaError_t launch_build_gemm_cache(Weight& w, cudaStream_t s) { return by_dtype<GemmCacheF>(w.dtype, w, s); }
+
+cudaError_t launch_build_fold_cache(Weight& w, cudaStream_t s) { return by_dtype<FoldCacheF>(w.dtype, w, s); }
 
 cudaError_t launch_quantize_acts(const float* a, const ActsView& v, bool want_gemm, cudaStream_t s) {
     const int m_pad = want_gemm ? v.m_pad : v.m;

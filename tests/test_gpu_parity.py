@@ -209,3 +209,71 @@ def test_qacts_reuse_matches_matmul(rq):
             assert torch.equal(qa.matmul(w), rq.matmul_t_q(a, w))
     with pytest.raises(ValueError):
         qa.quantize(torch.zeros((401, k), device="cuda"))
+
+
+@pytest.mark.parametrize("dtype", FORMATS)
+def test_exact_integer_gemm_path_matches_oracle(rq, orc, dtype):
+    """Path 3: the tensor-core GEMM that forms every block's integer dot
+    exactly and scales it on the CUDA cores."""
+    m, k, n = 300, 768, 520
+    a, raw = _case(dtype, m, k, n, 17 * dtype)
+    w = rq.QTensor([n, k], dtype, raw)
+    rq.set_gemm_path(3)
+    try:
+        y3 = host(rq.matmul_t_q(cuda(a), w))
+    finally:
+        rq.set_gemm_path(0)
+    y2 = host(rq.matmul_t_q(cuda(a), w))
+    ref = orc.matmul_t_q(a, dtype, raw, n)
+    assert close(y3, ref) < TOL
+    assert close(y2, ref) < TOL
+
+
+@pytest.mark.parametrize("dtype", FORMATS)
+def test_extreme_block_scales(rq, orc, dtype):
+    """Rows whose f16 scales span huge, tiny and subnormal values: the
+    folded-scale GEMM normalises each row by a power of two."""
+    m, k, n = 150, 256, 64
+    a, raw = _case(dtype, m, k, n, 23 * dtype)
+    bb = orc.block_bytes(dtype)
+    blocks = raw.reshape(-1, bb).copy()
+    nb = k // 32
+    for j in range(n):
+        h = [0x6400, 0x5BFF, 0x0400, 0x0010, 0x3C00, 0x1400][j % 6]   # 1024, 255.9, 6.1e-5, 9.5e-7 (subnormal), 1, 2^-6
+        for bl in range(nb):
+            blocks[j * nb + bl, 0] = h & 0xFF
+            blocks[j * nb + bl, 1] = h >> 8
+    raw = blocks.reshape(-1)
+    w = rq.QTensor([n, k], dtype, raw)
+    y = host(rq.matmul_t_q(cuda(a), w))
+    # The scalar int8 oracle is the reference's own tight check
+    # (quant.rs:1336-1370).  At these magnitudes the VNNI tier's -128*sum(q_b)
+    # offset loses f32 digits by cancellation, so it is not used here.
+    assert close(y, orc.int8_scalar_matmul(a, dtype, raw, n)) < TOL
+
+
+def test_unaligned_device_pointers(rq, orc):
+    """Bias and output buffers offset by one float (4-byte aligned only)."""
+    import torch
+    from rusty_whisper_b200 import synth
+    for m in (5, 200):
+        dtype, k, n = 6, 256, 384
+        a, raw = _case(dtype, m, k, n, 31 + m)
+        w = rq.QTensor([n, k], dtype, raw)
+        bias_buf = torch.from_numpy(synth.normal(9, n + 1)).cuda()
+        bias = bias_buf[1:]
+        out_buf = torch.empty(m * n + 1, device="cuda")
+        out = out_buf[1:].view(m, n)
+        rq.matmul_t_q(cuda(a), w, out=out, bias=bias)
+        ref = orc.matmul_t_q(a, dtype, raw, n) + bias.cpu().numpy()[None, :]
+        assert close(host(out), ref) < TOL
+    rq.set_gemm_path(3)
+    try:
+        out_buf = torch.empty(200 * n + 1, device="cuda")
+        out = out_buf[1:].view(200, n)
+        a, raw = _case(6, 200, 256, n, 77)
+        w = rq.QTensor([n, 256], 6, raw)
+        rq.matmul_t_q(cuda(a), w, out=out, bias=bias)
+        assert close(host(out), orc.matmul_t_q(a, 6, raw, n) + bias.cpu().numpy()[None, :]) < TOL
+    finally:
+        rq.set_gemm_path(0)
