@@ -236,7 +236,7 @@ def run_ours(args, rank, world, local_rank):
                    "l2": "256 MiB buffer written before every timed step (L2 126 MB)"},
         "gpu_launches": 18 * args.steps,
         "roofline": {
-            "bound": "tensor", "kernel": "k_gemm_tc (tcgen05 kind::f16, per-block TMEM epilogue)",
+            "bound": "tensor", "kernel": "k_gemm_fold (tcgen05 kind::f16, scales folded into an f16 hi|lo weight operand)",
             "achieved": round(gemm_tops, 2), "peak": tc_peak, "unit": "TFLOP/s",
             "frac": round(gemm_tops / tc_peak, 4), "peak_kind": f"{peak_kind} dense bf16 (burst)",
             "traffic": profile_traffic("gemm_tc_config2.txt"),

@@ -15,14 +15,16 @@
 // in an f32 TMEM buffer; the epilogue does acc <- fma(d_a, T, acc) with
 // packed f32x2 math, and finally y = acc * 2^-e_j (+ bias).
 //
-// Roles (320 threads, one CTA per 128 x BN output tile, BN = 128 or 256):
-//   warp 0     TMA producer: A (q_a f16, two blocks = 64 K per stage),
-//              B (hi|lo rows, 64 f16 per block), both 128-byte swizzled,
-//              and a 1-D bulk copy of the block's d_a row into a shared
-//              ring; allocates / frees the 512 TMEM columns.
-//   warp 1     MMA issuer (one thread), NBUF = 512/BN accumulator buffers.
+// Roles (320 threads, one CTA per 128 x 128 output tile):
+//   warp 0     TMA producer: per pair of blocks one stage with A (q_a
+//              f16, 128 x 64) and B (two 128-row hi|lo tiles), 128-byte
+//              swizzled, plus 1-D bulk copies of the pair's d_a rows into a
+//              shared ring; allocates / frees the 512 TMEM columns.
+//   warp 1     MMA issuer (one thread): 8 MMAs per pair into a pair of
+//              TMEM buffers, then one commit to the pair's accumulator
+//              barrier and one to the stage's empty barrier.
 //   warps 2-9  epilogue: warp w reads TMEM lanes 32*(w%4).., columns
-//              (w-2)/4 * BN/2 .. + BN/2, 64 per round trip; at the end it
+//              (w-2)/4 * 64 .. + 64 of each block; at the end it
 //              scales, adds the bias, stages its 32-row block in shared
 //              memory (the drained B ring) and writes it with TMA stores,
 //              which clip the ragged M and N edges.
@@ -42,61 +44,56 @@ namespace {
 using namespace tc;
 
 constexpr int BM = 128;
-constexpr int SA = 3;                      // A stages, two 32-wide blocks each (128-byte swizzle)
-constexpr int SB = 4;                      // B stages, one block each
+constexpr int BN = 128;
+// The MMA-issuing thread is the critical resource: the tensor pipe only
+// queues about one MMA ahead, so every barrier wait or commit between
+// MMAs idles it.  Work is therefore handled in pairs of 32-wide blocks:
+// one stage (A: 128 rows x 64 f16, B: two 128-row hi|lo tiles) per pair,
+// one full/empty barrier per stage, and TMEM buffers used in pairs, so an
+// iteration is 2 waits + 8 MMAs + 2 commits.
+constexpr int STAGES = 4;                  // 8 blocks in flight
 constexpr int EPI_WARPS = 8;
 constexpr int THREADS = (2 + EPI_WARPS) * 32;
-constexpr int A_STAGE = BM * 64 * 2;       // 16 KiB: 128 rows x 64 f16
-constexpr int SC_SLOTS = 8;                // d_a rows, 128 floats each
+constexpr int A_BYTES = BM * 64 * 2;       // 16 KiB
+constexpr int B_BYTES = BN * 64 * 2;       // 16 KiB per block (32 hi + 32 lo f16 per row)
+constexpr int STAGE_BYTES = A_BYTES + 2 * B_BYTES;
+constexpr int SC_SLOTS = 8;                // d_a rows for a pair of blocks: 2 x 128 floats
+constexpr int NPAIR = 2;                   // TMEM: 2 pairs x 2 blocks x 128 columns = 512
 constexpr int TMEM_COLS = 512;
-
-template <int BN>
-struct Cfg {
-    static constexpr int B_STAGE = BN * 64 * 2;      // BN rows x (32 hi + 32 lo) f16
-    static constexpr int NBUF = TMEM_COLS / BN;
-    static constexpr int CPW = BN / 2;               // output columns per epilogue warp
-    static constexpr int SMEM = SB * B_STAGE + SA * A_STAGE + SC_SLOTS * 512 + 1024 + 512;
-    // kind::f16, D f32, A/B f16, K-major, N>>3 at bit 17, M>>4 at bit 24.
-    static constexpr uint32_t IDESC = (1u << 4) | (uint32_t(BN >> 3) << 17) | (uint32_t(BM >> 4) << 24);
-    // The output staging (one 32 x CPW f32 block per epilogue warp) reuses the B ring.
-    static_assert(EPI_WARPS * 32 * CPW * 4 <= SB * B_STAGE, "staging must fit in the B ring");
-};
+constexpr int CPW = BN / 2;                // output columns per epilogue warp
+// kind::f16, D f32, A/B f16, K-major, N>>3 at bit 17, M>>4 at bit 24.
+constexpr uint32_t IDESC = (1u << 4) | (uint32_t(BN >> 3) << 17) | (uint32_t(BM >> 4) << 24);
 
 struct Bars {
-    uint64_t fullA[SA], emptyA[SA], fullB[SB], emptyB[SB], acc_full[4], acc_empty[4], sc_full[SC_SLOTS],
-        sc_empty[SC_SLOTS];
+    uint64_t full[STAGES], empty[STAGES], acc_full[NPAIR], acc_empty[NPAIR], sc_full[SC_SLOTS], sc_empty[SC_SLOTS];
     uint32_t tmem_base;
     int abort;
 };
+constexpr int SMEM = STAGES * STAGE_BYTES + SC_SLOTS * 1024 + int(sizeof(Bars)) + 1024;
+static_assert(SMEM <= 227 * 1024, "shared memory budget");
+static_assert(EPI_WARPS * 32 * CPW * 4 <= STAGES * STAGE_BYTES, "output staging must fit in the stages");
 
-template <int BN>
 __global__ void __launch_bounds__(THREADS, 1)
     k_gemm_fold(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                 const __grid_constant__ CUtensorMap tmY, int use_tma_store, const float* __restrict__ daT,
                 const float* __restrict__ colscale, const float* __restrict__ bias, float* __restrict__ Y, int M,
                 int N, int nb, int m_pad, int* __restrict__ err_flag) {
-    using C = Cfg<BN>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* base = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
-    uint8_t* sB = base;                                   // all stages 1024-aligned (128-byte swizzle)
-    uint8_t* sA = base + SB * C::B_STAGE;
-    float* ring = reinterpret_cast<float*>(sA + SA * A_STAGE);
-    Bars* bar = reinterpret_cast<Bars*>(reinterpret_cast<uint8_t*>(ring) + SC_SLOTS * 512);
+    float* ring = reinterpret_cast<float*>(base + STAGES * STAGE_BYTES);
+    Bars* bar = reinterpret_cast<Bars*>(reinterpret_cast<uint8_t*>(ring) + SC_SLOTS * 1024);
     volatile int* abort = &bar->abort;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int n0 = blockIdx.x * BN, m0 = blockIdx.y * BM;
+    const int npairs = (nb + 1) / 2;
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < SA; ++s) {
-            mbar_init(&bar->fullA[s], 1);
-            mbar_init(&bar->emptyA[s], 1);
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(&bar->full[s], 1);
+            mbar_init(&bar->empty[s], 1);
         }
-        for (int s = 0; s < SB; ++s) {
-            mbar_init(&bar->fullB[s], 1);
-            mbar_init(&bar->emptyB[s], 1);
-        }
-        for (int b = 0; b < C::NBUF; ++b) {
+        for (int b = 0; b < NPAIR; ++b) {
             mbar_init(&bar->acc_full[b], 1);
             mbar_init(&bar->acc_empty[b], EPI_WARPS);
         }
@@ -124,92 +121,91 @@ __global__ void __launch_bounds__(THREADS, 1)
         if (lane == 0) {
             asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmA)) : "memory");
             asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmB)) : "memory");
-            for (int kb = 0; kb < nb; ++kb) {
-                if ((kb & 1) == 0) {
-                    const int t = kb >> 1, s = t % SA;
-                    if (!mbar_wait(&bar->emptyA[s], ((t / SA) & 1) ^ 1, abort, err_flag, 1)) break;
-                    mbar_expect_tx(&bar->fullA[s], A_STAGE);
-                    tma_load_2d(sA + s * A_STAGE, &tmA, kb * 32, m0, &bar->fullA[s]);
-                }
-                const int s = kb % SB;
-                if (!mbar_wait(&bar->emptyB[s], ((kb / SB) & 1) ^ 1, abort, err_flag, 1)) break;
-                mbar_expect_tx(&bar->fullB[s], C::B_STAGE);
-                tma_load_2d(sB + s * C::B_STAGE, &tmB, kb * 64, n0, &bar->fullB[s]);
-                const int c = kb % SC_SLOTS;
-                if (!mbar_wait(&bar->sc_empty[c], ((kb / SC_SLOTS) & 1) ^ 1, abort, err_flag, 5)) break;
-                mbar_expect_tx(&bar->sc_full[c], 512);
-                bulk_load(ring + c * 128, daT + size_t(kb) * m_pad + m0, 512, &bar->sc_full[c]);
+            for (int pr = 0; pr < npairs; ++pr) {
+                const int s = pr % STAGES;
+                if (!mbar_wait(&bar->empty[s], ((pr / STAGES) & 1) ^ 1, abort, err_flag, 1)) break;
+                uint8_t* st = base + s * STAGE_BYTES;
+                mbar_expect_tx(&bar->full[s], STAGE_BYTES);
+                tma_load_2d(st, &tmA, pr * 64, m0, &bar->full[s]);                        // blocks 2pr, 2pr+1
+                tma_load_2d(st + A_BYTES, &tmB, pr * 128, n0, &bar->full[s]);             // block 2pr
+                tma_load_2d(st + A_BYTES + B_BYTES, &tmB, pr * 128 + 64, n0, &bar->full[s]);  // block 2pr+1
+                const int c = pr % SC_SLOTS;
+                if (!mbar_wait(&bar->sc_empty[c], ((pr / SC_SLOTS) & 1) ^ 1, abort, err_flag, 5)) break;
+                const int two = (2 * pr + 1 < nb) ? 2 : 1;
+                mbar_expect_tx(&bar->sc_full[c], 512u * two);
+                for (int j = 0; j < two; ++j)
+                    bulk_load(ring + c * 256 + j * 128, daT + size_t(2 * pr + j) * m_pad + m0, 512, &bar->sc_full[c]);
             }
         }
     } else if (warp == 1) {
         if (lane == 0) {
-            for (int kb = 0; kb < nb; ++kb) {
-                const int t = kb >> 1, sa = t % SA, sb = kb % SB;
-                if ((kb & 1) == 0 && !mbar_wait(&bar->fullA[sa], (t / SA) & 1, abort, err_flag, 2)) break;
-                if (!mbar_wait(&bar->fullB[sb], (kb / SB) & 1, abort, err_flag, 2)) break;
-                const int buf = kb % C::NBUF;
-                if (!mbar_wait(&bar->acc_empty[buf], ((kb / C::NBUF) & 1) ^ 1, abort, err_flag, 3)) break;
+            for (int pr = 0; pr < npairs; ++pr) {
+                const int s = pr % STAGES, p = pr % NPAIR;
+                if (!mbar_wait(&bar->full[s], (pr / STAGES) & 1, abort, err_flag, 2)) break;
+                if (!mbar_wait(&bar->acc_empty[p], ((pr / NPAIR) & 1) ^ 1, abort, err_flag, 3)) break;
                 tc_fence_after();
-                const uint32_t a0 = smem_u32(sA + sa * A_STAGE) + uint32_t((kb & 1) * 64);
-                const uint32_t b0 = smem_u32(sB + sb * C::B_STAGE);
-                const uint32_t d = tmem + uint32_t(buf * BN);
-                // K half 0: A bytes +0..31, B hi +0..31, lo +64..95;
-                // K half 1: A bytes +32..63, B hi +32..63, lo +96..127.
-                mma_f16_id(d, sw128_desc(a0), sw128_desc(b0), C::IDESC, 0);
-                mma_f16_id(d, sw128_desc(a0), sw128_desc(b0 + 64), C::IDESC, 1);
-                mma_f16_id(d, sw128_desc(a0 + 32), sw128_desc(b0 + 32), C::IDESC, 1);
-                mma_f16_id(d, sw128_desc(a0 + 32), sw128_desc(b0 + 96), C::IDESC, 1);
-                mma_commit(&bar->acc_full[buf]);
-                mma_commit(&bar->emptyB[sb]);
-                if ((kb & 1) == 1 || kb == nb - 1) mma_commit(&bar->emptyA[sa]);
+                const uint32_t a0 = smem_u32(base + s * STAGE_BYTES);
+#pragma unroll
+                for (int j = 0; j < 2; ++j) {
+                    if (2 * pr + j >= nb) break;
+                    const uint32_t a = a0 + uint32_t(j * 64);
+                    const uint32_t b = a0 + uint32_t(A_BYTES + j * B_BYTES);
+                    const uint32_t d = tmem + uint32_t(p * 2 * BN + j * BN);
+                    // K half 0: A bytes +0..31, B hi +0..31, lo +64..95;
+                    // K half 1: A bytes +32..63, B hi +32..63, lo +96..127.
+                    mma_f16_id(d, sw128_desc(a), sw128_desc(b), IDESC, 0);
+                    mma_f16_id(d, sw128_desc(a), sw128_desc(b + 64), IDESC, 1);
+                    mma_f16_id(d, sw128_desc(a + 32), sw128_desc(b + 32), IDESC, 1);
+                    mma_f16_id(d, sw128_desc(a + 32), sw128_desc(b + 96), IDESC, 1);
+                }
+                mma_commit(&bar->acc_full[p]);
+                mma_commit(&bar->empty[s]);
             }
         }
     } else {
         const int q = warp & 3;
         const int h = (warp - 2) >> 2;
-        constexpr int CPW = C::CPW;
         float2 acc[CPW / 2];
 #pragma unroll
         for (int c = 0; c < CPW / 2; ++c) acc[c] = make_float2(0.f, 0.f);
-        for (int kb = 0; kb < nb; ++kb) {
-            const int buf = kb % C::NBUF;
-            const int c = kb % SC_SLOTS;
-            const bool got = mbar_wait(&bar->sc_full[c], (kb / SC_SLOTS) & 1, abort, err_flag, 6) &&
-                             mbar_wait(&bar->acc_full[buf], (kb / C::NBUF) & 1, abort, err_flag, 4);
+        for (int pr = 0; pr < npairs; ++pr) {
+            const int p = pr % NPAIR, c = pr % SC_SLOTS;
+            const bool got = mbar_wait(&bar->sc_full[c], (pr / SC_SLOTS) & 1, abort, err_flag, 6) &&
+                             mbar_wait(&bar->acc_full[p], (pr / NPAIR) & 1, abort, err_flag, 4);
             if (!__all_sync(0xffffffffu, got)) break;
             tc_fence_after();
-            const float da = ring[c * 128 + q * 32 + lane];
-            const float2 da2 = make_float2(da, da);
-            const uint32_t taddr = tmem + (uint32_t(q * 32) << 16) + uint32_t(buf * BN + h * CPW);
-            // 64 columns per TMEM round trip.
 #pragma unroll
-            for (int ch = 0; ch < CPW / 64; ++ch) {
+            for (int j = 0; j < 2; ++j) {
+                if (2 * pr + j >= nb) break;
+                const float da = ring[c * 256 + j * 128 + q * 32 + lane];
+                const float2 da2 = make_float2(da, da);
+                const uint32_t taddr = tmem + (uint32_t(q * 32) << 16) + uint32_t(p * 2 * BN + j * BN + h * CPW);
                 uint32_t r[64];
-                tmem_ld32(taddr + ch * 64, r);
-                tmem_ld32(taddr + ch * 64 + 32, r + 32);
+                tmem_ld32(taddr, r);
+                tmem_ld32(taddr + 32, r + 32);
                 tmem_wait_ld();
 #pragma unroll
                 for (int i = 0; i < 32; ++i)
-                    acc[ch * 32 + i] =
-                        __ffma2_rn(da2, make_float2(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1])),
-                                   acc[ch * 32 + i]);
+                    acc[i] = __ffma2_rn(da2, make_float2(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1])),
+                                        acc[i]);
             }
             tc_fence_before();
             __syncwarp();
             if (lane == 0) {
-                mbar_arrive(&bar->acc_empty[buf]);
+                mbar_arrive(&bar->acc_empty[p]);
                 mbar_arrive(&bar->sc_empty[c]);
             }
         }
         // y = acc * 2^-e_j (+ bias), written through shared memory.
         const int col0 = n0 + h * CPW;
-        const bool bias_vec = (reinterpret_cast<uintptr_t>(bias) & 15) == 0;
         const int row = m0 + q * 32 + lane;
+        const bool bias_vec = (reinterpret_cast<uintptr_t>(bias) & 15) == 0;
         if (!*abort) {
             if (use_tma_store) {
-                // Staging for this warp: CPW/32 boxes of 32 rows x 128 bytes,
-                // 128-byte swizzle (16-byte chunk c of row r at c ^ (r & 7)).
-                uint8_t* stg = sB + (warp - 2) * (32 * CPW * 4);
+                // Staging for this warp (in the drained stage ring): CPW/32
+                // boxes of 32 rows x 128 bytes, 128-byte swizzle (16-byte
+                // chunk c of row r at c ^ (r & 7)).
+                uint8_t* stg = base + (warp - 2) * (32 * CPW * 4);
 #pragma unroll
                 for (int b = 0; b < CPW / 32; ++b) {
                     uint8_t* box = stg + b * 4096 + lane * 128;
@@ -297,9 +293,8 @@ bool encode_map(CUtensorMap* map, CUtensorMapDataType dt, int esize, const void*
     return true;
 }
 
-template <int BN>
-cudaError_t launch_bn(const ActsView& v, const Weight& w, const float* bias, float* y, int* err_flag,
-                      cudaStream_t s, char* why, size_t why_len) {
+cudaError_t launch_fold(const ActsView& v, const Weight& w, const float* bias, float* y, int* err_flag,
+                        cudaStream_t s, char* why, size_t why_len) {
     CUtensorMap ma, mb, my;
     if (!encode_map(&ma, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, v.q16, uint64_t(v.k), uint64_t(v.m), 64, BM,
                     CU_TENSOR_MAP_SWIZZLE_128B, why, why_len))
@@ -313,18 +308,17 @@ cudaError_t launch_bn(const ActsView& v, const Weight& w, const float* bias, flo
                                      CU_TENSOR_MAP_SWIZZLE_128B, why, why_len))
         use_tma_store = 0;
     if (!use_tma_store) memset(&my, 0, sizeof my);
-    auto kern = k_gemm_fold<BN>;
     static int attr_dev_mask = 0;
     int dev = 0;
     cudaGetDevice(&dev);
     if (!(attr_dev_mask & (1 << dev))) {
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<BN>::SMEM);
+        cudaError_t e = cudaFuncSetAttribute(k_gemm_fold, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
         if (e != cudaSuccess) return e;
         attr_dev_mask |= 1 << dev;
     }
     dim3 grid((w.n + BN - 1) / BN, (v.m + BM - 1) / BM);
-    kern<<<grid, THREADS, Cfg<BN>::SMEM, s>>>(ma, mb, my, use_tma_store, v.dT, w.colscale, bias, y, v.m, w.n, w.nb,
-                                              v.m_pad, err_flag);
+    k_gemm_fold<<<grid, THREADS, SMEM, s>>>(ma, mb, my, use_tma_store, v.dT, w.colscale, bias, y, v.m, w.n, w.nb,
+                                            v.m_pad, err_flag);
     return cudaGetLastError();
 }
 
@@ -333,10 +327,7 @@ cudaError_t launch_bn(const ActsView& v, const Weight& w, const float* bias, flo
 cudaError_t launch_gemm_fold(const ActsView& v, const Weight& w, const float* bias, float* y, int* err_flag,
                              cudaStream_t s, char* why, size_t why_len) {
     if (v.m <= 0 || w.n <= 0) return cudaSuccess;
-    // 256-wide tiles for wide outputs.  The choice depends on N only, so a
-    // row's result never depends on M.
-    if (w.n >= 2304) return launch_bn<256>(v, w, bias, y, err_flag, s, why, why_len);
-    return launch_bn<128>(v, w, bias, y, err_flag, s, why, why_len);
+    return launch_fold(v, w, bias, y, err_flag, s, why, why_len);
 }
 
 }  // namespace rwq

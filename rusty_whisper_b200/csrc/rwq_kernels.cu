@@ -224,44 +224,58 @@ __device__ __forceinline__ void decode(const RawBlock<DT>& rb, BlockCodes<DT>& b
 
 // Decoder GEMV, M <= 8 activation rows.  Each warp owns 32/L weight rows
 // (a "row group"), L lanes per row; lane `sub` takes blocks kb = sub +
-// L*t, t < BPL.  A row group's code planes are read with 128-bit loads
-// one group ahead of use (the first group before the activations are
-// staged), nibbles and high bits are unpacked in registers, the exact
-// integer block dot comes from dp4a, and per block in kb order
+// L*t, t < BPL.  Because a lane always visits the same blocks, its
+// activation codes and scales for those blocks are loaded into registers
+// once.  Weight blocks are read with 128-bit loads of the code plane, PF
+// row groups ahead of use; nibbles and high bits are unpacked in
+// registers.  The dp4a chain starts from the bits of 1.5*2^23 (minus the
+// Q4_0/Q5_0 code offset times sum(q_a)), so for |S| < 2^22 its result is
+// the f32 1.5*2^23 + S exactly and S = bits - 1.5*2^23 is one FADD.  Per
+// block, in kb order,
 //     acc <- fma(d_a*d_b, S, acc);  acc <- fma(d_a*sum(q_a), m_b, acc)
-// before an xor butterfly over the L lanes.  L and BPL depend on K only,
-// so every output row is bit-identical whatever M (quant.rs:1372-1384).
-template <int DT, int L, int BPL, int MR>
+// then an xor butterfly over the L lanes.  L and BPL depend on K only, so
+// every output row is bit-identical whatever M (quant.rs:1372-1384).
+constexpr uint32_t MAGIC_BITS = 0x4B400000u;  // 12582912.0f
+constexpr float MAGIC_F = 12582912.0f;
+
+template <int DT, int L, int BPL, int MR, int PF, bool REGA>
 __global__ void __launch_bounds__(TPB) k_gemv_i8(const uint8_t* __restrict__ qs, const uint32_t* __restrict__ qh,
                                                  const uint16_t* __restrict__ dp, const uint16_t* __restrict__ mp,
                                                  const int8_t* __restrict__ q8, const float* __restrict__ da,
                                                  const int32_t* __restrict__ sa, const float* __restrict__ ua, int M,
                                                  int N, int K, const float* __restrict__ bias, float* __restrict__ y) {
-    extern __shared__ __align__(16) uint8_t smem[];
     const int nb = K / QK;
     constexpr int RPW = 32 / L;
     const int lane = threadIdx.x & 31, sub = lane % L, slot = lane / L;
     const int warps_per_cta = blockDim.x >> 5;
     const int nw = gridDim.x * warps_per_cta;
     const int groups = (N + RPW - 1) / RPW;
-    int g = blockIdx.x * warps_per_cta + (threadIdx.x >> 5);
+    const int g0 = blockIdx.x * warps_per_cta + (threadIdx.x >> 5);
 
-    RawBlock<DT> cur[BPL];
+    RawBlock<DT> ring[PF][BPL];
     auto fetch = [&](int grp, RawBlock<DT>(&dst)[BPL]) {
         const int j = grp * RPW + slot;
 #pragma unroll
         for (int t = 0; t < BPL; ++t) {
             const int kb = sub + L * t;
-            if (j < N && kb < nb) load_raw<DT>(qs, qh, dp, mp, size_t(j) * nb + kb, dst[t]);
+            if (grp < groups && j < N && kb < nb) load_raw<DT>(qs, qh, dp, mp, size_t(j) * nb + kb, dst[t]);
         }
     };
-    if (g < groups) fetch(g, cur);
+#pragma unroll
+    for (int u = 0; u < PF; ++u) fetch(g0 + u * nw, ring[u]);
 
+    // This lane's activation blocks, for every row: in registers when they
+    // are few (REGA), else staged once per CTA in shared memory.
+    constexpr int TB = REGA ? BPL : 1, TR = REGA ? MR : 1;
+    int4 a0[TB][TR], a1[TB][TR];
+    float ad[TB][TR], au[TB][TR];
+    uint32_t init[TB][TR];
+    extern __shared__ __align__(16) uint8_t smem[];
     int8_t* s_q = reinterpret_cast<int8_t*>(smem);
     float* s_d = reinterpret_cast<float*>(smem + size_t(M) * K);
     float* s_u = s_d + M * nb;
     int32_t* s_s = reinterpret_cast<int32_t*>(s_u + M * nb);
-    {
+    if (!REGA) {
         const int4* src = reinterpret_cast<const int4*>(q8);
         int4* dst = reinterpret_cast<int4*>(s_q);
         for (int i = threadIdx.x; i < M * K / 16; i += blockDim.x) dst[i] = __ldg(src + i);
@@ -270,46 +284,90 @@ __global__ void __launch_bounds__(TPB) k_gemv_i8(const uint8_t* __restrict__ qs,
             s_u[i] = __ldg(ua + i);
             s_s[i] = __ldg(sa + i);
         }
+        __syncthreads();
     }
-    __syncthreads();
+#pragma unroll
+    for (int t = 0; t < TB; ++t) {
+        const int kb = sub + L * t;
+#pragma unroll
+        for (int r = 0; r < TR; ++r) {
+            if (REGA && r < M && kb < nb) {
+                const int4* a = reinterpret_cast<const int4*>(q8 + size_t(r) * K + size_t(kb) * QK);
+                a0[t][r] = __ldg(a);
+                a1[t][r] = __ldg(a + 1);
+                ad[t][r] = __ldg(da + r * nb + kb);
+                au[t][r] = has_min(DT) ? __ldg(ua + r * nb + kb) : 0.f;
+                init[t][r] = MAGIC_BITS - uint32_t(code_offset(DT) * __ldg(sa + r * nb + kb));
+            } else {
+                a0[t][r] = a1[t][r] = make_int4(0, 0, 0, 0);
+                ad[t][r] = au[t][r] = 0.f;
+                init[t][r] = MAGIC_BITS;
+            }
+        }
+    }
 
-    for (; g < groups; g += nw) {
-        RawBlock<DT> nxt[BPL];
-        if (g + nw < groups) fetch(g + nw, nxt);
-        const int j = g * RPW + slot;
-        float acc[MR];
+    for (int gb = g0; gb < groups; gb += PF * nw) {
 #pragma unroll
-        for (int r = 0; r < MR; ++r) acc[r] = 0.f;
+        for (int u = 0; u < PF; ++u) {
+            const int g = gb + u * nw;
+            const int j = g * RPW + slot;
+            float acc[MR];
 #pragma unroll
-        for (int t = 0; t < BPL; ++t) {
-            const int kb = sub + L * t;
-            if (j < N && kb < nb) {
-                BlockCodes<DT> bc;
-                decode<DT>(cur[t], bc);
+            for (int r = 0; r < MR; ++r) acc[r] = 0.f;
 #pragma unroll
-                for (int r = 0; r < MR; ++r) {
-                    if (r < M) {
-                        const int4* a = reinterpret_cast<const int4*>(s_q + size_t(r) * K + kb * QK);
-                        const int S = block_dot<DT>(bc.w, a[0], a[1], s_s[r * nb + kb]);
-                        acc[r] = __fmaf_rn(__fmul_rn(s_d[r * nb + kb], bc.d), float(S), acc[r]);
-                        if (has_min(DT)) acc[r] = __fmaf_rn(s_u[r * nb + kb], bc.m, acc[r]);
+            for (int t = 0; t < BPL; ++t) {
+                const int kb = sub + L * t;
+                if (g < groups && j < N && kb < nb) {
+                    BlockCodes<DT> bc;
+                    decode<DT>(ring[u][t], bc);
+#pragma unroll
+                    for (int r = 0; r < MR; ++r) {
+                        if (r < M) {
+                            int4 x0, x1;
+                            float xd, xu;
+                            uint32_t xi;
+                            if (REGA) {
+                                x0 = a0[REGA ? t : 0][REGA ? r : 0];
+                                x1 = a1[REGA ? t : 0][REGA ? r : 0];
+                                xd = ad[REGA ? t : 0][REGA ? r : 0];
+                                xu = au[REGA ? t : 0][REGA ? r : 0];
+                                xi = init[REGA ? t : 0][REGA ? r : 0];
+                            } else {
+                                const int4* ap = reinterpret_cast<const int4*>(s_q + size_t(r) * K + kb * QK);
+                                x0 = ap[0];
+                                x1 = ap[1];
+                                xd = s_d[r * nb + kb];
+                                xu = has_min(DT) ? s_u[r * nb + kb] : 0.f;
+                                xi = MAGIC_BITS - uint32_t(code_offset(DT) * s_s[r * nb + kb]);
+                            }
+                            const uint32_t av[8] = {uint32_t(x0.x), uint32_t(x0.y), uint32_t(x0.z), uint32_t(x0.w),
+                                                    uint32_t(x1.x), uint32_t(x1.y), uint32_t(x1.z), uint32_t(x1.w)};
+                            int sbits = int(xi);
+#pragma unroll
+                            for (int w = 0; w < 8; ++w)
+                                sbits = DT == Q8_0 ? dp4a_ss(av[w], bc.w[w], sbits) : dp4a_su(av[w], bc.w[w], sbits);
+                            const float S = __fsub_rn(__int_as_float(sbits), MAGIC_F);
+                            acc[r] = __fmaf_rn(__fmul_rn(xd, bc.d), S, acc[r]);
+                            if (has_min(DT)) acc[r] = __fmaf_rn(xu, bc.m, acc[r]);
+                        }
                     }
                 }
             }
+            // refill this ring slot PF groups ahead
+            fetch(g + PF * nw, ring[u]);
+#pragma unroll
+            for (int r = 0; r < MR; ++r) {
+#pragma unroll
+                for (int o = L / 2; o > 0; o >>= 1)
+                    acc[r] = __fadd_rn(acc[r], __shfl_xor_sync(0xffffffffu, acc[r], o));
+            }
+            if (g < groups && j < N && sub == 0) {
+                const float b = bias ? __ldg(bias + j) : 0.f;
+#pragma unroll
+                for (int r = 0; r < MR; ++r)
+                    if (r < M) y[size_t(r) * N + j] = bias ? __fadd_rn(acc[r], b) : acc[r];
+            }
         }
-#pragma unroll
-        for (int r = 0; r < MR; ++r) {
-#pragma unroll
-            for (int o = L / 2; o > 0; o >>= 1) acc[r] = __fadd_rn(acc[r], __shfl_xor_sync(0xffffffffu, acc[r], o));
-        }
-        if (j < N && sub == 0) {
-            const float b = bias ? __ldg(bias + j) : 0.f;
-#pragma unroll
-            for (int r = 0; r < MR; ++r)
-                if (r < M) y[size_t(r) * N + j] = bias ? __fadd_rn(acc[r], b) : acc[r];
-        }
-#pragma unroll
-        for (int t = 0; t < BPL; ++t) cur[t] = nxt[t];
     }
 }
 
@@ -547,18 +605,23 @@ inline unsigned gemv_grid(int n, int L) {
 
 template <int DT, int L, int BPL, int MR>
 cudaError_t gemv_i8_launch(const ActsView& v, const Weight& w, const float* bias, float* y, cudaStream_t s) {
-    const size_t smem = size_t(v.m) * v.k + size_t(v.m) * w.nb * 12;
-    static int attr_dev_mask = 0;  // one bit per device with the attribute set
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (!(attr_dev_mask & (1 << dev))) {
-        cudaError_t e = cudaFuncSetAttribute(k_gemv_i8<DT, L, BPL, MR>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             200 * 1024);
-        if (e != cudaSuccess) return e;
-        attr_dev_mask |= 1 << dev;
+    constexpr int PF = BPL == 1 ? 3 : (BPL == 2 ? 2 : 1);
+    constexpr bool REGA = BPL * MR <= 8;
+    size_t smem = 0;
+    if (!REGA) {
+        smem = size_t(v.m) * v.k + size_t(v.m) * w.nb * 12;
+        static int attr_dev_mask = 0;  // one bit per device with the attribute set
+        int dev = 0;
+        cudaGetDevice(&dev);
+        if (!(attr_dev_mask & (1 << dev))) {
+            cudaError_t e = cudaFuncSetAttribute(k_gemv_i8<DT, L, BPL, MR, PF, REGA>,
+                                                 cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+            if (e != cudaSuccess) return e;
+            attr_dev_mask |= 1 << dev;
+        }
     }
-    k_gemv_i8<DT, L, BPL, MR><<<gemv_grid(w.n, L), TPB, smem, s>>>(w.qs, w.qh, w.d, w.m, v.q8, v.d, v.sum, v.u, v.m,
-                                                                   w.n, w.k, bias, y);
+    k_gemv_i8<DT, L, BPL, MR, PF, REGA><<<gemv_grid(w.n, L), TPB, smem, s>>>(w.qs, w.qh, w.d, w.m, v.q8, v.d, v.sum,
+                                                                             v.u, v.m, w.n, w.k, bias, y);
     return cudaGetLastError();
 }
 
