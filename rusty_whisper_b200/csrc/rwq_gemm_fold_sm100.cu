@@ -112,15 +112,20 @@ __global__ void __launch_bounds__(THREADS, 1)
                      : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
+    if (threadIdx.x == 0) {
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmA)) : "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmB)) : "memory");
+    }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = bar->tmem_base;
+    // Setup above overlaps the previous kernel; global memory only below.
+    pdl_trigger();
+    pdl_wait();
 
     if (warp == 0) {
         if (lane == 0) {
-            asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmA)) : "memory");
-            asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmB)) : "memory");
             for (int pr = 0; pr < npairs; ++pr) {
                 const int s = pr % STAGES;
                 if (!mbar_wait(&bar->empty[s], ((pr / STAGES) & 1) ^ 1, abort, err_flag, 1)) break;
@@ -317,9 +322,8 @@ cudaError_t launch_fold(const ActsView& v, const Weight& w, const float* bias, f
         attr_dev_mask |= 1 << dev;
     }
     dim3 grid((w.n + BN - 1) / BN, (v.m + BM - 1) / BM);
-    k_gemm_fold<<<grid, THREADS, SMEM, s>>>(ma, mb, my, use_tma_store, v.dT, w.colscale, bias, y, v.m, w.n, w.nb,
-                                            v.m_pad, err_flag);
-    return cudaGetLastError();
+    return launch_pdl(k_gemm_fold, grid, dim3(THREADS), SMEM, s, ma, mb, my, use_tma_store, v.dT, w.colscale, bias, y,
+                      v.m, w.n, w.nb, v.m_pad, err_flag);
 }
 
 }  // namespace

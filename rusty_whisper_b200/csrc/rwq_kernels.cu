@@ -44,38 +44,57 @@ __global__ void k_repack(const uint8_t* __restrict__ raw, uint8_t* __restrict__ 
 }
 
 // ------------------------------------------------------------ quantizer
-// quantize_acts_i8 (quant.rs:690-716), one warp per 32-element block:
-// d = amax/127 (IEEE division), inv = 1/d or 0, q = round(x*inv) half away
-// from zero, clamped to [-127,127]; NaN codes become 0 as Rust's `as i32`.
+// quantize_acts_i8 (quant.rs:690-716): per 32-element block d = amax/127
+// (IEEE division), inv = 1/d or 0, q = round(x*inv) half away from zero,
+// clamped to [-127,127]; NaN codes become 0 as Rust's `as i32` makes them.
+// Eight lanes share a block (4 elements each, one 16-byte load), so a warp
+// quantizes four blocks; amax and sum(q) are xor-reduced over the 8 lanes.
 // Rows m..m_pad-1 of the transposed scale planes are written as zeros.
+template <bool VEC>
 __global__ void k_quantize(const float* __restrict__ a, int m, int k, int nb, int m_pad, int8_t* __restrict__ q8,
                            float* __restrict__ dd, int32_t* __restrict__ sum, float* __restrict__ uu,
                            uint16_t* __restrict__ q16, float* __restrict__ dT, float* __restrict__ uT) {
-    const int lane = threadIdx.x & 31;
-    const size_t warp = (size_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
-    if (warp >= size_t(m_pad) * nb) return;
-    const int i = int(warp / nb), bl = int(warp % nb);
+    pdl_trigger();
+    pdl_wait();
+    const size_t t = size_t(blockIdx.x) * blockDim.x + threadIdx.x;
+    const size_t blk = t >> 3;
+    const int sub = int(t & 7);
+    if (blk >= size_t(m_pad) * nb) return;  // whole groups of 8 lanes leave together
+    const int i = int(blk / nb), bl = int(blk % nb);
     if (i >= m) {
-        if (lane == 0 && dT) {
+        if (sub == 0 && dT) {
             dT[size_t(bl) * m_pad + i] = 0.f;
             uT[size_t(bl) * m_pad + i] = 0.f;
         }
         return;
     }
-    const size_t off = size_t(i) * k + size_t(bl) * QK + lane;
-    const float x = a[off];
-    float ax = fabsf(x);
-    if (isnan(ax)) ax = 0.f;  // f32::max ignores a NaN operand
-    // Non-negative floats order like their bit patterns.
-    const float amax = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(ax)));
+    const size_t off = size_t(i) * k + size_t(bl) * QK + sub * 4;
+    const float4 x = VEC ? *reinterpret_cast<const float4*>(a + off)
+                         : make_float4(a[off], a[off + 1], a[off + 2], a[off + 3]);
+    auto absnn = [](float v) { const float w = fabsf(v); return isnan(w) ? 0.f : w; };  // f32::max skips NaN
+    float amax = fmaxf(fmaxf(absnn(x.x), absnn(x.y)), fmaxf(absnn(x.z), absnn(x.w)));
+    const unsigned grp = 0xFFu << (threadIdx.x & 24);
+#pragma unroll
+    for (int o = 4; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(grp, amax, o));
     const float d = __fdiv_rn(amax, 127.0f);
     const float inv = d > 0.f ? __fdiv_rn(1.0f, d) : 0.f;
-    const float r = roundf(__fmul_rn(x, inv));
-    const int qi = isnan(r) ? 0 : int(fminf(127.f, fmaxf(-127.f, r)));
-    const int s = __reduce_add_sync(0xffffffffu, qi);
-    if (q8) q8[off] = int8_t(qi);
-    if (q16) q16[off] = __half_as_ushort(__int2half_rn(qi));
-    if (lane == 0) {
+    auto code = [inv](float v) {
+        const float r = roundf(__fmul_rn(v, inv));
+        return isnan(r) ? 0 : int(fminf(127.f, fmaxf(-127.f, r)));
+    };
+    const int c0 = code(x.x), c1 = code(x.y), c2 = code(x.z), c3 = code(x.w);
+    int s = c0 + c1 + c2 + c3;
+#pragma unroll
+    for (int o = 4; o > 0; o >>= 1) s += __shfl_xor_sync(grp, s, o);
+    if (q8)
+        *reinterpret_cast<uint32_t*>(q8 + off) =
+            uint32_t(uint8_t(c0)) | (uint32_t(uint8_t(c1)) << 8) | (uint32_t(uint8_t(c2)) << 16) | (uint32_t(uint8_t(c3)) << 24);
+    if (q16) {
+        const uint32_t h01 = uint32_t(__half_as_ushort(__int2half_rn(c0))) | (uint32_t(__half_as_ushort(__int2half_rn(c1))) << 16);
+        const uint32_t h23 = uint32_t(__half_as_ushort(__int2half_rn(c2))) | (uint32_t(__half_as_ushort(__int2half_rn(c3))) << 16);
+        *reinterpret_cast<uint2*>(q16 + off) = make_uint2(h01, h23);
+    }
+    if (sub == 0) {
         const size_t o = size_t(i) * nb + bl;
         const float u = __fmul_rn(d, float(s));
         dd[o] = d;
@@ -244,6 +263,8 @@ __global__ void __launch_bounds__(TPB) k_gemv_i8(const uint8_t* __restrict__ qs,
                                                  const int8_t* __restrict__ q8, const float* __restrict__ da,
                                                  const int32_t* __restrict__ sa, const float* __restrict__ ua, int M,
                                                  int N, int K, const float* __restrict__ bias, float* __restrict__ y) {
+    pdl_trigger();
+    pdl_wait();
     const int nb = K / QK;
     constexpr int RPW = 32 / L;
     const int lane = threadIdx.x & 31, sub = lane % L, slot = lane / L;
@@ -620,9 +641,8 @@ cudaError_t gemv_i8_launch(const ActsView& v, const Weight& w, const float* bias
             attr_dev_mask |= 1 << dev;
         }
     }
-    k_gemv_i8<DT, L, BPL, MR, PF, REGA><<<gemv_grid(w.n, L), TPB, smem, s>>>(w.qs, w.qh, w.d, w.m, v.q8, v.d, v.sum,
-                                                                             v.u, v.m, w.n, w.k, bias, y);
-    return cudaGetLastError();
+    return launch_pdl(k_gemv_i8<DT, L, BPL, MR, PF, REGA>, dim3(gemv_grid(w.n, L)), dim3(TPB), smem, s, w.qs, w.qh,
+                      w.d, w.m, v.q8, v.d, v.sum, v.u, v.m, w.n, w.k, bias, y);
 }
 
 template <int DT, int L, int BPL>
@@ -681,12 +701,12 @@ cudaError_t launch_build_fold_cache(Weight& w, cudaStream_t s) { return by_dtype
 
 cudaError_t launch_quantize_acts(const float* a, const ActsView& v, bool want_gemm, cudaStream_t s) {
     const int m_pad = want_gemm ? v.m_pad : v.m;
-    const size_t warps = size_t(m_pad) * v.nb;
-    if (!warps) return cudaSuccess;
-    k_quantize<<<grid_for(warps * 32, TPB), TPB, 0, s>>>(a, v.m, v.k, v.nb, m_pad, want_gemm ? nullptr : v.q8, v.d, v.sum, v.u,
-                                                        want_gemm ? v.q16 : nullptr, want_gemm ? v.dT : nullptr,
-                                                        want_gemm ? v.uT : nullptr);
-    return cudaGetLastError();
+    const size_t blocks = size_t(m_pad) * v.nb;
+    if (!blocks) return cudaSuccess;
+    auto kern = (reinterpret_cast<uintptr_t>(a) & 15) ? k_quantize<false> : k_quantize<true>;
+    return launch_pdl(kern, dim3(grid_for(blocks * 8, TPB)), dim3(TPB), 0, s, a, v.m, v.k, v.nb, m_pad,
+                      want_gemm ? nullptr : v.q8, v.d, v.sum, v.u, want_gemm ? v.q16 : nullptr,
+                      want_gemm ? v.dT : nullptr, want_gemm ? v.uT : nullptr);
 }
 
 cudaError_t launch_dequant_rows(const Weight& w, const int32_t* rows, int nrows, float* out, cudaStream_t s) {

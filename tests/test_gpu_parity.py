@@ -277,3 +277,22 @@ def test_unaligned_device_pointers(rq, orc):
         assert close(host(out), orc.matmul_t_q(a, 6, raw, n) + bias.cpu().numpy()[None, :]) < TOL
     finally:
         rq.set_gemm_path(0)
+
+
+def test_quantizer_unaligned_and_nan(rq, orc):
+    """Activations at a 4-byte (not 16-byte) offset, with NaN and inf."""
+    import torch
+    from rusty_whisper_b200 import synth
+    m, k = 7, 96
+    a = synth.normal(3, m * k).reshape(m, k)
+    a[1, 5] = np.nan
+    a[2, 40] = np.inf
+    a[3, 64:96] = 0.0
+    buf = torch.zeros(m * k + 1, device="cuda")
+    buf[1:] = torch.from_numpy(a.ravel()).cuda()
+    av = buf[1:].view(m, k)
+    q, d, s = rq.quantize_acts_i8(av)
+    qr, dr, sr = orc.quantize_acts_i8(a)
+    assert np.array_equal(host(q), qr)
+    assert np.array_equal(host(d).view(np.uint32), dr.view(np.uint32))
+    assert np.array_equal(host(s), sr)
