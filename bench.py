@@ -198,15 +198,26 @@ def run_ours(args, rank, world, local_rank):
     if world > 1:
         dist.barrier()
     quant.stream_check()
-    # ---- per-kernel pass (roofline): events around every GEMM launch
+    # ---- per-kernel pass (roofline): for each GEMM, R back-to-back launches
+    # of that kernel between one event pair (its steady-state launch time)
     per_gemm = []
-    for _ in range(args.steps):
-        flush.zero_()
-        torch.cuda._sleep(GATE_CYCLES)
-        step(per_gemm)
+    R = 8
+    for s_ in synth.SWEEP_SHAPES:
+        qa[s_].quantize(acts[s_])
+        for dt in synth.SWEEP_FORMATS:
+            key = (dt, s_[0], s_[1])
+            torch.cuda.synchronize()
+            torch.cuda._sleep(GATE_CYCLES)
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for _ in range(R):
+                qa[s_].matmul(W[key], out=Y[key])
+            e1.record(stream)
+            per_gemm.append((key, e0, e1, R))
     torch.cuda.synchronize()
     t_steps = sum(a.elapsed_time(b) for a, b in steps) / 1e3      # seconds
-    t_gemm = sum(a.elapsed_time(b) for _, a, b in per_gemm) / 1e3
+    t_gemm = sum(a.elapsed_time(b) / r for _, a, b, r in per_gemm) / 1e3
     tmax = t_steps
     if world > 1:
         t = torch.tensor([t_steps], dtype=torch.float64, device=dev)
@@ -214,15 +225,15 @@ def run_ours(args, rank, world, local_rank):
         tmax = float(t.item())
     ops_step = gemm_ops()
     value = world * ops_step * args.steps / tmax / 1e12
-    gemm_tops = ops_step * args.steps / t_gemm / 1e12   # kernel-level, this rank
+    gemm_tops = ops_step / t_gemm / 1e12   # kernel-level, this rank
 
     # per-format kernel numbers (this rank)
     by_fmt = {}
-    for key, a, b in per_gemm:
+    for key, a, b, r in per_gemm:
         dt, k, n = key
         by_fmt.setdefault(NAMES[dt], [0.0, 0.0])
         by_fmt[NAMES[dt]][0] += 2.0 * synth.ENCODER_M * n * k
-        by_fmt[NAMES[dt]][1] += a.elapsed_time(b) / 1e3
+        by_fmt[NAMES[dt]][1] += a.elapsed_time(b) / r / 1e3
     by_fmt = {f: round(o / t / 1e12, 2) for f, (o, t) in by_fmt.items()}
 
     gemv = run_gemv(args, dev, quant, w_np, hbm_peak, stream) if args.only == "all" else None
@@ -245,7 +256,8 @@ def run_ours(args, rank, world, local_rank):
             "bound": "tensor", "kernel": "k_gemm_fold (tcgen05 kind::f16, scales folded into an f16 hi|lo weight operand)",
             "achieved": round(gemm_tops, 2), "peak": tc_peak, "unit": "TFLOP/s",
             "frac": round(gemm_tops / tc_peak, 4), "peak_kind": f"{peak_kind} dense bf16 (burst)",
-            "traffic": profile_traffic("gemm_tc_config2.txt"),
+            "traffic": profile_traffic("k_gemm_fold_config2_768x3072.md"),
+            "traffic_launch": "ncu, Q4_0 M=1500 K=768 N=3072 launch (profiles/)",
             "per_format_tops": by_fmt,
         },
         "gemv": gemv,
@@ -258,7 +270,8 @@ def run_ours(args, rank, world, local_rank):
 
 
 def run_gemv(args, dev, quant, w_np, hbm_peak, stream):
-    """Decoder GEMVs of config 2 over weight copies rotated past L2."""
+    """Decoder GEMVs of config 2: for each weight, R back-to-back launches
+    over copies rotated past L2, one event pair per batch."""
     import torch
     total_w = sum(r.nbytes for r in w_np.values())
     copies = max(2, int(np.ceil(300e6 / total_w)))
@@ -270,48 +283,42 @@ def run_gemv(args, dev, quant, w_np, hbm_peak, stream):
         for s in synth.SWEEP_SHAPES:
             qa[s].quantize(xs[s])
         ys = {key: torch.empty((mm, key[2]), device=dev) for key in w_np}
-
-        def one(c, rec=None):
-            for key in w_np:
-                s = (key[1], key[2])
-                if rec is not None:
-                    e0 = torch.cuda.Event(enable_timing=True)
-                    e1 = torch.cuda.Event(enable_timing=True)
-                    e0.record(stream)
-                qa[s].matmul(Wc[c][key], out=ys[key])
-                if rec is not None:
-                    e1.record(stream)
-                    rec.append((key, e0, e1))
-
         for c in range(copies):
-            one(c)
-        torch.cuda.synchronize()
-        rec = []
-        reps = max(args.steps, 4)
-        for r in range(reps):
-            torch.cuda._sleep(GATE_CYCLES)
-            one(r % copies, rec)
+            for key in w_np:
+                qa[(key[1], key[2])].matmul(Wc[c][key], out=ys[key])
         torch.cuda.synchronize()
         nbytes = 0.0
         t = 0.0
         per_fmt = {}
-        for key, e0, e1 in rec:
+        launches = 0
+        for key in w_np:
             dt, k, n = key
-            b = n * (k // QK) * block_bytes(dt) + 4.0 * mm * k + 4.0 * mm * n
+            s = (k, n)
+            torch.cuda._sleep(GATE_CYCLES)
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for c in range(copies):
+                qa[s].matmul(Wc[c][key], out=ys[key])
+            e1.record(stream)
+            torch.cuda.synchronize()
             dtm = e0.elapsed_time(e1) / 1e3
+            b = copies * (n * (k // QK) * block_bytes(dt) + 4.0 * mm * k + 4.0 * mm * n)
             nbytes += b
             t += dtm
+            launches += copies
             pf = per_fmt.setdefault(NAMES[dt], [0.0, 0.0])
             pf[0] += b
             pf[1] += dtm
         gbs = nbytes / t / 1e9
         res[f"M={mm}"] = {"GB/s": round(gbs, 1), "frac_of_measured_hbm": round(gbs / hbm_peak, 4),
-                          "us_per_gemv": round(t / len(rec) * 1e6, 3),
+                          "us_per_gemv": round(t / launches * 1e6, 3),
                           "per_format_GBs": {f: round(b / x / 1e9, 1) for f, (b, x) in per_fmt.items()}}
     res["logits_Q5_0_51865x1024"] = gemv_logits(args, dev, quant, hbm_peak, stream)
     res["bound"] = "hbm"
     res["peak_GBs"] = hbm_peak
     res["bytes"] = "N*(K/32)*block_bytes + 4*M*K + 4*M*N per GEMV (algorithmic)"
+    res["timing"] = "back-to-back launches of one GEMV over weight copies, one event pair per batch"
     res["l2"] = f"{copies} rotating weight copies ({copies * total_w / 1e6:.0f} MB > 126 MB L2)"
     return res
 
@@ -331,17 +338,16 @@ def gemv_logits(args, dev, quant, hbm_peak, stream):
         for w in Wl:
             qa.matmul(w, out=y)
         torch.cuda.synchronize()
-        rec = []
-        for r in range(max(args.steps, 8)):
-            torch.cuda._sleep(GATE_CYCLES // 4)
-            e0 = torch.cuda.Event(enable_timing=True)
-            e1 = torch.cuda.Event(enable_timing=True)
-            e0.record(stream)
+        reps = max(args.steps, 8)
+        torch.cuda._sleep(GATE_CYCLES)
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for r in range(reps):
             qa.matmul(Wl[r % 4], out=y)
-            e1.record(stream)
-            rec.append((e0, e1))
+        e1.record(stream)
         torch.cuda.synchronize()
-        t = sum(a.elapsed_time(b) for a, b in rec) / 1e3 / len(rec)
+        t = e0.elapsed_time(e1) / 1e3 / reps
         b = n * (k // QK) * block_bytes(dt) + 4.0 * mm * k + 4.0 * mm * n
         out[f"M={mm}"] = {"GB/s": round(b / t / 1e9, 1), "frac_of_measured_hbm": round(b / t / 1e9 / hbm_peak, 4),
                           "us": round(t * 1e6, 2)}

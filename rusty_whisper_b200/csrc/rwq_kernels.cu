@@ -617,10 +617,19 @@ inline int lanes_for(int nb) {
     return nb >= 32 ? 32 : 8;
 }
 
-inline unsigned gemv_grid(int n, int L) {
+// Grid for a grid-stride GEMV kernel: one CTA per row group of the
+// output, but never more than fit on the GPU at once (a second, partial
+// wave would redo a full wave's per-warp work).
+template <typename Kern>
+unsigned gemv_grid(Kern kern, int n, int L, size_t smem) {
     const int rows_per_cta = (TPB / 32) * (32 / L);
     unsigned g = unsigned((n + rows_per_cta - 1) / rows_per_cta);
-    const unsigned cap = 148u * 8u;
+    int dev = 0, sms = 148, per_sm = 1;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, TPB, smem) != cudaSuccess || per_sm < 1)
+        per_sm = 1;
+    const unsigned cap = unsigned(sms) * unsigned(per_sm);
     return g < 1 ? 1 : (g > cap ? cap : g);
 }
 
@@ -641,8 +650,9 @@ cudaError_t gemv_i8_launch(const ActsView& v, const Weight& w, const float* bias
             attr_dev_mask |= 1 << dev;
         }
     }
-    return launch_pdl(k_gemv_i8<DT, L, BPL, MR, PF, REGA>, dim3(gemv_grid(w.n, L)), dim3(TPB), smem, s, w.qs, w.qh,
-                      w.d, w.m, v.q8, v.d, v.sum, v.u, v.m, w.n, w.k, bias, y);
+    auto kern = k_gemv_i8<DT, L, BPL, MR, PF, REGA>;
+    return launch_pdl(kern, dim3(gemv_grid(kern, w.n, L, smem)), dim3(TPB), smem, s, w.qs, w.qh, w.d, w.m, v.q8, v.d,
+                      v.sum, v.u, v.m, w.n, w.k, bias, y);
 }
 
 template <int DT, int L, int BPL>
@@ -655,11 +665,14 @@ cudaError_t gemv_i8_mr(const ActsView& v, const Weight& w, const float* bias, fl
 template <int DT>
 struct GemvI8F {
     static cudaError_t run(const ActsView& v, const Weight& w, const float* bias, float* y, cudaStream_t s) {
+        // Lanes per row (L) and blocks per lane (BPL) depend on K only, so
+        // results do not depend on M.  Several blocks per lane keep the
+        // xor reduction (log2 L steps per row) small next to the block work.
         const int nb = w.nb;
         if (nb <= 8) return gemv_i8_mr<DT, 8, 1>(v, w, bias, y, s);
         if (nb <= 16) return gemv_i8_mr<DT, 8, 2>(v, w, bias, y, s);
-        if (nb <= 32) return gemv_i8_mr<DT, 32, 1>(v, w, bias, y, s);
-        if (nb <= 64) return gemv_i8_mr<DT, 32, 2>(v, w, bias, y, s);
+        if (nb <= 32) return gemv_i8_mr<DT, 8, 4>(v, w, bias, y, s);
+        if (nb <= 64) return gemv_i8_mr<DT, 16, 4>(v, w, bias, y, s);
         if (nb <= 128) return gemv_i8_mr<DT, 32, 4>(v, w, bias, y, s);
         if (nb <= 256) return gemv_i8_mr<DT, 32, 8>(v, w, bias, y, s);
         return cudaErrorInvalidValue;
@@ -668,7 +681,8 @@ struct GemvI8F {
 
 template <int DT, int L, int MR>
 cudaError_t gemv_f32_launch(const float* a, int m, const Weight& w, const float* bias, float* y, cudaStream_t s) {
-    k_gemv_f32<DT, L, MR><<<gemv_grid(w.n, L), TPB, 0, s>>>(w.qs, w.qh, w.d, w.m, a, m, w.n, w.k, bias, y);
+    k_gemv_f32<DT, L, MR><<<gemv_grid(k_gemv_f32<DT, L, MR>, w.n, L, 0), TPB, 0, s>>>(w.qs, w.qh, w.d, w.m, a, m, w.n,
+                                                                                      w.k, bias, y);
     return cudaGetLastError();
 }
 
