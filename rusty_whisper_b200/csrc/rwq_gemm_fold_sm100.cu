@@ -15,16 +15,17 @@
 // in an f32 TMEM buffer; the epilogue does acc <- fma(d_a, T, acc) with
 // packed f32x2 math, and finally y = acc * 2^-e_j (+ bias).
 //
-// Roles (320 threads, one CTA per 128 x 128 output tile):
+// Roles (352 threads, one CTA per 128 x 128 output tile):
 //   warp 0     TMA producer: per pair of blocks one stage with A (q_a
 //              f16, 128 x 64) and B (two 128-row hi|lo tiles), 128-byte
 //              swizzled, plus 1-D bulk copies of the pair's d_a rows into a
 //              shared ring; allocates / frees the 512 TMEM columns.
-//   warp 1     MMA issuer (one thread): 8 MMAs per pair into a pair of
-//              TMEM buffers, then one commit to the pair's accumulator
-//              barrier and one to the stage's empty barrier.
-//   warps 2-9  epilogue: warp w reads TMEM lanes 32*(w%4).., columns
-//              (w-2)/4 * 64 .. + 64 of each block; at the end it
+//   warps 1-2  MMA issuers (one thread each; even / odd pairs): 8 MMAs per
+//              pair into a pair of TMEM buffers, then one commit to the
+//              pair's accumulator barrier and one to the stage's empty
+//              barrier.
+//   warps 3-10 epilogue: warp w reads TMEM lanes 32*(w%4).., columns
+//              (w-3)/4 * 64 .. + 64 of each block; at the end it
 //              scales, adds the bias, stages its 32-row block in shared
 //              memory (the drained B ring) and writes it with TMA stores,
 //              which clip the ragged M and N edges.
@@ -53,7 +54,8 @@ constexpr int BN = 128;
 // iteration is 2 waits + 8 MMAs + 2 commits.
 constexpr int STAGES = 4;                  // 8 blocks in flight
 constexpr int EPI_WARPS = 8;
-constexpr int THREADS = (2 + EPI_WARPS) * 32;
+constexpr int EPI0 = 3;                    // first epilogue warp (warps 1, 2 issue MMAs)
+constexpr int THREADS = (EPI0 + EPI_WARPS) * 32;
 constexpr int A_BYTES = BM * 64 * 2;       // 16 KiB
 constexpr int B_BYTES = BN * 64 * 2;       // 16 KiB per block (32 hi + 32 lo f16 per row)
 constexpr int STAGE_BYTES = A_BYTES + 2 * B_BYTES;
@@ -142,9 +144,14 @@ __global__ void __launch_bounds__(THREADS, 1)
                     bulk_load(ring + c * 256 + j * 128, daT + size_t(2 * pr + j) * m_pad + m0, 512, &bar->sc_full[c]);
             }
         }
-    } else if (warp == 1) {
+    } else if (warp == 1 || warp == 2) {
+        // Two issuing threads: warp 1 takes the even pairs (TMEM pair 0),
+        // warp 2 the odd ones (pair 1).  Each commit tracks the issuing
+        // thread's own MMAs, and the two accumulators are independent, so
+        // one thread's MMAs keep the tensor pipe busy while the other waits
+        // on its barriers or commits.
         if (lane == 0) {
-            for (int pr = 0; pr < npairs; ++pr) {
+            for (int pr = warp - 1; pr < npairs; pr += 2) {
                 const int s = pr % STAGES, p = pr % NPAIR;
                 if (!mbar_wait(&bar->full[s], (pr / STAGES) & 1, abort, err_flag, 2)) break;
                 if (!mbar_wait(&bar->acc_empty[p], ((pr / NPAIR) & 1) ^ 1, abort, err_flag, 3)) break;
@@ -169,7 +176,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
     } else {
         const int q = warp & 3;
-        const int h = (warp - 2) >> 2;
+        const int h = (warp - EPI0) >> 2;
         float2 acc[CPW / 2];
 #pragma unroll
         for (int c = 0; c < CPW / 2; ++c) acc[c] = make_float2(0.f, 0.f);
@@ -210,7 +217,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                 // Staging for this warp (in the drained stage ring): CPW/32
                 // boxes of 32 rows x 128 bytes, 128-byte swizzle (16-byte
                 // chunk c of row r at c ^ (r & 7)).
-                uint8_t* stg = base + (warp - 2) * (32 * CPW * 4);
+                uint8_t* stg = base + (warp - EPI0) * (32 * CPW * 4);
 #pragma unroll
                 for (int b = 0; b < CPW / 32; ++b) {
                     uint8_t* box = stg + b * 4096 + lane * 128;
