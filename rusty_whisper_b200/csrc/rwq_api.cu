@@ -118,7 +118,7 @@ int ensure_cap(Workspace* ws, size_t bytes) {
 // Carve an activation view out of the arena starting at `base`.
 size_t acts_layout(int m, int k, bool gemm, rwq::ActsView* v, uint8_t* base) {
     const int nb = k / rwq::QK;
-    const int m_pad = (m + 127) / 128 * 128;
+    const int m_pad = (m + 255) / 256 * 256;   // the fold GEMM's CTA pairs cover 256 rows
     size_t off = 0;
     auto take = [&](size_t bytes) {
         uint8_t* p = base ? base + off : nullptr;

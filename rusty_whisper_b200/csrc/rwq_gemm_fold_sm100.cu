@@ -18,11 +18,12 @@
 // Roles (352 threads, one CTA per 128 x 128 output tile):
 //   warp 0     TMA producer: per pair of blocks one stage with A (q_a
 //              f16, 128 x 64) and B (two 128-row hi|lo tiles), 128-byte
-//              swizzled, plus 1-D bulk copies of the pair's d_a rows into a
-//              shared ring; allocates / frees the 512 TMEM columns.
-//   warps 1-2  MMA issuers (one thread each; even / odd pairs): 8 MMAs per
-//              pair into a pair of TMEM buffers, then one commit to the
-//              pair's accumulator barrier and one to the stage's empty
+//              swizzled; per 16 blocks one 2-D load of their d_a rows
+//              (16 x 128 floats) into a 3-slot ring; allocates / frees the
+//              512 TMEM columns.
+//   warps 1-2  MMA issuers (one thread each; even / odd pairs): per block
+//              4 MMAs into one of four 128-column TMEM buffers and a commit
+//              to that buffer's barrier, then a commit to the stage's empty
 //              barrier.
 //   warps 3-10 epilogue: warp w reads TMEM lanes 32*(w%4).., columns
 //              (w-3)/4 * 64 .. + 64 of each block; at the end it
@@ -45,45 +46,66 @@ namespace {
 using namespace tc;
 
 constexpr int BM = 128;
-constexpr int BN = 128;
 // The MMA-issuing thread is the critical resource: the tensor pipe only
 // queues about one MMA ahead, so every barrier wait or commit between
 // MMAs idles it.  Work is therefore handled in pairs of 32-wide blocks:
-// one stage (A: 128 rows x 64 f16, B: two 128-row hi|lo tiles) per pair,
-// one full/empty barrier per stage, and TMEM buffers used in pairs, so an
-// iteration is 2 waits + 8 MMAs + 2 commits.
-constexpr int STAGES = 4;                  // 8 blocks in flight
+// one stage (A: 128 rows x 64 f16, B: two BN-row hi|lo tiles) per pair and
+// one full/empty barrier per stage.
+//
+// Tile width BN is 128 or 64.  At 128 the MMAs are most efficient; 64 is
+// used when 128-wide tiles would leave half the SMs idle (the N = 768
+// encoder shapes at M = 1500 give 72 tiles for 148 SMs): its MMAs are a
+// third less efficient per flop, but twice the SMs run, and each block's
+// accumulator is half as many TMEM bytes for the epilogue to read.
 constexpr int EPI_WARPS = 8;
 constexpr int EPI0 = 3;                    // first epilogue warp (warps 1, 2 issue MMAs)
 constexpr int THREADS = (EPI0 + EPI_WARPS) * 32;
 constexpr int A_BYTES = BM * 64 * 2;       // 16 KiB
-constexpr int B_BYTES = BN * 64 * 2;       // 16 KiB per block (32 hi + 32 lo f16 per row)
-constexpr int STAGE_BYTES = A_BYTES + 2 * B_BYTES;
-constexpr int SC_SLOTS = 8;                // d_a rows for a pair of blocks: 2 x 128 floats
-constexpr int NPAIR = 2;                   // TMEM: 2 pairs x 2 blocks x 128 columns = 512
+// d_a arrives 16 blocks at a time (one 8 KiB TMA load instead of 16
+// small copies: each copy is a TMA operation, and at two per block pair
+// they slowed the operand stream by a seventh).
+constexpr int DA_GROUP = 16;
+constexpr int DA_SLOTS = 3;
+constexpr int DA_BYTES = DA_GROUP * BM * 4;
 constexpr int TMEM_COLS = 512;
-constexpr int CPW = BN / 2;                // output columns per epilogue warp
-// kind::f16, D f32, A/B f16, K-major, N>>3 at bit 17, M>>4 at bit 24.
-constexpr uint32_t IDESC = (1u << 4) | (uint32_t(BN >> 3) << 17) | (uint32_t(BM >> 4) << 24);
 
-struct Bars {
-    uint64_t full[STAGES], empty[STAGES], acc_full[NPAIR], acc_empty[NPAIR], sc_full[SC_SLOTS], sc_empty[SC_SLOTS];
-    uint32_t tmem_base;
-    int abort;
+template <int BN>
+struct Fold {
+    static constexpr int B_BYTES = BN * 64 * 2;   // per block: BN rows x (32 hi + 32 lo f16)
+    static constexpr int STAGE_BYTES = A_BYTES + 2 * B_BYTES;
+    static constexpr int STAGES = BN == 128 ? 4 : 6;   // 192 KiB of stages either way
+    // TMEM: single-block accumulators of BN columns.  A block's buffer is
+    // handed back as soon as the epilogue has read it, so the MMAs can run
+    // up to NBUF - 1 blocks ahead of the epilogue.
+    static constexpr int NBUF = TMEM_COLS / BN;
+    static constexpr int CPW = BN / 2;            // output columns per epilogue warp
+    // kind::f16, D f32, A/B f16, K-major, N>>3 at bit 17, M>>4 at bit 24.
+    static constexpr uint32_t IDESC = (1u << 4) | (uint32_t(BN >> 3) << 17) | (uint32_t(BM >> 4) << 24);
+    struct Bars {
+        uint64_t full[STAGES], empty[STAGES], acc_full[NBUF], acc_empty[NBUF], da_full[DA_SLOTS], da_empty[DA_SLOTS];
+        uint32_t tmem_base;
+        int abort;
+    };
+    static constexpr int SMEM = STAGES * STAGE_BYTES + DA_SLOTS * DA_BYTES + int(sizeof(Bars)) + 1024;
+    static_assert(SMEM <= 227 * 1024, "shared memory budget");
+    static_assert(EPI_WARPS * 32 * CPW * 4 <= STAGES * STAGE_BYTES, "output staging must fit in the stages");
 };
-constexpr int SMEM = STAGES * STAGE_BYTES + SC_SLOTS * 1024 + int(sizeof(Bars)) + 1024;
-static_assert(SMEM <= 227 * 1024, "shared memory budget");
-static_assert(EPI_WARPS * 32 * CPW * 4 <= STAGES * STAGE_BYTES, "output staging must fit in the stages");
 
+template <int BN>
 __global__ void __launch_bounds__(THREADS, 1)
     k_gemm_fold(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                const __grid_constant__ CUtensorMap tmY, int use_tma_store, const float* __restrict__ daT,
+                const __grid_constant__ CUtensorMap tmY, const __grid_constant__ CUtensorMap tmD, int use_tma_store,
                 const float* __restrict__ colscale, const float* __restrict__ bias, float* __restrict__ Y, int M,
-                int N, int nb, int m_pad, int* __restrict__ err_flag) {
+                int N, int nb, int* __restrict__ err_flag) {
+    using F = Fold<BN>;
+    constexpr int STAGES = F::STAGES, STAGE_BYTES = F::STAGE_BYTES, B_BYTES = F::B_BYTES, NBUF = F::NBUF;
+    constexpr int CPW = F::CPW;
+    constexpr uint32_t IDESC = F::IDESC;
+    using Bars = typename F::Bars;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* base = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     float* ring = reinterpret_cast<float*>(base + STAGES * STAGE_BYTES);
-    Bars* bar = reinterpret_cast<Bars*>(reinterpret_cast<uint8_t*>(ring) + SC_SLOTS * 1024);
+    Bars* bar = reinterpret_cast<Bars*>(reinterpret_cast<uint8_t*>(ring) + DA_SLOTS * DA_BYTES);
     volatile int* abort = &bar->abort;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -95,13 +117,13 @@ __global__ void __launch_bounds__(THREADS, 1)
             mbar_init(&bar->full[s], 1);
             mbar_init(&bar->empty[s], 1);
         }
-        for (int b = 0; b < NPAIR; ++b) {
+        for (int b = 0; b < NBUF; ++b) {
             mbar_init(&bar->acc_full[b], 1);
             mbar_init(&bar->acc_empty[b], EPI_WARPS);
         }
-        for (int c = 0; c < SC_SLOTS; ++c) {
-            mbar_init(&bar->sc_full[c], 1);
-            mbar_init(&bar->sc_empty[c], EPI_WARPS);
+        for (int c = 0; c < DA_SLOTS; ++c) {
+            mbar_init(&bar->da_full[c], 1);
+            mbar_init(&bar->da_empty[c], EPI_WARPS);
         }
         bar->abort = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -117,6 +139,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     if (threadIdx.x == 0) {
         asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmA)) : "memory");
         asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmB)) : "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmD)) : "memory");
     }
     tc_fence_before();
     __syncthreads();
@@ -130,47 +153,54 @@ __global__ void __launch_bounds__(THREADS, 1)
         if (lane == 0) {
             for (int pr = 0; pr < npairs; ++pr) {
                 const int s = pr % STAGES;
+                if ((2 * pr) % DA_GROUP == 0) {
+                    // d_a rows of blocks 2pr .. 2pr+15 (rows past nb read as 0).
+                    const int g = 2 * pr / DA_GROUP, c = g % DA_SLOTS;
+                    if (!mbar_wait(&bar->da_empty[c], ((g / DA_SLOTS) & 1) ^ 1, abort, err_flag, 5)) break;
+                    mbar_expect_tx(&bar->da_full[c], DA_BYTES);
+                    tma_load_2d(ring + c * (DA_BYTES / 4), &tmD, m0, g * DA_GROUP, &bar->da_full[c]);
+                }
                 if (!mbar_wait(&bar->empty[s], ((pr / STAGES) & 1) ^ 1, abort, err_flag, 1)) break;
                 uint8_t* st = base + s * STAGE_BYTES;
                 mbar_expect_tx(&bar->full[s], STAGE_BYTES);
                 tma_load_2d(st, &tmA, pr * 64, m0, &bar->full[s]);                        // blocks 2pr, 2pr+1
                 tma_load_2d(st + A_BYTES, &tmB, pr * 128, n0, &bar->full[s]);             // block 2pr
                 tma_load_2d(st + A_BYTES + B_BYTES, &tmB, pr * 128 + 64, n0, &bar->full[s]);  // block 2pr+1
-                const int c = pr % SC_SLOTS;
-                if (!mbar_wait(&bar->sc_empty[c], ((pr / SC_SLOTS) & 1) ^ 1, abort, err_flag, 5)) break;
-                const int two = (2 * pr + 1 < nb) ? 2 : 1;
-                mbar_expect_tx(&bar->sc_full[c], 512u * two);
-                for (int j = 0; j < two; ++j)
-                    bulk_load(ring + c * 256 + j * 128, daT + size_t(2 * pr + j) * m_pad + m0, 512, &bar->sc_full[c]);
             }
         }
     } else if (warp == 1 || warp == 2) {
-        // Two issuing threads: warp 1 takes the even pairs (TMEM pair 0),
-        // warp 2 the odd ones (pair 1).  Each commit tracks the issuing
-        // thread's own MMAs, and the two accumulators are independent, so
+        // Two issuing threads: warp 1 takes the even pairs (TMEM buffers 0
+        // and 1), warp 2 the odd ones (buffers 2 and 3).  Each commit tracks
+        // the issuing thread's own MMAs and the buffers are independent, so
         // one thread's MMAs keep the tensor pipe busy while the other waits
         // on its barriers or commits.
         if (lane == 0) {
-            for (int pr = warp - 1; pr < npairs; pr += 2) {
-                const int s = pr % STAGES, p = pr % NPAIR;
+            bool ok = true;
+            for (int pr = warp - 1; pr < npairs && ok; pr += 2) {
+                const int s = pr % STAGES;
                 if (!mbar_wait(&bar->full[s], (pr / STAGES) & 1, abort, err_flag, 2)) break;
-                if (!mbar_wait(&bar->acc_empty[p], ((pr / NPAIR) & 1) ^ 1, abort, err_flag, 3)) break;
-                tc_fence_after();
                 const uint32_t a0 = smem_u32(base + s * STAGE_BYTES);
 #pragma unroll
                 for (int j = 0; j < 2; ++j) {
-                    if (2 * pr + j >= nb) break;
+                    const int blk = 2 * pr + j;
+                    if (blk >= nb) break;
+                    const int u = blk % NBUF;
+                    if (!mbar_wait(&bar->acc_empty[u], ((blk / NBUF) & 1) ^ 1, abort, err_flag, 3)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
                     const uint32_t a = a0 + uint32_t(j * 64);
                     const uint32_t b = a0 + uint32_t(A_BYTES + j * B_BYTES);
-                    const uint32_t d = tmem + uint32_t(p * 2 * BN + j * BN);
+                    const uint32_t d = tmem + uint32_t(u * BN);
                     // K half 0: A bytes +0..31, B hi +0..31, lo +64..95;
                     // K half 1: A bytes +32..63, B hi +32..63, lo +96..127.
                     mma_f16_id(d, sw128_desc(a), sw128_desc(b), IDESC, 0);
                     mma_f16_id(d, sw128_desc(a), sw128_desc(b + 64), IDESC, 1);
                     mma_f16_id(d, sw128_desc(a + 32), sw128_desc(b + 32), IDESC, 1);
                     mma_f16_id(d, sw128_desc(a + 32), sw128_desc(b + 96), IDESC, 1);
+                    mma_commit(&bar->acc_full[u]);
                 }
-                mma_commit(&bar->acc_full[p]);
                 mma_commit(&bar->empty[s]);
             }
         }
@@ -180,33 +210,28 @@ __global__ void __launch_bounds__(THREADS, 1)
         float2 acc[CPW / 2];
 #pragma unroll
         for (int c = 0; c < CPW / 2; ++c) acc[c] = make_float2(0.f, 0.f);
-        for (int pr = 0; pr < npairs; ++pr) {
-            const int p = pr % NPAIR, c = pr % SC_SLOTS;
-            const bool got = mbar_wait(&bar->sc_full[c], (pr / SC_SLOTS) & 1, abort, err_flag, 6) &&
-                             mbar_wait(&bar->acc_full[p], (pr / NPAIR) & 1, abort, err_flag, 4);
+        for (int blk = 0; blk < nb; ++blk) {
+            const int u = blk % NBUF, g = blk / DA_GROUP, c = g % DA_SLOTS;
+            const bool got = (blk % DA_GROUP != 0 || mbar_wait(&bar->da_full[c], (g / DA_SLOTS) & 1, abort, err_flag, 6)) &&
+                             mbar_wait(&bar->acc_full[u], (blk / NBUF) & 1, abort, err_flag, 4);
             if (!__all_sync(0xffffffffu, got)) break;
             tc_fence_after();
-#pragma unroll
-            for (int j = 0; j < 2; ++j) {
-                if (2 * pr + j >= nb) break;
-                const float da = ring[c * 256 + j * 128 + q * 32 + lane];
-                const float2 da2 = make_float2(da, da);
-                const uint32_t taddr = tmem + (uint32_t(q * 32) << 16) + uint32_t(p * 2 * BN + j * BN + h * CPW);
-                uint32_t r[64];
-                tmem_ld32(taddr, r);
-                tmem_ld32(taddr + 32, r + 32);
-                tmem_wait_ld();
-#pragma unroll
-                for (int i = 0; i < 32; ++i)
-                    acc[i] = __ffma2_rn(da2, make_float2(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1])),
-                                        acc[i]);
-            }
+            const float da = ring[c * (DA_BYTES / 4) + (blk % DA_GROUP) * BM + q * 32 + lane];
+            const float2 da2 = make_float2(da, da);
+            const uint32_t taddr = tmem + (uint32_t(q * 32) << 16) + uint32_t(u * BN + h * CPW);
+            uint32_t r[CPW];
+            tmem_ld32(taddr, r);
+            if constexpr (CPW == 64) tmem_ld32(taddr + 32, r + 32);
+            tmem_wait_ld();
             tc_fence_before();
             __syncwarp();
             if (lane == 0) {
-                mbar_arrive(&bar->acc_empty[p]);
-                mbar_arrive(&bar->sc_empty[c]);
+                mbar_arrive(&bar->acc_empty[u]);
+                if (blk % DA_GROUP == DA_GROUP - 1 || blk == nb - 1) mbar_arrive(&bar->da_empty[c]);
             }
+#pragma unroll
+            for (int i = 0; i < CPW / 2; ++i)
+                acc[i] = __ffma2_rn(da2, make_float2(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1])), acc[i]);
         }
         // y = acc * 2^-e_j (+ bias), written through shared memory.
         const int col0 = n0 + h * CPW;
@@ -305,14 +330,19 @@ bool encode_map(CUtensorMap* map, CUtensorMapDataType dt, int esize, const void*
     return true;
 }
 
-cudaError_t launch_fold(const ActsView& v, const Weight& w, const float* bias, float* y, int* err_flag,
+template <int BN>
+cudaError_t launch_fold_bn(const ActsView& v, const Weight& w, const float* bias, float* y, int* err_flag,
                         cudaStream_t s, char* why, size_t why_len) {
-    CUtensorMap ma, mb, my;
+    CUtensorMap ma, mb, my, md;
     if (!encode_map(&ma, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, v.q16, uint64_t(v.k), uint64_t(v.m), 64, BM,
                     CU_TENSOR_MAP_SWIZZLE_128B, why, why_len))
         return cudaErrorInvalidValue;
     if (!encode_map(&mb, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, w.bhl, uint64_t(w.nb) * 64, uint64_t(w.n), 64, BN,
                     CU_TENSOR_MAP_SWIZZLE_128B, why, why_len))
+        return cudaErrorInvalidValue;
+    // d_a rows, transposed [nb][m_pad]: a box is 16 blocks x 128 rows.
+    if (!encode_map(&md, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, v.dT, uint64_t(v.m_pad), uint64_t(w.nb), BM, DA_GROUP,
+                    CU_TENSOR_MAP_SWIZZLE_NONE, why, why_len))
         return cudaErrorInvalidValue;
     // Output through TMA stores when the row pitch is 16-byte aligned.
     int use_tma_store = (w.n % 4 == 0) && (reinterpret_cast<uintptr_t>(y) % 16 == 0);
@@ -324,13 +354,28 @@ cudaError_t launch_fold(const ActsView& v, const Weight& w, const float* bias, f
     int dev = 0;
     cudaGetDevice(&dev);
     if (!(attr_dev_mask & (1 << dev))) {
-        cudaError_t e = cudaFuncSetAttribute(k_gemm_fold, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
+        cudaError_t e = cudaFuncSetAttribute(k_gemm_fold<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             Fold<BN>::SMEM);
         if (e != cudaSuccess) return e;
         attr_dev_mask |= 1 << dev;
     }
     dim3 grid((w.n + BN - 1) / BN, (v.m + BM - 1) / BM);
-    return launch_pdl(k_gemm_fold, grid, dim3(THREADS), SMEM, s, ma, mb, my, use_tma_store, v.dT, w.colscale, bias, y,
-                      v.m, w.n, w.nb, v.m_pad, err_flag);
+    return launch_pdl(k_gemm_fold<BN>, grid, dim3(THREADS), Fold<BN>::SMEM, s, ma, mb, my, md, use_tma_store, w.colscale, bias, y,
+                      v.m, w.n, w.nb, err_flag);
+}
+
+cudaError_t launch_fold(const ActsView& v, const Weight& w, const float* bias, float* y, int* err_flag,
+                        cudaStream_t s, char* why, size_t why_len) {
+    static int sm_count[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 64 && sm_count[dev] == 0) cudaDeviceGetAttribute(&sm_count[dev], cudaDevAttrMultiProcessorCount, dev);
+    const int sms = dev < 64 ? sm_count[dev] : 148;
+    const long tiles128 = long((w.n + 127) / 128) * ((v.m + BM - 1) / BM);
+    // 64-wide tiles when they still fit in one wave and 128-wide ones
+    // would leave at least half the SMs idle.
+    if (2 * tiles128 <= sms) return launch_fold_bn<64>(v, w, bias, y, err_flag, s, why, why_len);
+    return launch_fold_bn<128>(v, w, bias, y, err_flag, s, why, why_len);
 }
 
 }  // namespace
