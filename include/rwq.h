@@ -151,6 +151,40 @@ int rwq_set_gemm_path(int path);
 /* Synchronize `stream` and report any fault a kernel recorded on it. */
 int rwq_stream_check(void* stream);
 
+/* ---- Model files ---------------------------------------------------------
+ * Replace `model::load_model` (reference src/model.rs:145-275, legacy ggml
+ * container) and `gguf::load` (src/gguf.rs:156-300, GGUF v2/v3), chosen by
+ * the file's magic.  Parsing touches no GPU: hyper-parameters, the mel
+ * filterbank, the vocabulary (padded with "[_extra_token_<i>]" to n_vocab)
+ * and the tensors (f32; f16 widened to f32; quantized blocks kept verbatim).
+ * A 2-D quantized tensor becomes a device weight the first time
+ * rwq_model_qtensor asks for it (raw blocks uploaded unchanged, on the
+ * current device); the model owns it.  Tensor shapes are row-major (the
+ * reverse of ggml's ne[]), shape3 padded with 1s. */
+typedef struct rwq_model rwq_model;
+
+int rwq_model_load(const char* path, rwq_model** out);
+int rwq_model_load_memory(const uint8_t* data, size_t len, rwq_model** out);
+int rwq_model_free(rwq_model* m);
+/* n_vocab, n_audio_ctx, n_audio_state, n_audio_head, n_audio_layer,
+ * n_text_ctx, n_text_state, n_text_head, n_text_layer, n_mels, ftype
+ * (the reference's HParams field order). */
+int rwq_model_hparams(const rwq_model* m, int32_t* out11);
+int rwq_model_mel_filters(const rwq_model* m, const float** data, int64_t* n_mel, int64_t* n_fft_bins);
+int rwq_model_vocab_size(const rwq_model* m, int64_t* n);
+int rwq_model_token(const rwq_model* m, int64_t id, const char** bytes, int64_t* len);
+int rwq_model_n_tensors(const rwq_model* m, int64_t* n);
+int rwq_model_find(const rwq_model* m, const char* name, int64_t* index);
+int rwq_model_tensor(const rwq_model* m, int64_t i, const char** name, int* dtype, int* ndims, int64_t* shape3);
+/* The raw ggml blocks of a quantized tensor (host memory owned by m). */
+int rwq_model_tensor_raw(const rwq_model* m, int64_t i, const uint8_t** data, size_t* len);
+/* Device weight of a 2-D quantized tensor (owned by m; do not free). */
+int rwq_model_qtensor(rwq_model* m, int64_t i, rwq_qtensor** out);
+/* Host f32 values of a dense tensor (f32/f16), or of a quantized tensor
+ * of rank 1 or 3 (dequantized bit-exactly on the GPU on first call, like
+ * the reference's load-time `to_dense`). */
+int rwq_model_dense(rwq_model* m, int64_t i, const float** data, int64_t* n);
+
 #ifdef __cplusplus
 }
 #endif

@@ -43,6 +43,21 @@ SIGNATURES = {
     "rwq_matmul_t_q_noalloc": (_I, [_P, _L, _L, _P, _P, _P, _P]),
     "rwq_set_gemm_path": (_I, [_I]),
     "rwq_stream_check": (_I, [_P]),
+    "rwq_model_load": (_I, [ctypes.c_char_p, ctypes.POINTER(_P)]),
+    "rwq_model_load_memory": (_I, [_P, _SZ, ctypes.POINTER(_P)]),
+    "rwq_model_free": (_I, [_P]),
+    "rwq_model_hparams": (_I, [_P, ctypes.POINTER(ctypes.c_int32)]),
+    "rwq_model_mel_filters": (_I, [_P, ctypes.POINTER(ctypes.POINTER(ctypes.c_float)), ctypes.POINTER(_L),
+                                   ctypes.POINTER(_L)]),
+    "rwq_model_vocab_size": (_I, [_P, ctypes.POINTER(_L)]),
+    "rwq_model_token": (_I, [_P, _L, ctypes.POINTER(ctypes.c_void_p), ctypes.POINTER(_L)]),
+    "rwq_model_n_tensors": (_I, [_P, ctypes.POINTER(_L)]),
+    "rwq_model_find": (_I, [_P, ctypes.c_char_p, ctypes.POINTER(_L)]),
+    "rwq_model_tensor": (_I, [_P, _L, ctypes.POINTER(ctypes.c_char_p), ctypes.POINTER(_I), ctypes.POINTER(_I),
+                              ctypes.POINTER(_L)]),
+    "rwq_model_tensor_raw": (_I, [_P, _L, ctypes.POINTER(ctypes.c_void_p), ctypes.POINTER(_SZ)]),
+    "rwq_model_qtensor": (_I, [_P, _L, ctypes.POINTER(_P)]),
+    "rwq_model_dense": (_I, [_P, _L, ctypes.POINTER(ctypes.POINTER(ctypes.c_float)), ctypes.POINTER(_L)]),
 }
 
 _lib = None

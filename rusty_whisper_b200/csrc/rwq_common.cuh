@@ -12,8 +12,8 @@
 // On the device a weight lives as "planes" (same bytes per block as the
 // ggml record, split so every block's code bytes start on a 16-byte
 // boundary):  qs [n][nb][QSB]  (QSB = 16, or 32 for Q8_0),
-//             qh [n][nb] u32 (Q5 only), d [n][nb] f16 bits,
-//             m [n][nb] f16 bits (Q4_1/Q5_1 only).
+//             qh [n][nb] u32 (Q5 only, bits permuted: see qh_plane_bits),
+//             d [n][nb] f16 bits, m [n][nb] f16 bits (Q4_1/Q5_1 only).
 #pragma once
 #include <cstdint>
 #include <cuda_runtime.h>
@@ -49,12 +49,25 @@ __device__ __forceinline__ float h2f(uint16_t h) {
     return f;
 }
 
-// Spread 4 bits b[3:0] to bit 4 of bytes 0..3: bit i*(1+7) lands on bit
-// 4+8i and no two shifted copies overlap, so the product never carries.
-__device__ __forceinline__ uint32_t spread4_to_bit4(uint32_t b4) { return (b4 * 0x02040810u) & 0x10101010u; }
+// The Q5 high-bit plane stores ggml's qh with its bits permuted so that a
+// code word's four fifth bits come out with one shift and one mask: bit
+// 4t+i (element 4t+i, i < 4) moves to bit 8i+t and bit 16+4t+i to bit
+// 8i+4+t.  Then for word t (elements 4t..4t+3) the fifth bits are
+// (p << (4-t)) & 0x10101010 and for word 4+t (elements 16+4t..) they are
+// (p >> t) & 0x10101010; no other bit lands on bit 4 of a byte.  Applied
+// once when a weight is uploaded (k_repack).
+__host__ __device__ inline uint32_t qh_plane_bits(uint32_t h) {
+    uint32_t p = 0;
+    for (int e = 0; e < 32; ++e) {
+        const int upper = e >> 4, t = (e & 15) >> 2, i = e & 3;
+        p |= ((h >> e) & 1u) << (8 * i + 4 * upper + t);
+    }
+    return p;
+}
 
 // Unsigned 5-/4-bit code words for one block: word t < 4 holds elements
 // 4t..4t+3, word 4+t holds elements 16+4t..16+4t+3, one code per byte.
+// `qh` is the permuted plane word (qh_plane_bits).
 template <int DT>
 __device__ __forceinline__ void codes_u8x4(const uint4 qs, uint32_t qh, uint32_t (&w)[8]) {
     const uint32_t v[4] = {qs.x, qs.y, qs.z, qs.w};
@@ -63,8 +76,8 @@ __device__ __forceinline__ void codes_u8x4(const uint4 qs, uint32_t qh, uint32_t
         uint32_t lo = v[t] & 0x0F0F0F0Fu;
         uint32_t hi = (v[t] >> 4) & 0x0F0F0F0Fu;
         if (has_qh(DT)) {
-            lo |= spread4_to_bit4((qh >> (4 * t)) & 0xFu);
-            hi |= spread4_to_bit4((qh >> (16 + 4 * t)) & 0xFu);
+            lo |= (qh << (4 - t)) & 0x10101010u;
+            hi |= (qh >> t) & 0x10101010u;
         }
         w[t] = lo;
         w[4 + t] = hi;

@@ -31,7 +31,8 @@ __global__ void k_repack(const uint8_t* __restrict__ raw, uint8_t* __restrict__ 
     if (has_min(DT)) m[b] = uint16_t(p[2] | (p[3] << 8));
     if (has_qh(DT)) {
         const uint8_t* h = p + raw_qh_off(DT);
-        qh[b] = uint32_t(h[0]) | (uint32_t(h[1]) << 8) | (uint32_t(h[2]) << 16) | (uint32_t(h[3]) << 24);
+        qh[b] = qh_plane_bits(uint32_t(h[0]) | (uint32_t(h[1]) << 8) | (uint32_t(h[2]) << 16) |
+                              (uint32_t(h[3]) << 24));
     }
     uint32_t words[QSB / 4];
 #pragma unroll
@@ -264,7 +265,6 @@ __global__ void __launch_bounds__(TPB) k_gemv_i8(const uint8_t* __restrict__ qs,
                                                  const int32_t* __restrict__ sa, const float* __restrict__ ua, int M,
                                                  int N, int K, const float* __restrict__ bias, float* __restrict__ y) {
     pdl_trigger();
-    pdl_wait();
     const int nb = K / QK;
     constexpr int RPW = 32 / L;
     const int lane = threadIdx.x & 31, sub = lane % L, slot = lane / L;
@@ -282,8 +282,12 @@ __global__ void __launch_bounds__(TPB) k_gemv_i8(const uint8_t* __restrict__ qs,
             if (grp < groups && j < N && kb < nb) load_raw<DT>(qs, qh, dp, mp, size_t(j) * nb + kb, dst[t]);
         }
     };
+    // The weights are not written by the previous kernel in the stream, so
+    // their first loads go out before waiting for it; the activations and
+    // the output are, so everything else waits.
 #pragma unroll
     for (int u = 0; u < PF; ++u) fetch(g0 + u * nw, ring[u]);
+    pdl_wait();
 
     // This lane's activation blocks, for every row: in registers when they
     // are few (REGA), else staged once per CTA in shared memory.
@@ -378,9 +382,11 @@ __global__ void __launch_bounds__(TPB) k_gemv_i8(const uint8_t* __restrict__ qs,
             fetch(g + PF * nw, ring[u]);
 #pragma unroll
             for (int r = 0; r < MR; ++r) {
+                if (r < M) {   // M is the same for the whole warp
 #pragma unroll
-                for (int o = L / 2; o > 0; o >>= 1)
-                    acc[r] = __fadd_rn(acc[r], __shfl_xor_sync(0xffffffffu, acc[r], o));
+                    for (int o = L / 2; o > 0; o >>= 1)
+                        acc[r] = __fadd_rn(acc[r], __shfl_xor_sync(0xffffffffu, acc[r], o));
+                }
             }
             if (g < groups && j < N && sub == 0) {
                 const float b = bias ? __ldg(bias + j) : 0.f;

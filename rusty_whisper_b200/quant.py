@@ -81,6 +81,18 @@ class QTensor:
         _lib.check(rc)
         self._h = h
 
+    @classmethod
+    def _borrowed(cls, handle, shape, dtype: int, device: int, owner) -> "QTensor":
+        """A view of a device weight owned by ``owner`` (a loaded model):
+        never freed here, and it keeps the owner alive."""
+        q = cls.__new__(cls)
+        q.shape = [int(shape[0]), int(shape[1])]
+        q.dtype = int(dtype)
+        q.device = device
+        q._h = handle
+        q._owner = owner
+        return q
+
     @property
     def handle(self) -> ctypes.c_void_p:
         return self._h
@@ -119,6 +131,9 @@ class QTensor:
             return out
 
     def free(self) -> None:
+        if getattr(self, "_owner", None) is not None:
+            self._h = None   # borrowed: the owner frees it
+            return
         if getattr(self, "_h", None):
             try:
                 _lib.lib().rwq_qtensor_free(self._h)
