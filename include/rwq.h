@@ -185,6 +185,28 @@ int rwq_model_qtensor(rwq_model* m, int64_t i, rwq_qtensor** out);
  * the reference's load-time `to_dense`). */
 int rwq_model_dense(rwq_model* m, int64_t i, const float** data, int64_t* n);
 
+/* ---- Log-mel front end -----------------------------------------------
+ * Replaces `audio::log_mel_spectrogram` (reference src/audio.rs:147-198):
+ * periodic Hann window, 400-point FFT with hop 160 over the reflect-padded
+ * signal, power, the mel filterbank, log10, then per window the clamp to
+ * (max - 8) and (x + 4) / 4.  A plan holds a filterbank ([n_mels][201]
+ * f32, host memory, e.g. from rwq_model_mel_filters or
+ * rwq_mel_filterbank) prepared for the GPU. */
+typedef struct rwq_mel rwq_mel;
+
+/* `audio::mel_filterbank` (src/audio.rs:107-130) into out[n_mels][n_fft/2+1]. */
+int rwq_mel_filterbank(int n_mels, int n_fft, int sample_rate, float* out);
+int rwq_mel_new(const float* filters, int n_mels, rwq_mel** out);
+int rwq_mel_free(rwq_mel* p);
+/* Device buffers: samples [n_windows][n_samples] -> out
+ * [n_windows][n_mels][n_samples / 160], each window normalised on its own
+ * maximum; asynchronous on `stream`.  One plan serves one stream at a
+ * time.  n_samples >= 201. */
+int rwq_log_mel_dev(rwq_mel* p, const float* samples, int64_t n_windows, int64_t n_samples, float* out,
+                    void* stream);
+/* One window, host buffers (copies inside, synchronous). */
+int rwq_log_mel(rwq_mel* p, const float* samples, int64_t n_samples, float* out);
+
 #ifdef __cplusplus
 }
 #endif

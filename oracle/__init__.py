@@ -64,6 +64,10 @@ def lib():
             "orc_qtensor_new": (P, [i32, P, i32, i32]),
             "orc_qtensor_free": (None, [P]),
             "orc_qtensor_matmul": (i32, [P, P, i32, P, i32, i32]),
+            "orc_hann_window": (None, [i32, P]),
+            "orc_fft": (i32, [P, P, i32, P, P, i32]),
+            "orc_mel_filterbank": (None, [i32, i32, i32, P]),
+            "orc_log_mel": (i32, [P, i32, P, i32, P, P, i32]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(L, name)
@@ -236,4 +240,41 @@ def quantize_q5_1(x: np.ndarray) -> np.ndarray:
     x = np.ascontiguousarray(x, np.float32).ravel()
     out = np.zeros(x.size // QK * 24, np.uint8)
     lib().orc_quantize_q5_1(_p(x), x.size, _p(out))
+    return out
+
+
+# ---------------------------------------------------------------- log-mel
+N_FFT, HOP_LENGTH, N_FREQS, SAMPLE_RATE = 400, 160, 201, 16000
+
+
+def hann_window(n: int = N_FFT) -> np.ndarray:
+    out = np.zeros(n, np.float32)
+    lib().orc_hann_window(n, _p(out))
+    return out
+
+
+def fft(re: np.ndarray, im: np.ndarray, naive: bool = False):
+    re = np.ascontiguousarray(re, np.float32)
+    im = np.ascontiguousarray(im, np.float32)
+    n = re.size
+    o_re, o_im = np.zeros(n, np.float32), np.zeros(n, np.float32)
+    _check(lib().orc_fft(_p(re), _p(im), n, _p(o_re), _p(o_im), int(naive)), "fft")
+    return o_re, o_im
+
+
+def mel_filterbank(n_mels: int = 80, n_fft: int = N_FFT, sample_rate: int = SAMPLE_RATE) -> np.ndarray:
+    out = np.zeros((n_mels, n_fft // 2 + 1), np.float32)
+    lib().orc_mel_filterbank(n_mels, n_fft, sample_rate, _p(out))
+    return out
+
+
+def log_mel_spectrogram(samples: np.ndarray, filters: np.ndarray, n_mels: int, threads: int = 0) -> np.ndarray:
+    """audio.rs:147-198: [n_mels, n_samples // 160] f32."""
+    samples = np.ascontiguousarray(samples, np.float32)
+    filters = np.ascontiguousarray(filters, np.float32)
+    n_frames = samples.size // HOP_LENGTH
+    out = np.zeros((n_mels, n_frames), np.float32)
+    nf = ctypes.c_int(0)
+    _check(lib().orc_log_mel(_p(samples), samples.size, _p(filters), n_mels, _p(out), ctypes.byref(nf), threads),
+           "log_mel")
     return out

@@ -17,6 +17,9 @@
 //                                      quant.rs:754-1051
 //   * f32 fallback (dequant + dot4)    quant.rs:995-1018, tensor.rs:104-158
 //   * dense matmul_t                   tensor.rs:165-258
+//   * log-mel front end: periodic Hann window, 400-point FFT (radix-2
+//     recursion down to odd-length DFTs), power spectrum, Slaney mel
+//     filterbank, log10 + dynamic-range clamp  audio.rs:10-198
 //   * test helpers: LCG test_matrix, rand_byte, quantize_q8_0, quantize_q5_1
 //                                      quant.rs:1071-1123, quant.rs:1131-1135
 //
@@ -882,6 +885,168 @@ void orc_quantize_q5_1(const float* x, size_t count, uint8_t* raw) {
         for (int b = 0; b < 4; ++b) *raw++ = uint8_t(qh >> (8 * b));
         for (int e = 0; e < 16; ++e) *raw++ = uint8_t((qs[e] & 0xF) | ((qs[e + 16] & 0xF) << 4));
     }
+}
+
+// ------------------------------------------------------------- log-mel
+// audio.rs:10-198, operation for operation in f32 (libm sinf/cosf/logf/
+// expf/log10f are what Rust's f32 methods call on this platform).
+
+}  // extern "C"
+
+namespace {
+
+constexpr int A_N_FFT = 400, A_HOP = 160, A_N_FREQS = A_N_FFT / 2 + 1;
+constexpr float A_PI = 3.14159265358979323846f;   // std::f32::consts::PI
+
+// audio.rs:55-72
+void dft_ref(const std::vector<float>& re, const std::vector<float>& im, std::vector<float>& ore,
+             std::vector<float>& oim) {
+    const size_t n = re.size();
+    ore.assign(n, 0.f);
+    oim.assign(n, 0.f);
+    for (size_t k = 0; k < n; ++k) {
+        float sr = 0.f, si = 0.f;
+        for (size_t t = 0; t < n; ++t) {
+            const float theta = -2.0f * A_PI * float(k * t) / float(n);
+            const float s = std::sin(theta), c = std::cos(theta);
+            sr += re[t] * c - im[t] * s;
+            si += re[t] * s + im[t] * c;
+        }
+        ore[k] = sr;
+        oim[k] = si;
+    }
+}
+
+// audio.rs:20-53: even n splits into even/odd halves, odd n is a DFT.
+void fft_ref(const std::vector<float>& re, const std::vector<float>& im, std::vector<float>& ore,
+             std::vector<float>& oim) {
+    const size_t n = re.size();
+    if (n == 1) {
+        ore = re;
+        oim = im;
+        return;
+    }
+    if (n % 2 == 1) {
+        dft_ref(re, im, ore, oim);
+        return;
+    }
+    const size_t half = n / 2;
+    std::vector<float> er(half), ei(half), odr(half), odi(half);
+    for (size_t i = 0; i < half; ++i) {
+        er[i] = re[2 * i];
+        ei[i] = im[2 * i];
+        odr[i] = re[2 * i + 1];
+        odi[i] = im[2 * i + 1];
+    }
+    std::vector<float> Er, Ei, Or, Oi;
+    fft_ref(er, ei, Er, Ei);
+    fft_ref(odr, odi, Or, Oi);
+    ore.assign(n, 0.f);
+    oim.assign(n, 0.f);
+    for (size_t k = 0; k < half; ++k) {
+        const float theta = -2.0f * A_PI * float(k) / float(n);
+        const float s = std::sin(theta), c = std::cos(theta);
+        const float tr = c * Or[k] - s * Oi[k];
+        const float ti = c * Oi[k] + s * Or[k];
+        ore[k] = Er[k] + tr;
+        oim[k] = Ei[k] + ti;
+        ore[k + half] = Er[k] - tr;
+        oim[k + half] = Ei[k] - ti;
+    }
+}
+
+// audio.rs:81-102 (Slaney scale)
+float hz_to_mel(float hz) {
+    const float F_SP = 200.0f / 3.0f, MIN_LOG_HZ = 1000.0f, MIN_LOG_MEL = MIN_LOG_HZ / F_SP;
+    if (hz < MIN_LOG_HZ) return hz / F_SP;
+    return MIN_LOG_MEL + std::log(hz / MIN_LOG_HZ) / (std::log(6.4f) / 27.0f);
+}
+float mel_to_hz(float mel) {
+    const float F_SP = 200.0f / 3.0f, MIN_LOG_HZ = 1000.0f, MIN_LOG_MEL = MIN_LOG_HZ / F_SP;
+    if (mel < MIN_LOG_MEL) return mel * F_SP;
+    return MIN_LOG_HZ * std::exp((mel - MIN_LOG_MEL) * (std::log(6.4f) / 27.0f));
+}
+
+}  // namespace
+
+extern "C" {
+
+// audio.rs:74-79
+void orc_hann_window(int n, float* out) {
+    for (int i = 0; i < n; ++i) out[i] = 0.5f * (1.0f - std::cos(2.0f * A_PI * float(i) / float(n)));
+}
+
+int orc_fft(const float* re, const float* im, int n, float* ore, float* oim, int naive) {
+    std::vector<float> r(re, re + n), m(im, im + n), a, b;
+    if (naive) dft_ref(r, m, a, b);
+    else fft_ref(r, m, a, b);
+    std::memcpy(ore, a.data(), sizeof(float) * n);
+    std::memcpy(oim, b.data(), sizeof(float) * n);
+    return 0;
+}
+
+// audio.rs:107-130
+void orc_mel_filterbank(int n_mels, int n_fft, int sample_rate, float* out) {
+    const int n_freqs = n_fft / 2 + 1;
+    const float fmax = float(sample_rate) / 2.0f;
+    const float mel_max = hz_to_mel(fmax);
+    std::vector<float> edges(size_t(n_mels) + 2);
+    for (int i = 0; i < n_mels + 2; ++i) edges[size_t(i)] = mel_to_hz(mel_max * float(i) / float(n_mels + 1));
+    std::fill(out, out + size_t(n_mels) * n_freqs, 0.f);
+    for (int m = 0; m < n_mels; ++m) {
+        const float f_lo = edges[size_t(m)], f_center = edges[size_t(m) + 1], f_hi = edges[size_t(m) + 2];
+        const float norm = 2.0f / (f_hi - f_lo);
+        for (int k = 0; k < n_freqs; ++k) {
+            const float f = float(k) * float(sample_rate) / float(n_fft);
+            const float w = std::fmin((f - f_lo) / (f_center - f_lo), (f_hi - f) / (f_hi - f_center));
+            if (w > 0.0f) out[size_t(m) * n_freqs + k] = w * norm;
+        }
+    }
+}
+
+// audio.rs:147-198: `out` is n_mels x n_frames, n_frames = n / 160.
+int orc_log_mel(const float* samples, int n, const float* filters, int n_mels, float* out, int* n_frames_out,
+                int threads) {
+    if (n < A_N_FFT / 2 + 1) return -1;
+    std::vector<float> window(A_N_FFT);
+    orc_hann_window(A_N_FFT, window.data());
+    const int pad = A_N_FFT / 2;
+    std::vector<float> padded(size_t(n) + 2 * pad);
+    for (long i = 0; i < long(n) + 2 * pad; ++i) {
+        long j = i - pad;
+        if (j < 0) j = -j;
+        else if (j >= n) j = 2L * (n - 1) - j;
+        padded[size_t(i)] = samples[std::min<long>(j, n - 1)];
+    }
+    const int n_frames = n / A_HOP;
+    std::vector<float> power(size_t(n_frames) * A_N_FREQS);
+    auto frames = [&](int t0, int t1) {
+        std::vector<float> re(A_N_FFT), im(A_N_FFT, 0.f), fr, fi;
+        for (int t = t0; t < t1; ++t) {
+            for (int i = 0; i < A_N_FFT; ++i) re[size_t(i)] = padded[size_t(t) * A_HOP + i] * window[size_t(i)];
+            std::fill(im.begin(), im.end(), 0.f);
+            fft_ref(re, im, fr, fi);
+            for (int k = 0; k < A_N_FREQS; ++k)
+                power[size_t(t) * A_N_FREQS + k] = fr[size_t(k)] * fr[size_t(k)] + fi[size_t(k)] * fi[size_t(k)];
+        }
+    };
+    if (threads <= 0) threads = n_threads_default();
+    if (threads > 1 && n_frames >= threads) {
+        const int chunk = (n_frames + threads - 1) / threads;
+        std::vector<std::thread> ths;
+        for (int t0 = 0; t0 < n_frames; t0 += chunk) ths.emplace_back(frames, t0, std::min(n_frames, t0 + chunk));
+        for (auto& th : ths) th.join();
+    } else {
+        frames(0, n_frames);
+    }
+    orc_matmul_t(filters, n_mels, A_N_FREQS, power.data(), n_frames, out, threads);
+    const size_t total = size_t(n_mels) * n_frames;
+    for (size_t i = 0; i < total; ++i) out[i] = std::log10(std::fmax(out[i], 1e-10f));
+    float mmax = -3.40282347e+38f;   // f32::MIN
+    for (size_t i = 0; i < total; ++i) mmax = std::fmax(mmax, out[i]);
+    for (size_t i = 0; i < total; ++i) out[i] = (std::fmax(out[i], mmax - 8.0f) + 4.0f) / 4.0f;
+    if (n_frames_out) *n_frames_out = n_frames;
+    return 0;
 }
 
 }  // extern "C"

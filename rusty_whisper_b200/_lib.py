@@ -58,6 +58,11 @@ SIGNATURES = {
     "rwq_model_tensor_raw": (_I, [_P, _L, ctypes.POINTER(ctypes.c_void_p), ctypes.POINTER(_SZ)]),
     "rwq_model_qtensor": (_I, [_P, _L, ctypes.POINTER(_P)]),
     "rwq_model_dense": (_I, [_P, _L, ctypes.POINTER(ctypes.POINTER(ctypes.c_float)), ctypes.POINTER(_L)]),
+    "rwq_mel_filterbank": (_I, [_I, _I, _I, _P]),
+    "rwq_mel_new": (_I, [_P, _I, ctypes.POINTER(_P)]),
+    "rwq_mel_free": (_I, [_P]),
+    "rwq_log_mel_dev": (_I, [_P, _P, _L, _L, _P, _P]),
+    "rwq_log_mel": (_I, [_P, _P, _L, _P]),
 }
 
 _lib = None
