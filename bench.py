@@ -238,6 +238,7 @@ def run_ours(args, rank, world, local_rank):
 
     gemv = run_gemv(args, dev, quant, w_np, hbm_peak, stream) if args.only == "all" else None
     e2e = run_e2e(args, dev, quant, W, acts_np, world) if args.only == "all" else None
+    frontend = run_frontend(args, dev, hbm_peak, stream, rank, world) if args.only == "all" else None
     clk.__exit__(None, None, None)
 
     if rank != 0:
@@ -261,12 +262,61 @@ def run_ours(args, rank, world, local_rank):
             "per_format_tops": by_fmt,
         },
         "gemv": gemv,
+        "frontend": frontend,
         "e2e": e2e,
         "clocks": clk.summary(),
     }
     if world == 1 and not args.no_cpu:
         line["cpu_baseline"] = cpu_baseline(acts_np, w_np)
     print(json.dumps(line), flush=True)
+
+
+def run_frontend(args, dev, hbm_peak, stream, rank, world):
+    """BASELINE config 5's front end: log-mel of 256 windows of 30 s
+    (audio.rs:147-198) on the GPU in one batch, against the C restatement
+    of the reference on this host's cores (a bounded sample)."""
+    import torch
+    from rusty_whisper_b200 import audio
+    n_win, n_mels = 256, 80
+    distinct = [synth.speechlike_window(500 + 7 * i) for i in range(8)]
+    host = np.stack([distinct[i % 8] for i in range(n_win)])
+    x = torch.from_numpy(host).to(dev)
+    fb = audio.mel_filterbank(n_mels)
+    plan = audio.LogMel(fb, n_mels)
+    out = torch.empty((n_win, n_mels, synth.AUDIO_WINDOW // audio.HOP_LENGTH), device=dev)
+    for _ in range(3):
+        plan.batch(x, out)
+    torch.cuda.synchronize()
+    reps = max(3, min(args.steps, 10))
+    torch.cuda._sleep(GATE_CYCLES)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(reps):
+        plan.batch(x, out)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    t = e0.elapsed_time(e1) / 1e3 / reps
+    frames = synth.AUDIO_WINDOW // audio.HOP_LENGTH
+    # samples read once; mel written, then read and written by the normaliser
+    nbytes = n_win * (4.0 * synth.AUDIO_WINDOW + 3 * 4.0 * n_mels * frames)
+    res = {"workload": f"{n_win} windows x 30 s, {n_mels} mels (BASELINE config 5 front end)",
+           "windows_per_s": round(world * n_win / t, 1), "audio_s_per_s": round(world * n_win * 30.0 / t, 1),
+           "us_per_window": round(t / n_win * 1e6, 3), "GB/s": round(nbytes / t / 1e9, 1),
+           "frac_of_measured_hbm": round(nbytes / t / 1e9 / hbm_peak, 4), "bound": "hbm",
+           "kernels": "k_log_mel + k_mel_norm (csrc/rwq_mel.cu)", "gpu_launches": 3 * reps}
+    if rank == 0 and world == 1 and not args.no_cpu:
+        import time
+        import oracle
+        threads = oracle.default_threads()
+        t0 = time.perf_counter()
+        for i in range(2):
+            oracle.log_mel_spectrogram(distinct[i], fb, n_mels, threads=threads)
+        tc = (time.perf_counter() - t0) / 2
+        res["cpu_baseline"] = {"audio_s_per_s": round(30.0 / tc, 1), "s_per_window": round(tc, 4),
+                               "cores": threads, "kind": "port",
+                               "sample": "2 windows of 30 s through the C restatement of audio.rs:147-198"}
+    return res
 
 
 def run_gemv(args, dev, quant, w_np, hbm_peak, stream):

@@ -129,3 +129,21 @@ def sweep_weight(dtype: int, k: int, n: int, seed: int = 0) -> np.ndarray:
 
 def sweep_acts(m: int, k: int, seed: int = 0) -> np.ndarray:
     return normal(5000 + 31 * seed + m + 3 * k, m * k).reshape(m, k)
+
+
+# BASELINE config 5's audio: 30 s windows of 16 kHz band-limited noise at
+# about -20 dBFS with random silences of 0.2-2 s (synthetic speech stand-in).
+AUDIO_WINDOW = 480_000
+
+
+def speechlike_window(seed: int, n: int = AUDIO_WINDOW) -> np.ndarray:
+    x = normal(seed, n, 0.0, 1.0).astype(np.float64)
+    # band-limit with a 9-tap Hann smoother, then scale to ~-20 dBFS RMS
+    k = np.hanning(11)[1:-1]
+    x = np.convolve(x, k / k.sum(), mode="same")
+    x *= 0.1 / max(float(np.sqrt(np.mean(x * x))), 1e-12)
+    starts = randint(seed + 1, 8, 0, n - 1)
+    lens = randint(seed + 2, 8, 3200, 32000)
+    for a, ln in zip(starts, lens):
+        x[int(a):int(a) + int(ln)] = 0.0
+    return x.astype(np.float32)
