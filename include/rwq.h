@@ -148,6 +148,16 @@ int rwq_matmul_t_q_noalloc(const float* a, int64_t m, int64_t k, const rwq_qtens
  * host thread. */
 int rwq_set_gemm_path(int path);
 
+/* Force the kernel of the CUDA-core / GEMV family (m <= 8, or path 1
+ * above) for testing and benchmarking: 0 = automatic (the integer-MMA
+ * kernel for every m <= 8, so a row's result does not depend on m),
+ * 1 = dp4a kernel (one warp lane per block, lanes per row from k),
+ * 2 = integer-MMA kernel (mma.sync m16n8k32: one instruction per block for
+ * 16 weight rows x 8 activation rows).  Both compute the reference's per-block formula
+ * (quant.rs:349-351, :452-454) with exact integer block dots; they differ
+ * only in f32 summation order.  Applies to this host thread. */
+int rwq_set_gemv_kernel(int kind);
+
 /* Synchronize `stream` and report any fault a kernel recorded on it. */
 int rwq_stream_check(void* stream);
 

@@ -42,6 +42,7 @@ SIGNATURES = {
     "rwq_matmul_t_q_qacts": (_I, [_P, _P, _P, _P, _P]),
     "rwq_matmul_t_q_noalloc": (_I, [_P, _L, _L, _P, _P, _P, _P]),
     "rwq_set_gemm_path": (_I, [_I]),
+    "rwq_set_gemv_kernel": (_I, [_I]),
     "rwq_stream_check": (_I, [_P]),
     "rwq_model_load": (_I, [ctypes.c_char_p, ctypes.POINTER(_P)]),
     "rwq_model_load_memory": (_I, [_P, _SZ, ctypes.POINTER(_P)]),

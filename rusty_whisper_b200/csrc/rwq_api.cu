@@ -321,13 +321,20 @@ static int qtensor_new_impl(const void* raw, bool raw_on_device, size_t raw_len,
         return rc;
     };
     cudaError_t e;
-    const size_t nalloc = nblk ? nblk : 1;
+    // Planes hold nb4 = round4(nb) blocks per row; pad blocks stay zero.
+    const size_t nalloc = nblk ? size_t(n) * size_t(rwq::round4(int(nb))) : 1;
     if ((e = cudaMalloc(&w.qs, nalloc * rwq::qs_bytes(dtype))) != cudaSuccess) return cleanup(cuda_fail(e, "cudaMalloc(qs)"));
     if ((e = cudaMalloc(&w.d, nalloc * 2)) != cudaSuccess) return cleanup(cuda_fail(e, "cudaMalloc(d)"));
     if (rwq::has_min(dtype) && (e = cudaMalloc(&w.m, nalloc * 2)) != cudaSuccess)
         return cleanup(cuda_fail(e, "cudaMalloc(m)"));
     if (rwq::has_qh(dtype) && (e = cudaMalloc(&w.qh, nalloc * 4)) != cudaSuccess)
         return cleanup(cuda_fail(e, "cudaMalloc(qh)"));
+    if (nblk && nalloc != nblk) {
+        cudaMemsetAsync(w.qs, 0, nalloc * rwq::qs_bytes(dtype), s);
+        cudaMemsetAsync(w.d, 0, nalloc * 2, s);
+        if (w.m) cudaMemsetAsync(w.m, 0, nalloc * 2, s);
+        if (w.qh) cudaMemsetAsync(w.qh, 0, nalloc * 4, s);
+    }
     if (nblk) {
         const uint8_t* src = static_cast<const uint8_t*>(raw);
         uint8_t* tmp = nullptr;
@@ -506,6 +513,12 @@ int rwq_block_dots_dev(const float* a, int64_t m, int64_t k, const rwq_qtensor* 
 int rwq_set_gemm_path(int path) {
     if (path < 0 || path > 3) return fail(RWQ_ERR_ARG, "path must be 0, 1, 2 or 3");
     t_gemm_path = path;
+    return RWQ_OK;
+}
+
+int rwq_set_gemv_kernel(int kind) {
+    if (kind < 0 || kind > 2) return fail(RWQ_ERR_ARG, "kind must be 0, 1 or 2");
+    rwq::set_gemv_kind(kind);
     return RWQ_OK;
 }
 

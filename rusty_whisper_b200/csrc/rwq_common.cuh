@@ -10,10 +10,17 @@
 // qs[j-16]; bit j of qh is element j's fifth bit.
 //
 // On the device a weight lives as "planes" (same bytes per block as the
-// ggml record, split so every block's code bytes start on a 16-byte
-// boundary):  qs [n][nb][QSB]  (QSB = 16, or 32 for Q8_0),
-//             qh [n][nb] u32 (Q5 only, bits permuted: see qh_plane_bits),
-//             d [n][nb] f16 bits, m [n][nb] f16 bits (Q4_1/Q5_1 only).
+// ggml record, split so that code bytes are 16-byte aligned).  Each row is
+// padded to nb4 = nb rounded up to a multiple of 4 blocks (pad blocks are
+// zero):
+//             qs [n][nb4/4][4*QSB]  (QSB = 16, or 32 for Q8_0), see below,
+//             qh [n][nb4] u32 (Q5 only, bits permuted: see qh_plane_bits),
+//             d [n][nb4] f16 bits, m [n][nb4] f16 bits (Q4_1/Q5_1 only).
+// The code plane interleaves each group of four blocks by 4-byte word:
+// word w of block b (b = kb % 4) sits at w*16 + b*4 of the group (Q8_0:
+// (w%4)*32 + b*8 + (w/4)*4), so one 16-byte load (32 for Q8_0) at c*16
+// (c*32) returns word c (and 4+c) of all four blocks -- exactly the
+// operand fragment lane c of a quad feeds to an m16n8k32 integer MMA.
 #pragma once
 #include <cstdint>
 #include <cuda_runtime.h>
@@ -39,6 +46,19 @@ __host__ __device__ constexpr int raw_m_off(int) { return 2; }
 __host__ __device__ constexpr int raw_qh_off(int dt) { return dt == Q5_0 ? 2 : 4; }
 __host__ __device__ constexpr int raw_qs_off(int dt) {
     return dt == Q4_0 ? 2 : dt == Q4_1 ? 4 : dt == Q5_0 ? 6 : dt == Q5_1 ? 8 : 2;
+}
+
+// Plane addressing (see the layout above).
+__host__ __device__ constexpr int round4(int nb) { return (nb + 3) & ~3; }
+// Byte offset of code word w of block b (0..3) inside its 4-block group.
+template <int DT>
+__host__ __device__ constexpr int qs_word_off(int w, int b) {
+    return DT == Q8_0 ? ((w & 3) * 32 + b * 8 + (w >> 2) * 4) : (w * 16 + b * 4);
+}
+// First byte of the 4-block group holding block kb of row j.
+template <int DT>
+__host__ __device__ inline size_t qs_group_off(size_t j, int kb, int nb4) {
+    return (j * size_t(nb4) + size_t(kb & ~3)) * size_t(qs_bytes(DT));
 }
 
 // Exact f16 -> f32 (model.rs:68-86 semantics; the hardware conversion is

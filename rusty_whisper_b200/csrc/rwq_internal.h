@@ -11,10 +11,10 @@ namespace rwq {
 // lazily built tensor-core operand cache.
 struct Weight {
     int dtype = 0, n = 0, k = 0, nb = 0, device = 0;
-    uint8_t* qs = nullptr;     // [n][nb][qs_bytes]
-    uint32_t* qh = nullptr;    // [n][nb]          (Q5_0 / Q5_1)
-    uint16_t* d = nullptr;     // [n][nb] f16 bits
-    uint16_t* m = nullptr;     // [n][nb] f16 bits (Q4_1 / Q5_1)
+    uint8_t* qs = nullptr;     // [n][nb4/4][4*qs_bytes], word-interleaved groups (rwq_common.cuh)
+    uint32_t* qh = nullptr;    // [n][nb4]         (Q5_0 / Q5_1)
+    uint16_t* d = nullptr;     // [n][nb4] f16 bits
+    uint16_t* m = nullptr;     // [n][nb4] f16 bits (Q4_1 / Q5_1)
     // tensor-core operand cache (built on first GEMM-sized call)
     uint16_t* q16 = nullptr;   // [n][k] centred codes as f16
     float* dT = nullptr;       // [nb][n_pad] d as f32, transposed
@@ -49,6 +49,9 @@ cudaError_t launch_quantize_acts(const float* a, const ActsView& v, bool want_ge
 cudaError_t launch_dequant_rows(const Weight& w, const int32_t* rows, int nrows, float* out, cudaStream_t s);
 cudaError_t launch_block_dots(const ActsView& v, const Weight& w, int32_t* S, cudaStream_t s);
 cudaError_t launch_gemv_i8(const ActsView& v, const Weight& w, const float* bias, float* y, cudaStream_t s);
+// GEMV kernel choice for the calling host thread: 0 auto (integer MMA),
+// 1 dp4a, 2 integer MMA.
+void set_gemv_kind(int kind);
 cudaError_t launch_gemv_f32(const float* a, int m, const Weight& w, const float* bias, float* y, cudaStream_t s);
 // tcgen05 GEMM.  S_dump (optional, small shapes) receives the per-block
 // integer dots read back from tensor memory.

@@ -18,30 +18,34 @@ inline unsigned grid_for(size_t work, int per_block) {
 }
 
 // ---------------------------------------------------------------- repack
-// raw ggml records [n*nb][bb] -> planes.  One thread per block; the raw
-// records are not 16-byte aligned, so they are read bytewise, once.
+// raw ggml records [n*nb][bb] -> planes (layout in rwq_common.cuh).  One
+// thread per block; the raw records are not 16-byte aligned, so they are
+// read bytewise, once.  Pad blocks (kb >= nb) keep the zeros the planes
+// were cleared to.
 template <int DT>
 __global__ void k_repack(const uint8_t* __restrict__ raw, uint8_t* __restrict__ qs, uint32_t* __restrict__ qh,
-                         uint16_t* __restrict__ d, uint16_t* __restrict__ m, size_t nblk) {
+                         uint16_t* __restrict__ d, uint16_t* __restrict__ m, size_t nblk, int nb, int nb4) {
     size_t b = size_t(blockIdx.x) * blockDim.x + threadIdx.x;
     if (b >= nblk) return;
     constexpr int BB = block_bytes(DT), QSB = qs_bytes(DT), QO = raw_qs_off(DT);
+    const size_t j = b / size_t(nb);
+    const int kb = int(b % size_t(nb));
+    const size_t pb = j * size_t(nb4) + kb;
     const uint8_t* p = raw + b * BB;
-    d[b] = uint16_t(p[0] | (p[1] << 8));
-    if (has_min(DT)) m[b] = uint16_t(p[2] | (p[3] << 8));
+    d[pb] = uint16_t(p[0] | (p[1] << 8));
+    if (has_min(DT)) m[pb] = uint16_t(p[2] | (p[3] << 8));
     if (has_qh(DT)) {
         const uint8_t* h = p + raw_qh_off(DT);
-        qh[b] = qh_plane_bits(uint32_t(h[0]) | (uint32_t(h[1]) << 8) | (uint32_t(h[2]) << 16) |
-                              (uint32_t(h[3]) << 24));
+        qh[pb] = qh_plane_bits(uint32_t(h[0]) | (uint32_t(h[1]) << 8) | (uint32_t(h[2]) << 16) |
+                               (uint32_t(h[3]) << 24));
     }
-    uint32_t words[QSB / 4];
+    uint8_t* grp = qs + qs_group_off<DT>(j, kb, nb4);
 #pragma unroll
-    for (int i = 0; i < QSB / 4; ++i)
-        words[i] = uint32_t(p[QO + 4 * i]) | (uint32_t(p[QO + 4 * i + 1]) << 8) |
-                   (uint32_t(p[QO + 4 * i + 2]) << 16) | (uint32_t(p[QO + 4 * i + 3]) << 24);
-    uint4* dst = reinterpret_cast<uint4*>(qs + b * QSB);
-#pragma unroll
-    for (int i = 0; i < QSB / 16; ++i) dst[i] = make_uint4(words[4 * i], words[4 * i + 1], words[4 * i + 2], words[4 * i + 3]);
+    for (int i = 0; i < QSB / 4; ++i) {
+        const uint32_t word = uint32_t(p[QO + 4 * i]) | (uint32_t(p[QO + 4 * i + 1]) << 8) |
+                              (uint32_t(p[QO + 4 * i + 2]) << 16) | (uint32_t(p[QO + 4 * i + 3]) << 24);
+        *reinterpret_cast<uint32_t*>(grp + qs_word_off<DT>(i, kb & 3)) = word;
+    }
 }
 
 // ------------------------------------------------------------ quantizer
@@ -116,19 +120,37 @@ struct BlockCodes {
     float d, m;
 };
 
+// The code words of block kb of row j (gathered from the interleaved
+// group: four 4-byte loads, or four 8-byte loads for Q8_0).
+template <int DT>
+__device__ __forceinline__ void load_words(const uint8_t* __restrict__ qs, size_t j, int kb, int nb4, uint32_t (&w)[8]) {
+    const uint8_t* g = qs + qs_group_off<DT>(j, kb, nb4);
+    const int b = kb & 3;
+    if (DT == Q8_0) {
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            const uint2 v = __ldg(reinterpret_cast<const uint2*>(g + qs_word_off<DT>(c, b)));
+            w[c] = v.x;
+            w[4 + c] = v.y;
+        }
+    } else {
+#pragma unroll
+        for (int c = 0; c < 4; ++c) w[c] = __ldg(reinterpret_cast<const uint32_t*>(g + qs_word_off<DT>(c, b)));
+    }
+}
+
 template <int DT>
 __device__ __forceinline__ void load_block(const uint8_t* __restrict__ qs, const uint32_t* __restrict__ qh,
                                            const uint16_t* __restrict__ dp, const uint16_t* __restrict__ mp,
-                                           size_t b, BlockCodes<DT>& bc) {
+                                           size_t j, int kb, int nb4, BlockCodes<DT>& bc) {
+    const size_t b = j * size_t(nb4) + kb;
     if (DT == Q8_0) {
-        const uint4* p = reinterpret_cast<const uint4*>(qs + b * 32);
-        uint4 v0 = __ldg(p), v1 = __ldg(p + 1);
-        bc.w[0] = v0.x; bc.w[1] = v0.y; bc.w[2] = v0.z; bc.w[3] = v0.w;
-        bc.w[4] = v1.x; bc.w[5] = v1.y; bc.w[6] = v1.z; bc.w[7] = v1.w;
+        load_words<DT>(qs, j, kb, nb4, bc.w);
     } else {
-        uint4 v = __ldg(reinterpret_cast<const uint4*>(qs + b * 16));
+        uint32_t v[8];
+        load_words<DT>(qs, j, kb, nb4, v);
         uint32_t h = has_qh(DT) ? __ldg(qh + b) : 0u;
-        codes_u8x4<DT>(v, h, bc.w);
+        codes_u8x4<DT>(make_uint4(v[0], v[1], v[2], v[3]), h, bc.w);
     }
     bc.d = h2f(__ldg(dp + b));
     bc.m = has_min(DT) ? h2f(__ldg(mp + b)) : 0.f;
@@ -174,7 +196,7 @@ __global__ void k_dequant_rows(const uint8_t* __restrict__ qs, const uint32_t* _
     const int j = rows ? rows[r] : r;
     if (j < 0 || j >= n) return;  // host validated; guard anyway
     BlockCodes<DT> bc;
-    load_block<DT>(qs, qh, dp, mp, size_t(j) * nb + bl, bc);
+    load_block<DT>(qs, qh, dp, mp, size_t(j), bl, round4(nb), bc);
     float* o = out + size_t(r) * nb * QK + size_t(bl) * QK;
 #pragma unroll
     for (int e = 0; e < QK; e += 4) {
@@ -200,7 +222,7 @@ __global__ void k_block_dots(const uint8_t* __restrict__ qs, const uint32_t* __r
     const int j = int((t / nb) % n);
     const int i = int(t / (size_t(nb) * n));
     BlockCodes<DT> bc;
-    load_block<DT>(qs, qh, dp, mp, size_t(j) * nb + bl, bc);
+    load_block<DT>(qs, qh, dp, mp, size_t(j), bl, round4(nb), bc);
     const int4* a = reinterpret_cast<const int4*>(q8 + size_t(i) * nb * QK + size_t(bl) * QK);
     S[t] = block_dot<DT>(bc.w, a[0], a[1], suma[size_t(i) * nb + bl]);
 }
@@ -216,15 +238,13 @@ struct RawBlock {
 
 template <int DT>
 __device__ __forceinline__ void load_raw(const uint8_t* __restrict__ qs, const uint32_t* __restrict__ qh,
-                                         const uint16_t* __restrict__ dp, const uint16_t* __restrict__ mp, size_t b,
-                                         RawBlock<DT>& rb) {
-    if (DT == Q8_0) {
-        const uint4* p = reinterpret_cast<const uint4*>(qs + b * 32);
-        rb.v0 = __ldg(p);
-        rb.v1 = __ldg(p + 1);
-    } else {
-        rb.v0 = __ldg(reinterpret_cast<const uint4*>(qs + b * 16));
-    }
+                                         const uint16_t* __restrict__ dp, const uint16_t* __restrict__ mp, size_t j,
+                                         int kb, int nb4, RawBlock<DT>& rb) {
+    uint32_t w[8];
+    load_words<DT>(qs, j, kb, nb4, w);
+    rb.v0 = make_uint4(w[0], w[1], w[2], w[3]);
+    if (DT == Q8_0) rb.v1 = make_uint4(w[4], w[5], w[6], w[7]);
+    const size_t b = j * size_t(nb4) + kb;
     if (has_qh(DT)) rb.qh = __ldg(qh + b);
     rb.d = __ldg(dp + b);
     if (has_min(DT)) rb.m = __ldg(mp + b);
@@ -265,7 +285,7 @@ __global__ void __launch_bounds__(TPB) k_gemv_i8(const uint8_t* __restrict__ qs,
                                                  const int32_t* __restrict__ sa, const float* __restrict__ ua, int M,
                                                  int N, int K, const float* __restrict__ bias, float* __restrict__ y) {
     pdl_trigger();
-    const int nb = K / QK;
+    const int nb = K / QK, nb4 = round4(nb);
     constexpr int RPW = 32 / L;
     const int lane = threadIdx.x & 31, sub = lane % L, slot = lane / L;
     const int warps_per_cta = blockDim.x >> 5;
@@ -279,7 +299,7 @@ __global__ void __launch_bounds__(TPB) k_gemv_i8(const uint8_t* __restrict__ qs,
 #pragma unroll
         for (int t = 0; t < BPL; ++t) {
             const int kb = sub + L * t;
-            if (grp < groups && j < N && kb < nb) load_raw<DT>(qs, qh, dp, mp, size_t(j) * nb + kb, dst[t]);
+            if (grp < groups && j < N && kb < nb) load_raw<DT>(qs, qh, dp, mp, size_t(j), kb, nb4, dst[t]);
         }
     };
     // The weights are not written by the previous kernel in the stream, so
@@ -398,6 +418,391 @@ __global__ void __launch_bounds__(TPB) k_gemv_i8(const uint8_t* __restrict__ qs,
     }
 }
 
+// ------------------------------------------------------------ GEMV mma
+// Decoder GEMV on the integer MMA (mma.sync m16n8k32, s32 accumulate),
+// M <= 8 activation rows.  A warp owns a tile of 16 weight rows and walks
+// its K range one 4-block group at a time; quad lane c (lane = 4g + c)
+// loads word c of the group's four blocks for rows g and g+8 with one
+// 16-byte load per row (32 for Q8_0) -- the interleaved code plane makes
+// that exactly its A fragment: low nibbles are elements 4c..4c+3, high
+// nibbles elements 16+4c..16+4c+3, fifth bits from the permuted qh word
+// with one shift and mask.  The activation codes (B fragments) and their
+// per-block scales are staged once per CTA in shared memory in fragment
+// order.  Each block is one MMA whose accumulator starts at the bits of
+// 1.5*2^23 minus the code offset times sum(q_a), so S = D - 1.5*2^23 is
+// the exact centred integer block dot, then per output (row j, act row i)
+//     acc <- fma(d_a*d_b, S, acc);  acc <- fma(d_a*sum(q_a), m_b, acc)
+// in kb order (the formula of quant.rs:349-351 / :452-454).  With KS > 1
+// the K range is split over KS warps of a CTA and their partial sums are
+// added in slice order.  KS depends on N and K only, so a row's result
+// does not depend on M (quant.rs:1372-1384).
+constexpr int GM_THREADS = 256;
+
+// 4-byte cp.async global -> shared; `ok` false writes zeros and reads nothing.
+__device__ __forceinline__ void cp_async4(void* dst, const void* src, bool ok) {
+    const uint32_t d = uint32_t(__cvta_generic_to_shared(dst));
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(d), "l"(src), "r"(ok ? 4 : 0) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
+template <int DT>
+struct MmaGroup {
+    uint32_t q[2][qs_bytes(DT) / 4];    // [row g, g+8][word c (and 4+c) of blocks 0..3]
+    uint32_t h[2][has_qh(DT) ? 4 : 1];  // qh words of blocks 0..3
+    uint2 d[2], m[2];                   // f16 d (m) of blocks 0..3
+};
+
+// Per-warp shared-memory ring of weight groups, filled with cp.async so
+// that the data in flight costs no registers.  Slot layout (one 4-block
+// group of the warp's 16 rows): codes [16 rows][4 lanes][QSB] (the 16- or
+// 32-byte share of quad lane c), then qh [16][16 B], d [16][8 B],
+// m [16][8 B].
+template <int DT>
+struct Slot {
+    static constexpr int Q = 16 * 4 * qs_bytes(DT);
+    static constexpr int QH = Q, D = Q + 256, M = Q + 384, BYTES = Q + 512;
+};
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async8(uint32_t dst, const void* src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+// Request group G of tile T into the slot at shared address `slot`.
+// Rows past N are not copied (their slot bytes are stale; the sums they
+// feed are never stored).  Offsets fit 32 bits: the host checks
+// n * nb4 * qs_bytes < 2^32.
+template <int DT>
+__device__ __forceinline__ void ring_issue(const uint8_t* __restrict__ qs, const uint32_t* __restrict__ qh,
+                                           const uint16_t* __restrict__ dp, const uint16_t* __restrict__ mp, int N,
+                                           int nb4, int T, int G, int lane, uint32_t slot) {
+    // Rows past N re-read row N-1 (their sums are never stored).
+    const int g = lane >> 2, c = lane & 3;
+#pragma unroll
+    for (int rr = 0; rr < 2; ++rr) {
+        const int r = g + 8 * rr, row = min(T * 16 + r, N - 1);
+        const uint32_t pb = uint32_t(row) * uint32_t(nb4) + uint32_t(4 * G);
+        const uint8_t* src = qs + (pb * qs_bytes(DT) + uint32_t(c * qs_bytes(DT)));
+        const uint32_t dst = slot + uint32_t((r * 4 + c) * qs_bytes(DT));
+        cp_async16(dst, src);
+        if (DT == Q8_0) cp_async16(dst + 16, src + 16);
+    }
+    const int r = lane & 15, row = min(T * 16 + r, N - 1);
+    const uint32_t pb = uint32_t(row) * uint32_t(nb4) + uint32_t(4 * G);
+    if (lane < 16) {
+        if (has_qh(DT)) cp_async16(slot + Slot<DT>::QH + r * 16, qh + pb);
+        if (has_min(DT)) cp_async8(slot + Slot<DT>::M + r * 8, mp + pb);
+    } else {
+        cp_async8(slot + Slot<DT>::D + r * 8, dp + pb);
+    }
+}
+
+// This lane's share of a landed slot, into registers.
+template <int DT>
+__device__ __forceinline__ void ring_read(const uint8_t* slot, int lane, MmaGroup<DT>& r) {
+    const int g = lane >> 2, c = lane & 3;
+#pragma unroll
+    for (int rr = 0; rr < 2; ++rr) {
+        const int row = g + 8 * rr;
+        const uint4 v = *reinterpret_cast<const uint4*>(slot + (row * 4 + c) * qs_bytes(DT));
+        r.q[rr][0] = v.x; r.q[rr][1] = v.y; r.q[rr][2] = v.z; r.q[rr][3] = v.w;
+        if (DT == Q8_0) {
+            const uint4 v2 = *reinterpret_cast<const uint4*>(slot + (row * 4 + c) * qs_bytes(DT) + 16);
+            r.q[rr][4 % (qs_bytes(DT) / 4)] = v2.x; r.q[rr][5 % (qs_bytes(DT) / 4)] = v2.y;
+            r.q[rr][6 % (qs_bytes(DT) / 4)] = v2.z; r.q[rr][7 % (qs_bytes(DT) / 4)] = v2.w;
+        }
+        if (has_qh(DT)) {
+            const uint4 h = *reinterpret_cast<const uint4*>(slot + Slot<DT>::QH + row * 16);
+            r.h[rr][0] = h.x; r.h[rr][1 % 4] = h.y; r.h[rr][2 % 4] = h.z; r.h[rr][3 % 4] = h.w;
+        }
+        r.d[rr] = *reinterpret_cast<const uint2*>(slot + Slot<DT>::D + row * 8);
+        if (has_min(DT)) r.m[rr] = *reinterpret_cast<const uint2*>(slot + Slot<DT>::M + row * 8);
+    }
+}
+
+// Two f16 (low half first) to f32, exactly.
+__device__ __forceinline__ float2 h2f2(uint32_t w) {
+    return __half22float2(*reinterpret_cast<const __half2*>(&w));
+}
+
+template <bool SA>
+__device__ __forceinline__ void mma_i8(const uint32_t (&a)[4], uint2 b, int2 ci, int (&d)[4]) {
+    if (SA)
+        asm volatile("mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+                     "{%10,%11,%12,%13};"
+                     : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+                     : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b.x), "r"(b.y), "r"(ci.x), "r"(ci.y),
+                       "r"(ci.x), "r"(ci.y));
+    else
+        asm volatile("mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+                     "{%10,%11,%12,%13};"
+                     : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+                     : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b.x), "r"(b.y), "r"(ci.x), "r"(ci.y),
+                       "r"(ci.x), "r"(ci.y));
+}
+
+// Shared-memory staging of the activations, per block kb: 32 B-fragment
+// pairs (lane order); per quad lane c the seeds and d_a of act rows 2c and
+// 2c+1 as one 16-byte record {seed, seed, d_a, d_a}; d_a*sum(q_a) of act
+// rows 0..7.
+struct MmaActs {
+    const uint2* frag;   // [nb4][32]
+    const int4* sc;      // [nb4][4]
+    const float* ua;     // [nb4][8]
+};
+
+template <int DT>
+__device__ __forceinline__ void mma_compute(const MmaGroup<DT>& r, const MmaActs& A, int G, int nb, int lane,
+                                            float2& a01, float2& a23) {
+    const int c = lane & 3;
+    const float2 dr0[2] = {h2f2(r.d[0].x), h2f2(r.d[0].y)}, dr1[2] = {h2f2(r.d[1].x), h2f2(r.d[1].y)};
+    float2 mr0[2], mr1[2];
+    if (has_min(DT)) {
+        mr0[0] = h2f2(r.m[0].x); mr0[1] = h2f2(r.m[0].y);
+        mr1[0] = h2f2(r.m[1].x); mr1[1] = h2f2(r.m[1].y);
+    }
+    const float2 nmag = make_float2(-MAGIC_F, -MAGIC_F);
+    // Pad blocks (kb >= nb) need no test: their weight codes and scales
+    // are zero and their activation records are staged as zero scales with
+    // seed 1.5*2^23, so they add exactly 0.
+#pragma unroll
+    for (int b = 0; b < 4; ++b) {
+        const int kb = 4 * G + b;
+        {
+            uint32_t a[4];
+            if (DT == Q8_0) {
+                a[0] = r.q[0][(2 * b) % (qs_bytes(DT) / 4)];
+                a[1] = r.q[1][(2 * b) % (qs_bytes(DT) / 4)];
+                a[2] = r.q[0][(2 * b + 1) % (qs_bytes(DT) / 4)];
+                a[3] = r.q[1][(2 * b + 1) % (qs_bytes(DT) / 4)];
+            } else {
+#pragma unroll
+                for (int rr = 0; rr < 2; ++rr) {
+                    const uint32_t w = r.q[rr][b % (qs_bytes(DT) / 4)];
+                    uint32_t lo = w & 0x0F0F0F0Fu, hi = (w >> 4) & 0x0F0F0F0Fu;
+                    if (has_qh(DT)) {
+                        const uint32_t h = r.h[rr][b % (has_qh(DT) ? 4 : 1)];
+                        lo |= (h << (4 - c)) & 0x10101010u;
+                        hi |= (h >> c) & 0x10101010u;
+                    }
+                    a[rr] = lo;
+                    a[2 + rr] = hi;
+                }
+            }
+            const uint2 bf = A.frag[kb * 32 + lane];
+            const int4 sc = A.sc[kb * 4 + c];
+            int dd[4];
+            mma_i8<DT == Q8_0>(a, bf, make_int2(sc.x, sc.y), dd);
+            const float2 da = make_float2(__int_as_float(sc.z), __int_as_float(sc.w));
+            const float db0 = (b & 1) ? dr0[b >> 1].y : dr0[b >> 1].x;
+            const float db1 = (b & 1) ? dr1[b >> 1].y : dr1[b >> 1].x;
+            // S exactly (integer < 2^22 below 1.5*2^23); acc += (d_a*d_b)*S
+            const float2 s01 = __fadd2_rn(make_float2(__int_as_float(dd[0]), __int_as_float(dd[1])), nmag);
+            const float2 s23 = __fadd2_rn(make_float2(__int_as_float(dd[2]), __int_as_float(dd[3])), nmag);
+            a01 = __ffma2_rn(__fmul2_rn(da, make_float2(db0, db0)), s01, a01);
+            a23 = __ffma2_rn(__fmul2_rn(da, make_float2(db1, db1)), s23, a23);
+            if (has_min(DT)) {
+                const float2 ua = *reinterpret_cast<const float2*>(A.ua + kb * 8 + 2 * c);
+                const float mb0 = (b & 1) ? mr0[b >> 1].y : mr0[b >> 1].x;
+                const float mb1 = (b & 1) ? mr1[b >> 1].y : mr1[b >> 1].x;
+                a01 = __ffma2_rn(ua, make_float2(mb0, mb0), a01);
+                a23 = __ffma2_rn(ua, make_float2(mb1, mb1), a23);
+            }
+        }
+    }
+}
+
+__device__ __forceinline__ void mma_store(float2 a01, float2 a23, int T, int lane, int M, int N,
+                                          const float* __restrict__ bias, float* __restrict__ y) {
+    const int g = lane >> 2, c = lane & 3;
+    const float v[4] = {a01.x, a01.y, a23.x, a23.y};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int row = T * 16 + g + ((i & 2) ? 8 : 0), col = 2 * c + (i & 1);
+        if (row < N && col < M) y[size_t(col) * N + row] = bias ? __fadd_rn(v[i], __ldg(bias + row)) : v[i];
+    }
+}
+
+// PF groups in flight per warp (4 or 8, chosen by the launcher from the
+// shared memory left after the activations).
+template <int DT, int KS, int PF>
+__global__ void __launch_bounds__(GM_THREADS, 2)
+    k_gemv_mma(const uint8_t* __restrict__ qs, const uint32_t* __restrict__ qh, const uint16_t* __restrict__ dp,
+               const uint16_t* __restrict__ mp, const int8_t* __restrict__ q8, const float* __restrict__ da,
+               const int32_t* __restrict__ sa, const float* __restrict__ ua, int M, int N, int K,
+               const float* __restrict__ bias, float* __restrict__ y) {
+    constexpr int pf = PF;
+    pdl_trigger();
+    constexpr int WARPS = GM_THREADS / 32;
+    const int nb = K / QK, nb4 = round4(nb), ng = nb4 / 4;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int tiles = (N + 15) / 16;
+
+    extern __shared__ __align__(16) uint8_t smem[];
+    uint2* s_frag = reinterpret_cast<uint2*>(smem);                       // [nb4][32]
+    int* s_sc = reinterpret_cast<int*>(smem + size_t(nb4) * 256);          // [nb4][4 lanes][seed, seed, d_a, d_a]
+    float* s_ua = reinterpret_cast<float*>(s_sc + nb4 * 16);               // [nb4][8]
+    float* s_red = s_ua + nb4 * 8;                                         // [8 warps][32 lanes][4]
+    uint8_t* ring = reinterpret_cast<uint8_t*>(s_red + WARPS * 32 * 4) + size_t(warp) * pf * Slot<DT>::BYTES;
+    const uint32_t ring_s = uint32_t(__cvta_generic_to_shared(ring));
+    const MmaActs A{s_frag, reinterpret_cast<const int4*>(s_sc), s_ua};
+
+    auto stage = [&]() {
+        pdl_wait();
+        // Only entries of existing rows and blocks are copied: the other
+        // columns' sums are never stored and pad blocks are skipped.
+        for (int i = tid; i < nb * M * 4; i += GM_THREADS) {
+            const int cc = i & 3, row = (i >> 2) % M, kb = (i >> 2) / M;
+            const int8_t* p = q8 + size_t(row) * K + kb * QK + 4 * cc;
+            uint2* dst = s_frag + kb * 32 + row * 4 + cc;
+            cp_async4(&dst->x, p, true);
+            cp_async4(&dst->y, p + 16, true);
+        }
+        // record of (kb, act row col): s_sc[(kb*4 + col/2)*4 + {0,1} seed, {2,3} d_a]
+        auto sc_at = [&](int kb, int col, int f) { return s_sc + (kb * 4 + (col >> 1)) * 4 + 2 * f + (col & 1); };
+        for (int i = tid; i < nb * M; i += GM_THREADS) {
+            const int col = i % M, kb = i / M;
+            const size_t o = size_t(col) * nb + kb;
+            if (code_offset(DT)) cp_async4(sc_at(kb, col, 0), sa + o, true);
+            cp_async4(sc_at(kb, col, 1), da + o, true);
+            if (has_min(DT)) cp_async4(s_ua + kb * 8 + col, ua + o, true);
+        }
+        // Pad blocks: zero codes, zero scales, seed 1.5*2^23 -> add 0.
+        for (int i = tid; i < (nb4 - nb) * 32; i += GM_THREADS) {
+            const int kb = nb + i / 32, l = i & 31;
+            s_frag[kb * 32 + l] = make_uint2(0u, 0u);
+            if (l < 8) {
+                *sc_at(kb, l, 0) = int(MAGIC_BITS);
+                *reinterpret_cast<float*>(sc_at(kb, l, 1)) = 0.f;
+                s_ua[kb * 8 + l] = 0.f;
+            }
+        }
+        cp_async_wait_all();
+        __syncthreads();
+        for (int i = tid; i < nb * M; i += GM_THREADS) {
+            int* p = sc_at(i / M, i % M, 0);
+            *p = code_offset(DT) ? int(MAGIC_BITS - uint32_t(code_offset(DT) * *p)) : int(MAGIC_BITS);
+        }
+        __syncthreads();
+    };
+
+    // One item: wait for its slot, read it, refill the slot with the item
+    // pf places ahead (or commit an empty group, so the pending count stays
+    // pf - 1), then run the block MMAs.
+    MmaGroup<DT> cur;
+    float2 a01, a23;
+    auto consume = [&](int u, int G, bool refill, int nT, int nG) {
+        asm volatile("cp.async.wait_group %0;" ::"n"(PF - 1) : "memory");
+        __syncwarp();
+        ring_read<DT>(ring + u * Slot<DT>::BYTES, lane, cur);
+        __syncwarp();
+        if (refill) ring_issue<DT>(qs, qh, dp, mp, N, nb4, nT, nG, lane, ring_s + u * Slot<DT>::BYTES);
+        cp_async_commit();
+        mma_compute<DT>(cur, A, G, nb, lane, a01, a23);
+    };
+
+    if (KS == 1) {
+        // The CTA owns the contiguous tiles [t_lo, t_hi); its warps split
+        // the (tile, group) items evenly into contiguous ranges.  With at
+        // least 8 tiles per CTA every range holds a full tile's groups, so
+        // a tile is shared by at most two neighbouring warps: the first
+        // ends with its head (groups 0..x-1), the next starts with its
+        // tail (x..); the tail is passed through shared memory and the
+        // head's owner stores head + tail.  Fewer tiles: whole tiles.
+        const int t_lo = int(int64_t(blockIdx.x) * tiles / gridDim.x);
+        const int t_hi = int(int64_t(blockIdx.x + 1) * tiles / gridDim.x);
+        const int nt = t_hi - t_lo, items = nt * ng;
+        int i_lo, i_hi;
+        if (nt >= WARPS) {
+            i_lo = warp * items / WARPS;
+            i_hi = (warp + 1) * items / WARPS;
+        } else {
+            i_lo = min(warp, nt) * ng;
+            i_hi = min(warp + 1, nt) * ng;
+        }
+        const int n_items = i_hi - i_lo;
+        int lt = t_lo + i_lo / ng, lG = i_lo % ng;
+        int ct = lt, cG = lG;
+        const int shared_first = lG != 0 ? lt : -1;   // tile whose head the previous warp holds
+        for (int u = 0; u < pf; ++u) {
+            if (u < n_items) {
+                ring_issue<DT>(qs, qh, dp, mp, N, nb4, lt, lG, lane, ring_s + u * Slot<DT>::BYTES);
+                if (++lG == ng) { lG = 0; ++lt; }
+            }
+            cp_async_commit();
+        }
+        stage();
+        a01 = a23 = make_float2(0.f, 0.f);
+        for (int i0 = 0; i0 < n_items; i0 += PF) {
+#pragma unroll
+        for (int u = 0; u < PF; ++u) {
+            const int i = i0 + u;
+            if (i >= n_items) break;
+            const bool refill = i + pf < n_items;
+            consume(u, cG, refill, lt, lG);
+            if (refill && ++lG == ng) { lG = 0; ++lt; }
+            if (++cG == ng) {
+                if (ct == shared_first)
+                    *reinterpret_cast<float4*>(s_red + (warp * 32 + lane) * 4) = make_float4(a01.x, a01.y, a23.x, a23.y);
+                else
+                    mma_store(a01, a23, ct, lane, M, N, bias, y);
+                a01 = a23 = make_float2(0.f, 0.f);
+                cG = 0;
+                ++ct;
+            }
+        }
+        }
+        __syncthreads();
+        if (n_items > 0 && cG != 0) {   // this warp holds the head of tile ct; warp + 1 its tail
+            const float4 t = *reinterpret_cast<const float4*>(s_red + ((warp + 1) * 32 + lane) * 4);
+            a01 = __fadd2_rn(a01, make_float2(t.x, t.y));
+            a23 = __fadd2_rn(a23, make_float2(t.z, t.w));
+            mma_store(a01, a23, ct, lane, M, N, bias, y);
+        }
+        asm volatile("cp.async.wait_group 0;" ::: "memory");
+        return;
+    }
+
+    // KS > 1: the CTA's warps form (8/KS) tiles x KS K-slices; each CTA
+    // iteration ends with a slice-ordered reduction in shared memory.
+    constexpr int TPC = WARPS / KS;
+    const int ks = warp % KS, tw = warp / KS;
+    const int g0 = ks * ng / KS, gn = (ks + 1) * ng / KS - g0;
+    int base = blockIdx.x * TPC;
+    for (bool first = true; base < tiles; base += gridDim.x * TPC, first = false) {
+        const int T = base + tw;
+        for (int u = 0; u < pf; ++u) {
+            if (u < gn) ring_issue<DT>(qs, qh, dp, mp, N, nb4, T, g0 + u, lane, ring_s + u * Slot<DT>::BYTES);
+            cp_async_commit();
+        }
+        if (first) stage();
+        a01 = a23 = make_float2(0.f, 0.f);
+        for (int i0 = 0; i0 < gn; i0 += PF) {
+#pragma unroll
+            for (int u = 0; u < PF; ++u) {
+                const int i = i0 + u;
+                if (i >= gn) break;
+                consume(u, g0 + i, i + pf < gn, T, g0 + i + pf);
+            }
+        }
+        *reinterpret_cast<float4*>(s_red + (warp * 32 + lane) * 4) = make_float4(a01.x, a01.y, a23.x, a23.y);
+        __syncthreads();
+        if (ks == 0) {
+#pragma unroll
+            for (int s2 = 1; s2 < KS; ++s2) {
+                const float4 p = *reinterpret_cast<const float4*>(s_red + ((warp + s2) * 32 + lane) * 4);
+                a01 = __fadd2_rn(a01, make_float2(p.x, p.y));
+                a23 = __fadd2_rn(a23, make_float2(p.z, p.w));
+            }
+            mma_store(a01, a23, T, lane, M, N, bias, y);
+        }
+        __syncthreads();
+    }
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
+}
+
 // ------------------------------------------------------------- GEMV f32
 // Dequant-then-fp path (the f32 tier, quant.rs:995-1018): weights
 // dequantized bit-exactly, dotted with unquantized f32 activations.
@@ -420,7 +825,7 @@ __global__ void __launch_bounds__(TPB) k_gemv_f32(const uint8_t* __restrict__ qs
         if (j < N) {
             for (int kb = sub; kb < nb; kb += L) {
                 BlockCodes<DT> bc;
-                load_block<DT>(qs, qh, dp, mp, size_t(j) * nb + kb, bc);
+                load_block<DT>(qs, qh, dp, mp, size_t(j), kb, round4(nb), bc);
                 float w[QK];
 #pragma unroll
                 for (int e = 0; e < QK; ++e) w[e] = __fadd_rn(__fmul_rn(bc.d, float(code_at<DT>(bc.w, e))), bc.m);
@@ -473,7 +878,7 @@ __global__ void k_build_gemm_cache(const uint8_t* __restrict__ qs, const uint32_
         return;
     }
     BlockCodes<DT> bc;
-    load_block<DT>(qs, qh, dp, mp, size_t(j) * nb + bl, bc);
+    load_block<DT>(qs, qh, dp, mp, size_t(j), bl, round4(nb), bc);
     uint4* o = reinterpret_cast<uint4*>(q16 + size_t(j) * nb * QK + size_t(bl) * QK);
 #pragma unroll
     for (int e8 = 0; e8 < QK / 8; ++e8) {
@@ -510,7 +915,7 @@ __global__ void k_build_fold_cache(const uint8_t* __restrict__ qs, const uint32_
     float mx = 0.f;
     for (int kb = lane; kb < nb; kb += 32) {
         BlockCodes<DT> bc;
-        load_block<DT>(qs, qh, dp, mp, size_t(j) * nb + kb, bc);
+        load_block<DT>(qs, qh, dp, mp, size_t(j), kb, round4(nb), bc);
 #pragma unroll
         for (int e = 0; e < QK; ++e) {
             const float x = __fadd_rn(__fmul_rn(bc.d, float(code_at<DT>(bc.w, e))), bc.m);
@@ -529,7 +934,7 @@ __global__ void k_build_fold_cache(const uint8_t* __restrict__ qs, const uint32_
     const float up = ldexpf(1.0f, ex);
     for (int kb = lane; kb < nb; kb += 32) {
         BlockCodes<DT> bc;
-        load_block<DT>(qs, qh, dp, mp, size_t(j) * nb + kb, bc);
+        load_block<DT>(qs, qh, dp, mp, size_t(j), kb, round4(nb), bc);
         uint32_t hi2[16], lo2[16];
 #pragma unroll
         for (int e = 0; e < QK; e += 2) {
@@ -568,7 +973,7 @@ struct RepackF {
     static cudaError_t run(const uint8_t* raw, Weight& w, cudaStream_t s) {
         size_t nblk = size_t(w.n) * w.nb;
         if (!nblk) return cudaSuccess;
-        k_repack<DT><<<grid_for(nblk, TPB), TPB, 0, s>>>(raw, w.qs, w.qh, w.d, w.m, nblk);
+        k_repack<DT><<<grid_for(nblk, TPB), TPB, 0, s>>>(raw, w.qs, w.qh, w.d, w.m, nblk, w.nb, round4(w.nb));
         return cudaGetLastError();
     }
 };
@@ -685,6 +1090,75 @@ struct GemvI8F {
     }
 };
 
+// Shared memory of k_gemv_mma: per block B fragments (256 B), seed/d_a
+// records (64 B), d_a*sum(q_a) (32 B); the K-slice reduction buffer; then
+// each warp's weight ring.
+inline size_t gemv_mma_act_smem(int nb) { return size_t(round4(nb)) * 352 + 4096; }
+
+template <int DT, int KS, int PF>
+cudaError_t gemv_mma_go(const ActsView& v, const Weight& w, const float* bias, float* y, cudaStream_t s,
+                        int per_sm_target) {
+    auto kern = k_gemv_mma<DT, KS, PF>;
+    const size_t smem = gemv_mma_act_smem(w.nb) + size_t(PF) * Slot<DT>::BYTES * (GM_THREADS / 32);
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    static unsigned attr_dev_mask = 0;  // one bit per device with the attribute set
+    if (!(attr_dev_mask & (1u << dev))) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 224 * 1024);
+        if (e != cudaSuccess) return e;
+        attr_dev_mask |= 1u << dev;
+    }
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int tiles = (w.n + 15) / 16, tpc = (GM_THREADS / 32) / KS;
+    // KS == 1: one contiguous range of at least 8 tiles per CTA (see the
+    // kernel); KS > 1: grid-stride over groups of tpc tiles.
+    unsigned grid = KS == 1 ? unsigned(tiles / (GM_THREADS / 32)) : unsigned((tiles + tpc - 1) / tpc);
+    const unsigned cap = unsigned(sms) * unsigned(per_sm_target);
+    grid = grid < 1 ? 1 : (grid > cap ? cap : grid);
+    return launch_pdl(kern, dim3(grid), dim3(GM_THREADS), smem, s, w.qs, w.qh, w.d, w.m, v.q8, v.d, v.sum, v.u, v.m,
+                      w.n, w.k, bias, y);
+}
+
+// Ring depth and CTAs per SM: 8 groups per warp with two CTAs per SM when
+// that fits in half of the SM's shared memory, else 4 groups (two CTAs,
+// then one).
+template <int DT, int KS>
+cudaError_t gemv_mma_launch(const ActsView& v, const Weight& w, const float* bias, float* y, cudaStream_t s) {
+    const size_t act = gemv_mma_act_smem(w.nb), slot8 = size_t(Slot<DT>::BYTES) * (GM_THREADS / 32);
+    constexpr size_t HALF = 112 * 1024, FULL = 224 * 1024;
+    if (act + 8 * slot8 <= HALF) return gemv_mma_go<DT, KS, 8>(v, w, bias, y, s, 2);
+    if (act + 4 * slot8 <= HALF) return gemv_mma_go<DT, KS, 4>(v, w, bias, y, s, 2);
+    if (act + 4 * slot8 <= FULL) return gemv_mma_go<DT, KS, 4>(v, w, bias, y, s, 1);
+    return cudaErrorInvalidValue;
+}
+
+// K-split of k_gemv_mma: keep splitting while the GPU would hold fewer
+// than 8 warps per SM and every slice keeps at least two block groups.
+// Depends on N and K only (results stay independent of M).
+inline int gemv_mma_ks(int n, int nb) {
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int tiles = (n + 15) / 16, ng = round4(nb) / 4;
+    int ks = 1;
+    while (ks < 8 && ng >= 2 * ks && tiles * ks < sms * 8) ks *= 2;
+    return ks;
+}
+
+template <int DT>
+struct GemvMmaF {
+    static cudaError_t run(const ActsView& v, const Weight& w, const float* bias, float* y, cudaStream_t s) {
+        switch (gemv_mma_ks(w.n, w.nb)) {
+            case 1: return gemv_mma_launch<DT, 1>(v, w, bias, y, s);
+            case 2: return gemv_mma_launch<DT, 2>(v, w, bias, y, s);
+            case 4: return gemv_mma_launch<DT, 4>(v, w, bias, y, s);
+            default: return gemv_mma_launch<DT, 8>(v, w, bias, y, s);
+        }
+    }
+};
+
+thread_local int t_gemv_kind = 0;
+
 template <int DT, int L, int MR>
 cudaError_t gemv_f32_launch(const float* a, int m, const Weight& w, const float* bias, float* y, cudaStream_t s) {
     k_gemv_f32<DT, L, MR><<<gemv_grid(k_gemv_f32<DT, L, MR>, w.n, L, 0), TPB, 0, s>>>(w.qs, w.qh, w.d, w.m, a, m, w.n,
@@ -737,8 +1211,17 @@ cudaError_t launch_block_dots(const ActsView& v, const Weight& w, int32_t* S, cu
     return by_dtype<BlockDotsF>(w.dtype, v, w, S, s);
 }
 
+void set_gemv_kind(int kind) { t_gemv_kind = kind; }
+
 cudaError_t launch_gemv_i8(const ActsView& v, const Weight& w, const float* bias, float* y, cudaStream_t s) {
     if (v.m <= 0 || w.n <= 0) return cudaSuccess;
+    // The integer-MMA kernel serves every m <= 8 (one instruction per block
+    // for 16 x 8 dots, cost flat in m), so a row's result never depends on
+    // m; the dp4a kernel is kept as an alternative (tests, benchmarks).
+    // The MMA kernel addresses the planes with 32-bit offsets.
+    const int kind = t_gemv_kind ? t_gemv_kind : 2;
+    if (kind == 2 && uint64_t(w.n) * uint64_t(round4(w.nb)) * uint64_t(qs_bytes(w.dtype)) < (uint64_t(1) << 32))
+        return by_dtype<GemvMmaF>(w.dtype, v, w, bias, y, s);
     return by_dtype<GemvI8F>(w.dtype, v, w, bias, y, s);
 }
 

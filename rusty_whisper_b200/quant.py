@@ -297,6 +297,11 @@ def set_gemm_path(path: int) -> None:
     _lib.check(_lib.lib().rwq_set_gemm_path(path))
 
 
+def set_gemv_kernel(kind: int) -> None:
+    """GEMV kernel for m <= 8: 0 automatic, 1 dp4a, 2 integer MMA."""
+    _lib.check(_lib.lib().rwq_set_gemv_kernel(kind))
+
+
 def stream_check(stream=None) -> None:
     """Synchronize the stream and raise if a kernel recorded a fault."""
     torch = _torch()

@@ -103,6 +103,48 @@ def test_matmul_int8_matches_oracle(rq, orc, dtype, m, k, n):
         assert close(y, orc.int8_scalar_matmul(a, dtype, raw, n)) < TOL
 
 
+@pytest.mark.parametrize("kind", [1, 2])
+@pytest.mark.parametrize("dtype", FORMATS)
+@pytest.mark.parametrize("m,k,n", [(1, 1024, 1000), (2, 96, 41), (5, 768, 3072), (7, 160, 333), (8, 3072, 768),
+                                   (3, 1280, 5120), (5, 4096, 257), (6, 8192, 40)])
+def test_gemv_kernels_match_oracle(rq, orc, kind, dtype, m, k, n):
+    """Both GEMV kernels (dp4a, integer MMA) at every K-split and tail."""
+    a, raw = _case(dtype, m, k, n, 17 * dtype + m + k + kind)
+    w = rq.QTensor([n, k], dtype, raw)
+    rq.set_gemv_kernel(kind)
+    try:
+        y = host(rq.matmul_t_q(cuda(a), w))
+        rq.stream_check()
+    finally:
+        rq.set_gemv_kernel(0)
+    assert close(y, orc.int8_scalar_matmul(a, dtype, raw, n)) < TOL
+    if k <= 4096:
+        # The reference's x86 tier rounds its per-block f32 terms (the
+        # +128 offset correction and the min term, quant.rs:452-454) on
+        # its own: at k = 8192 the tier alone is ~1e-3 away from the exact
+        # block dots for Q4_1/Q5_1, so the long row is held to the scalar
+        # int8 oracle only.
+        assert close(y, orc.matmul_t_q(a, dtype, raw, n)) < TOL
+
+
+@pytest.mark.parametrize("kind", [1, 2])
+def test_gemv_batch_invariance_per_kernel(rq, kind):
+    """Within each GEMV kernel a row's result is the same for M = 1..8."""
+    import torch
+    from rusty_whisper_b200 import synth
+    rq.set_gemv_kernel(kind)
+    try:
+        for dtype in FORMATS:
+            for k, n in ((1024, 3000), (768, 200)):
+                w = rq.QTensor([n, k], dtype, synth.random_blocks(dtype, n, k, 31 + k))
+                a = cuda(synth.normal(32, 8 * k).reshape(8, k))
+                y8 = rq.matmul_t_q(a, w)
+                for mm in (1, 2, 5, 7):
+                    assert torch.equal(rq.matmul_t_q(a[:mm], w), y8[:mm])
+    finally:
+        rq.set_gemv_kernel(0)
+
+
 @pytest.mark.parametrize("dtype", FORMATS)
 @pytest.mark.parametrize("m,k,n", [(1, 768, 768), (5, 256, 300), (20, 96, 41)])
 def test_matmul_f32_mode_matches_dequant_then_fp(rq, orc, dtype, m, k, n):
