@@ -217,6 +217,37 @@ int rwq_log_mel_dev(rwq_mel* p, const float* samples, int64_t n_windows, int64_t
 /* One window, host buffers (copies inside, synchronous). */
 int rwq_log_mel(rwq_mel* p, const float* samples, int64_t n_samples, float* out);
 
+/* ---- Encoder forward -----------------------------------------------------
+ * Replaces `encoder::encode` (reference src/encoder.rs:180-234) for a batch
+ * of 30 s windows, on the device: conv stem (k3 s1 then k3 s2, GELU),
+ * positions, n_layer pre-LN blocks {attention, MLP}, ln_post, with every
+ * block linear (`linear_w`, src/quant.rs:1054) on the quantized tensor-core
+ * GEMM with int8 activation semantics.  Tensors are set by their
+ * whisper.cpp names (those `encoder.rs` looks up), dense ones as f32
+ * (conv weights [n_state][in][3], biases, LayerNorm, positions
+ * [n_ctx][n_state]) and the six linears of each block as raw ggml blocks.
+ * Head dim 64 and n_state % 128 == 0 (every Whisper size).  An encoder
+ * serves one call at a time (its workspace is shared). */
+typedef struct rwq_encoder rwq_encoder;
+
+int rwq_encoder_new(int n_mels, int n_ctx, int n_state, int n_head, int n_layer, rwq_encoder** out);
+int rwq_encoder_free(rwq_encoder* e);
+int rwq_encoder_set_dense(rwq_encoder* e, const char* name, const float* data, int64_t count);
+int rwq_encoder_set_quant(rwq_encoder* e, const char* name, int dtype, const uint8_t* raw, size_t raw_len, int64_t n,
+                          int64_t k);
+/* Device buffers: mel [n_windows][n_mels][2*n_ctx] -> out
+ * [n_windows][n_ctx][n_state]; asynchronous on `stream`. */
+int rwq_encoder_encode_dev(rwq_encoder* e, const float* mel, int64_t n_windows, float* out, void* stream);
+/* Host buffers (copies inside, synchronous). */
+int rwq_encoder_encode(rwq_encoder* e, const float* mel, int64_t n_windows, float* out);
+
+/* Non-causal multi-head attention over projected q, k, v
+ * [n_windows][t][n_state] (`multi_head_attention`, src/encoder.rs:107-121,
+ * with `mha_split_kv` :48-80): softmax(q k^T / 8) v per head of 64, on f16
+ * tensor-core MMAs with f32 accumulation.  Device buffers, 16-byte aligned. */
+int rwq_attention_dev(const float* q, const float* k, const float* v, int64_t n_windows, int64_t t, int64_t n_state,
+                      int64_t n_head, float* out, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

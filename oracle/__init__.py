@@ -68,6 +68,14 @@ def lib():
             "orc_fft": (i32, [P, P, i32, P, P, i32]),
             "orc_mel_filterbank": (None, [i32, i32, i32, P]),
             "orc_log_mel": (i32, [P, i32, P, i32, P, P, i32]),
+            "orc_encoder_new": (P, [i32, i32, i32, i32, i32]),
+            "orc_encoder_free": (None, [P]),
+            "orc_encoder_set": (i32, [P, ctypes.c_char_p, P, sz, i32, P, i32, i32]),
+            "orc_encode": (i32, [P, P, P, i32]),
+            "orc_layernorm": (None, [P, sz, i32, P, P]),
+            "orc_gelu": (None, [P, sz]),
+            "orc_mha": (i32, [P, i32, P, P, i32, i32, i32, i32, P, i32]),
+            "orc_conv1d": (i32, [P, i32, i32, P, i32, i32, P, i32, P, i32]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(L, name)
@@ -278,3 +286,83 @@ def log_mel_spectrogram(samples: np.ndarray, filters: np.ndarray, n_mels: int, t
     _check(lib().orc_log_mel(_p(samples), samples.size, _p(filters), n_mels, _p(out), ctypes.byref(nf), threads),
            "log_mel")
     return out
+
+
+# ---------------------------------------------------------------- encoder
+def layernorm(x: np.ndarray, w: np.ndarray, b: np.ndarray) -> np.ndarray:
+    """tensor.rs:274-289 over the last dimension (returns a copy)."""
+    x = np.array(x, np.float32, order="C")
+    w = np.ascontiguousarray(w, np.float32)
+    b = np.ascontiguousarray(b, np.float32)
+    lib().orc_layernorm(_p(x), x.size // x.shape[-1], x.shape[-1], _p(w), _p(b))
+    return x
+
+
+def gelu(x: np.ndarray) -> np.ndarray:
+    """tensor.rs:291-306 (tanh approximation; returns a copy)."""
+    x = np.array(x, np.float32, order="C")
+    lib().orc_gelu(_p(x), x.size)
+    return x
+
+
+def mha(q: np.ndarray, k: np.ndarray, v: np.ndarray, n_head: int, causal: bool = False,
+        threads: int = 0) -> np.ndarray:
+    """encoder.rs:107-121 multi_head_attention over projected [t, n_state]."""
+    q = np.ascontiguousarray(q, np.float32)
+    k = np.ascontiguousarray(k, np.float32)
+    v = np.ascontiguousarray(v, np.float32)
+    out = np.zeros_like(q)
+    _check(lib().orc_mha(_p(q), q.shape[0], _p(k), _p(v), k.shape[0], q.shape[1], n_head, int(causal), _p(out),
+                         threads), "mha")
+    return out
+
+
+def conv1d(x: np.ndarray, w: np.ndarray, b: np.ndarray, stride: int, threads: int = 0) -> np.ndarray:
+    """tensor.rs:335-370: x [in_ch, t], w [out_ch, in_ch, kernel]."""
+    x = np.ascontiguousarray(x, np.float32)
+    w = np.ascontiguousarray(w, np.float32)
+    b = np.ascontiguousarray(b, np.float32)
+    in_ch, t = x.shape
+    out_ch, _, kernel = w.shape
+    t_out = (t + 2 * (kernel // 2) - kernel) // stride + 1
+    out = np.zeros((out_ch, t_out), np.float32)
+    _check(lib().orc_conv1d(_p(x), in_ch, t, _p(w), out_ch, kernel, _p(b), stride, _p(out), threads), "conv1d")
+    return out
+
+
+class Encoder:
+    """encoder.rs:180-234 with every quantized linear on matmul_t_q.
+
+    ``tensors`` maps whisper.cpp names to either an f32 array (dense) or a
+    ``(dtype, raw_bytes, n, k)`` tuple (quantized linear)."""
+
+    def __init__(self, n_mels: int, n_ctx: int, n_state: int, n_head: int, n_layer: int, tensors: dict):
+        self.shape = (n_mels, n_ctx, n_state, n_head, n_layer)
+        self._h = lib().orc_encoder_new(n_mels, n_ctx, n_state, n_head, n_layer)
+        if not self._h:
+            raise ValueError("bad encoder shape")
+        self._keep = []
+        for name, t in tensors.items():
+            if isinstance(t, tuple):
+                dtype, raw, n, k = t
+                raw = np.ascontiguousarray(raw, np.uint8)
+                self._keep.append(raw)
+                rc = lib().orc_encoder_set(self._h, name.encode(), None, 0, dtype, _p(raw), n, k)
+            else:
+                a = np.ascontiguousarray(t, np.float32).ravel()
+                self._keep.append(a)
+                rc = lib().orc_encoder_set(self._h, name.encode(), _p(a), a.size, 0, None, 0, 0)
+            _check(rc, f"encoder_set({name})")
+
+    def encode(self, mel: np.ndarray, threads: int = 0) -> np.ndarray:
+        n_mels, n_ctx, n_state = self.shape[:3]
+        mel = np.ascontiguousarray(mel, np.float32)
+        assert mel.shape == (n_mels, 2 * n_ctx)
+        out = np.zeros((n_ctx, n_state), np.float32)
+        _check(lib().orc_encode(self._h, _p(mel), _p(out), threads), "encode")
+        return out
+
+    def __del__(self):
+        if getattr(self, "_h", None):
+            lib().orc_encoder_free(self._h)
+            self._h = None

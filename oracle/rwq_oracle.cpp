@@ -20,6 +20,9 @@
 //   * log-mel front end: periodic Hann window, 400-point FFT (radix-2
 //     recursion down to odd-length DFTs), power spectrum, Slaney mel
 //     filterbank, log10 + dynamic-range clamp  audio.rs:10-198
+//   * encoder graph: conv stem, pre-LN attention / MLP blocks, ln_post,
+//     with layernorm, tanh-GELU, softmax, conv1d and matmul
+//                                      encoder.rs:48-234, tensor.rs:75-100, 274-370
 //   * test helpers: LCG test_matrix, rand_byte, quantize_q8_0, quantize_q5_1
 //                                      quant.rs:1071-1123, quant.rs:1131-1135
 //
@@ -32,6 +35,8 @@
 // Build: oracle/build.sh (g++ -O2 -ffp-contract=off, no fast-math; the
 // reference never fuses d*q+m, and neither may this file).
 #include <immintrin.h>
+#include <cstdlib>
+#include <string>
 #include <algorithm>
 #include <cmath>
 #include <cstdint>
@@ -1046,6 +1051,277 @@ int orc_log_mel(const float* samples, int n, const float* filters, int n_mels, f
     for (size_t i = 0; i < total; ++i) mmax = std::fmax(mmax, out[i]);
     for (size_t i = 0; i < total; ++i) out[i] = (std::fmax(out[i], mmax - 8.0f) + 4.0f) / 4.0f;
     if (n_frames_out) *n_frames_out = n_frames;
+    return 0;
+}
+
+}  // extern "C"
+
+// ================================================================ encoder
+// Restatement of the reference's encoder graph (encoder.rs:1-234) and the
+// dense tensor ops it uses (tensor.rs:75-100 matmul, :274-370 layernorm,
+// gelu, softmax, conv1d), with every quantized linear going through the
+// persistent-weight matmul_t_q above (quant.rs:1054-1063 linear_w).
+namespace {
+
+// tensor.rs:274-289 (eps as ggml: 1e-5)
+void ln_rows(float* x, size_t rows, int cols, const float* w, const float* b) {
+    for (size_t r = 0; r < rows; ++r) {
+        float* row = x + r * cols;
+        float s = 0.f;
+        for (int i = 0; i < cols; ++i) s += row[i];
+        const float mean = s / float(cols);
+        float v = 0.f;
+        for (int i = 0; i < cols; ++i) v += (row[i] - mean) * (row[i] - mean);
+        const float var = v / float(cols);
+        const float inv = 1.0f / std::sqrt(var + 1e-5f);
+        for (int i = 0; i < cols; ++i) row[i] = (row[i] - mean) * inv * w[i] + b[i];
+    }
+}
+
+// tensor.rs:291-306 (tanh approximation)
+void gelu_n(float* x, size_t n) {
+    const float C = 0.7978846f;
+    for (size_t i = 0; i < n; ++i) {
+        const float t = x[i];
+        x[i] = 0.5f * t * (1.0f + std::tanh(C * (t + 0.044715f * t * t * t)));
+    }
+}
+
+// tensor.rs:309-331
+void softmax_rows(float* x, size_t rows, int cols) {
+    for (size_t r = 0; r < rows; ++r) {
+        float* row = x + r * cols;
+        float mx = -3.40282347e+38f;  // f32::MIN, folded with f32::max
+        for (int i = 0; i < cols; ++i) mx = std::fmax(mx, row[i]);
+        float sum = 0.f;
+        for (int i = 0; i < cols; ++i) {
+            row[i] = std::exp(row[i] - mx);
+            sum += row[i];
+        }
+        for (int i = 0; i < cols; ++i) row[i] /= sum;
+    }
+}
+
+// tensor.rs:335-370: input [in_ch][t], weight [out][in][kernel], pad kernel/2.
+void conv1d_ref(const float* in, int in_ch, int t, const float* w, int out_ch, int kernel, const float* bias,
+                int stride, float* out, int threads) {
+    const int pad = kernel / 2, t_out = (t + 2 * pad - kernel) / stride + 1;
+    auto chans = [&](int o0, int o1) {
+        for (int oc = o0; oc < o1; ++oc)
+            for (int ot = 0; ot < t_out; ++ot) {
+                float sum = bias[oc];
+                for (int ic = 0; ic < in_ch; ++ic) {
+                    const float* wr = w + (size_t(oc) * in_ch + ic) * kernel;
+                    const float* ir = in + size_t(ic) * t;
+                    for (int k = 0; k < kernel; ++k) {
+                        const long it = long(ot) * stride + k - pad;
+                        if (it >= 0 && it < t) sum += wr[k] * ir[it];
+                    }
+                }
+                out[size_t(oc) * t_out + ot] = sum;
+            }
+    };
+    if (threads > 1 && out_ch >= threads) {
+        const int chunk = (out_ch + threads - 1) / threads;
+        std::vector<std::thread> ths;
+        for (int o0 = 0; o0 < out_ch; o0 += chunk) ths.emplace_back(chans, o0, std::min(out_ch, o0 + chunk));
+        for (auto& th : ths) th.join();
+    } else {
+        chans(0, out_ch);
+    }
+}
+
+// tensor.rs:75-100: C = A[m,k] x B[k,n], zero A entries skipped.
+void matmul_ref(const float* a, int m, int k, const float* b, int n, float* out) {
+    std::fill(out, out + size_t(m) * n, 0.f);
+    for (int i = 0; i < m; ++i) {
+        float* o = out + size_t(i) * n;
+        for (int p = 0; p < k; ++p) {
+            const float av = a[size_t(i) * k + p];
+            if (av == 0.0f) continue;
+            const float* br = b + size_t(p) * n;
+            for (int j = 0; j < n; ++j) o[j] += av * br[j];
+        }
+    }
+}
+
+// encoder.rs:48-80 (mha_split_kv over already-projected q, k, v [t, n_state]).
+void mha_ref(const float* q, int tq, const float* k, const float* v, int tkv, int n_state, int n_head, bool causal,
+             float* out, int threads) {
+    const int dh = n_state / n_head;
+    const float scale = 1.0f / std::sqrt(float(dh));
+    auto heads = [&](int h0, int h1) {
+        std::vector<float> qh(size_t(tq) * dh), kh(size_t(tkv) * dh), vh(size_t(tkv) * dh), sc(size_t(tq) * tkv),
+            oh(size_t(tq) * dh);
+        for (int h = h0; h < h1; ++h) {
+            for (int r = 0; r < tq; ++r)
+                std::memcpy(&qh[size_t(r) * dh], q + size_t(r) * n_state + h * dh, sizeof(float) * dh);
+            for (int r = 0; r < tkv; ++r) {
+                std::memcpy(&kh[size_t(r) * dh], k + size_t(r) * n_state + h * dh, sizeof(float) * dh);
+                std::memcpy(&vh[size_t(r) * dh], v + size_t(r) * n_state + h * dh, sizeof(float) * dh);
+            }
+            orc_matmul_t(qh.data(), tq, dh, kh.data(), tkv, sc.data(), 1);
+            for (auto& s : sc) s *= scale;
+            if (causal) {
+                const int off = tkv - tq;
+                for (int i = 0; i < tq; ++i)
+                    for (int j = off + i + 1; j < tkv; ++j) sc[size_t(i) * tkv + j] = -INFINITY;
+            }
+            softmax_rows(sc.data(), size_t(tq), tkv);
+            matmul_ref(sc.data(), tq, tkv, vh.data(), dh, oh.data());
+            for (int r = 0; r < tq; ++r)
+                std::memcpy(out + size_t(r) * n_state + h * dh, &oh[size_t(r) * dh], sizeof(float) * dh);
+        }
+    };
+    if (threads > 1 && n_head > 1) {
+        std::vector<std::thread> ths;
+        const int per = (n_head + threads - 1) / threads;
+        for (int h0 = 0; h0 < n_head; h0 += per) ths.emplace_back(heads, h0, std::min(n_head, h0 + per));
+        for (auto& th : ths) th.join();
+    } else {
+        heads(0, n_head);
+    }
+}
+
+struct OrcLayer {
+    std::vector<float> attn_ln_w, attn_ln_b, q_b, v_b, o_b, mlp_ln_w, mlp_ln_b, fc1_b, fc2_b;
+    OrcQTensor *q = nullptr, *k = nullptr, *v = nullptr, *o = nullptr, *fc1 = nullptr, *fc2 = nullptr;
+};
+
+struct OrcEncoder {
+    int n_mels, n_ctx, n_state, n_head, n_layer;
+    std::vector<float> conv1_w, conv1_b, conv2_w, conv2_b, pos, ln_post_w, ln_post_b;
+    std::vector<OrcLayer> layers;
+    ~OrcEncoder() {
+        for (auto& l : layers)
+            for (OrcQTensor* t : {l.q, l.k, l.v, l.o, l.fc1, l.fc2}) delete t;
+    }
+};
+
+// quant.rs:1054-1063: y = x W^T (+ b) through the weight's own matmul_t_q.
+void linear_q(OrcQTensor* w, const float* x, int m, const float* bias, float* y, int threads) {
+    orc_qtensor_matmul(w, x, m, y, 0, threads);
+    if (bias)
+        for (int i = 0; i < m; ++i)
+            for (int j = 0; j < w->n; ++j) y[size_t(i) * w->n + j] += bias[j];
+}
+
+}  // namespace
+
+extern "C" {
+
+void* orc_encoder_new(int n_mels, int n_ctx, int n_state, int n_head, int n_layer) {
+    if (n_mels <= 0 || n_ctx <= 0 || n_state <= 0 || n_head <= 0 || n_state % n_head || n_layer < 0) return nullptr;
+    auto* e = new OrcEncoder{n_mels, n_ctx, n_state, n_head, n_layer, {}, {}, {}, {}, {}, {}, {}, {}};
+    e->layers.resize(size_t(n_layer));
+    return e;
+}
+
+void orc_encoder_free(void* h) { delete static_cast<OrcEncoder*>(h); }
+
+// Tensors by their whisper.cpp names (encoder.rs:130-234).  Dense ones are
+// f32 arrays; the six linears per block are raw ggml blocks.
+int orc_encoder_set(void* h, const char* name, const float* dense, size_t count, int dtype, const uint8_t* raw,
+                    int n, int k) {
+    auto* e = static_cast<OrcEncoder*>(h);
+    std::string s(name);
+    auto vec = [&](std::vector<float>& dst) {
+        if (!dense) return -1;
+        dst.assign(dense, dense + count);
+        return 0;
+    };
+    if (s == "encoder.conv1.weight") return vec(e->conv1_w);
+    if (s == "encoder.conv1.bias") return vec(e->conv1_b);
+    if (s == "encoder.conv2.weight") return vec(e->conv2_w);
+    if (s == "encoder.conv2.bias") return vec(e->conv2_b);
+    if (s == "encoder.positional_embedding") return vec(e->pos);
+    if (s == "encoder.ln_post.weight") return vec(e->ln_post_w);
+    if (s == "encoder.ln_post.bias") return vec(e->ln_post_b);
+    const std::string pre = "encoder.blocks.";
+    if (s.compare(0, pre.size(), pre) != 0) return -1;
+    size_t dot = s.find('.', pre.size());
+    if (dot == std::string::npos) return -1;
+    const int l = std::atoi(s.substr(pre.size(), dot - pre.size()).c_str());
+    if (l < 0 || l >= e->n_layer) return -1;
+    OrcLayer& L = e->layers[size_t(l)];
+    const std::string f = s.substr(dot + 1);
+    auto quant = [&](OrcQTensor*& dst) {
+        if (!raw) return -1;
+        delete dst;
+        dst = static_cast<OrcQTensor*>(orc_qtensor_new(dtype, raw, n, k));
+        return dst ? 0 : -1;
+    };
+    if (f == "attn_ln.weight") return vec(L.attn_ln_w);
+    if (f == "attn_ln.bias") return vec(L.attn_ln_b);
+    if (f == "attn.query.weight") return quant(L.q);
+    if (f == "attn.query.bias") return vec(L.q_b);
+    if (f == "attn.key.weight") return quant(L.k);
+    if (f == "attn.value.weight") return quant(L.v);
+    if (f == "attn.value.bias") return vec(L.v_b);
+    if (f == "attn.out.weight") return quant(L.o);
+    if (f == "attn.out.bias") return vec(L.o_b);
+    if (f == "mlp_ln.weight") return vec(L.mlp_ln_w);
+    if (f == "mlp_ln.bias") return vec(L.mlp_ln_b);
+    if (f == "mlp.0.weight") return quant(L.fc1);
+    if (f == "mlp.0.bias") return vec(L.fc1_b);
+    if (f == "mlp.2.weight") return quant(L.fc2);
+    if (f == "mlp.2.bias") return vec(L.fc2_b);
+    return -1;
+}
+
+// encoder.rs:180-234 for one window: mel [n_mels][2*n_ctx] -> out [n_ctx][n_state].
+int orc_encode(void* h, const float* mel, float* out, int threads) {
+    auto* e = static_cast<OrcEncoder*>(h);
+    if (!e) return -1;
+    if (threads <= 0) threads = n_threads_default();
+    const int T = e->n_ctx, D = e->n_state, F = 2 * T;
+    for (auto& L : e->layers)
+        if (!L.q || !L.k || !L.v || !L.o || !L.fc1 || !L.fc2) return -2;
+    std::vector<float> c1(size_t(D) * F), c2(size_t(D) * T);
+    conv1d_ref(mel, e->n_mels, F, e->conv1_w.data(), D, 3, e->conv1_b.data(), 1, c1.data(), threads);
+    gelu_n(c1.data(), c1.size());
+    conv1d_ref(c1.data(), D, F, e->conv2_w.data(), D, 3, e->conv2_b.data(), 2, c2.data(), threads);
+    gelu_n(c2.data(), c2.size());
+    std::vector<float> x(size_t(T) * D);
+    for (int i = 0; i < D; ++i)
+        for (int t = 0; t < T; ++t) x[size_t(t) * D + i] = c2[size_t(i) * T + t];
+    for (size_t i = 0; i < x.size(); ++i) x[i] += e->pos[i];
+    const int F4 = e->layers.empty() ? 0 : e->layers[0].fc1->n;
+    std::vector<float> cur(x.size()), q(x.size()), k(x.size()), v(x.size()), att(x.size()), proj(x.size()),
+        hbuf(size_t(T) * std::max(F4, 1));
+    for (auto& L : e->layers) {
+        cur = x;
+        ln_rows(cur.data(), size_t(T), D, L.attn_ln_w.data(), L.attn_ln_b.data());
+        linear_q(L.q, cur.data(), T, L.q_b.data(), q.data(), threads);
+        linear_q(L.k, cur.data(), T, nullptr, k.data(), threads);
+        linear_q(L.v, cur.data(), T, L.v_b.data(), v.data(), threads);
+        mha_ref(q.data(), T, k.data(), v.data(), T, D, e->n_head, false, att.data(), threads);
+        linear_q(L.o, att.data(), T, L.o_b.data(), proj.data(), threads);
+        for (size_t i = 0; i < x.size(); ++i) x[i] += proj[i];
+        cur = x;
+        ln_rows(cur.data(), size_t(T), D, L.mlp_ln_w.data(), L.mlp_ln_b.data());
+        linear_q(L.fc1, cur.data(), T, L.fc1_b.data(), hbuf.data(), threads);
+        gelu_n(hbuf.data(), hbuf.size());
+        linear_q(L.fc2, hbuf.data(), T, L.fc2_b.data(), proj.data(), threads);
+        for (size_t i = 0; i < x.size(); ++i) x[i] += proj[i];
+    }
+    ln_rows(x.data(), size_t(T), D, e->ln_post_w.data(), e->ln_post_b.data());
+    std::memcpy(out, x.data(), sizeof(float) * x.size());
+    return 0;
+}
+
+// Pieces, for the kernels' own parity tests.
+void orc_layernorm(float* x, size_t rows, int cols, const float* w, const float* b) { ln_rows(x, rows, cols, w, b); }
+void orc_gelu(float* x, size_t n) { gelu_n(x, n); }
+int orc_mha(const float* q, int tq, const float* k, const float* v, int tkv, int n_state, int n_head, int causal,
+            float* out, int threads) {
+    if (n_head <= 0 || n_state % n_head) return -1;
+    mha_ref(q, tq, k, v, tkv, n_state, n_head, causal != 0, out, threads <= 0 ? n_threads_default() : threads);
+    return 0;
+}
+int orc_conv1d(const float* in, int in_ch, int t, const float* w, int out_ch, int kernel, const float* bias,
+               int stride, float* out, int threads) {
+    conv1d_ref(in, in_ch, t, w, out_ch, kernel, bias, stride, out, threads <= 0 ? n_threads_default() : threads);
     return 0;
 }
 

@@ -64,6 +64,13 @@ SIGNATURES = {
     "rwq_mel_free": (_I, [_P]),
     "rwq_log_mel_dev": (_I, [_P, _P, _L, _L, _P, _P]),
     "rwq_log_mel": (_I, [_P, _P, _L, _P]),
+    "rwq_encoder_new": (_I, [_I, _I, _I, _I, _I, ctypes.POINTER(_P)]),
+    "rwq_encoder_free": (_I, [_P]),
+    "rwq_encoder_set_dense": (_I, [_P, ctypes.c_char_p, _P, _L]),
+    "rwq_encoder_set_quant": (_I, [_P, ctypes.c_char_p, _I, _P, _SZ, _L, _L]),
+    "rwq_encoder_encode_dev": (_I, [_P, _P, _L, _P, _P]),
+    "rwq_encoder_encode": (_I, [_P, _P, _L, _P]),
+    "rwq_attention_dev": (_I, [_P, _P, _P, _L, _L, _L, _L, _P, _P]),
 }
 
 _lib = None

@@ -12,6 +12,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <functional>
 #include <map>
 #include <mutex>
 #include <string>
@@ -19,6 +20,7 @@
 #include "../../include/rwq.h"
 #include "rwq_common.cuh"
 #include "rwq_internal.h"
+#include "rwq_encoder.h"
 
 struct rwq_qtensor {
     rwq::Weight w;
@@ -275,6 +277,23 @@ cudaStream_t thread_stream() {
 }
 
 }  // namespace
+
+int rwq::gemm_quantized(const ActsView& v, rwq_qtensor* w, const float* bias, float* out, cudaStream_t s) {
+    Workspace* ws = nullptr;
+    int rc = get_workspace(s, &ws);
+    if (rc) return rc;
+    if (v.k != w->w.k) return fail(RWQ_ERR_SHAPE, "gemm inner dims: %d vs %d", v.k, w->w.k);
+    return run_quantized(v, true, w, bias, out, s, nullptr, ws->err);
+}
+
+int rwq::with_stream_scratch(cudaStream_t s, size_t bytes, const std::function<int(void*)>& fn) {
+    Workspace* ws = nullptr;
+    int rc = get_workspace(s, &ws);
+    if (rc) return rc;
+    std::lock_guard<std::mutex> g(ws->mu);
+    if ((rc = ensure_cap(ws, bytes))) return rc;
+    return fn(ws->buf);
+}
 
 extern "C" {
 

@@ -1,0 +1,40 @@
+// rwq_encoder.h -- internal declarations of the encoder forward's kernels
+// (rwq_encoder_kernels.cu) and the quantized-GEMM hook the encoder uses
+// (rwq_api.cu).  Not part of the public C ABI (include/rwq.h).
+#pragma once
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <cstddef>
+#include <cstdint>
+#include <functional>
+#include "rwq_internal.h"
+
+struct rwq_qtensor;
+
+namespace rwq {
+
+// Row transforms in front of the int8 quantizer (k_rows_quant).
+enum RowQuantMode : int { RQ_PLAIN = 0, RQ_GELU = 1, RQ_LN = 2, RQ_ADD_LN = 3 };
+
+cudaError_t launch_rows_quant(int mode, const float* x, const float* add, float* xout, const float* lw,
+                              const float* lb, int m, int k, int m_pad, uint16_t* q16, float* dT, float* uT,
+                              float* yout, cudaStream_t s);
+cudaError_t launch_im2col3(const float* in, int n_win, int c_in, int t_in, int t_out, int stride, size_t sw,
+                           size_t sc, size_t st, float* out, cudaStream_t s);
+cudaError_t launch_bias_gelu(float* y, size_t rows, int cols, const float* bias, const float* pos, int t_per_win,
+                             cudaStream_t s);
+cudaError_t launch_to_heads(const float* src, int ld, int col0, int n_win, int T, int H, float scale, __half* dst,
+                            cudaStream_t s);
+cudaError_t launch_attention(const __half* Qh, const __half* Kh, const __half* Vh, int n_win, int T, int H,
+                             float* out, cudaStream_t s);
+
+// The tensor-core GEMM on activations already quantized into `v` (GEMM
+// layout): out = A W^T (+ bias).  Builds the weight's operand cache on
+// first use.  Returns an RWQ_* status (error text set).
+int gemm_quantized(const ActsView& v, rwq_qtensor* w, const float* bias, float* out, cudaStream_t s);
+
+// Run `fn` with this stream's scratch arena (at least `bytes`), holding
+// its lock.  Returns fn's status (or an RWQ_* error).
+int with_stream_scratch(cudaStream_t s, size_t bytes, const std::function<int(void*)>& fn);
+
+}  // namespace rwq

@@ -1,0 +1,438 @@
+// rwq_encoder_kernels.cu -- the device kernels of the encoder forward
+// (reference encoder.rs:123-234) around the quantized GEMM:
+//   * k_rows_quant: per row, optional residual add, LayerNorm
+//     (tensor.rs:274-289) or tanh-GELU (tensor.rs:291-306), then the int8
+//     activation quantizer (quant.rs:690-716) writing the tensor-core
+//     GEMM's operand directly (f16 codes + transposed block scales);
+//   * the conv stem as im2col + GEMM with a bias/GELU/position epilogue;
+//   * k_to_heads + k_attn: non-causal multi-head attention
+//     (encoder.rs:48-80) as a flash-style kernel on f16 tensor-core MMAs
+//     with f32 accumulation and an online softmax, so the [T, T] score
+//     matrix never leaves the SM.
+#include <cuda_fp16.h>
+#include <cstdint>
+#include "rwq_common.cuh"
+#include "rwq_encoder.h"
+
+namespace rwq {
+
+namespace {
+
+// tensor.rs:291-306, same operation order:
+//   0.5 * t * (1 + tanh(C * (t + 0.044715 * t * t * t)))
+__device__ __forceinline__ float gelu_ref(float t) {
+    const float C = 0.7978846f;
+    const float cube = __fmul_rn(__fmul_rn(__fmul_rn(0.044715f, t), t), t);
+    return __fmul_rn(__fmul_rn(0.5f, t), __fadd_rn(1.0f, tanhf(__fmul_rn(C, __fadd_rn(t, cube)))));
+}
+
+// One 32-element block held as 4 values by each of 8 consecutive lanes
+// (lane & 7 = position): the reference quantizer (quant.rs:690-716), as
+// k_quantize does it -- d = amax/127, inv = 1/d or 0, q = round(x*inv)
+// half away from zero, clamped to +-127, NaN -> 0.
+__device__ __forceinline__ void quant_block4(float4 x, int row, int bl, int m_pad, uint16_t* __restrict__ q16p,
+                                             float* __restrict__ dT, float* __restrict__ uT) {
+    auto absnn = [](float v) { const float w = fabsf(v); return isnan(w) ? 0.f : w; };
+    float amax = fmaxf(fmaxf(absnn(x.x), absnn(x.y)), fmaxf(absnn(x.z), absnn(x.w)));
+#pragma unroll
+    for (int o = 4; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    const float d = __fdiv_rn(amax, 127.0f);
+    const float inv = d > 0.f ? __fdiv_rn(1.0f, d) : 0.f;
+    auto code = [inv](float v) {
+        const float r = roundf(__fmul_rn(v, inv));
+        return isnan(r) ? 0 : int(fminf(127.f, fmaxf(-127.f, r)));
+    };
+    const int c0 = code(x.x), c1 = code(x.y), c2 = code(x.z), c3 = code(x.w);
+    int s = c0 + c1 + c2 + c3;
+#pragma unroll
+    for (int o = 4; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    const uint32_t h01 = uint32_t(__half_as_ushort(__int2half_rn(c0))) | (uint32_t(__half_as_ushort(__int2half_rn(c1))) << 16);
+    const uint32_t h23 = uint32_t(__half_as_ushort(__int2half_rn(c2))) | (uint32_t(__half_as_ushort(__int2half_rn(c3))) << 16);
+    *reinterpret_cast<uint2*>(q16p) = make_uint2(h01, h23);
+    if ((threadIdx.x & 7) == 0) {
+        dT[size_t(bl) * m_pad + row] = d;
+        uT[size_t(bl) * m_pad + row] = __fmul_rn(d, float(s));
+    }
+}
+
+// One warp per row of k elements (k % 128 == 0); lane l covers elements
+// 4l..4l+3 of each 128-element chunk, so 8 lanes share a quant block.
+// MODE: RQ_PLAIN quantize x; RQ_GELU quantize gelu(x); RQ_LN quantize
+// LayerNorm(x); RQ_ADD_LN x += add (written back to xout), then as RQ_LN.
+// With q16 == nullptr the transformed row is written to yout (f32) instead
+// (ln_post).  Rows m..m_pad-1 get zero block scales.  x and xout may
+// alias: the residual stream is updated in place.
+template <int MODE, int NV>
+__global__ void __launch_bounds__(256) k_rows_quant(const float* x, const float* __restrict__ add, float* xout,
+                                                    const float* __restrict__ lw, const float* __restrict__ lb,
+                                                    int m, int k, int m_pad,
+                                                    uint16_t* __restrict__ q16, float* __restrict__ dT,
+                                                    float* __restrict__ uT, float* __restrict__ yout) {
+    pdl_trigger();
+    pdl_wait();
+    const int lane = threadIdx.x & 31;
+    const int row = int((size_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5);
+    if (row >= m_pad) return;
+    const int nb = k / QK, nch = k / 128;
+    if (row >= m) {
+        if (q16)
+            for (int bl = lane; bl < nb; bl += 32) {
+                dT[size_t(bl) * m_pad + row] = 0.f;
+                uT[size_t(bl) * m_pad + row] = 0.f;
+            }
+        return;
+    }
+    const float4* xr = reinterpret_cast<const float4*>(x + size_t(row) * k);
+    auto emit = [&](int c, float4 v) {
+        const int e = c * 128 + lane * 4;
+        if (q16) quant_block4(v, row, e / QK, m_pad, q16 + size_t(row) * k + e, dT, uT);
+        else *reinterpret_cast<float4*>(yout + size_t(row) * k + e) = v;
+    };
+    if (MODE == RQ_PLAIN || MODE == RQ_GELU) {
+        for (int c = 0; c < nch; ++c) {
+            float4 v = __ldg(xr + c * 32 + lane);
+            if (MODE == RQ_GELU) v = make_float4(gelu_ref(v.x), gelu_ref(v.y), gelu_ref(v.z), gelu_ref(v.w));
+            emit(c, v);
+        }
+        return;
+    }
+    // LayerNorm: the row stays in registers (nch <= NV).
+    float4 v[NV];
+    float s = 0.f;
+#pragma unroll
+    for (int c = 0; c < NV; ++c) {
+        if (c < nch) {
+            v[c] = xr[c * 32 + lane];
+            if (MODE == RQ_ADD_LN) {
+                const float4 a = __ldg(reinterpret_cast<const float4*>(add + size_t(row) * k) + c * 32 + lane);
+                v[c] = make_float4(__fadd_rn(v[c].x, a.x), __fadd_rn(v[c].y, a.y), __fadd_rn(v[c].z, a.z),
+                                   __fadd_rn(v[c].w, a.w));
+                reinterpret_cast<float4*>(xout + size_t(row) * k)[c * 32 + lane] = v[c];
+            }
+            s += (v[c].x + v[c].y) + (v[c].z + v[c].w);
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    const float mean = __fdiv_rn(s, float(k));
+    float q = 0.f;
+#pragma unroll
+    for (int c = 0; c < NV; ++c) {
+        if (c < nch) {
+            const float a = __fsub_rn(v[c].x, mean), b = __fsub_rn(v[c].y, mean), cc = __fsub_rn(v[c].z, mean),
+                        dd = __fsub_rn(v[c].w, mean);
+            q += (__fmul_rn(a, a) + __fmul_rn(b, b)) + (__fmul_rn(cc, cc) + __fmul_rn(dd, dd));
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) q += __shfl_xor_sync(0xffffffffu, q, o);
+    const float var = __fdiv_rn(q, float(k));
+    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, 1e-5f)));
+#pragma unroll
+    for (int c = 0; c < NV; ++c) {
+        if (c < nch) {
+            const int e = c * 128 + lane * 4;
+            const float4 w = __ldg(reinterpret_cast<const float4*>(lw + e));
+            const float4 b = __ldg(reinterpret_cast<const float4*>(lb + e));
+            auto f = [&](float xv, float wv, float bv) {
+                return __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(xv, mean), inv), wv), bv);
+            };
+            emit(c, make_float4(f(v[c].x, w.x, b.x), f(v[c].y, w.y, b.y), f(v[c].z, w.z, b.z), f(v[c].w, w.w, b.w)));
+        }
+    }
+}
+
+// im2col for a kernel-3, pad-1 conv over windows: out row (w, t) holds
+// in(w, ic, t*stride + j - 1) at column ic*3 + j (zero outside [0, t_in)).
+// in(w, ic, t) = in[w*sw + ic*sc + t*st].
+__global__ void k_im2col3(const float* __restrict__ in, int n_win, int c_in, int t_in, int t_out, int stride,
+                          size_t sw, size_t sc, size_t st, float* __restrict__ out) {
+    const size_t kcols = size_t(c_in) * 3;
+    const size_t total = size_t(n_win) * t_out * kcols;
+    for (size_t i = size_t(blockIdx.x) * blockDim.x + threadIdx.x; i < total; i += size_t(gridDim.x) * blockDim.x) {
+        const size_t col = i % kcols, r = i / kcols;
+        const int t = int(r % t_out), w = int(r / t_out);
+        const int ic = int(col / 3), j = int(col % 3);
+        const int ti = t * stride + j - 1;
+        out[i] = (ti >= 0 && ti < t_in) ? in[size_t(w) * sw + size_t(ic) * sc + size_t(ti) * st] : 0.f;
+    }
+}
+
+// y[r][c] = gelu(y[r][c] + bias[c]) (+ pos[(r % t_per_win)][c] if pos).
+__global__ void k_bias_gelu(float* __restrict__ y, size_t rows, int cols, const float* __restrict__ bias,
+                            const float* __restrict__ pos, int t_per_win) {
+    const size_t total = rows * size_t(cols);
+    for (size_t i = size_t(blockIdx.x) * blockDim.x + threadIdx.x; i < total; i += size_t(gridDim.x) * blockDim.x) {
+        const int c = int(i % cols);
+        float v = gelu_ref(__fadd_rn(y[i], bias[c]));
+        if (pos) v = __fadd_rn(v, pos[size_t((i / cols) % t_per_win) * cols + c]);
+        y[i] = v;
+    }
+}
+
+// f32 [n_win*T][ld] (head h = columns col0 + h*64 ..) -> f16 [n_win][H][T][64],
+// multiplied by `scale` (a power of two: exact).
+__global__ void k_to_heads(const float* __restrict__ src, int ld, int col0, int n_win, int T, int H, float scale,
+                           __half* __restrict__ dst) {
+    const size_t total = size_t(n_win) * H * T * 16;   // float4 groups
+    for (size_t i = size_t(blockIdx.x) * blockDim.x + threadIdx.x; i < total; i += size_t(gridDim.x) * blockDim.x) {
+        const int c4 = int(i & 15);
+        const size_t r = i >> 4;                         // (w, h, t)
+        const int t = int(r % T), h = int((r / T) % H), w = int(r / (size_t(T) * H));
+        const float4 v = __ldg(reinterpret_cast<const float4*>(src + (size_t(w) * T + t) * ld + col0 + h * 64) + c4);
+        const __half2 a = __floats2half2_rn(__fmul_rn(v.x, scale), __fmul_rn(v.y, scale));
+        const __half2 b = __floats2half2_rn(__fmul_rn(v.z, scale), __fmul_rn(v.w, scale));
+        uint2 o;
+        o.x = *reinterpret_cast<const uint32_t*>(&a);
+        o.y = *reinterpret_cast<const uint32_t*>(&b);
+        reinterpret_cast<uint2*>(dst + r * 64)[c4] = o;
+    }
+}
+
+// ------------------------------------------------------------ attention
+// Flash-style attention, head dim 64.  CTA: 4 warps x 16 query rows; K/V
+// tiles of 64 keys double-buffered in shared memory by cp.async; f16
+// m16n8k16 MMAs with f32 accumulators; 128-byte rows swizzled by 16-byte
+// chunk (chunk ^ (row & 7)) so ldmatrix is conflict-free.
+constexpr int AT_Q = 64, AT_K = 64, AT_D = 64, AT_THREADS = 128;
+
+__device__ __forceinline__ uint32_t swz(int row, int chunk) { return uint32_t(row * 128 + ((chunk ^ (row & 7)) << 4)); }
+
+__device__ __forceinline__ void cpa16(uint32_t dst, const void* src, bool ok) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(ok ? 16 : 0) : "memory");
+}
+
+__device__ __forceinline__ void ldm_x4(uint32_t addr, uint32_t (&r)[4]) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(addr));
+}
+__device__ __forceinline__ void ldm_x4_t(uint32_t addr, uint32_t (&r)[4]) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(addr));
+}
+__device__ __forceinline__ void mma16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+                 "{%0,%1,%2,%3};"
+                 : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+                 : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
+    const __half2 h = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+__global__ void __launch_bounds__(AT_THREADS) k_attn(const __half* __restrict__ Qh, const __half* __restrict__ Kh,
+                                                     const __half* __restrict__ Vh, int T, int H,
+                                                     float* __restrict__ out) {
+    pdl_trigger();
+    __shared__ __align__(128) uint8_t sQ[AT_Q * 128];
+    __shared__ __align__(128) uint8_t sK[2][AT_K * 128];
+    __shared__ __align__(128) uint8_t sV[2][AT_K * 128];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, g = lane >> 2, tig = lane & 3;
+    const int w = blockIdx.z, h = blockIdx.y, q0 = blockIdx.x * AT_Q;
+    const size_t head = (size_t(w) * H + h) * size_t(T) * AT_D;
+    const __half* Qb = Qh + head;
+    const __half* Kb = Kh + head;
+    const __half* Vb = Vh + head;
+    const uint32_t sQa = uint32_t(__cvta_generic_to_shared(sQ));
+    const uint32_t sKa[2] = {uint32_t(__cvta_generic_to_shared(sK[0])), uint32_t(__cvta_generic_to_shared(sK[1]))};
+    const uint32_t sVa[2] = {uint32_t(__cvta_generic_to_shared(sV[0])), uint32_t(__cvta_generic_to_shared(sV[1]))};
+
+    auto load_tile = [&](const __half* base, int r0, uint32_t dst) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int idx = tid + i * AT_THREADS, row = idx >> 3, ch = idx & 7;
+            const bool ok = r0 + row < T;
+            cpa16(dst + swz(row, ch), base + size_t(ok ? r0 + row : 0) * AT_D + ch * 8, ok);
+        }
+    };
+    pdl_wait();
+    load_tile(Qb, q0, sQa);
+    load_tile(Kb, 0, sKa[0]);
+    load_tile(Vb, 0, sVa[0]);
+    asm volatile("cp.async.commit_group;" ::: "memory");
+
+    const int nkv = (T + AT_K - 1) / AT_K;
+    float o[8][4];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+    float mrow[2] = {-INFINITY, -INFINITY}, lrow[2] = {0.f, 0.f};
+    uint32_t qf[4][4];
+    const float L2E = 1.4426950408889634f;
+
+    for (int j = 0; j < nkv; ++j) {
+        const int st = j & 1;
+        if (j + 1 < nkv) {
+            load_tile(Kb, (j + 1) * AT_K, sKa[st ^ 1]);
+            load_tile(Vb, (j + 1) * AT_K, sVa[st ^ 1]);
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+        asm volatile("cp.async.wait_group 1;" ::: "memory");
+        __syncthreads();
+        if (j == 0) {
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk) {
+                const int mi = lane >> 3, row = warp * 16 + (lane & 7) + (mi & 1) * 8, ch = kk * 2 + (mi >> 1);
+                ldm_x4(sQa + swz(row, ch), qf[kk]);
+            }
+        }
+        // S = Q K^T for this warp's 16 rows x 64 keys
+        float s[8][4];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) s[i][0] = s[i][1] = s[i][2] = s[i][3] = 0.f;
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+#pragma unroll
+            for (int np = 0; np < 4; ++np) {
+                uint32_t b[4];
+                const int mi = lane >> 3, key = np * 16 + (lane & 7) + (mi >> 1) * 8, ch = kk * 2 + (mi & 1);
+                ldm_x4(sKa[st] + swz(key, ch), b);
+                mma16816(s[2 * np], qf[kk], b[0], b[1]);
+                mma16816(s[2 * np + 1], qf[kk], b[2], b[3]);
+            }
+        }
+        // mask keys past T, then the online softmax (log2 domain)
+        const int kbase = j * AT_K;
+        float mx[2] = {mrow[0], mrow[1]};
+#pragma unroll
+        for (int nt = 0; nt < 8; ++nt) {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const int key = kbase + nt * 8 + tig * 2 + (e & 1);
+                float v = key < T ? s[nt][e] * L2E : -INFINITY;
+                s[nt][e] = v;
+                mx[e >> 1] = fmaxf(mx[e >> 1], v);
+            }
+        }
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+            mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 1));
+            mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 2));
+        }
+        float alpha[2];
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+            alpha[r] = exp2f(mrow[r] - mx[r]);
+            mrow[r] = mx[r];
+            lrow[r] *= alpha[r];
+        }
+#pragma unroll
+        for (int nt = 0; nt < 8; ++nt) {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const float p = exp2f(s[nt][e] - mx[e >> 1]);
+                s[nt][e] = p;
+                lrow[e >> 1] += p;
+                o[nt][e] *= alpha[e >> 1];
+            }
+        }
+        // O += P V
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+            uint32_t a[4];
+            a[0] = pack_h2(s[2 * kk][0], s[2 * kk][1]);
+            a[1] = pack_h2(s[2 * kk][2], s[2 * kk][3]);
+            a[2] = pack_h2(s[2 * kk + 1][0], s[2 * kk + 1][1]);
+            a[3] = pack_h2(s[2 * kk + 1][2], s[2 * kk + 1][3]);
+#pragma unroll
+            for (int np = 0; np < 4; ++np) {
+                uint32_t b[4];
+                const int mi = lane >> 3, key = kk * 16 + (lane & 7) + (mi & 1) * 8, ch = np * 2 + (mi >> 1);
+                ldm_x4_t(sVa[st] + swz(key, ch), b);
+                mma16816(o[2 * np], a, b[0], b[1]);
+                mma16816(o[2 * np + 1], a, b[2], b[3]);
+            }
+        }
+        __syncthreads();
+    }
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+        lrow[r] += __shfl_xor_sync(0xffffffffu, lrow[r], 1);
+        lrow[r] += __shfl_xor_sync(0xffffffffu, lrow[r], 2);
+    }
+    const int D = H * AT_D;
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+        const int t = q0 + warp * 16 + g + r * 8;
+        if (t >= T) continue;
+        const float inv = 1.0f / lrow[r];
+        float* dst = out + (size_t(w) * T + t) * D + h * AT_D;
+#pragma unroll
+        for (int nt = 0; nt < 8; ++nt)
+            *reinterpret_cast<float2*>(dst + nt * 8 + tig * 2) = make_float2(o[nt][2 * r] * inv, o[nt][2 * r + 1] * inv);
+    }
+}
+
+unsigned grid_stride(size_t total, int tpb) {
+    size_t g = (total + tpb - 1) / tpb;
+    return unsigned(g > 148 * 16 ? 148 * 16 : (g ? g : 1));
+}
+
+template <int MODE>
+cudaError_t rows_quant_mode(const float* x, const float* add, float* xout, const float* lw, const float* lb, int m,
+                            int k, int m_pad, uint16_t* q16, float* dT, float* uT, float* yout, cudaStream_t s) {
+    const unsigned grid = unsigned((size_t(m_pad) * 32 + 255) / 256);
+    const int nch = k / 128;
+    if (MODE == RQ_PLAIN || MODE == RQ_GELU || nch <= 4)
+        return launch_pdl(k_rows_quant<MODE, 4>, dim3(grid), dim3(256), 0, s, x, add, xout, lw, lb, m, k, m_pad, q16,
+                          dT, uT, yout);
+    if (nch <= 8)
+        return launch_pdl(k_rows_quant<MODE, 8>, dim3(grid), dim3(256), 0, s, x, add, xout, lw, lb, m, k, m_pad, q16,
+                          dT, uT, yout);
+    if (nch <= 16)
+        return launch_pdl(k_rows_quant<MODE, 16>, dim3(grid), dim3(256), 0, s, x, add, xout, lw, lb, m, k, m_pad,
+                          q16, dT, uT, yout);
+    return cudaErrorInvalidValue;
+}
+
+}  // namespace
+
+cudaError_t launch_rows_quant(int mode, const float* x, const float* add, float* xout, const float* lw,
+                              const float* lb, int m, int k, int m_pad, uint16_t* q16, float* dT, float* uT,
+                              float* yout, cudaStream_t s) {
+    if (k % 128) return cudaErrorInvalidValue;
+    if (m_pad <= 0) return cudaSuccess;
+    switch (mode) {
+        case RQ_PLAIN: return rows_quant_mode<RQ_PLAIN>(x, add, xout, lw, lb, m, k, m_pad, q16, dT, uT, yout, s);
+        case RQ_GELU: return rows_quant_mode<RQ_GELU>(x, add, xout, lw, lb, m, k, m_pad, q16, dT, uT, yout, s);
+        case RQ_LN: return rows_quant_mode<RQ_LN>(x, add, xout, lw, lb, m, k, m_pad, q16, dT, uT, yout, s);
+        case RQ_ADD_LN: return rows_quant_mode<RQ_ADD_LN>(x, add, xout, lw, lb, m, k, m_pad, q16, dT, uT, yout, s);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+cudaError_t launch_im2col3(const float* in, int n_win, int c_in, int t_in, int t_out, int stride, size_t sw,
+                           size_t sc, size_t st, float* out, cudaStream_t s) {
+    const size_t total = size_t(n_win) * t_out * c_in * 3;
+    if (!total) return cudaSuccess;
+    k_im2col3<<<grid_stride(total, 256), 256, 0, s>>>(in, n_win, c_in, t_in, t_out, stride, sw, sc, st, out);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_bias_gelu(float* y, size_t rows, int cols, const float* bias, const float* pos, int t_per_win,
+                             cudaStream_t s) {
+    const size_t total = rows * size_t(cols);
+    if (!total) return cudaSuccess;
+    k_bias_gelu<<<grid_stride(total, 256), 256, 0, s>>>(y, rows, cols, bias, pos, t_per_win);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_to_heads(const float* src, int ld, int col0, int n_win, int T, int H, float scale, __half* dst,
+                            cudaStream_t s) {
+    const size_t total = size_t(n_win) * H * T * 16;
+    if (!total) return cudaSuccess;
+    k_to_heads<<<grid_stride(total, 256), 256, 0, s>>>(src, ld, col0, n_win, T, H, scale, dst);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_attention(const __half* Qh, const __half* Kh, const __half* Vh, int n_win, int T, int H,
+                             float* out, cudaStream_t s) {
+    if (!n_win || !T || !H) return cudaSuccess;
+    dim3 grid((T + AT_Q - 1) / AT_Q, H, n_win);
+    return launch_pdl(k_attn, grid, dim3(AT_THREADS), 0, s, Qh, Kh, Vh, T, H, out);
+}
+
+}  // namespace rwq

@@ -1,0 +1,93 @@
+"""The Whisper encoder forward on the GPU (mirror of the reference's
+``encoder::encode``, src/encoder.rs:180-234, over the C ABI ``rwq_encoder_*``).
+
+    enc = Encoder(n_mels, n_ctx, n_state, n_head, n_layer, tensors)
+    out = enc.encode(mel)        # mel [W, n_mels, 2*n_ctx] CUDA f32 -> [W, n_ctx, n_state]
+
+``tensors`` maps whisper.cpp names to f32 arrays (dense tensors) or
+``(dtype, raw_ggml_bytes, n, k)`` tuples (the six quantized linears of each
+block), the layout :func:`rusty_whisper_b200.synth.encoder_tensors` makes.
+"""
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+
+from . import _lib
+from .quant import _ptr, _stream_ptr, _torch
+
+
+class Encoder:
+    def __init__(self, n_mels: int, n_ctx: int, n_state: int, n_head: int, n_layer: int, tensors: dict | None = None,
+                 device: int | None = None):
+        torch = _torch()
+        self.device = torch.cuda.current_device() if device is None else device
+        self.shape = (n_mels, n_ctx, n_state, n_head, n_layer)
+        h = ctypes.c_void_p()
+        with torch.cuda.device(self.device):
+            _lib.check(_lib.lib().rwq_encoder_new(n_mels, n_ctx, n_state, n_head, n_layer, ctypes.byref(h)))
+        self._h = h
+        for name, t in (tensors or {}).items():
+            self.set(name, t)
+
+    def set(self, name: str, t) -> None:
+        torch = _torch()
+        with torch.cuda.device(self.device):
+            if isinstance(t, tuple):
+                dtype, raw, n, k = t
+                raw = np.ascontiguousarray(raw, np.uint8)
+                _lib.check(_lib.lib().rwq_encoder_set_quant(self._h, name.encode(), dtype,
+                                                            raw.ctypes.data_as(ctypes.c_void_p), raw.nbytes, n, k))
+            else:
+                a = np.ascontiguousarray(t, np.float32).ravel()
+                _lib.check(_lib.lib().rwq_encoder_set_dense(self._h, name.encode(), a.ctypes.data_as(ctypes.c_void_p),
+                                                            a.size))
+
+    def encode(self, mel, out=None):
+        """mel: CUDA f32 [W, n_mels, 2*n_ctx] -> [W, n_ctx, n_state] (async on
+        the current stream)."""
+        torch = _torch()
+        n_mels, n_ctx, n_state = self.shape[:3]
+        if mel.dim() == 2:
+            mel = mel.unsqueeze(0)
+        assert mel.is_cuda and mel.dtype == torch.float32 and tuple(mel.shape[1:]) == (n_mels, 2 * n_ctx)
+        mel = mel.contiguous()
+        if out is None:
+            out = torch.empty((mel.shape[0], n_ctx, n_state), device=mel.device, dtype=torch.float32)
+        _lib.check(_lib.lib().rwq_encoder_encode_dev(self._h, _ptr(mel), mel.shape[0], _ptr(out),
+                                                     ctypes.c_void_p(_stream_ptr(mel.device))))
+        return out
+
+    def encode_host(self, mel: np.ndarray) -> np.ndarray:
+        """Host buffers through rwq_encoder_encode (copies inside the call)."""
+        n_mels, n_ctx, n_state = self.shape[:3]
+        mel = np.ascontiguousarray(mel, np.float32).reshape(-1, n_mels, 2 * n_ctx)
+        out = np.zeros((mel.shape[0], n_ctx, n_state), np.float32)
+        _lib.check(_lib.lib().rwq_encoder_encode(self._h, mel.ctypes.data_as(ctypes.c_void_p), mel.shape[0],
+                                                 out.ctypes.data_as(ctypes.c_void_p)))
+        return out
+
+    def free(self) -> None:
+        if getattr(self, "_h", None):
+            _lib.lib().rwq_encoder_free(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass
+
+
+def multi_head_attention(q, k, v, n_head: int):
+    """Non-causal attention over projected q, k, v (CUDA f32 [W, t, n_state]
+    or [t, n_state]); encoder.rs:107-121."""
+    torch = _torch()
+    squeeze = q.dim() == 2
+    q, k, v = (x.unsqueeze(0) if squeeze else x for x in (q, k, v))
+    q, k, v = (x.contiguous() for x in (q, k, v))
+    out = torch.empty_like(q)
+    _lib.check(_lib.lib().rwq_attention_dev(_ptr(q), _ptr(k), _ptr(v), q.shape[0], q.shape[1], q.shape[2], n_head,
+                                            _ptr(out), ctypes.c_void_p(_stream_ptr(q.device))))
+    return out[0] if squeeze else out

@@ -147,3 +147,107 @@ def speechlike_window(seed: int, n: int = AUDIO_WINDOW) -> np.ndarray:
     for a, ln in zip(starts, lens):
         x[int(a):int(a) + int(ln)] = 0.0
     return x.astype(np.float32)
+
+
+# ---------------------------------------------------------------- models
+def quantize_q5_1(x: np.ndarray) -> np.ndarray:
+    """rusty_whisper's Q5_1 test quantizer (quant.rs:1088-1113), vectorised:
+    per block d = (max-min)/31, q = round((x-min)/d) clamped to [0, 31]
+    (half away from zero), d and min as f16 (half-up, model.rs:90-115)."""
+    x = np.ascontiguousarray(x, np.float32).reshape(-1, QK)
+    mn = x.min(axis=1)
+    mx = x.max(axis=1)
+    d = ((mx - mn) / np.float32(31.0)).astype(np.float32)
+    inv = np.where(d > 0, np.float32(1.0) / np.where(d > 0, d, np.float32(1.0)), np.float32(0.0)).astype(np.float32)
+    t = ((x - mn[:, None]).astype(np.float32) * inv[:, None]).astype(np.float32)
+    q = np.clip(np.floor(t.astype(np.float64) + 0.5), 0, 31).astype(np.uint32)
+    nblk = x.shape[0]
+    raw = np.zeros((nblk, 24), np.uint8)
+    db = f32_to_f16_bits(d)
+    mb = f32_to_f16_bits(mn.astype(np.float32))
+    raw[:, 0], raw[:, 1] = db & 0xFF, db >> 8
+    raw[:, 2], raw[:, 3] = mb & 0xFF, mb >> 8
+    qh = np.zeros(nblk, np.uint32)
+    for e in range(QK):
+        qh |= ((q[:, e] >> 4) & 1) << np.uint32(e)
+    raw[:, 4:8] = qh.view(np.uint8).reshape(nblk, 4)
+    raw[:, 8:24] = ((q[:, :16] & 0xF) | ((q[:, 16:] & 0xF) << 4)).astype(np.uint8)
+    return raw.reshape(-1)
+
+
+def quantize_q8_0(x: np.ndarray) -> np.ndarray:
+    """rusty_whisper's Q8_0 test quantizer (quant.rs:1071-1083), vectorised:
+    per block d = amax/127, q = round(x/d) half away from zero, clamped to
+    [-127, 127], d as f16 (half-up)."""
+    x = np.ascontiguousarray(x, np.float32).reshape(-1, QK)
+    amax = np.abs(x).max(axis=1)
+    d = (amax / np.float32(127.0)).astype(np.float32)
+    inv = np.where(d > 0, np.float32(1.0) / np.where(d > 0, d, np.float32(1.0)), np.float32(0.0)).astype(np.float32)
+    t = (x * inv[:, None]).astype(np.float32).astype(np.float64)
+    q = np.clip(np.sign(t) * np.floor(np.abs(t) + 0.5), -127, 127).astype(np.int8)
+    nblk = x.shape[0]
+    raw = np.zeros((nblk, 34), np.uint8)
+    db = f32_to_f16_bits(d)
+    raw[:, 0], raw[:, 1] = db & 0xFF, db >> 8
+    raw[:, 2:] = q.view(np.uint8)
+    return raw.reshape(-1)
+
+
+def encoder_tensors(n_mels: int, n_ctx: int, n_state: int, n_layer: int, dtype: int, seed: int) -> dict:
+    """Random-init whisper encoder tensors by their whisper.cpp names
+    (encoder.rs:130-234): dense entries are f32 arrays, the six linears of
+    each block ``(dtype, raw, n, k)``.  Weights ~ N(0, 0.02); Q5_1 and Q8_0
+    linears are quantized from them with the reference's own test
+    quantizers (BASELINE config 3 is Q5_1), the other formats get random
+    codes with d ~ U(0.001, 0.02); LayerNorm weights 1 + N(0, 0.02);
+    positions are whisper's sinusoids."""
+    t = {}
+    ctr = [seed * 1000]
+
+    def nrm(*shape, std=0.02, mean=0.0):
+        ctr[0] += 1
+        return normal(ctr[0], int(np.prod(shape)), mean, std).reshape(shape)
+
+    def lin(n, k):
+        ctr[0] += 1
+        if dtype == Q5_1:
+            return (dtype, quantize_q5_1(normal(ctr[0], n * k, 0.0, 0.02)), n, k)
+        if dtype == Q8_0:
+            return (dtype, quantize_q8_0(normal(ctr[0], n * k, 0.0, 0.02)), n, k)
+        return (dtype, random_blocks(dtype, n, k, ctr[0]), n, k)
+
+    t["encoder.conv1.weight"] = nrm(n_state, n_mels, 3)
+    t["encoder.conv1.bias"] = nrm(n_state)
+    t["encoder.conv2.weight"] = nrm(n_state, n_state, 3)
+    t["encoder.conv2.bias"] = nrm(n_state)
+    half = n_state // 2
+    inc = np.log(10000.0) / (half - 1)
+    inv = np.exp(-inc * np.arange(half))
+    ang = np.arange(n_ctx)[:, None] * inv[None, :]
+    t["encoder.positional_embedding"] = np.concatenate([np.sin(ang), np.cos(ang)], axis=1).astype(np.float32)
+    for l in range(n_layer):
+        p = f"encoder.blocks.{l}"
+        t[f"{p}.attn_ln.weight"] = nrm(n_state, mean=1.0)
+        t[f"{p}.attn_ln.bias"] = nrm(n_state)
+        t[f"{p}.attn.query.weight"] = lin(n_state, n_state)
+        t[f"{p}.attn.query.bias"] = nrm(n_state)
+        t[f"{p}.attn.key.weight"] = lin(n_state, n_state)
+        t[f"{p}.attn.value.weight"] = lin(n_state, n_state)
+        t[f"{p}.attn.value.bias"] = nrm(n_state)
+        t[f"{p}.attn.out.weight"] = lin(n_state, n_state)
+        t[f"{p}.attn.out.bias"] = nrm(n_state)
+        t[f"{p}.mlp_ln.weight"] = nrm(n_state, mean=1.0)
+        t[f"{p}.mlp_ln.bias"] = nrm(n_state)
+        t[f"{p}.mlp.0.weight"] = lin(4 * n_state, n_state)
+        t[f"{p}.mlp.0.bias"] = nrm(4 * n_state)
+        t[f"{p}.mlp.2.weight"] = lin(n_state, 4 * n_state)
+        t[f"{p}.mlp.2.bias"] = nrm(n_state)
+    t["encoder.ln_post.weight"] = nrm(n_state, mean=1.0)
+    t["encoder.ln_post.bias"] = nrm(n_state)
+    return t
+
+
+def encoder_mel(n_windows: int, n_mels: int, n_frames: int, seed: int) -> np.ndarray:
+    """Log-mel input of BASELINE config 3: N(-0.5, 0.3) clamped to [-1.5, 1.5]."""
+    x = normal(seed, n_windows * n_mels * n_frames, -0.5, 0.3)
+    return np.clip(x, -1.5, 1.5).astype(np.float32).reshape(n_windows, n_mels, n_frames)

@@ -1,0 +1,101 @@
+"""GPU encoder forward against the oracle's restatement of the reference
+encoder (encoder.rs:48-234), marked gpu.
+
+Bars:
+  * attention (f16 tensor-core MMAs, f32 accumulation) against the f32
+    reference multi_head_attention: |err| <= 5e-3 * max|ref| per window;
+  * the whole encoder (int8 activations between layers, so a rounding
+    difference upstream can move an activation code by one): relative RMS
+    error <= 2e-2 per window and max |err| <= 0.25 on LayerNorm-scaled
+    outputs, against the oracle encoder run on the same tensors;
+  * batch composition: a window encodes the same alone or in a batch
+    (within 1e-4 relative RMS; the conv stem's SGEMM may pick
+    size-dependent kernels).
+"""
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def torch_mod():
+    import torch
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    from rusty_whisper_b200 import quant
+    quant.init(0)
+    return torch
+
+
+def _rel_rms(got, ref):
+    got = np.asarray(got, np.float64)
+    ref = np.asarray(ref, np.float64)
+    return float(np.sqrt(np.mean((got - ref) ** 2)) / max(np.sqrt(np.mean(ref ** 2)), 1e-30))
+
+
+@pytest.mark.parametrize("w,t,n_head", [(1, 37, 1), (2, 100, 4), (1, 1500, 2), (3, 64, 8)])
+def test_attention_matches_reference_mha(torch_mod, w, t, n_head):
+    import oracle
+    from rusty_whisper_b200 import encoder, synth
+    d = 64 * n_head
+    q = synth.normal(1 + t, w * t * d).reshape(w, t, d)
+    k = synth.normal(2 + t, w * t * d).reshape(w, t, d)
+    v = synth.normal(3 + t, w * t * d).reshape(w, t, d)
+    out = encoder.multi_head_attention(*(torch_mod.from_numpy(x).cuda() for x in (q, k, v)), n_head)
+    got = out.cpu().numpy()
+    for i in range(w):
+        ref = oracle.mha(q[i], k[i], v[i], n_head)
+        err = np.max(np.abs(got[i] - ref))
+        assert err <= 5e-3 * np.max(np.abs(ref)), (i, err)
+
+
+def _encoder_pair(dtype, n_ctx=100, n_state=256, n_head=4, n_layer=2, n_mels=80, seed=5):
+    import oracle
+    from rusty_whisper_b200 import encoder, synth
+    t = synth.encoder_tensors(n_mels, n_ctx, n_state, n_layer, dtype, seed)
+    gpu = encoder.Encoder(n_mels, n_ctx, n_state, n_head, n_layer, t)
+    cpu = oracle.Encoder(n_mels, n_ctx, n_state, n_head, n_layer, t)
+    return gpu, cpu
+
+
+@pytest.mark.parametrize("dtype", [7, 2, 8])
+def test_encoder_matches_oracle(torch_mod, dtype):
+    from rusty_whisper_b200 import synth
+    gpu, cpu = _encoder_pair(dtype)
+    mel = synth.encoder_mel(3, 80, 200, 11)
+    got = gpu.encode(torch_mod.from_numpy(mel).cuda()).cpu().numpy()
+    assert np.all(np.isfinite(got))
+    for i in range(3):
+        ref = cpu.encode(mel[i])
+        assert _rel_rms(got[i], ref) <= 2e-2, (dtype, i, _rel_rms(got[i], ref))
+        assert np.max(np.abs(got[i] - ref)) <= 0.25, (dtype, i, np.max(np.abs(got[i] - ref)))
+
+
+def test_encoder_batch_composition_and_host_path(torch_mod):
+    from rusty_whisper_b200 import synth
+    gpu, _ = _encoder_pair(7, n_ctx=128, n_layer=1)
+    mel = synth.encoder_mel(4, 80, 256, 12)
+    batch = gpu.encode(torch_mod.from_numpy(mel).cuda()).cpu().numpy()
+    one = gpu.encode(torch_mod.from_numpy(mel[2:3]).cuda()).cpu().numpy()
+    assert _rel_rms(one[0], batch[2]) <= 1e-4
+    host = gpu.encode_host(mel)
+    assert _rel_rms(host, batch) <= 1e-4
+
+
+def test_encoder_errors(torch_mod):
+    from rusty_whisper_b200 import encoder, synth
+    with pytest.raises(ValueError):
+        encoder.Encoder(80, 16, 200, 4, 1)          # head dim 50
+    e = encoder.Encoder(80, 16, 256, 4, 1)
+    with pytest.raises(ValueError):
+        e.set("encoder.conv1.bias", np.zeros(3, np.float32))        # wrong size
+    with pytest.raises(ValueError):
+        e.set("encoder.blocks.5.attn.key.weight", (7, b"", 256, 256))   # no such block
+    with pytest.raises(ValueError):
+        e.encode(torch_mod.zeros((1, 80, 32), device="cuda"))        # tensors missing
+    t = synth.encoder_tensors(80, 16, 256, 1, 7, 3)
+    for name, v in t.items():
+        e.set(name, v)
+    out = e.encode(torch_mod.zeros((2, 80, 32), device="cuda"))
+    assert out.shape == (2, 16, 256) and bool(torch_mod.isfinite(out).all())
