@@ -239,6 +239,7 @@ def run_ours(args, rank, world, local_rank):
     gemv = run_gemv(args, dev, quant, w_np, hbm_peak, stream) if args.only == "all" else None
     e2e = run_e2e(args, dev, quant, W, acts_np, world) if args.only == "all" else None
     frontend = run_frontend(args, dev, hbm_peak, stream, rank, world) if args.only == "all" else None
+    enc = run_encoder(args, dev, tc_peak, stream, rank, world) if args.only == "all" else None
     clk.__exit__(None, None, None)
 
     if rank != 0:
@@ -263,6 +264,7 @@ def run_ours(args, rank, world, local_rank):
         },
         "gemv": gemv,
         "frontend": frontend,
+        "encoder": enc,
         "e2e": e2e,
         "clocks": clk.summary(),
     }
@@ -316,6 +318,77 @@ def run_frontend(args, dev, hbm_peak, stream, rank, world):
         res["cpu_baseline"] = {"audio_s_per_s": round(30.0 / tc, 1), "s_per_window": round(tc, 4),
                                "cores": threads, "kind": "port",
                                "sample": "2 windows of 30 s through the C restatement of audio.rs:147-198"}
+    return res
+
+
+ENC_BASE = dict(n_mels=80, n_ctx=1500, n_state=512, n_head=8, n_layer=6)   # whisper-base
+
+
+def encoder_flops(n_ctx, n_state, n_layer, n_mels):
+    """Per window: quantized linears 2*T*(4*D*D + 2*D*4D) per block,
+    attention 2 * 2*T*T*D per block, conv stem 2*(2T*D*3*n_mels + T*D*3*D)."""
+    T, D = n_ctx, n_state
+    lin = n_layer * 2.0 * T * (4 * D * D + 8 * D * D)
+    att = n_layer * 4.0 * T * T * D
+    conv = 2.0 * (2 * T * D * 3 * n_mels + T * D * 3 * D)
+    return lin, att, conv
+
+
+def run_encoder(args, dev, tc_peak, stream, rank, world):
+    """whisper-base encoder forward, Q5_1 linears from
+    N(0, 0.02) weights, batch of 8 windows (log-mel N(-0.5, 0.3) clamped
+    to +-1.5), audio-seconds per second; the oracle's restatement of
+    encoder.rs timed beside it on the host cores (one window)."""
+    import torch
+    from rusty_whisper_b200 import encoder
+    cfg = ENC_BASE
+    n_win = 8
+    t = synth.encoder_tensors(cfg["n_mels"], cfg["n_ctx"], cfg["n_state"], cfg["n_layer"], 7, seed=3)
+    enc = encoder.Encoder(cfg["n_mels"], cfg["n_ctx"], cfg["n_state"], cfg["n_head"], cfg["n_layer"], t)
+    mel_np = synth.encoder_mel(n_win, cfg["n_mels"], 2 * cfg["n_ctx"], seed=100 + rank)
+    mel = torch.from_numpy(mel_np).to(dev)
+    out = torch.empty((n_win, cfg["n_ctx"], cfg["n_state"]), device=dev)
+    for _ in range(2):
+        enc.encode(mel, out)
+    torch.cuda.synchronize()
+    reps = max(3, min(args.steps, 10))
+    times = []
+    for _ in range(reps):
+        torch.cuda._sleep(GATE_CYCLES)
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        enc.encode(mel, out)
+        e1.record(stream)
+        times.append((e0, e1))
+    torch.cuda.synchronize()
+    from rusty_whisper_b200 import quant
+    quant.stream_check()
+    tb = statistics.median(a.elapsed_time(b) for a, b in times) / 1e3
+    lin, att, conv = encoder_flops(cfg["n_ctx"], cfg["n_state"], cfg["n_layer"], cfg["n_mels"])
+    fl = n_win * (lin + att + conv)
+    res = {"workload": f"BASELINE config 3: whisper-base encoder (6 x d512/8 heads/FFN 2048), Q5_1 linears, "
+                       f"batch {n_win} windows of 30 s",
+           "audio_s_per_s": round(world * n_win * 30.0 / tb, 1), "ms_per_batch": round(tb * 1e3, 3),
+           "windows_per_s": round(world * n_win / tb, 2),
+           "gflop_per_window": {"quant_linear": round(lin / 1e9, 2), "attention": round(att / 1e9, 2),
+                                "conv": round(conv / 1e9, 2)},
+           "achieved_TFLOPs": round(fl / tb / 1e12, 1), "frac_of_measured_bf16": round(fl / tb / 1e12 / tc_peak, 4),
+           "kernels": "k_rows_quant, k_gemm_fold, k_to_heads, k_attn, cuBLAS SGEMM + k_im2col3/k_bias_gelu (conv)",
+           "gpu_launches_per_batch": 4 + 6 * 13 + 1,
+           "data": "synthetic (seeded): random-init weights N(0, 0.02) quantized to Q5_1, mel N(-0.5, 0.3)"}
+    if rank == 0 and world == 1 and not args.no_cpu:
+        import oracle
+        threads = oracle.default_threads()
+        ref = oracle.Encoder(cfg["n_mels"], cfg["n_ctx"], cfg["n_state"], cfg["n_head"], cfg["n_layer"], t)
+        ref.encode(mel_np[0], threads=threads)       # first call: the reference's cold weight path
+        t0 = time.perf_counter()
+        ref.encode(mel_np[1], threads=threads)
+        tc = time.perf_counter() - t0
+        res["cpu_baseline"] = {"audio_s_per_s": round(30.0 / tc, 2), "s_per_window": round(tc, 3), "cores": threads,
+                               "kind": "port", "tier": oracle.TIER_NAMES[oracle.dispatch_tier()],
+                               "sample": "1 window (second call, packed weights) through the C++ restatement "
+                                         "of encoder.rs:180-234"}
     return res
 
 
@@ -515,8 +588,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
-    ap.add_argument("--only", default="all", choices=["all", "gemm"],
-                    help="gemm: skip the GEMV and e2e legs (short runs for profiling)")
+    ap.add_argument("--only", default="all", choices=["all", "gemm", "encoder"],
+                    help="gemm: skip the GEMV, e2e, front-end and encoder legs; encoder: only the config-3 "
+                         "encoder leg (short runs for profiling)")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", 1))
@@ -533,6 +607,16 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local_rank))
     try:
+        if args.only == "encoder":
+            import torch
+            from rusty_whisper_b200 import quant
+            torch.cuda.set_device(local_rank)
+            quant.init(local_rank)
+            res = run_encoder(args, torch.device("cuda", local_rank), peaks()[1], torch.cuda.current_stream(), rank,
+                              world)
+            if rank == 0:
+                print(json.dumps({"encoder": res}), flush=True)
+            return
         run_ours(args, rank, world, local_rank)
     finally:
         if world > 1:
