@@ -248,6 +248,40 @@ int rwq_encoder_encode(rwq_encoder* e, const float* mel, int64_t n_windows, floa
 int rwq_attention_dev(const float* q, const float* k, const float* v, int64_t n_windows, int64_t t, int64_t n_state,
                       int64_t n_head, float* out, void* stream);
 
+/* ---- Decoder ---------------------------------------------------------------
+ * Replaces the KV-cached `decoder::Decoder` (reference src/decoder.rs:36-321)
+ * for S decode streams stepping in lockstep on the device.  A stream decodes
+ * one window; streams of the same window (beams) share its cross K/V.
+ * Tensors are set by their whisper.cpp names: dense f32 (LayerNorms,
+ * biases, positional_embedding [n_text_ctx][n_state]) and raw ggml blocks
+ * for the token embedding (also the tied logits matrix) and the ten
+ * linears of each block.  Head dim 64, n_state % 128 == 0.  A decoder
+ * serves one call at a time. */
+typedef struct rwq_decoder rwq_decoder;
+
+int rwq_decoder_new(int n_vocab, int n_text_ctx, int n_state, int n_head, int n_layer, rwq_decoder** out);
+int rwq_decoder_free(rwq_decoder* d);
+int rwq_decoder_set_dense(rwq_decoder* d, const char* name, const float* data, int64_t count);
+int rwq_decoder_set_quant(rwq_decoder* d, const char* name, int dtype, const uint8_t* raw, size_t raw_len, int64_t n,
+                          int64_t k);
+/* `Decoder::new` for every stream (decoder.rs:36-69): cross K/V from the
+ * windows' encoder outputs enc_out [n_windows][n_audio][n_state] (device),
+ * stream i decoding window stream_window[i] (host array; NULL: stream i ->
+ * window i), self caches cleared.  Asynchronous on `stream`. */
+int rwq_decoder_begin(rwq_decoder* d, const float* enc_out, int64_t n_windows, int64_t n_audio,
+                      const int32_t* stream_window, int64_t n_streams, void* stream);
+/* One position for every stream (`forward(&[token])`, decoder.rs:102-206):
+ * tokens [S] (device).  logits [S][n_vocab] (device, may be NULL) gets the
+ * tied projection; best [S] (device, may be NULL) the greedy choice: the
+ * first maximum over ids < limit if it beats logits[limit], else limit
+ * (decoder.rs:345-365); limit < 0: the first maximum of the whole row.
+ * With both NULL the projection is skipped (prompt positions).  A full
+ * context (n_text_ctx positions) returns RWQ_ERR_ARG (decoder.rs:115-120). */
+int rwq_decoder_step(rwq_decoder* d, const int32_t* tokens, float* logits, int32_t* best, int32_t limit, void* stream);
+/* `Decoder::reset` (decoder.rs:83-91): positions restart at 0, cross K/V kept. */
+int rwq_decoder_reset(rwq_decoder* d);
+int rwq_decoder_n_past(const rwq_decoder* d, int64_t* n_past);
+
 #ifdef __cplusplus
 }
 #endif

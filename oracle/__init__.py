@@ -76,6 +76,13 @@ def lib():
             "orc_gelu": (None, [P, sz]),
             "orc_mha": (i32, [P, i32, P, P, i32, i32, i32, i32, P, i32]),
             "orc_conv1d": (i32, [P, i32, i32, P, i32, i32, P, i32, P, i32]),
+            "orc_decoder_new": (P, [i32, i32, i32, i32, i32]),
+            "orc_decoder_free": (None, [P]),
+            "orc_decoder_set": (i32, [P, ctypes.c_char_p, P, sz, i32, P, i32, i32]),
+            "orc_decoder_begin": (i32, [P, P, i32, i32]),
+            "orc_decoder_forward": (i32, [P, P, i32, P, i32]),
+            "orc_decoder_reset": (None, [P]),
+            "orc_decoder_n_past": (i32, [P]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(L, name)
@@ -365,4 +372,49 @@ class Encoder:
     def __del__(self):
         if getattr(self, "_h", None):
             lib().orc_encoder_free(self._h)
+            self._h = None
+
+
+class Decoder:
+    """decoder.rs:36-321: ``begin(enc_out)`` is ``Decoder::new`` (cross K/V
+    of one window), ``forward(tokens)`` returns logits [n_tok, n_vocab]."""
+
+    def __init__(self, n_vocab: int, n_ctx: int, n_state: int, n_head: int, n_layer: int, tensors: dict):
+        self.shape = (n_vocab, n_ctx, n_state, n_head, n_layer)
+        self._h = lib().orc_decoder_new(n_vocab, n_ctx, n_state, n_head, n_layer)
+        if not self._h:
+            raise ValueError("bad decoder shape")
+        self._keep = []
+        for name, t in tensors.items():
+            if isinstance(t, tuple):
+                dtype, raw, n, k = t
+                raw = np.ascontiguousarray(raw, np.uint8)
+                self._keep.append(raw)
+                rc = lib().orc_decoder_set(self._h, name.encode(), None, 0, dtype, _p(raw), n, k)
+            else:
+                a = np.ascontiguousarray(t, np.float32).ravel()
+                self._keep.append(a)
+                rc = lib().orc_decoder_set(self._h, name.encode(), _p(a), a.size, 0, None, 0, 0)
+            _check(rc, f"decoder_set({name})")
+
+    def begin(self, enc_out: np.ndarray, threads: int = 0) -> None:
+        e = np.ascontiguousarray(enc_out, np.float32)
+        _check(lib().orc_decoder_begin(self._h, _p(e), e.shape[0], threads), "decoder_begin")
+
+    def forward(self, tokens, threads: int = 0) -> np.ndarray:
+        t = np.ascontiguousarray(tokens, np.int32).ravel()
+        out = np.zeros((t.size, self.shape[0]), np.float32)
+        _check(lib().orc_decoder_forward(self._h, _p(t), t.size, _p(out), threads), "decoder_forward")
+        return out
+
+    def reset(self) -> None:
+        lib().orc_decoder_reset(self._h)
+
+    @property
+    def n_past(self) -> int:
+        return lib().orc_decoder_n_past(self._h)
+
+    def __del__(self):
+        if getattr(self, "_h", None):
+            lib().orc_decoder_free(self._h)
             self._h = None

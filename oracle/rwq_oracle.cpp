@@ -23,6 +23,8 @@
 //   * encoder graph: conv stem, pre-LN attention / MLP blocks, ln_post,
 //     with layernorm, tanh-GELU, softmax, conv1d and matmul
 //                                      encoder.rs:48-234, tensor.rs:75-100, 274-370
+//   * KV-cached decoder: cross K/V, causal self-attention, cross-attention,
+//     MLP, final LN, tied logits          decoder.rs:36-321
 //   * test helpers: LCG test_matrix, rand_byte, quantize_q8_0, quantize_q5_1
 //                                      quant.rs:1071-1123, quant.rs:1131-1135
 //
@@ -1324,5 +1326,192 @@ int orc_conv1d(const float* in, int in_ch, int t, const float* w, int out_ch, in
     conv1d_ref(in, in_ch, t, w, out_ch, kernel, bias, stride, out, threads <= 0 ? n_threads_default() : threads);
     return 0;
 }
+
+}  // extern "C"
+
+// ================================================================ decoder
+// Restatement of the reference's KV-cached decoder (decoder.rs:36-321):
+// cross K/V projected once per window, per step token + learned position,
+// n_text_layer x {causal self-attention over the cache, cross-attention,
+// MLP}, final LN, tied logits through the token-embedding matrix.
+namespace {
+
+struct OrcDecLayer {
+    std::vector<float> attn_ln_w, attn_ln_b, q_b, v_b, o_b, x_ln_w, x_ln_b, xq_b, xv_b, xo_b, mlp_ln_w, mlp_ln_b,
+        fc1_b, fc2_b;
+    OrcQTensor *q = nullptr, *k = nullptr, *v = nullptr, *o = nullptr, *xq = nullptr, *xk = nullptr, *xv = nullptr,
+               *xo = nullptr, *fc1 = nullptr, *fc2 = nullptr;
+};
+
+struct OrcDecoder {
+    int n_vocab, n_ctx, n_state, n_head, n_layer;
+    std::vector<float> pos, ln_w, ln_b;
+    OrcQTensor* emb = nullptr;
+    std::vector<OrcDecLayer> layers;
+    // state
+    int n_audio = 0;
+    std::vector<std::vector<float>> cross_k, cross_v, self_k, self_v;
+    int n_past = 0;
+    bool owns = true;
+    ~OrcDecoder() {
+        if (!owns) return;
+        delete emb;
+        for (auto& l : layers)
+            for (OrcQTensor* t : {l.q, l.k, l.v, l.o, l.xq, l.xk, l.xv, l.xo, l.fc1, l.fc2}) delete t;
+    }
+};
+
+}  // namespace
+
+extern "C" {
+
+void* orc_decoder_new(int n_vocab, int n_ctx, int n_state, int n_head, int n_layer) {
+    if (n_vocab <= 0 || n_ctx <= 0 || n_state <= 0 || n_head <= 0 || n_state % n_head || n_layer < 0) return nullptr;
+    auto* d = new OrcDecoder{n_vocab, n_ctx, n_state, n_head, n_layer, {}, {}, {}, nullptr, {}, 0, {}, {}, {}, {}, 0,
+                             true};
+    d->layers.resize(size_t(n_layer));
+    d->self_k.resize(size_t(n_layer));
+    d->self_v.resize(size_t(n_layer));
+    return d;
+}
+
+void orc_decoder_free(void* h) { delete static_cast<OrcDecoder*>(h); }
+
+int orc_decoder_set(void* h, const char* name, const float* dense, size_t count, int dtype, const uint8_t* raw, int n,
+                    int k) {
+    auto* d = static_cast<OrcDecoder*>(h);
+    std::string s(name);
+    auto vec = [&](std::vector<float>& dst) {
+        if (!dense) return -1;
+        dst.assign(dense, dense + count);
+        return 0;
+    };
+    auto quant = [&](OrcQTensor*& dst) {
+        if (!raw) return -1;
+        delete dst;
+        dst = static_cast<OrcQTensor*>(orc_qtensor_new(dtype, raw, n, k));
+        return dst ? 0 : -1;
+    };
+    if (s == "decoder.positional_embedding") return vec(d->pos);
+    if (s == "decoder.ln.weight") return vec(d->ln_w);
+    if (s == "decoder.ln.bias") return vec(d->ln_b);
+    if (s == "decoder.token_embedding.weight") return quant(d->emb);
+    const std::string pre = "decoder.blocks.";
+    if (s.compare(0, pre.size(), pre) != 0) return -1;
+    const size_t dot = s.find('.', pre.size());
+    if (dot == std::string::npos) return -1;
+    const int l = std::atoi(s.substr(pre.size(), dot - pre.size()).c_str());
+    if (l < 0 || l >= d->n_layer) return -1;
+    OrcDecLayer& L = d->layers[size_t(l)];
+    const std::string f = s.substr(dot + 1);
+    if (f == "attn_ln.weight") return vec(L.attn_ln_w);
+    if (f == "attn_ln.bias") return vec(L.attn_ln_b);
+    if (f == "attn.query.weight") return quant(L.q);
+    if (f == "attn.query.bias") return vec(L.q_b);
+    if (f == "attn.key.weight") return quant(L.k);
+    if (f == "attn.value.weight") return quant(L.v);
+    if (f == "attn.value.bias") return vec(L.v_b);
+    if (f == "attn.out.weight") return quant(L.o);
+    if (f == "attn.out.bias") return vec(L.o_b);
+    if (f == "cross_attn_ln.weight") return vec(L.x_ln_w);
+    if (f == "cross_attn_ln.bias") return vec(L.x_ln_b);
+    if (f == "cross_attn.query.weight") return quant(L.xq);
+    if (f == "cross_attn.query.bias") return vec(L.xq_b);
+    if (f == "cross_attn.key.weight") return quant(L.xk);
+    if (f == "cross_attn.value.weight") return quant(L.xv);
+    if (f == "cross_attn.value.bias") return vec(L.xv_b);
+    if (f == "cross_attn.out.weight") return quant(L.xo);
+    if (f == "cross_attn.out.bias") return vec(L.xo_b);
+    if (f == "mlp_ln.weight") return vec(L.mlp_ln_w);
+    if (f == "mlp_ln.bias") return vec(L.mlp_ln_b);
+    if (f == "mlp.0.weight") return quant(L.fc1);
+    if (f == "mlp.0.bias") return vec(L.fc1_b);
+    if (f == "mlp.2.weight") return quant(L.fc2);
+    if (f == "mlp.2.bias") return vec(L.fc2_b);
+    return -1;
+}
+
+// Decoder::new (decoder.rs:36-69): cross K (no bias) and V per layer from
+// the window's encoder output [n_audio][n_state]; clears the self cache.
+int orc_decoder_begin(void* h, const float* enc_out, int n_audio, int threads) {
+    auto* d = static_cast<OrcDecoder*>(h);
+    if (!d || n_audio <= 0) return -1;
+    if (threads <= 0) threads = n_threads_default();
+    d->n_audio = n_audio;
+    d->cross_k.assign(size_t(d->n_layer), {});
+    d->cross_v.assign(size_t(d->n_layer), {});
+    for (int l = 0; l < d->n_layer; ++l) {
+        OrcDecLayer& L = d->layers[size_t(l)];
+        if (!L.xk || !L.xv) return -2;
+        d->cross_k[size_t(l)].assign(size_t(n_audio) * d->n_state, 0.f);
+        d->cross_v[size_t(l)].assign(size_t(n_audio) * d->n_state, 0.f);
+        linear_q(L.xk, enc_out, n_audio, nullptr, d->cross_k[size_t(l)].data(), threads);
+        linear_q(L.xv, enc_out, n_audio, L.xv_b.data(), d->cross_v[size_t(l)].data(), threads);
+    }
+    for (auto& v : d->self_k) v.clear();
+    for (auto& v : d->self_v) v.clear();
+    d->n_past = 0;
+    return 0;
+}
+
+// Decoder::forward (decoder.rs:102-206, 315-321): logits [n_tok][n_vocab].
+int orc_decoder_forward(void* h, const int32_t* tokens, int n_tok, float* logits, int threads) {
+    auto* d = static_cast<OrcDecoder*>(h);
+    if (!d || n_tok <= 0 || !d->emb) return -1;
+    if (d->n_past + n_tok > d->n_ctx) return -3;   // context overflow (decoder.rs:115-120)
+    if (threads <= 0) threads = n_threads_default();
+    const int D = d->n_state, H = d->n_head;
+    std::vector<float> x(size_t(n_tok) * D), cur, q(x.size()), kn(x.size()), vn(x.size()), att(x.size()),
+        proj(x.size());
+    const int nbe = D / QK, bb = block_bytes(d->emb->dtype);
+    for (int i = 0; i < n_tok; ++i) {
+        if (tokens[i] < 0 || tokens[i] >= d->n_vocab) return -4;
+        dequant_row_scalar(d->emb->dtype, d->emb->raw.data() + size_t(tokens[i]) * nbe * bb, size_t(nbe),
+                           &x[size_t(i) * D]);
+        for (int c = 0; c < D; ++c) x[size_t(i) * D + c] += d->pos[size_t(d->n_past + i) * D + c];
+    }
+    for (int l = 0; l < d->n_layer; ++l) {
+        OrcDecLayer& L = d->layers[size_t(l)];
+        cur = x;
+        ln_rows(cur.data(), size_t(n_tok), D, L.attn_ln_w.data(), L.attn_ln_b.data());
+        linear_q(L.q, cur.data(), n_tok, L.q_b.data(), q.data(), threads);
+        linear_q(L.k, cur.data(), n_tok, nullptr, kn.data(), threads);
+        linear_q(L.v, cur.data(), n_tok, L.v_b.data(), vn.data(), threads);
+        d->self_k[size_t(l)].insert(d->self_k[size_t(l)].end(), kn.begin(), kn.end());
+        d->self_v[size_t(l)].insert(d->self_v[size_t(l)].end(), vn.begin(), vn.end());
+        const int t_kv = d->n_past + n_tok;
+        mha_ref(q.data(), n_tok, d->self_k[size_t(l)].data(), d->self_v[size_t(l)].data(), t_kv, D, H, true,
+                att.data(), 1);
+        linear_q(L.o, att.data(), n_tok, L.o_b.data(), proj.data(), threads);
+        for (size_t i = 0; i < x.size(); ++i) x[i] += proj[i];
+        cur = x;
+        ln_rows(cur.data(), size_t(n_tok), D, L.x_ln_w.data(), L.x_ln_b.data());
+        linear_q(L.xq, cur.data(), n_tok, L.xq_b.data(), q.data(), threads);
+        mha_ref(q.data(), n_tok, d->cross_k[size_t(l)].data(), d->cross_v[size_t(l)].data(), d->n_audio, D, H, false,
+                att.data(), 1);
+        linear_q(L.xo, att.data(), n_tok, L.xo_b.data(), proj.data(), threads);
+        for (size_t i = 0; i < x.size(); ++i) x[i] += proj[i];
+        cur = x;
+        ln_rows(cur.data(), size_t(n_tok), D, L.mlp_ln_w.data(), L.mlp_ln_b.data());
+        std::vector<float> hb(size_t(n_tok) * L.fc1->n);
+        linear_q(L.fc1, cur.data(), n_tok, L.fc1_b.data(), hb.data(), threads);
+        gelu_n(hb.data(), hb.size());
+        linear_q(L.fc2, hb.data(), n_tok, L.fc2_b.data(), proj.data(), threads);
+        for (size_t i = 0; i < x.size(); ++i) x[i] += proj[i];
+    }
+    d->n_past += n_tok;
+    ln_rows(x.data(), size_t(n_tok), D, d->ln_w.data(), d->ln_b.data());
+    linear_q(d->emb, x.data(), n_tok, nullptr, logits, threads);
+    return 0;
+}
+
+void orc_decoder_reset(void* h) {
+    auto* d = static_cast<OrcDecoder*>(h);
+    for (auto& v : d->self_k) v.clear();
+    for (auto& v : d->self_v) v.clear();
+    d->n_past = 0;
+}
+
+int orc_decoder_n_past(void* h) { return static_cast<OrcDecoder*>(h)->n_past; }
 
 }  // extern "C"

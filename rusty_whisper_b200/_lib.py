@@ -71,6 +71,14 @@ SIGNATURES = {
     "rwq_encoder_encode_dev": (_I, [_P, _P, _L, _P, _P]),
     "rwq_encoder_encode": (_I, [_P, _P, _L, _P]),
     "rwq_attention_dev": (_I, [_P, _P, _P, _L, _L, _L, _L, _P, _P]),
+    "rwq_decoder_new": (_I, [_I, _I, _I, _I, _I, ctypes.POINTER(_P)]),
+    "rwq_decoder_free": (_I, [_P]),
+    "rwq_decoder_set_dense": (_I, [_P, ctypes.c_char_p, _P, _L]),
+    "rwq_decoder_set_quant": (_I, [_P, ctypes.c_char_p, _I, _P, _SZ, _L, _L]),
+    "rwq_decoder_begin": (_I, [_P, _P, _L, _L, _P, _L, _P]),
+    "rwq_decoder_step": (_I, [_P, _P, _P, _P, ctypes.c_int32, _P]),
+    "rwq_decoder_reset": (_I, [_P]),
+    "rwq_decoder_n_past": (_I, [_P, ctypes.POINTER(_L)]),
 }
 
 _lib = None

@@ -286,6 +286,14 @@ int rwq::gemm_quantized(const ActsView& v, rwq_qtensor* w, const float* bias, fl
     return run_quantized(v, true, w, bias, out, s, nullptr, ws->err);
 }
 
+int rwq::linear_acts(const ActsView& v, bool gemm, rwq_qtensor* w, const float* bias, float* out, cudaStream_t s) {
+    Workspace* ws = nullptr;
+    int rc = get_workspace(s, &ws);
+    if (rc) return rc;
+    if (v.k != w->w.k) return fail(RWQ_ERR_SHAPE, "linear inner dims: %d vs %d", v.k, w->w.k);
+    return run_quantized(v, gemm, w, bias, out, s, nullptr, ws->err);
+}
+
 int rwq::with_stream_scratch(cudaStream_t s, size_t bytes, const std::function<int(void*)>& fn) {
     Workspace* ws = nullptr;
     int rc = get_workspace(s, &ws);

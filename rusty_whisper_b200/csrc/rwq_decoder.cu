@@ -1,0 +1,472 @@
+// rwq_decoder.cu -- the device-resident KV-cached decoder behind the C ABI
+// (rwq_decoder_* in include/rwq.h): the reference's Decoder
+// (decoder.rs:36-321) for S decode streams in lockstep.  A stream decodes
+// one window; several streams may share a window (beams), and then share
+// its cross-attention K/V (the reference shares them through an Arc,
+// decoder.rs:18-24, 71-79).
+//
+//   begin   cross K (no bias) and V of every layer from the windows'
+//           encoder outputs: one quantization, two GEMMs per layer, f16
+//           heads [win][H][n_audio][64] kept in HBM for the whole decode;
+//   step    token + position -> per layer {[residual +] LN + quantize ->
+//           Q, K, V linears -> KV-cache append -> self-attention ->
+//           quantize -> out linear -> residual + LN + quantize -> cross Q
+//           -> cross-attention (per window: K/V read once for all its
+//           streams) -> quantize -> cross out -> residual + LN + quantize
+//           -> fc1 -> GELU + quantize -> fc2} -> residual + final LN +
+//           quantize -> tied logits -> greedy argmax.
+// Linears take the integer-MMA GEMV for up to 8 streams and the tensor-core
+// GEMM above that; everything stays on the device between steps.
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <mutex>
+#include <string>
+#include <vector>
+#include "../../include/rwq.h"
+#include "rwq_common.cuh"
+#include "rwq_decoder.h"
+#include "rwq_encoder.h"
+#include "rwq_internal.h"
+
+namespace {
+
+int dfail(int code, const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    rwq::set_last_error(buf);
+    return code;
+}
+
+#define DEC_CUDA(call, what)                                                                               \
+    do {                                                                                                   \
+        cudaError_t e_ = (call);                                                                           \
+        if (e_ != cudaSuccess)                                                                             \
+            return dfail(e_ == cudaErrorMemoryAllocation ? RWQ_ERR_NOMEM : RWQ_ERR_CUDA, "%s: %s", what,   \
+                         cudaGetErrorString(e_));                                                          \
+    } while (0)
+
+#define DEC_RC(call)             \
+    do {                         \
+        int rc_ = (call);        \
+        if (rc_) return rc_;     \
+    } while (0)
+
+size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+struct DLayer {
+    rwq_qtensor *q = nullptr, *k = nullptr, *v = nullptr, *o = nullptr;
+    rwq_qtensor *xq = nullptr, *xk = nullptr, *xv = nullptr, *xo = nullptr;
+    rwq_qtensor *fc1 = nullptr, *fc2 = nullptr;
+};
+
+const char* const kDenseLayer[] = {"attn_ln.weight", "attn_ln.bias", "attn.query.bias", "attn.value.bias",
+                                   "attn.out.bias", "cross_attn_ln.weight", "cross_attn_ln.bias",
+                                   "cross_attn.query.bias", "cross_attn.value.bias", "cross_attn.out.bias",
+                                   "mlp_ln.weight", "mlp_ln.bias", "mlp.2.bias"};
+
+}  // namespace
+
+struct rwq_decoder {
+    int device = 0;
+    int n_vocab = 0, n_ctx = 0, n_state = 0, n_head = 0, n_layer = 0, n_ff = 0;
+    std::map<std::string, float*> dense;
+    std::map<std::string, size_t> dense_len;
+    std::vector<DLayer> layers;
+    rwq_qtensor* emb = nullptr;
+    // decode state (begin)
+    int n_streams = 0, n_windows = 0, n_audio = 0, n_past = 0, n_cross_groups = 0;
+    void* state = nullptr;        // caches, group tables and step buffers
+    size_t state_bytes = 0;
+    __half *cross_k = nullptr, *cross_v = nullptr, *self_k = nullptr, *self_v = nullptr;
+    int *cross_kv = nullptr, *cross_off = nullptr, *cross_streams = nullptr;
+    int *self_kv = nullptr, *self_off = nullptr;   // identity tables for self-attention
+    float *x = nullptr, *tmp = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *att = nullptr, *h = nullptr,
+          *logits = nullptr;
+    int32_t* best = nullptr;
+    rwq::ActsView gemv, gemm;
+    std::mutex mu;
+};
+
+namespace {
+
+std::string lname(int l, const char* f) { return "decoder.blocks." + std::to_string(l) + "." + f; }
+
+rwq_qtensor** quant_slot(rwq_decoder* d, const std::string& name, int64_t* wn, int64_t* wk) {
+    const int64_t D = d->n_state, F = d->n_ff;
+    *wn = D;
+    *wk = D;
+    if (name == "decoder.token_embedding.weight") {
+        *wn = d->n_vocab;
+        return &d->emb;
+    }
+    const std::string pre = "decoder.blocks.";
+    if (name.compare(0, pre.size(), pre) != 0) return nullptr;
+    const size_t dot = name.find('.', pre.size());
+    if (dot == std::string::npos) return nullptr;
+    const std::string idx = name.substr(pre.size(), dot - pre.size());
+    if (idx.empty() || idx.find_first_not_of("0123456789") != std::string::npos) return nullptr;
+    const int l = std::atoi(idx.c_str());
+    if (l < 0 || l >= d->n_layer) return nullptr;
+    DLayer& L = d->layers[size_t(l)];
+    const std::string f = name.substr(dot + 1);
+    if (f == "attn.query.weight") return &L.q;
+    if (f == "attn.key.weight") return &L.k;
+    if (f == "attn.value.weight") return &L.v;
+    if (f == "attn.out.weight") return &L.o;
+    if (f == "cross_attn.query.weight") return &L.xq;
+    if (f == "cross_attn.key.weight") return &L.xk;
+    if (f == "cross_attn.value.weight") return &L.xv;
+    if (f == "cross_attn.out.weight") return &L.xo;
+    if (f == "mlp.0.weight") { *wn = F; return &L.fc1; }
+    if (f == "mlp.2.weight") { *wk = F; return &L.fc2; }
+    return nullptr;
+}
+
+int check_ready(rwq_decoder* d) {
+    for (auto& kv : d->dense_len)
+        if (!d->dense.count(kv.first)) return dfail(RWQ_ERR_ARG, "decoder tensor '%s' was not set", kv.first.c_str());
+    if (!d->emb) return dfail(RWQ_ERR_ARG, "decoder.token_embedding.weight was not set");
+    for (int l = 0; l < d->n_layer; ++l) {
+        const DLayer& L = d->layers[size_t(l)];
+        for (rwq_qtensor* t : {L.q, L.k, L.v, L.o, L.xq, L.xk, L.xv, L.xo, L.fc1, L.fc2})
+            if (!t) return dfail(RWQ_ERR_ARG, "decoder block %d: a linear weight was not set", l);
+    }
+    return RWQ_OK;
+}
+
+// Lay out (base == nullptr: size) the decode state for S streams, W windows.
+size_t layout_state(rwq_decoder* d, int S, int W, int n_audio, int n_groups, uint8_t* base) {
+    const size_t D = size_t(d->n_state), F = size_t(d->n_ff), H = size_t(d->n_head), L = size_t(d->n_layer);
+    const size_t kmax = std::max(D, F), m_pad = align_up(size_t(S), 256);
+    size_t off = 0;
+    auto take = [&](size_t bytes) {
+        uint8_t* p = base ? base + off : nullptr;
+        off = align_up(off + bytes, 256);
+        return p;
+    };
+    d->cross_k = reinterpret_cast<__half*>(take(L * W * H * n_audio * 64 * 2));
+    d->cross_v = reinterpret_cast<__half*>(take(L * W * H * n_audio * 64 * 2));
+    d->self_k = reinterpret_cast<__half*>(take(L * S * H * d->n_ctx * 64 * 2));
+    d->self_v = reinterpret_cast<__half*>(take(L * S * H * d->n_ctx * 64 * 2));
+    d->cross_kv = reinterpret_cast<int*>(take(size_t(n_groups) * 4));
+    d->cross_off = reinterpret_cast<int*>(take(size_t(n_groups + 1) * 4));
+    d->cross_streams = reinterpret_cast<int*>(take(size_t(S) * 4));
+    d->self_kv = reinterpret_cast<int*>(take(size_t(S) * 4));
+    d->self_off = reinterpret_cast<int*>(take(size_t(S + 1) * 4));
+    d->x = reinterpret_cast<float*>(take(S * D * 4));
+    d->tmp = reinterpret_cast<float*>(take(S * D * 4));
+    d->q = reinterpret_cast<float*>(take(S * D * 4));
+    d->k = reinterpret_cast<float*>(take(S * D * 4));
+    d->v = reinterpret_cast<float*>(take(S * D * 4));
+    d->att = reinterpret_cast<float*>(take(S * D * 4));
+    d->h = reinterpret_cast<float*>(take(S * F * 4));
+    d->logits = reinterpret_cast<float*>(take(S * size_t(d->n_vocab) * 4));
+    d->best = reinterpret_cast<int32_t*>(take(size_t(S) * 4));
+    rwq::ActsView& g = d->gemv;
+    g = rwq::ActsView();
+    g.m = S;
+    g.q8 = reinterpret_cast<int8_t*>(take(S * kmax));
+    g.d = reinterpret_cast<float*>(take(S * (kmax / 32) * 4));
+    g.sum = reinterpret_cast<int32_t*>(take(S * (kmax / 32) * 4));
+    g.u = reinterpret_cast<float*>(take(S * (kmax / 32) * 4));
+    rwq::ActsView& m = d->gemm;
+    m = rwq::ActsView();
+    m.m = S;
+    m.m_pad = int(m_pad);
+    m.q16 = reinterpret_cast<uint16_t*>(take(S * kmax * 2));
+    m.dT = reinterpret_cast<float*>(take((kmax / 32) * m_pad * 4));
+    m.uT = reinterpret_cast<float*>(take((kmax / 32) * m_pad * 4));
+    return off;
+}
+
+rwq::ActsView with_k(rwq::ActsView v, int k) {
+    v.k = k;
+    v.nb = k / rwq::QK;
+    return v;
+}
+
+// Row transform + quantize into the layout the linears of this step read.
+int rows(rwq_decoder* d, int mode, const float* x, const float* add, float* xout, const char* ln, int k,
+         cudaStream_t s, int layer = -1) {
+    const int S = d->n_streams;
+    const bool gemm = S > rwq::GEMV_MAX_M;
+    const rwq::ActsView a = with_k(gemm ? d->gemm : d->gemv, k);
+    const float* w = nullptr;
+    const float* b = nullptr;
+    if (ln) {
+        const std::string base = layer >= 0 ? lname(layer, ln) : std::string(ln);
+        w = d->dense[base + ".weight"];
+        b = d->dense[base + ".bias"];
+    }
+    DEC_CUDA(rwq::launch_rows_quant_v(mode, x, add, xout, w, b, S, k, gemm ? &a : nullptr, gemm ? nullptr : &a, nullptr,
+                                      s),
+             "decoder row transform");
+    return RWQ_OK;
+}
+
+int linear(rwq_decoder* d, rwq_qtensor* w, const float* bias, float* out, cudaStream_t s) {
+    const bool gemm = d->n_streams > rwq::GEMV_MAX_M;
+    const rwq::ActsView a = with_k(gemm ? d->gemm : d->gemv, rwq::weight_of(w).k);
+    return rwq::linear_acts(a, gemm, w, bias, out, s);
+}
+
+}  // namespace
+
+extern "C" {
+
+int rwq_decoder_new(int n_vocab, int n_ctx, int n_state, int n_head, int n_layer, rwq_decoder** out) {
+    if (!out) return dfail(RWQ_ERR_ARG, "out is null");
+    *out = nullptr;
+    if (n_vocab <= 0 || n_ctx <= 0 || n_state <= 0 || n_head <= 0 || n_layer < 0)
+        return dfail(RWQ_ERR_ARG, "bad decoder shape");
+    if (n_state % n_head || n_state / n_head != 64)
+        return dfail(RWQ_ERR_ARG, "head dim must be 64 (n_state %d, n_head %d)", n_state, n_head);
+    if (n_state % 128) return dfail(RWQ_ERR_ARG, "n_state must be a multiple of 128 (got %d)", n_state);
+    auto* d = new rwq_decoder;
+    cudaGetDevice(&d->device);
+    d->n_vocab = n_vocab;
+    d->n_ctx = n_ctx;
+    d->n_state = n_state;
+    d->n_head = n_head;
+    d->n_layer = n_layer;
+    d->n_ff = 4 * n_state;
+    d->layers.resize(size_t(n_layer));
+    d->dense_len["decoder.positional_embedding"] = size_t(n_ctx) * n_state;
+    d->dense_len["decoder.ln.weight"] = size_t(n_state);
+    d->dense_len["decoder.ln.bias"] = size_t(n_state);
+    for (int l = 0; l < n_layer; ++l) {
+        for (const char* f : kDenseLayer) d->dense_len[lname(l, f)] = size_t(n_state);
+        d->dense_len[lname(l, "mlp.0.bias")] = size_t(d->n_ff);
+    }
+    *out = d;
+    return RWQ_OK;
+}
+
+int rwq_decoder_free(rwq_decoder* d) {
+    if (!d) return RWQ_OK;
+    int prev = 0;
+    cudaGetDevice(&prev);
+    if (prev != d->device) cudaSetDevice(d->device);
+    for (auto& kv : d->dense) cudaFree(kv.second);
+    for (auto& L : d->layers)
+        for (rwq_qtensor* t : {L.q, L.k, L.v, L.o, L.xq, L.xk, L.xv, L.xo, L.fc1, L.fc2}) rwq_qtensor_free(t);
+    rwq_qtensor_free(d->emb);
+    cudaFree(d->state);
+    if (prev != d->device) cudaSetDevice(prev);
+    delete d;
+    return RWQ_OK;
+}
+
+int rwq_decoder_set_dense(rwq_decoder* d, const char* name, const float* data, int64_t count) {
+    if (!d || !name || !data) return dfail(RWQ_ERR_ARG, "null argument");
+    std::lock_guard<std::mutex> g(d->mu);
+    auto it = d->dense_len.find(name);
+    if (it == d->dense_len.end()) return dfail(RWQ_ERR_ARG, "'%s' is not a dense decoder tensor", name);
+    if (count < 0 || size_t(count) != it->second)
+        return dfail(RWQ_ERR_SHAPE, "'%s': %lld elements, expected %zu", name, (long long)count, it->second);
+    float*& dst = d->dense[name];
+    if (!dst) DEC_CUDA(cudaMalloc(&dst, it->second * 4), "cudaMalloc(dense tensor)");
+    DEC_CUDA(cudaMemcpy(dst, data, it->second * 4, cudaMemcpyHostToDevice), "copy dense tensor");
+    return RWQ_OK;
+}
+
+int rwq_decoder_set_quant(rwq_decoder* d, const char* name, int dtype, const uint8_t* raw, size_t raw_len, int64_t n,
+                          int64_t k) {
+    if (!d || !name) return dfail(RWQ_ERR_ARG, "null argument");
+    std::lock_guard<std::mutex> g(d->mu);
+    int64_t wn = 0, wk = 0;
+    rwq_qtensor** slot = quant_slot(d, name, &wn, &wk);
+    if (!slot) return dfail(RWQ_ERR_ARG, "'%s' is not a quantized decoder matrix", name);
+    if (n != wn || k != wk)
+        return dfail(RWQ_ERR_SHAPE, "'%s': [%lld, %lld], expected [%lld, %lld]", name, (long long)n, (long long)k,
+                     (long long)wn, (long long)wk);
+    rwq_qtensor* t = nullptr;
+    DEC_RC(rwq_qtensor_new(raw, raw_len, dtype, n, k, &t));
+    rwq_qtensor_free(*slot);
+    *slot = t;
+    return RWQ_OK;
+}
+
+int rwq_decoder_begin(rwq_decoder* d, const float* enc_out, int64_t n_windows, int64_t n_audio,
+                      const int32_t* stream_window, int64_t n_streams, void* stream) {
+    if (!d) return dfail(RWQ_ERR_ARG, "decoder is null");
+    if (n_windows <= 0 || n_audio <= 0 || n_streams <= 0) return dfail(RWQ_ERR_ARG, "bad begin shape");
+    if (!enc_out || (reinterpret_cast<uintptr_t>(enc_out) & 15))
+        return dfail(RWQ_ERR_ARG, "encoder output must be a 16-byte aligned device pointer");
+    if (n_windows > (1 << 20) || n_streams > (1 << 20) || n_audio > 8192) return dfail(RWQ_ERR_ARG, "begin too large");
+    std::lock_guard<std::mutex> g(d->mu);
+    DEC_RC(check_ready(d));
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev != d->device) return dfail(RWQ_ERR_ARG, "decoder lives on device %d, current device is %d", d->device, dev);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const int S = int(n_streams), W = int(n_windows), T = int(n_audio), D = d->n_state, H = d->n_head;
+    // stream -> window map and the cross-attention groups (<= DEC_MAX_G
+    // streams of one window each)
+    std::vector<int> win(static_cast<size_t>(S));
+    for (int i = 0; i < S; ++i) {
+        win[size_t(i)] = stream_window ? stream_window[i] : (W == S ? i : -1);
+        if (win[size_t(i)] < 0 || win[size_t(i)] >= W)
+            return dfail(RWQ_ERR_ARG, "stream %d maps to window %d of %d", i, win[size_t(i)], W);
+    }
+    std::vector<int> gkv, goff(1, 0), gst;
+    for (int w = 0; w < W; ++w) {
+        int in_group = 0;
+        for (int i = 0; i < S; ++i) {
+            if (win[size_t(i)] != w) continue;
+            if (in_group == rwq::DEC_MAX_G) {
+                gkv.push_back(w);
+                goff.push_back(int(gst.size()));
+                in_group = 0;
+            }
+            gst.push_back(i);
+            ++in_group;
+        }
+        if (in_group) {
+            gkv.push_back(w);
+            goff.push_back(int(gst.size()));
+        }
+    }
+    const int NG = int(gkv.size());
+    const size_t need = layout_state(d, S, W, T, NG, nullptr);
+    if (d->state_bytes < need) {
+        DEC_CUDA(cudaStreamSynchronize(s), "cudaStreamSynchronize");
+        cudaFree(d->state);
+        d->state = nullptr;
+        d->state_bytes = 0;
+        DEC_CUDA(cudaMalloc(&d->state, need), "cudaMalloc(decoder state)");
+        d->state_bytes = need;
+    }
+    layout_state(d, S, W, T, NG, static_cast<uint8_t*>(d->state));
+    d->n_streams = S;
+    d->n_windows = W;
+    d->n_audio = T;
+    d->n_cross_groups = NG;
+    d->n_past = 0;
+    std::vector<int> sid(static_cast<size_t>(S)), soff(static_cast<size_t>(S) + 1);
+    for (int i = 0; i <= S; ++i) {
+        if (i < S) sid[size_t(i)] = i;
+        soff[size_t(i)] = i;
+    }
+    DEC_CUDA(cudaMemcpyAsync(d->cross_kv, gkv.data(), gkv.size() * 4, cudaMemcpyHostToDevice, s), "copy groups");
+    DEC_CUDA(cudaMemcpyAsync(d->cross_off, goff.data(), goff.size() * 4, cudaMemcpyHostToDevice, s), "copy groups");
+    DEC_CUDA(cudaMemcpyAsync(d->cross_streams, gst.data(), gst.size() * 4, cudaMemcpyHostToDevice, s), "copy groups");
+    DEC_CUDA(cudaMemcpyAsync(d->self_kv, sid.data(), sid.size() * 4, cudaMemcpyHostToDevice, s), "copy groups");
+    DEC_CUDA(cudaMemcpyAsync(d->self_off, soff.data(), soff.size() * 4, cudaMemcpyHostToDevice, s), "copy groups");
+    // cross K/V (decoder.rs:41-56): quantize the encoder output once, then
+    // two GEMMs per layer, windows in chunks to bound the scratch.
+    const int per = std::max(1, int((size_t(1) << 30) / (size_t(T) * D * 14)));
+    for (int w0 = 0; w0 < W; w0 += per) {
+        const int nw = std::min(per, W - w0);
+        const int M = nw * T;
+        const size_t m_pad = align_up(size_t(M), 256);
+        const size_t kv_b = align_up(size_t(M) * D * 4, 256), q_b = align_up(size_t(M) * D * 2, 256),
+                     sc_b = align_up(size_t(D / 32) * m_pad * 4, 256);
+        int rc = rwq::with_stream_scratch(s, 2 * kv_b + q_b + 2 * sc_b, [&](void* buf) {
+            uint8_t* p = static_cast<uint8_t*>(buf);
+            float* kt = reinterpret_cast<float*>(p);
+            float* vt = reinterpret_cast<float*>(p + kv_b);
+            rwq::ActsView a;
+            a.m = M;
+            a.k = D;
+            a.nb = D / 32;
+            a.m_pad = int(m_pad);
+            a.q16 = reinterpret_cast<uint16_t*>(p + 2 * kv_b);
+            a.dT = reinterpret_cast<float*>(p + 2 * kv_b + q_b);
+            a.uT = reinterpret_cast<float*>(p + 2 * kv_b + q_b + sc_b);
+            DEC_CUDA(rwq::launch_rows_quant_v(rwq::RQ_PLAIN, enc_out + size_t(w0) * T * D, nullptr, nullptr, nullptr,
+                                              nullptr, M, D, &a, nullptr, nullptr, s),
+                     "quantize encoder output");
+            for (int l = 0; l < d->n_layer; ++l) {
+                const DLayer& L = d->layers[size_t(l)];
+                DEC_RC(rwq::gemm_quantized(a, L.xk, nullptr, kt, s));
+                DEC_RC(rwq::gemm_quantized(a, L.xv, d->dense[lname(l, "cross_attn.value.bias")], vt, s));
+                const size_t lo = (size_t(l) * W + w0) * H * size_t(T) * 64;
+                DEC_CUDA(rwq::launch_to_heads(kt, D, 0, nw, T, H, 1.0f, d->cross_k + lo, s), "cross k heads");
+                DEC_CUDA(rwq::launch_to_heads(vt, D, 0, nw, T, H, 1.0f, d->cross_v + lo, s), "cross v heads");
+            }
+            return int(RWQ_OK);
+        });
+        if (rc) return rc;
+    }
+    return RWQ_OK;
+}
+
+int rwq_decoder_step(rwq_decoder* d, const int32_t* tokens, float* logits, int32_t* best, int32_t limit,
+                     void* stream) {
+    if (!d) return dfail(RWQ_ERR_ARG, "decoder is null");
+    if (!tokens) return dfail(RWQ_ERR_ARG, "tokens is null");
+    std::lock_guard<std::mutex> g(d->mu);
+    if (!d->n_streams) return dfail(RWQ_ERR_ARG, "rwq_decoder_begin was not called");
+    if (d->n_past >= d->n_ctx)
+        return dfail(RWQ_ERR_ARG, "decoder context overflow: %d + 1 > %d", d->n_past, d->n_ctx);   // decoder.rs:115-120
+    if (limit >= d->n_vocab) return dfail(RWQ_ERR_ARG, "limit %d >= n_vocab %d", limit, d->n_vocab);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const int S = d->n_streams, D = d->n_state, H = d->n_head, F = d->n_ff, P = d->n_past;
+    DEC_CUDA(rwq::launch_embed(rwq::weight_of(d->emb), tokens, S, d->dense["decoder.positional_embedding"] + size_t(P) * D,
+                               d->x, s),
+             "embed");
+    const size_t self_layer = size_t(S) * H * d->n_ctx * 64, cross_layer = size_t(d->n_windows) * H * d->n_audio * 64;
+    for (int l = 0; l < d->n_layer; ++l) {
+        const DLayer& L = d->layers[size_t(l)];
+        auto B = [&](const char* f) { return d->dense[lname(l, f)]; };
+        // causal self-attention over the cache (decoder.rs:140-171)
+        DEC_RC(rows(d, l ? rwq::RQ_ADD_LN : rwq::RQ_LN, d->x, d->tmp, d->x, "attn_ln", D, s, l));
+        DEC_RC(linear(d, L.q, B("attn.query.bias"), d->q, s));
+        DEC_RC(linear(d, L.k, nullptr, d->k, s));
+        DEC_RC(linear(d, L.v, B("attn.value.bias"), d->v, s));
+        __half* kc = d->self_k + size_t(l) * self_layer;
+        __half* vc = d->self_v + size_t(l) * self_layer;
+        DEC_CUDA(rwq::launch_kv_append(d->k, d->v, S, H, d->n_ctx, P, kc, vc, s), "kv append");
+        DEC_CUDA(rwq::launch_attn_dec(d->q, kc, vc, size_t(d->n_ctx) * 64, P + 1, H, S, d->self_kv, d->self_off,
+                                      d->self_kv, d->att, s),
+                 "self attention");
+        DEC_RC(rows(d, rwq::RQ_PLAIN, d->att, nullptr, nullptr, nullptr, D, s));
+        DEC_RC(linear(d, L.o, B("attn.out.bias"), d->tmp, s));
+        // cross-attention to the window's K/V (decoder.rs:173-188)
+        DEC_RC(rows(d, rwq::RQ_ADD_LN, d->x, d->tmp, d->x, "cross_attn_ln", D, s, l));
+        DEC_RC(linear(d, L.xq, B("cross_attn.query.bias"), d->q, s));
+        DEC_CUDA(rwq::launch_attn_dec(d->q, d->cross_k + size_t(l) * cross_layer, d->cross_v + size_t(l) * cross_layer,
+                                      size_t(d->n_audio) * 64, d->n_audio, H, d->n_cross_groups, d->cross_kv,
+                                      d->cross_off, d->cross_streams, d->att, s),
+                 "cross attention");
+        DEC_RC(rows(d, rwq::RQ_PLAIN, d->att, nullptr, nullptr, nullptr, D, s));
+        DEC_RC(linear(d, L.xo, B("cross_attn.out.bias"), d->tmp, s));
+        // MLP (encoder.rs:154-172)
+        DEC_RC(rows(d, rwq::RQ_ADD_LN, d->x, d->tmp, d->x, "mlp_ln", D, s, l));
+        DEC_RC(linear(d, L.fc1, B("mlp.0.bias"), d->h, s));
+        DEC_RC(rows(d, rwq::RQ_GELU, d->h, nullptr, nullptr, nullptr, F, s));
+        DEC_RC(linear(d, L.fc2, B("mlp.2.bias"), d->tmp, s));
+    }
+    d->n_past = P + 1;
+    if (!logits && !best) return RWQ_OK;   // a prompt position: no projection needed
+    // final LN (decoder.rs:200-204), tied logits (decoder.rs:315-321)
+    DEC_RC(rows(d, d->n_layer ? rwq::RQ_ADD_LN : rwq::RQ_LN, d->x, d->tmp, d->x, "decoder.ln", D, s));
+    float* lg = logits ? logits : d->logits;
+    DEC_RC(linear(d, d->emb, nullptr, lg, s));
+    if (best) DEC_CUDA(rwq::launch_argmax(lg, S, d->n_vocab, limit, best, s), "argmax");
+    return RWQ_OK;
+}
+
+int rwq_decoder_reset(rwq_decoder* d) {
+    if (!d) return dfail(RWQ_ERR_ARG, "decoder is null");
+    std::lock_guard<std::mutex> g(d->mu);
+    d->n_past = 0;   // the self-attention cache is overwritten from position 0
+    return RWQ_OK;
+}
+
+int rwq_decoder_n_past(const rwq_decoder* d, int64_t* n_past) {
+    if (!d || !n_past) return dfail(RWQ_ERR_ARG, "null argument");
+    *n_past = d->n_past;
+    return RWQ_OK;
+}
+
+}  // extern "C"

@@ -19,6 +19,11 @@ enum RowQuantMode : int { RQ_PLAIN = 0, RQ_GELU = 1, RQ_LN = 2, RQ_ADD_LN = 3 };
 cudaError_t launch_rows_quant(int mode, const float* x, const float* add, float* xout, const float* lw,
                               const float* lb, int m, int k, int m_pad, uint16_t* q16, float* dT, float* uT,
                               float* yout, cudaStream_t s);
+// Same with the codes going to the GEMM layout (`gemm`: q16, dT, uT,
+// m_pad), the GEMV layout (`gemv`: q8, d, sum, u), or both.
+cudaError_t launch_rows_quant_v(int mode, const float* x, const float* add, float* xout, const float* lw,
+                                const float* lb, int m, int k, const ActsView* gemm, const ActsView* gemv,
+                                float* yout, cudaStream_t s);
 cudaError_t launch_im2col3(const float* in, int n_win, int c_in, int t_in, int t_out, int stride, size_t sw,
                            size_t sc, size_t st, float* out, cudaStream_t s);
 cudaError_t launch_bias_gelu(float* y, size_t rows, int cols, const float* bias, const float* pos, int t_per_win,
@@ -32,6 +37,10 @@ cudaError_t launch_attention(const __half* Qh, const __half* Kh, const __half* V
 // layout): out = A W^T (+ bias).  Builds the weight's operand cache on
 // first use.  Returns an RWQ_* status (error text set).
 int gemm_quantized(const ActsView& v, rwq_qtensor* w, const float* bias, float* out, cudaStream_t s);
+
+// Same on either layout: `gemm` false reads the GEMV layout (q8, d, sum, u;
+// integer-MMA GEMV in chunks of 8 rows), true the GEMM layout.
+int linear_acts(const ActsView& v, bool gemm, rwq_qtensor* w, const float* bias, float* out, cudaStream_t s);
 
 // Run `fn` with this stream's scratch arena (at least `bytes`), holding
 // its lock.  Returns fn's status (or an RWQ_* error).

@@ -30,8 +30,18 @@ __device__ __forceinline__ float gelu_ref(float t) {
 // (lane & 7 = position): the reference quantizer (quant.rs:690-716), as
 // k_quantize does it -- d = amax/127, inv = 1/d or 0, q = round(x*inv)
 // half away from zero, clamped to +-127, NaN -> 0.
-__device__ __forceinline__ void quant_block4(float4 x, int row, int bl, int m_pad, uint16_t* __restrict__ q16p,
-                                             float* __restrict__ dT, float* __restrict__ uT) {
+struct QOut {
+    uint16_t* q16;   // GEMM layout: f16 codes [m][k], d_a and d_a*sum transposed [nb][m_pad]
+    float* dT;
+    float* uT;
+    int m_pad;
+    int8_t* q8;      // GEMV layout: int8 codes [m][k], d_a, sum, d_a*sum [m][nb]
+    float* d;
+    int32_t* sum;
+    float* u;
+};
+
+__device__ __forceinline__ void quant_block4(float4 x, int row, int k, int e, const QOut& o) {
     auto absnn = [](float v) { const float w = fabsf(v); return isnan(w) ? 0.f : w; };
     float amax = fmaxf(fmaxf(absnn(x.x), absnn(x.y)), fmaxf(absnn(x.z), absnn(x.w)));
 #pragma unroll
@@ -46,12 +56,28 @@ __device__ __forceinline__ void quant_block4(float4 x, int row, int bl, int m_pa
     int s = c0 + c1 + c2 + c3;
 #pragma unroll
     for (int o = 4; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-    const uint32_t h01 = uint32_t(__half_as_ushort(__int2half_rn(c0))) | (uint32_t(__half_as_ushort(__int2half_rn(c1))) << 16);
-    const uint32_t h23 = uint32_t(__half_as_ushort(__int2half_rn(c2))) | (uint32_t(__half_as_ushort(__int2half_rn(c3))) << 16);
-    *reinterpret_cast<uint2*>(q16p) = make_uint2(h01, h23);
-    if ((threadIdx.x & 7) == 0) {
-        dT[size_t(bl) * m_pad + row] = d;
-        uT[size_t(bl) * m_pad + row] = __fmul_rn(d, float(s));
+    const int bl = e / QK, nb = k / QK;
+    const float u = __fmul_rn(d, float(s));
+    if (o.q16) {
+        const uint32_t h01 =
+            uint32_t(__half_as_ushort(__int2half_rn(c0))) | (uint32_t(__half_as_ushort(__int2half_rn(c1))) << 16);
+        const uint32_t h23 =
+            uint32_t(__half_as_ushort(__int2half_rn(c2))) | (uint32_t(__half_as_ushort(__int2half_rn(c3))) << 16);
+        *reinterpret_cast<uint2*>(o.q16 + size_t(row) * k + e) = make_uint2(h01, h23);
+        if ((threadIdx.x & 7) == 0) {
+            o.dT[size_t(bl) * o.m_pad + row] = d;
+            o.uT[size_t(bl) * o.m_pad + row] = u;
+        }
+    }
+    if (o.q8) {
+        *reinterpret_cast<uint32_t*>(o.q8 + size_t(row) * k + e) = uint32_t(uint8_t(c0)) | (uint32_t(uint8_t(c1)) << 8) |
+                                                                 (uint32_t(uint8_t(c2)) << 16) |
+                                                                 (uint32_t(uint8_t(c3)) << 24);
+        if ((threadIdx.x & 7) == 0) {
+            o.d[size_t(row) * nb + bl] = d;
+            o.sum[size_t(row) * nb + bl] = s;
+            o.u[size_t(row) * nb + bl] = u;
+        }
     }
 }
 
@@ -59,34 +85,34 @@ __device__ __forceinline__ void quant_block4(float4 x, int row, int bl, int m_pa
 // 4l..4l+3 of each 128-element chunk, so 8 lanes share a quant block.
 // MODE: RQ_PLAIN quantize x; RQ_GELU quantize gelu(x); RQ_LN quantize
 // LayerNorm(x); RQ_ADD_LN x += add (written back to xout), then as RQ_LN.
-// With q16 == nullptr the transformed row is written to yout (f32) instead
-// (ln_post).  Rows m..m_pad-1 get zero block scales.  x and xout may
+// The codes go to the GEMM layout (q16/dT/uT), the GEMV layout (q8/d/sum/
+// u), or both; with yout the transformed row is also written as f32 (e.g.
+// ln_post).  GEMM-layout rows m..m_pad-1 get zero block scales.  x and xout may
 // alias: the residual stream is updated in place.
 template <int MODE, int NV>
 __global__ void __launch_bounds__(256) k_rows_quant(const float* x, const float* __restrict__ add, float* xout,
                                                     const float* __restrict__ lw, const float* __restrict__ lb,
-                                                    int m, int k, int m_pad,
-                                                    uint16_t* __restrict__ q16, float* __restrict__ dT,
-                                                    float* __restrict__ uT, float* __restrict__ yout) {
+                                                    int m, int k, QOut o, float* __restrict__ yout) {
     pdl_trigger();
     pdl_wait();
     const int lane = threadIdx.x & 31;
     const int row = int((size_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5);
-    if (row >= m_pad) return;
+    const int rows = o.q16 ? o.m_pad : m;
+    if (row >= rows) return;
     const int nb = k / QK, nch = k / 128;
     if (row >= m) {
-        if (q16)
-            for (int bl = lane; bl < nb; bl += 32) {
-                dT[size_t(bl) * m_pad + row] = 0.f;
-                uT[size_t(bl) * m_pad + row] = 0.f;
-            }
+        for (int bl = lane; bl < nb; bl += 32) {
+            o.dT[size_t(bl) * o.m_pad + row] = 0.f;
+            o.uT[size_t(bl) * o.m_pad + row] = 0.f;
+        }
         return;
     }
     const float4* xr = reinterpret_cast<const float4*>(x + size_t(row) * k);
+    const bool quant = o.q16 || o.q8;
     auto emit = [&](int c, float4 v) {
         const int e = c * 128 + lane * 4;
-        if (q16) quant_block4(v, row, e / QK, m_pad, q16 + size_t(row) * k + e, dT, uT);
-        else *reinterpret_cast<float4*>(yout + size_t(row) * k + e) = v;
+        if (quant) quant_block4(v, row, k, e, o);
+        if (yout) *reinterpret_cast<float4*>(yout + size_t(row) * k + e) = v;
     };
     if (MODE == RQ_PLAIN || MODE == RQ_GELU) {
         for (int c = 0; c < nch; ++c) {
@@ -373,18 +399,16 @@ unsigned grid_stride(size_t total, int tpb) {
 
 template <int MODE>
 cudaError_t rows_quant_mode(const float* x, const float* add, float* xout, const float* lw, const float* lb, int m,
-                            int k, int m_pad, uint16_t* q16, float* dT, float* uT, float* yout, cudaStream_t s) {
-    const unsigned grid = unsigned((size_t(m_pad) * 32 + 255) / 256);
+                            int k, const QOut& o, float* yout, cudaStream_t s) {
+    const int rows = o.q16 ? o.m_pad : m;
+    const unsigned grid = unsigned((size_t(rows) * 32 + 255) / 256);
     const int nch = k / 128;
     if (MODE == RQ_PLAIN || MODE == RQ_GELU || nch <= 4)
-        return launch_pdl(k_rows_quant<MODE, 4>, dim3(grid), dim3(256), 0, s, x, add, xout, lw, lb, m, k, m_pad, q16,
-                          dT, uT, yout);
+        return launch_pdl(k_rows_quant<MODE, 4>, dim3(grid), dim3(256), 0, s, x, add, xout, lw, lb, m, k, o, yout);
     if (nch <= 8)
-        return launch_pdl(k_rows_quant<MODE, 8>, dim3(grid), dim3(256), 0, s, x, add, xout, lw, lb, m, k, m_pad, q16,
-                          dT, uT, yout);
+        return launch_pdl(k_rows_quant<MODE, 8>, dim3(grid), dim3(256), 0, s, x, add, xout, lw, lb, m, k, o, yout);
     if (nch <= 16)
-        return launch_pdl(k_rows_quant<MODE, 16>, dim3(grid), dim3(256), 0, s, x, add, xout, lw, lb, m, k, m_pad,
-                          q16, dT, uT, yout);
+        return launch_pdl(k_rows_quant<MODE, 16>, dim3(grid), dim3(256), 0, s, x, add, xout, lw, lb, m, k, o, yout);
     return cudaErrorInvalidValue;
 }
 
@@ -393,13 +417,37 @@ cudaError_t rows_quant_mode(const float* x, const float* add, float* xout, const
 cudaError_t launch_rows_quant(int mode, const float* x, const float* add, float* xout, const float* lw,
                               const float* lb, int m, int k, int m_pad, uint16_t* q16, float* dT, float* uT,
                               float* yout, cudaStream_t s) {
+    ActsView v;
+    v.m_pad = m_pad;
+    v.q16 = q16;
+    v.dT = dT;
+    v.uT = uT;
+    return launch_rows_quant_v(mode, x, add, xout, lw, lb, m, k, q16 ? &v : nullptr, nullptr, yout, s);
+}
+
+cudaError_t launch_rows_quant_v(int mode, const float* x, const float* add, float* xout, const float* lw,
+                                const float* lb, int m, int k, const ActsView* gemm, const ActsView* gemv,
+                                float* yout, cudaStream_t s) {
     if (k % 128) return cudaErrorInvalidValue;
-    if (m_pad <= 0) return cudaSuccess;
+    if (m <= 0) return cudaSuccess;
+    QOut o = {};
+    if (gemm) {
+        o.q16 = gemm->q16;
+        o.dT = gemm->dT;
+        o.uT = gemm->uT;
+        o.m_pad = gemm->m_pad;
+    }
+    if (gemv) {
+        o.q8 = gemv->q8;
+        o.d = gemv->d;
+        o.sum = gemv->sum;
+        o.u = gemv->u;
+    }
     switch (mode) {
-        case RQ_PLAIN: return rows_quant_mode<RQ_PLAIN>(x, add, xout, lw, lb, m, k, m_pad, q16, dT, uT, yout, s);
-        case RQ_GELU: return rows_quant_mode<RQ_GELU>(x, add, xout, lw, lb, m, k, m_pad, q16, dT, uT, yout, s);
-        case RQ_LN: return rows_quant_mode<RQ_LN>(x, add, xout, lw, lb, m, k, m_pad, q16, dT, uT, yout, s);
-        case RQ_ADD_LN: return rows_quant_mode<RQ_ADD_LN>(x, add, xout, lw, lb, m, k, m_pad, q16, dT, uT, yout, s);
+        case RQ_PLAIN: return rows_quant_mode<RQ_PLAIN>(x, add, xout, lw, lb, m, k, o, yout, s);
+        case RQ_GELU: return rows_quant_mode<RQ_GELU>(x, add, xout, lw, lb, m, k, o, yout, s);
+        case RQ_LN: return rows_quant_mode<RQ_LN>(x, add, xout, lw, lb, m, k, o, yout, s);
+        case RQ_ADD_LN: return rows_quant_mode<RQ_ADD_LN>(x, add, xout, lw, lb, m, k, o, yout, s);
         default: return cudaErrorInvalidValue;
     }
 }

@@ -5,6 +5,7 @@
 #include <cuda_fp16.h>
 #include "rwq_common.cuh"
 #include "rwq_internal.h"
+#include "rwq_decoder.h"
 
 namespace rwq {
 
@@ -205,6 +206,36 @@ __global__ void k_dequant_rows(const uint8_t* __restrict__ qs, const uint32_t* _
         v.y = __fadd_rn(__fmul_rn(bc.d, float(code_at<DT>(bc.w, e + 1))), bc.m);
         v.z = __fadd_rn(__fmul_rn(bc.d, float(code_at<DT>(bc.w, e + 2))), bc.m);
         v.w = __fadd_rn(__fmul_rn(bc.d, float(code_at<DT>(bc.w, e + 3))), bc.m);
+        *reinterpret_cast<float4*>(o + e) = v;
+    }
+}
+
+// Token embedding gather for the decoder (decoder.rs:125-136): row
+// tokens[r] dequantized exactly like QTensor::row_f32, plus the learned
+// position row `pos` (x = dequant + pos, one rounding).
+template <int DT>
+__global__ void k_embed(const uint8_t* __restrict__ qs, const uint32_t* __restrict__ qh,
+                        const uint16_t* __restrict__ dp, const uint16_t* __restrict__ mp,
+                        const int32_t* __restrict__ tokens, int nrows, int n, int nb, const float* __restrict__ pos,
+                        float* __restrict__ x) {
+    pdl_trigger();
+    pdl_wait();
+    size_t t = size_t(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (t >= size_t(nrows) * nb) return;
+    const int r = int(t / nb), bl = int(t % nb);
+    int j = tokens[r];
+    j = j < 0 ? 0 : (j >= n ? n - 1 : j);   // the host validates ids; keep the access in bounds regardless
+    BlockCodes<DT> bc;
+    load_block<DT>(qs, qh, dp, mp, size_t(j), bl, round4(nb), bc);
+    float* o = x + size_t(r) * nb * QK + size_t(bl) * QK;
+    const float* p = pos + size_t(bl) * QK;
+#pragma unroll
+    for (int e = 0; e < QK; e += 4) {
+        float4 v;
+        v.x = __fadd_rn(__fadd_rn(__fmul_rn(bc.d, float(code_at<DT>(bc.w, e + 0))), bc.m), p[e + 0]);
+        v.y = __fadd_rn(__fadd_rn(__fmul_rn(bc.d, float(code_at<DT>(bc.w, e + 1))), bc.m), p[e + 1]);
+        v.z = __fadd_rn(__fadd_rn(__fmul_rn(bc.d, float(code_at<DT>(bc.w, e + 2))), bc.m), p[e + 2]);
+        v.w = __fadd_rn(__fadd_rn(__fmul_rn(bc.d, float(code_at<DT>(bc.w, e + 3))), bc.m), p[e + 3]);
         *reinterpret_cast<float4*>(o + e) = v;
     }
 }
@@ -989,6 +1020,17 @@ struct DequantF {
 };
 
 template <int DT>
+struct EmbedF {
+    static cudaError_t run(const Weight& w, const int32_t* tokens, int nrows, const float* pos, float* x,
+                           cudaStream_t s) {
+        size_t work = size_t(nrows) * w.nb;
+        if (!work) return cudaSuccess;
+        return launch_pdl(k_embed<DT>, dim3(grid_for(work, TPB)), dim3(TPB), 0, s, w.qs, w.qh, w.d, w.m, tokens,
+                          nrows, w.n, w.nb, pos, x);
+    }
+};
+
+template <int DT>
 struct BlockDotsF {
     static cudaError_t run(const ActsView& v, const Weight& w, int32_t* S, cudaStream_t s) {
         size_t work = size_t(v.m) * w.n * w.nb;
@@ -1205,6 +1247,10 @@ cudaError_t launch_quantize_acts(const float* a, const ActsView& v, bool want_ge
 
 cudaError_t launch_dequant_rows(const Weight& w, const int32_t* rows, int nrows, float* out, cudaStream_t s) {
     return by_dtype<DequantF>(w.dtype, w, rows, nrows, out, s);
+}
+
+cudaError_t launch_embed(const Weight& w, const int32_t* tokens, int n, const float* pos, float* x, cudaStream_t s) {
+    return by_dtype<EmbedF>(w.dtype, w, tokens, n, pos, x, s);
 }
 
 cudaError_t launch_block_dots(const ActsView& v, const Weight& w, int32_t* S, cudaStream_t s) {

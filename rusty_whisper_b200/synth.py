@@ -85,18 +85,18 @@ def f32_to_f16_bits(x: np.ndarray) -> np.ndarray:
     return out.astype(np.uint16)
 
 
-def random_blocks(dtype: int, n: int, k: int, seed: int) -> np.ndarray:
+def random_blocks(dtype: int, n: int, k: int, seed: int, d_range=(0.001, 0.02), m_range=(-0.05, 0.05)) -> np.ndarray:
     """Raw ggml bytes for an ``[n, k]`` weight: codes uniform over their
-    range, d ~ U(0.001, 0.02), m ~ U(-0.05, 0.05)."""
+    range, d ~ U(d_range), m ~ U(m_range) (defaults)."""
     assert k % QK == 0
     nblk = n * (k // QK)
     bb = block_bytes(dtype)
     raw = np.zeros((nblk, bb), np.uint8)
-    d = f32_to_f16_bits(uniform(seed * 4 + 1, nblk, 0.001, 0.02))
+    d = f32_to_f16_bits(uniform(seed * 4 + 1, nblk, *d_range))
     raw[:, 0] = d & 0xFF
     raw[:, 1] = d >> 8
     if dtype in (Q4_1, Q5_1):
-        mm = f32_to_f16_bits(uniform(seed * 4 + 2, nblk, -0.05, 0.05))
+        mm = f32_to_f16_bits(uniform(seed * 4 + 2, nblk, *m_range))
         raw[:, 2] = mm & 0xFF
         raw[:, 3] = mm >> 8
     if dtype == Q8_0:
@@ -193,13 +193,24 @@ def quantize_q8_0(x: np.ndarray) -> np.ndarray:
     return raw.reshape(-1)
 
 
+# Random-code model weights (formats without a reference quantizer): block
+# scales chosen so that the weights' standard deviation is about 0.02, like
+# the N(0, 0.02) init the other formats are quantized from.
+MODEL_CODE_SCALES = {
+    Q4_0: ((0.002, 0.007), (0.0, 0.0)),        # q in -8..7: std ~ 4.6 d
+    Q4_1: ((0.002, 0.007), (-0.04, -0.02)),    # q in 0..15, m ~ -7.5 d
+    Q5_0: ((0.001, 0.0035), (0.0, 0.0)),       # q in -16..15: std ~ 9.2 d
+}
+
+
 def encoder_tensors(n_mels: int, n_ctx: int, n_state: int, n_layer: int, dtype: int, seed: int) -> dict:
     """Random-init whisper encoder tensors by their whisper.cpp names
     (encoder.rs:130-234): dense entries are f32 arrays, the six linears of
     each block ``(dtype, raw, n, k)``.  Weights ~ N(0, 0.02); Q5_1 and Q8_0
     linears are quantized from them with the reference's own test
     quantizers (BASELINE config 3 is Q5_1), the other formats get random
-    codes with d ~ U(0.001, 0.02); LayerNorm weights 1 + N(0, 0.02);
+    codes with block scales giving a similar spread (MODEL_CODE_SCALES);
+    LayerNorm weights 1 + N(0, 0.02);
     positions are whisper's sinusoids."""
     t = {}
     ctr = [seed * 1000]
@@ -214,7 +225,7 @@ def encoder_tensors(n_mels: int, n_ctx: int, n_state: int, n_layer: int, dtype: 
             return (dtype, quantize_q5_1(normal(ctr[0], n * k, 0.0, 0.02)), n, k)
         if dtype == Q8_0:
             return (dtype, quantize_q8_0(normal(ctr[0], n * k, 0.0, 0.02)), n, k)
-        return (dtype, random_blocks(dtype, n, k, ctr[0]), n, k)
+        return (dtype, random_blocks(dtype, n, k, ctr[0], *MODEL_CODE_SCALES[dtype]), n, k)
 
     t["encoder.conv1.weight"] = nrm(n_state, n_mels, 3)
     t["encoder.conv1.bias"] = nrm(n_state)
@@ -251,3 +262,47 @@ def encoder_mel(n_windows: int, n_mels: int, n_frames: int, seed: int) -> np.nda
     """Log-mel input of BASELINE config 3: N(-0.5, 0.3) clamped to [-1.5, 1.5]."""
     x = normal(seed, n_windows * n_mels * n_frames, -0.5, 0.3)
     return np.clip(x, -1.5, 1.5).astype(np.float32).reshape(n_windows, n_mels, n_frames)
+
+
+def decoder_tensors(n_vocab: int, n_ctx: int, n_state: int, n_layer: int, dtype: int, seed: int) -> dict:
+    """Random-init whisper decoder tensors by their whisper.cpp names
+    (decoder.rs:36-321), same conventions as :func:`encoder_tensors`; the
+    token embedding (also the tied logits matrix) is quantized like the
+    block linears; learned positions ~ N(0, 0.02)."""
+    t = {}
+    ctr = [seed * 1000 + 500]
+
+    def nrm(*shape, std=0.02, mean=0.0):
+        ctr[0] += 1
+        return normal(ctr[0], int(np.prod(shape)), mean, std).reshape(shape)
+
+    def lin(n, k):
+        ctr[0] += 1
+        if dtype == Q5_1:
+            return (dtype, quantize_q5_1(normal(ctr[0], n * k, 0.0, 0.02)), n, k)
+        if dtype == Q8_0:
+            return (dtype, quantize_q8_0(normal(ctr[0], n * k, 0.0, 0.02)), n, k)
+        return (dtype, random_blocks(dtype, n, k, ctr[0], *MODEL_CODE_SCALES[dtype]), n, k)
+
+    t["decoder.token_embedding.weight"] = lin(n_vocab, n_state)
+    t["decoder.positional_embedding"] = nrm(n_ctx, n_state)
+    for l in range(n_layer):
+        p = f"decoder.blocks.{l}"
+        for ln in ("attn_ln", "cross_attn_ln", "mlp_ln"):
+            t[f"{p}.{ln}.weight"] = nrm(n_state, mean=1.0)
+            t[f"{p}.{ln}.bias"] = nrm(n_state)
+        for a in ("attn", "cross_attn"):
+            t[f"{p}.{a}.query.weight"] = lin(n_state, n_state)
+            t[f"{p}.{a}.query.bias"] = nrm(n_state)
+            t[f"{p}.{a}.key.weight"] = lin(n_state, n_state)
+            t[f"{p}.{a}.value.weight"] = lin(n_state, n_state)
+            t[f"{p}.{a}.value.bias"] = nrm(n_state)
+            t[f"{p}.{a}.out.weight"] = lin(n_state, n_state)
+            t[f"{p}.{a}.out.bias"] = nrm(n_state)
+        t[f"{p}.mlp.0.weight"] = lin(4 * n_state, n_state)
+        t[f"{p}.mlp.0.bias"] = nrm(4 * n_state)
+        t[f"{p}.mlp.2.weight"] = lin(n_state, 4 * n_state)
+        t[f"{p}.mlp.2.bias"] = nrm(n_state)
+    t["decoder.ln.weight"] = nrm(n_state, mean=1.0)
+    t["decoder.ln.bias"] = nrm(n_state)
+    return t
