@@ -392,6 +392,183 @@ def run_encoder(args, dev, tc_peak, stream, rank, world):
     return res
 
 
+DEC_MEDIUM = dict(n_vocab=51865, n_ctx=448, n_state=1024, n_head=16, n_layer=24)   # whisper-medium decoder (config 4)
+LARGE_V3 = dict(n_mels=128, n_audio=1500, n_state=1280, n_head=20, enc_layers=32, dec_layers=32, n_vocab=51866,
+                n_ctx=448)
+
+
+def run_decoder_beams(args, dev, hbm_peak, stream, rank, world):
+    """whisper-medium decoder, Q5_0, 16 windows x 5 beam
+    streams (80 streams; the five streams of a window share its cross K/V),
+    224 fixed steps after a 4-token seeded random prefix, cross-attention
+    over a 1500 x 1024 N(0, 1) encoder output per window.  Each stream is
+    fed its own greedy choice (the beam re-ranking itself is host policy,
+    not part of the step).  Tokens per second of all streams."""
+    import torch
+    from rusty_whisper_b200 import decoder
+    c = DEC_MEDIUM
+    n_win, beams, steps, prefix = 16, 5, 224, 4
+    S = n_win * beams
+    t = synth.decoder_tensors(c["n_vocab"], c["n_ctx"], c["n_state"], c["n_layer"], 6, seed=7, reuse_layers=True)
+    dec = decoder.Decoder(c["n_vocab"], c["n_ctx"], c["n_state"], c["n_head"], c["n_layer"], t)
+    enc = torch.from_numpy(synth.normal(300 + rank, n_win * 1500 * c["n_state"]).reshape(n_win, 1500, c["n_state"]))
+    enc = enc.to(dev)
+    sw = [w for w in range(n_win) for _ in range(beams)]
+    pre = torch.from_numpy(synth.randint(400 + rank, prefix * S, 0, 50256).astype(np.int32).reshape(prefix, S))
+    pre = pre.to(dev)
+
+    def run(n_steps):
+        dec.begin(enc, sw)
+        for i in range(prefix - 1):
+            dec.step(pre[i], want="none")
+        tok = dec.step(pre[prefix - 1], want="best")
+        for _ in range(n_steps - 1):
+            tok = dec.step(tok, want="best")
+        return tok
+
+    run(8)
+    torch.cuda.synchronize()
+    torch.cuda._sleep(GATE_CYCLES)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    run(steps)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    from rusty_whisper_b200 import quant
+    quant.stream_check()
+    tt = e0.elapsed_time(e1) / 1e3
+    D, Lr = c["n_state"], c["n_layer"]
+    cross_bytes = n_win * Lr * 2 * 1500 * D * 2.0
+    res = {"workload": "BASELINE config 4: whisper-medium decoder (24 x d1024/16 heads/FFN 4096, vocab 51865), Q5_0, "
+                       f"{n_win} windows x {beams} beam streams, {steps} steps after a {prefix}-token prefix",
+           "tokens_per_s": round(world * S * steps / tt, 1), "ms_per_step": round(tt / (steps + prefix) * 1e3, 3),
+           "streams": S,
+           "bytes_per_step": {"quantized_weights": round(sum(v[1].nbytes for v in t.values() if isinstance(v, tuple)) / 1e6, 1),
+                              "cross_kv_f16_MB": round(cross_bytes / 1e6, 1)},
+           "note": "streams > 8: the linears run on the tensor-core GEMM (f16 hi|lo weight operand); each stream "
+                   "takes its own greedy id",
+           "data": "synthetic (seeded): random-code Q5_0 weights (block 0 values reused by every block, each block its "
+                   "own device copy), encoder output N(0, 1)"}
+    if rank == 0 and world == 1 and not args.no_cpu:
+        import oracle
+        threads = oracle.default_threads()
+        ref = oracle.Decoder(c["n_vocab"], c["n_ctx"], c["n_state"], c["n_head"], c["n_layer"], t)
+        ref.begin(enc[0].cpu().numpy(), threads=threads)
+        ref.forward([1], threads=threads)               # first call: the reference's cold weight path
+        t0 = time.perf_counter()
+        for tk in (2, 3, 4):
+            ref.forward([tk], threads=threads)
+        tc = (time.perf_counter() - t0) / 3
+        res["cpu_baseline"] = {"tokens_per_s": round(1.0 / tc, 2), "s_per_token": round(tc, 4), "cores": threads,
+                               "kind": "port", "tier": oracle.TIER_NAMES[oracle.dispatch_tier()],
+                               "sample": "3 decode steps of one stream (forward(&[token]), packed weights) through the "
+                                         "C++ restatement of decoder.rs:102-206, 315-321"}
+    return res
+
+
+def run_large_v3(args, dev, stream, rank, world):
+    """large-v3-shaped end to end, Q4_0: 256 windows of 30 s
+    synthetic audio sharded evenly over the ranks; per rank, host audio ->
+    log-mel (128 mels) -> encoder (32 blocks, d1280) -> decoder (32 blocks,
+    vocab 51866) greedy for 224 tokens after the 4-token start sequence ->
+    token ids back on the host.  Audio-seconds per second of all ranks (time:
+    max over ranks)."""
+    import torch
+    import torch.distributed as dist
+    from rusty_whisper_b200 import audio, decoder, encoder
+    c = LARGE_V3
+    total_win, steps = 256, 224
+    n_win = total_win // world
+    te = synth.encoder_tensors(c["n_mels"], c["n_audio"], c["n_state"], c["enc_layers"], 2, seed=11, reuse_layers=True)
+    td = synth.decoder_tensors(c["n_vocab"], c["n_ctx"], c["n_state"], c["dec_layers"], 2, seed=12, reuse_layers=True)
+    enc = encoder.Encoder(c["n_mels"], c["n_audio"], c["n_state"], c["n_head"], c["enc_layers"], te)
+    dec = decoder.Decoder(c["n_vocab"], c["n_ctx"], c["n_state"], c["n_head"], c["dec_layers"], td)
+    del te, td
+    mel_plan = audio.LogMel(audio.mel_filterbank(c["n_mels"]), c["n_mels"])
+    distinct = [synth.speechlike_window(900 + 13 * i) for i in range(8)]
+    host = torch.from_numpy(np.stack([distinct[(rank * n_win + i) % 8] for i in range(n_win)])).pin_memory()
+    toks_host = torch.empty((steps, n_win), dtype=torch.int32).pin_memory()
+    sot = torch.tensor([50258, 50259, 50360, 50364], dtype=torch.int32)     # sot, lang, transcribe, notimestamps
+    prompt = sot.repeat(n_win, 1).t().contiguous().to(dev)
+    eot = 50257
+
+    def pipeline(n_steps, copy_out=True):
+        x = host.to(dev, non_blocking=True)
+        mel = mel_plan.batch(x)
+        eo = enc.encode(mel)
+        dec.begin(eo)
+        for i in range(3):
+            dec.step(prompt[i], want="none")
+        out = torch.empty((n_steps, n_win), dtype=torch.int32, device=dev)
+        tok = dec.step(prompt[3], want="best", limit=eot, out=out[0])
+        for i in range(1, n_steps):
+            tok = dec.step(tok, want="best", limit=eot, out=out[i])
+        if copy_out:
+            toks_host[:n_steps].copy_(out, non_blocking=True)
+        return out
+
+    pipeline(4)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    pipeline(steps)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    from rusty_whisper_b200 import quant
+    quant.stream_check()
+    tt = e0.elapsed_time(e1) / 1e3
+    tmax = tt
+    if world > 1:
+        tm = torch.tensor([tt], dtype=torch.float64, device=dev)
+        dist.all_reduce(tm, op=dist.ReduceOp.MAX)
+        tmax = float(tm.item())
+    res = {"workload": "BASELINE config 5: large-v3 shape (128 mels; encoder 32 x d1280/20 heads/FFN 5120; decoder 32 "
+                       "blocks, vocab 51866), Q4_0, 256 windows x 30 s sharded over the ranks, greedy 224 tokens",
+           "audio_s_per_s": round(total_win * 30.0 / tmax, 1), "s_per_job": round(tmax, 3),
+           "windows_per_rank": n_win, "scaling": "strong (256 windows in total)",
+           "h2d_bytes_per_rank": int(host.numel() * 4), "d2h_bytes_per_rank": int(steps * n_win * 4),
+           "timing": "CUDA events around host audio -> tokens on the host, max over ranks",
+           "data": "synthetic (seeded): band-limited noise at -20 dBFS with 0.2-2 s silences; random-code Q4_0 "
+                   "weights (block 0 values reused by every block, each block its own device copy)"}
+    if rank == 0 and world == 1 and not args.no_cpu:
+        import oracle
+        threads = oracle.default_threads()
+        tc0 = time.perf_counter()
+        te = synth.encoder_tensors(c["n_mels"], c["n_audio"], c["n_state"], c["enc_layers"], 2, seed=11,
+                                   reuse_layers=True)
+        te = {k: v for k, v in te.items() if not k.startswith("encoder.blocks.") or k.split(".")[2] in ("0", "1")}
+        ref_e = oracle.Encoder(c["n_mels"], c["n_audio"], c["n_state"], c["n_head"], 2, te)   # 2 of the 32 blocks
+        mel1 = mel_plan(distinct[0])
+        t0 = time.perf_counter()
+        eo1 = ref_e.encode(mel1, threads=threads)
+        t_enc2 = time.perf_counter() - t0
+        del ref_e, te
+        td = synth.decoder_tensors(c["n_vocab"], c["n_ctx"], c["n_state"], c["dec_layers"], 2, seed=12,
+                                   reuse_layers=True)
+        ref_d = oracle.Decoder(c["n_vocab"], c["n_ctx"], c["n_state"], c["n_head"], c["dec_layers"], td)
+        ref_d.begin(eo1, threads=threads)
+        ref_d.forward([50258], threads=threads)
+        t0 = time.perf_counter()
+        for tk in (50259, 50360):
+            ref_d.forward([tk], threads=threads)
+        t_tok = (time.perf_counter() - t0) / 2
+        # extrapolation: the encoder's 32 blocks from 2 (the conv stem is in
+        # both), the decoder's 228 positions from 2
+        t_win = t_enc2 * 16 + t_tok * (steps + 4)
+        res["cpu_baseline"] = {"audio_s_per_s": round(30.0 / t_win, 4), "s_per_window": round(t_win, 2),
+                               "cores": threads, "kind": "port", "tier": oracle.TIER_NAMES[oracle.dispatch_tier()],
+                               "sample": f"one window: encoder with 2 of 32 blocks ({t_enc2:.1f} s) and 2 decoder "
+                                         f"positions ({t_tok:.2f} s each) through the C++ restatement, extrapolated "
+                                         f"linearly to 32 blocks and 228 positions (extrapolated; "
+                                         f"{time.perf_counter() - tc0:.0f} s of CPU work)"}
+    return res
+
+
 def run_gemv(args, dev, quant, w_np, hbm_peak, stream):
     """Decoder GEMVs of config 2: for each weight, R back-to-back launches
     over copies rotated past L2, one event pair per batch."""
@@ -588,7 +765,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
-    ap.add_argument("--only", default="all", choices=["all", "gemm", "encoder"],
+    ap.add_argument("--only", default="all", choices=["all", "gemm", "encoder", "decoder", "large"],
                     help="gemm: skip the GEMV, e2e, front-end and encoder legs; encoder: only the config-3 "
                          "encoder leg (short runs for profiling)")
     args = ap.parse_args()
@@ -607,15 +784,20 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local_rank))
     try:
-        if args.only == "encoder":
+        if args.only in ("encoder", "decoder", "large"):
             import torch
             from rusty_whisper_b200 import quant
             torch.cuda.set_device(local_rank)
             quant.init(local_rank)
-            res = run_encoder(args, torch.device("cuda", local_rank), peaks()[1], torch.cuda.current_stream(), rank,
-                              world)
+            dev, st = torch.device("cuda", local_rank), torch.cuda.current_stream()
+            if args.only == "encoder":
+                res = run_encoder(args, dev, peaks()[1], st, rank, world)
+            elif args.only == "decoder":
+                res = run_decoder_beams(args, dev, peaks()[0], st, rank, world)
+            else:
+                res = run_large_v3(args, dev, st, rank, world)
             if rank == 0:
-                print(json.dumps({"encoder": res}), flush=True)
+                print(json.dumps({args.only: res}), flush=True)
             return
         run_ours(args, rank, world, local_rank)
     finally:

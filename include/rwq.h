@@ -140,20 +140,21 @@ int rwq_block_dots_dev(const float* a, int64_t m, int64_t k, const rwq_qtensor* 
 int rwq_matmul_t_q_noalloc(const float* a, int64_t m, int64_t k, const rwq_qtensor* b, const float* bias,
                            float* out, void* stream);
 
-/* Force the kernel family for matmuls with m > 8 (testing and
- * benchmarking): 0 = automatic, 1 = CUDA-core GEMV kernel in row chunks,
+/* Force the kernel family (testing and benchmarking): 0 = automatic
+ * (GEMV family for m <= 256, GEMM above), 1 = GEMV family in row chunks,
  * 2 = tensor-core GEMM with the weight scales folded into the operand
  * (the automatic choice), 3 = tensor-core GEMM that forms each block's
  * integer dot exactly and scales it on the CUDA cores.  Applies to this
  * host thread. */
 int rwq_set_gemm_path(int path);
 
-/* Force the kernel of the CUDA-core / GEMV family (m <= 8, or path 1
- * above) for testing and benchmarking: 0 = automatic (the integer-MMA
- * kernel for every m <= 8, so a row's result does not depend on m),
- * 1 = dp4a kernel (one warp lane per block, lanes per row from k),
- * 2 = integer-MMA kernel (mma.sync m16n8k32: one instruction per block for
- * 16 weight rows x 8 activation rows).  Both compute the reference's per-block formula
+/* Force the kernel of the GEMV family (m <= 256, or path 1 above) for
+ * testing and benchmarking: 0 = automatic (the integer-MMA kernel for every
+ * m, so a row's result does not depend on m), 1 = dp4a kernel (one warp
+ * lane per block, lanes per row from k, launches of 8 rows), 2 =
+ * integer-MMA kernel (mma.sync m16n8k32: one instruction per block for 16
+ * weight rows x 8 activation rows, up to 64 rows per launch sharing each
+ * decoded weight fragment).  Both compute the reference's per-block formula
  * (quant.rs:349-351, :452-454) with exact integer block dots; they differ
  * only in f32 summation order.  Applies to this host thread. */
 int rwq_set_gemv_kernel(int kind);

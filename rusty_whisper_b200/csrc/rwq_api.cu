@@ -4,8 +4,9 @@
 // Dispatch of a matmul (quant.rs:754-1051 restated for the GPU):
 //   mode INT8 (the reference's tier on every x86 host):
 //     quantize activations (one launch), then
-//       m <= 8  -> GEMV kernel (decoder shapes; CUDA cores, HBM-bound)
-//       m >  8  -> tcgen05 GEMM (encoder shapes)
+//       m <= 256 -> GEMV family (decoder shapes, HBM-bound): the integer-
+//                   MMA kernel, launches of up to 64 rows
+//       m >  256 -> tcgen05 GEMM (encoder shapes)
 //   mode F32 (the reference's f32 fallback): dequant-then-f32 GEMV kernel
 //     over row chunks of 8.
 #include <cuda_runtime.h>
@@ -202,18 +203,9 @@ int run_quantized(const rwq::ActsView& v, bool gemm, rwq_qtensor* b, const float
     const rwq::Weight& w = b->w;
     const int64_t m = v.m, k = v.k;
     if (!gemm) {
-        const size_t smem = size_t(rwq::GEMV_MAX_M) * k + size_t(rwq::GEMV_MAX_M) * (k / 32) * 12;
-        if (smem > 200 * 1024 || k > 8192)
-            return fail(RWQ_ERR_ARG, "k=%lld too large for the GEMV kernel (max 8192)", (long long)k);
-        for (int64_t m0 = 0; m0 < m; m0 += rwq::GEMV_MAX_M) {
-            rwq::ActsView c = v;
-            c.m = int(m - m0 < rwq::GEMV_MAX_M ? m - m0 : rwq::GEMV_MAX_M);
-            c.q8 = v.q8 + m0 * k;
-            c.d = v.d + m0 * v.nb;
-            c.sum = v.sum + m0 * v.nb;
-            c.u = v.u + m0 * v.nb;
-            RWQ_CUDA(rwq::launch_gemv_i8(c, w, bias, out + m0 * w.n, s), "gemv_i8 launch");
-        }
+        if (k > 8192) return fail(RWQ_ERR_ARG, "k=%lld too large for the GEMV kernels (max 8192)", (long long)k);
+        (void)m;
+        RWQ_CUDA(rwq::launch_gemv_i8(v, w, bias, out, s), "gemv launch");
         return RWQ_OK;
     }
     int rc;
@@ -248,7 +240,7 @@ int matmul_dev_impl(const float* a, int64_t m, int64_t k, rwq_qtensor* b, const 
         return RWQ_OK;
     }
     int path = force_path ? force_path : t_gemm_path;
-    if (path == 0) path = (m <= rwq::GEMV_MAX_M) ? 1 : 2;
+    if (path == 0) path = (m <= rwq::GEMV_FAMILY_MAX_M) ? 1 : 2;
     const bool gemm = path >= 2;
     if (gemm && (k * 2) % 16) return fail(RWQ_ERR_ARG, "k*2 bytes must be a multiple of 16 for the GEMM");
     Workspace* ws = nullptr;
@@ -595,7 +587,7 @@ int rwq_qacts_quantize(rwq_qacts* q, const float* a, int64_t m, void* stream) {
     if (m < 0 || m > q->max_m) return fail(RWQ_ERR_ARG, "m=%lld outside [0, %d]", (long long)m, q->max_m);
     if (m > 0 && !a) return fail(RWQ_ERR_ARG, "activations are null");
     int path = t_gemm_path;
-    if (path == 0) path = (m <= rwq::GEMV_MAX_M) ? 1 : 2;
+    if (path == 0) path = (m <= rwq::GEMV_FAMILY_MAX_M) ? 1 : 2;
     q->gemm = path >= 2;
     // Carve for the current m (row strides depend on m); the arena was
     // sized for max_m in the GEMM layout, which is the larger one.

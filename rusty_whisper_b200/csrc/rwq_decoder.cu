@@ -15,8 +15,9 @@
 //           streams) -> quantize -> cross out -> residual + LN + quantize
 //           -> fc1 -> GELU + quantize -> fc2} -> residual + final LN +
 //           quantize -> tied logits -> greedy argmax.
-// Linears take the integer-MMA GEMV for up to 8 streams and the tensor-core
-// GEMM above that; everything stays on the device between steps.
+// Linears take the integer-MMA GEMV (weights streamed from HBM once per
+// step for up to 64 streams per launch) for up to 256 streams and the
+// tensor-core GEMM above that; everything stays on the device between steps.
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <cmath>
@@ -197,7 +198,7 @@ rwq::ActsView with_k(rwq::ActsView v, int k) {
 int rows(rwq_decoder* d, int mode, const float* x, const float* add, float* xout, const char* ln, int k,
          cudaStream_t s, int layer = -1) {
     const int S = d->n_streams;
-    const bool gemm = S > rwq::GEMV_MAX_M;
+    const bool gemm = S > rwq::GEMV_FAMILY_MAX_M;
     const rwq::ActsView a = with_k(gemm ? d->gemm : d->gemv, k);
     const float* w = nullptr;
     const float* b = nullptr;
@@ -213,7 +214,7 @@ int rows(rwq_decoder* d, int mode, const float* x, const float* add, float* xout
 }
 
 int linear(rwq_decoder* d, rwq_qtensor* w, const float* bias, float* out, cudaStream_t s) {
-    const bool gemm = d->n_streams > rwq::GEMV_MAX_M;
+    const bool gemm = d->n_streams > rwq::GEMV_FAMILY_MAX_M;
     const rwq::ActsView a = with_k(gemm ? d->gemm : d->gemv, rwq::weight_of(w).k);
     return rwq::linear_acts(a, gemm, w, bias, out, s);
 }

@@ -62,7 +62,15 @@ cudaError_t launch_gemm_tc(const ActsView& v, const Weight& w, const float* bias
 cudaError_t launch_gemm_fold(const ActsView& v, const Weight& w, const float* bias, float* y, int* err_flag,
                              cudaStream_t s, char* why, size_t why_len);
 
+// The dp4a GEMV takes at most 8 activation rows per launch.
 constexpr int GEMV_MAX_M = 8;
+// Matmuls of up to this many rows take the GEMV family (the integer-MMA
+// kernel, several launches of up to 64 rows that re-read the weights from
+// L2); more rows take the tensor-core GEMM.
+constexpr int GEMV_FAMILY_MAX_M = 256;
+// Activation rows one integer-MMA GEMV launch takes for a weight of this
+// dtype and k (64 unless the staging of 64 rows would not fit).
+int gemv_rows_per_launch(int dtype, int k);
 
 }  // namespace rwq
 

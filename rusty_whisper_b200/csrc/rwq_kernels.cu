@@ -483,6 +483,118 @@ struct MmaGroup {
     uint2 d[2], m[2];                   // f16 d (m) of blocks 0..3
 };
 
+// Two f16 (low half first) to f32, exactly.
+__device__ __forceinline__ float2 h2f2(uint32_t w) {
+    return __half22float2(*reinterpret_cast<const __half2*>(&w));
+}
+
+template <bool SA>
+__device__ __forceinline__ void mma_i8(const uint32_t (&a)[4], uint2 b, int2 ci, int (&d)[4]) {
+    if (SA)
+        asm volatile("mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+                     "{%10,%11,%12,%13};"
+                     : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+                     : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b.x), "r"(b.y), "r"(ci.x), "r"(ci.y),
+                       "r"(ci.x), "r"(ci.y));
+    else
+        asm volatile("mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+                     "{%10,%11,%12,%13};"
+                     : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+                     : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b.x), "r"(b.y), "r"(ci.x), "r"(ci.y),
+                       "r"(ci.x), "r"(ci.y));
+}
+
+// Shared-memory staging of the activations, per block kb and n-tile nt
+// (8 activation rows each): 32 B-fragment pairs (lane order); per quad
+// lane c the seeds and d_a of act rows 2c and 2c+1 as one 16-byte record
+// {seed, seed, d_a, d_a}; d_a*sum(q_a) of the tile's 8 rows.
+struct MmaActs {
+    const uint2* frag;   // [nb4][NT][32]
+    const int4* sc;      // [nb4][NT][4]
+    const float* ua;     // [nb4][NT][8]
+};
+
+template <int DT, int NT>
+__device__ __forceinline__ void mma_compute(const MmaGroup<DT>& r, const MmaActs& A, int G, int lane, float2 (&a01)[NT],
+                                            float2 (&a23)[NT]) {
+    const int c = lane & 3;
+    const float2 dr0[2] = {h2f2(r.d[0].x), h2f2(r.d[0].y)}, dr1[2] = {h2f2(r.d[1].x), h2f2(r.d[1].y)};
+    float2 mr0[2], mr1[2];
+    if (has_min(DT)) {
+        mr0[0] = h2f2(r.m[0].x); mr0[1] = h2f2(r.m[0].y);
+        mr1[0] = h2f2(r.m[1].x); mr1[1] = h2f2(r.m[1].y);
+    }
+    const float2 nmag = make_float2(-MAGIC_F, -MAGIC_F);
+    // Pad blocks (kb >= nb) need no test: their weight codes and scales
+    // are zero and their activation records are staged as zero scales with
+    // seed 1.5*2^23, so they add exactly 0.
+#pragma unroll
+    for (int b = 0; b < 4; ++b) {
+        const int kb = 4 * G + b;
+        uint32_t a[4];
+        if (DT == Q8_0) {
+            a[0] = r.q[0][(2 * b) % (qs_bytes(DT) / 4)];
+            a[1] = r.q[1][(2 * b) % (qs_bytes(DT) / 4)];
+            a[2] = r.q[0][(2 * b + 1) % (qs_bytes(DT) / 4)];
+            a[3] = r.q[1][(2 * b + 1) % (qs_bytes(DT) / 4)];
+        } else {
+#pragma unroll
+            for (int rr = 0; rr < 2; ++rr) {
+                const uint32_t w = r.q[rr][b % (qs_bytes(DT) / 4)];
+                uint32_t lo = w & 0x0F0F0F0Fu, hi = (w >> 4) & 0x0F0F0F0Fu;
+                if (has_qh(DT)) {
+                    const uint32_t h = r.h[rr][b % (has_qh(DT) ? 4 : 1)];
+                    lo |= (h << (4 - c)) & 0x10101010u;
+                    hi |= (h >> c) & 0x10101010u;
+                }
+                a[rr] = lo;
+                a[2 + rr] = hi;
+            }
+        }
+        const float db0 = (b & 1) ? dr0[b >> 1].y : dr0[b >> 1].x;
+        const float db1 = (b & 1) ? dr1[b >> 1].y : dr1[b >> 1].x;
+        float mb0 = 0.f, mb1 = 0.f;
+        if (has_min(DT)) {
+            mb0 = (b & 1) ? mr0[b >> 1].y : mr0[b >> 1].x;
+            mb1 = (b & 1) ? mr1[b >> 1].y : mr1[b >> 1].x;
+        }
+        // One MMA per 8 activation rows, all on the same decoded A fragment.
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+            const uint2 bf = A.frag[(kb * NT + nt) * 32 + lane];
+            const int4 sc = A.sc[(kb * NT + nt) * 4 + c];
+            int dd[4];
+            mma_i8<DT == Q8_0>(a, bf, make_int2(sc.x, sc.y), dd);
+            const float2 da = make_float2(__int_as_float(sc.z), __int_as_float(sc.w));
+            // S exactly (integer < 2^22 below 1.5*2^23); acc += (d_a*d_b)*S
+            const float2 s01 = __fadd2_rn(make_float2(__int_as_float(dd[0]), __int_as_float(dd[1])), nmag);
+            const float2 s23 = __fadd2_rn(make_float2(__int_as_float(dd[2]), __int_as_float(dd[3])), nmag);
+            a01[nt] = __ffma2_rn(__fmul2_rn(da, make_float2(db0, db0)), s01, a01[nt]);
+            a23[nt] = __ffma2_rn(__fmul2_rn(da, make_float2(db1, db1)), s23, a23[nt]);
+            if (has_min(DT)) {
+                const float2 ua = *reinterpret_cast<const float2*>(A.ua + (kb * NT + nt) * 8 + 2 * c);
+                a01[nt] = __ffma2_rn(ua, make_float2(mb0, mb0), a01[nt]);
+                a23[nt] = __ffma2_rn(ua, make_float2(mb1, mb1), a23[nt]);
+            }
+        }
+    }
+}
+
+template <int NT>
+__device__ __forceinline__ void mma_store(const float2 (&a01)[NT], const float2 (&a23)[NT], int T, int lane, int M,
+                                          int N, const float* __restrict__ bias, float* __restrict__ y) {
+    const int g = lane >> 2, c = lane & 3;
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+        const float v[4] = {a01[nt].x, a01[nt].y, a23[nt].x, a23[nt].y};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int row = T * 16 + g + ((i & 2) ? 8 : 0), col = nt * 8 + 2 * c + (i & 1);
+            if (row < N && col < M) y[size_t(col) * N + row] = bias ? __fadd_rn(v[i], __ldg(bias + row)) : v[i];
+        }
+    }
+}
+
 // Per-warp shared-memory ring of weight groups, filled with cp.async so
 // that the data in flight costs no registers.  Slot layout (one 4-block
 // group of the warp's 16 rows): codes [16 rows][4 lanes][QSB] (the 16- or
@@ -501,15 +613,14 @@ __device__ __forceinline__ void cp_async8(uint32_t dst, const void* src) {
     asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(dst), "l"(src) : "memory");
 }
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+
 // Request group G of tile T into the slot at shared address `slot`.
-// Rows past N are not copied (their slot bytes are stale; the sums they
-// feed are never stored).  Offsets fit 32 bits: the host checks
-// n * nb4 * qs_bytes < 2^32.
 template <int DT>
 __device__ __forceinline__ void ring_issue(const uint8_t* __restrict__ qs, const uint32_t* __restrict__ qh,
                                            const uint16_t* __restrict__ dp, const uint16_t* __restrict__ mp, int N,
                                            int nb4, int T, int G, int lane, uint32_t slot) {
-    // Rows past N re-read row N-1 (their sums are never stored).
+    // Rows past N re-read row N-1 (their sums are never stored).  Offsets
+    // fit 32 bits: the host checks n * nb4 * qs_bytes < 2^32.
     const int g = lane >> 2, c = lane & 3;
 #pragma unroll
     for (int rr = 0; rr < 2; ++rr) {
@@ -553,113 +664,17 @@ __device__ __forceinline__ void ring_read(const uint8_t* slot, int lane, MmaGrou
     }
 }
 
-// Two f16 (low half first) to f32, exactly.
-__device__ __forceinline__ float2 h2f2(uint32_t w) {
-    return __half22float2(*reinterpret_cast<const __half2*>(&w));
+// Shared memory of k_gemv_mma for NT n-tiles: per block and n-tile the B
+// fragments (256 B), seed/d_a records (64 B) and d_a*sum(q_a) (32 B); the
+// partial-sum buffer (4 KB per n-tile); then each warp's weight ring.
+__host__ __device__ constexpr size_t gemv_mma_act_smem(int nb, int nt) {
+    return size_t(round4(nb)) * size_t(nt) * 352 + size_t(nt) * 4096;
 }
 
-template <bool SA>
-__device__ __forceinline__ void mma_i8(const uint32_t (&a)[4], uint2 b, int2 ci, int (&d)[4]) {
-    if (SA)
-        asm volatile("mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-                     "{%10,%11,%12,%13};"
-                     : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
-                     : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b.x), "r"(b.y), "r"(ci.x), "r"(ci.y),
-                       "r"(ci.x), "r"(ci.y));
-    else
-        asm volatile("mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-                     "{%10,%11,%12,%13};"
-                     : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
-                     : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b.x), "r"(b.y), "r"(ci.x), "r"(ci.y),
-                       "r"(ci.x), "r"(ci.y));
-}
-
-// Shared-memory staging of the activations, per block kb: 32 B-fragment
-// pairs (lane order); per quad lane c the seeds and d_a of act rows 2c and
-// 2c+1 as one 16-byte record {seed, seed, d_a, d_a}; d_a*sum(q_a) of act
-// rows 0..7.
-struct MmaActs {
-    const uint2* frag;   // [nb4][32]
-    const int4* sc;      // [nb4][4]
-    const float* ua;     // [nb4][8]
-};
-
-template <int DT>
-__device__ __forceinline__ void mma_compute(const MmaGroup<DT>& r, const MmaActs& A, int G, int nb, int lane,
-                                            float2& a01, float2& a23) {
-    const int c = lane & 3;
-    const float2 dr0[2] = {h2f2(r.d[0].x), h2f2(r.d[0].y)}, dr1[2] = {h2f2(r.d[1].x), h2f2(r.d[1].y)};
-    float2 mr0[2], mr1[2];
-    if (has_min(DT)) {
-        mr0[0] = h2f2(r.m[0].x); mr0[1] = h2f2(r.m[0].y);
-        mr1[0] = h2f2(r.m[1].x); mr1[1] = h2f2(r.m[1].y);
-    }
-    const float2 nmag = make_float2(-MAGIC_F, -MAGIC_F);
-    // Pad blocks (kb >= nb) need no test: their weight codes and scales
-    // are zero and their activation records are staged as zero scales with
-    // seed 1.5*2^23, so they add exactly 0.
-#pragma unroll
-    for (int b = 0; b < 4; ++b) {
-        const int kb = 4 * G + b;
-        {
-            uint32_t a[4];
-            if (DT == Q8_0) {
-                a[0] = r.q[0][(2 * b) % (qs_bytes(DT) / 4)];
-                a[1] = r.q[1][(2 * b) % (qs_bytes(DT) / 4)];
-                a[2] = r.q[0][(2 * b + 1) % (qs_bytes(DT) / 4)];
-                a[3] = r.q[1][(2 * b + 1) % (qs_bytes(DT) / 4)];
-            } else {
-#pragma unroll
-                for (int rr = 0; rr < 2; ++rr) {
-                    const uint32_t w = r.q[rr][b % (qs_bytes(DT) / 4)];
-                    uint32_t lo = w & 0x0F0F0F0Fu, hi = (w >> 4) & 0x0F0F0F0Fu;
-                    if (has_qh(DT)) {
-                        const uint32_t h = r.h[rr][b % (has_qh(DT) ? 4 : 1)];
-                        lo |= (h << (4 - c)) & 0x10101010u;
-                        hi |= (h >> c) & 0x10101010u;
-                    }
-                    a[rr] = lo;
-                    a[2 + rr] = hi;
-                }
-            }
-            const uint2 bf = A.frag[kb * 32 + lane];
-            const int4 sc = A.sc[kb * 4 + c];
-            int dd[4];
-            mma_i8<DT == Q8_0>(a, bf, make_int2(sc.x, sc.y), dd);
-            const float2 da = make_float2(__int_as_float(sc.z), __int_as_float(sc.w));
-            const float db0 = (b & 1) ? dr0[b >> 1].y : dr0[b >> 1].x;
-            const float db1 = (b & 1) ? dr1[b >> 1].y : dr1[b >> 1].x;
-            // S exactly (integer < 2^22 below 1.5*2^23); acc += (d_a*d_b)*S
-            const float2 s01 = __fadd2_rn(make_float2(__int_as_float(dd[0]), __int_as_float(dd[1])), nmag);
-            const float2 s23 = __fadd2_rn(make_float2(__int_as_float(dd[2]), __int_as_float(dd[3])), nmag);
-            a01 = __ffma2_rn(__fmul2_rn(da, make_float2(db0, db0)), s01, a01);
-            a23 = __ffma2_rn(__fmul2_rn(da, make_float2(db1, db1)), s23, a23);
-            if (has_min(DT)) {
-                const float2 ua = *reinterpret_cast<const float2*>(A.ua + kb * 8 + 2 * c);
-                const float mb0 = (b & 1) ? mr0[b >> 1].y : mr0[b >> 1].x;
-                const float mb1 = (b & 1) ? mr1[b >> 1].y : mr1[b >> 1].x;
-                a01 = __ffma2_rn(ua, make_float2(mb0, mb0), a01);
-                a23 = __ffma2_rn(ua, make_float2(mb1, mb1), a23);
-            }
-        }
-    }
-}
-
-__device__ __forceinline__ void mma_store(float2 a01, float2 a23, int T, int lane, int M, int N,
-                                          const float* __restrict__ bias, float* __restrict__ y) {
-    const int g = lane >> 2, c = lane & 3;
-    const float v[4] = {a01.x, a01.y, a23.x, a23.y};
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        const int row = T * 16 + g + ((i & 2) ? 8 : 0), col = 2 * c + (i & 1);
-        if (row < N && col < M) y[size_t(col) * N + row] = bias ? __fadd_rn(v[i], __ldg(bias + row)) : v[i];
-    }
-}
-
-// PF groups in flight per warp (4 or 8, chosen by the launcher from the
-// shared memory left after the activations).
-template <int DT, int KS, int PF>
-__global__ void __launch_bounds__(GM_THREADS, 2)
+// PF groups in flight per warp; NT n-tiles of 8 activation rows per launch
+// (M <= 8*NT).
+template <int DT, int KS, int PF, int NT>
+__global__ void __launch_bounds__(GM_THREADS, 1)
     k_gemv_mma(const uint8_t* __restrict__ qs, const uint32_t* __restrict__ qh, const uint16_t* __restrict__ dp,
                const uint16_t* __restrict__ mp, const int8_t* __restrict__ q8, const float* __restrict__ da,
                const int32_t* __restrict__ sa, const float* __restrict__ ua, int M, int N, int K,
@@ -672,42 +687,44 @@ __global__ void __launch_bounds__(GM_THREADS, 2)
     const int tiles = (N + 15) / 16;
 
     extern __shared__ __align__(16) uint8_t smem[];
-    uint2* s_frag = reinterpret_cast<uint2*>(smem);                       // [nb4][32]
-    int* s_sc = reinterpret_cast<int*>(smem + size_t(nb4) * 256);          // [nb4][4 lanes][seed, seed, d_a, d_a]
-    float* s_ua = reinterpret_cast<float*>(s_sc + nb4 * 16);               // [nb4][8]
-    float* s_red = s_ua + nb4 * 8;                                         // [8 warps][32 lanes][4]
-    uint8_t* ring = reinterpret_cast<uint8_t*>(s_red + WARPS * 32 * 4) + size_t(warp) * pf * Slot<DT>::BYTES;
+    uint2* s_frag = reinterpret_cast<uint2*>(smem);                          // [nb4][NT][32]
+    int* s_sc = reinterpret_cast<int*>(smem + size_t(nb4) * NT * 256);        // [nb4][NT][4 lanes][seed, seed, d_a, d_a]
+    float* s_ua = reinterpret_cast<float*>(s_sc + nb4 * NT * 16);             // [nb4][NT][8]
+    float* s_red = s_ua + nb4 * NT * 8;                                       // [8 warps][32 lanes][NT][4]
+    uint8_t* ring = reinterpret_cast<uint8_t*>(s_red + WARPS * 32 * 4 * NT) + size_t(warp) * pf * Slot<DT>::BYTES;
     const uint32_t ring_s = uint32_t(__cvta_generic_to_shared(ring));
     const MmaActs A{s_frag, reinterpret_cast<const int4*>(s_sc), s_ua};
 
     auto stage = [&]() {
         pdl_wait();
         // Only entries of existing rows and blocks are copied: the other
-        // columns' sums are never stored and pad blocks are skipped.
+        // columns' sums are never stored.
         for (int i = tid; i < nb * M * 4; i += GM_THREADS) {
             const int cc = i & 3, row = (i >> 2) % M, kb = (i >> 2) / M;
             const int8_t* p = q8 + size_t(row) * K + kb * QK + 4 * cc;
-            uint2* dst = s_frag + kb * 32 + row * 4 + cc;
+            uint2* dst = s_frag + (kb * NT + (row >> 3)) * 32 + (row & 7) * 4 + cc;
             cp_async4(&dst->x, p, true);
             cp_async4(&dst->y, p + 16, true);
         }
-        // record of (kb, act row col): s_sc[(kb*4 + col/2)*4 + {0,1} seed, {2,3} d_a]
-        auto sc_at = [&](int kb, int col, int f) { return s_sc + (kb * 4 + (col >> 1)) * 4 + 2 * f + (col & 1); };
+        // record of (kb, act row col): {0,1} seed, {2,3} d_a of rows 2c, 2c+1
+        auto sc_at = [&](int kb, int col, int f) {
+            return s_sc + ((kb * NT + (col >> 3)) * 4 + ((col & 7) >> 1)) * 4 + 2 * f + (col & 1);
+        };
         for (int i = tid; i < nb * M; i += GM_THREADS) {
             const int col = i % M, kb = i / M;
             const size_t o = size_t(col) * nb + kb;
             if (code_offset(DT)) cp_async4(sc_at(kb, col, 0), sa + o, true);
             cp_async4(sc_at(kb, col, 1), da + o, true);
-            if (has_min(DT)) cp_async4(s_ua + kb * 8 + col, ua + o, true);
+            if (has_min(DT)) cp_async4(s_ua + (kb * NT + (col >> 3)) * 8 + (col & 7), ua + o, true);
         }
         // Pad blocks: zero codes, zero scales, seed 1.5*2^23 -> add 0.
-        for (int i = tid; i < (nb4 - nb) * 32; i += GM_THREADS) {
-            const int kb = nb + i / 32, l = i & 31;
-            s_frag[kb * 32 + l] = make_uint2(0u, 0u);
+        for (int i = tid; i < (nb4 - nb) * NT * 32; i += GM_THREADS) {
+            const int kb = nb + i / (NT * 32), nt = (i / 32) % NT, l = i & 31;
+            s_frag[(kb * NT + nt) * 32 + l] = make_uint2(0u, 0u);
             if (l < 8) {
-                *sc_at(kb, l, 0) = int(MAGIC_BITS);
-                *reinterpret_cast<float*>(sc_at(kb, l, 1)) = 0.f;
-                s_ua[kb * 8 + l] = 0.f;
+                *sc_at(kb, nt * 8 + l, 0) = int(MAGIC_BITS);
+                *reinterpret_cast<float*>(sc_at(kb, nt * 8 + l, 1)) = 0.f;
+                s_ua[(kb * NT + nt) * 8 + l] = 0.f;
             }
         }
         cp_async_wait_all();
@@ -723,7 +740,11 @@ __global__ void __launch_bounds__(GM_THREADS, 2)
     // pf places ahead (or commit an empty group, so the pending count stays
     // pf - 1), then run the block MMAs.
     MmaGroup<DT> cur;
-    float2 a01, a23;
+    float2 a01[NT], a23[NT];
+    auto zero = [&]() {
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) a01[nt] = a23[nt] = make_float2(0.f, 0.f);
+    };
     auto consume = [&](int u, int G, bool refill, int nT, int nG) {
         asm volatile("cp.async.wait_group %0;" ::"n"(PF - 1) : "memory");
         __syncwarp();
@@ -731,7 +752,20 @@ __global__ void __launch_bounds__(GM_THREADS, 2)
         __syncwarp();
         if (refill) ring_issue<DT>(qs, qh, dp, mp, N, nb4, nT, nG, lane, ring_s + u * Slot<DT>::BYTES);
         cp_async_commit();
-        mma_compute<DT>(cur, A, G, nb, lane, a01, a23);
+        mma_compute<DT, NT>(cur, A, G, lane, a01, a23);
+    };
+    float4* red_me = reinterpret_cast<float4*>(s_red) + (warp * 32 + lane) * NT;
+    auto park = [&](float4* dst) {
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) dst[nt] = make_float4(a01[nt].x, a01[nt].y, a23[nt].x, a23[nt].y);
+    };
+    auto add_parked = [&](const float4* src) {
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+            const float4 t = src[nt];
+            a01[nt] = __fadd2_rn(a01[nt], make_float2(t.x, t.y));
+            a23[nt] = __fadd2_rn(a23[nt], make_float2(t.z, t.w));
+        }
     };
 
     if (KS == 1) {
@@ -744,14 +778,14 @@ __global__ void __launch_bounds__(GM_THREADS, 2)
         // head's owner stores head + tail.  Fewer tiles: whole tiles.
         const int t_lo = int(int64_t(blockIdx.x) * tiles / gridDim.x);
         const int t_hi = int(int64_t(blockIdx.x + 1) * tiles / gridDim.x);
-        const int nt = t_hi - t_lo, items = nt * ng;
+        const int nt_ = t_hi - t_lo, items = nt_ * ng;
         int i_lo, i_hi;
-        if (nt >= WARPS) {
+        if (nt_ >= WARPS) {
             i_lo = warp * items / WARPS;
             i_hi = (warp + 1) * items / WARPS;
         } else {
-            i_lo = min(warp, nt) * ng;
-            i_hi = min(warp + 1, nt) * ng;
+            i_lo = min(warp, nt_) * ng;
+            i_hi = min(warp + 1, nt_) * ng;
         }
         const int n_items = i_hi - i_lo;
         int lt = t_lo + i_lo / ng, lG = i_lo % ng;
@@ -765,32 +799,28 @@ __global__ void __launch_bounds__(GM_THREADS, 2)
             cp_async_commit();
         }
         stage();
-        a01 = a23 = make_float2(0.f, 0.f);
+        zero();
         for (int i0 = 0; i0 < n_items; i0 += PF) {
 #pragma unroll
-        for (int u = 0; u < PF; ++u) {
-            const int i = i0 + u;
-            if (i >= n_items) break;
-            const bool refill = i + pf < n_items;
-            consume(u, cG, refill, lt, lG);
-            if (refill && ++lG == ng) { lG = 0; ++lt; }
-            if (++cG == ng) {
-                if (ct == shared_first)
-                    *reinterpret_cast<float4*>(s_red + (warp * 32 + lane) * 4) = make_float4(a01.x, a01.y, a23.x, a23.y);
-                else
-                    mma_store(a01, a23, ct, lane, M, N, bias, y);
-                a01 = a23 = make_float2(0.f, 0.f);
-                cG = 0;
-                ++ct;
+            for (int u = 0; u < PF; ++u) {
+                const int i = i0 + u;
+                if (i >= n_items) break;
+                const bool refill = i + pf < n_items;
+                consume(u, cG, refill, lt, lG);
+                if (refill && ++lG == ng) { lG = 0; ++lt; }
+                if (++cG == ng) {
+                    if (ct == shared_first) park(red_me);
+                    else mma_store<NT>(a01, a23, ct, lane, M, N, bias, y);
+                    zero();
+                    cG = 0;
+                    ++ct;
+                }
             }
-        }
         }
         __syncthreads();
         if (n_items > 0 && cG != 0) {   // this warp holds the head of tile ct; warp + 1 its tail
-            const float4 t = *reinterpret_cast<const float4*>(s_red + ((warp + 1) * 32 + lane) * 4);
-            a01 = __fadd2_rn(a01, make_float2(t.x, t.y));
-            a23 = __fadd2_rn(a23, make_float2(t.z, t.w));
-            mma_store(a01, a23, ct, lane, M, N, bias, y);
+            add_parked(reinterpret_cast<const float4*>(s_red) + ((warp + 1) * 32 + lane) * NT);
+            mma_store<NT>(a01, a23, ct, lane, M, N, bias, y);
         }
         asm volatile("cp.async.wait_group 0;" ::: "memory");
         return;
@@ -809,7 +839,7 @@ __global__ void __launch_bounds__(GM_THREADS, 2)
             cp_async_commit();
         }
         if (first) stage();
-        a01 = a23 = make_float2(0.f, 0.f);
+        zero();
         for (int i0 = 0; i0 < gn; i0 += PF) {
 #pragma unroll
             for (int u = 0; u < PF; ++u) {
@@ -818,16 +848,12 @@ __global__ void __launch_bounds__(GM_THREADS, 2)
                 consume(u, g0 + i, i + pf < gn, T, g0 + i + pf);
             }
         }
-        *reinterpret_cast<float4*>(s_red + (warp * 32 + lane) * 4) = make_float4(a01.x, a01.y, a23.x, a23.y);
+        park(red_me);
         __syncthreads();
         if (ks == 0) {
 #pragma unroll
-            for (int s2 = 1; s2 < KS; ++s2) {
-                const float4 p = *reinterpret_cast<const float4*>(s_red + ((warp + s2) * 32 + lane) * 4);
-                a01 = __fadd2_rn(a01, make_float2(p.x, p.y));
-                a23 = __fadd2_rn(a23, make_float2(p.z, p.w));
-            }
-            mma_store(a01, a23, T, lane, M, N, bias, y);
+            for (int s2 = 1; s2 < KS; ++s2) add_parked(reinterpret_cast<const float4*>(s_red) + ((warp + s2) * 32 + lane) * NT);
+            mma_store<NT>(a01, a23, T, lane, M, N, bias, y);
         }
         __syncthreads();
     }
@@ -1132,16 +1158,14 @@ struct GemvI8F {
     }
 };
 
-// Shared memory of k_gemv_mma: per block B fragments (256 B), seed/d_a
-// records (64 B), d_a*sum(q_a) (32 B); the K-slice reduction buffer; then
-// each warp's weight ring.
-inline size_t gemv_mma_act_smem(int nb) { return size_t(round4(nb)) * 352 + 4096; }
-
-template <int DT, int KS, int PF>
-cudaError_t gemv_mma_go(const ActsView& v, const Weight& w, const float* bias, float* y, cudaStream_t s,
-                        int per_sm_target) {
-    auto kern = k_gemv_mma<DT, KS, PF>;
-    const size_t smem = gemv_mma_act_smem(w.nb) + size_t(PF) * Slot<DT>::BYTES * (GM_THREADS / 32);
+// Ring depth, n-tiles and grid.  The grid does not depend on NT or on the
+// occupancy (two CTAs per SM are assumed for the cap), so a row's result
+// is the same for every M: the K-split and the KS == 1 tile ranges depend
+// on N, K and the SM count only.
+template <int DT, int KS, int PF, int NT>
+cudaError_t gemv_mma_go(const ActsView& v, const Weight& w, const float* bias, float* y, cudaStream_t s) {
+    auto kern = k_gemv_mma<DT, KS, PF, NT>;
+    const size_t smem = gemv_mma_act_smem(w.nb, NT) + size_t(PF) * Slot<DT>::BYTES * (GM_THREADS / 32);
     int dev = 0, sms = 148;
     cudaGetDevice(&dev);
     static unsigned attr_dev_mask = 0;  // one bit per device with the attribute set
@@ -1155,23 +1179,39 @@ cudaError_t gemv_mma_go(const ActsView& v, const Weight& w, const float* bias, f
     // KS == 1: one contiguous range of at least 8 tiles per CTA (see the
     // kernel); KS > 1: grid-stride over groups of tpc tiles.
     unsigned grid = KS == 1 ? unsigned(tiles / (GM_THREADS / 32)) : unsigned((tiles + tpc - 1) / tpc);
-    const unsigned cap = unsigned(sms) * unsigned(per_sm_target);
+    const unsigned cap = unsigned(sms) * 2u;
     grid = grid < 1 ? 1 : (grid > cap ? cap : grid);
     return launch_pdl(kern, dim3(grid), dim3(GM_THREADS), smem, s, w.qs, w.qh, w.d, w.m, v.q8, v.d, v.sum, v.u, v.m,
                       w.n, w.k, bias, y);
 }
 
-// Ring depth and CTAs per SM: 8 groups per warp with two CTAs per SM when
-// that fits in half of the SM's shared memory, else 4 groups (two CTAs,
-// then one).
+constexpr size_t GEMV_SMEM_MAX = 224 * 1024;
+
+template <int DT>
+size_t gemv_slot8() { return size_t(Slot<DT>::BYTES) * (GM_THREADS / 32); }
+
+// The most n-tiles (of 1, 2, 4, 8) whose staging fits with a 4-deep ring.
+template <int DT>
+int gemv_mma_nt_max(int nb) {
+    for (int nt = 8; nt > 1; nt >>= 1)
+        if (gemv_mma_act_smem(nb, nt) + 4 * gemv_slot8<DT>() <= GEMV_SMEM_MAX) return nt;
+    return 1;
+}
+
 template <int DT, int KS>
 cudaError_t gemv_mma_launch(const ActsView& v, const Weight& w, const float* bias, float* y, cudaStream_t s) {
-    const size_t act = gemv_mma_act_smem(w.nb), slot8 = size_t(Slot<DT>::BYTES) * (GM_THREADS / 32);
-    constexpr size_t HALF = 112 * 1024, FULL = 224 * 1024;
-    if (act + 8 * slot8 <= HALF) return gemv_mma_go<DT, KS, 8>(v, w, bias, y, s, 2);
-    if (act + 4 * slot8 <= HALF) return gemv_mma_go<DT, KS, 4>(v, w, bias, y, s, 2);
-    if (act + 4 * slot8 <= FULL) return gemv_mma_go<DT, KS, 4>(v, w, bias, y, s, 1);
-    return cudaErrorInvalidValue;
+    const int need = (v.m + 7) / 8;
+    const int nt = need <= 1 ? 1 : need <= 2 ? 2 : need <= 4 ? 4 : 8;
+    if (nt > gemv_mma_nt_max<DT>(w.nb)) return cudaErrorInvalidValue;
+    switch (nt) {
+        case 1:
+            if (gemv_mma_act_smem(w.nb, 1) + 8 * gemv_slot8<DT>() <= GEMV_SMEM_MAX / 2)
+                return gemv_mma_go<DT, KS, 8, 1>(v, w, bias, y, s);
+            return gemv_mma_go<DT, KS, 4, 1>(v, w, bias, y, s);
+        case 2: return gemv_mma_go<DT, KS, 4, 2>(v, w, bias, y, s);
+        case 4: return gemv_mma_go<DT, KS, 4, 4>(v, w, bias, y, s);
+        default: return gemv_mma_go<DT, KS, 4, 8>(v, w, bias, y, s);
+    }
 }
 
 // K-split of k_gemv_mma: keep splitting while the GPU would hold fewer
@@ -1196,6 +1236,14 @@ struct GemvMmaF {
             case 4: return gemv_mma_launch<DT, 4>(v, w, bias, y, s);
             default: return gemv_mma_launch<DT, 8>(v, w, bias, y, s);
         }
+    }
+};
+
+template <int DT>
+struct GemvRowsF {
+    static cudaError_t run(int nb, int* out) {
+        *out = 8 * gemv_mma_nt_max<DT>(nb);
+        return cudaSuccess;
     }
 };
 
@@ -1259,16 +1307,38 @@ cudaError_t launch_block_dots(const ActsView& v, const Weight& w, int32_t* S, cu
 
 void set_gemv_kind(int kind) { t_gemv_kind = kind; }
 
+int gemv_rows_per_launch(int dtype, int k) {
+    int r = 8;
+    by_dtype<GemvRowsF>(dtype, k / QK, &r);
+    return r;
+}
+
 cudaError_t launch_gemv_i8(const ActsView& v, const Weight& w, const float* bias, float* y, cudaStream_t s) {
     if (v.m <= 0 || w.n <= 0) return cudaSuccess;
-    // The integer-MMA kernel serves every m <= 8 (one instruction per block
-    // for 16 x 8 dots, cost flat in m), so a row's result never depends on
-    // m; the dp4a kernel is kept as an alternative (tests, benchmarks).
-    // The MMA kernel addresses the planes with 32-bit offsets.
+    // The integer-MMA kernel serves every m (one instruction per block for
+    // 16 x 8 dots, up to 64 rows per launch), so a row's result never
+    // depends on m; the dp4a kernel (8 rows per launch) is kept as an
+    // alternative (tests, benchmarks).  The MMA kernel addresses the planes
+    // with 32-bit offsets.
     const int kind = t_gemv_kind ? t_gemv_kind : 2;
-    if (kind == 2 && uint64_t(w.n) * uint64_t(round4(w.nb)) * uint64_t(qs_bytes(w.dtype)) < (uint64_t(1) << 32))
-        return by_dtype<GemvMmaF>(w.dtype, v, w, bias, y, s);
-    return by_dtype<GemvI8F>(w.dtype, v, w, bias, y, s);
+    const bool mma =
+        kind == 2 && uint64_t(w.n) * uint64_t(round4(w.nb)) * uint64_t(qs_bytes(w.dtype)) < (uint64_t(1) << 32);
+    // Rows in launches of up to `per`: after the first launch the weights
+    // come from L2 for every weight that fits there.
+    const int per = mma ? gemv_rows_per_launch(w.dtype, w.k) : GEMV_MAX_M;
+    for (int m0 = 0; m0 < v.m; m0 += per) {
+        ActsView c = v;
+        c.m = v.m - m0 < per ? v.m - m0 : per;
+        c.q8 = v.q8 + size_t(m0) * v.k;
+        c.d = v.d + size_t(m0) * v.nb;
+        c.sum = v.sum + size_t(m0) * v.nb;
+        c.u = v.u + size_t(m0) * v.nb;
+        float* yc = y + size_t(m0) * w.n;
+        const cudaError_t e = mma ? by_dtype<GemvMmaF>(w.dtype, c, w, bias, yc, s)
+                                  : by_dtype<GemvI8F>(w.dtype, c, w, bias, yc, s);
+        if (e != cudaSuccess) return e;
+    }
+    return cudaSuccess;
 }
 
 cudaError_t launch_gemv_f32(const float* a, int m, const Weight& w, const float* bias, float* y, cudaStream_t s) {

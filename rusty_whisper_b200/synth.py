@@ -203,7 +203,8 @@ MODEL_CODE_SCALES = {
 }
 
 
-def encoder_tensors(n_mels: int, n_ctx: int, n_state: int, n_layer: int, dtype: int, seed: int) -> dict:
+def encoder_tensors(n_mels: int, n_ctx: int, n_state: int, n_layer: int, dtype: int, seed: int,
+                    reuse_layers: bool = False) -> dict:
     """Random-init whisper encoder tensors by their whisper.cpp names
     (encoder.rs:130-234): dense entries are f32 arrays, the six linears of
     each block ``(dtype, raw, n, k)``.  Weights ~ N(0, 0.02); Q5_1 and Q8_0
@@ -211,7 +212,9 @@ def encoder_tensors(n_mels: int, n_ctx: int, n_state: int, n_layer: int, dtype: 
     quantizers (BASELINE config 3 is Q5_1), the other formats get random
     codes with block scales giving a similar spread (MODEL_CODE_SCALES);
     LayerNorm weights 1 + N(0, 0.02);
-    positions are whisper's sinusoids."""
+    positions are whisper's sinusoids.  With ``reuse_layers`` every block
+    gets block 0's values (each still becomes its own device copy; for
+    throughput runs of deep models, where drawing every layer is slow)."""
     t = {}
     ctr = [seed * 1000]
 
@@ -238,6 +241,10 @@ def encoder_tensors(n_mels: int, n_ctx: int, n_state: int, n_layer: int, dtype: 
     t["encoder.positional_embedding"] = np.concatenate([np.sin(ang), np.cos(ang)], axis=1).astype(np.float32)
     for l in range(n_layer):
         p = f"encoder.blocks.{l}"
+        if reuse_layers and l > 0:
+            for key in [x for x in t if x.startswith("encoder.blocks.0.")]:
+                t[key.replace("encoder.blocks.0.", f"{p}.", 1)] = t[key]
+            continue
         t[f"{p}.attn_ln.weight"] = nrm(n_state, mean=1.0)
         t[f"{p}.attn_ln.bias"] = nrm(n_state)
         t[f"{p}.attn.query.weight"] = lin(n_state, n_state)
@@ -264,7 +271,8 @@ def encoder_mel(n_windows: int, n_mels: int, n_frames: int, seed: int) -> np.nda
     return np.clip(x, -1.5, 1.5).astype(np.float32).reshape(n_windows, n_mels, n_frames)
 
 
-def decoder_tensors(n_vocab: int, n_ctx: int, n_state: int, n_layer: int, dtype: int, seed: int) -> dict:
+def decoder_tensors(n_vocab: int, n_ctx: int, n_state: int, n_layer: int, dtype: int, seed: int,
+                    reuse_layers: bool = False) -> dict:
     """Random-init whisper decoder tensors by their whisper.cpp names
     (decoder.rs:36-321), same conventions as :func:`encoder_tensors`; the
     token embedding (also the tied logits matrix) is quantized like the
@@ -288,6 +296,10 @@ def decoder_tensors(n_vocab: int, n_ctx: int, n_state: int, n_layer: int, dtype:
     t["decoder.positional_embedding"] = nrm(n_ctx, n_state)
     for l in range(n_layer):
         p = f"decoder.blocks.{l}"
+        if reuse_layers and l > 0:
+            for key in [x for x in t if x.startswith("decoder.blocks.0.")]:
+                t[key.replace("decoder.blocks.0.", f"{p}.", 1)] = t[key]
+            continue
         for ln in ("attn_ln", "cross_attn_ln", "mlp_ln"):
             t[f"{p}.{ln}.weight"] = nrm(n_state, mean=1.0)
             t[f"{p}.{ln}.bias"] = nrm(n_state)

@@ -106,9 +106,13 @@ def test_matmul_int8_matches_oracle(rq, orc, dtype, m, k, n):
 @pytest.mark.parametrize("kind", [1, 2])
 @pytest.mark.parametrize("dtype", FORMATS)
 @pytest.mark.parametrize("m,k,n", [(1, 1024, 1000), (2, 96, 41), (5, 768, 3072), (7, 160, 333), (8, 3072, 768),
-                                   (3, 1280, 5120), (5, 4096, 257), (6, 8192, 40)])
+                                   (3, 1280, 5120), (5, 4096, 257), (6, 8192, 40), (13, 1024, 700), (40, 256, 300),
+                                   (64, 1280, 1280), (80, 1024, 1024), (200, 5120, 256)])
 def test_gemv_kernels_match_oracle(rq, orc, kind, dtype, m, k, n):
-    """Both GEMV kernels (dp4a, integer MMA) at every K-split and tail."""
+    """Both GEMV kernels (dp4a, integer MMA) at every K-split and tail, one
+    to several launches of rows."""
+    if m * n * k > 100_000_000 and kind == 1:
+        pytest.skip("dp4a at this size is covered by the smaller cases")
     a, raw = _case(dtype, m, k, n, 17 * dtype + m + k + kind)
     w = rq.QTensor([n, k], dtype, raw)
     rq.set_gemv_kernel(kind)
@@ -169,19 +173,20 @@ def test_dequant_rows_bit_exact(rq, orc, dtype):
 
 def test_batch_invariance(rq):
     """Row results do not depend on M (quant.rs:1372-1384), within each
-    kernel family: the GEMV (M <= 8) and the tensor-core GEMM (M > 8)."""
+    kernel family: the GEMV family (M <= 256, integer-MMA launches of up to
+    64 rows) and the tensor-core GEMM (M > 256)."""
     import torch
     from rusty_whisper_b200 import synth
     for dtype in FORMATS:
         k, n = 512, 1200
         w = rq.QTensor([n, k], dtype, synth.random_blocks(dtype, n, k, 21))
-        a = cuda(synth.normal(22, 300 * k).reshape(300, k))
-        y8 = rq.matmul_t_q(a[:8], w)
-        for mm in (1, 3, 5):
-            assert torch.equal(rq.matmul_t_q(a[:mm], w), y8[:mm])
-        y300 = rq.matmul_t_q(a, w)
-        for mm in (9, 128, 129, 256):
-            assert torch.equal(rq.matmul_t_q(a[:mm], w), y300[:mm])
+        a = cuda(synth.normal(22, 700 * k).reshape(700, k))
+        y256 = rq.matmul_t_q(a[:256], w)
+        for mm in (1, 3, 8, 9, 17, 64, 65, 200):
+            assert torch.equal(rq.matmul_t_q(a[:mm], w), y256[:mm])
+        y700 = rq.matmul_t_q(a, w)
+        for mm in (257, 300, 640):
+            assert torch.equal(rq.matmul_t_q(a[:mm], w), y700[:mm])
 
 
 def test_bias_and_host_path(rq, orc):
