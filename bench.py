@@ -240,6 +240,8 @@ def run_ours(args, rank, world, local_rank):
     e2e = run_e2e(args, dev, quant, W, acts_np, world) if args.only == "all" else None
     frontend = run_frontend(args, dev, hbm_peak, stream, rank, world) if args.only == "all" else None
     enc = run_encoder(args, dev, tc_peak, stream, rank, world) if args.only == "all" else None
+    dec = run_decoder_beams(args, dev, hbm_peak, stream, rank, world) if args.only == "all" else None
+    large = run_large_v3(args, dev, stream, rank, world) if args.only == "all" else None
     clk.__exit__(None, None, None)
 
     if rank != 0:
@@ -265,6 +267,8 @@ def run_ours(args, rank, world, local_rank):
         "gemv": gemv,
         "frontend": frontend,
         "encoder": enc,
+        "decoder_beams": dec,
+        "large_v3_e2e": large,
         "e2e": e2e,
         "clocks": clk.summary(),
     }

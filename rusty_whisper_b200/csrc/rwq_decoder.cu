@@ -23,6 +23,7 @@
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <map>
 #include <mutex>
@@ -66,6 +67,10 @@ struct DLayer {
     rwq_qtensor *q = nullptr, *k = nullptr, *v = nullptr, *o = nullptr;
     rwq_qtensor *xq = nullptr, *xk = nullptr, *xv = nullptr, *xo = nullptr;
     rwq_qtensor *fc1 = nullptr, *fc2 = nullptr;
+    // device pointers of the dense tensors, resolved once per begin
+    const float *attn_ln_w = nullptr, *attn_ln_b = nullptr, *q_b = nullptr, *v_b = nullptr, *o_b = nullptr;
+    const float *x_ln_w = nullptr, *x_ln_b = nullptr, *xq_b = nullptr, *xo_b = nullptr;
+    const float *mlp_ln_w = nullptr, *mlp_ln_b = nullptr, *fc1_b = nullptr, *fc2_b = nullptr;
 };
 
 const char* const kDenseLayer[] = {"attn_ln.weight", "attn_ln.bias", "attn.query.bias", "attn.value.bias",
@@ -92,7 +97,18 @@ struct rwq_decoder {
     float *x = nullptr, *tmp = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *att = nullptr, *h = nullptr,
           *logits = nullptr;
     int32_t* best = nullptr;
+    int* dpos = nullptr;           // the decode position, on the device
+    int32_t* tok_in = nullptr;     // this step's tokens (graph input)
     rwq::ActsView gemv, gemm;
+    // One captured step per (output mode, limit); a mode runs eagerly once
+    // (first-use set-up happens there) before it is captured.
+    std::map<std::pair<int, int>, cudaGraphExec_t> graphs;
+    std::map<std::pair<int, int>, int> eager_runs;
+    // Steps run on this decoder's own stream (graphs cannot be captured on
+    // the legacy default stream), ordered after and before the caller's
+    // stream by two events.
+    cudaStream_t gs = nullptr;
+    cudaEvent_t ev_in = nullptr, ev_out = nullptr;
     std::mutex mu;
 };
 
@@ -171,6 +187,8 @@ size_t layout_state(rwq_decoder* d, int S, int W, int n_audio, int n_groups, uin
     d->h = reinterpret_cast<float*>(take(S * F * 4));
     d->logits = reinterpret_cast<float*>(take(S * size_t(d->n_vocab) * 4));
     d->best = reinterpret_cast<int32_t*>(take(size_t(S) * 4));
+    d->dpos = reinterpret_cast<int*>(take(4));
+    d->tok_in = reinterpret_cast<int32_t*>(take(size_t(S) * 4));
     rwq::ActsView& g = d->gemv;
     g = rwq::ActsView();
     g.m = S;
@@ -195,18 +213,11 @@ rwq::ActsView with_k(rwq::ActsView v, int k) {
 }
 
 // Row transform + quantize into the layout the linears of this step read.
-int rows(rwq_decoder* d, int mode, const float* x, const float* add, float* xout, const char* ln, int k,
-         cudaStream_t s, int layer = -1) {
+int rows(rwq_decoder* d, int mode, const float* x, const float* add, float* xout, const float* w, const float* b, int k,
+         cudaStream_t s) {
     const int S = d->n_streams;
     const bool gemm = S > rwq::GEMV_FAMILY_MAX_M;
     const rwq::ActsView a = with_k(gemm ? d->gemm : d->gemv, k);
-    const float* w = nullptr;
-    const float* b = nullptr;
-    if (ln) {
-        const std::string base = layer >= 0 ? lname(layer, ln) : std::string(ln);
-        w = d->dense[base + ".weight"];
-        b = d->dense[base + ".bias"];
-    }
     DEC_CUDA(rwq::launch_rows_quant_v(mode, x, add, xout, w, b, S, k, gemm ? &a : nullptr, gemm ? nullptr : &a, nullptr,
                                       s),
              "decoder row transform");
@@ -217,6 +228,107 @@ int linear(rwq_decoder* d, rwq_qtensor* w, const float* bias, float* out, cudaSt
     const bool gemm = d->n_streams > rwq::GEMV_FAMILY_MAX_M;
     const rwq::ActsView a = with_k(gemm ? d->gemm : d->gemv, rwq::weight_of(w).k);
     return rwq::linear_acts(a, gemm, w, bias, out, s);
+}
+
+void drop_graphs(rwq_decoder* d) {
+    for (auto& kv : d->graphs) cudaGraphExecDestroy(kv.second);
+    d->graphs.clear();
+    d->eager_runs.clear();
+}
+
+bool graphs_enabled() {
+    static const bool on = [] {
+        const char* v = std::getenv("RWQ_DECODER_GRAPHS");
+        return !(v && v[0] == '0');
+    }();
+    return on;
+}
+
+// The kernels of one decode position (decoder.rs:102-206), reading the
+// tokens from d->tok_in and the position from d->dpos; mode bit 0: tied
+// logits into d->logits, bit 1: greedy choice into d->best.
+int issue_step(rwq_decoder* d, int mode, int32_t limit, cudaStream_t s) {
+    const int S = d->n_streams, D = d->n_state, H = d->n_head, F = d->n_ff;
+    DEC_CUDA(rwq::launch_embed(rwq::weight_of(d->emb), d->tok_in, S, d->dense["decoder.positional_embedding"], d->dpos,
+                               d->x, s),
+             "embed");
+    const size_t self_layer = size_t(S) * H * d->n_ctx * 64, cross_layer = size_t(d->n_windows) * H * d->n_audio * 64;
+    for (int l = 0; l < d->n_layer; ++l) {
+        const DLayer& L = d->layers[size_t(l)];
+        // causal self-attention over the cache (decoder.rs:140-171)
+        DEC_RC(rows(d, l ? rwq::RQ_ADD_LN : rwq::RQ_LN, d->x, d->tmp, d->x, L.attn_ln_w, L.attn_ln_b, D, s));
+        DEC_RC(linear(d, L.q, L.q_b, d->q, s));
+        DEC_RC(linear(d, L.k, nullptr, d->k, s));
+        DEC_RC(linear(d, L.v, L.v_b, d->v, s));
+        __half* kc = d->self_k + size_t(l) * self_layer;
+        __half* vc = d->self_v + size_t(l) * self_layer;
+        DEC_CUDA(rwq::launch_kv_append(d->k, d->v, S, H, d->n_ctx, d->dpos, kc, vc, s), "kv append");
+        DEC_CUDA(rwq::launch_attn_dec(d->q, kc, vc, size_t(d->n_ctx) * 64, d->n_ctx, d->dpos, H, S, d->self_kv,
+                                      d->self_off, d->self_kv, d->att, s),
+                 "self attention");
+        DEC_RC(rows(d, rwq::RQ_PLAIN, d->att, nullptr, nullptr, nullptr, nullptr, D, s));
+        DEC_RC(linear(d, L.o, L.o_b, d->tmp, s));
+        // cross-attention to the window's K/V (decoder.rs:173-188)
+        DEC_RC(rows(d, rwq::RQ_ADD_LN, d->x, d->tmp, d->x, L.x_ln_w, L.x_ln_b, D, s));
+        DEC_RC(linear(d, L.xq, L.xq_b, d->q, s));
+        DEC_CUDA(rwq::launch_attn_dec(d->q, d->cross_k + size_t(l) * cross_layer, d->cross_v + size_t(l) * cross_layer,
+                                      size_t(d->n_audio) * 64, d->n_audio, nullptr, H, d->n_cross_groups, d->cross_kv,
+                                      d->cross_off, d->cross_streams, d->att, s),
+                 "cross attention");
+        DEC_RC(rows(d, rwq::RQ_PLAIN, d->att, nullptr, nullptr, nullptr, nullptr, D, s));
+        DEC_RC(linear(d, L.xo, L.xo_b, d->tmp, s));
+        // MLP (encoder.rs:154-172)
+        DEC_RC(rows(d, rwq::RQ_ADD_LN, d->x, d->tmp, d->x, L.mlp_ln_w, L.mlp_ln_b, D, s));
+        DEC_RC(linear(d, L.fc1, L.fc1_b, d->h, s));
+        DEC_RC(rows(d, rwq::RQ_GELU, d->h, nullptr, nullptr, nullptr, nullptr, F, s));
+        DEC_RC(linear(d, L.fc2, L.fc2_b, d->tmp, s));
+    }
+    if (mode) {
+        // final LN (decoder.rs:200-204), tied logits (decoder.rs:315-321)
+        DEC_RC(rows(d, d->n_layer ? rwq::RQ_ADD_LN : rwq::RQ_LN, d->x, d->tmp, d->x, d->dense["decoder.ln.weight"],
+                    d->dense["decoder.ln.bias"], D, s));
+        DEC_RC(linear(d, d->emb, nullptr, d->logits, s));
+        if (mode & 2) DEC_CUDA(rwq::launch_argmax(d->logits, S, d->n_vocab, limit, d->best, s), "argmax");
+    }
+    DEC_CUDA(rwq::launch_pos_advance(d->dpos, s), "position advance");
+    return RWQ_OK;
+}
+
+// Run one position: replay its graph, capture it (second run of a mode),
+// or issue it eagerly.
+int run_step(rwq_decoder* d, int mode, int32_t limit, cudaStream_t s) {
+    const std::pair<int, int> key(mode, (mode & 2) ? limit : 0);
+    auto it = d->graphs.find(key);
+    if (it != d->graphs.end()) {
+        DEC_CUDA(cudaGraphLaunch(it->second, s), "cudaGraphLaunch(decoder step)");
+        return RWQ_OK;
+    }
+    if (!graphs_enabled() || d->eager_runs[key] == 0) {
+        ++d->eager_runs[key];
+        return issue_step(d, mode, limit, s);
+    }
+    cudaGraph_t g = nullptr;
+    DEC_CUDA(cudaStreamBeginCapture(s, cudaStreamCaptureModeRelaxed), "cudaStreamBeginCapture");
+    const int rc = issue_step(d, mode, limit, s);
+    const cudaError_t ec = cudaStreamEndCapture(s, &g);
+    if (rc || ec != cudaSuccess || !g) {
+        if (g) cudaGraphDestroy(g);
+        cudaGetLastError();
+        if (rc) return rc;
+        ++d->eager_runs[key];
+        return issue_step(d, mode, limit, s);   // not capturable here: stay eager
+    }
+    cudaGraphExec_t ex = nullptr;
+    const cudaError_t ei = cudaGraphInstantiate(&ex, g, 0);
+    cudaGraphDestroy(g);
+    if (ei != cudaSuccess) {
+        cudaGetLastError();
+        ++d->eager_runs[key];
+        return issue_step(d, mode, limit, s);
+    }
+    d->graphs[key] = ex;
+    DEC_CUDA(cudaGraphLaunch(ex, s), "cudaGraphLaunch(decoder step)");
+    return RWQ_OK;
 }
 
 }  // namespace
@@ -240,6 +352,12 @@ int rwq_decoder_new(int n_vocab, int n_ctx, int n_state, int n_head, int n_layer
     d->n_layer = n_layer;
     d->n_ff = 4 * n_state;
     d->layers.resize(size_t(n_layer));
+    if (cudaStreamCreateWithFlags(&d->gs, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaEventCreateWithFlags(&d->ev_in, cudaEventDisableTiming) != cudaSuccess ||
+        cudaEventCreateWithFlags(&d->ev_out, cudaEventDisableTiming) != cudaSuccess) {
+        rwq_decoder_free(d);
+        return dfail(RWQ_ERR_CUDA, "decoder stream/event creation failed");
+    }
     d->dense_len["decoder.positional_embedding"] = size_t(n_ctx) * n_state;
     d->dense_len["decoder.ln.weight"] = size_t(n_state);
     d->dense_len["decoder.ln.bias"] = size_t(n_state);
@@ -260,7 +378,12 @@ int rwq_decoder_free(rwq_decoder* d) {
     for (auto& L : d->layers)
         for (rwq_qtensor* t : {L.q, L.k, L.v, L.o, L.xq, L.xk, L.xv, L.xo, L.fc1, L.fc2}) rwq_qtensor_free(t);
     rwq_qtensor_free(d->emb);
+    if (d->gs) cudaStreamSynchronize(d->gs);
+    drop_graphs(d);
     cudaFree(d->state);
+    if (d->ev_in) cudaEventDestroy(d->ev_in);
+    if (d->ev_out) cudaEventDestroy(d->ev_out);
+    if (d->gs) cudaStreamDestroy(d->gs);
     if (prev != d->device) cudaSetDevice(prev);
     delete d;
     return RWQ_OK;
@@ -308,6 +431,23 @@ int rwq_decoder_begin(rwq_decoder* d, const float* enc_out, int64_t n_windows, i
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev != d->device) return dfail(RWQ_ERR_ARG, "decoder lives on device %d, current device is %d", d->device, dev);
+    for (int l = 0; l < d->n_layer; ++l) {
+        DLayer& L = d->layers[size_t(l)];
+        auto P = [&](const char* f) { return static_cast<const float*>(d->dense[lname(l, f)]); };
+        L.attn_ln_w = P("attn_ln.weight");
+        L.attn_ln_b = P("attn_ln.bias");
+        L.q_b = P("attn.query.bias");
+        L.v_b = P("attn.value.bias");
+        L.o_b = P("attn.out.bias");
+        L.x_ln_w = P("cross_attn_ln.weight");
+        L.x_ln_b = P("cross_attn_ln.bias");
+        L.xq_b = P("cross_attn.query.bias");
+        L.xo_b = P("cross_attn.out.bias");
+        L.mlp_ln_w = P("mlp_ln.weight");
+        L.mlp_ln_b = P("mlp_ln.bias");
+        L.fc1_b = P("mlp.0.bias");
+        L.fc2_b = P("mlp.2.bias");
+    }
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     const int S = int(n_streams), W = int(n_windows), T = int(n_audio), D = d->n_state, H = d->n_head;
     // stream -> window map and the cross-attention groups (<= DEC_MAX_G
@@ -337,6 +477,8 @@ int rwq_decoder_begin(rwq_decoder* d, const float* enc_out, int64_t n_windows, i
         }
     }
     const int NG = int(gkv.size());
+    DEC_CUDA(cudaStreamSynchronize(d->gs), "cudaStreamSynchronize(decoder)");
+    drop_graphs(d);
     const size_t need = layout_state(d, S, W, T, NG, nullptr);
     if (d->state_bytes < need) {
         DEC_CUDA(cudaStreamSynchronize(s), "cudaStreamSynchronize");
@@ -357,6 +499,7 @@ int rwq_decoder_begin(rwq_decoder* d, const float* enc_out, int64_t n_windows, i
         if (i < S) sid[size_t(i)] = i;
         soff[size_t(i)] = i;
     }
+    DEC_CUDA(cudaMemsetAsync(d->dpos, 0, sizeof(int), s), "reset position");
     DEC_CUDA(cudaMemcpyAsync(d->cross_kv, gkv.data(), gkv.size() * 4, cudaMemcpyHostToDevice, s), "copy groups");
     DEC_CUDA(cudaMemcpyAsync(d->cross_off, goff.data(), goff.size() * 4, cudaMemcpyHostToDevice, s), "copy groups");
     DEC_CUDA(cudaMemcpyAsync(d->cross_streams, gst.data(), gst.size() * 4, cudaMemcpyHostToDevice, s), "copy groups");
@@ -411,49 +554,20 @@ int rwq_decoder_step(rwq_decoder* d, const int32_t* tokens, float* logits, int32
         return dfail(RWQ_ERR_ARG, "decoder context overflow: %d + 1 > %d", d->n_past, d->n_ctx);   // decoder.rs:115-120
     if (limit >= d->n_vocab) return dfail(RWQ_ERR_ARG, "limit %d >= n_vocab %d", limit, d->n_vocab);
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    const int S = d->n_streams, D = d->n_state, H = d->n_head, F = d->n_ff, P = d->n_past;
-    DEC_CUDA(rwq::launch_embed(rwq::weight_of(d->emb), tokens, S, d->dense["decoder.positional_embedding"] + size_t(P) * D,
-                               d->x, s),
-             "embed");
-    const size_t self_layer = size_t(S) * H * d->n_ctx * 64, cross_layer = size_t(d->n_windows) * H * d->n_audio * 64;
-    for (int l = 0; l < d->n_layer; ++l) {
-        const DLayer& L = d->layers[size_t(l)];
-        auto B = [&](const char* f) { return d->dense[lname(l, f)]; };
-        // causal self-attention over the cache (decoder.rs:140-171)
-        DEC_RC(rows(d, l ? rwq::RQ_ADD_LN : rwq::RQ_LN, d->x, d->tmp, d->x, "attn_ln", D, s, l));
-        DEC_RC(linear(d, L.q, B("attn.query.bias"), d->q, s));
-        DEC_RC(linear(d, L.k, nullptr, d->k, s));
-        DEC_RC(linear(d, L.v, B("attn.value.bias"), d->v, s));
-        __half* kc = d->self_k + size_t(l) * self_layer;
-        __half* vc = d->self_v + size_t(l) * self_layer;
-        DEC_CUDA(rwq::launch_kv_append(d->k, d->v, S, H, d->n_ctx, P, kc, vc, s), "kv append");
-        DEC_CUDA(rwq::launch_attn_dec(d->q, kc, vc, size_t(d->n_ctx) * 64, P + 1, H, S, d->self_kv, d->self_off,
-                                      d->self_kv, d->att, s),
-                 "self attention");
-        DEC_RC(rows(d, rwq::RQ_PLAIN, d->att, nullptr, nullptr, nullptr, D, s));
-        DEC_RC(linear(d, L.o, B("attn.out.bias"), d->tmp, s));
-        // cross-attention to the window's K/V (decoder.rs:173-188)
-        DEC_RC(rows(d, rwq::RQ_ADD_LN, d->x, d->tmp, d->x, "cross_attn_ln", D, s, l));
-        DEC_RC(linear(d, L.xq, B("cross_attn.query.bias"), d->q, s));
-        DEC_CUDA(rwq::launch_attn_dec(d->q, d->cross_k + size_t(l) * cross_layer, d->cross_v + size_t(l) * cross_layer,
-                                      size_t(d->n_audio) * 64, d->n_audio, H, d->n_cross_groups, d->cross_kv,
-                                      d->cross_off, d->cross_streams, d->att, s),
-                 "cross attention");
-        DEC_RC(rows(d, rwq::RQ_PLAIN, d->att, nullptr, nullptr, nullptr, D, s));
-        DEC_RC(linear(d, L.xo, B("cross_attn.out.bias"), d->tmp, s));
-        // MLP (encoder.rs:154-172)
-        DEC_RC(rows(d, rwq::RQ_ADD_LN, d->x, d->tmp, d->x, "mlp_ln", D, s, l));
-        DEC_RC(linear(d, L.fc1, B("mlp.0.bias"), d->h, s));
-        DEC_RC(rows(d, rwq::RQ_GELU, d->h, nullptr, nullptr, nullptr, F, s));
-        DEC_RC(linear(d, L.fc2, B("mlp.2.bias"), d->tmp, s));
-    }
-    d->n_past = P + 1;
-    if (!logits && !best) return RWQ_OK;   // a prompt position: no projection needed
-    // final LN (decoder.rs:200-204), tied logits (decoder.rs:315-321)
-    DEC_RC(rows(d, d->n_layer ? rwq::RQ_ADD_LN : rwq::RQ_LN, d->x, d->tmp, d->x, "decoder.ln", D, s));
-    float* lg = logits ? logits : d->logits;
-    DEC_RC(linear(d, d->emb, nullptr, lg, s));
-    if (best) DEC_CUDA(rwq::launch_argmax(lg, S, d->n_vocab, limit, best, s), "argmax");
+    const int S = d->n_streams;
+    if (tokens != d->tok_in)
+        DEC_CUDA(cudaMemcpyAsync(d->tok_in, tokens, size_t(S) * 4, cudaMemcpyDeviceToDevice, s), "copy tokens");
+    const int mode = (logits ? 1 : 0) | (best ? 2 : 0);
+    DEC_CUDA(cudaEventRecord(d->ev_in, s), "cudaEventRecord");
+    DEC_CUDA(cudaStreamWaitEvent(d->gs, d->ev_in, 0), "cudaStreamWaitEvent");
+    DEC_RC(run_step(d, mode, limit, d->gs));
+    DEC_CUDA(cudaEventRecord(d->ev_out, d->gs), "cudaEventRecord");
+    DEC_CUDA(cudaStreamWaitEvent(s, d->ev_out, 0), "cudaStreamWaitEvent");
+    d->n_past += 1;
+    if (logits)
+        DEC_CUDA(cudaMemcpyAsync(logits, d->logits, size_t(S) * d->n_vocab * 4, cudaMemcpyDeviceToDevice, s),
+                 "copy logits");
+    if (best) DEC_CUDA(cudaMemcpyAsync(best, d->best, size_t(S) * 4, cudaMemcpyDeviceToDevice, s), "copy ids");
     return RWQ_OK;
 }
 
@@ -461,6 +575,10 @@ int rwq_decoder_reset(rwq_decoder* d) {
     if (!d) return dfail(RWQ_ERR_ARG, "decoder is null");
     std::lock_guard<std::mutex> g(d->mu);
     d->n_past = 0;   // the self-attention cache is overwritten from position 0
+    if (d->dpos) {
+        DEC_CUDA(cudaDeviceSynchronize(), "cudaDeviceSynchronize");   // no step of this decoder in flight
+        DEC_CUDA(cudaMemset(d->dpos, 0, sizeof(int)), "reset position");
+    }
     return RWQ_OK;
 }
 

@@ -11,17 +11,23 @@ namespace rwq {
 
 constexpr int DEC_MAX_G = 8;   // streams sharing one key group in k_attn_dec
 
-cudaError_t launch_kv_append(const float* k_new, const float* v_new, int S, int H, int ctx, int pos, __half* kc,
-                             __half* vc, cudaStream_t s);
+// The decode position lives on the device (*dpos), so a step replays from
+// a CUDA graph.
+cudaError_t launch_kv_append(const float* k_new, const float* v_new, int S, int H, int ctx, const int* dpos,
+                             __half* kc, __half* vc, cudaStream_t s);
+cudaError_t launch_pos_advance(int* dpos, cudaStream_t s);
 // Attention of one query per stream (q [S][H*64] f32) over n_groups
 // groups: group g's keys/values are kc/vc + (grp_kv[g]*H + h)*kv_stride,
 // f16 [L][64]; its streams are grp_streams[grp_off[g] .. grp_off[g+1])
-// (<= DEC_MAX_G).  Device arrays.
-cudaError_t launch_attn_dec(const float* q, const __half* kc, const __half* vc, size_t kv_stride, int L, int H,
-                            int n_groups, const int* grp_kv, const int* grp_off, const int* grp_streams, float* out,
-                            cudaStream_t s);
+// (<= DEC_MAX_G).  Device arrays.  With dpos the keys are 0..*dpos
+// (self-attention over the cache; L is then the capacity).
+cudaError_t launch_attn_dec(const float* q, const __half* kc, const __half* vc, size_t kv_stride, int L,
+                            const int* dpos, int H, int n_groups, const int* grp_kv, const int* grp_off,
+                            const int* grp_streams, float* out, cudaStream_t s);
 cudaError_t launch_argmax(const float* logits, int rows, int V, int limit, int32_t* best, cudaStream_t s);
-// x[i] = dequant(w row tokens[i]) + pos (bit-exact dequant, quant.rs:528-537).
-cudaError_t launch_embed(const Weight& w, const int32_t* tokens, int n, const float* pos, float* x, cudaStream_t s);
+// x[i] = dequant(w row tokens[i]) + pos[*dpos] (bit-exact dequant,
+// quant.rs:528-537); pos is [ctx][k].
+cudaError_t launch_embed(const Weight& w, const int32_t* tokens, int n, const float* pos, const int* dpos, float* x,
+                         cudaStream_t s);
 
 }  // namespace rwq

@@ -30,6 +30,8 @@ __device__ __forceinline__ float gelu_ref(float t) {
 // (lane & 7 = position): the reference quantizer (quant.rs:690-716), as
 // k_quantize does it -- d = amax/127, inv = 1/d or 0, q = round(x*inv)
 // half away from zero, clamped to +-127, NaN -> 0.
+constexpr int RQ_SLICE = 4;   // 128-element chunks per warp in the PLAIN / GELU modes
+
 struct QOut {
     uint16_t* q16;   // GEMM layout: f16 codes [m][k], d_a and d_a*sum transposed [nb][m_pad]
     float* dT;
@@ -96,11 +98,17 @@ __global__ void __launch_bounds__(256) k_rows_quant(const float* x, const float*
     pdl_trigger();
     pdl_wait();
     const int lane = threadIdx.x & 31;
-    const int row = int((size_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5);
+    const int nb = k / QK, nch = k / 128;
+    // PLAIN / GELU rows are split over several warps (RQ_SLICE chunks of
+    // 128 elements each); LayerNorm rows take one warp (they need the row's
+    // statistics).
+    const int slices = (MODE == RQ_PLAIN || MODE == RQ_GELU) ? (nch + RQ_SLICE - 1) / RQ_SLICE : 1;
+    const size_t wg = (size_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    const int row = int(wg / slices), slice = int(wg % slices);
     const int rows = o.q16 ? o.m_pad : m;
     if (row >= rows) return;
-    const int nb = k / QK, nch = k / 128;
     if (row >= m) {
+        if (slice) return;
         for (int bl = lane; bl < nb; bl += 32) {
             o.dT[size_t(bl) * o.m_pad + row] = 0.f;
             o.uT[size_t(bl) * o.m_pad + row] = 0.f;
@@ -115,7 +123,8 @@ __global__ void __launch_bounds__(256) k_rows_quant(const float* x, const float*
         if (yout) *reinterpret_cast<float4*>(yout + size_t(row) * k + e) = v;
     };
     if (MODE == RQ_PLAIN || MODE == RQ_GELU) {
-        for (int c = 0; c < nch; ++c) {
+        const int c1 = min(nch, (slice + 1) * RQ_SLICE);
+        for (int c = slice * RQ_SLICE; c < c1; ++c) {
             float4 v = __ldg(xr + c * 32 + lane);
             if (MODE == RQ_GELU) v = make_float4(gelu_ref(v.x), gelu_ref(v.y), gelu_ref(v.z), gelu_ref(v.w));
             emit(c, v);
@@ -401,8 +410,9 @@ template <int MODE>
 cudaError_t rows_quant_mode(const float* x, const float* add, float* xout, const float* lw, const float* lb, int m,
                             int k, const QOut& o, float* yout, cudaStream_t s) {
     const int rows = o.q16 ? o.m_pad : m;
-    const unsigned grid = unsigned((size_t(rows) * 32 + 255) / 256);
     const int nch = k / 128;
+    const int slices = (MODE == RQ_PLAIN || MODE == RQ_GELU) ? (nch + RQ_SLICE - 1) / RQ_SLICE : 1;
+    const unsigned grid = unsigned((size_t(rows) * slices * 32 + 255) / 256);
     if (MODE == RQ_PLAIN || MODE == RQ_GELU || nch <= 4)
         return launch_pdl(k_rows_quant<MODE, 4>, dim3(grid), dim3(256), 0, s, x, add, xout, lw, lb, m, k, o, yout);
     if (nch <= 8)

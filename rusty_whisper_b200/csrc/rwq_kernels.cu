@@ -13,6 +13,19 @@ namespace {
 
 constexpr int TPB = 256;
 
+// Current device and its SM count, cached per device (launch paths run per
+// call; the attribute query is not free).
+inline void dev_sms(int* dev, int* sms) {
+    static int cache[64] = {};
+    cudaGetDevice(dev);
+    if (*dev < 0 || *dev >= 64) {
+        cudaDeviceGetAttribute(sms, cudaDevAttrMultiProcessorCount, *dev);
+        return;
+    }
+    if (!cache[*dev]) cudaDeviceGetAttribute(&cache[*dev], cudaDevAttrMultiProcessorCount, *dev);
+    *sms = cache[*dev];
+}
+
 inline unsigned grid_for(size_t work, int per_block) {
     size_t g = (work + per_block - 1) / per_block;
     return unsigned(g ? g : 1);
@@ -212,14 +225,15 @@ __global__ void k_dequant_rows(const uint8_t* __restrict__ qs, const uint32_t* _
 
 // Token embedding gather for the decoder (decoder.rs:125-136): row
 // tokens[r] dequantized exactly like QTensor::row_f32, plus the learned
-// position row `pos` (x = dequant + pos, one rounding).
+// position row *dpos of `pos` (x = dequant + pos, one rounding).
 template <int DT>
 __global__ void k_embed(const uint8_t* __restrict__ qs, const uint32_t* __restrict__ qh,
                         const uint16_t* __restrict__ dp, const uint16_t* __restrict__ mp,
                         const int32_t* __restrict__ tokens, int nrows, int n, int nb, const float* __restrict__ pos,
-                        float* __restrict__ x) {
+                        const int* __restrict__ dpos, float* __restrict__ x) {
     pdl_trigger();
     pdl_wait();
+    pos += size_t(*dpos) * nb * QK;
     size_t t = size_t(blockIdx.x) * blockDim.x + threadIdx.x;
     if (t >= size_t(nrows) * nb) return;
     const int r = int(t / nb), bl = int(t % nb);
@@ -671,8 +685,9 @@ __host__ __device__ constexpr size_t gemv_mma_act_smem(int nb, int nt) {
     return size_t(round4(nb)) * size_t(nt) * 352 + size_t(nt) * 4096;
 }
 
-// PF groups in flight per warp; NT n-tiles of 8 activation rows per launch
-// (M <= 8*NT).
+// PF groups in flight per warp; NT n-tiles of 8 activation rows per CTA:
+// CTA row blockIdx.y takes activation rows [8*NT*y, 8*NT*(y+1)) of the M
+// (the CTAs of different rows share the weights through L2).
 template <int DT, int KS, int PF, int NT>
 __global__ void __launch_bounds__(GM_THREADS, 1)
     k_gemv_mma(const uint8_t* __restrict__ qs, const uint32_t* __restrict__ qh, const uint16_t* __restrict__ dp,
@@ -683,6 +698,15 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
     pdl_trigger();
     constexpr int WARPS = GM_THREADS / 32;
     const int nb = K / QK, nb4 = round4(nb), ng = nb4 / 4;
+    {
+        const int row0 = int(blockIdx.y) * 8 * NT;
+        M = min(M - row0, 8 * NT);
+        q8 += size_t(row0) * K;
+        da += size_t(row0) * nb;
+        sa += size_t(row0) * nb;
+        ua += size_t(row0) * nb;
+        y += size_t(row0) * N;
+    }
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int tiles = (N + 15) / 16;
 
@@ -1047,12 +1071,12 @@ struct DequantF {
 
 template <int DT>
 struct EmbedF {
-    static cudaError_t run(const Weight& w, const int32_t* tokens, int nrows, const float* pos, float* x,
-                           cudaStream_t s) {
+    static cudaError_t run(const Weight& w, const int32_t* tokens, int nrows, const float* pos, const int* dpos,
+                           float* x, cudaStream_t s) {
         size_t work = size_t(nrows) * w.nb;
         if (!work) return cudaSuccess;
         return launch_pdl(k_embed<DT>, dim3(grid_for(work, TPB)), dim3(TPB), 0, s, w.qs, w.qh, w.d, w.m, tokens,
-                          nrows, w.n, w.nb, pos, x);
+                          nrows, w.n, w.nb, pos, dpos, x);
     }
 };
 
@@ -1104,8 +1128,7 @@ unsigned gemv_grid(Kern kern, int n, int L, size_t smem) {
     const int rows_per_cta = (TPB / 32) * (32 / L);
     unsigned g = unsigned((n + rows_per_cta - 1) / rows_per_cta);
     int dev = 0, sms = 148, per_sm = 1;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    dev_sms(&dev, &sms);
     if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, TPB, smem) != cudaSuccess || per_sm < 1)
         per_sm = 1;
     const unsigned cap = unsigned(sms) * unsigned(per_sm);
@@ -1167,22 +1190,22 @@ cudaError_t gemv_mma_go(const ActsView& v, const Weight& w, const float* bias, f
     auto kern = k_gemv_mma<DT, KS, PF, NT>;
     const size_t smem = gemv_mma_act_smem(w.nb, NT) + size_t(PF) * Slot<DT>::BYTES * (GM_THREADS / 32);
     int dev = 0, sms = 148;
-    cudaGetDevice(&dev);
+    dev_sms(&dev, &sms);
     static unsigned attr_dev_mask = 0;  // one bit per device with the attribute set
     if (!(attr_dev_mask & (1u << dev))) {
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 224 * 1024);
         if (e != cudaSuccess) return e;
         attr_dev_mask |= 1u << dev;
     }
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     const int tiles = (w.n + 15) / 16, tpc = (GM_THREADS / 32) / KS;
     // KS == 1: one contiguous range of at least 8 tiles per CTA (see the
     // kernel); KS > 1: grid-stride over groups of tpc tiles.
     unsigned grid = KS == 1 ? unsigned(tiles / (GM_THREADS / 32)) : unsigned((tiles + tpc - 1) / tpc);
     const unsigned cap = unsigned(sms) * 2u;
     grid = grid < 1 ? 1 : (grid > cap ? cap : grid);
-    return launch_pdl(kern, dim3(grid), dim3(GM_THREADS), smem, s, w.qs, w.qh, w.d, w.m, v.q8, v.d, v.sum, v.u, v.m,
-                      w.n, w.k, bias, y);
+    const unsigned rows = unsigned((v.m + 8 * NT - 1) / (8 * NT));
+    return launch_pdl(kern, dim3(grid, rows), dim3(GM_THREADS), smem, s, w.qs, w.qh, w.d, w.m, v.q8, v.d, v.sum, v.u,
+                      v.m, w.n, w.k, bias, y);
 }
 
 constexpr size_t GEMV_SMEM_MAX = 224 * 1024;
@@ -1198,11 +1221,19 @@ int gemv_mma_nt_max(int nb) {
     return 1;
 }
 
+// n-tiles per CTA: as many as the rows need (up to what fits) when the
+// weight gives the grid enough CTAs on its own; otherwise two (16 rows),
+// so that more CTAs share the rows.
 template <int DT, int KS>
 cudaError_t gemv_mma_launch(const ActsView& v, const Weight& w, const float* bias, float* y, cudaStream_t s) {
     const int need = (v.m + 7) / 8;
-    const int nt = need <= 1 ? 1 : need <= 2 ? 2 : need <= 4 ? 4 : 8;
-    if (nt > gemv_mma_nt_max<DT>(w.nb)) return cudaErrorInvalidValue;
+    int nt = need <= 1 ? 1 : need <= 2 ? 2 : need <= 4 ? 4 : 8;
+    const int nt_max = gemv_mma_nt_max<DT>(w.nb);
+    int dev = 0, sms = 148;
+    dev_sms(&dev, &sms);
+    const int tiles = (w.n + 15) / 16;
+    if (nt > 2 && tiles * KS < 2 * sms * (GM_THREADS / 32)) nt = 2;
+    if (nt > nt_max) nt = nt_max;
     switch (nt) {
         case 1:
             if (gemv_mma_act_smem(w.nb, 1) + 8 * gemv_slot8<DT>() <= GEMV_SMEM_MAX / 2)
@@ -1219,8 +1250,7 @@ cudaError_t gemv_mma_launch(const ActsView& v, const Weight& w, const float* bia
 // Depends on N and K only (results stay independent of M).
 inline int gemv_mma_ks(int n, int nb) {
     int dev = 0, sms = 148;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    dev_sms(&dev, &sms);
     const int tiles = (n + 15) / 16, ng = round4(nb) / 4;
     int ks = 1;
     while (ks < 8 && ng >= 2 * ks && tiles * ks < sms * 8) ks *= 2;
@@ -1297,8 +1327,9 @@ cudaError_t launch_dequant_rows(const Weight& w, const int32_t* rows, int nrows,
     return by_dtype<DequantF>(w.dtype, w, rows, nrows, out, s);
 }
 
-cudaError_t launch_embed(const Weight& w, const int32_t* tokens, int n, const float* pos, float* x, cudaStream_t s) {
-    return by_dtype<EmbedF>(w.dtype, w, tokens, n, pos, x, s);
+cudaError_t launch_embed(const Weight& w, const int32_t* tokens, int n, const float* pos, const int* dpos, float* x,
+                         cudaStream_t s) {
+    return by_dtype<EmbedF>(w.dtype, w, tokens, n, pos, dpos, x, s);
 }
 
 cudaError_t launch_block_dots(const ActsView& v, const Weight& w, int32_t* S, cudaStream_t s) {
@@ -1323,9 +1354,9 @@ cudaError_t launch_gemv_i8(const ActsView& v, const Weight& w, const float* bias
     const int kind = t_gemv_kind ? t_gemv_kind : 2;
     const bool mma =
         kind == 2 && uint64_t(w.n) * uint64_t(round4(w.nb)) * uint64_t(qs_bytes(w.dtype)) < (uint64_t(1) << 32);
-    // Rows in launches of up to `per`: after the first launch the weights
-    // come from L2 for every weight that fits there.
-    const int per = mma ? gemv_rows_per_launch(w.dtype, w.k) : GEMV_MAX_M;
+    // The MMA kernel takes all rows in one launch (CTA rows of up to 64
+    // activation rows share the weights through L2); dp4a launches 8 rows.
+    const int per = mma ? GEMV_FAMILY_MAX_M : GEMV_MAX_M;
     for (int m0 = 0; m0 < v.m; m0 += per) {
         ActsView c = v;
         c.m = v.m - m0 < per ? v.m - m0 : per;
