@@ -88,7 +88,7 @@ struct rwq_decoder {
     std::vector<DLayer> layers;
     rwq_qtensor* emb = nullptr;
     // decode state (begin)
-    int n_streams = 0, n_windows = 0, n_audio = 0, n_past = 0, n_cross_groups = 0;
+    int n_streams = 0, n_windows = 0, n_audio = 0, n_past = 0, n_cross_groups = 0, max_group = 1;
     void* state = nullptr;        // caches, group tables and step buffers
     size_t state_bytes = 0;
     __half *cross_k = nullptr, *cross_v = nullptr, *self_k = nullptr, *self_v = nullptr;
@@ -263,7 +263,7 @@ int issue_step(rwq_decoder* d, int mode, int32_t limit, cudaStream_t s) {
         __half* kc = d->self_k + size_t(l) * self_layer;
         __half* vc = d->self_v + size_t(l) * self_layer;
         DEC_CUDA(rwq::launch_kv_append(d->k, d->v, S, H, d->n_ctx, d->dpos, kc, vc, s), "kv append");
-        DEC_CUDA(rwq::launch_attn_dec(d->q, kc, vc, size_t(d->n_ctx) * 64, d->n_ctx, d->dpos, H, S, d->self_kv,
+        DEC_CUDA(rwq::launch_attn_dec(d->q, kc, vc, size_t(d->n_ctx) * 64, d->n_ctx, d->dpos, H, S, 1, d->self_kv,
                                       d->self_off, d->self_kv, d->att, s),
                  "self attention");
         DEC_RC(rows(d, rwq::RQ_PLAIN, d->att, nullptr, nullptr, nullptr, nullptr, D, s));
@@ -272,8 +272,8 @@ int issue_step(rwq_decoder* d, int mode, int32_t limit, cudaStream_t s) {
         DEC_RC(rows(d, rwq::RQ_ADD_LN, d->x, d->tmp, d->x, L.x_ln_w, L.x_ln_b, D, s));
         DEC_RC(linear(d, L.xq, L.xq_b, d->q, s));
         DEC_CUDA(rwq::launch_attn_dec(d->q, d->cross_k + size_t(l) * cross_layer, d->cross_v + size_t(l) * cross_layer,
-                                      size_t(d->n_audio) * 64, d->n_audio, nullptr, H, d->n_cross_groups, d->cross_kv,
-                                      d->cross_off, d->cross_streams, d->att, s),
+                                      size_t(d->n_audio) * 64, d->n_audio, nullptr, H, d->n_cross_groups, d->max_group,
+                                      d->cross_kv, d->cross_off, d->cross_streams, d->att, s),
                  "cross attention");
         DEC_RC(rows(d, rwq::RQ_PLAIN, d->att, nullptr, nullptr, nullptr, nullptr, D, s));
         DEC_RC(linear(d, L.xo, L.xo_b, d->tmp, s));
@@ -458,20 +458,16 @@ int rwq_decoder_begin(rwq_decoder* d, const float* enc_out, int64_t n_windows, i
         if (win[size_t(i)] < 0 || win[size_t(i)] >= W)
             return dfail(RWQ_ERR_ARG, "stream %d maps to window %d of %d", i, win[size_t(i)], W);
     }
+    // Cross-attention groups: one stream each, ordered by window, so the
+    // CTAs of one window's streams are adjacent in the grid and its K/V
+    // comes from L2 after the first read (a group holding several streams
+    // would read it once but carry every query's state per lane, which
+    // costs more occupancy than the L2 re-reads).
     std::vector<int> gkv, goff(1, 0), gst;
     for (int w = 0; w < W; ++w) {
-        int in_group = 0;
         for (int i = 0; i < S; ++i) {
             if (win[size_t(i)] != w) continue;
-            if (in_group == rwq::DEC_MAX_G) {
-                gkv.push_back(w);
-                goff.push_back(int(gst.size()));
-                in_group = 0;
-            }
             gst.push_back(i);
-            ++in_group;
-        }
-        if (in_group) {
             gkv.push_back(w);
             goff.push_back(int(gst.size()));
         }
@@ -493,6 +489,8 @@ int rwq_decoder_begin(rwq_decoder* d, const float* enc_out, int64_t n_windows, i
     d->n_windows = W;
     d->n_audio = T;
     d->n_cross_groups = NG;
+    d->max_group = 1;
+    for (int i = 0; i < NG; ++i) d->max_group = std::max(d->max_group, goff[size_t(i) + 1] - goff[size_t(i)]);
     d->n_past = 0;
     std::vector<int> sid(static_cast<size_t>(S)), soff(static_cast<size_t>(S) + 1);
     for (int i = 0; i <= S; ++i) {

@@ -19,10 +19,10 @@ cudaError_t launch_pos_advance(int* dpos, cudaStream_t s);
 // Attention of one query per stream (q [S][H*64] f32) over n_groups
 // groups: group g's keys/values are kc/vc + (grp_kv[g]*H + h)*kv_stride,
 // f16 [L][64]; its streams are grp_streams[grp_off[g] .. grp_off[g+1])
-// (<= DEC_MAX_G).  Device arrays.  With dpos the keys are 0..*dpos
+// (<= max_group <= DEC_MAX_G).  Device arrays.  With dpos the keys are 0..*dpos
 // (self-attention over the cache; L is then the capacity).
 cudaError_t launch_attn_dec(const float* q, const __half* kc, const __half* vc, size_t kv_stride, int L,
-                            const int* dpos, int H, int n_groups, const int* grp_kv, const int* grp_off,
+                            const int* dpos, int H, int n_groups, int max_group, const int* grp_kv, const int* grp_off,
                             const int* grp_streams, float* out, cudaStream_t s);
 cudaError_t launch_argmax(const float* logits, int rows, int V, int limit, int32_t* best, cudaStream_t s);
 // x[i] = dequant(w row tokens[i]) + pos[*dpos] (bit-exact dequant,

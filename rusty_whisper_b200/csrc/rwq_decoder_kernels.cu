@@ -35,129 +35,107 @@ __global__ void k_kv_append(const float* __restrict__ k_new, const float* __rest
 
 // One CTA per (head, group).  Group g reads the keys/values at
 // kc/vc + (grp_kv[g]*H + h)*kv_stride (f16 [L][64]) for its streams
-// grp_streams[grp_off[g] .. grp_off[g+1]) (at most DEC_MAX_G).  Scores stay in shared memory; q is scaled by 1/8
-// (1/sqrt(64), exact) as the reference scales the scores (encoder.rs:58).
+// grp_streams[grp_off[g] .. grp_off[g+1]) (at most DEC_MAX_G).  One pass
+// over K and V with an online softmax (flash decoding): warp w streams keys
+// 4w + 32t .. 4w + 32t + 3, 8 lanes per key with 16-byte loads of the K and
+// V rows, keeping a running max, sum and 8-dim partial output per query;
+// the 8 warps combine through shared memory at the end.  q is scaled by
+// 1/8 (1/sqrt(64), exact) as the reference scales the scores
+// (encoder.rs:58); exponentials are base 2 on log2(e)-scaled scores.
 constexpr int DEC_THREADS = 256;
+constexpr int DEC_WARPS = DEC_THREADS / 32;
 
+__device__ __forceinline__ void h8_to_f(const uint4 u, float (&f)[8]) {
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+        const float2 x = __half22float2(*reinterpret_cast<const __half2*>(&w[t]));
+        f[2 * t] = x.x;
+        f[2 * t + 1] = x.y;
+    }
+}
+
+template <int GM>
 __global__ void __launch_bounds__(DEC_THREADS) k_attn_dec(const float* __restrict__ q, const __half* __restrict__ kc,
                                                          const __half* __restrict__ vc, size_t kv_stride, int L,
                                                          const int* __restrict__ dpos, int H,
                                                          const int* __restrict__ grp_kv, const int* __restrict__ grp_off,
                                                          const int* __restrict__ grp_streams, float* __restrict__ out) {
     pdl_trigger();
-    extern __shared__ __align__(16) float sm[];
+    __shared__ float s_acc[DEC_WARPS][GM][HD];
+    __shared__ float s_ml[DEC_WARPS][GM][2];
     const int h = blockIdx.x, g = blockIdx.y, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int D = H * HD;
     pdl_wait();
     if (dpos) L = min(*dpos + 1, L);   // self-attention: keys 0..pos (L is the cache capacity)
     const int s0 = grp_off[g], G = grp_off[g + 1] - s0;
     if (G <= 0) return;
-    constexpr int PH = DEC_THREADS / 32;          // key phases of the output pass (one per warp)
-    float* sq = sm;                               // [G][64] scaled queries
-    float* part = sq + DEC_MAX_G * HD;            // [PH][G][64] partial outputs
-    float* sums = part + PH * DEC_MAX_G * HD;     // [G] softmax denominators
-    float* sc = sums + DEC_MAX_G;                 // [G][L] scores, then probabilities
-    for (int i = tid; i < G * HD; i += DEC_THREADS) {
-        const int gi = i / HD, e = i % HD;
-        sq[i] = __fmul_rn(q[size_t(grp_streams[s0 + gi]) * D + h * HD + e], 0.125f);
+    const float L2E = 1.4426950408889634f;
+    const int kq = lane >> 3, e8 = (lane & 7) * 8;
+    // this lane's 8 query dims, scaled by 1/8 and log2(e)
+    float qv[GM][8];
+#pragma unroll
+    for (int gi = 0; gi < GM; ++gi) {
+        if (gi < G) {
+            const float4* qp = reinterpret_cast<const float4*>(q + size_t(grp_streams[s0 + gi]) * D + h * HD + e8);
+            const float4 a = __ldg(qp), b = __ldg(qp + 1);
+            const float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+            for (int t = 0; t < 8; ++t) qv[gi][t] = __fmul_rn(v[t], 0.125f) * L2E;
+        } else {
+#pragma unroll
+            for (int t = 0; t < 8; ++t) qv[gi][t] = 0.f;
+        }
     }
-    __syncthreads();
     const __half* K = kc + (size_t(grp_kv[g]) * H + h) * kv_stride;
     const __half* V = vc + (size_t(grp_kv[g]) * H + h) * kv_stride;
-    // scores: 8 lanes per key (16 bytes = 8 dims each), so a warp
-    // instruction reads four whole 128-byte key rows; warp w takes keys
-    // 4w + 32t .. 4w + 32t + 3, two rounds in flight.
-    {
-        const int kq = lane >> 3, e8 = (lane & 7) * 8;
-        float qv[DEC_MAX_G][8];
+    float m[GM], l[GM], acc[GM][8];
 #pragma unroll
-        for (int gi = 0; gi < DEC_MAX_G; ++gi)
-#pragma unroll
-            for (int t = 0; t < 8; ++t) qv[gi][t] = gi < G ? sq[gi * HD + e8 + t] : 0.f;
-#pragma unroll 2
-        for (int j0 = warp * 4; j0 < L; j0 += 4 * (DEC_THREADS / 32)) {
-            const int j = j0 + kq;
-            float kf[8];
-            if (j < L) {
-                const uint4 u = __ldg(reinterpret_cast<const uint4*>(K + size_t(j) * HD + e8));
-                const uint32_t wv[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-                for (int t = 0; t < 4; ++t) {
-                    const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&wv[t]));
-                    kf[2 * t] = f.x;
-                    kf[2 * t + 1] = f.y;
-                }
-            } else {
-#pragma unroll
-                for (int t = 0; t < 8; ++t) kf[t] = 0.f;
-            }
-#pragma unroll
-            for (int gi = 0; gi < DEC_MAX_G; ++gi) {
-                if (gi < G) {
-                    float a = 0.f;
-#pragma unroll
-                    for (int t = 0; t < 8; ++t) a = fmaf(qv[gi][t], kf[t], a);
-                    a += __shfl_xor_sync(0xffffffffu, a, 1);
-                    a += __shfl_xor_sync(0xffffffffu, a, 2);
-                    a += __shfl_xor_sync(0xffffffffu, a, 4);
-                    if ((lane & 7) == 0 && j < L) sc[size_t(gi) * L + j] = a;
-                }
-            }
-        }
-    }
-    __syncthreads();
-    // softmax per query: one warp each
-    for (int gi = warp; gi < G; gi += DEC_THREADS / 32) {
-        float* row = sc + size_t(gi) * L;
-        float mx = -INFINITY;
-        for (int j = lane; j < L; j += 32) mx = fmaxf(mx, row[j]);
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-        float sum = 0.f;
-        for (int j = lane; j < L; j += 32) {
-            const float p = expf(row[j] - mx);
-            row[j] = p;
-            sum += p;
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-        if (lane == 0) sums[gi] = sum;
-    }
-    __syncthreads();
-    // out[g][e] = sum_j p[g][j] v[j][e]: a warp instruction reads four
-    // whole 128-byte rows (lane: key j0 + lane/8, dims 8*(lane%8)..+7);
-    // warp w takes keys 4w + 32t .. 4w + 32t + 3.
-    const int kq = lane >> 3, e8 = (lane & 7) * 8;
-    float acc[DEC_MAX_G][8];
-#pragma unroll
-    for (int gi = 0; gi < DEC_MAX_G; ++gi)
+    for (int gi = 0; gi < GM; ++gi) {
+        m[gi] = -INFINITY;
+        l[gi] = 0.f;
 #pragma unroll
         for (int t = 0; t < 8; ++t) acc[gi][t] = 0.f;
-#pragma unroll 4
-    for (int j0 = warp * 4; j0 < L; j0 += 4 * PH) {
+    }
+#pragma unroll 2
+    for (int j0 = warp * 4; j0 < L; j0 += 4 * DEC_WARPS) {
         const int j = j0 + kq;
+        float kf[8], vf[8];
         if (j < L) {
-            const uint4 u = __ldg(reinterpret_cast<const uint4*>(V + size_t(j) * HD + e8));
-            const uint32_t wv[4] = {u.x, u.y, u.z, u.w};
-            float v[8];
+            h8_to_f(__ldg(reinterpret_cast<const uint4*>(K + size_t(j) * HD + e8)), kf);
+            h8_to_f(__ldg(reinterpret_cast<const uint4*>(V + size_t(j) * HD + e8)), vf);
+        } else {
 #pragma unroll
-            for (int t = 0; t < 4; ++t) {
-                const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&wv[t]));
-                v[2 * t] = f.x;
-                v[2 * t + 1] = f.y;
+            for (int t = 0; t < 8; ++t) kf[t] = vf[t] = 0.f;
+        }
+#pragma unroll
+        for (int gi = 0; gi < GM; ++gi) {
+            if (gi < G) {
+                float sc = 0.f;
+#pragma unroll
+                for (int t = 0; t < 8; ++t) sc = fmaf(qv[gi][t], kf[t], sc);
+                sc += __shfl_xor_sync(0xffffffffu, sc, 1);
+                sc += __shfl_xor_sync(0xffffffffu, sc, 2);
+                sc += __shfl_xor_sync(0xffffffffu, sc, 4);
+                if (j >= L) sc = -INFINITY;
+                // the four keys of this round
+                float mr = fmaxf(sc, __shfl_xor_sync(0xffffffffu, sc, 8));
+                mr = fmaxf(mr, __shfl_xor_sync(0xffffffffu, mr, 16));
+                const float mn = fmaxf(m[gi], mr);
+                const float scale = exp2f(m[gi] - mn);   // 0 on the first round (m = -inf)
+                const float p = exp2f(sc - mn);
+                float ps = p + __shfl_xor_sync(0xffffffffu, p, 8);
+                ps += __shfl_xor_sync(0xffffffffu, ps, 16);
+                l[gi] = fmaf(l[gi], scale, ps);
+#pragma unroll
+                for (int t = 0; t < 8; ++t) acc[gi][t] = fmaf(acc[gi][t], scale, p * vf[t]);
+                m[gi] = mn;
             }
-#pragma unroll
-            for (int gi = 0; gi < DEC_MAX_G; ++gi)
-                if (gi < G) {
-                    const float p = sc[size_t(gi) * L + j];
-#pragma unroll
-                    for (int t = 0; t < 8; ++t) acc[gi][t] = fmaf(p, v[t], acc[gi][t]);
-                }
         }
     }
-    // lanes with the same dims (4 keys) then warps (phases) are summed
+    // lanes with the same dims (the four key slots) share m: sum their parts
 #pragma unroll
-    for (int gi = 0; gi < DEC_MAX_G; ++gi)
+    for (int gi = 0; gi < GM; ++gi)
 #pragma unroll
         for (int t = 0; t < 8; ++t) {
             acc[gi][t] += __shfl_xor_sync(0xffffffffu, acc[gi][t], 8);
@@ -165,19 +143,30 @@ __global__ void __launch_bounds__(DEC_THREADS) k_attn_dec(const float* __restric
         }
     if (kq == 0) {
 #pragma unroll
-        for (int gi = 0; gi < DEC_MAX_G; ++gi)
+        for (int gi = 0; gi < GM; ++gi)
             if (gi < G) {
-                float* dst = part + (size_t(warp) * G + gi) * HD + e8;
-                *reinterpret_cast<float4*>(dst) = make_float4(acc[gi][0], acc[gi][1], acc[gi][2], acc[gi][3]);
-                *reinterpret_cast<float4*>(dst + 4) = make_float4(acc[gi][4], acc[gi][5], acc[gi][6], acc[gi][7]);
+#pragma unroll
+                for (int t = 0; t < 8; ++t) s_acc[warp][gi][e8 + t] = acc[gi][t];
+                if (lane == 0) {
+                    s_ml[warp][gi][0] = m[gi];
+                    s_ml[warp][gi][1] = l[gi];
+                }
             }
     }
     __syncthreads();
     for (int i = tid; i < G * HD; i += DEC_THREADS) {
-        const int gi = i / HD, ee = i % HD;
-        float a = 0.f;
-        for (int p = 0; p < PH; ++p) a += part[(size_t(p) * G + gi) * HD + ee];
-        out[size_t(grp_streams[s0 + gi]) * D + h * HD + ee] = a / sums[gi];
+        const int gi = i / HD, e = i % HD;
+        float M = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < DEC_WARPS; ++w) M = fmaxf(M, s_ml[w][gi][0]);
+        float num = 0.f, den = 0.f;
+#pragma unroll
+        for (int w = 0; w < DEC_WARPS; ++w) {
+            const float f = s_ml[w][gi][0] == -INFINITY ? 0.f : exp2f(s_ml[w][gi][0] - M);
+            num = fmaf(s_acc[w][gi][e], f, num);
+            den = fmaf(s_ml[w][gi][1], f, den);
+        }
+        out[size_t(grp_streams[s0 + gi]) * D + h * HD + e] = num / den;
     }
 }
 
@@ -228,10 +217,6 @@ __global__ void __launch_bounds__(256) k_argmax(const float* __restrict__ logits
 
 }  // namespace
 
-size_t attn_dec_smem(int L) {
-    return (size_t(DEC_MAX_G) * HD * (1 + DEC_THREADS / 32) + DEC_MAX_G + size_t(DEC_MAX_G) * L) * 4;
-}
-
 cudaError_t launch_kv_append(const float* k_new, const float* v_new, int S, int H, int ctx, const int* dpos,
                              __half* kc, __half* vc, cudaStream_t s) {
     const size_t total = size_t(S) * H * HD;
@@ -253,20 +238,22 @@ cudaError_t launch_pos_advance(int* dpos, cudaStream_t s) {
 }
 
 cudaError_t launch_attn_dec(const float* q, const __half* kc, const __half* vc, size_t kv_stride, int L,
-                            const int* dpos, int H, int n_groups, const int* grp_kv, const int* grp_off,
+                            const int* dpos, int H, int n_groups, int max_group, const int* grp_kv, const int* grp_off,
                             const int* grp_streams, float* out, cudaStream_t s) {
     if (!n_groups || !L) return cudaSuccess;
-    const size_t smem = attn_dec_smem(L);
-    static unsigned attr_dev_mask = 0;
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (smem > 48 * 1024 && !(attr_dev_mask & (1u << dev))) {
-        cudaError_t e = cudaFuncSetAttribute(k_attn_dec, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-        if (e != cudaSuccess) return e;
-        attr_dev_mask |= 1u << dev;
-    }
-    return launch_pdl(k_attn_dec, dim3(unsigned(H), unsigned(n_groups)), dim3(DEC_THREADS), smem, s, q, kc, vc,
-                      kv_stride, L, dpos, H, grp_kv, grp_off, grp_streams, out);
+    const dim3 grid = dim3(unsigned(H), unsigned(n_groups));
+    // registers scale with the queries a group may hold
+    if (max_group <= 1)
+        return launch_pdl(k_attn_dec<1>, grid, dim3(DEC_THREADS), 0, s, q, kc, vc, kv_stride, L, dpos, H, grp_kv,
+                          grp_off, grp_streams, out);
+    if (max_group <= 2)
+        return launch_pdl(k_attn_dec<2>, grid, dim3(DEC_THREADS), 0, s, q, kc, vc, kv_stride, L, dpos, H, grp_kv,
+                          grp_off, grp_streams, out);
+    if (max_group <= 4)
+        return launch_pdl(k_attn_dec<4>, grid, dim3(DEC_THREADS), 0, s, q, kc, vc, kv_stride, L, dpos, H, grp_kv,
+                          grp_off, grp_streams, out);
+    return launch_pdl(k_attn_dec<DEC_MAX_G>, grid, dim3(DEC_THREADS), 0, s, q, kc, vc, kv_stride, L, dpos, H, grp_kv,
+                      grp_off, grp_streams, out);
 }
 
 cudaError_t launch_argmax(const float* logits, int rows, int V, int limit, int32_t* best, cudaStream_t s) {
