@@ -573,6 +573,39 @@ def run_large_v3(args, dev, stream, rank, world):
     return res
 
 
+def run_profile_driver(args):
+    """Small fixed workloads for ncu captures (no timing line of record):
+    `logits` -- config 4's tied-logits GEMV (Q5_0 51865 x 1024, four weight
+    copies) at --m rows, --steps back-to-back launches; `decode` -- the
+    config-4 decoder (80 streams), begin then --steps greedy steps."""
+    import torch
+    from rusty_whisper_b200 import quant
+    quant.init(0)
+    dev = torch.device("cuda", 0)
+    if args.only == "logits":
+        n, k, dt = 51865, 1024, 6
+        raw = synth.random_blocks(dt, n, k, 5)
+        W = [quant.QTensor([n, k], dt, raw) for _ in range(4)]
+        x = torch.from_numpy(synth.normal(9, args.m * k).reshape(args.m, k)).to(dev)
+        qa = quant.QActs(args.m, k).quantize(x)
+        y = torch.empty((args.m, n), device=dev)
+        for r in range(args.steps):
+            qa.matmul(W[r % 4], out=y)
+    else:
+        from rusty_whisper_b200 import decoder
+        c = DEC_MEDIUM
+        t = synth.decoder_tensors(c["n_vocab"], c["n_ctx"], c["n_state"], c["n_layer"], 6, seed=7, reuse_layers=True)
+        dec = decoder.Decoder(c["n_vocab"], c["n_ctx"], c["n_state"], c["n_head"], c["n_layer"], t)
+        enc = torch.from_numpy(synth.normal(300, 16 * 1500 * c["n_state"]).reshape(16, 1500, c["n_state"])).to(dev)
+        dec.begin(enc, [w for w in range(16) for _ in range(5)])
+        tok = torch.zeros(80, dtype=torch.int32, device=dev)
+        for _ in range(args.steps):
+            tok = dec.step(tok, want="best")
+    torch.cuda.synchronize()
+    quant.stream_check()
+    print(json.dumps({"profile_driver": args.only, "m": args.m, "steps": args.steps}), flush=True)
+
+
 def run_gemv(args, dev, quant, w_np, hbm_peak, stream):
     """Decoder GEMVs of config 2: for each weight, R back-to-back launches
     over copies rotated past L2, one event pair per batch."""
@@ -769,9 +802,11 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
-    ap.add_argument("--only", default="all", choices=["all", "gemm", "encoder", "decoder", "large"],
-                    help="gemm: skip the GEMV, e2e, front-end and encoder legs; encoder: only the config-3 "
-                         "encoder leg (short runs for profiling)")
+    ap.add_argument("--m", type=int, default=1, help="activation rows for --only logits")
+    ap.add_argument("--only", default="all", choices=["all", "gemm", "encoder", "decoder", "large", "logits", "decode"],
+                    help="gemm: only the config-2 GEMM sweep; encoder / decoder / large: only that leg; "
+                         "logits: --steps launches of config 4's tied-logits GEMV at --m rows; decode: --steps "
+                         "config-4 decode steps, graphs off when RWQ_DECODER_GRAPHS=0 (short runs for profiling)")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", 1))
@@ -788,6 +823,9 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local_rank))
     try:
+        if args.only in ("logits", "decode"):
+            run_profile_driver(args)
+            return
         if args.only in ("encoder", "decoder", "large"):
             import torch
             from rusty_whisper_b200 import quant
