@@ -497,11 +497,17 @@ def run_large_v3(args, dev, stream, rank, world):
     prompt = sot.repeat(n_win, 1).t().contiguous().to(dev)
     eot = 50257
 
+    marks = {}
+
     def pipeline(n_steps, copy_out=True):
         x = host.to(dev, non_blocking=True)
         mel = mel_plan.batch(x)
         eo = enc.encode(mel)
+        marks["enc"] = torch.cuda.Event(enable_timing=True)
+        marks["enc"].record(stream)
         dec.begin(eo)
+        marks["begin"] = torch.cuda.Event(enable_timing=True)
+        marks["begin"].record(stream)
         for i in range(3):
             dec.step(prompt[i], want="none")
         out = torch.empty((n_steps, n_win), dtype=torch.int32, device=dev)
@@ -531,9 +537,13 @@ def run_large_v3(args, dev, stream, rank, world):
         tm = torch.tensor([tt], dtype=torch.float64, device=dev)
         dist.all_reduce(tm, op=dist.ReduceOp.MAX)
         tmax = float(tm.item())
+    stages = {"audio_mel_encoder_s": round(e0.elapsed_time(marks["enc"]) / 1e3, 3),
+              "cross_kv_s": round(marks["enc"].elapsed_time(marks["begin"]) / 1e3, 3),
+              "decode_s": round(marks["begin"].elapsed_time(e1) / 1e3, 3)}
     res = {"workload": "BASELINE config 5: large-v3 shape (128 mels; encoder 32 x d1280/20 heads/FFN 5120; decoder 32 "
                        "blocks, vocab 51866), Q4_0, 256 windows x 30 s sharded over the ranks, greedy 224 tokens",
            "audio_s_per_s": round(total_win * 30.0 / tmax, 1), "s_per_job": round(tmax, 3),
+           "rank0_stages": stages, "ms_per_decode_step": round(stages["decode_s"] / (steps + 4) * 1e3, 3),
            "windows_per_rank": n_win, "scaling": "strong (256 windows in total)",
            "h2d_bytes_per_rank": int(host.numel() * 4), "d2h_bytes_per_rank": int(steps * n_win * 4),
            "timing": "CUDA events around host audio -> tokens on the host, max over ranks",
@@ -593,12 +603,18 @@ def run_profile_driver(args):
             qa.matmul(W[r % 4], out=y)
     else:
         from rusty_whisper_b200 import decoder
-        c = DEC_MEDIUM
-        t = synth.decoder_tensors(c["n_vocab"], c["n_ctx"], c["n_state"], c["n_layer"], 6, seed=7, reuse_layers=True)
+        if args.m == 256:   # config 5's decoder: large-v3 shape, Q4_0, 256 windows, one stream each
+            c = dict(n_vocab=LARGE_V3["n_vocab"], n_ctx=448, n_state=1280, n_head=20, n_layer=32)
+            n_win, per, dt = 256, 1, 2
+        else:               # config 4: whisper-medium, Q5_0, 16 windows x 5 streams
+            c, n_win, per, dt = DEC_MEDIUM, 16, 5, 6
+        t = synth.decoder_tensors(c["n_vocab"], c["n_ctx"], c["n_state"], c["n_layer"], dt, seed=7, reuse_layers=True)
         dec = decoder.Decoder(c["n_vocab"], c["n_ctx"], c["n_state"], c["n_head"], c["n_layer"], t)
-        enc = torch.from_numpy(synth.normal(300, 16 * 1500 * c["n_state"]).reshape(16, 1500, c["n_state"])).to(dev)
-        dec.begin(enc, [w for w in range(16) for _ in range(5)])
-        tok = torch.zeros(80, dtype=torch.int32, device=dev)
+        enc = torch.empty((n_win, 1500, c["n_state"]), device=dev)
+        for w in range(n_win):   # seeded rows, drawn per window to bound host memory
+            enc[w] = torch.from_numpy(synth.normal(300 + w % 8, 1500 * c["n_state"]).reshape(1500, c["n_state"]))
+        dec.begin(enc, [w for w in range(n_win) for _ in range(per)])
+        tok = torch.zeros(n_win * per, dtype=torch.int32, device=dev)
         for _ in range(args.steps):
             tok = dec.step(tok, want="best")
     torch.cuda.synchronize()
@@ -802,7 +818,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
-    ap.add_argument("--m", type=int, default=1, help="activation rows for --only logits")
+    ap.add_argument("--m", type=int, default=1,
+                    help="--only logits: activation rows; --only decode: 256 selects config 5's decoder")
     ap.add_argument("--only", default="all", choices=["all", "gemm", "encoder", "decoder", "large", "logits", "decode"],
                     help="gemm: only the config-2 GEMM sweep; encoder / decoder / large: only that leg; "
                          "logits: --steps launches of config 4's tied-logits GEMV at --m rows; decode: --steps "
