@@ -154,9 +154,13 @@ int rwq_set_gemm_path(int path);
  * lane per block, lanes per row from k, launches of 8 rows), 2 =
  * integer-MMA kernel (mma.sync m16n8k32: one instruction per block for 16
  * weight rows x 8 activation rows, up to 64 rows per launch sharing each
- * decoded weight fragment).  Both compute the reference's per-block formula
- * (quant.rs:349-351, :452-454) with exact integer block dots; they differ
- * only in f32 summation order.  Applies to this host thread. */
+ * decoded weight fragment), 3 = tiled integer-MMA kernel (the same
+ * arithmetic tiled like a GEMM: 32-64 weight rows x 32-64 activation rows
+ * per CTA, K streamed through shared memory; automatic from 32 rows on).
+ * All compute the reference's per-block formula (quant.rs:349-351,
+ * :452-454) with exact integer block dots; 1 differs from the others only
+ * in f32 summation order, 0, 2 and 3 give identical bits.  Applies to this
+ * host thread. */
 int rwq_set_gemv_kernel(int kind);
 
 /* Synchronize `stream` and report any fault a kernel recorded on it. */

@@ -536,7 +536,7 @@ int rwq_set_gemm_path(int path) {
 }
 
 int rwq_set_gemv_kernel(int kind) {
-    if (kind < 0 || kind > 2) return fail(RWQ_ERR_ARG, "kind must be 0, 1 or 2");
+    if (kind < 0 || kind > 3) return fail(RWQ_ERR_ARG, "kind must be 0, 1, 2 or 3");
     rwq::set_gemv_kind(kind);
     return RWQ_OK;
 }

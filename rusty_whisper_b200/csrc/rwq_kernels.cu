@@ -3,6 +3,8 @@
 // per-block integer dots (debug/parity), the decoder GEMVs (int8 and
 // dequant-then-f32), and the builder of the tensor-core operand cache.
 #include <cuda_fp16.h>
+#include <cstdio>
+#include <cstdlib>
 #include "rwq_common.cuh"
 #include "rwq_internal.h"
 #include "rwq_decoder.h"
@@ -884,6 +886,370 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
     asm volatile("cp.async.wait_group 0;" ::: "memory");
 }
 
+// ------------------------------------------------------------ GEMV tiles
+// The GEMV family at many activation rows (one decoder step over many
+// streams): the integer-MMA arithmetic of k_gemv_mma, tiled like a GEMM so
+// that each decoded weight fragment serves 8*NT activation rows and each
+// staged activation fragment 16*WN weight rows.  A CTA of 2 x 2 warps owns
+// BN = 32*WN weight rows x BM = 16*NT activation rows and walks K one
+// 4-block group at a time through a cp.async ring of GT_STAGES groups
+// (weight codes/qh/d/m as in the planes; activation codes row-major with a
+// 144-byte row pitch, so the B-fragment words of 8 rows x 4 quad lanes
+// fall in 32 distinct banks; sum(q_a), d_a, d_a*sum(q_a) as [row][4]).
+//
+// Every output accumulates its blocks in kb order with exactly the
+// operations of k_gemv_mma, and the K ranges that k_gemv_mma gives to
+// different warps are accumulated separately here and added in the same
+// order: for KS > 1 each of its K slices is one CTA of a cluster of KS
+// CTAs, whose partial tiles are added in slice order through distributed
+// shared memory (each CTA adds and stores 1/KS of the tile); for KS == 1
+// the head/tail split of a tile shared by two of its warps is reproduced
+// inside the CTA.  The results are therefore bit-identical to k_gemv_mma's
+// for every m, and a row's result stays independent of m across the whole
+// GEMV family (quant.rs:1372-1384).
+constexpr int GT_THREADS = 128;
+constexpr int GT_STAGES = 4;
+constexpr int GT_APITCH = 144;   // activation code bytes per row in shared memory
+
+template <int DT, int WN, int NT>
+struct TileSmem {
+    static constexpr int BN = 32 * WN, BM = 16 * NT;
+    static constexpr int QROW = 4 * qs_bytes(DT) + (DT == Q8_0 ? 16 : 0);   // padded for Q8_0 (bank spread)
+    static constexpr int WQ = 0;
+    static constexpr int WH = WQ + BN * QROW;
+    static constexpr int WD = WH + (has_qh(DT) ? BN * 16 : 0);
+    static constexpr int WM = WD + BN * 8;
+    static constexpr int AQ = WM + (has_min(DT) ? BN * 8 : 0);
+    static constexpr int AS = AQ + BM * GT_APITCH;                       // sum(q_a)  [BM][4] int
+    static constexpr int AD = AS + (code_offset(DT) ? BM * 16 : 0);      // d_a       [BM][4] f32
+    static constexpr int AU = AD + BM * 16;                              // d_a*sum   [BM][4] f32
+    static constexpr int STAGE = AU + (has_min(DT) ? BM * 16 : 0);
+    static constexpr int BYTES = GT_STAGES * STAGE;
+};
+
+__device__ __forceinline__ void gt_cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// Shared::cluster address of shared byte offset `off` in cluster CTA `rank`.
+__device__ __forceinline__ uint32_t gt_mapa(uint32_t off, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(off), "r"(rank));
+    return r;
+}
+__device__ __forceinline__ float4 gt_ld_cluster4(uint32_t addr) {
+    float4 v;
+    asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(addr) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ void cp_async16z(uint32_t dst, const void* src, bool ok) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(ok ? 16 : 0) : "memory");
+}
+__device__ __forceinline__ void cp_async4z(uint32_t dst, const void* src, bool ok) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(dst), "l"(src), "r"(ok ? 4 : 0) : "memory");
+}
+
+// Start of the s-th K slice (s >= 1) that k_gemv_mma uses for weight tile
+// T, or a value past every group if there is none.  KS > 1: slice s of the
+// group range starts at s*ng/KS.  KS == 1: k_gemv_mma's CTA c owns tiles
+// [c*tiles/gx, (c+1)*tiles/gx) and its 8 warps split the (tile, group)
+// items evenly; a warp range that starts inside tile T splits it there.
+__device__ inline int gemv_slice_start(int T, int s, int ks, int ng, int gx, int tiles) {
+    constexpr int NONE = 1 << 30;
+    if (ks > 1) return s < ks ? s * ng / ks : NONE;
+    if (s != 1 || gx <= 0) return NONE;
+    int c = int(int64_t(T) * gx / tiles);
+    while (c > 0 && int(int64_t(c) * tiles / gx) > T) --c;
+    while (c + 1 < gx && int(int64_t(c + 1) * tiles / gx) <= T) ++c;
+    const int t_lo = int(int64_t(c) * tiles / gx), t_hi = int(int64_t(c + 1) * tiles / gx);
+    const int nt = t_hi - t_lo;
+    if (nt < 8) return NONE;   // whole tiles per warp
+    const int items = nt * ng, local = (T - t_lo) * ng;
+    for (int w = 1; w < 8; ++w) {
+        const int i = w * items / 8;
+        if (i > local && i < local + ng) return i - local;
+    }
+    return NONE;
+}
+
+template <int DT, int WN, int NT>
+__global__ void __launch_bounds__(GT_THREADS)
+    k_gemv_tile(const uint8_t* __restrict__ qs, const uint32_t* __restrict__ qh, const uint16_t* __restrict__ dp,
+                const uint16_t* __restrict__ mp, const int8_t* __restrict__ q8, const float* __restrict__ da,
+                const int32_t* __restrict__ sa, const float* __restrict__ ua, int M, int N, int K,
+                const float* __restrict__ bias, float* __restrict__ y, int ks, int gx, int vec16) {
+    using L = TileSmem<DT, WN, NT>;
+    constexpr int QSB = qs_bytes(DT), WCH = 4 * QSB / 16;   // 16-byte chunks of one row's group codes
+    pdl_trigger();
+    const int nb = K / QK, nb4 = round4(nb), ng = nb4 / 4, tiles = (N + 15) / 16;
+    // ks > 1: the launch has clusters of ks CTAs along x, CTA `rank` of a
+    // cluster takes K slice `rank`; ks == 1: one CTA takes all of K.
+    const int cs = ks > 1 ? ks : 1, rank = int(blockIdx.x) % cs;
+    const int g_lo = rank * ng / cs, g_hi = (rank + 1) * ng / cs;
+    const int n0 = int(blockIdx.x) / cs * L::BN, m0 = int(blockIdx.y) * L::BM;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, wn = warp & 1, wm = warp >> 1;
+    const int g = lane >> 2, c = lane & 3;
+
+    extern __shared__ __align__(16) uint8_t smem[];
+    const uint32_t sbase = uint32_t(__cvta_generic_to_shared(smem));
+
+    auto issue_w = [&](int G, int slot) {
+        const uint32_t st = sbase + uint32_t(slot * L::STAGE);
+        for (int i = tid; i < L::BN * WCH; i += GT_THREADS) {
+            const int r = i / WCH, ch = i % WCH, row = min(n0 + r, N - 1);
+            const uint8_t* src = qs + ((size_t(row) * nb4 + size_t(4 * G)) * QSB + ch * 16);
+            cp_async16(st + L::WQ + r * L::QROW + ch * 16, src);
+        }
+        for (int r = tid; r < L::BN; r += GT_THREADS) {
+            const size_t pb = size_t(min(n0 + r, N - 1)) * nb4 + size_t(4 * G);
+            if (has_qh(DT)) cp_async16(st + L::WH + r * 16, qh + pb);
+            cp_async8(st + L::WD + r * 8, dp + pb);
+            if (has_min(DT)) cp_async8(st + L::WM + r * 8, mp + pb);
+        }
+    };
+    auto issue_a = [&](int G, int slot) {
+        const uint32_t st = sbase + uint32_t(slot * L::STAGE);
+        for (int i = tid; i < L::BM * 8; i += GT_THREADS) {
+            const int r = i >> 3, ch = i & 7, row = m0 + r;
+            const bool ok = row < M && 4 * G + (ch >> 1) < nb;
+            const int8_t* src = ok ? q8 + (size_t(row) * K + size_t(128 * G) + ch * 16) : q8;
+            cp_async16z(st + L::AQ + r * GT_APITCH + ch * 16, src, ok);
+        }
+        if (vec16) {   // nb % 4 == 0: every group is whole
+            for (int r = tid; r < L::BM; r += GT_THREADS) {
+                const bool ok = m0 + r < M;
+                const size_t o = ok ? size_t(m0 + r) * nb + size_t(4 * G) : 0;
+                if (code_offset(DT)) cp_async16z(st + L::AS + r * 16, sa + o, ok);
+                cp_async16z(st + L::AD + r * 16, da + o, ok);
+                if (has_min(DT)) cp_async16z(st + L::AU + r * 16, ua + o, ok);
+            }
+        } else {       // pad blocks (kb >= nb) read as zeros: seed 1.5*2^23, scales 0
+            for (int i = tid; i < L::BM * 4; i += GT_THREADS) {
+                const int r = i >> 2, b = i & 3;
+                const bool ok = m0 + r < M && 4 * G + b < nb;
+                const size_t o = ok ? size_t(m0 + r) * nb + size_t(4 * G + b) : 0;
+                if (code_offset(DT)) cp_async4z(st + L::AS + i * 4, sa + o, ok);
+                cp_async4z(st + L::AD + i * 4, da + o, ok);
+                if (has_min(DT)) cp_async4z(st + L::AU + i * 4, ua + o, ok);
+            }
+        }
+    };
+
+    // Slice bookkeeping per m-tile: `tot` holds the finished slices, `part`
+    // the running one.
+    float2 t01[WN][NT], t23[WN][NT], p01[WN][NT], p23[WN][NT];
+    int nsl[WN], nxt[WN];
+#pragma unroll
+    for (int mt = 0; mt < WN; ++mt) {
+        const int T = (n0 >> 4) + wn * WN + mt;
+        nsl[mt] = 0;
+        nxt[mt] = cs > 1 ? (1 << 30) : gemv_slice_start(T, 1, ks, ng, gx, tiles);
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+            p01[mt][nt] = p23[mt][nt] = t01[mt][nt] = t23[mt][nt] = make_float2(0.f, 0.f);
+        }
+    }
+    auto close_slice = [&](int mt) {
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+            if (nsl[mt] == 0) {
+                t01[mt][nt] = p01[mt][nt];
+                t23[mt][nt] = p23[mt][nt];
+            } else {
+                t01[mt][nt] = __fadd2_rn(t01[mt][nt], p01[mt][nt]);
+                t23[mt][nt] = __fadd2_rn(t23[mt][nt], p23[mt][nt]);
+            }
+            p01[mt][nt] = p23[mt][nt] = make_float2(0.f, 0.f);
+        }
+        ++nsl[mt];
+        nxt[mt] = cs > 1 ? (1 << 30) : gemv_slice_start((n0 >> 4) + wn * WN + mt, nsl[mt] + 1, ks, ng, gx, tiles);
+    };
+
+    const int n_g = g_hi - g_lo;
+    for (int u = 0; u < GT_STAGES - 1; ++u)
+        if (u < n_g) issue_w(g_lo + u, u);
+    pdl_wait();
+    for (int u = 0; u < GT_STAGES - 1; ++u) {
+        if (u < n_g) issue_a(g_lo + u, u);
+        cp_async_commit();
+    }
+
+    const float2 nmag = make_float2(-MAGIC_F, -MAGIC_F);
+    for (int i = 0; i < n_g; ++i) {
+        const int G = g_lo + i;
+        asm volatile("cp.async.wait_group %0;" ::"n"(GT_STAGES - 2) : "memory");
+        __syncthreads();
+        {
+            const int in = i + GT_STAGES - 1;
+            if (in < n_g) {
+                issue_w(g_lo + in, in % GT_STAGES);
+                issue_a(g_lo + in, in % GT_STAGES);
+            }
+            cp_async_commit();
+        }
+#pragma unroll
+        for (int mt = 0; mt < WN; ++mt)
+            while (G == nxt[mt]) close_slice(mt);
+
+        const uint8_t* st = smem + (i % GT_STAGES) * L::STAGE;
+        // Weight fragments of this warp's m-tiles, decoded for all 4 blocks.
+        uint32_t a[WN][4][4];
+        float db[WN][2][4], mb[WN][2][4];
+#pragma unroll
+        for (int mt = 0; mt < WN; ++mt) {
+            MmaGroup<DT> r;
+#pragma unroll
+            for (int rr = 0; rr < 2; ++rr) {
+                const int row = (wn * WN + mt) * 16 + g + 8 * rr;
+                const uint8_t* q = st + L::WQ + row * L::QROW + c * QSB;
+                const uint4 v = *reinterpret_cast<const uint4*>(q);
+                r.q[rr][0] = v.x; r.q[rr][1] = v.y; r.q[rr][2] = v.z; r.q[rr][3] = v.w;
+                if (DT == Q8_0) {
+                    const uint4 v2 = *reinterpret_cast<const uint4*>(q + 16);
+                    r.q[rr][4 % (QSB / 4)] = v2.x; r.q[rr][5 % (QSB / 4)] = v2.y;
+                    r.q[rr][6 % (QSB / 4)] = v2.z; r.q[rr][7 % (QSB / 4)] = v2.w;
+                }
+                if (has_qh(DT)) {
+                    const uint4 h = *reinterpret_cast<const uint4*>(st + L::WH + row * 16);
+                    r.h[rr][0] = h.x; r.h[rr][1 % 4] = h.y; r.h[rr][2 % 4] = h.z; r.h[rr][3 % 4] = h.w;
+                }
+                const uint2 dd = *reinterpret_cast<const uint2*>(st + L::WD + row * 8);
+                const float2 d01 = h2f2(dd.x), d23 = h2f2(dd.y);
+                db[mt][rr][0] = d01.x; db[mt][rr][1] = d01.y; db[mt][rr][2] = d23.x; db[mt][rr][3] = d23.y;
+                if (has_min(DT)) {
+                    const uint2 mm = *reinterpret_cast<const uint2*>(st + L::WM + row * 8);
+                    const float2 m01 = h2f2(mm.x), m23 = h2f2(mm.y);
+                    mb[mt][rr][0] = m01.x; mb[mt][rr][1] = m01.y; mb[mt][rr][2] = m23.x; mb[mt][rr][3] = m23.y;
+                }
+            }
+#pragma unroll
+            for (int b = 0; b < 4; ++b) {
+                if (DT == Q8_0) {
+                    a[mt][b][0] = r.q[0][(2 * b) % (QSB / 4)];
+                    a[mt][b][1] = r.q[1][(2 * b) % (QSB / 4)];
+                    a[mt][b][2] = r.q[0][(2 * b + 1) % (QSB / 4)];
+                    a[mt][b][3] = r.q[1][(2 * b + 1) % (QSB / 4)];
+                } else {
+#pragma unroll
+                    for (int rr = 0; rr < 2; ++rr) {
+                        const uint32_t w = r.q[rr][b % (QSB / 4)];
+                        uint32_t lo = w & 0x0F0F0F0Fu, hi = (w >> 4) & 0x0F0F0F0Fu;
+                        if (has_qh(DT)) {
+                            const uint32_t h = r.h[rr][b % (has_qh(DT) ? 4 : 1)];
+                            lo |= (h << (4 - c)) & 0x10101010u;
+                            hi |= (h >> c) & 0x10101010u;
+                        }
+                        a[mt][b][rr] = lo;
+                        a[mt][b][2 + rr] = hi;
+                    }
+                }
+            }
+        }
+        // Activation n-tiles: B fragments (row g of the n-tile, words c and
+        // 4+c of each block) and the scales of columns 2c, 2c+1.
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+            const int col = (wm * NT + nt) * 8;
+            const uint8_t* aq = st + L::AQ + (col + g) * GT_APITCH + 4 * c;
+            const int r0 = col + 2 * c;
+            int4 s0 = make_int4(0, 0, 0, 0), s1 = make_int4(0, 0, 0, 0);
+            if (code_offset(DT)) {
+                s0 = *reinterpret_cast<const int4*>(st + L::AS + r0 * 16);
+                s1 = *reinterpret_cast<const int4*>(st + L::AS + (r0 + 1) * 16);
+            }
+            const float4 d0 = *reinterpret_cast<const float4*>(st + L::AD + r0 * 16);
+            const float4 d1 = *reinterpret_cast<const float4*>(st + L::AD + (r0 + 1) * 16);
+            float4 u0 = make_float4(0.f, 0.f, 0.f, 0.f), u1 = u0;
+            if (has_min(DT)) {
+                u0 = *reinterpret_cast<const float4*>(st + L::AU + r0 * 16);
+                u1 = *reinterpret_cast<const float4*>(st + L::AU + (r0 + 1) * 16);
+            }
+            const int sx[4] = {s0.x, s0.y, s0.z, s0.w}, sy[4] = {s1.x, s1.y, s1.z, s1.w};
+            const float dx[4] = {d0.x, d0.y, d0.z, d0.w}, dy[4] = {d1.x, d1.y, d1.z, d1.w};
+            const float ux[4] = {u0.x, u0.y, u0.z, u0.w}, uy[4] = {u1.x, u1.y, u1.z, u1.w};
+#pragma unroll
+            for (int b = 0; b < 4; ++b) {
+                const uint2 bf = make_uint2(*reinterpret_cast<const uint32_t*>(aq + b * 32),
+                                            *reinterpret_cast<const uint32_t*>(aq + b * 32 + 16));
+                const int2 ci = code_offset(DT)
+                                    ? make_int2(int(MAGIC_BITS - uint32_t(code_offset(DT) * sx[b])),
+                                                int(MAGIC_BITS - uint32_t(code_offset(DT) * sy[b])))
+                                    : make_int2(int(MAGIC_BITS), int(MAGIC_BITS));
+                const float2 dab = make_float2(dx[b], dy[b]);
+#pragma unroll
+                for (int mt = 0; mt < WN; ++mt) {
+                    int dd[4];
+                    mma_i8<DT == Q8_0>(a[mt][b], bf, ci, dd);
+                    const float2 s01 = __fadd2_rn(make_float2(__int_as_float(dd[0]), __int_as_float(dd[1])), nmag);
+                    const float2 s23 = __fadd2_rn(make_float2(__int_as_float(dd[2]), __int_as_float(dd[3])), nmag);
+                    p01[mt][nt] = __ffma2_rn(__fmul2_rn(dab, make_float2(db[mt][0][b], db[mt][0][b])), s01, p01[mt][nt]);
+                    p23[mt][nt] = __ffma2_rn(__fmul2_rn(dab, make_float2(db[mt][1][b], db[mt][1][b])), s23, p23[mt][nt]);
+                    if (has_min(DT)) {
+                        const float2 uab = make_float2(ux[b], uy[b]);
+                        p01[mt][nt] = __ffma2_rn(uab, make_float2(mb[mt][0][b], mb[mt][0][b]), p01[mt][nt]);
+                        p23[mt][nt] = __ffma2_rn(uab, make_float2(mb[mt][1][b], mb[mt][1][b]), p23[mt][nt]);
+                    }
+                }
+            }
+        }
+    }
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
+    if (cs > 1) {
+        // This CTA's slice partial -> own shared memory [BM][BN]; after the
+        // cluster barrier CTA `rank` adds the slices of its share of the
+        // tile in slice order (k_gemv_mma's order) and stores it.
+        __syncthreads();
+        float* part = reinterpret_cast<float*>(smem);
+#pragma unroll
+        for (int mt = 0; mt < WN; ++mt)
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) {
+                const int rl = (wn * WN + mt) * 16 + g, cl = (wm * NT + nt) * 8 + 2 * c;
+                part[cl * L::BN + rl] = p01[mt][nt].x;
+                part[(cl + 1) * L::BN + rl] = p01[mt][nt].y;
+                part[cl * L::BN + rl + 8] = p23[mt][nt].x;
+                part[(cl + 1) * L::BN + rl + 8] = p23[mt][nt].y;
+            }
+        gt_cluster_sync();
+        constexpr int Q4 = L::BN * L::BM / 4;
+        const int q_lo = rank * Q4 / cs, q_hi = (rank + 1) * Q4 / cs;
+        for (int q = q_lo + tid; q < q_hi; q += GT_THREADS) {
+            const uint32_t off = sbase + uint32_t(q * 16);
+            float4 v = gt_ld_cluster4(gt_mapa(off, 0));
+            for (int s2 = 1; s2 < cs; ++s2) {
+                const float4 t = gt_ld_cluster4(gt_mapa(off, uint32_t(s2)));
+                v.x = __fadd_rn(v.x, t.x); v.y = __fadd_rn(v.y, t.y);
+                v.z = __fadd_rn(v.z, t.z); v.w = __fadd_rn(v.w, t.w);
+            }
+            const int col = m0 + 4 * q / L::BN, row = n0 + 4 * q % L::BN;
+            const float vv[4] = {v.x, v.y, v.z, v.w};
+            if (col < M) {
+#pragma unroll
+                for (int j = 0; j < 4; ++j)
+                    if (row + j < N) y[size_t(col) * N + row + j] = bias ? __fadd_rn(vv[j], __ldg(bias + row + j)) : vv[j];
+            }
+        }
+        gt_cluster_sync();   // no CTA leaves while its partial is being read
+        return;
+    }
+#pragma unroll
+    for (int mt = 0; mt < WN; ++mt) {
+        close_slice(mt);
+        const int T = (n0 >> 4) + wn * WN + mt;
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+            const float v[4] = {t01[mt][nt].x, t01[mt][nt].y, t23[mt][nt].x, t23[mt][nt].y};
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const int row = T * 16 + g + ((i & 2) ? 8 : 0);
+                const int col = m0 + (wm * NT + nt) * 8 + 2 * c + (i & 1);
+                if (row < N && col < M) y[size_t(col) * N + row] = bias ? __fadd_rn(v[i], __ldg(bias + row)) : v[i];
+            }
+        }
+    }
+}
+
 // ------------------------------------------------------------- GEMV f32
 // Dequant-then-fp path (the f32 tier, quant.rs:995-1018): weights
 // dequantized bit-exactly, dotted with unquantized f32 activations.
@@ -1269,6 +1635,72 @@ struct GemvMmaF {
     }
 };
 
+// Tile configuration of k_gemv_tile: RWQ_GEMV_TILE="WN,NT" (WN in {1,2},
+// NT in {2,4}) fixes it for sweeps; otherwise NT = 4 when the rows fill
+// 64-row CTA tiles with little waste, WN = 2 when the larger weight tile
+// still leaves two CTAs per SM.  Every configuration gives the same bits.
+inline void gemv_tile_cfg(int m, int n, int ks, int sms, int* wn, int* nt) {
+    static int env_wn = -1, env_nt = -1;
+    if (env_wn < 0) {
+        env_wn = env_nt = 0;
+        if (const char* e = getenv("RWQ_GEMV_TILE")) {
+            int a = 0, b = 0;
+            if (sscanf(e, "%d,%d", &a, &b) == 2 && (a == 1 || a == 2) && (b == 2 || b == 4)) env_wn = a, env_nt = b;
+        }
+    }
+    if (env_wn) { *wn = env_wn; *nt = env_nt; return; }
+    *nt = (m % 64 == 0 || m > 128) ? 4 : 2;
+    const long rows = (m + 16 * *nt - 1) / (16 * *nt);
+    *wn = (long((n + 63) / 64) * rows * ks >= 2L * sms) ? 2 : 1;
+}
+
+template <int DT, int WN, int NT>
+cudaError_t gemv_tile_go(const ActsView& v, const Weight& w, const float* bias, float* y, int ks, int gx,
+                         int vec16, cudaStream_t s) {
+    using L = TileSmem<DT, WN, NT>;
+    auto kern = k_gemv_tile<DT, WN, NT>;
+    int dev = 0, sms = 148;
+    dev_sms(&dev, &sms);
+    static unsigned attr_dev_mask = 0;
+    if (!(attr_dev_mask & (1u << dev))) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::BYTES);
+        if (e != cudaSuccess) return e;
+        attr_dev_mask |= 1u << dev;
+    }
+    const int cs = ks > 1 ? ks : 1;
+    const dim3 grid(unsigned((w.n + L::BN - 1) / L::BN * cs), unsigned((v.m + L::BM - 1) / L::BM));
+    if (cs == 1)
+        return launch_pdl(kern, grid, dim3(GT_THREADS), size_t(L::BYTES), s, w.qs, w.qh, w.d, w.m, v.q8, v.d,
+                          v.sum, v.u, v.m, w.n, w.k, bias, y, ks, gx, vec16);
+    return launch_pdl_cluster(kern, grid, dim3(GT_THREADS), size_t(L::BYTES), cs, s, w.qs, w.qh, w.d, w.m, v.q8,
+                              v.d, v.sum, v.u, v.m, w.n, w.k, bias, y, ks, gx, vec16);
+}
+
+template <int DT>
+struct GemvTileF {
+    static cudaError_t run(const ActsView& v, const Weight& w, const float* bias, float* y, cudaStream_t s) {
+        int dev = 0, sms = 148;
+        dev_sms(&dev, &sms);
+        // k_gemv_mma's K-split and (KS == 1) grid, whose summation order
+        // k_gemv_tile reproduces.
+        const int ks = gemv_mma_ks(w.n, w.nb), tiles = (w.n + 15) / 16;
+        int gx = 0;
+        if (ks == 1) {
+            gx = tiles / (GM_THREADS / 32);
+            gx = gx < 1 ? 1 : (gx > 2 * sms ? 2 * sms : gx);
+        }
+        const int vec16 = (v.nb % 4 == 0 && (reinterpret_cast<uintptr_t>(v.d) & 15) == 0 &&
+                           (reinterpret_cast<uintptr_t>(v.sum) & 15) == 0 &&
+                           (reinterpret_cast<uintptr_t>(v.u) & 15) == 0) ? 1 : 0;
+        int wn = 1, nt = 2;
+        gemv_tile_cfg(v.m, w.n, ks, sms, &wn, &nt);
+        if (wn == 1) return nt == 2 ? gemv_tile_go<DT, 1, 2>(v, w, bias, y, ks, gx, vec16, s)
+                                    : gemv_tile_go<DT, 1, 4>(v, w, bias, y, ks, gx, vec16, s);
+        return nt == 2 ? gemv_tile_go<DT, 2, 2>(v, w, bias, y, ks, gx, vec16, s)
+                       : gemv_tile_go<DT, 2, 4>(v, w, bias, y, ks, gx, vec16, s);
+    }
+};
+
 template <int DT>
 struct GemvRowsF {
     static cudaError_t run(int nb, int* out) {
@@ -1278,6 +1710,12 @@ struct GemvRowsF {
 };
 
 thread_local int t_gemv_kind = 0;
+
+// Rows from which the automatic choice takes k_gemv_tile (measured on the
+// whisper decoder shapes): 32 when k_gemv_mma splits K (its CTAs then
+// re-stage the activations per 16 weight rows), 80 for the wide weights
+// it runs without a split (the logits), where both are close below that.
+int gemv_tile_min_m(int n, int nb) { return gemv_mma_ks(n, nb) > 1 ? 32 : 80; }
 
 template <int DT, int L, int MR>
 cudaError_t gemv_f32_launch(const float* a, int m, const Weight& w, const float* bias, float* y, cudaStream_t s) {
@@ -1352,8 +1790,11 @@ cudaError_t launch_gemv_i8(const ActsView& v, const Weight& w, const float* bias
     // alternative (tests, benchmarks).  The MMA kernel addresses the planes
     // with 32-bit offsets.
     const int kind = t_gemv_kind ? t_gemv_kind : 2;
-    const bool mma =
-        kind == 2 && uint64_t(w.n) * uint64_t(round4(w.nb)) * uint64_t(qs_bytes(w.dtype)) < (uint64_t(1) << 32);
+    const bool mma = (kind == 2 || kind == 3) &&
+                     uint64_t(w.n) * uint64_t(round4(w.nb)) * uint64_t(qs_bytes(w.dtype)) < (uint64_t(1) << 32);
+    // The tiled kernel needs 16-byte aligned activation codes; it computes
+    // exactly what k_gemv_mma does, so the switch point is a speed choice.
+    const bool tile_ok = mma && (reinterpret_cast<uintptr_t>(v.q8) & 15) == 0;
     // The MMA kernel takes all rows in one launch (CTA rows of up to 64
     // activation rows share the weights through L2); dp4a launches 8 rows.
     const int per = mma ? GEMV_FAMILY_MAX_M : GEMV_MAX_M;
@@ -1365,8 +1806,10 @@ cudaError_t launch_gemv_i8(const ActsView& v, const Weight& w, const float* bias
         c.sum = v.sum + size_t(m0) * v.nb;
         c.u = v.u + size_t(m0) * v.nb;
         float* yc = y + size_t(m0) * w.n;
-        const cudaError_t e = mma ? by_dtype<GemvMmaF>(w.dtype, c, w, bias, yc, s)
-                                  : by_dtype<GemvI8F>(w.dtype, c, w, bias, yc, s);
+        const bool tile = tile_ok && (kind == 3 || (t_gemv_kind == 0 && c.m >= gemv_tile_min_m(w.n, w.nb)));
+        const cudaError_t e = tile  ? by_dtype<GemvTileF>(w.dtype, c, w, bias, yc, s)
+                              : mma ? by_dtype<GemvMmaF>(w.dtype, c, w, bias, yc, s)
+                                    : by_dtype<GemvI8F>(w.dtype, c, w, bias, yc, s);
         if (e != cudaSuccess) return e;
     }
     return cudaSuccess;

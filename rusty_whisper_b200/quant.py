@@ -298,7 +298,9 @@ def set_gemm_path(path: int) -> None:
 
 
 def set_gemv_kernel(kind: int) -> None:
-    """GEMV kernel for m <= 8: 0 automatic, 1 dp4a, 2 integer MMA."""
+    """Kernel of the GEMV family (m <= 256): 0 automatic (integer MMA, tiled
+    from 32 rows on), 1 dp4a, 2 integer MMA only, 3 tiled integer MMA only.
+    Kinds 0, 2 and 3 give bit-identical results."""
     _lib.check(_lib.lib().rwq_set_gemv_kernel(kind))
 
 

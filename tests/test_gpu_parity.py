@@ -103,14 +103,14 @@ def test_matmul_int8_matches_oracle(rq, orc, dtype, m, k, n):
         assert close(y, orc.int8_scalar_matmul(a, dtype, raw, n)) < TOL
 
 
-@pytest.mark.parametrize("kind", [1, 2])
+@pytest.mark.parametrize("kind", [1, 2, 3])
 @pytest.mark.parametrize("dtype", FORMATS)
 @pytest.mark.parametrize("m,k,n", [(1, 1024, 1000), (2, 96, 41), (5, 768, 3072), (7, 160, 333), (8, 3072, 768),
                                    (3, 1280, 5120), (5, 4096, 257), (6, 8192, 40), (13, 1024, 700), (40, 256, 300),
                                    (64, 1280, 1280), (80, 1024, 1024), (200, 5120, 256)])
 def test_gemv_kernels_match_oracle(rq, orc, kind, dtype, m, k, n):
-    """Both GEMV kernels (dp4a, integer MMA) at every K-split and tail, one
-    to several launches of rows."""
+    """The GEMV kernels (dp4a, integer MMA, tiled integer MMA) at every
+    K-split and tail, one to several launches of rows."""
     if m * n * k > 100_000_000 and kind == 1:
         pytest.skip("dp4a at this size is covered by the smaller cases")
     a, raw = _case(dtype, m, k, n, 17 * dtype + m + k + kind)
@@ -131,7 +131,7 @@ def test_gemv_kernels_match_oracle(rq, orc, kind, dtype, m, k, n):
         assert close(y, orc.matmul_t_q(a, dtype, raw, n)) < TOL
 
 
-@pytest.mark.parametrize("kind", [1, 2])
+@pytest.mark.parametrize("kind", [1, 2, 3])
 def test_gemv_batch_invariance_per_kernel(rq, kind):
     """Within each GEMV kernel a row's result is the same for M = 1..8."""
     import torch
@@ -145,6 +145,33 @@ def test_gemv_batch_invariance_per_kernel(rq, kind):
                 y8 = rq.matmul_t_q(a, w)
                 for mm in (1, 2, 5, 7):
                     assert torch.equal(rq.matmul_t_q(a[:mm], w), y8[:mm])
+    finally:
+        rq.set_gemv_kernel(0)
+
+
+@pytest.mark.parametrize("dtype", FORMATS)
+@pytest.mark.parametrize("k,n", [(1280, 1280), (1280, 5120), (5120, 1280), (160, 333), (96, 41),
+                                 (1280, 20000), (224, 19000)])
+def test_gemv_tile_bit_identical_to_mma(rq, dtype, k, n):
+    """The tiled kernel reproduces the integer-MMA GEMV's summation order
+    (its K slices for KS > 1, the head/tail split of tiles shared by two
+    warps for KS == 1, pad blocks when K/32 is not a multiple of 4), so the
+    two give identical bits at every m and the switch between them keeps
+    a row's result independent of m."""
+    import torch
+    from rusty_whisper_b200 import synth
+    w = rq.QTensor([n, k], dtype, synth.random_blocks(dtype, n, k, 5 * dtype + n))
+    bias = torch.from_numpy(synth.normal(3, n)).cuda()
+    a = cuda(synth.normal(40 + k, 256 * k).reshape(256, k))
+    try:
+        for m in (1, 5, 16, 31, 32, 33, 63, 64, 80, 128, 200, 256):
+            outs = []
+            for kind in (2, 3, 0):
+                rq.set_gemv_kernel(kind)
+                outs.append(rq.matmul_t_q(a[:m], w, bias=bias if m % 2 else None))
+            rq.stream_check()
+            assert torch.equal(outs[0].view(torch.int32), outs[1].view(torch.int32)), (m, "mma vs tile")
+            assert torch.equal(outs[0].view(torch.int32), outs[2].view(torch.int32)), (m, "mma vs auto")
     finally:
         rq.set_gemv_kernel(0)
 
