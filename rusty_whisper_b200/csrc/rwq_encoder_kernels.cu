@@ -30,7 +30,7 @@ __device__ __forceinline__ float gelu_ref(float t) {
 // (lane & 7 = position): the reference quantizer (quant.rs:690-716), as
 // k_quantize does it -- d = amax/127, inv = 1/d or 0, q = round(x*inv)
 // half away from zero, clamped to +-127, NaN -> 0.
-constexpr int RQ_SLICE = 4;   // 128-element chunks per warp in the PLAIN / GELU modes
+constexpr int RQ_WPR = 4;     // warps per row in the LayerNorm modes
 
 struct QOut {
     uint16_t* q16;   // GEMM layout: f16 codes [m][k], d_a and d_a*sum transposed [nb][m_pad]
@@ -83,10 +83,15 @@ __device__ __forceinline__ void quant_block4(float4 x, int row, int k, int e, co
     }
 }
 
-// One warp per row of k elements (k % 128 == 0); lane l covers elements
-// 4l..4l+3 of each 128-element chunk, so 8 lanes share a quant block.
+// Rows of k elements (k % 128 == 0) in 128-element chunks; lane l covers
+// elements 4l..4l+3 of a chunk, so 8 lanes share a quant block.
 // MODE: RQ_PLAIN quantize x; RQ_GELU quantize gelu(x); RQ_LN quantize
 // LayerNorm(x); RQ_ADD_LN x += add (written back to xout), then as RQ_LN.
+// PLAIN / GELU: each warp takes `slice` consecutive chunks of a row.
+// LayerNorm: RQ_WPR warps per row (chunks c = w, w + RQ_WPR, ...; at most
+// NV each, held in registers); the row statistics add each lane's chunks
+// in order, then the lanes (xor tree), then the warps in order, so a row's
+// result depends on k only.
 // The codes go to the GEMM layout (q16/dT/uT), the GEMV layout (q8/d/sum/
 // u), or both; with yout the transformed row is also written as f32 (e.g.
 // ln_post).  GEMM-layout rows m..m_pad-1 get zero block scales.  x and xout may
@@ -94,21 +99,19 @@ __device__ __forceinline__ void quant_block4(float4 x, int row, int k, int e, co
 template <int MODE, int NV>
 __global__ void __launch_bounds__(256) k_rows_quant(const float* x, const float* __restrict__ add, float* xout,
                                                     const float* __restrict__ lw, const float* __restrict__ lb,
-                                                    int m, int k, QOut o, float* __restrict__ yout) {
+                                                    int m, int k, QOut o, float* __restrict__ yout, int slice_len) {
+    constexpr bool LN = MODE == RQ_LN || MODE == RQ_ADD_LN;
     pdl_trigger();
     pdl_wait();
     const int lane = threadIdx.x & 31;
     const int nb = k / QK, nch = k / 128;
-    // PLAIN / GELU rows are split over several warps (RQ_SLICE chunks of
-    // 128 elements each); LayerNorm rows take one warp (they need the row's
-    // statistics).
-    const int slices = (MODE == RQ_PLAIN || MODE == RQ_GELU) ? (nch + RQ_SLICE - 1) / RQ_SLICE : 1;
+    const int wpr = LN ? RQ_WPR : (nch + slice_len - 1) / slice_len;   // warps per row
     const size_t wg = (size_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
-    const int row = int(wg / slices), slice = int(wg % slices);
+    const int row = int(wg / wpr), wr = int(wg % wpr);
     const int rows = o.q16 ? o.m_pad : m;
-    if (row >= rows) return;
-    if (row >= m) {
-        if (slice) return;
+    const bool live = row < m;
+    if (!LN && !live) {
+        if (row >= rows || wr) return;
         for (int bl = lane; bl < nb; bl += 32) {
             o.dT[size_t(bl) * o.m_pad + row] = 0.f;
             o.uT[size_t(bl) * o.m_pad + row] = 0.f;
@@ -122,57 +125,83 @@ __global__ void __launch_bounds__(256) k_rows_quant(const float* x, const float*
         if (quant) quant_block4(v, row, k, e, o);
         if (yout) *reinterpret_cast<float4*>(yout + size_t(row) * k + e) = v;
     };
-    if (MODE == RQ_PLAIN || MODE == RQ_GELU) {
-        const int c1 = min(nch, (slice + 1) * RQ_SLICE);
-        for (int c = slice * RQ_SLICE; c < c1; ++c) {
+    if constexpr (!LN) {
+        const int c1 = min(nch, (wr + 1) * slice_len);
+        for (int c = wr * slice_len; c < c1; ++c) {
             float4 v = __ldg(xr + c * 32 + lane);
             if (MODE == RQ_GELU) v = make_float4(gelu_ref(v.x), gelu_ref(v.y), gelu_ref(v.z), gelu_ref(v.w));
             emit(c, v);
         }
         return;
-    }
-    // LayerNorm: the row stays in registers (nch <= NV).
-    float4 v[NV];
-    float s = 0.f;
+    } else {
+        // Every warp of the CTA reaches both barriers (rows past m too).
+        __shared__ float s_red[256 / 32];
+        const int wi = int(threadIdx.x >> 5), w0 = wi - wr;   // this row's first warp in the CTA
+        float4 v[NV];
+        float s = 0.f;
 #pragma unroll
-    for (int c = 0; c < NV; ++c) {
-        if (c < nch) {
-            v[c] = xr[c * 32 + lane];
-            if (MODE == RQ_ADD_LN) {
-                const float4 a = __ldg(reinterpret_cast<const float4*>(add + size_t(row) * k) + c * 32 + lane);
-                v[c] = make_float4(__fadd_rn(v[c].x, a.x), __fadd_rn(v[c].y, a.y), __fadd_rn(v[c].z, a.z),
-                                   __fadd_rn(v[c].w, a.w));
-                reinterpret_cast<float4*>(xout + size_t(row) * k)[c * 32 + lane] = v[c];
+        for (int j = 0; j < NV; ++j) {
+            const int c = wr + RQ_WPR * j;
+            if (live && c < nch) {
+                v[j] = xr[c * 32 + lane];
+                if (MODE == RQ_ADD_LN) {
+                    const float4 a = __ldg(reinterpret_cast<const float4*>(add + size_t(row) * k) + c * 32 + lane);
+                    v[j] = make_float4(__fadd_rn(v[j].x, a.x), __fadd_rn(v[j].y, a.y), __fadd_rn(v[j].z, a.z),
+                                       __fadd_rn(v[j].w, a.w));
+                    reinterpret_cast<float4*>(xout + size_t(row) * k)[c * 32 + lane] = v[j];
+                }
+                s += (v[j].x + v[j].y) + (v[j].z + v[j].w);
             }
-            s += (v[c].x + v[c].y) + (v[c].z + v[c].w);
         }
-    }
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-    const float mean = __fdiv_rn(s, float(k));
-    float q = 0.f;
+        for (int o2 = 16; o2 > 0; o2 >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o2);
+        if (lane == 0) s_red[wi] = s;
+        __syncthreads();
+        float tot = s_red[w0];
 #pragma unroll
-    for (int c = 0; c < NV; ++c) {
-        if (c < nch) {
-            const float a = __fsub_rn(v[c].x, mean), b = __fsub_rn(v[c].y, mean), cc = __fsub_rn(v[c].z, mean),
-                        dd = __fsub_rn(v[c].w, mean);
-            q += (__fmul_rn(a, a) + __fmul_rn(b, b)) + (__fmul_rn(cc, cc) + __fmul_rn(dd, dd));
+        for (int w = 1; w < RQ_WPR; ++w) tot = __fadd_rn(tot, s_red[w0 + w]);
+        const float mean = __fdiv_rn(tot, float(k));
+        float q = 0.f;
+#pragma unroll
+        for (int j = 0; j < NV; ++j) {
+            const int c = wr + RQ_WPR * j;
+            if (live && c < nch) {
+                const float a = __fsub_rn(v[j].x, mean), b = __fsub_rn(v[j].y, mean), cc = __fsub_rn(v[j].z, mean),
+                            dd = __fsub_rn(v[j].w, mean);
+                q += (__fmul_rn(a, a) + __fmul_rn(b, b)) + (__fmul_rn(cc, cc) + __fmul_rn(dd, dd));
+            }
         }
-    }
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) q += __shfl_xor_sync(0xffffffffu, q, o);
-    const float var = __fdiv_rn(q, float(k));
-    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, 1e-5f)));
+        for (int o2 = 16; o2 > 0; o2 >>= 1) q += __shfl_xor_sync(0xffffffffu, q, o2);
+        __syncthreads();
+        if (lane == 0) s_red[wi] = q;
+        __syncthreads();
+        float qt = s_red[w0];
 #pragma unroll
-    for (int c = 0; c < NV; ++c) {
-        if (c < nch) {
-            const int e = c * 128 + lane * 4;
-            const float4 w = __ldg(reinterpret_cast<const float4*>(lw + e));
-            const float4 b = __ldg(reinterpret_cast<const float4*>(lb + e));
-            auto f = [&](float xv, float wv, float bv) {
-                return __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(xv, mean), inv), wv), bv);
-            };
-            emit(c, make_float4(f(v[c].x, w.x, b.x), f(v[c].y, w.y, b.y), f(v[c].z, w.z, b.z), f(v[c].w, w.w, b.w)));
+        for (int w = 1; w < RQ_WPR; ++w) qt = __fadd_rn(qt, s_red[w0 + w]);
+        if (!live) {
+            if (row < rows && wr == 0)
+                for (int bl = lane; bl < nb; bl += 32) {
+                    o.dT[size_t(bl) * o.m_pad + row] = 0.f;
+                    o.uT[size_t(bl) * o.m_pad + row] = 0.f;
+                }
+            return;
+        }
+        const float var = __fdiv_rn(qt, float(k));
+        const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, 1e-5f)));
+#pragma unroll
+        for (int j = 0; j < NV; ++j) {
+            const int c = wr + RQ_WPR * j;
+            if (c < nch) {
+                const int e = c * 128 + lane * 4;
+                const float4 w = __ldg(reinterpret_cast<const float4*>(lw + e));
+                const float4 b = __ldg(reinterpret_cast<const float4*>(lb + e));
+                auto f = [&](float xv, float wv, float bv) {
+                    return __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(xv, mean), inv), wv), bv);
+                };
+                emit(c, make_float4(f(v[j].x, w.x, b.x), f(v[j].y, w.y, b.y), f(v[j].z, w.z, b.z),
+                                    f(v[j].w, w.w, b.w)));
+            }
         }
     }
 }
@@ -411,14 +440,20 @@ cudaError_t rows_quant_mode(const float* x, const float* add, float* xout, const
                             int k, const QOut& o, float* yout, cudaStream_t s) {
     const int rows = o.q16 ? o.m_pad : m;
     const int nch = k / 128;
-    const int slices = (MODE == RQ_PLAIN || MODE == RQ_GELU) ? (nch + RQ_SLICE - 1) / RQ_SLICE : 1;
-    const unsigned grid = unsigned((size_t(rows) * slices * 32 + 255) / 256);
-    if (MODE == RQ_PLAIN || MODE == RQ_GELU || nch <= 4)
-        return launch_pdl(k_rows_quant<MODE, 4>, dim3(grid), dim3(256), 0, s, x, add, xout, lw, lb, m, k, o, yout);
-    if (nch <= 8)
-        return launch_pdl(k_rows_quant<MODE, 8>, dim3(grid), dim3(256), 0, s, x, add, xout, lw, lb, m, k, o, yout);
-    if (nch <= 16)
-        return launch_pdl(k_rows_quant<MODE, 16>, dim3(grid), dim3(256), 0, s, x, add, xout, lw, lb, m, k, o, yout);
+    if (MODE == RQ_PLAIN || MODE == RQ_GELU) {
+        // One chunk per warp for decoder-sized batches (latency), four for
+        // encoder-sized ones; the result does not depend on the split.
+        const int slice = size_t(rows) * nch >= size_t(1) << 16 ? 4 : 1;
+        const int wpr = (nch + slice - 1) / slice;
+        const unsigned grid = unsigned((size_t(rows) * wpr * 32 + 255) / 256);
+        return launch_pdl(k_rows_quant<MODE, 1>, dim3(grid), dim3(256), 0, s, x, add, xout, lw, lb, m, k, o, yout,
+                          slice);
+    }
+    const unsigned grid = unsigned((size_t(rows) * RQ_WPR * 32 + 255) / 256);
+    if (nch <= RQ_WPR * 2)
+        return launch_pdl(k_rows_quant<MODE, 2>, dim3(grid), dim3(256), 0, s, x, add, xout, lw, lb, m, k, o, yout, 1);
+    if (nch <= RQ_WPR * 4)
+        return launch_pdl(k_rows_quant<MODE, 4>, dim3(grid), dim3(256), 0, s, x, add, xout, lw, lb, m, k, o, yout, 1);
     return cudaErrorInvalidValue;
 }
 

@@ -973,8 +973,8 @@ __device__ inline int gemv_slice_start(int T, int s, int ks, int ng, int gx, int
     return NONE;
 }
 
-template <int DT, int WN, int NT>
-__global__ void __launch_bounds__(GT_THREADS)
+template <int DT, int WN, int NT, bool CL>
+__global__ void __launch_bounds__(GT_THREADS, 3)
     k_gemv_tile(const uint8_t* __restrict__ qs, const uint32_t* __restrict__ qh, const uint16_t* __restrict__ dp,
                 const uint16_t* __restrict__ mp, const int8_t* __restrict__ q8, const float* __restrict__ da,
                 const int32_t* __restrict__ sa, const float* __restrict__ ua, int M, int N, int K,
@@ -985,7 +985,7 @@ __global__ void __launch_bounds__(GT_THREADS)
     const int nb = K / QK, nb4 = round4(nb), ng = nb4 / 4, tiles = (N + 15) / 16;
     // ks > 1: the launch has clusters of ks CTAs along x, CTA `rank` of a
     // cluster takes K slice `rank`; ks == 1: one CTA takes all of K.
-    const int cs = ks > 1 ? ks : 1, rank = int(blockIdx.x) % cs;
+    const int cs = CL ? ks : 1, rank = int(blockIdx.x) % cs;
     const int g_lo = rank * ng / cs, g_hi = (rank + 1) * ng / cs;
     const int n0 = int(blockIdx.x) / cs * L::BN, m0 = int(blockIdx.y) * L::BM;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, wn = warp & 1, wm = warp >> 1;
@@ -1036,34 +1036,36 @@ __global__ void __launch_bounds__(GT_THREADS)
         }
     };
 
-    // Slice bookkeeping per m-tile: `tot` holds the finished slices, `part`
-    // the running one.
-    float2 t01[WN][NT], t23[WN][NT], p01[WN][NT], p23[WN][NT];
+    // CL (clusters): the CTA's K range is one slice, its sum is a partial.
+    // Otherwise `tot` holds the finished slices of a tile and `part` (q02,
+    // q13) the running one.  Accumulator pairs: q02 = (row g, row g+8) at
+    // column 2c, q13 = the same rows at column 2c+1.
+    float2 q02[WN][NT], q13[WN][NT];
+    float2 t02[CL ? 1 : WN][CL ? 1 : NT], t13[CL ? 1 : WN][CL ? 1 : NT];
     int nsl[WN], nxt[WN];
 #pragma unroll
     for (int mt = 0; mt < WN; ++mt) {
-        const int T = (n0 >> 4) + wn * WN + mt;
         nsl[mt] = 0;
-        nxt[mt] = cs > 1 ? (1 << 30) : gemv_slice_start(T, 1, ks, ng, gx, tiles);
+        nxt[mt] = CL ? (1 << 30) : gemv_slice_start((n0 >> 4) + wn * WN + mt, 1, ks, ng, gx, tiles);
 #pragma unroll
-        for (int nt = 0; nt < NT; ++nt) {
-            p01[mt][nt] = p23[mt][nt] = t01[mt][nt] = t23[mt][nt] = make_float2(0.f, 0.f);
-        }
+        for (int nt = 0; nt < NT; ++nt) q02[mt][nt] = q13[mt][nt] = make_float2(0.f, 0.f);
     }
     auto close_slice = [&](int mt) {
+        if constexpr (!CL) {
 #pragma unroll
-        for (int nt = 0; nt < NT; ++nt) {
-            if (nsl[mt] == 0) {
-                t01[mt][nt] = p01[mt][nt];
-                t23[mt][nt] = p23[mt][nt];
-            } else {
-                t01[mt][nt] = __fadd2_rn(t01[mt][nt], p01[mt][nt]);
-                t23[mt][nt] = __fadd2_rn(t23[mt][nt], p23[mt][nt]);
+            for (int nt = 0; nt < NT; ++nt) {
+                if (nsl[mt] == 0) {
+                    t02[mt][nt] = q02[mt][nt];
+                    t13[mt][nt] = q13[mt][nt];
+                } else {
+                    t02[mt][nt] = __fadd2_rn(t02[mt][nt], q02[mt][nt]);
+                    t13[mt][nt] = __fadd2_rn(t13[mt][nt], q13[mt][nt]);
+                }
+                q02[mt][nt] = q13[mt][nt] = make_float2(0.f, 0.f);
             }
-            p01[mt][nt] = p23[mt][nt] = make_float2(0.f, 0.f);
+            ++nsl[mt];
+            nxt[mt] = gemv_slice_start((n0 >> 4) + wn * WN + mt, nsl[mt] + 1, ks, ng, gx, tiles);
         }
-        ++nsl[mt];
-        nxt[mt] = cs > 1 ? (1 << 30) : gemv_slice_start((n0 >> 4) + wn * WN + mt, nsl[mt] + 1, ks, ng, gx, tiles);
     };
 
     const int n_g = g_hi - g_lo;
@@ -1088,17 +1090,21 @@ __global__ void __launch_bounds__(GT_THREADS)
             }
             cp_async_commit();
         }
+        if constexpr (!CL) {
 #pragma unroll
-        for (int mt = 0; mt < WN; ++mt)
-            while (G == nxt[mt]) close_slice(mt);
+            for (int mt = 0; mt < WN; ++mt)
+                while (G == nxt[mt]) close_slice(mt);
+        }
 
         const uint8_t* st = smem + (i % GT_STAGES) * L::STAGE;
-        // Weight fragments of this warp's m-tiles, decoded for all 4 blocks.
+        // Weight fragments of this warp's m-tiles, decoded for all 4 blocks;
+        // d_b (m_b) of rows g and g+8 as pairs.
         uint32_t a[WN][4][4];
-        float db[WN][2][4], mb[WN][2][4];
+        float2 dbp[WN][4], mbp[WN][4];
 #pragma unroll
         for (int mt = 0; mt < WN; ++mt) {
             MmaGroup<DT> r;
+            float dbv[2][4], mbv[2][4];
 #pragma unroll
             for (int rr = 0; rr < 2; ++rr) {
                 const int row = (wn * WN + mt) * 16 + g + 8 * rr;
@@ -1114,17 +1120,19 @@ __global__ void __launch_bounds__(GT_THREADS)
                     const uint4 h = *reinterpret_cast<const uint4*>(st + L::WH + row * 16);
                     r.h[rr][0] = h.x; r.h[rr][1 % 4] = h.y; r.h[rr][2 % 4] = h.z; r.h[rr][3 % 4] = h.w;
                 }
-                const uint2 dd = *reinterpret_cast<const uint2*>(st + L::WD + row * 8);
-                const float2 d01 = h2f2(dd.x), d23 = h2f2(dd.y);
-                db[mt][rr][0] = d01.x; db[mt][rr][1] = d01.y; db[mt][rr][2] = d23.x; db[mt][rr][3] = d23.y;
+                const uint2 dw = *reinterpret_cast<const uint2*>(st + L::WD + row * 8);
+                const float2 d01 = h2f2(dw.x), d23 = h2f2(dw.y);
+                dbv[rr][0] = d01.x; dbv[rr][1] = d01.y; dbv[rr][2] = d23.x; dbv[rr][3] = d23.y;
                 if (has_min(DT)) {
-                    const uint2 mm = *reinterpret_cast<const uint2*>(st + L::WM + row * 8);
-                    const float2 m01 = h2f2(mm.x), m23 = h2f2(mm.y);
-                    mb[mt][rr][0] = m01.x; mb[mt][rr][1] = m01.y; mb[mt][rr][2] = m23.x; mb[mt][rr][3] = m23.y;
+                    const uint2 mw = *reinterpret_cast<const uint2*>(st + L::WM + row * 8);
+                    const float2 m01 = h2f2(mw.x), m23 = h2f2(mw.y);
+                    mbv[rr][0] = m01.x; mbv[rr][1] = m01.y; mbv[rr][2] = m23.x; mbv[rr][3] = m23.y;
                 }
             }
 #pragma unroll
             for (int b = 0; b < 4; ++b) {
+                dbp[mt][b] = make_float2(dbv[0][b], dbv[1][b]);
+                if (has_min(DT)) mbp[mt][b] = make_float2(mbv[0][b], mbv[1][b]);
                 if (DT == Q8_0) {
                     a[mt][b][0] = r.q[0][(2 * b) % (QSB / 4)];
                     a[mt][b][1] = r.q[1][(2 * b) % (QSB / 4)];
@@ -1147,7 +1155,9 @@ __global__ void __launch_bounds__(GT_THREADS)
             }
         }
         // Activation n-tiles: B fragments (row g of the n-tile, words c and
-        // 4+c of each block) and the scales of columns 2c, 2c+1.
+        // 4+c of each block) and the scales of columns 2c, 2c+1.  The MMAs
+        // of all blocks and m-tiles issue first; the f32 updates follow, in
+        // kb order for every output.
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
             const int col = (wm * NT + nt) * 8;
@@ -1158,6 +1168,7 @@ __global__ void __launch_bounds__(GT_THREADS)
                 s0 = *reinterpret_cast<const int4*>(st + L::AS + r0 * 16);
                 s1 = *reinterpret_cast<const int4*>(st + L::AS + (r0 + 1) * 16);
             }
+            const int sx[4] = {s0.x, s0.y, s0.z, s0.w}, sy[4] = {s1.x, s1.y, s1.z, s1.w};
             const float4 d0 = *reinterpret_cast<const float4*>(st + L::AD + r0 * 16);
             const float4 d1 = *reinterpret_cast<const float4*>(st + L::AD + (r0 + 1) * 16);
             float4 u0 = make_float4(0.f, 0.f, 0.f, 0.f), u1 = u0;
@@ -1165,37 +1176,50 @@ __global__ void __launch_bounds__(GT_THREADS)
                 u0 = *reinterpret_cast<const float4*>(st + L::AU + r0 * 16);
                 u1 = *reinterpret_cast<const float4*>(st + L::AU + (r0 + 1) * 16);
             }
-            const int sx[4] = {s0.x, s0.y, s0.z, s0.w}, sy[4] = {s1.x, s1.y, s1.z, s1.w};
             const float dx[4] = {d0.x, d0.y, d0.z, d0.w}, dy[4] = {d1.x, d1.y, d1.z, d1.w};
             const float ux[4] = {u0.x, u0.y, u0.z, u0.w}, uy[4] = {u1.x, u1.y, u1.z, u1.w};
+            // Blocks in batches of MB: MB * WN MMAs in flight before their
+            // f32 updates (fewer where the slice totals hold registers).
+            constexpr int MB = (CL || WN * NT <= 4) ? 4 : 2;
 #pragma unroll
-            for (int b = 0; b < 4; ++b) {
-                const uint2 bf = make_uint2(*reinterpret_cast<const uint32_t*>(aq + b * 32),
-                                            *reinterpret_cast<const uint32_t*>(aq + b * 32 + 16));
-                const int2 ci = code_offset(DT)
-                                    ? make_int2(int(MAGIC_BITS - uint32_t(code_offset(DT) * sx[b])),
-                                                int(MAGIC_BITS - uint32_t(code_offset(DT) * sy[b])))
-                                    : make_int2(int(MAGIC_BITS), int(MAGIC_BITS));
-                const float2 dab = make_float2(dx[b], dy[b]);
+            for (int b0 = 0; b0 < 4; b0 += MB) {
+                int dd[MB][WN][4];
 #pragma unroll
-                for (int mt = 0; mt < WN; ++mt) {
-                    int dd[4];
-                    mma_i8<DT == Q8_0>(a[mt][b], bf, ci, dd);
-                    const float2 s01 = __fadd2_rn(make_float2(__int_as_float(dd[0]), __int_as_float(dd[1])), nmag);
-                    const float2 s23 = __fadd2_rn(make_float2(__int_as_float(dd[2]), __int_as_float(dd[3])), nmag);
-                    p01[mt][nt] = __ffma2_rn(__fmul2_rn(dab, make_float2(db[mt][0][b], db[mt][0][b])), s01, p01[mt][nt]);
-                    p23[mt][nt] = __ffma2_rn(__fmul2_rn(dab, make_float2(db[mt][1][b], db[mt][1][b])), s23, p23[mt][nt]);
-                    if (has_min(DT)) {
-                        const float2 uab = make_float2(ux[b], uy[b]);
-                        p01[mt][nt] = __ffma2_rn(uab, make_float2(mb[mt][0][b], mb[mt][0][b]), p01[mt][nt]);
-                        p23[mt][nt] = __ffma2_rn(uab, make_float2(mb[mt][1][b], mb[mt][1][b]), p23[mt][nt]);
+                for (int bb = 0; bb < MB; ++bb) {
+                    const int b = b0 + bb;
+                    const uint2 bf = make_uint2(*reinterpret_cast<const uint32_t*>(aq + b * 32),
+                                                *reinterpret_cast<const uint32_t*>(aq + b * 32 + 16));
+                    const int2 ci = code_offset(DT)
+                                        ? make_int2(int(MAGIC_BITS - uint32_t(code_offset(DT) * sx[b])),
+                                                    int(MAGIC_BITS - uint32_t(code_offset(DT) * sy[b])))
+                                        : make_int2(int(MAGIC_BITS), int(MAGIC_BITS));
+#pragma unroll
+                    for (int mt = 0; mt < WN; ++mt) mma_i8<DT == Q8_0>(a[mt][b], bf, ci, dd[bb][mt]);
+                }
+#pragma unroll
+                for (int bb = 0; bb < MB; ++bb) {
+                    const int b = b0 + bb;
+                    const float2 da0 = make_float2(dx[b], dx[b]), da1 = make_float2(dy[b], dy[b]);
+#pragma unroll
+                    for (int mt = 0; mt < WN; ++mt) {
+                        // S exactly, then acc <- fma(d_a*d_b, S, acc) (+ fma(d_a*sum, m_b, acc))
+                        const float2 s02 = __fadd2_rn(
+                            make_float2(__int_as_float(dd[bb][mt][0]), __int_as_float(dd[bb][mt][2])), nmag);
+                        const float2 s13 = __fadd2_rn(
+                            make_float2(__int_as_float(dd[bb][mt][1]), __int_as_float(dd[bb][mt][3])), nmag);
+                        q02[mt][nt] = __ffma2_rn(__fmul2_rn(dbp[mt][b], da0), s02, q02[mt][nt]);
+                        q13[mt][nt] = __ffma2_rn(__fmul2_rn(dbp[mt][b], da1), s13, q13[mt][nt]);
+                        if (has_min(DT)) {
+                            q02[mt][nt] = __ffma2_rn(mbp[mt][b], make_float2(ux[b], ux[b]), q02[mt][nt]);
+                            q13[mt][nt] = __ffma2_rn(mbp[mt][b], make_float2(uy[b], uy[b]), q13[mt][nt]);
+                        }
                     }
                 }
             }
         }
     }
     asm volatile("cp.async.wait_group 0;" ::: "memory");
-    if (cs > 1) {
+    if constexpr (CL) {
         // This CTA's slice partial -> own shared memory [BM][BN]; after the
         // cluster barrier CTA `rank` adds the slices of its share of the
         // tile in slice order (k_gemv_mma's order) and stores it.
@@ -1206,10 +1230,10 @@ __global__ void __launch_bounds__(GT_THREADS)
 #pragma unroll
             for (int nt = 0; nt < NT; ++nt) {
                 const int rl = (wn * WN + mt) * 16 + g, cl = (wm * NT + nt) * 8 + 2 * c;
-                part[cl * L::BN + rl] = p01[mt][nt].x;
-                part[(cl + 1) * L::BN + rl] = p01[mt][nt].y;
-                part[cl * L::BN + rl + 8] = p23[mt][nt].x;
-                part[(cl + 1) * L::BN + rl + 8] = p23[mt][nt].y;
+                part[cl * L::BN + rl] = q02[mt][nt].x;
+                part[cl * L::BN + rl + 8] = q02[mt][nt].y;
+                part[(cl + 1) * L::BN + rl] = q13[mt][nt].x;
+                part[(cl + 1) * L::BN + rl + 8] = q13[mt][nt].y;
             }
         gt_cluster_sync();
         constexpr int Q4 = L::BN * L::BM / 4;
@@ -1231,20 +1255,21 @@ __global__ void __launch_bounds__(GT_THREADS)
             }
         }
         gt_cluster_sync();   // no CTA leaves while its partial is being read
-        return;
-    }
+    } else {
 #pragma unroll
-    for (int mt = 0; mt < WN; ++mt) {
-        close_slice(mt);
-        const int T = (n0 >> 4) + wn * WN + mt;
+        for (int mt = 0; mt < WN; ++mt) {
+            close_slice(mt);
+            const int T = (n0 >> 4) + wn * WN + mt;
 #pragma unroll
-        for (int nt = 0; nt < NT; ++nt) {
-            const float v[4] = {t01[mt][nt].x, t01[mt][nt].y, t23[mt][nt].x, t23[mt][nt].y};
+            for (int nt = 0; nt < NT; ++nt) {
+                // (row g, col 2c), (row g+8, col 2c), (row g, col 2c+1), (row g+8, col 2c+1)
+                const float v[4] = {t02[mt][nt].x, t02[mt][nt].y, t13[mt][nt].x, t13[mt][nt].y};
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const int row = T * 16 + g + ((i & 2) ? 8 : 0);
-                const int col = m0 + (wm * NT + nt) * 8 + 2 * c + (i & 1);
-                if (row < N && col < M) y[size_t(col) * N + row] = bias ? __fadd_rn(v[i], __ldg(bias + row)) : v[i];
+                for (int i = 0; i < 4; ++i) {
+                    const int row = T * 16 + g + ((i & 1) ? 8 : 0);
+                    const int col = m0 + (wm * NT + nt) * 8 + 2 * c + (i >> 1);
+                    if (row < N && col < M) y[size_t(col) * N + row] = bias ? __fadd_rn(v[i], __ldg(bias + row)) : v[i];
+                }
             }
         }
     }
@@ -1636,9 +1661,9 @@ struct GemvMmaF {
 };
 
 // Tile configuration of k_gemv_tile: RWQ_GEMV_TILE="WN,NT" (WN in {1,2},
-// NT in {2,4}) fixes it for sweeps; otherwise NT = 4 when the rows fill
-// 64-row CTA tiles with little waste, WN = 2 when the larger weight tile
-// still leaves two CTAs per SM.  Every configuration gives the same bits.
+// NT in {2,4}) fixes it for sweeps; otherwise WN = 2 and NT = 4 above 80
+// rows, 2 up to 80 (the fastest on the whisper decoder shapes, B200
+// sweep).  Every configuration gives the same bits.
 inline void gemv_tile_cfg(int m, int n, int ks, int sms, int* wn, int* nt) {
     static int env_wn = -1, env_nt = -1;
     if (env_wn < 0) {
@@ -1649,31 +1674,41 @@ inline void gemv_tile_cfg(int m, int n, int ks, int sms, int* wn, int* nt) {
         }
     }
     if (env_wn) { *wn = env_wn; *nt = env_nt; return; }
-    *nt = (m % 64 == 0 || m > 128) ? 4 : 2;
-    const long rows = (m + 16 * *nt - 1) / (16 * *nt);
-    *wn = (long((n + 63) / 64) * rows * ks >= 2L * sms) ? 2 : 1;
+    (void)n; (void)ks; (void)sms;
+    *nt = m > 80 ? 4 : 2;
+    *wn = 2;
 }
 
-template <int DT, int WN, int NT>
-cudaError_t gemv_tile_go(const ActsView& v, const Weight& w, const float* bias, float* y, int ks, int gx,
-                         int vec16, cudaStream_t s) {
+template <int DT, int WN, int NT, bool CL>
+cudaError_t gemv_tile_launch(const ActsView& v, const Weight& w, const float* bias, float* y, int ks, int gx,
+                             int vec16, cudaStream_t s) {
     using L = TileSmem<DT, WN, NT>;
-    auto kern = k_gemv_tile<DT, WN, NT>;
+    auto kern = k_gemv_tile<DT, WN, NT, CL>;
     int dev = 0, sms = 148;
     dev_sms(&dev, &sms);
     static unsigned attr_dev_mask = 0;
     if (!(attr_dev_mask & (1u << dev))) {
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::BYTES);
         if (e != cudaSuccess) return e;
+        // Three CTAs per SM need more shared memory than the default split.
+        e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+        if (e != cudaSuccess) return e;
         attr_dev_mask |= 1u << dev;
     }
-    const int cs = ks > 1 ? ks : 1;
+    const int cs = CL ? ks : 1;
     const dim3 grid(unsigned((w.n + L::BN - 1) / L::BN * cs), unsigned((v.m + L::BM - 1) / L::BM));
-    if (cs == 1)
+    if (!CL)
         return launch_pdl(kern, grid, dim3(GT_THREADS), size_t(L::BYTES), s, w.qs, w.qh, w.d, w.m, v.q8, v.d,
                           v.sum, v.u, v.m, w.n, w.k, bias, y, ks, gx, vec16);
     return launch_pdl_cluster(kern, grid, dim3(GT_THREADS), size_t(L::BYTES), cs, s, w.qs, w.qh, w.d, w.m, v.q8,
                               v.d, v.sum, v.u, v.m, w.n, w.k, bias, y, ks, gx, vec16);
+}
+
+template <int DT, int WN, int NT>
+cudaError_t gemv_tile_go(const ActsView& v, const Weight& w, const float* bias, float* y, int ks, int gx,
+                         int vec16, cudaStream_t s) {
+    return ks > 1 ? gemv_tile_launch<DT, WN, NT, true>(v, w, bias, y, ks, gx, vec16, s)
+                  : gemv_tile_launch<DT, WN, NT, false>(v, w, bias, y, ks, gx, vec16, s);
 }
 
 template <int DT>
