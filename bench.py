@@ -586,21 +586,42 @@ def run_large_v3(args, dev, stream, rank, world):
 def run_profile_driver(args):
     """Small fixed workloads for ncu captures (no timing line of record):
     `logits` -- config 4's tied-logits GEMV (Q5_0 51865 x 1024, four weight
-    copies) at --m rows, --steps back-to-back launches; `decode` -- the
-    config-4 decoder (80 streams), begin then --steps greedy steps."""
+    copies) at --m rows, --steps back-to-back launches; `gemv` -- the same
+    for config 5's decoder projection (Q4_0 1280 x 1280, eight copies);
+    `decode` -- the config-4 decoder (80 streams; config 5's with --m 256),
+    begin then --steps greedy steps."""
     import torch
     from rusty_whisper_b200 import quant
     quant.init(0)
     dev = torch.device("cuda", 0)
-    if args.only == "logits":
-        n, k, dt = 51865, 1024, 6
+    if args.only in ("logits", "gemv"):
+        n, k, dt, copies = (51865, 1024, 6, 4) if args.only == "logits" else (1280, 1280, 2, 8)
         raw = synth.random_blocks(dt, n, k, 5)
-        W = [quant.QTensor([n, k], dt, raw) for _ in range(4)]
+        W = [quant.QTensor([n, k], dt, raw) for _ in range(copies)]
         x = torch.from_numpy(synth.normal(9, args.m * k).reshape(args.m, k)).to(dev)
         qa = quant.QActs(args.m, k).quantize(x)
         y = torch.empty((args.m, n), device=dev)
         for r in range(args.steps):
-            qa.matmul(W[r % 4], out=y)
+            qa.matmul(W[r % copies], out=y)
+        # The same launches replayed from a CUDA graph, timed with events
+        # (no host gaps between them).
+        st = torch.cuda.Stream()
+        with torch.cuda.stream(st):
+            qa.matmul(W[0], out=y)
+        torch.cuda.synchronize()
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr, stream=st):
+            for r in range(args.steps):
+                qa.matmul(W[r % copies], out=y)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(st):
+            gr.replay()
+            e0.record(st)
+            gr.replay()
+            e1.record(st)
+        torch.cuda.synchronize()
+        us_per_launch = e0.elapsed_time(e1) * 1e3 / max(args.steps, 1)
+        del gr
     else:
         from rusty_whisper_b200 import decoder
         if args.m == 256:   # config 5's decoder: large-v3 shape, Q4_0, 256 windows, one stream each
@@ -619,7 +640,10 @@ def run_profile_driver(args):
             tok = dec.step(tok, want="best")
     torch.cuda.synchronize()
     quant.stream_check()
-    print(json.dumps({"profile_driver": args.only, "m": args.m, "steps": args.steps}), flush=True)
+    line = {"profile_driver": args.only, "m": args.m, "steps": args.steps}
+    if args.only in ("logits", "gemv"):
+        line.update(us_per_launch=round(us_per_launch, 2), tops=round(2 * args.m * n * k / us_per_launch / 1e6, 1))
+    print(json.dumps(line), flush=True)
 
 
 def run_gemv(args, dev, quant, w_np, hbm_peak, stream):
@@ -820,7 +844,7 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--m", type=int, default=1,
                     help="--only logits: activation rows; --only decode: 256 selects config 5's decoder")
-    ap.add_argument("--only", default="all", choices=["all", "gemm", "encoder", "decoder", "large", "logits", "decode"],
+    ap.add_argument("--only", default="all", choices=["all", "gemm", "encoder", "decoder", "large", "logits", "gemv", "decode"],
                     help="gemm: only the config-2 GEMM sweep; encoder / decoder / large: only that leg; "
                          "logits: --steps launches of config 4's tied-logits GEMV at --m rows; decode: --steps "
                          "config-4 decode steps, graphs off when RWQ_DECODER_GRAPHS=0 (short runs for profiling)")
@@ -840,7 +864,7 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local_rank))
     try:
-        if args.only in ("logits", "decode"):
+        if args.only in ("logits", "gemv", "decode"):
             run_profile_driver(args)
             return
         if args.only in ("encoder", "decoder", "large"):
