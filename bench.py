@@ -450,8 +450,8 @@ def run_decoder_beams(args, dev, hbm_peak, stream, rank, world):
            "streams": S,
            "bytes_per_step": {"quantized_weights": round(sum(v[1].nbytes for v in t.values() if isinstance(v, tuple)) / 1e6, 1),
                               "cross_kv_f16_MB": round(cross_bytes / 1e6, 1)},
-           "note": "linears on the integer-MMA GEMV (up to 64 streams per CTA row, weights through L2); each stream "
-                   "takes its own greedy id; the step replays from a CUDA graph",
+           "note": "linears on the tiled integer-MMA GEMV (k_gemv_tile: 80 streams as 32-row tiles, bit-identical "
+                   "to the per-stream GEMV); each stream takes its own greedy id; the step replays from a CUDA graph",
            "data": "synthetic (seeded): random-code Q5_0 weights (block 0 values reused by every block, each block its "
                    "own device copy), encoder output N(0, 1)"}
     if rank == 0 and world == 1 and not args.no_cpu:

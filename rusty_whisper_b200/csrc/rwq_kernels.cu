@@ -930,16 +930,23 @@ struct TileSmem {
 __device__ __forceinline__ void gt_cluster_sync() {
     asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
+// Exit guard only (no memory ordering needed: the peers' reads of this
+// CTA's shared memory have returned their values before they arrive).
+__device__ __forceinline__ void gt_cluster_sync_relaxed() {
+    asm volatile("barrier.cluster.arrive.relaxed.aligned;\n\tbarrier.cluster.wait.aligned;" ::: "memory");
+}
 // Shared::cluster address of shared byte offset `off` in cluster CTA `rank`.
 __device__ __forceinline__ uint32_t gt_mapa(uint32_t off, uint32_t rank) {
     uint32_t r;
     asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(off), "r"(rank));
     return r;
 }
+// (No memory clobber: the loads of one output's slices are issued back to
+// back; the cluster barriers order them against the partials' writes.)
 __device__ __forceinline__ float4 gt_ld_cluster4(uint32_t addr) {
     float4 v;
     asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
-                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(addr) : "memory");
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(addr));
     return v;
 }
 
@@ -1240,12 +1247,17 @@ __global__ void __launch_bounds__(GT_THREADS, 3)
         const int q_lo = rank * Q4 / cs, q_hi = (rank + 1) * Q4 / cs;
         for (int q = q_lo + tid; q < q_hi; q += GT_THREADS) {
             const uint32_t off = sbase + uint32_t(q * 16);
-            float4 v = gt_ld_cluster4(gt_mapa(off, 0));
-            for (int s2 = 1; s2 < cs; ++s2) {
-                const float4 t = gt_ld_cluster4(gt_mapa(off, uint32_t(s2)));
-                v.x = __fadd_rn(v.x, t.x); v.y = __fadd_rn(v.y, t.y);
-                v.z = __fadd_rn(v.z, t.z); v.w = __fadd_rn(v.w, t.w);
-            }
+            float4 t[8];
+#pragma unroll
+            for (int s2 = 0; s2 < 8; ++s2)
+                if (s2 < cs) t[s2] = gt_ld_cluster4(gt_mapa(off, uint32_t(s2)));
+            float4 v = t[0];
+#pragma unroll
+            for (int s2 = 1; s2 < 8; ++s2)
+                if (s2 < cs) {
+                    v.x = __fadd_rn(v.x, t[s2].x); v.y = __fadd_rn(v.y, t[s2].y);
+                    v.z = __fadd_rn(v.z, t[s2].z); v.w = __fadd_rn(v.w, t[s2].w);
+                }
             const int col = m0 + 4 * q / L::BN, row = n0 + 4 * q % L::BN;
             const float vv[4] = {v.x, v.y, v.z, v.w};
             if (col < M) {
@@ -1254,7 +1266,7 @@ __global__ void __launch_bounds__(GT_THREADS, 3)
                     if (row + j < N) y[size_t(col) * N + row + j] = bias ? __fadd_rn(vv[j], __ldg(bias + row + j)) : vv[j];
             }
         }
-        gt_cluster_sync();   // no CTA leaves while its partial is being read
+        gt_cluster_sync_relaxed();   // no CTA leaves while its partial is being read
     } else {
 #pragma unroll
         for (int mt = 0; mt < WN; ++mt) {
@@ -1660,23 +1672,34 @@ struct GemvMmaF {
     }
 };
 
-// Tile configuration of k_gemv_tile: RWQ_GEMV_TILE="WN,NT" (WN in {1,2},
-// NT in {2,4}) fixes it for sweeps; otherwise WN = 2 and NT = 4 above 80
-// rows, 2 up to 80 (the fastest on the whisper decoder shapes, B200
-// sweep).  Every configuration gives the same bits.
-inline void gemv_tile_cfg(int m, int n, int ks, int sms, int* wn, int* nt) {
-    static int env_wn = -1, env_nt = -1;
+// Tile configuration of k_gemv_tile (every configuration gives the same
+// bits; chosen from a B200 sweep over the whisper decoder shapes):
+//   * K-split weights (ks > 1) with short K (<= 16 groups) and enough
+//     32 x 32 tiles for 1.5 CTAs per SM: one CTA walks all K slices of a
+//     32 x 32 tile (WN = 1, NT = 2, no cluster) -- the pipeline then hides
+//     the loads, and the tiles fill the GPU on their own;
+//   * other K-split weights: clusters of ks CTAs, one per slice, on 64 x
+//     32 tiles (up to 80 rows) or 64 x 64 tiles;
+//   * unsplit (wide) weights: 64 x 32 or 64 x 64 tiles, no cluster.
+// RWQ_GEMV_TILE="WN,NT" and RWQ_GEMV_TILE_CL=0|1 override (sweeps).
+inline void gemv_tile_cfg(int m, int n, int nb, int ks, int sms, int* wn, int* nt, bool* cl) {
+    static int env_wn = -1, env_nt = -1, env_cl = -1;
     if (env_wn < 0) {
         env_wn = env_nt = 0;
         if (const char* e = getenv("RWQ_GEMV_TILE")) {
             int a = 0, b = 0;
             if (sscanf(e, "%d,%d", &a, &b) == 2 && (a == 1 || a == 2) && (b == 2 || b == 4)) env_wn = a, env_nt = b;
         }
+        const char* c = getenv("RWQ_GEMV_TILE_CL");
+        env_cl = (c && (c[0] == '0' || c[0] == '1')) ? c[0] - '0' : 2;
     }
-    if (env_wn) { *wn = env_wn; *nt = env_nt; return; }
-    (void)n; (void)ks; (void)sms;
-    *nt = m > 80 ? 4 : 2;
-    *wn = 2;
+    const long small_tiles = long((n + 31) / 32) * long((m + 31) / 32);
+    const bool walk = ks > 1 && round4(nb) / 4 <= 16 && small_tiles * 2 >= long(sms) * 3;
+    *cl = ks > 1 && !walk;
+    *wn = walk ? 1 : 2;
+    *nt = walk ? 2 : (m > 80 ? 4 : 2);
+    if (env_wn) { *wn = env_wn; *nt = env_nt; }
+    if (env_cl != 2) *cl = ks > 1 && env_cl == 1;
 }
 
 template <int DT, int WN, int NT, bool CL>
@@ -1704,11 +1727,13 @@ cudaError_t gemv_tile_launch(const ActsView& v, const Weight& w, const float* bi
                               v.d, v.sum, v.u, v.m, w.n, w.k, bias, y, ks, gx, vec16);
 }
 
+// cl: K slices as clusters (one CTA per slice); otherwise one CTA walks
+// all slices, keeping their order with the slice totals.
 template <int DT, int WN, int NT>
 cudaError_t gemv_tile_go(const ActsView& v, const Weight& w, const float* bias, float* y, int ks, int gx,
-                         int vec16, cudaStream_t s) {
-    return ks > 1 ? gemv_tile_launch<DT, WN, NT, true>(v, w, bias, y, ks, gx, vec16, s)
-                  : gemv_tile_launch<DT, WN, NT, false>(v, w, bias, y, ks, gx, vec16, s);
+                         int vec16, bool cl, cudaStream_t s) {
+    return cl ? gemv_tile_launch<DT, WN, NT, true>(v, w, bias, y, ks, gx, vec16, s)
+              : gemv_tile_launch<DT, WN, NT, false>(v, w, bias, y, ks, gx, vec16, s);
 }
 
 template <int DT>
@@ -1728,11 +1753,12 @@ struct GemvTileF {
                            (reinterpret_cast<uintptr_t>(v.sum) & 15) == 0 &&
                            (reinterpret_cast<uintptr_t>(v.u) & 15) == 0) ? 1 : 0;
         int wn = 1, nt = 2;
-        gemv_tile_cfg(v.m, w.n, ks, sms, &wn, &nt);
-        if (wn == 1) return nt == 2 ? gemv_tile_go<DT, 1, 2>(v, w, bias, y, ks, gx, vec16, s)
-                                    : gemv_tile_go<DT, 1, 4>(v, w, bias, y, ks, gx, vec16, s);
-        return nt == 2 ? gemv_tile_go<DT, 2, 2>(v, w, bias, y, ks, gx, vec16, s)
-                       : gemv_tile_go<DT, 2, 4>(v, w, bias, y, ks, gx, vec16, s);
+        bool cl = false;
+        gemv_tile_cfg(v.m, w.n, w.nb, ks, sms, &wn, &nt, &cl);
+        if (wn == 1) return nt == 2 ? gemv_tile_go<DT, 1, 2>(v, w, bias, y, ks, gx, vec16, cl, s)
+                                    : gemv_tile_go<DT, 1, 4>(v, w, bias, y, ks, gx, vec16, cl, s);
+        return nt == 2 ? gemv_tile_go<DT, 2, 2>(v, w, bias, y, ks, gx, vec16, cl, s)
+                       : gemv_tile_go<DT, 2, 4>(v, w, bias, y, ks, gx, vec16, cl, s);
     }
 };
 
