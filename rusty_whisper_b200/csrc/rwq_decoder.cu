@@ -94,6 +94,9 @@ struct rwq_decoder {
     __half *cross_k = nullptr, *cross_v = nullptr, *self_k = nullptr, *self_v = nullptr;
     int *cross_kv = nullptr, *cross_off = nullptr, *cross_streams = nullptr;
     int *self_kv = nullptr, *self_off = nullptr;   // identity tables for self-attention
+    int cross_splits = 1;          // key splits of the cross-attention (multi-stream groups)
+    float* attn_part = nullptr;    // per-split partial results of the cross-attention
+    unsigned* attn_cnt = nullptr;  // per (group, head) split counters, zero between launches
     float *x = nullptr, *tmp = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *att = nullptr, *h = nullptr,
           *logits = nullptr;
     int32_t* best = nullptr;
@@ -160,7 +163,7 @@ int check_ready(rwq_decoder* d) {
 }
 
 // Lay out (base == nullptr: size) the decode state for S streams, W windows.
-size_t layout_state(rwq_decoder* d, int S, int W, int n_audio, int n_groups, uint8_t* base) {
+size_t layout_state(rwq_decoder* d, int S, int W, int n_audio, int n_groups, int splits, uint8_t* base) {
     const size_t D = size_t(d->n_state), F = size_t(d->n_ff), H = size_t(d->n_head), L = size_t(d->n_layer);
     const size_t kmax = std::max(D, F), m_pad = align_up(size_t(S), 256);
     size_t off = 0;
@@ -178,6 +181,9 @@ size_t layout_state(rwq_decoder* d, int S, int W, int n_audio, int n_groups, uin
     d->cross_streams = reinterpret_cast<int*>(take(size_t(S) * 4));
     d->self_kv = reinterpret_cast<int*>(take(size_t(S) * 4));
     d->self_off = reinterpret_cast<int*>(take(size_t(S + 1) * 4));
+    d->attn_part = splits > 1 ? reinterpret_cast<float*>(take(size_t(n_groups) * splits * H * rwq::DEC_MAX_G * 66 * 4))
+                              : nullptr;
+    d->attn_cnt = splits > 1 ? reinterpret_cast<unsigned*>(take(size_t(n_groups) * H * 4)) : nullptr;
     d->x = reinterpret_cast<float*>(take(S * D * 4));
     d->tmp = reinterpret_cast<float*>(take(S * D * 4));
     d->q = reinterpret_cast<float*>(take(S * D * 4));
@@ -264,7 +270,7 @@ int issue_step(rwq_decoder* d, int mode, int32_t limit, cudaStream_t s) {
         __half* vc = d->self_v + size_t(l) * self_layer;
         DEC_CUDA(rwq::launch_kv_append(d->k, d->v, S, H, d->n_ctx, d->dpos, kc, vc, s), "kv append");
         DEC_CUDA(rwq::launch_attn_dec(d->q, kc, vc, size_t(d->n_ctx) * 64, d->n_ctx, d->dpos, H, S, 1, d->self_kv,
-                                      d->self_off, d->self_kv, d->att, s),
+                                      d->self_off, d->self_kv, d->att, 1, nullptr, nullptr, s),
                  "self attention");
         DEC_RC(rows(d, rwq::RQ_PLAIN, d->att, nullptr, nullptr, nullptr, nullptr, D, s));
         DEC_RC(linear(d, L.o, L.o_b, d->tmp, s));
@@ -273,7 +279,8 @@ int issue_step(rwq_decoder* d, int mode, int32_t limit, cudaStream_t s) {
         DEC_RC(linear(d, L.xq, L.xq_b, d->q, s));
         DEC_CUDA(rwq::launch_attn_dec(d->q, d->cross_k + size_t(l) * cross_layer, d->cross_v + size_t(l) * cross_layer,
                                       size_t(d->n_audio) * 64, d->n_audio, nullptr, H, d->n_cross_groups, d->max_group,
-                                      d->cross_kv, d->cross_off, d->cross_streams, d->att, s),
+                                      d->cross_kv, d->cross_off, d->cross_streams, d->att, d->cross_splits,
+                                      d->attn_part, d->attn_cnt, s),
                  "cross attention");
         DEC_RC(rows(d, rwq::RQ_PLAIN, d->att, nullptr, nullptr, nullptr, nullptr, D, s));
         DEC_RC(linear(d, L.xo, L.xo_b, d->tmp, s));
@@ -458,24 +465,35 @@ int rwq_decoder_begin(rwq_decoder* d, const float* enc_out, int64_t n_windows, i
         if (win[size_t(i)] < 0 || win[size_t(i)] >= W)
             return dfail(RWQ_ERR_ARG, "stream %d maps to window %d of %d", i, win[size_t(i)], W);
     }
-    // Cross-attention groups: one stream each, ordered by window, so the
-    // CTAs of one window's streams are adjacent in the grid and its K/V
-    // comes from L2 after the first read (a group holding several streams
-    // would read it once but carry every query's state per lane, which
-    // costs more occupancy than the L2 re-reads).
+    // Cross-attention groups: the streams of one window (beams) share a
+    // group of up to DEC_MAX_G, which reads the window's K/V once on the
+    // tensor-core kernel, with the keys split over several CTAs per (head,
+    // group) to fill the GPU.  One stream per window: one group each,
+    // ordered by window, on the CUDA-core kernel.
     std::vector<int> gkv, goff(1, 0), gst;
     for (int w = 0; w < W; ++w) {
+        int in_group = 0;
         for (int i = 0; i < S; ++i) {
             if (win[size_t(i)] != w) continue;
+            if (in_group == rwq::DEC_MAX_G) {
+                goff.push_back(int(gst.size()));
+                in_group = 0;
+            }
+            if (in_group == 0) gkv.push_back(w);
             gst.push_back(i);
-            gkv.push_back(w);
-            goff.push_back(int(gst.size()));
+            ++in_group;
         }
+        if (in_group) goff.push_back(int(gst.size()));
     }
     const int NG = int(gkv.size());
+    int max_group = 1;
+    for (int i = 0; i < NG; ++i) max_group = std::max(max_group, goff[size_t(i) + 1] - goff[size_t(i)]);
+    int sms = 148;
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, d->device);
+    const int splits = rwq::attn_dec_splits(H, NG, max_group, T, sms);
     DEC_CUDA(cudaStreamSynchronize(d->gs), "cudaStreamSynchronize(decoder)");
     drop_graphs(d);
-    const size_t need = layout_state(d, S, W, T, NG, nullptr);
+    const size_t need = layout_state(d, S, W, T, NG, splits, nullptr);
     if (d->state_bytes < need) {
         DEC_CUDA(cudaStreamSynchronize(s), "cudaStreamSynchronize");
         cudaFree(d->state);
@@ -484,13 +502,14 @@ int rwq_decoder_begin(rwq_decoder* d, const float* enc_out, int64_t n_windows, i
         DEC_CUDA(cudaMalloc(&d->state, need), "cudaMalloc(decoder state)");
         d->state_bytes = need;
     }
-    layout_state(d, S, W, T, NG, static_cast<uint8_t*>(d->state));
+    layout_state(d, S, W, T, NG, splits, static_cast<uint8_t*>(d->state));
     d->n_streams = S;
     d->n_windows = W;
     d->n_audio = T;
     d->n_cross_groups = NG;
-    d->max_group = 1;
-    for (int i = 0; i < NG; ++i) d->max_group = std::max(d->max_group, goff[size_t(i) + 1] - goff[size_t(i)]);
+    d->max_group = max_group;
+    d->cross_splits = splits;
+    if (d->attn_cnt) DEC_CUDA(cudaMemsetAsync(d->attn_cnt, 0, size_t(NG) * H * 4, s), "zero split counters");
     d->n_past = 0;
     std::vector<int> sid(static_cast<size_t>(S)), soff(static_cast<size_t>(S) + 1);
     for (int i = 0; i <= S; ++i) {

@@ -21,9 +21,17 @@ cudaError_t launch_pos_advance(int* dpos, cudaStream_t s);
 // f16 [L][64]; its streams are grp_streams[grp_off[g] .. grp_off[g+1])
 // (<= max_group <= DEC_MAX_G).  Device arrays.  With dpos the keys are 0..*dpos
 // (self-attention over the cache; L is then the capacity).
+// Groups of several streams run on the tensor cores (no dpos); splits > 1
+// (those groups only) divides the keys over that many CTAs per (head,
+// group): part then holds n_groups * splits * H * DEC_MAX_G * 66 floats
+// and cnt n_groups * H zeroed counters (left zeroed).
 cudaError_t launch_attn_dec(const float* q, const __half* kc, const __half* vc, size_t kv_stride, int L,
                             const int* dpos, int H, int n_groups, int max_group, const int* grp_kv, const int* grp_off,
-                            const int* grp_streams, float* out, cudaStream_t s);
+                            const int* grp_streams, float* out, int splits, float* part, unsigned* cnt,
+                            cudaStream_t s);
+// Key splits for a grid of H x n_groups CTAs: 1 for single-stream groups,
+// else enough for one CTA per SM, at most 8 splits of at least 128 keys.
+int attn_dec_splits(int H, int n_groups, int max_group, int L, int sms);
 cudaError_t launch_argmax(const float* logits, int rows, int V, int limit, int32_t* best, cudaStream_t s);
 // x[i] = dequant(w row tokens[i]) + pos[*dpos] (bit-exact dequant,
 // quant.rs:528-537); pos is [ctx][k].

@@ -9,6 +9,7 @@
 //   * k_argmax: greedy choice over the logits (decoder.rs:339-367).
 #include <cuda_fp16.h>
 #include <cstdint>
+#include <cstdlib>
 #include "rwq_common.cuh"
 #include "rwq_decoder.h"
 
@@ -170,6 +171,245 @@ __global__ void __launch_bounds__(DEC_THREADS) k_attn_dec(const float* __restric
     }
 }
 
+// ------------------------------------------------- decode attention, MMA
+// Groups of several streams (the beams of one window) on the f16 tensor
+// cores (mma.sync m16n8k16, f32 accumulate).  The 16 rows of the A operand
+// hold each query twice: rows 0..7 its f16 high part, rows 8..15 the low
+// part (q - hi), so S[g] + S[g+8] is the score with q to 22 bits, as with
+// the f32 queries of k_attn_dec; P is split the same way for O = P V, and
+// O[g] + O[g+8] is the output row.  K and V stay f16 as cached.
+// CTA (head, group, split): 4 warps, each streaming its own 32-key K/V
+// tiles (warp w: tiles w, w+4, ...) through a two-stage cp.async buffer
+// (128-byte rows, 16-byte chunks swizzled by chunk ^ (row & 7) so ldmatrix
+// is conflict-free), with an online softmax per query in the log2 domain;
+// the warps are combined through shared memory at the end.
+// Split keys (gridDim.z = splits > 1, when the (head, group) grid alone
+// would leave the GPU idle): CTA z takes keys [z*L/splits, (z+1)*L/splits)
+// and leaves its per-query running max, sum and 64-dim numerator in
+// `part`; the CTA that finishes a (head, group) last (counter `cnt`, reset
+// after use) adds the splits in split order, so the result does not depend
+// on which CTA finishes when.
+constexpr int TC_WARPS = 4, TC_KEYS = 32;
+constexpr int TC_TILE = TC_KEYS * 128;                  // bytes of one K (or V) tile
+constexpr int TC_SMEM = TC_WARPS * 2 * 2 * TC_TILE;     // warps x stages x {K, V}
+
+__device__ __forceinline__ uint32_t tc_swz(int row, int chunk) {
+    return uint32_t(row * 128 + ((chunk ^ (row & 7)) << 4));
+}
+__device__ __forceinline__ void tc_cp16(uint32_t dst, const void* src, bool ok) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(ok ? 16 : 0) : "memory");
+}
+__device__ __forceinline__ void tc_ldm4(uint32_t addr, uint32_t (&r)[4]) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(addr));
+}
+__device__ __forceinline__ void tc_ldm4t(uint32_t addr, uint32_t (&r)[4]) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(addr));
+}
+__device__ __forceinline__ void tc_mma(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+                 "{%0,%1,%2,%3};"
+                 : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+                 : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+// f16 pair of (x0, x1) and the pair of the remainders.
+__device__ __forceinline__ void tc_split2(float x0, float x1, uint32_t& hi, uint32_t& lo) {
+    const __half2 h = __floats2half2_rn(x0, x1);
+    const float2 hf = __half22float2(h);
+    const __half2 l = __floats2half2_rn(x0 - hf.x, x1 - hf.y);
+    hi = *reinterpret_cast<const uint32_t*>(&h);
+    lo = *reinterpret_cast<const uint32_t*>(&l);
+}
+
+__global__ void __launch_bounds__(TC_WARPS * 32) k_attn_dec_tc(const float* __restrict__ q, const __half* __restrict__ kc,
+                                                              const __half* __restrict__ vc, size_t kv_stride, int L,
+                                                              int H, const int* __restrict__ grp_kv,
+                                                              const int* __restrict__ grp_off,
+                                                              const int* __restrict__ grp_streams,
+                                                              float* __restrict__ out, float* __restrict__ part,
+                                                              unsigned* __restrict__ cnt) {
+    pdl_trigger();
+    extern __shared__ __align__(128) uint8_t tc_smem[];
+    __shared__ float s_acc[TC_WARPS][DEC_MAX_G][HD];
+    __shared__ float s_ml[TC_WARPS][DEC_MAX_G][2];
+    __shared__ int s_last;
+    const int h = blockIdx.x, gr = blockIdx.y, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int g = lane >> 2, c = lane & 3;
+    const int D = H * HD, splits = int(gridDim.z), sp = int(blockIdx.z);
+    pdl_wait();
+    const int s0 = grp_off[gr], G = grp_off[gr + 1] - s0;
+    if (G <= 0) return;
+    const int k_lo = int(int64_t(sp) * L / splits), k_hi = int(int64_t(sp + 1) * L / splits);
+    const __half* K = kc + (size_t(grp_kv[gr]) * H + h) * kv_stride;
+    const __half* V = vc + (size_t(grp_kv[gr]) * H + h) * kv_stride;
+    const uint32_t sb = uint32_t(__cvta_generic_to_shared(tc_smem)) + uint32_t(warp * 4 * TC_TILE);
+    // stage st: K tile at sb + st*2*TC_TILE, the V tile after it
+    auto load = [&](int t, int st) {
+        const int r0 = k_lo + t * TC_KEYS;
+        const uint32_t dk = sb + uint32_t(st * 2 * TC_TILE), dv = dk + TC_TILE;
+#pragma unroll
+        for (int i = 0; i < TC_KEYS * 8 / 32; ++i) {
+            const int idx = lane + 32 * i, row = idx >> 3, ch = idx & 7;
+            const bool ok = r0 + row < k_hi;
+            const size_t o = size_t(ok ? r0 + row : 0) * HD + ch * 8;
+            tc_cp16(dk + tc_swz(row, ch), K + o, ok);
+            tc_cp16(dv + tc_swz(row, ch), V + o, ok);
+        }
+    };
+    // A fragments of the queries (scaled by log2(e)/8): row g = hi, g+8 = lo.
+    const float L2E = 1.4426950408889634f;
+    uint32_t qa[4][4];
+    {
+        const bool live = g < G;
+        const float* qp = q + size_t(live ? grp_streams[s0 + g] : 0) * D + h * HD;
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+                const float2 v = live ? __ldg(reinterpret_cast<const float2*>(qp + kk * 16 + u * 8 + 2 * c))
+                                      : make_float2(0.f, 0.f);
+                tc_split2(__fmul_rn(v.x, 0.125f) * L2E, __fmul_rn(v.y, 0.125f) * L2E, qa[kk][2 * u], qa[kk][2 * u + 1]);
+            }
+    }
+    const int ntiles = (k_hi - k_lo + TC_KEYS - 1) / TC_KEYS;
+    float o[8][4];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+    float m = -INFINITY, l = 0.f;   // query g (the four lanes of one g agree on m)
+    if (warp < ntiles) load(warp, 0);
+    asm volatile("cp.async.commit_group;" ::: "memory");
+    for (int t = warp, it = 0; t < ntiles; t += TC_WARPS, ++it) {
+        const int st = it & 1;
+        if (t + TC_WARPS < ntiles) load(t + TC_WARPS, st ^ 1);
+        asm volatile("cp.async.commit_group;" ::: "memory");
+        asm volatile("cp.async.wait_group 1;" ::: "memory");
+        __syncwarp();
+        const uint32_t sk = sb + uint32_t(st * 2 * TC_TILE), sv = sk + TC_TILE;
+        // S = Q K^T over 32 keys: s[nt] keys nt*8 + 2c, +1; [0,1] hi row, [2,3] lo row
+        float s[4][4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) s[i][0] = s[i][1] = s[i][2] = s[i][3] = 0.f;
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)
+#pragma unroll
+            for (int np = 0; np < 2; ++np) {
+                uint32_t b[4];
+                const int mi = lane >> 3, key = np * 16 + (lane & 7) + (mi >> 1) * 8, ch = kk * 2 + (mi & 1);
+                tc_ldm4(sk + tc_swz(key, ch), b);
+                tc_mma(s[2 * np], qa[kk], b[0], b[1]);
+                tc_mma(s[2 * np + 1], qa[kk], b[2], b[3]);
+            }
+        const int kb = k_lo + t * TC_KEYS;
+        float sc[4][2], mx = m;
+#pragma unroll
+        for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+                const int key = kb + nt * 8 + 2 * c + e;
+                sc[nt][e] = key < k_hi ? s[nt][e] + s[nt][2 + e] : -INFINITY;
+                mx = fmaxf(mx, sc[nt][e]);
+            }
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+        const float alpha = exp2f(m - mx);   // 0 on the first tile (m = -inf)
+        m = mx;
+        l *= alpha;
+#pragma unroll
+        for (int nt = 0; nt < 8; ++nt)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) o[nt][e] *= alpha;
+        // O += P V with P split hi (row g) / lo (row g+8)
+#pragma unroll
+        for (int kk = 0; kk < 2; ++kk) {
+            float p[2][2];
+#pragma unroll
+            for (int hh = 0; hh < 2; ++hh)
+#pragma unroll
+                for (int e = 0; e < 2; ++e) {
+                    p[hh][e] = exp2f(sc[2 * kk + hh][e] - mx);
+                    l += p[hh][e];
+                }
+            uint32_t a[4];
+            tc_split2(p[0][0], p[0][1], a[0], a[1]);
+            tc_split2(p[1][0], p[1][1], a[2], a[3]);
+#pragma unroll
+            for (int np = 0; np < 4; ++np) {
+                uint32_t b[4];
+                const int mi = lane >> 3, key = kk * 16 + (lane & 7) + (mi & 1) * 8, ch = np * 2 + (mi >> 1);
+                tc_ldm4t(sv + tc_swz(key, ch), b);
+                tc_mma(o[2 * np], a, b[0], b[1]);
+                tc_mma(o[2 * np + 1], a, b[2], b[3]);
+            }
+        }
+        __syncwarp();
+    }
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
+    l += __shfl_xor_sync(0xffffffffu, l, 1);
+    l += __shfl_xor_sync(0xffffffffu, l, 2);
+    if (g < G) {
+#pragma unroll
+        for (int nt = 0; nt < 8; ++nt) {
+            s_acc[warp][g][nt * 8 + 2 * c] = o[nt][0] + o[nt][2];
+            s_acc[warp][g][nt * 8 + 2 * c + 1] = o[nt][1] + o[nt][3];
+        }
+        if (c == 0) {
+            s_ml[warp][g][0] = m;
+            s_ml[warp][g][1] = l;
+        }
+    }
+    __syncthreads();
+    constexpr int REC = HD + 2;   // part record: {max, sum, numerator[64]}
+    auto rec = [&](int z, int gi) {
+        return part + ((size_t(gr) * splits + z) * H + h) * size_t(DEC_MAX_G * REC) + size_t(gi) * REC;
+    };
+    for (int i = tid; i < G * HD; i += TC_WARPS * 32) {
+        const int gi = i / HD, e = i % HD;
+        float M = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < TC_WARPS; ++w) M = fmaxf(M, s_ml[w][gi][0]);
+        float num = 0.f, den = 0.f;
+#pragma unroll
+        for (int w = 0; w < TC_WARPS; ++w) {
+            const float f = s_ml[w][gi][0] == -INFINITY ? 0.f : exp2f(s_ml[w][gi][0] - M);
+            num = fmaf(s_acc[w][gi][e], f, num);
+            den = fmaf(s_ml[w][gi][1], f, den);
+        }
+        if (splits == 1) {
+            out[size_t(grp_streams[s0 + gi]) * D + h * HD + e] = num / den;
+        } else {
+            float* r = rec(sp, gi);
+            r[2 + e] = num;
+            if (e == 0) {
+                r[0] = M;
+                r[1] = den;
+            }
+        }
+    }
+    if (splits == 1) return;
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) s_last = atomicAdd(cnt + size_t(gr) * H + h, 1u) == unsigned(splits - 1);
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    for (int i = tid; i < G * HD; i += TC_WARPS * 32) {
+        const int gi = i / HD, e = i % HD;
+        float M = -INFINITY;
+        for (int z = 0; z < splits; ++z) M = fmaxf(M, __ldcg(rec(z, gi)));
+        float num = 0.f, den = 0.f;
+        for (int z = 0; z < splits; ++z) {
+            const float* r = rec(z, gi);
+            const float mz = __ldcg(r);
+            const float f = mz == -INFINITY ? 0.f : exp2f(mz - M);
+            num = fmaf(__ldcg(r + 2 + e), f, num);
+            den = fmaf(__ldcg(r + 1), f, den);
+        }
+        out[size_t(grp_streams[s0 + gi]) * D + h * HD + e] = num / den;
+    }
+    if (tid == 0) cnt[size_t(gr) * H + h] = 0u;   // ready for the next launch
+}
+
 // Greedy choice (decoder.rs:345-365): the first maximum over ids
 // [0, limit), taken only if it is strictly above logits[limit]; else limit.
 // limit < 0: the first maximum over the whole row.
@@ -239,21 +479,46 @@ cudaError_t launch_pos_advance(int* dpos, cudaStream_t s) {
 
 cudaError_t launch_attn_dec(const float* q, const __half* kc, const __half* vc, size_t kv_stride, int L,
                             const int* dpos, int H, int n_groups, int max_group, const int* grp_kv, const int* grp_off,
-                            const int* grp_streams, float* out, cudaStream_t s) {
+                            const int* grp_streams, float* out, int splits, float* part, unsigned* cnt,
+                            cudaStream_t s) {
     if (!n_groups || !L) return cudaSuccess;
-    const dim3 grid = dim3(unsigned(H), unsigned(n_groups));
-    // registers scale with the queries a group may hold
-    if (max_group <= 1)
-        return launch_pdl(k_attn_dec<1>, grid, dim3(DEC_THREADS), 0, s, q, kc, vc, kv_stride, L, dpos, H, grp_kv,
-                          grp_off, grp_streams, out);
-    if (max_group <= 2)
-        return launch_pdl(k_attn_dec<2>, grid, dim3(DEC_THREADS), 0, s, q, kc, vc, kv_stride, L, dpos, H, grp_kv,
-                          grp_off, grp_streams, out);
-    if (max_group <= 4)
-        return launch_pdl(k_attn_dec<4>, grid, dim3(DEC_THREADS), 0, s, q, kc, vc, kv_stride, L, dpos, H, grp_kv,
-                          grp_off, grp_streams, out);
-    return launch_pdl(k_attn_dec<DEC_MAX_G>, grid, dim3(DEC_THREADS), 0, s, q, kc, vc, kv_stride, L, dpos, H, grp_kv,
-                      grp_off, grp_streams, out);
+    if (max_group > DEC_MAX_G || splits < 1 || splits > 8 || (splits > 1 && (!part || !cnt || max_group <= 1)))
+        return cudaErrorInvalidValue;
+    const dim3 grid = dim3(unsigned(H), unsigned(n_groups), unsigned(splits));
+    // Several streams per group (cross-attention of beams): the
+    // tensor-core kernel; one stream per group: the CUDA-core kernel.
+    if (max_group > 1) {
+        if (dpos) return cudaErrorInvalidValue;
+        static unsigned attr_mask = 0;
+        int dev = 0;
+        cudaGetDevice(&dev);
+        if (!(attr_mask & (1u << (dev & 31)))) {
+            const cudaError_t e =
+                cudaFuncSetAttribute(k_attn_dec_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, TC_SMEM);
+            if (e != cudaSuccess) return e;
+            attr_mask |= 1u << (dev & 31);
+        }
+        return launch_pdl(k_attn_dec_tc, grid, dim3(TC_WARPS * 32), size_t(TC_SMEM), s, q, kc, vc, kv_stride, L, H,
+                          grp_kv, grp_off, grp_streams, out, part, cnt);
+    }
+    return launch_pdl(k_attn_dec<1>, grid, dim3(DEC_THREADS), 0, s, q, kc, vc, kv_stride, L, dpos, H, grp_kv, grp_off,
+                      grp_streams, out);
+}
+
+int attn_dec_splits(int H, int n_groups, int max_group, int L, int sms) {
+    if (max_group <= 1) return 1;
+    if (const char* e = getenv("RWQ_ATTN_SPLITS")) {   // fixed split count (sweeps)
+        const int z = atoi(e);
+        if (z >= 1 && z <= 8) return z;
+    }
+    // Split only when the (head, group) grid alone leaves SMs without a
+    // CTA (measured on config 4, 256 CTAs: no split 2.84 ms per step, 2-6
+    // splits 3.06-3.15 ms).
+    const long ctas = long(H) * n_groups;
+    int z = int((long(sms) + ctas - 1) / ctas);
+    z = z < 1 ? 1 : (z > 8 ? 8 : z);
+    while (z > 1 && L / z < 128) --z;
+    return z;
 }
 
 cudaError_t launch_argmax(const float* logits, int rows, int V, int limit, int32_t* best, cudaStream_t s) {

@@ -63,6 +63,35 @@ def test_decoder_matches_oracle(torch_mod, dtype, n_win, stream_window):
     assert gpu.n_past == 6
 
 
+def test_decoder_beam_groups_split_keys(torch_mod):
+    """Streams sharing a window attend to its K/V as one group on the
+    tensor-core kernel, a window with more than 8 streams as several
+    groups, and enough encoder frames split the keys over several CTAs per
+    (head, group).  Against the oracle, and bit-identical on a rerun (the
+    splits are added in a fixed order whichever CTA finishes last)."""
+    import oracle
+    from rusty_whisper_b200 import decoder, synth
+    T = 640
+    sw = [0] * 5 + [1] * 9
+    t = synth.decoder_tensors(V, CTX, D, L, 6, 11)
+    enc = synth.normal(61, 2 * T * D).reshape(2, T, D)
+    toks = synth.randint(19, len(sw) * 3, 0, V - 1).reshape(3, len(sw))
+    outs = []
+    for _ in range(2):
+        gpu = decoder.Decoder(V, CTX, D, H, L, t)
+        gpu.begin(torch_mod.from_numpy(enc).cuda(), sw)
+        outs.append([gpu.step(torch_mod.from_numpy(toks[p].astype(np.int32)).cuda()).cpu() for p in range(3)])
+    for a, b in zip(*outs):
+        assert torch_mod.equal(a, b)
+    for i in (0, 4, 5, 12, 13):
+        r = oracle.Decoder(V, CTX, D, H, L, t)
+        r.begin(enc[sw[i]])
+        for p in range(3):
+            ref = r.forward([int(toks[p, i])])[0]
+            err = _rel_rms(outs[0][p].numpy()[i], ref)
+            assert err <= 2e-2, (i, p, err)
+
+
 def test_decoder_greedy_choice_and_prompt_positions(torch_mod):
     from rusty_whisper_b200 import synth
     gpu, refs, enc = _setup(7, 2, [0, 1])
