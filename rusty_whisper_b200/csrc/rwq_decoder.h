@@ -21,7 +21,8 @@ cudaError_t launch_pos_advance(int* dpos, cudaStream_t s);
 // f16 [L][64]; its streams are grp_streams[grp_off[g] .. grp_off[g+1])
 // (<= max_group <= DEC_MAX_G).  Device arrays.  With dpos the keys are 0..*dpos
 // (self-attention over the cache; L is then the capacity).
-// Groups of several streams run on the tensor cores (no dpos); splits > 1
+// Runs on the tensor cores (k_attn_dec_tc; RWQ_ATTN_TC=0 keeps
+// single-stream groups on the CUDA-core k_attn_dec); splits > 1
 // (those groups only) divides the keys over that many CTAs per (head,
 // group): part then holds n_groups * splits * H * DEC_MAX_G * 66 floats
 // and cnt n_groups * H zeroed counters (left zeroed).
