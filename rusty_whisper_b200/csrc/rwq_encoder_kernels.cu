@@ -449,11 +449,14 @@ cudaError_t rows_quant_mode(const float* x, const float* add, float* xout, const
         return launch_pdl(k_rows_quant<MODE, 1>, dim3(grid), dim3(256), 0, s, x, add, xout, lw, lb, m, k, o, yout,
                           slice);
     }
-    const unsigned grid = unsigned((size_t(rows) * RQ_WPR * 32 + 255) / 256);
+    // One row per CTA for decoder-sized batches (twice the CTAs to spread
+    // over the SMs), two for encoder-sized ones; the result is the same.
+    const int tpb = rows < 2048 ? RQ_WPR * 32 : 2 * RQ_WPR * 32;
+    const unsigned grid = unsigned((size_t(rows) * RQ_WPR * 32 + tpb - 1) / tpb);
     if (nch <= RQ_WPR * 2)
-        return launch_pdl(k_rows_quant<MODE, 2>, dim3(grid), dim3(256), 0, s, x, add, xout, lw, lb, m, k, o, yout, 1);
+        return launch_pdl(k_rows_quant<MODE, 2>, dim3(grid), dim3(tpb), 0, s, x, add, xout, lw, lb, m, k, o, yout, 1);
     if (nch <= RQ_WPR * 4)
-        return launch_pdl(k_rows_quant<MODE, 4>, dim3(grid), dim3(256), 0, s, x, add, xout, lw, lb, m, k, o, yout, 1);
+        return launch_pdl(k_rows_quant<MODE, 4>, dim3(grid), dim3(tpb), 0, s, x, add, xout, lw, lb, m, k, o, yout, 1);
     return cudaErrorInvalidValue;
 }
 
