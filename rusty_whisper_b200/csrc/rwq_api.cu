@@ -14,6 +14,7 @@
 #include <cstdio>
 #include <cstring>
 #include <functional>
+#include <algorithm>
 #include <map>
 #include <mutex>
 #include <string>
@@ -268,6 +269,35 @@ cudaStream_t thread_stream() {
     return s;
 }
 
+
+// Copy streams of the chunked host-buffer matmul, per (host thread, device).
+struct CopyPipe {
+    cudaStream_t up = nullptr, down = nullptr;
+    cudaEvent_t ev_up[6] = {}, ev_mm[6] = {}, ev_in = nullptr, ev_out = nullptr;
+};
+
+int copy_pipe(CopyPipe** out) {
+    thread_local std::map<int, CopyPipe> pipes;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    auto it = pipes.find(dev);
+    if (it != pipes.end()) {
+        *out = &it->second;
+        return RWQ_OK;
+    }
+    CopyPipe p;
+    RWQ_CUDA(cudaStreamCreateWithFlags(&p.up, cudaStreamNonBlocking), "cudaStreamCreate");
+    RWQ_CUDA(cudaStreamCreateWithFlags(&p.down, cudaStreamNonBlocking), "cudaStreamCreate");
+    for (int i = 0; i < 6; ++i) {
+        RWQ_CUDA(cudaEventCreateWithFlags(&p.ev_up[i], cudaEventDisableTiming), "cudaEventCreate");
+        RWQ_CUDA(cudaEventCreateWithFlags(&p.ev_mm[i], cudaEventDisableTiming), "cudaEventCreate");
+    }
+    RWQ_CUDA(cudaEventCreateWithFlags(&p.ev_in, cudaEventDisableTiming), "cudaEventCreate");
+    RWQ_CUDA(cudaEventCreateWithFlags(&p.ev_out, cudaEventDisableTiming), "cudaEventCreate");
+    *out = &(pipes[dev] = p);
+    return RWQ_OK;
+}
+
 }  // namespace
 
 int rwq::gemm_quantized(const ActsView& v, rwq_qtensor* w, const float* bias, float* out, cudaStream_t s) {
@@ -440,10 +470,50 @@ int rwq_matmul_t_q(const float* a, int64_t m, int64_t k, const rwq_qtensor* b, c
     float* da = static_cast<float*>(ws->buf);
     float* dout = reinterpret_cast<float*>(static_cast<uint8_t*>(ws->buf) + a_b);
     float* dbias = bias ? reinterpret_cast<float*>(static_cast<uint8_t*>(ws->buf) + a_b + o_b) : nullptr;
-    RWQ_CUDA(cudaMemcpyAsync(da, a, size_t(m) * k * 4, cudaMemcpyHostToDevice, s), "copy A to device");
     if (bias) RWQ_CUDA(cudaMemcpyAsync(dbias, bias, size_t(n) * 4, cudaMemcpyHostToDevice, s), "copy bias");
-    if ((rc = matmul_dev_impl(da, m, k, const_cast<rwq_qtensor*>(b), dbias, dout, mode, s, nullptr, 0))) return rc;
-    RWQ_CUDA(cudaMemcpyAsync(out, dout, size_t(m) * n * 4, cudaMemcpyDeviceToHost, s), "copy C to host");
+    // GEMM-family calls (m > 256 and no forced path) run in row chunks of
+    // more than 256 rows, so every chunk stays in the family and the results
+    // are those of one call: the upload of chunk c+1, the matmul of chunk c
+    // and the download of chunk c-1 overlap (PCIe is full duplex).  With
+    // pageable host buffers the copies still work, without the overlap.
+    const int chunks = (mode == RWQ_MODE_INT8 && t_gemm_path == 0) ? int(std::min<int64_t>(6, m / 257)) : 1;
+    if (chunks < 2) {
+        RWQ_CUDA(cudaMemcpyAsync(da, a, size_t(m) * k * 4, cudaMemcpyHostToDevice, s), "copy A to device");
+        if ((rc = matmul_dev_impl(da, m, k, const_cast<rwq_qtensor*>(b), dbias, dout, mode, s, nullptr, 0)))
+            return rc;
+        RWQ_CUDA(cudaMemcpyAsync(out, dout, size_t(m) * n * 4, cudaMemcpyDeviceToHost, s), "copy C to host");
+    } else {
+        CopyPipe* cp = nullptr;
+        if ((rc = copy_pipe(&cp))) return rc;
+        RWQ_CUDA(cudaEventRecord(cp->ev_in, s), "event");
+        RWQ_CUDA(cudaStreamWaitEvent(cp->up, cp->ev_in, 0), "event wait");
+        RWQ_CUDA(cudaStreamWaitEvent(cp->down, cp->ev_in, 0), "event wait");
+        for (int c = 0; c < chunks && !rc; ++c) {
+            const int64_t r0 = c * m / chunks, rows = (c + 1) * m / chunks - r0;   // > 256 each
+            RWQ_CUDA(cudaMemcpyAsync(da + r0 * k, a + r0 * k, size_t(rows) * k * 4, cudaMemcpyHostToDevice, cp->up),
+                     "copy A to device");
+            RWQ_CUDA(cudaEventRecord(cp->ev_up[c], cp->up), "event");
+            RWQ_CUDA(cudaStreamWaitEvent(s, cp->ev_up[c], 0), "event wait");
+            rc = matmul_dev_impl(da + r0 * k, rows, k, const_cast<rwq_qtensor*>(b), dbias, dout + r0 * n, mode, s,
+                                 nullptr, 0);
+            if (rc) break;
+            RWQ_CUDA(cudaEventRecord(cp->ev_mm[c], s), "event");
+            RWQ_CUDA(cudaStreamWaitEvent(cp->down, cp->ev_mm[c], 0), "event wait");
+            RWQ_CUDA(cudaMemcpyAsync(out + r0 * n, dout + r0 * n, size_t(rows) * n * 4, cudaMemcpyDeviceToHost,
+                                     cp->down),
+                     "copy C to host");
+        }
+        // The caller's buffers and this workspace are free again only when
+        // both copy streams are done.
+        cudaEventRecord(cp->ev_out, cp->down);
+        cudaStreamWaitEvent(s, cp->ev_out, 0);
+        cudaEventRecord(cp->ev_in, cp->up);
+        cudaStreamWaitEvent(s, cp->ev_in, 0);
+        if (rc) {
+            cudaStreamSynchronize(s);
+            return rc;
+        }
+    }
     Workspace* mws = nullptr;
     if ((rc = get_workspace(s, &mws))) return rc;
     return read_device_error(mws, s);

@@ -232,6 +232,28 @@ def test_bias_and_host_path(rq, orc):
         assert close(y, ref[:mm]) < TOL
 
 
+@pytest.mark.parametrize("m", [514, 1030, 1500])
+def test_host_path_chunks_match_device_path(rq, orc, m):
+    """Host-buffer calls of the GEMM family run in overlapped row chunks of
+    more than 256 rows (1030 rows: four chunks of 257-258); the result is
+    bit-identical to one device call, and pinned host buffers give the
+    same as pageable ones."""
+    import torch
+    from rusty_whisper_b200 import synth
+    dtype, k, n = 6, 768, 640
+    a, raw = _case(dtype, m, k, n, 9 + m)
+    b = synth.normal(8, n)
+    w = rq.QTensor([n, k], dtype, raw)
+    y_dev = host(rq.linear_w(cuda(a), w, cuda(b)))
+    y_host = rq.linear_w(a, w, b)
+    assert np.array_equal(y_dev.view(np.uint32), np.asarray(y_host).view(np.uint32))
+    a_pin = torch.from_numpy(a).pin_memory()
+    y_pin = rq.linear_w(a_pin.numpy(), w, b)
+    assert np.array_equal(y_dev.view(np.uint32), np.asarray(y_pin).view(np.uint32))
+    if m == 514:
+        assert close(y_host, orc.matmul_t_q(a, dtype, raw, n) + b[None, :]) < TOL
+
+
 def test_errors_and_edges(rq):
     import torch
     from rusty_whisper_b200 import synth
