@@ -325,6 +325,56 @@ int rwq::with_stream_scratch(cudaStream_t s, size_t bytes, const std::function<i
     return fn(ws->buf);
 }
 
+namespace rwq {
+// A weight whose rows are those of `parts` one after another (same dtype
+// and k, same device): each plane is row-major, so the planes are copied
+// end to end.  Used by the decoder to run the Q, K and V projections of a
+// layer as one GEMV.
+int qtensor_concat_rows(rwq_qtensor* const* parts, int np, cudaStream_t s, rwq_qtensor** out) {
+    *out = nullptr;
+    if (np <= 0) return fail(RWQ_ERR_ARG, "no parts");
+    const Weight& w0 = parts[0]->w;
+    int64_t n = 0;
+    for (int i = 0; i < np; ++i) {
+        const Weight& wi = parts[i]->w;
+        if (wi.dtype != w0.dtype || wi.k != w0.k || wi.device != w0.device)
+            return fail(RWQ_ERR_ARG, "parts differ in dtype, k or device");
+        n += wi.n;
+    }
+    if (n > INT32_MAX) return fail(RWQ_ERR_ARG, "weight too large");
+    auto* t = new rwq_qtensor;
+    Weight& w = t->w;
+    w.dtype = w0.dtype;
+    w.n = int(n);
+    w.k = w0.k;
+    w.nb = w0.nb;
+    w.device = w0.device;
+    const size_t nb4 = size_t(round4(w.nb)), rows = size_t(n) * nb4;
+    cudaError_t e;
+    auto cleanup = [&](int rc) {
+        rwq_qtensor_free(t);
+        return rc;
+    };
+    if ((e = cudaMalloc(&w.qs, rows * qs_bytes(w.dtype))) != cudaSuccess) return cleanup(cuda_fail(e, "cudaMalloc(qs)"));
+    if ((e = cudaMalloc(&w.d, rows * 2)) != cudaSuccess) return cleanup(cuda_fail(e, "cudaMalloc(d)"));
+    if (has_min(w.dtype) && (e = cudaMalloc(&w.m, rows * 2)) != cudaSuccess) return cleanup(cuda_fail(e, "cudaMalloc(m)"));
+    if (has_qh(w.dtype) && (e = cudaMalloc(&w.qh, rows * 4)) != cudaSuccess) return cleanup(cuda_fail(e, "cudaMalloc(qh)"));
+    size_t r0 = 0;
+    for (int i = 0; i < np; ++i) {
+        const Weight& wi = parts[i]->w;
+        const size_t ri = size_t(wi.n) * nb4;
+        e = cudaMemcpyAsync(w.qs + r0 * qs_bytes(w.dtype), wi.qs, ri * qs_bytes(w.dtype), cudaMemcpyDeviceToDevice, s);
+        if (e == cudaSuccess) e = cudaMemcpyAsync(w.d + r0, wi.d, ri * 2, cudaMemcpyDeviceToDevice, s);
+        if (e == cudaSuccess && w.m) e = cudaMemcpyAsync(w.m + r0, wi.m, ri * 2, cudaMemcpyDeviceToDevice, s);
+        if (e == cudaSuccess && w.qh) e = cudaMemcpyAsync(w.qh + r0, wi.qh, ri * 4, cudaMemcpyDeviceToDevice, s);
+        if (e != cudaSuccess) return cleanup(cuda_fail(e, "copy weight planes"));
+        r0 += ri;
+    }
+    *out = t;
+    return RWQ_OK;
+}
+}  // namespace rwq
+
 extern "C" {
 
 int rwq_block_bytes(int dtype) {

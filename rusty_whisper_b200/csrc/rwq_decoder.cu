@@ -67,6 +67,10 @@ struct DLayer {
     rwq_qtensor *q = nullptr, *k = nullptr, *v = nullptr, *o = nullptr;
     rwq_qtensor *xq = nullptr, *xk = nullptr, *xv = nullptr, *xo = nullptr;
     rwq_qtensor *fc1 = nullptr, *fc2 = nullptr;
+    // Q, K, V as one weight [3D][D] (built at begin) and its bias
+    // [q_b, 0, v_b]: one GEMV per layer instead of three.
+    rwq_qtensor* qkv = nullptr;
+    float* qkv_b = nullptr;
     // device pointers of the dense tensors, resolved once per begin
     const float *attn_ln_w = nullptr, *attn_ln_b = nullptr, *q_b = nullptr, *v_b = nullptr, *o_b = nullptr;
     const float *x_ln_w = nullptr, *x_ln_b = nullptr, *xq_b = nullptr, *xo_b = nullptr;
@@ -98,7 +102,7 @@ struct rwq_decoder {
     float* attn_part = nullptr;    // per-split partial results of the cross-attention
     unsigned* attn_cnt = nullptr;  // per (group, head) split counters, zero between launches
     float *x = nullptr, *tmp = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *att = nullptr, *h = nullptr,
-          *logits = nullptr;
+          *logits = nullptr, *qkv = nullptr;
     int32_t* best = nullptr;
     int* dpos = nullptr;           // the decode position, on the device
     int32_t* tok_in = nullptr;     // this step's tokens (graph input)
@@ -190,6 +194,7 @@ size_t layout_state(rwq_decoder* d, int S, int W, int n_audio, int n_groups, int
     d->k = reinterpret_cast<float*>(take(S * D * 4));
     d->v = reinterpret_cast<float*>(take(S * D * 4));
     d->att = reinterpret_cast<float*>(take(S * D * 4));
+    d->qkv = reinterpret_cast<float*>(take(S * 3 * D * 4));
     d->h = reinterpret_cast<float*>(take(S * F * 4));
     d->logits = reinterpret_cast<float*>(take(S * size_t(d->n_vocab) * 4));
     d->best = reinterpret_cast<int32_t*>(take(size_t(S) * 4));
@@ -263,14 +268,24 @@ int issue_step(rwq_decoder* d, int mode, int32_t limit, cudaStream_t s) {
         const DLayer& L = d->layers[size_t(l)];
         // causal self-attention over the cache (decoder.rs:140-171)
         DEC_RC(rows(d, l ? rwq::RQ_ADD_LN : rwq::RQ_LN, d->x, d->tmp, d->x, L.attn_ln_w, L.attn_ln_b, D, s));
-        DEC_RC(linear(d, L.q, L.q_b, d->q, s));
-        DEC_RC(linear(d, L.k, nullptr, d->k, s));
-        DEC_RC(linear(d, L.v, L.v_b, d->v, s));
+        const float *qp = d->q, *kp = d->k, *vp = d->v;
+        int ld = D;
+        if (L.qkv) {   // rows [q | k | v]
+            DEC_RC(linear(d, L.qkv, L.qkv_b, d->qkv, s));
+            qp = d->qkv;
+            kp = d->qkv + D;
+            vp = d->qkv + 2 * D;
+            ld = 3 * D;
+        } else {
+            DEC_RC(linear(d, L.q, L.q_b, d->q, s));
+            DEC_RC(linear(d, L.k, nullptr, d->k, s));
+            DEC_RC(linear(d, L.v, L.v_b, d->v, s));
+        }
         __half* kc = d->self_k + size_t(l) * self_layer;
         __half* vc = d->self_v + size_t(l) * self_layer;
-        DEC_CUDA(rwq::launch_kv_append(d->k, d->v, S, H, d->n_ctx, d->dpos, kc, vc, s), "kv append");
-        DEC_CUDA(rwq::launch_attn_dec(d->q, kc, vc, size_t(d->n_ctx) * 64, d->n_ctx, d->dpos, H, S, 1, d->self_kv,
-                                      d->self_off, d->self_kv, d->att, 1, nullptr, nullptr, s),
+        DEC_CUDA(rwq::launch_kv_append(kp, vp, ld, S, H, d->n_ctx, d->dpos, kc, vc, s), "kv append");
+        DEC_CUDA(rwq::launch_attn_dec(qp, kc, vc, size_t(d->n_ctx) * 64, d->n_ctx, d->dpos, H, S, 1, d->self_kv,
+                                      d->self_off, d->self_kv, d->att, 1, nullptr, nullptr, ld, s),
                  "self attention");
         DEC_RC(rows(d, rwq::RQ_PLAIN, d->att, nullptr, nullptr, nullptr, nullptr, D, s));
         DEC_RC(linear(d, L.o, L.o_b, d->tmp, s));
@@ -280,7 +295,7 @@ int issue_step(rwq_decoder* d, int mode, int32_t limit, cudaStream_t s) {
         DEC_CUDA(rwq::launch_attn_dec(d->q, d->cross_k + size_t(l) * cross_layer, d->cross_v + size_t(l) * cross_layer,
                                       size_t(d->n_audio) * 64, d->n_audio, nullptr, H, d->n_cross_groups, d->max_group,
                                       d->cross_kv, d->cross_off, d->cross_streams, d->att, d->cross_splits,
-                                      d->attn_part, d->attn_cnt, s),
+                                      d->attn_part, d->attn_cnt, D, s),
                  "cross attention");
         DEC_RC(rows(d, rwq::RQ_PLAIN, d->att, nullptr, nullptr, nullptr, nullptr, D, s));
         DEC_RC(linear(d, L.xo, L.xo_b, d->tmp, s));
@@ -382,8 +397,10 @@ int rwq_decoder_free(rwq_decoder* d) {
     cudaGetDevice(&prev);
     if (prev != d->device) cudaSetDevice(d->device);
     for (auto& kv : d->dense) cudaFree(kv.second);
-    for (auto& L : d->layers)
-        for (rwq_qtensor* t : {L.q, L.k, L.v, L.o, L.xq, L.xk, L.xv, L.xo, L.fc1, L.fc2}) rwq_qtensor_free(t);
+    for (auto& L : d->layers) {
+        for (rwq_qtensor* t : {L.q, L.k, L.v, L.o, L.xq, L.xk, L.xv, L.xo, L.fc1, L.fc2, L.qkv}) rwq_qtensor_free(t);
+        cudaFree(L.qkv_b);
+    }
     rwq_qtensor_free(d->emb);
     if (d->gs) cudaStreamSynchronize(d->gs);
     drop_graphs(d);
@@ -423,6 +440,11 @@ int rwq_decoder_set_quant(rwq_decoder* d, const char* name, int dtype, const uin
     DEC_RC(rwq_qtensor_new(raw, raw_len, dtype, n, k, &t));
     rwq_qtensor_free(*slot);
     *slot = t;
+    for (auto& L : d->layers)   // rebuilt from the new matrices at the next begin
+        if (slot == &L.q || slot == &L.k || slot == &L.v) {
+            rwq_qtensor_free(L.qkv);
+            L.qkv = nullptr;
+        }
     return RWQ_OK;
 }
 
@@ -457,6 +479,25 @@ int rwq_decoder_begin(rwq_decoder* d, const float* enc_out, int64_t n_windows, i
     }
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     const int S = int(n_streams), W = int(n_windows), T = int(n_audio), D = d->n_state, H = d->n_head;
+    // Q, K and V of each layer as one weight (same bits as three GEMVs:
+    // the GEMV family's summation order depends on N only through its K
+    // split, the same at D and 3D rows for whisper's sizes; the GEMM
+    // family's does not depend on N), bias [q_b, 0, v_b].
+    for (int l = 0; l < d->n_layer; ++l) {
+        DLayer& L = d->layers[size_t(l)];
+        if (!L.q || !L.k || !L.v) continue;
+        if (!L.qkv) {
+            rwq_qtensor* parts[3] = {L.q, L.k, L.v};
+            if (rwq::qtensor_concat_rows(parts, 3, s, &L.qkv) != RWQ_OK) L.qkv = nullptr;   // three GEMVs then
+        }
+        if (L.qkv && !L.qkv_b) DEC_CUDA(cudaMalloc(&L.qkv_b, size_t(3) * D * 4), "cudaMalloc(qkv bias)");
+        if (L.qkv) {
+            DEC_CUDA(cudaMemsetAsync(L.qkv_b, 0, size_t(3) * D * 4, s), "qkv bias");
+            if (L.q_b) DEC_CUDA(cudaMemcpyAsync(L.qkv_b, L.q_b, size_t(D) * 4, cudaMemcpyDeviceToDevice, s), "qkv bias");
+            if (L.v_b)
+                DEC_CUDA(cudaMemcpyAsync(L.qkv_b + 2 * D, L.v_b, size_t(D) * 4, cudaMemcpyDeviceToDevice, s), "qkv bias");
+        }
+    }
     // stream -> window map and the cross-attention groups (<= DEC_MAX_G
     // streams of one window each)
     std::vector<int> win(static_cast<size_t>(S));

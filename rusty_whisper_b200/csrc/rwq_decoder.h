@@ -13,7 +13,8 @@ constexpr int DEC_MAX_G = 8;   // streams sharing one key group in k_attn_dec
 
 // The decode position lives on the device (*dpos), so a step replays from
 // a CUDA graph.
-cudaError_t launch_kv_append(const float* k_new, const float* v_new, int S, int H, int ctx, const int* dpos,
+// k_new / v_new rows are ld floats apart.
+cudaError_t launch_kv_append(const float* k_new, const float* v_new, int ld, int S, int H, int ctx, const int* dpos,
                              __half* kc, __half* vc, cudaStream_t s);
 cudaError_t launch_pos_advance(int* dpos, cudaStream_t s);
 // Attention of one query per stream (q [S][H*64] f32) over n_groups
@@ -28,7 +29,7 @@ cudaError_t launch_pos_advance(int* dpos, cudaStream_t s);
 // and cnt n_groups * H zeroed counters (left zeroed).
 cudaError_t launch_attn_dec(const float* q, const __half* kc, const __half* vc, size_t kv_stride, int L,
                             const int* dpos, int H, int n_groups, int max_group, const int* grp_kv, const int* grp_off,
-                            const int* grp_streams, float* out, int splits, float* part, unsigned* cnt,
+                            const int* grp_streams, float* out, int splits, float* part, unsigned* cnt, int ldq,
                             cudaStream_t s);
 // Key splits for a grid of H x n_groups CTAs: 1 for single-stream groups,
 // else enough for one CTA per SM, at most 8 splits of at least 128 keys.

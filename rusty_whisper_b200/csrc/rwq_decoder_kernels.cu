@@ -19,9 +19,10 @@ namespace {
 
 constexpr int HD = 64;   // head dim (every Whisper size)
 
-// k_new, v_new [S][D] f32 -> cache [S][H][ctx][64] f16 at position *dpos.
-__global__ void k_kv_append(const float* __restrict__ k_new, const float* __restrict__ v_new, int S, int H, int ctx,
-                            const int* __restrict__ dpos, __half* __restrict__ kc, __half* __restrict__ vc) {
+// k_new, v_new [S][D] f32 (row stride ld) -> cache [S][H][ctx][64] f16 at
+// position *dpos.
+__global__ void k_kv_append(const float* __restrict__ k_new, const float* __restrict__ v_new, int ld, int S, int H,
+                            int ctx, const int* __restrict__ dpos, __half* __restrict__ kc, __half* __restrict__ vc) {
     pdl_trigger();
     pdl_wait();
     const int pos = *dpos;
@@ -30,8 +31,8 @@ __global__ void k_kv_append(const float* __restrict__ k_new, const float* __rest
     if (i >= size_t(S) * D) return;
     const int s = int(i / D), c = int(i % D), h = c / HD, e = c % HD;
     const size_t o = ((size_t(s) * H + h) * ctx + pos) * HD + e;
-    kc[o] = __float2half_rn(k_new[i]);
-    vc[o] = __float2half_rn(v_new[i]);
+    kc[o] = __float2half_rn(k_new[size_t(s) * ld + c]);
+    vc[o] = __float2half_rn(v_new[size_t(s) * ld + c]);
 }
 
 // One CTA per (head, group).  Group g reads the keys/values at
@@ -61,7 +62,8 @@ __global__ void __launch_bounds__(DEC_THREADS) k_attn_dec(const float* __restric
                                                          const __half* __restrict__ vc, size_t kv_stride, int L,
                                                          const int* __restrict__ dpos, int H,
                                                          const int* __restrict__ grp_kv, const int* __restrict__ grp_off,
-                                                         const int* __restrict__ grp_streams, float* __restrict__ out) {
+                                                         const int* __restrict__ grp_streams, float* __restrict__ out,
+                                                         int ldq) {
     pdl_trigger();
     __shared__ float s_acc[DEC_WARPS][GM][HD];
     __shared__ float s_ml[DEC_WARPS][GM][2];
@@ -78,7 +80,7 @@ __global__ void __launch_bounds__(DEC_THREADS) k_attn_dec(const float* __restric
 #pragma unroll
     for (int gi = 0; gi < GM; ++gi) {
         if (gi < G) {
-            const float4* qp = reinterpret_cast<const float4*>(q + size_t(grp_streams[s0 + gi]) * D + h * HD + e8);
+            const float4* qp = reinterpret_cast<const float4*>(q + size_t(grp_streams[s0 + gi]) * ldq + h * HD + e8);
             const float4 a = __ldg(qp), b = __ldg(qp + 1);
             const float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
 #pragma unroll
@@ -231,7 +233,7 @@ __global__ void __launch_bounds__(TC_WARPS * 32) k_attn_dec_tc(const float* __re
                                                               const int* __restrict__ grp_off,
                                                               const int* __restrict__ grp_streams,
                                                               float* __restrict__ out, float* __restrict__ part,
-                                                              unsigned* __restrict__ cnt) {
+                                                              unsigned* __restrict__ cnt, int ldq) {
     pdl_trigger();
     extern __shared__ __align__(128) uint8_t tc_smem[];
     __shared__ float s_acc[TC_WARPS][DEC_MAX_G][HD];
@@ -266,7 +268,7 @@ __global__ void __launch_bounds__(TC_WARPS * 32) k_attn_dec_tc(const float* __re
     uint32_t qa[4][4];
     {
         const bool live = g < G;
-        const float* qp = q + size_t(live ? grp_streams[s0 + g] : 0) * D + h * HD;
+        const float* qp = q + size_t(live ? grp_streams[s0 + g] : 0) * ldq + h * HD;
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk)
 #pragma unroll
@@ -461,12 +463,12 @@ __global__ void __launch_bounds__(256) k_argmax(const float* __restrict__ logits
 
 }  // namespace
 
-cudaError_t launch_kv_append(const float* k_new, const float* v_new, int S, int H, int ctx, const int* dpos,
+cudaError_t launch_kv_append(const float* k_new, const float* v_new, int ld, int S, int H, int ctx, const int* dpos,
                              __half* kc, __half* vc, cudaStream_t s) {
     const size_t total = size_t(S) * H * HD;
     if (!total) return cudaSuccess;
-    return launch_pdl(k_kv_append, dim3(unsigned((total + 255) / 256)), dim3(256), 0, s, k_new, v_new, S, H, ctx, dpos,
-                      kc, vc);
+    return launch_pdl(k_kv_append, dim3(unsigned((total + 255) / 256)), dim3(256), 0, s, k_new, v_new, ld, S, H, ctx,
+                      dpos, kc, vc);
 }
 
 // *dpos += 1 (the decode position, advanced on the device so that a step
@@ -483,7 +485,7 @@ cudaError_t launch_pos_advance(int* dpos, cudaStream_t s) {
 
 cudaError_t launch_attn_dec(const float* q, const __half* kc, const __half* vc, size_t kv_stride, int L,
                             const int* dpos, int H, int n_groups, int max_group, const int* grp_kv, const int* grp_off,
-                            const int* grp_streams, float* out, int splits, float* part, unsigned* cnt,
+                            const int* grp_streams, float* out, int splits, float* part, unsigned* cnt, int ldq,
                             cudaStream_t s) {
     if (!n_groups || !L) return cudaSuccess;
     if (max_group > DEC_MAX_G || splits < 1 || splits > 8 || (splits > 1 && (!part || !cnt || max_group <= 1)))
@@ -509,10 +511,10 @@ cudaError_t launch_attn_dec(const float* q, const __half* kc, const __half* vc, 
             attr_mask |= 1u << (dev & 31);
         }
         return launch_pdl(k_attn_dec_tc, grid, dim3(TC_WARPS * 32), size_t(TC_SMEM), s, q, kc, vc, kv_stride, L, dpos,
-                          H, grp_kv, grp_off, grp_streams, out, part, cnt);
+                          H, grp_kv, grp_off, grp_streams, out, part, cnt, ldq);
     }
     return launch_pdl(k_attn_dec<1>, grid, dim3(DEC_THREADS), 0, s, q, kc, vc, kv_stride, L, dpos, H, grp_kv, grp_off,
-                      grp_streams, out);
+                      grp_streams, out, ldq);
 }
 
 int attn_dec_splits(int H, int n_groups, int max_group, int L, int sms) {

@@ -78,6 +78,9 @@ struct rwq_qtensor;
 namespace rwq {
 // The device weight behind a C-ABI handle (defined in rwq_api.cu).
 const Weight& weight_of(const rwq_qtensor* t);
+// A new weight holding the rows of `parts` in order (same dtype, k and
+// device); status code as the C ABI.
+int qtensor_concat_rows(rwq_qtensor* const* parts, int np, cudaStream_t s, rwq_qtensor** out);
 // Set the text rwq_last_error() returns on this host thread.
 void set_last_error(const char* msg);
 }  // namespace rwq
