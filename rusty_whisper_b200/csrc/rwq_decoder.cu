@@ -264,6 +264,20 @@ int issue_step(rwq_decoder* d, int mode, int32_t limit, cudaStream_t s) {
                                d->x, s),
              "embed");
     const size_t self_layer = size_t(S) * H * d->n_ctx * 64, cross_layer = size_t(d->n_windows) * H * d->n_audio * 64;
+    // GEMV-family steps: the attention kernels quantize their output rows
+    // themselves (the layout k_rows_quant would write), one launch less
+    // per attention.
+    const bool gemv = S <= rwq::GEMV_FAMILY_MAX_M;
+    rwq::AttnQuantOut qo;
+    {
+        const rwq::ActsView a = with_k(d->gemv, D);
+        qo.q8 = a.q8;
+        qo.d = a.d;
+        qo.sum = a.sum;
+        qo.u = a.u;
+    }
+    const rwq::AttnQuantOut* q_self = gemv && rwq::attn_dec_quantizes(1) ? &qo : nullptr;
+    const rwq::AttnQuantOut* q_cross = gemv && rwq::attn_dec_quantizes(d->max_group) ? &qo : nullptr;
     for (int l = 0; l < d->n_layer; ++l) {
         const DLayer& L = d->layers[size_t(l)];
         // causal self-attention over the cache (decoder.rs:140-171)
@@ -285,9 +299,9 @@ int issue_step(rwq_decoder* d, int mode, int32_t limit, cudaStream_t s) {
         __half* vc = d->self_v + size_t(l) * self_layer;
         DEC_CUDA(rwq::launch_kv_append(kp, vp, ld, S, H, d->n_ctx, d->dpos, kc, vc, s), "kv append");
         DEC_CUDA(rwq::launch_attn_dec(qp, kc, vc, size_t(d->n_ctx) * 64, d->n_ctx, d->dpos, H, S, 1, d->self_kv,
-                                      d->self_off, d->self_kv, d->att, 1, nullptr, nullptr, ld, s),
+                                      d->self_off, d->self_kv, d->att, 1, nullptr, nullptr, ld, q_self, s),
                  "self attention");
-        DEC_RC(rows(d, rwq::RQ_PLAIN, d->att, nullptr, nullptr, nullptr, nullptr, D, s));
+        if (!q_self) DEC_RC(rows(d, rwq::RQ_PLAIN, d->att, nullptr, nullptr, nullptr, nullptr, D, s));
         DEC_RC(linear(d, L.o, L.o_b, d->tmp, s));
         // cross-attention to the window's K/V (decoder.rs:173-188)
         DEC_RC(rows(d, rwq::RQ_ADD_LN, d->x, d->tmp, d->x, L.x_ln_w, L.x_ln_b, D, s));
@@ -295,9 +309,9 @@ int issue_step(rwq_decoder* d, int mode, int32_t limit, cudaStream_t s) {
         DEC_CUDA(rwq::launch_attn_dec(d->q, d->cross_k + size_t(l) * cross_layer, d->cross_v + size_t(l) * cross_layer,
                                       size_t(d->n_audio) * 64, d->n_audio, nullptr, H, d->n_cross_groups, d->max_group,
                                       d->cross_kv, d->cross_off, d->cross_streams, d->att, d->cross_splits,
-                                      d->attn_part, d->attn_cnt, D, s),
+                                      d->attn_part, d->attn_cnt, D, q_cross, s),
                  "cross attention");
-        DEC_RC(rows(d, rwq::RQ_PLAIN, d->att, nullptr, nullptr, nullptr, nullptr, D, s));
+        if (!q_cross) DEC_RC(rows(d, rwq::RQ_PLAIN, d->att, nullptr, nullptr, nullptr, nullptr, D, s));
         DEC_RC(linear(d, L.xo, L.xo_b, d->tmp, s));
         // MLP (encoder.rs:154-172)
         DEC_RC(rows(d, rwq::RQ_ADD_LN, d->x, d->tmp, d->x, L.mlp_ln_w, L.mlp_ln_b, D, s));

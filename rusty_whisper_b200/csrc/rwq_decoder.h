@@ -22,6 +22,15 @@ cudaError_t launch_pos_advance(int* dpos, cudaStream_t s);
 // f16 [L][64]; its streams are grp_streams[grp_off[g] .. grp_off[g+1])
 // (<= max_group <= DEC_MAX_G).  Device arrays.  With dpos the keys are 0..*dpos
 // (self-attention over the cache; L is then the capacity).
+// With qout the output rows go straight to the int8 GEMV layout (codes
+// [S][D], d / sum / d*sum [S][D/32], as k_rows_quant writes them; out is
+// then unused).
+struct AttnQuantOut {
+    int8_t* q8 = nullptr;
+    float* d = nullptr;
+    int32_t* sum = nullptr;
+    float* u = nullptr;
+};
 // Runs on the tensor cores (k_attn_dec_tc; RWQ_ATTN_TC=0 keeps
 // single-stream groups on the CUDA-core k_attn_dec); splits > 1
 // (those groups only) divides the keys over that many CTAs per (head,
@@ -30,7 +39,10 @@ cudaError_t launch_pos_advance(int* dpos, cudaStream_t s);
 cudaError_t launch_attn_dec(const float* q, const __half* kc, const __half* vc, size_t kv_stride, int L,
                             const int* dpos, int H, int n_groups, int max_group, const int* grp_kv, const int* grp_off,
                             const int* grp_streams, float* out, int splits, float* part, unsigned* cnt, int ldq,
-                            cudaStream_t s);
+                            const AttnQuantOut* qout, cudaStream_t s);
+// Whether launch_attn_dec takes qout for groups of this size (the
+// tensor-core kernel; not the CUDA-core one that RWQ_ATTN_TC=0 selects).
+bool attn_dec_quantizes(int max_group);
 // Key splits for a grid of H x n_groups CTAs: 1 for single-stream groups,
 // else enough for one CTA per SM, at most 8 splits of at least 128 keys.
 int attn_dec_splits(int H, int n_groups, int max_group, int L, int sms);

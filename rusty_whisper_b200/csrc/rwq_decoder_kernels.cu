@@ -226,6 +226,31 @@ __device__ __forceinline__ void tc_split2(float x0, float x1, uint32_t& hi, uint
     lo = *reinterpret_cast<const uint32_t*>(&l);
 }
 
+// The GEMV-layout int8 quantizer of the activation row kernels
+// (quant.rs:690-716) on one 32-element block held one element per lane:
+// d = amax/127, inv = 1/d or 0, q = round(x*inv) half away from zero,
+// clamped to +-127, NaN -> 0; sum(q) and d*sum(q).  Max and integer sums
+// do not depend on the order, so the bits equal k_rows_quant's.
+__device__ __forceinline__ void tc_quant32(float x, int lane, int8_t* q, float* d_out, int32_t* s_out, float* u_out) {
+    float a = fabsf(x);
+    a = isnan(a) ? 0.f : a;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, o));
+    const float d = __fdiv_rn(a, 127.0f);
+    const float inv = d > 0.f ? __fdiv_rn(1.0f, d) : 0.f;
+    const float r = roundf(__fmul_rn(x, inv));
+    const int c = isnan(r) ? 0 : int(fminf(127.f, fmaxf(-127.f, r)));
+    q[lane] = int8_t(c);
+    int sm = c;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sm += __shfl_xor_sync(0xffffffffu, sm, o);
+    if (lane == 0) {
+        *d_out = d;
+        *s_out = sm;
+        *u_out = __fmul_rn(d, float(sm));
+    }
+}
+
 __global__ void __launch_bounds__(TC_WARPS * 32) k_attn_dec_tc(const float* __restrict__ q, const __half* __restrict__ kc,
                                                               const __half* __restrict__ vc, size_t kv_stride, int L,
                                                               const int* __restrict__ dpos, int H,
@@ -233,14 +258,32 @@ __global__ void __launch_bounds__(TC_WARPS * 32) k_attn_dec_tc(const float* __re
                                                               const int* __restrict__ grp_off,
                                                               const int* __restrict__ grp_streams,
                                                               float* __restrict__ out, float* __restrict__ part,
-                                                              unsigned* __restrict__ cnt, int ldq) {
+                                                              unsigned* __restrict__ cnt, int ldq, AttnQuantOut qo) {
     pdl_trigger();
     extern __shared__ __align__(128) uint8_t tc_smem[];
     __shared__ float s_acc[TC_WARPS][DEC_MAX_G][HD];
     __shared__ float s_ml[TC_WARPS][DEC_MAX_G][2];
+    __shared__ float s_o[DEC_MAX_G][HD];   // quantized output: the rows before quantizing
     __shared__ int s_last;
     const int h = blockIdx.x, gr = blockIdx.y, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int g = lane >> 2, c = lane & 3;
+    // Output element (query gi, dim e) of this head: f32, or kept for the
+    // quantizer below.
+    auto emit = [&](int gi, int e, float v) {
+        if (qo.q8) s_o[gi][e] = v;
+        else out[size_t(grp_streams[grp_off[gr] + gi]) * (H * HD) + h * HD + e] = v;
+    };
+    // Blocks 2h, 2h+1 of each query's row, one warp per block.
+    auto quantize = [&]() {
+        if (!qo.q8) return;
+        __syncthreads();
+        const int s0q = grp_off[gr], Gq = grp_off[gr + 1] - s0q, nbq = H * HD / QK;
+        for (int i = warp; i < 2 * Gq; i += TC_WARPS) {
+            const int gi = i >> 1, half = i & 1, st = grp_streams[s0q + gi], kb = 2 * h + half;
+            tc_quant32(s_o[gi][half * 32 + lane], lane, qo.q8 + size_t(st) * (H * HD) + kb * QK,
+                       qo.d + size_t(st) * nbq + kb, qo.sum + size_t(st) * nbq + kb, qo.u + size_t(st) * nbq + kb);
+        }
+    };
     const int D = H * HD, splits = int(gridDim.z), sp = int(blockIdx.z);
     pdl_wait();
     if (dpos) L = min(*dpos + 1, L);   // self-attention: keys 0..pos (L is the cache capacity)
@@ -382,7 +425,7 @@ __global__ void __launch_bounds__(TC_WARPS * 32) k_attn_dec_tc(const float* __re
             den = fmaf(s_ml[w][gi][1], f, den);
         }
         if (splits == 1) {
-            out[size_t(grp_streams[s0 + gi]) * D + h * HD + e] = num / den;
+            emit(gi, e, num / den);
         } else {
             float* r = rec(sp, gi);
             r[2 + e] = num;
@@ -392,7 +435,10 @@ __global__ void __launch_bounds__(TC_WARPS * 32) k_attn_dec_tc(const float* __re
             }
         }
     }
-    if (splits == 1) return;
+    if (splits == 1) {
+        quantize();
+        return;
+    }
     __threadfence();
     __syncthreads();
     if (tid == 0) s_last = atomicAdd(cnt + size_t(gr) * H + h, 1u) == unsigned(splits - 1);
@@ -411,9 +457,10 @@ __global__ void __launch_bounds__(TC_WARPS * 32) k_attn_dec_tc(const float* __re
             num = fmaf(__ldcg(r + 2 + e), f, num);
             den = fmaf(__ldcg(r + 1), f, den);
         }
-        out[size_t(grp_streams[s0 + gi]) * D + h * HD + e] = num / den;
+        emit(gi, e, num / den);
     }
     if (tid == 0) cnt[size_t(gr) * H + h] = 0u;   // ready for the next launch
+    quantize();
 }
 
 // Greedy choice (decoder.rs:345-365): the first maximum over ids
@@ -486,7 +533,7 @@ cudaError_t launch_pos_advance(int* dpos, cudaStream_t s) {
 cudaError_t launch_attn_dec(const float* q, const __half* kc, const __half* vc, size_t kv_stride, int L,
                             const int* dpos, int H, int n_groups, int max_group, const int* grp_kv, const int* grp_off,
                             const int* grp_streams, float* out, int splits, float* part, unsigned* cnt, int ldq,
-                            cudaStream_t s) {
+                            const AttnQuantOut* qout, cudaStream_t s) {
     if (!n_groups || !L) return cudaSuccess;
     if (max_group > DEC_MAX_G || splits < 1 || splits > 8 || (splits > 1 && (!part || !cnt || max_group <= 1)))
         return cudaErrorInvalidValue;
@@ -511,10 +558,21 @@ cudaError_t launch_attn_dec(const float* q, const __half* kc, const __half* vc, 
             attr_mask |= 1u << (dev & 31);
         }
         return launch_pdl(k_attn_dec_tc, grid, dim3(TC_WARPS * 32), size_t(TC_SMEM), s, q, kc, vc, kv_stride, L, dpos,
-                          H, grp_kv, grp_off, grp_streams, out, part, cnt, ldq);
+                          H, grp_kv, grp_off, grp_streams, out, part, cnt, ldq, qout ? *qout : AttnQuantOut{});
     }
+    if (qout) return cudaErrorNotSupported;   // the CUDA-core kernel writes f32 only
     return launch_pdl(k_attn_dec<1>, grid, dim3(DEC_THREADS), 0, s, q, kc, vc, kv_stride, L, dpos, H, grp_kv, grp_off,
                       grp_streams, out, ldq);
+}
+
+bool attn_dec_quantizes(int max_group) {
+    (void)max_group;
+    static int use_tc = -1;
+    if (use_tc < 0) {
+        const char* e = getenv("RWQ_ATTN_TC");
+        use_tc = (e && e[0] == '0') ? 0 : 1;
+    }
+    return max_group > 1 || use_tc;
 }
 
 int attn_dec_splits(int H, int n_groups, int max_group, int L, int sms) {
