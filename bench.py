@@ -145,6 +145,7 @@ def run_ours(args, rank, world, local_rank):
 
     torch.cuda.set_device(local_rank)
     quant.init(local_rank)
+    quant.set_gemm_path(args.gemm_path)
     dev = torch.device("cuda", local_rank)
     hbm_peak, tc_peak, peak_kind = peaks()
 
@@ -413,7 +414,7 @@ def run_decoder_beams(args, dev, hbm_peak, stream, rank, world):
     c = DEC_MEDIUM
     n_win, beams, steps, prefix = 16, 5, 224, 4
     S = n_win * beams
-    t = synth.decoder_tensors(c["n_vocab"], c["n_ctx"], c["n_state"], c["n_layer"], 6, seed=7, reuse_layers=True)
+    t = synth.decoder_tensors(c["n_vocab"], c["n_ctx"], c["n_state"], c["n_layer"], 6, seed=7, gen_device=dev)
     dec = decoder.Decoder(c["n_vocab"], c["n_ctx"], c["n_state"], c["n_head"], c["n_layer"], t)
     enc = torch.from_numpy(synth.normal(300 + rank, n_win * 1500 * c["n_state"]).reshape(n_win, 1500, c["n_state"]))
     enc = enc.to(dev)
@@ -452,8 +453,7 @@ def run_decoder_beams(args, dev, hbm_peak, stream, rank, world):
                               "cross_kv_f16_MB": round(cross_bytes / 1e6, 1)},
            "note": "linears on the tiled integer-MMA GEMV (k_gemv_tile: 80 streams as 32-row tiles, bit-identical "
                    "to the per-stream GEMV); each stream takes its own greedy id; the step replays from a CUDA graph",
-           "data": "synthetic (seeded): random-code Q5_0 weights (block 0 values reused by every block, each block its "
-                   "own device copy), encoder output N(0, 1)"}
+           "data": "synthetic (seeded): random-code Q5_0 weights (every block its own draw), encoder output N(0, 1)"}
     if rank == 0 and world == 1 and not args.no_cpu:
         import oracle
         threads = oracle.default_threads()
@@ -484,8 +484,8 @@ def run_large_v3(args, dev, stream, rank, world):
     c = LARGE_V3
     total_win, steps = 256, 224
     n_win = total_win // world
-    te = synth.encoder_tensors(c["n_mels"], c["n_audio"], c["n_state"], c["enc_layers"], 2, seed=11, reuse_layers=True)
-    td = synth.decoder_tensors(c["n_vocab"], c["n_ctx"], c["n_state"], c["dec_layers"], 2, seed=12, reuse_layers=True)
+    te = synth.encoder_tensors(c["n_mels"], c["n_audio"], c["n_state"], c["enc_layers"], 2, seed=11, gen_device=dev)
+    td = synth.decoder_tensors(c["n_vocab"], c["n_ctx"], c["n_state"], c["dec_layers"], 2, seed=12, gen_device=dev)
     enc = encoder.Encoder(c["n_mels"], c["n_audio"], c["n_state"], c["n_head"], c["enc_layers"], te)
     dec = decoder.Decoder(c["n_vocab"], c["n_ctx"], c["n_state"], c["n_head"], c["dec_layers"], td)
     del te, td
@@ -548,14 +548,13 @@ def run_large_v3(args, dev, stream, rank, world):
            "h2d_bytes_per_rank": int(host.numel() * 4), "d2h_bytes_per_rank": int(steps * n_win * 4),
            "timing": "CUDA events around host audio -> tokens on the host, max over ranks",
            "data": "synthetic (seeded): band-limited noise at -20 dBFS with 0.2-2 s silences; random-code Q4_0 "
-                   "weights (block 0 values reused by every block, each block its own device copy)"}
+                   "weights (every block its own draw)"}
     if rank == 0 and world == 1 and not args.no_cpu:
         import oracle
         threads = oracle.default_threads()
         tc0 = time.perf_counter()
-        te = synth.encoder_tensors(c["n_mels"], c["n_audio"], c["n_state"], c["enc_layers"], 2, seed=11,
-                                   reuse_layers=True)
-        te = {k: v for k, v in te.items() if not k.startswith("encoder.blocks.") or k.split(".")[2] in ("0", "1")}
+        # blocks 0 and 1 of the same model (the generator draws blocks in order)
+        te = synth.encoder_tensors(c["n_mels"], c["n_audio"], c["n_state"], 2, 2, seed=11, gen_device=dev)
         ref_e = oracle.Encoder(c["n_mels"], c["n_audio"], c["n_state"], c["n_head"], 2, te)   # 2 of the 32 blocks
         mel1 = mel_plan(distinct[0])
         t0 = time.perf_counter()
@@ -563,7 +562,7 @@ def run_large_v3(args, dev, stream, rank, world):
         t_enc2 = time.perf_counter() - t0
         del ref_e, te
         td = synth.decoder_tensors(c["n_vocab"], c["n_ctx"], c["n_state"], c["dec_layers"], 2, seed=12,
-                                   reuse_layers=True)
+                                   gen_device=dev)
         ref_d = oracle.Decoder(c["n_vocab"], c["n_ctx"], c["n_state"], c["n_head"], c["dec_layers"], td)
         ref_d.begin(eo1, threads=threads)
         ref_d.forward([50258], threads=threads)
@@ -629,7 +628,7 @@ def run_profile_driver(args):
             n_win, per, dt = 256, 1, 2
         else:               # config 4: whisper-medium, Q5_0, 16 windows x 5 streams
             c, n_win, per, dt = DEC_MEDIUM, 16, 5, 6
-        t = synth.decoder_tensors(c["n_vocab"], c["n_ctx"], c["n_state"], c["n_layer"], dt, seed=7, reuse_layers=True)
+        t = synth.decoder_tensors(c["n_vocab"], c["n_ctx"], c["n_state"], c["n_layer"], dt, seed=7, gen_device=dev)
         dec = decoder.Decoder(c["n_vocab"], c["n_ctx"], c["n_state"], c["n_head"], c["n_layer"], t)
         enc = torch.empty((n_win, 1500, c["n_state"]), device=dev)
         for w in range(n_win):   # seeded rows, drawn per window to bound host memory
@@ -842,6 +841,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--gemm-path", type=int, default=0,
+                    help="GEMM kernel path of the sweep (rwq_set_gemm_path): 0 automatic (folded-scale), 2 folded-scale, "
+                         "3 exact integer, 4 hi|lo")
     ap.add_argument("--m", type=int, default=1,
                     help="--only logits: activation rows; --only decode: 256 selects config 5's decoder")
     ap.add_argument("--only", default="all", choices=["all", "gemm", "encoder", "decoder", "large", "logits", "gemv", "decode"],

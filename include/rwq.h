@@ -126,26 +126,37 @@ int rwq_block_dots_dev(const float* a, int64_t m, int64_t k, const rwq_qtensor* 
 
 /* Decoder-shaped int8 matmul that allocates no memory: out[m, n] =
  * A[m, k] * dequant(b)^T (+ bias) with m <= 8 and k <= 8192, device
- * pointers, asynchronous on `stream`, same results as rwq_matmul_t_q_dev.
+ * pointers, asynchronous on `stream`.  It runs the quantizer and GEMV
+ * kernels of rwq_matmul_t_q_dev (the same GEMV kind on the same host
+ * thread), so the results are bit-identical to that entry point's.
  * No counterpart in the reference.  For callers that may not allocate GPU
  * memory: a live-microphone decode loop on a latency-critical thread
  * (cudaMalloc/cudaFree can stall on an implicit device synchronization),
  * or an embedder whose GPU memory belongs to another allocator.  Its
  * scratch (the quantized activations, 88 KiB) is a fixed array that every
  * GPU loading this library holds until exit.  The first call on a device
- * looks up that array's device address; make that first call before any
- * stream capture.  All calls share the one array: calls that overlap on
- * the GPU (other streams, other host threads) race and must be ordered by
- * the caller, e.g. on one stream.  Larger m or k returns RWQ_ERR_ARG. */
+ * looks up that array's device address, which may make the driver load the
+ * library's module on that device (a driver-side allocation that can
+ * synchronize): make one warm-up call at initialisation, outside the
+ * latency-critical loop and before any stream capture.  The address is
+ * kept, so a cudaDeviceReset while the library is loaded is not supported.
+ * All calls share the one array: calls that overlap on the GPU (other
+ * streams, other host threads) race and must be ordered by the caller,
+ * e.g. on one stream.  Larger m or k returns RWQ_ERR_ARG. */
 int rwq_matmul_t_q_noalloc(const float* a, int64_t m, int64_t k, const rwq_qtensor* b, const float* bias,
                            float* out, void* stream);
 
 /* Force the kernel family (testing and benchmarking): 0 = automatic
- * (GEMV family for m <= 256, GEMM above), 1 = GEMV family in row chunks,
- * 2 = tensor-core GEMM with the weight scales folded into the operand
- * (the automatic choice), 3 = tensor-core GEMM that forms each block's
- * integer dot exactly and scales it on the CUDA cores.  Applies to this
- * host thread. */
+ * (GEMV family for m <= 256; above, path 2 for RWQ_MODE_INT8 and path 4
+ * for RWQ_MODE_F32), 1 = GEMV family in row
+ * chunks, 2 = tensor-core GEMM with the weight scales folded into the
+ * operand and each block's partial sum scaled by d_a on the CUDA cores,
+ * 3 = tensor-core GEMM that forms each block's integer dot exactly and
+ * scales it on the CUDA cores, 4 = tensor-core GEMM with both operands
+ * (dequantized activations d_a*q_a, or the f32 activations in
+ * RWQ_MODE_F32, and the dequantized weights) split into f16 hi + lo and
+ * the whole K accumulated in tensor memory (the f32 tier's kernel from
+ * 257 rows).  Applies to this host thread. */
 int rwq_set_gemm_path(int path);
 
 /* Force the kernel of the GEMV family (m <= 256, or path 1 above) for
@@ -165,6 +176,15 @@ int rwq_set_gemv_kernel(int kind);
 
 /* Synchronize `stream` and report any fault a kernel recorded on it. */
 int rwq_stream_check(void* stream);
+
+/* Dense tensor-core rate of the current device with the instructions the
+ * GEMMs issue: `iters` back-to-back tcgen05 MMAs of 128 x 256 (K = 32 for
+ * kind 0 = int8, K = 16 for kind 1 = f16) per CTA from shared memory into
+ * tensor memory, `ctas` CTAs (<= 0: one per SM), timed with CUDA events on
+ * the legacy stream after one shorter warm-up launch.  *tops = 2*M*N*K*
+ * iters*ctas / time in 1e12 ops/s; *ms (may be NULL) = the timed launch.
+ * A measurement aid for roofline denominators; no reference counterpart. */
+int rwq_mma_peak(int kind, long long iters, int ctas, double* tops, double* ms);
 
 /* ---- Model files ---------------------------------------------------------
  * Replace `model::load_model` (reference src/model.rs:145-275, legacy ggml

@@ -73,6 +73,9 @@ def lib():
             "orc_encoder_set": (i32, [P, ctypes.c_char_p, P, sz, i32, P, i32, i32]),
             "orc_encode": (i32, [P, P, P, i32]),
             "orc_layernorm": (None, [P, sz, i32, P, P]),
+            "orc_set_model_tier": (None, [i32]),
+            "orc_set_attn_f16": (None, [i32]),
+            "orc_round_f16": (ctypes.c_float, [ctypes.c_float]),
             "orc_gelu": (None, [P, sz]),
             "orc_mha": (i32, [P, i32, P, P, i32, i32, i32, i32, P, i32]),
             "orc_conv1d": (i32, [P, i32, i32, P, i32, i32, P, i32, P, i32]),
@@ -296,6 +299,25 @@ def log_mel_spectrogram(samples: np.ndarray, filters: np.ndarray, n_mels: int, t
 
 
 # ---------------------------------------------------------------- encoder
+def set_model_tier(tier: int) -> None:
+    """Tier of every quantized linear in the Encoder/Decoder restatements:
+    0 dispatched (default), 1 VNNI, 2 AVX2.  A test switch: the two x86
+    tiers are both the reference, and their outputs' drift through
+    requantized layers bounds what a faithful port can be held to."""
+    lib().orc_set_model_tier(int(tier))
+
+
+def set_attn_f16(on: bool) -> None:
+    """Round the attention operands (q, k, v, unnormalised softmax weights)
+    to f16 in the Encoder/Decoder restatements and ``mha``: a test switch
+    measuring the effect of the GPU kernels' f16 attention operands."""
+    lib().orc_set_attn_f16(1 if on else 0)
+
+
+def round_f16(x: float) -> float:
+    return float(lib().orc_round_f16(float(x)))
+
+
 def layernorm(x: np.ndarray, w: np.ndarray, b: np.ndarray) -> np.ndarray:
     """tensor.rs:274-289 over the last dimension (returns a copy)."""
     x = np.array(x, np.float32, order="C")

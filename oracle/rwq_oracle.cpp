@@ -1147,6 +1147,34 @@ void matmul_ref(const float* a, int m, int k, const float* b, int n, float* out)
     }
 }
 
+// Test switches of the model restatements (not reference behaviour):
+//   g_model_tier  0 = the dispatched tier for every quantized linear of the
+//                 encoder/decoder restatements, 1 = VNNI, 2 = AVX2: the
+//                 reference's two x86 tiers differ only in f32 rounding, so
+//                 running both measures how far two valid runs of the
+//                 reference drift apart through requantized layers;
+//   g_attn_f16    1 = attention operands rounded to f16 (q, k, v and the
+//                 unnormalised softmax weights exp(s - max), to nearest
+//                 even), the narrowing the GPU attention kernels apply,
+//                 so its effect on the outputs can be measured on the CPU.
+int g_model_tier = 0;
+int g_attn_f16 = 0;
+
+// f32 -> f16 -> f32, round to nearest even (IEEE 754 binary16), written
+// from the format's definition: 10 stored fraction bits, exponent range
+// [-14, 15], subnormals down to 2^-24, overflow to infinity.
+float round_f16(float x) {
+    if (!std::isfinite(x)) return x;
+    const float a = std::fabs(x);
+    if (a >= 65520.0f) return std::copysign(INFINITY, x);   // rounds past the largest f16 (65504)
+    int e;
+    std::frexp(a, &e);                       // a = f * 2^e, f in [0.5, 1)
+    const int q = std::max(e - 11, -24);     // quantum: 2^(e-11) (11 significant bits), 2^-24 floor
+    const float u = std::ldexp(1.0f, q);
+    const float r = std::nearbyint(a / u) * u;   // a / u is exact (power of two); nearbyint rounds half to even
+    return std::copysign(r, x);
+}
+
 // encoder.rs:48-80 (mha_split_kv over already-projected q, k, v [t, n_state]).
 void mha_ref(const float* q, int tq, const float* k, const float* v, int tkv, int n_state, int n_head, bool causal,
              float* out, int threads) {
@@ -1162,6 +1190,10 @@ void mha_ref(const float* q, int tq, const float* k, const float* v, int tkv, in
                 std::memcpy(&kh[size_t(r) * dh], k + size_t(r) * n_state + h * dh, sizeof(float) * dh);
                 std::memcpy(&vh[size_t(r) * dh], v + size_t(r) * n_state + h * dh, sizeof(float) * dh);
             }
+            if (g_attn_f16) {
+                for (auto* vec : {&qh, &kh, &vh})
+                    for (auto& x : *vec) x = round_f16(x);
+            }
             orc_matmul_t(qh.data(), tq, dh, kh.data(), tkv, sc.data(), 1);
             for (auto& s : sc) s *= scale;
             if (causal) {
@@ -1169,7 +1201,24 @@ void mha_ref(const float* q, int tq, const float* k, const float* v, int tkv, in
                 for (int i = 0; i < tq; ++i)
                     for (int j = off + i + 1; j < tkv; ++j) sc[size_t(i) * tkv + j] = -INFINITY;
             }
-            softmax_rows(sc.data(), size_t(tq), tkv);
+            if (g_attn_f16) {
+                // softmax with the weights exp(s - max) rounded to f16 before
+                // P.V and the normaliser summed from the unrounded weights
+                for (int i = 0; i < tq; ++i) {
+                    float* row = &sc[size_t(i) * tkv];
+                    float mx = -3.40282347e+38f;
+                    for (int j = 0; j < tkv; ++j) mx = std::fmax(mx, row[j]);
+                    float sum = 0.f;
+                    for (int j = 0; j < tkv; ++j) {
+                        const float e = std::exp(row[j] - mx);
+                        sum += e;
+                        row[j] = round_f16(e);
+                    }
+                    for (int j = 0; j < tkv; ++j) row[j] /= sum;
+                }
+            } else {
+                softmax_rows(sc.data(), size_t(tq), tkv);
+            }
             matmul_ref(sc.data(), tq, tkv, vh.data(), dh, oh.data());
             for (int r = 0; r < tq; ++r)
                 std::memcpy(out + size_t(r) * n_state + h * dh, &oh[size_t(r) * dh], sizeof(float) * dh);
@@ -1202,7 +1251,7 @@ struct OrcEncoder {
 
 // quant.rs:1054-1063: y = x W^T (+ b) through the weight's own matmul_t_q.
 void linear_q(OrcQTensor* w, const float* x, int m, const float* bias, float* y, int threads) {
-    orc_qtensor_matmul(w, x, m, y, 0, threads);
+    orc_qtensor_matmul(w, x, m, y, g_model_tier, threads);
     if (bias)
         for (int i = 0; i < m; ++i)
             for (int j = 0; j < w->n; ++j) y[size_t(i) * w->n + j] += bias[j];
@@ -1314,6 +1363,9 @@ int orc_encode(void* h, const float* mel, float* out, int threads) {
 
 // Pieces, for the kernels' own parity tests.
 void orc_layernorm(float* x, size_t rows, int cols, const float* w, const float* b) { ln_rows(x, rows, cols, w, b); }
+void orc_set_model_tier(int tier) { g_model_tier = (tier >= 0 && tier <= 2) ? tier : 0; }
+void orc_set_attn_f16(int on) { g_attn_f16 = on ? 1 : 0; }
+float orc_round_f16(float x) { return round_f16(x); }
 void orc_gelu(float* x, size_t n) { gelu_n(x, n); }
 int orc_mha(const float* q, int tq, const float* k, const float* v, int tkv, int n_state, int n_head, int causal,
             float* out, int threads) {

@@ -44,6 +44,7 @@ SIGNATURES = {
     "rwq_set_gemm_path": (_I, [_I]),
     "rwq_set_gemv_kernel": (_I, [_I]),
     "rwq_stream_check": (_I, [_P]),
+    "rwq_mma_peak": (_I, [_I, ctypes.c_longlong, _I, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_double)]),
     "rwq_model_load": (_I, [ctypes.c_char_p, ctypes.POINTER(_P)]),
     "rwq_model_load_memory": (_I, [_P, _SZ, ctypes.POINTER(_P)]),
     "rwq_model_free": (_I, [_P]),

@@ -43,13 +43,19 @@ def build(verbose: bool = False, force: bool = False) -> str:
     os.makedirs(objdir, exist_ok=True)
     objs = []
     procs = []
+    # An object is rebuilt when its source, or any header, is newer.
+    headers = glob.glob(os.path.join(CSRC, "*.cuh")) + glob.glob(os.path.join(CSRC, "*.h")) + \
+        [os.path.join(ROOT, "include", "rwq.h")]
+    t_hdr = max(os.path.getmtime(h) for h in headers)
     for src in sources():
         obj = os.path.join(objdir, os.path.basename(src) + ".o")
+        objs.append(obj)
+        if not force and os.path.exists(obj) and os.path.getmtime(obj) > max(os.path.getmtime(src), t_hdr):
+            continue
         cmd = [NVCC, *NVCC_FLAGS, "-c", src, "-o", obj]
         if verbose:
             print(" ".join(cmd), flush=True)
         procs.append((subprocess.Popen(cmd), src))
-        objs.append(obj)
     for p, src in procs:
         if p.wait() != 0:
             raise RuntimeError(f"nvcc failed on {src}")

@@ -3,12 +3,15 @@
 //
 // Dispatch of a matmul (quant.rs:754-1051 restated for the GPU):
 //   mode INT8 (the reference's tier on every x86 host):
-//     quantize activations (one launch), then
-//       m <= 256 -> GEMV family (decoder shapes, HBM-bound): the integer-
-//                   MMA kernel, launches of up to 64 rows
-//       m >  256 -> tcgen05 GEMM (encoder shapes)
-//   mode F32 (the reference's f32 fallback): dequant-then-f32 GEMV kernel
-//     over row chunks of 8.
+//     m <= 256 -> quantize (one launch), GEMV family (decoder shapes,
+//                 HBM-bound): the integer-MMA kernels
+//     m >  256 -> quantize (one launch), tcgen05 GEMM k_gemm_fold with the
+//                 weight scales folded into the operand (encoder shapes);
+//                 path 4 forces k_gemm_hl on the split dequantized
+//                 activations
+//   mode F32 (the reference's f32 fallback, dequant-then-f32):
+//     m <= 256 -> dequant-then-f32 GEMV kernel over row chunks of 8
+//     m >  256 -> split the f32 activations into f16 hi|lo, k_gemm_hl.
 #include <cuda_runtime.h>
 #include <cstdarg>
 #include <cstdio>
@@ -18,6 +21,7 @@
 #include <map>
 #include <mutex>
 #include <string>
+#include <tuple>
 #include <utility>
 #include "../../include/rwq.h"
 #include "rwq_common.cuh"
@@ -35,7 +39,7 @@ struct rwq_qacts {
     int max_m = 0, k = 0;
     void* buf = nullptr;
     rwq::ActsView v;       // valid rows: v.m
-    bool gemm = false;     // which operand layout the last quantize produced
+    int layout = rwq::LAYOUT_GEMV;   // the operand layout the last quantize produced
 };
 
 const rwq::Weight& rwq::weight_of(const rwq_qtensor* t) { return t->w; }
@@ -83,14 +87,21 @@ struct Workspace {
     int* err = nullptr;  // device-side fault code written by kernels
 };
 
-std::mutex g_ws_mu;
-std::map<std::pair<int, cudaStream_t>, Workspace*> g_ws;
+// What an arena serves on its (device, stream): the device-pointer
+// matmuls, the host-buffer entry points' copies of A/bias/C, and the
+// block-dot dumps' scratch output.  Part of the key, so no stream handle
+// value (cudaStreamLegacy, cudaStreamPerThread, ...) can alias another
+// purpose's arena.
+enum WsPurpose : int { WS_MATMUL = 0, WS_HOST_COPY = 1, WS_DOT_DUMP = 2 };
 
-int get_workspace(cudaStream_t s, Workspace** out) {
+std::mutex g_ws_mu;
+std::map<std::tuple<int, cudaStream_t, int>, Workspace*> g_ws;
+
+int get_workspace(cudaStream_t s, Workspace** out, int purpose = WS_MATMUL) {
     int dev = 0;
     RWQ_CUDA(cudaGetDevice(&dev), "cudaGetDevice");
     std::lock_guard<std::mutex> g(g_ws_mu);
-    auto& w = g_ws[{dev, s}];
+    auto& w = g_ws[std::make_tuple(dev, s, purpose)];
     if (!w) {
         auto* nw = new Workspace;
         cudaError_t e = cudaMalloc(&nw->err, sizeof(int));
@@ -119,8 +130,9 @@ int ensure_cap(Workspace* ws, size_t bytes) {
     return RWQ_OK;
 }
 
-// Carve an activation view out of the arena starting at `base`.
-size_t acts_layout(int m, int k, bool gemm, rwq::ActsView* v, uint8_t* base) {
+// Carve an activation view in `layout` out of the arena starting at
+// `base` (nullptr: only measure).  Returns the bytes used.
+size_t acts_layout(int m, int k, int layout, rwq::ActsView* v, uint8_t* base) {
     const int nb = k / rwq::QK;
     const int m_pad = (m + 255) / 256 * 256;   // the fold GEMM's CTA pairs cover 256 rows
     size_t off = 0;
@@ -129,23 +141,45 @@ size_t acts_layout(int m, int k, bool gemm, rwq::ActsView* v, uint8_t* base) {
         off = align_up(off + bytes, 256);
         return p;
     };
+    *v = rwq::ActsView();
     v->m = m;
     v->k = k;
     v->nb = nb;
     v->m_pad = m_pad;
+    if (layout == rwq::LAYOUT_HL) {
+        v->ahl = reinterpret_cast<uint16_t*>(take(size_t(m) * k * 4));
+        v->rowscale = reinterpret_cast<float*>(take(size_t(m) * 4));
+        return off;
+    }
     v->q8 = reinterpret_cast<int8_t*>(take(size_t(m) * k));
     v->d = reinterpret_cast<float*>(take(size_t(m) * nb * 4));
     v->sum = reinterpret_cast<int32_t*>(take(size_t(m) * nb * 4));
     v->u = reinterpret_cast<float*>(take(size_t(m) * nb * 4));
-    if (gemm) {
+    if (layout == rwq::LAYOUT_FOLD) {
         v->q16 = reinterpret_cast<uint16_t*>(take(size_t(m) * k * 2));
         v->dT = reinterpret_cast<float*>(take(size_t(nb) * m_pad * 4));
         v->uT = reinterpret_cast<float*>(take(size_t(nb) * m_pad * 4));
-    } else {
-        v->q16 = nullptr;
-        v->dT = v->uT = nullptr;
     }
     return off;
+}
+
+size_t acts_bytes_max(int m, int k) {
+    rwq::ActsView v;
+    size_t b = 0;
+    for (int l : {rwq::LAYOUT_GEMV, rwq::LAYOUT_FOLD, rwq::LAYOUT_HL}) b = std::max(b, acts_layout(m, k, l, &v, nullptr));
+    return b;
+}
+
+// Fill `v` (already carved in `layout`) from f32 activations `a`.
+cudaError_t prepare_acts(const float* a, const rwq::ActsView& v, int layout, bool quantize, cudaStream_t s) {
+    if (layout == rwq::LAYOUT_HL) return rwq::launch_split_rows(a, v.m, v.k, v.k, quantize, v.ahl, v.rowscale, s);
+    return rwq::launch_quantize_acts(a, v, layout == rwq::LAYOUT_FOLD, s);
+}
+
+// Activation layout of a kernel path (1 GEMV family, 2 fold GEMM, 3 exact
+// GEMM, 4 hi|lo GEMM).
+int layout_of_path(int path) {
+    return path == 1 ? rwq::LAYOUT_GEMV : path == 4 ? rwq::LAYOUT_HL : rwq::LAYOUT_FOLD;
 }
 
 int weight_gemm_cache(rwq_qtensor* t, cudaStream_t s) {
@@ -197,20 +231,27 @@ int read_device_error(Workspace* ws, cudaStream_t s) {
     return RWQ_OK;
 }
 
-// Second half of a matmul: quantized activations `v` (GEMV layout, plus
-// the GEMM layout when `gemm`) against weight `b`.
-int run_quantized(const rwq::ActsView& v, bool gemm, rwq_qtensor* b, const float* bias, float* out, cudaStream_t s,
+// Second half of a matmul: activations `v` prepared in `layout` against
+// weight `b`.  FOLD runs k_gemm_fold, or k_gemm_tc when block dots are
+// dumped or path 3 is forced.
+int run_quantized(const rwq::ActsView& v, int layout, rwq_qtensor* b, const float* bias, float* out, cudaStream_t s,
                   int32_t* S_dump, int* err_flag) {
     const rwq::Weight& w = b->w;
-    const int64_t m = v.m, k = v.k;
-    if (!gemm) {
+    const int64_t k = v.k;
+    if (layout == rwq::LAYOUT_GEMV) {
         if (k > 8192) return fail(RWQ_ERR_ARG, "k=%lld too large for the GEMV kernels (max 8192)", (long long)k);
-        (void)m;
         RWQ_CUDA(rwq::launch_gemv_i8(v, w, bias, out, s), "gemv launch");
         return RWQ_OK;
     }
     int rc;
     char why[256] = {0};
+    if (layout == rwq::LAYOUT_HL) {
+        if ((rc = weight_fold_cache(b, s))) return rc;
+        cudaError_t e = rwq::launch_gemm_hl(v.ahl, v.rowscale, v.m, w.bhl, w.colscale, w.n, w.nb, bias, out, err_flag,
+                                            s, why, sizeof why);
+        if (e != cudaSuccess) return fail(RWQ_ERR_CUDA, "gemm launch: %s %s", cudaGetErrorString(e), why);
+        return RWQ_OK;
+    }
     if (!S_dump && t_gemm_path != 3) {
         if ((rc = weight_fold_cache(b, s))) return rc;
         cudaError_t e = rwq::launch_gemm_fold(v, w, bias, out, err_flag, s, why, sizeof why);
@@ -223,36 +264,53 @@ int run_quantized(const rwq::ActsView& v, bool gemm, rwq_qtensor* b, const float
     return RWQ_OK;
 }
 
+// The kernel path of an m-row matmul: forced, this thread's setting, or
+// automatic: the GEMV family up to 256 rows; above, the folded-scale GEMM
+// for the int8 tier (faster than the hi|lo GEMM on the encoder's shapes:
+// both move the same operand bytes per flop, and the hi|lo kernel's K
+// splits cost more than they save at M = 1500) and the hi|lo GEMM for the
+// f32 tier.
+int pick_path(int64_t m, int force_path, int mode = RWQ_MODE_INT8) {
+    int path = force_path ? force_path : t_gemm_path;
+    if (path == 0) path = (m <= rwq::GEMV_FAMILY_MAX_M) ? 1 : (mode == RWQ_MODE_F32 ? 4 : 2);
+    return path;
+}
+
 // The core device-pointer matmul.  `S_dump` (tests) routes through the
-// GEMM and makes it write the per-block integer dots.
+// exact GEMM and makes it write the per-block integer dots.
 int matmul_dev_impl(const float* a, int64_t m, int64_t k, rwq_qtensor* b, const float* bias, float* out, int mode,
                     cudaStream_t s, int32_t* S_dump, int force_path) {
     int rc = check_matmul_args(a, m, k, b, out, mode);
     if (rc) return rc;
     if (m == 0 || b->w.n == 0) return RWQ_OK;
     const rwq::Weight& w = b->w;
+    int path = pick_path(m, force_path, mode);
     if (mode == RWQ_MODE_F32) {
-        if (reinterpret_cast<uintptr_t>(a) & 15)
-            return fail(RWQ_ERR_ARG, "f32 mode needs 16-byte aligned device activations");
-        for (int64_t m0 = 0; m0 < m; m0 += rwq::GEMV_MAX_M) {
-            const int mc = int(m - m0 < rwq::GEMV_MAX_M ? m - m0 : rwq::GEMV_MAX_M);
-            RWQ_CUDA(rwq::launch_gemv_f32(a + m0 * k, mc, w, bias, out + m0 * w.n, s), "gemv_f32 launch");
+        // The f32 tier has two kernels: the CUDA-core GEMV (rows in chunks
+        // of 8) and, from 257 rows (or path 4 forced), the hi|lo GEMM.
+        if (path != 4) {
+            if (reinterpret_cast<uintptr_t>(a) & 15)
+                return fail(RWQ_ERR_ARG, "f32 mode needs 16-byte aligned device activations");
+            for (int64_t m0 = 0; m0 < m; m0 += rwq::GEMV_MAX_M) {
+                const int mc = int(m - m0 < rwq::GEMV_MAX_M ? m - m0 : rwq::GEMV_MAX_M);
+                RWQ_CUDA(rwq::launch_gemv_f32(a + m0 * k, mc, w, bias, out + m0 * w.n, s), "gemv_f32 launch");
+            }
+            return RWQ_OK;
         }
-        return RWQ_OK;
     }
-    int path = force_path ? force_path : t_gemm_path;
-    if (path == 0) path = (m <= rwq::GEMV_FAMILY_MAX_M) ? 1 : 2;
-    const bool gemm = path >= 2;
-    if (gemm && (k * 2) % 16) return fail(RWQ_ERR_ARG, "k*2 bytes must be a multiple of 16 for the GEMM");
+    if (S_dump) path = 3;
+    const int layout = layout_of_path(path);
+    if (layout == rwq::LAYOUT_FOLD && (k * 2) % 16)
+        return fail(RWQ_ERR_ARG, "k*2 bytes must be a multiple of 16 for the GEMM");
     Workspace* ws = nullptr;
     if ((rc = get_workspace(s, &ws))) return rc;
     std::lock_guard<std::mutex> g(ws->mu);
     rwq::ActsView v;
-    const size_t need = acts_layout(int(m), int(k), gemm, &v, nullptr);
+    const size_t need = acts_layout(int(m), int(k), layout, &v, nullptr);
     if ((rc = ensure_cap(ws, need))) return rc;
-    acts_layout(int(m), int(k), gemm, &v, static_cast<uint8_t*>(ws->buf));
-    RWQ_CUDA(rwq::launch_quantize_acts(a, v, gemm, s), "quantize launch");
-    return run_quantized(v, gemm, b, bias, out, s, S_dump, ws->err);
+    acts_layout(int(m), int(k), layout, &v, static_cast<uint8_t*>(ws->buf));
+    RWQ_CUDA(prepare_acts(a, v, layout, mode == RWQ_MODE_INT8, s), "activation operand launch");
+    return run_quantized(v, layout, b, bias, out, s, S_dump, ws->err);
 }
 
 cudaStream_t thread_stream() {
@@ -305,7 +363,7 @@ int rwq::gemm_quantized(const ActsView& v, rwq_qtensor* w, const float* bias, fl
     int rc = get_workspace(s, &ws);
     if (rc) return rc;
     if (v.k != w->w.k) return fail(RWQ_ERR_SHAPE, "gemm inner dims: %d vs %d", v.k, w->w.k);
-    return run_quantized(v, true, w, bias, out, s, nullptr, ws->err);
+    return run_quantized(v, v.ahl ? LAYOUT_HL : LAYOUT_FOLD, w, bias, out, s, nullptr, ws->err);
 }
 
 int rwq::linear_acts(const ActsView& v, bool gemm, rwq_qtensor* w, const float* bias, float* out, cudaStream_t s) {
@@ -313,8 +371,10 @@ int rwq::linear_acts(const ActsView& v, bool gemm, rwq_qtensor* w, const float* 
     int rc = get_workspace(s, &ws);
     if (rc) return rc;
     if (v.k != w->w.k) return fail(RWQ_ERR_SHAPE, "linear inner dims: %d vs %d", v.k, w->w.k);
-    return run_quantized(v, gemm, w, bias, out, s, nullptr, ws->err);
+    return run_quantized(v, !gemm ? LAYOUT_GEMV : v.ahl ? LAYOUT_HL : LAYOUT_FOLD, w, bias, out, s, nullptr, ws->err);
 }
+
+int rwq::gemm_path() { return pick_path(GEMV_FAMILY_MAX_M + 1, 0); }
 
 int rwq::with_stream_scratch(cudaStream_t s, size_t bytes, const std::function<int(void*)>& fn) {
     Workspace* ws = nullptr;
@@ -512,7 +572,7 @@ int rwq_matmul_t_q(const float* a, int64_t m, int64_t k, const rwq_qtensor* b, c
     // Host-buffer compat path: device copies of A, bias and C live in a
     // second arena keyed on this thread's stream.
     Workspace* ws = nullptr;
-    if ((rc = get_workspace(reinterpret_cast<cudaStream_t>(reinterpret_cast<uintptr_t>(s) ^ 1), &ws))) return rc;
+    if ((rc = get_workspace(s, &ws, WS_HOST_COPY))) return rc;
     std::lock_guard<std::mutex> g(ws->mu);
     const size_t a_b = align_up(size_t(m) * k * 4, 256), o_b = align_up(size_t(m) * n * 4, 256),
                  b_b = align_up(size_t(n) * 4, 256);
@@ -523,10 +583,12 @@ int rwq_matmul_t_q(const float* a, int64_t m, int64_t k, const rwq_qtensor* b, c
     if (bias) RWQ_CUDA(cudaMemcpyAsync(dbias, bias, size_t(n) * 4, cudaMemcpyHostToDevice, s), "copy bias");
     // GEMM-family calls (m > 256 and no forced path) run in row chunks of
     // more than 256 rows, so every chunk stays in the family and the results
-    // are those of one call: the upload of chunk c+1, the matmul of chunk c
+    // are those of one call (each output row's sum does not depend on which
+    // other rows share the GEMM as long as the K split is the same; the
+    // K split is picked from the chunk's tile count, see k_gemm_hl): the upload of chunk c+1, the matmul of chunk c
     // and the download of chunk c-1 overlap (PCIe is full duplex).  With
     // pageable host buffers the copies still work, without the overlap.
-    const int chunks = (mode == RWQ_MODE_INT8 && t_gemm_path == 0) ? int(std::min<int64_t>(6, m / 257)) : 1;
+    const int chunks = (t_gemm_path == 0) ? int(std::min<int64_t>(6, m / 257)) : 1;
     if (chunks < 2) {
         RWQ_CUDA(cudaMemcpyAsync(da, a, size_t(m) * k * 4, cudaMemcpyHostToDevice, s), "copy A to device");
         if ((rc = matmul_dev_impl(da, m, k, const_cast<rwq_qtensor*>(b), dbias, dout, mode, s, nullptr, 0)))
@@ -535,6 +597,12 @@ int rwq_matmul_t_q(const float* a, int64_t m, int64_t k, const rwq_qtensor* b, c
     } else {
         CopyPipe* cp = nullptr;
         if ((rc = copy_pipe(&cp))) return rc;
+        // Every chunk runs with the K split of the whole call, so the
+        // chunks give the bits of one device call.
+        struct KsplitGuard {
+            explicit KsplitGuard(int S) { rwq::set_gemm_hl_ksplit(S); }
+            ~KsplitGuard() { rwq::set_gemm_hl_ksplit(0); }
+        } ks_guard(rwq::gemm_hl_ksplit(int(m), int(n), int(k / rwq::QK)));
         RWQ_CUDA(cudaEventRecord(cp->ev_in, s), "event");
         RWQ_CUDA(cudaStreamWaitEvent(cp->up, cp->ev_in, 0), "event wait");
         RWQ_CUDA(cudaStreamWaitEvent(cp->down, cp->ev_in, 0), "event wait");
@@ -585,7 +653,7 @@ int rwq_row_f32(const rwq_qtensor* t, int64_t row, float* out) {
     cudaStream_t s = thread_stream();
     Workspace* ws = nullptr;
     int rc;
-    if ((rc = get_workspace(reinterpret_cast<cudaStream_t>(reinterpret_cast<uintptr_t>(s) ^ 1), &ws))) return rc;
+    if ((rc = get_workspace(s, &ws, WS_HOST_COPY))) return rc;
     std::lock_guard<std::mutex> g(ws->mu);
     if ((rc = ensure_cap(ws, size_t(t->w.k) * 4 + 256))) return rc;
     int32_t* drow = reinterpret_cast<int32_t*>(static_cast<uint8_t*>(ws->buf) + size_t(t->w.k) * 4);
@@ -630,7 +698,7 @@ int rwq_block_dots_dev(const float* a, int64_t m, int64_t k, const rwq_qtensor* 
     if (path == 1) {
         // The GEMM writes S while computing C; C goes to scratch.
         Workspace* ws = nullptr;
-        if ((rc = get_workspace(reinterpret_cast<cudaStream_t>(reinterpret_cast<uintptr_t>(s) ^ 2), &ws))) return rc;
+        if ((rc = get_workspace(s, &ws, WS_DOT_DUMP))) return rc;
         std::lock_guard<std::mutex> g(ws->mu);
         if ((rc = ensure_cap(ws, size_t(m) * b->w.n * 4 + 256))) return rc;
         return matmul_dev_impl(a, m, k, const_cast<rwq_qtensor*>(b), nullptr, static_cast<float*>(ws->buf),
@@ -641,16 +709,16 @@ int rwq_block_dots_dev(const float* a, int64_t m, int64_t k, const rwq_qtensor* 
     if ((rc = get_workspace(s, &ws))) return rc;
     std::lock_guard<std::mutex> g(ws->mu);
     rwq::ActsView v;
-    const size_t need = acts_layout(int(m), int(k), false, &v, nullptr);
+    const size_t need = acts_layout(int(m), int(k), rwq::LAYOUT_GEMV, &v, nullptr);
     if ((rc = ensure_cap(ws, need))) return rc;
-    acts_layout(int(m), int(k), false, &v, static_cast<uint8_t*>(ws->buf));
+    acts_layout(int(m), int(k), rwq::LAYOUT_GEMV, &v, static_cast<uint8_t*>(ws->buf));
     RWQ_CUDA(rwq::launch_quantize_acts(a, v, false, s), "quantize launch");
     RWQ_CUDA(rwq::launch_block_dots(v, b->w, S, s), "block dots launch");
     return RWQ_OK;
 }
 
 int rwq_set_gemm_path(int path) {
-    if (path < 0 || path > 3) return fail(RWQ_ERR_ARG, "path must be 0, 1, 2 or 3");
+    if (path < 0 || path > 4) return fail(RWQ_ERR_ARG, "path must be 0, 1, 2, 3 or 4");
     t_gemm_path = path;
     return RWQ_OK;
 }
@@ -680,7 +748,7 @@ int rwq_qacts_new(int64_t max_m, int64_t k, rwq_qacts** out) {
     cudaGetDevice(&q->device);
     q->max_m = int(max_m);
     q->k = int(k);
-    const size_t bytes = acts_layout(q->max_m, q->k, true, &q->v, nullptr);
+    const size_t bytes = acts_bytes_max(q->max_m, q->k);
     cudaError_t e = cudaMalloc(&q->buf, bytes ? bytes : 256);
     if (e != cudaSuccess) {
         delete q;
@@ -706,14 +774,12 @@ int rwq_qacts_quantize(rwq_qacts* q, const float* a, int64_t m, void* stream) {
     if (!q) return fail(RWQ_ERR_ARG, "qacts is null");
     if (m < 0 || m > q->max_m) return fail(RWQ_ERR_ARG, "m=%lld outside [0, %d]", (long long)m, q->max_m);
     if (m > 0 && !a) return fail(RWQ_ERR_ARG, "activations are null");
-    int path = t_gemm_path;
-    if (path == 0) path = (m <= rwq::GEMV_FAMILY_MAX_M) ? 1 : 2;
-    q->gemm = path >= 2;
+    q->layout = layout_of_path(pick_path(m, 0));
     // Carve for the current m (row strides depend on m); the arena was
-    // sized for max_m in the GEMM layout, which is the larger one.
-    acts_layout(int(m), q->k, q->gemm, &q->v, static_cast<uint8_t*>(q->buf));
+    // sized for max_m in the largest layout.
+    acts_layout(int(m), q->k, q->layout, &q->v, static_cast<uint8_t*>(q->buf));
     if (m == 0) return RWQ_OK;
-    RWQ_CUDA(rwq::launch_quantize_acts(a, q->v, q->gemm, static_cast<cudaStream_t>(stream)), "quantize launch");
+    RWQ_CUDA(prepare_acts(a, q->v, q->layout, true, static_cast<cudaStream_t>(stream)), "quantize launch");
     return RWQ_OK;
 }
 
@@ -726,7 +792,7 @@ int rwq_matmul_t_q_qacts(const rwq_qacts* q, const rwq_qtensor* b, const float* 
     Workspace* ws = nullptr;
     int rc;
     if ((rc = get_workspace(s, &ws))) return rc;
-    return run_quantized(q->v, q->gemm, const_cast<rwq_qtensor*>(b), bias, out, s, nullptr, ws->err);
+    return run_quantized(q->v, q->layout, const_cast<rwq_qtensor*>(b), bias, out, s, nullptr, ws->err);
 }
 
 }  // extern "C"

@@ -42,6 +42,11 @@ int gemm_quantized(const ActsView& v, rwq_qtensor* w, const float* bias, float* 
 // integer-MMA GEMV in chunks of 8 rows), true the GEMM layout.
 int linear_acts(const ActsView& v, bool gemm, rwq_qtensor* w, const float* bias, float* out, cudaStream_t s);
 
+// The GEMM kernel path that GEMM-sized matmuls take on this host thread
+// (2 folded-scale, 3 exact-integer, 4 hi|lo; rwq_set_gemm_path), which
+// decides the activation layout (LAYOUT_FOLD or LAYOUT_HL) callers prepare.
+int gemm_path();
+
 // Run `fn` with this stream's scratch arena (at least `bytes`), holding
 // its lock.  Returns fn's status (or an RWQ_* error).
 int with_stream_scratch(cudaStream_t s, size_t bytes, const std::function<int(void*)>& fn);

@@ -39,6 +39,18 @@ struct ActsView {
     uint16_t* q16 = nullptr;   // [m][k] f16    GEMM operand (optional)
     float* dT = nullptr;       // [nb][m_pad]   (optional)
     float* uT = nullptr;       // [nb][m_pad]   (optional)
+    // hi|lo operand of k_gemm_hl (optional): per row and block 32 f16 hi
+    // then 32 f16 lo of a'*2^e_i (a' = d_a*q_a, or the f32 activation in
+    // f32 mode), rowscale[i] = 2^-e_i.
+    uint16_t* ahl = nullptr;   // [m][nb][64]
+    float* rowscale = nullptr; // [m]
+};
+
+// Operand layouts of a quantized activation matrix.
+enum ActsLayout : int {
+    LAYOUT_GEMV = 0,   // q8, d, sum, u
+    LAYOUT_FOLD = 1,   // d, sum, u, q16, dT, uT (k_gemm_fold, k_gemm_tc)
+    LAYOUT_HL = 2      // ahl, rowscale (k_gemm_hl)
 };
 
 // ---- launchers (return a cudaError_t of the launch) ----
@@ -61,6 +73,28 @@ cudaError_t launch_gemm_tc(const ActsView& v, const Weight& w, const float* bias
 // tcgen05 GEMM with the weight scales folded into the B operand.
 cudaError_t launch_gemm_fold(const ActsView& v, const Weight& w, const float* bias, float* y, int* err_flag,
                              cudaStream_t s, char* why, size_t why_len);
+
+// Rows of activations a[m][lda] (first k columns) into the hi|lo operand
+// of k_gemm_hl: with `quantize` the reference's int8 quantizer runs first
+// and the dequantized values d_a*q_a are split, else the f32 values.
+cudaError_t launch_split_rows(const float* a, int m, int k, int lda, bool quantize, uint16_t* ahl, float* rowscale,
+                              cudaStream_t s);
+// Dense f32 weight rows w[n][ldw] (first k columns) into the hi|lo
+// operand layout [n][k/32][64] with colscale[n_pad] (n_pad >= round4(n)).
+cudaError_t launch_split_dense(const float* w, int n, int k, int ldw, int n_pad, uint16_t* bhl, float* colscale,
+                               cudaStream_t s);
+// y[m][n] = (A'*2^e_i)(B*2^e_j)^T * 2^-e_i * 2^-e_j (+ bias) on tcgen05 with
+// both operands split into f16 hi + lo, the whole K accumulated in TMEM.
+cudaError_t launch_gemm_hl(const uint16_t* ahl, const float* rowscale, int m, const uint16_t* bhl,
+                           const float* colscale, int n, int nb, const float* bias, float* y, int* err_flag,
+                           cudaStream_t s, char* why, size_t why_len);
+// The K split (1, 2 or 4 CTAs per output tile) k_gemm_hl picks for an
+// m x n GEMM of nb blocks on the current device.
+int gemm_hl_ksplit(int m, int n, int nb);
+// Force the K split of this host thread's k_gemm_hl launches (1, 2 or 4;
+// anything else: automatic).  The host-buffer entry point runs row chunks
+// with the split of the whole call so that chunks give its bits.
+void set_gemm_hl_ksplit(int S);
 
 // The dp4a GEMV takes at most 8 activation rows per launch.
 constexpr int GEMV_MAX_M = 8;

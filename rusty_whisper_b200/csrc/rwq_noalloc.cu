@@ -6,9 +6,12 @@
 // memory is owned by another allocator (a framework's caching pool, a
 // fixed per-process budget) so the library may not reserve memory behind
 // its back.  rwq_matmul_t_q_noalloc serves them for the decoder's shapes
-// (m <= 8 rows, k <= 8192): the int8 activation quantizer and the dp4a
-// GEMV of rwq_matmul_t_q_dev, with their scratch (the quantized
-// activations) held in the file-scope array below instead of a workspace.
+// (m <= 8 rows, k <= 8192) with the int8 activation quantizer and the GEMV
+// family of rwq_matmul_t_q_dev (launch_gemv_i8: by default the integer-MMA
+// kernel, or whichever GEMV kind rwq_set_gemv_kernel chose on this host
+// thread), so its results are bit-identical to rwq_matmul_t_q_dev called
+// on the same thread.  Their scratch (the quantized activations) is held
+// in the file-scope array below instead of a workspace.
 #include <cuda_runtime.h>
 #include <cstdarg>
 #include <cstdio>
@@ -49,7 +52,9 @@ int fail(int code, const char* fmt, ...) {
 }
 
 // Device address of the scratch array on the current device; resolved on
-// the first call per device.
+// the first call per device and kept.  A cudaDeviceReset while the library
+// is loaded is not supported: the module would be reloaded elsewhere and
+// the kept address would be stale.
 int scratch_address(int dev, unsigned char** out) {
     if (dev < 0 || dev >= MAX_DEVICES) return fail(RWQ_ERR_ARG, "device %d out of range", dev);
     std::lock_guard<std::mutex> g(g_mu);

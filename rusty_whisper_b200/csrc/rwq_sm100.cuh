@@ -113,19 +113,16 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t* r) {
         : "r"(taddr));
 }
 
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t* r) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+}
+
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
-
-// K-major, 64-byte swizzle (layout type 4): 8-row core groups of 64-byte
-// rows, 512 bytes apart.
-__device__ __forceinline__ uint64_t sw64_desc(uint32_t saddr) {
-    uint64_t d = uint64_t((saddr & 0x3FFFFu) >> 4);
-    d |= uint64_t(16 >> 4) << 16;
-    d |= uint64_t(512 >> 4) << 32;
-    d |= uint64_t(1) << 46;
-    d |= uint64_t(4) << 61;
-    return d;
-}
 
 // D[tmem] (+)= A[smem] * B[smem]^T, kind::f16, instruction descriptor idesc.
 __device__ __forceinline__ void mma_f16_id(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
@@ -134,116 +131,6 @@ __device__ __forceinline__ void mma_f16_id(uint32_t d_tmem, uint64_t adesc, uint
         "{ .reg .pred p; setp.ne.b32 p, %4, 0; tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p; }" ::"r"(
             d_tmem),
         "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
-        : "memory");
-}
-
-// ---------------------------------------------------------------- CTA pairs
-// A cluster of two CTAs on neighbouring SMs runs one M=256 MMA per
-// instruction (`cta_group::2`): each CTA holds 128 rows of A and half of
-// B's rows in its own shared memory, and receives its 128 rows of D in its
-// own TMEM.  Loads stay per CTA (no multicast); only their completion is
-// counted on the leader's (rank 0) barrier.
-
-__device__ __forceinline__ uint32_t cluster_rank() {
-    uint32_t r;
-    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-    return r;
-}
-
-// shared::cluster address of the same shared variable in CTA `rank`.
-__device__ __forceinline__ uint32_t mapa_rank(const void* p, uint32_t rank) {
-    uint32_t r;
-    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
-    return r;
-}
-
-// All threads of both CTAs.
-__device__ __forceinline__ void cluster_sync_all() {
-    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
-
-// Arrive on a barrier given by its shared::cluster address (own or peer
-// CTA), default (.release.cta) semantics: a cluster-scope release would
-// fence every prior memory access of the thread.  TMEM reads are ordered
-// by tcgen05.wait::ld and tcgen05.fence::before_thread_sync instead.
-__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
-    asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
-}
-
-// Bounded parity wait on a barrier that the peer CTA also arrives on.
-// Returns false if the kernel is aborting.
-__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* b, uint32_t parity, volatile int* abort, int* err_flag,
-                                                  int code) {
-    const uint32_t addr = smem_u32(b);
-    long long t0 = 0;
-    for (uint32_t it = 0;; ++it) {
-        uint32_t ok;
-        asm volatile(
-            "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
-            : "=r"(ok)
-            : "r"(addr), "r"(parity)
-            : "memory");
-        if (ok) return true;
-        if ((it & 255u) == 0) {
-            if (*abort) return false;
-            const long long now = clock64();
-            if (it == 0) t0 = now;
-            else if (now - t0 > WAIT_CYCLES) {
-                *abort = 1;
-                if (err_flag) atomicCAS(err_flag, 0, code);
-                return false;
-            }
-        }
-    }
-}
-
-// Wait for a phase without looking at the abort flag, for at most
-// `max_cycles` (used to let copies in flight land before an aborting CTA
-// exits).  Returns whether the phase completed.
-__device__ __forceinline__ bool mbar_wait_for(uint64_t* b, uint32_t parity, long long max_cycles) {
-    const uint32_t addr = smem_u32(b);
-    const long long t0 = clock64();
-    for (;;) {
-        uint32_t ok;
-        asm volatile(
-            "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
-            : "=r"(ok)
-            : "r"(addr), "r"(parity)
-            : "memory");
-        if (ok) return true;
-        if (clock64() - t0 > max_cycles) return false;
-    }
-}
-
-// TMA tile load into this CTA's shared memory whose completion is counted
-// on the barrier at `bar_cluster` (the leader's), without multicast.
-__device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* map, int x, int y,
-                                                 uint32_t bar_cluster) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, "
-        "%3}], [%4];" ::"r"(smem_u32(dst)),
-        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar_cluster)
-        : "memory");
-}
-
-// D[tmem of both CTAs] (+)= A[smem of both] * B[smem of both]^T, M = 256.
-// Issued by one thread of the leader CTA; no output lanes disabled.
-__device__ __forceinline__ void mma_f16_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
-                                             uint32_t accumulate) {
-    asm volatile(
-        "{ .reg .pred p; setp.ne.b32 p, %4, 0; tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, {%5, %5, %5, %5, "
-        "%5, %5, %5, %5}, p; }" ::"r"(d_tmem),
-        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(0u)
-        : "memory");
-}
-
-// Arrive on the barrier at this offset in every CTA of `cta_mask` once the
-// issuing thread's prior pair MMAs have completed.
-__device__ __forceinline__ void mma_commit_pair(uint64_t* bar, uint16_t cta_mask) {
-    asm volatile(
-        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
-            smem_u32(bar)),
-        "h"(cta_mask)
         : "memory");
 }
 

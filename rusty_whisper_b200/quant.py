@@ -293,7 +293,12 @@ def block_dots(a, b: QTensor, path: int = 0):
 
 
 def set_gemm_path(path: int) -> None:
-    """0 automatic, 1 CUDA-core GEMV in row chunks, 2 tensor-core GEMM."""
+    """Kernel path of this host thread's matmuls: 0 automatic (GEMV family
+    up to 256 rows; above, 2 for the int8 tier and 4 for the f32 tier),
+    1 GEMV family in row chunks, 2 tensor-core GEMM
+    with the weight scales folded into the operand, 3 tensor-core GEMM with
+    exact per-block integer dots, 4 tensor-core GEMM with both operands
+    split into f16 hi + lo and the whole K accumulated in tensor memory."""
     _lib.check(_lib.lib().rwq_set_gemm_path(path))
 
 

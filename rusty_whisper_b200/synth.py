@@ -109,6 +109,88 @@ def random_blocks(dtype: int, n: int, k: int, seed: int, d_range=(0.001, 0.02), 
     return raw.reshape(-1)
 
 
+# ------------------------------------------- the same generator in torch
+# Bit-identical to ``splitmix64`` / ``uniform`` / ``randint`` /
+# ``f32_to_f16_bits`` / ``random_blocks`` above, on int64 torch tensors
+# (two's-complement wrap-around for the multiplies, masked shifts for the
+# logical right shifts), so deep models' weights can be drawn on the GPU:
+# every layer its own draw in a fraction of the time NumPy takes.
+def _s64(x: int) -> int:
+    x &= 0xFFFFFFFFFFFFFFFF
+    return x - (1 << 64) if x >= (1 << 63) else x
+
+
+def _t_srl(z, s: int):
+    return (z >> s) & ((1 << (64 - s)) - 1)
+
+
+def splitmix64_torch(seed: int, start: int, count: int, device):
+    import torch
+    idx = torch.arange(start + 1, start + count + 1, dtype=torch.int64, device=device)
+    z = idx * _s64(0x9E3779B97F4A7C15) + _s64(seed)
+    z = (z ^ _t_srl(z, 30)) * _s64(0xBF58476D1CE4E5B9)
+    z = (z ^ _t_srl(z, 27)) * _s64(0x94D049BB133111EB)
+    return z ^ _t_srl(z, 31)
+
+
+def uniform_torch(seed: int, count: int, lo: float, hi: float, device):
+    import torch
+    u = _t_srl(splitmix64_torch(seed, 0, count, device), 40).to(torch.float64) * (1.0 / (1 << 24))
+    return (lo + (hi - lo) * u).to(torch.float32)
+
+
+def f32_to_f16_bits_torch(x):
+    """``f32_to_f16_bits`` (the reference's half-up f32 -> f16) in torch."""
+    import torch
+    bits = x.contiguous().view(torch.int32).to(torch.int64) & 0xFFFFFFFF
+    sign = (bits >> 16) & 0x8000
+    exp = (bits >> 23) & 0xFF
+    frac = bits & 0x7FFFFF
+    e = exp - 127 + 15
+    out = torch.zeros_like(bits)
+    norm = ((e << 10) | (frac >> 13)) + ((frac >> 12) & 1)
+    out = torch.where((e > 0) & (e < 0x1F), sign | norm, out)
+    out = torch.where((e >= 0x1F) & (exp != 0xFF), sign | 0x7C00, out)
+    out = torch.where(exp == 0xFF, sign | 0x7C00 | torch.where(frac != 0, 0x200, 0), out)
+    sub = (e <= 0) & (e >= -10)
+    f = frac | 0x800000
+    shift = torch.clamp(14 - e, 1, 63)
+    subv = (f >> shift) + ((f >> (shift - 1)) & 1)
+    out = torch.where(sub, sign | subv, out)
+    out = torch.where(e < -10, sign, out)
+    return out
+
+
+def random_blocks_torch(dtype: int, n: int, k: int, seed: int, d_range=(0.001, 0.02), m_range=(-0.05, 0.05),
+                        device="cuda", chunk: int = 1 << 26):
+    """``random_blocks`` drawn on ``device``: a uint8 tensor with the same
+    bytes as the NumPy version."""
+    import torch
+    assert k % QK == 0
+    nblk = n * (k // QK)
+    bb = block_bytes(dtype)
+    raw = torch.zeros((nblk, bb), dtype=torch.uint8, device=device)
+    d = f32_to_f16_bits_torch(uniform_torch(seed * 4 + 1, nblk, *d_range, device))
+    raw[:, 0] = (d & 0xFF).to(torch.uint8)
+    raw[:, 1] = (d >> 8).to(torch.uint8)
+    if dtype in (Q4_1, Q5_1):
+        mm = f32_to_f16_bits_torch(uniform_torch(seed * 4 + 2, nblk, *m_range, device))
+        raw[:, 2] = (mm & 0xFF).to(torch.uint8)
+        raw[:, 3] = (mm >> 8).to(torch.uint8)
+    if dtype == Q8_0:
+        off, lo, hi = 2, -127, 127
+    else:
+        off, lo, hi = (2 if dtype in (Q4_0, Q5_0) else 4), 0, 255
+    body = raw[:, off:].reshape(-1)
+    span = hi - lo + 1
+    for c0 in range(0, body.numel(), chunk):
+        c = min(chunk, body.numel() - c0)
+        v = _t_srl(splitmix64_torch(seed * 4 + 3, c0, c, device), 11) % span + lo
+        body[c0:c0 + c] = (v & 0xFF).to(torch.uint8)
+    raw[:, off:] = body.view(nblk, bb - off)
+    return raw.reshape(-1)
+
+
 def config1_inputs(seed: int = 0):
     """Q8_0 W[1536x384], X[1500x384] ~ N(0,1), seed 0."""
     w = random_blocks(Q8_0, 1536, 384, seed)
@@ -204,7 +286,7 @@ MODEL_CODE_SCALES = {
 
 
 def encoder_tensors(n_mels: int, n_ctx: int, n_state: int, n_layer: int, dtype: int, seed: int,
-                    reuse_layers: bool = False) -> dict:
+                    reuse_layers: bool = False, gen_device=None) -> dict:
     """Random-init whisper encoder tensors by their whisper.cpp names
     (encoder.rs:130-234): dense entries are f32 arrays, the six linears of
     each block ``(dtype, raw, n, k)``.  Weights ~ N(0, 0.02); Q5_1 and Q8_0
@@ -213,8 +295,10 @@ def encoder_tensors(n_mels: int, n_ctx: int, n_state: int, n_layer: int, dtype: 
     codes with block scales giving a similar spread (MODEL_CODE_SCALES);
     LayerNorm weights 1 + N(0, 0.02);
     positions are whisper's sinusoids.  With ``reuse_layers`` every block
-    gets block 0's values (each still becomes its own device copy; for
-    throughput runs of deep models, where drawing every layer is slow)."""
+    gets block 0's values (each still becomes its own device copy).
+    ``gen_device`` (e.g. "cuda"): the random-code linears are drawn there
+    by ``random_blocks_torch`` (the same bytes, much faster for deep
+    models) and returned as host arrays."""
     t = {}
     ctr = [seed * 1000]
 
@@ -228,6 +312,9 @@ def encoder_tensors(n_mels: int, n_ctx: int, n_state: int, n_layer: int, dtype: 
             return (dtype, quantize_q5_1(normal(ctr[0], n * k, 0.0, 0.02)), n, k)
         if dtype == Q8_0:
             return (dtype, quantize_q8_0(normal(ctr[0], n * k, 0.0, 0.02)), n, k)
+        if gen_device is not None:
+            raw = random_blocks_torch(dtype, n, k, ctr[0], *MODEL_CODE_SCALES[dtype], device=gen_device)
+            return (dtype, raw.cpu().numpy(), n, k)
         return (dtype, random_blocks(dtype, n, k, ctr[0], *MODEL_CODE_SCALES[dtype]), n, k)
 
     t["encoder.conv1.weight"] = nrm(n_state, n_mels, 3)
@@ -272,7 +359,7 @@ def encoder_mel(n_windows: int, n_mels: int, n_frames: int, seed: int) -> np.nda
 
 
 def decoder_tensors(n_vocab: int, n_ctx: int, n_state: int, n_layer: int, dtype: int, seed: int,
-                    reuse_layers: bool = False) -> dict:
+                    reuse_layers: bool = False, gen_device=None) -> dict:
     """Random-init whisper decoder tensors by their whisper.cpp names
     (decoder.rs:36-321), same conventions as :func:`encoder_tensors`; the
     token embedding (also the tied logits matrix) is quantized like the
@@ -290,6 +377,9 @@ def decoder_tensors(n_vocab: int, n_ctx: int, n_state: int, n_layer: int, dtype:
             return (dtype, quantize_q5_1(normal(ctr[0], n * k, 0.0, 0.02)), n, k)
         if dtype == Q8_0:
             return (dtype, quantize_q8_0(normal(ctr[0], n * k, 0.0, 0.02)), n, k)
+        if gen_device is not None:
+            raw = random_blocks_torch(dtype, n, k, ctr[0], *MODEL_CODE_SCALES[dtype], device=gen_device)
+            return (dtype, raw.cpu().numpy(), n, k)
         return (dtype, random_blocks(dtype, n, k, ctr[0], *MODEL_CODE_SCALES[dtype]), n, k)
 
     t["decoder.token_embedding.weight"] = lin(n_vocab, n_state)

@@ -69,6 +69,18 @@ def test_golden_fixture_on_gpu(rq, path):
     assert close(yf, fx["y_f32"]) < TOL
 
 
+def exact_int8(orc, a, dtype, raw, n):
+    """The reference's int8 formula sum_kb d_a*(d_b*S + m_b*sum(q_a))
+    (quant.rs:349-354, 452-454) evaluated in float64: the activations are
+    quantized by the oracle (bit-exact), the weights dequantized by it
+    (bit-exact f32 x = d*q + m), then one f64 product."""
+    m, k = a.shape
+    qa, da, _ = orc.quantize_acts_i8(a)
+    deq = qa.astype(np.float64).reshape(m, k // 32, 32) * da.astype(np.float64).reshape(m, k // 32, 1)
+    x = orc.to_dense(dtype, raw, n, k).astype(np.float64)
+    return deq.reshape(m, k) @ x.T
+
+
 def _case(dtype, m, k, n, seed):
     from rusty_whisper_b200 import synth
     a = synth.normal(seed, m * k).reshape(m, k)
@@ -392,3 +404,105 @@ def test_quantizer_unaligned_and_nan(rq, orc):
     assert np.array_equal(host(q), qr)
     assert np.array_equal(host(d).view(np.uint32), dr.view(np.uint32))
     assert np.array_equal(host(s), sr)
+
+
+@pytest.mark.parametrize("dtype", FORMATS)
+@pytest.mark.parametrize("m,k,n", [(257, 96, 41), (300, 768, 257), (640, 256, 64), (700, 1024, 130),
+                                   (1500, 768, 768), (1500, 3072, 768), (1100, 5120, 1280)])
+def test_hl_gemm_both_modes_match_oracle(rq, orc, dtype, m, k, n):
+    """The hi|lo tensor-core GEMM in both tiers (forced for int8, the f32
+    tier's kernel from 257 rows): int8 activation semantics against the
+    exact int8 sum and the oracle's dispatched tier, and dequant-then-f32
+    against the oracle's f32 `matmul_t(a, to_dense)` (quant.rs:1194), at
+    every K split (1, 2, 4), tile width (64, 128, 256) and ragged M / N
+    edge."""
+    a, raw = _case(dtype, m, k, n, 19 * dtype + m + k)
+    w = rq.QTensor([n, k], dtype, raw)
+    rq.set_gemm_path(4)
+    try:
+        y = host(rq.matmul_t_q(cuda(a), w))
+        rq.stream_check()
+    finally:
+        rq.set_gemm_path(0)
+    assert close(y, exact_int8(orc, a, dtype, raw, n)) < TOL
+    if k <= 4096:
+        # Beyond k = 4096 the reference's x86 tier itself drifts ~1e-3 from
+        # the exact block dots for the min formats (its per-block f32
+        # terms, quant.rs:452-454), so long rows are held to the exact sum.
+        assert close(y, orc.matmul_t_q(a, dtype, raw, n)) < TOL
+    yf = host(rq.matmul_t_q(cuda(a), w, mode="f32"))
+    rq.stream_check()
+    assert close(yf, orc.matmul_t(a, orc.to_dense(dtype, raw, n, k))) < TOL
+
+
+@pytest.mark.parametrize("path", [2, 3, 4])
+def test_gemm_paths_agree_with_oracle(rq, orc, path):
+    """Each tensor-core GEMM path, forced, on the config-2 shapes of one
+    format (Q5_1: scales and minimums on both sides)."""
+    from rusty_whisper_b200 import synth
+    rq.set_gemm_path(path)
+    try:
+        for (k, n) in synth.SWEEP_SHAPES:
+            raw = synth.sweep_weight(7, k, n)
+            w = rq.QTensor([n, k], 7, raw)
+            a = synth.sweep_acts(synth.ENCODER_M, k)
+            y = host(rq.matmul_t_q(cuda(a), w))
+            rq.stream_check()
+            assert close(y, orc.matmul_t_q(a, 7, raw, n)) < TOL, (path, k, n)
+    finally:
+        rq.set_gemm_path(0)
+
+
+def test_hl_gemm_row_scales_span_f32_range(rq, orc):
+    """Activation rows of magnitude 1e-30 .. 1e30 and rows of zeros: each
+    row is normalised by its own power of two before the f16 split."""
+    from rusty_whisper_b200 import synth
+    dtype, m, k, n = 6, 300, 256, 200
+    a, raw = _case(dtype, m, k, n, 91)
+    scales = np.array([1e-30, 1e-12, 1e-3, 1.0, 37.0, 1e6, 1e20, 1e30, 0.0], np.float32)
+    a = (a * scales[np.arange(m) % scales.size][:, None]).astype(np.float32)
+    w = rq.QTensor([n, k], dtype, raw)
+    rq.set_gemm_path(4)
+    try:
+        y = host(rq.matmul_t_q(cuda(a), w))
+    finally:
+        rq.set_gemm_path(0)
+    ref = orc.int8_scalar_matmul(a, dtype, raw, n)
+    # The 1e-3 rule relative to max(|ref|, 1) is not scale-free (vacuous for
+    # tiny rows, elementwise-relative for huge ones, where outputs near
+    # zero come from cancellation), so every row is held to 1e-3 of its own
+    # largest output instead.
+    for i in range(m):
+        s = max(float(np.abs(ref[i]).max()), 1e-37)
+        assert float(np.abs(y[i] - ref[i]).max()) <= 1e-3 * s, i
+    yf = host(rq.matmul_t_q(cuda(a), w, mode="f32"))
+    reff = orc.matmul_t(a, orc.to_dense(dtype, raw, n, k))
+    for i in range(m):
+        s = max(float(np.abs(reff[i]).max()), 1e-37)
+        assert float(np.abs(yf[i] - reff[i]).max()) <= 1e-3 * s, i
+
+
+def test_hl_gemm_unaligned_and_host_f32(rq, orc):
+    """Activations, bias and output at 4-byte offsets on the hi|lo GEMM, and
+    the f32 tier through the host-buffer entry point (chunked)."""
+    import torch
+    from rusty_whisper_b200 import synth
+    dtype, m, k, n = 3, 600, 384, 258
+    a, raw = _case(dtype, m, k, n, 5)
+    w = rq.QTensor([n, k], dtype, raw)
+    abuf = torch.zeros(m * k + 1, device="cuda")
+    abuf[1:] = torch.from_numpy(a.ravel()).cuda()
+    bias_buf = torch.from_numpy(synth.normal(9, n + 1)).cuda()
+    out_buf = torch.empty(m * n + 1, device="cuda")
+    out = out_buf[1:].view(m, n)
+    rq.set_gemm_path(4)
+    try:
+        rq.matmul_t_q(abuf[1:].view(m, k), w, out=out, bias=bias_buf[1:])
+    finally:
+        rq.set_gemm_path(0)
+    ref = orc.matmul_t_q(a, dtype, raw, n) + bias_buf[1:].cpu().numpy()[None, :]
+    assert close(host(out), ref) < TOL
+    yh = rq.matmul_t_q(a, w, mode="f32")           # host buffers, row chunks
+    yd = host(rq.matmul_t_q(cuda(a), w, mode="f32"))
+    assert np.array_equal(np.asarray(yh).view(np.uint32), yd.view(np.uint32))
+    assert close(yh, orc.matmul_t(a, orc.to_dense(dtype, raw, n, k))) < TOL
