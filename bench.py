@@ -403,32 +403,40 @@ LARGE_V3 = dict(n_mels=128, n_audio=1500, n_state=1280, n_head=20, enc_layers=32
 
 
 def run_decoder_beams(args, dev, hbm_peak, stream, rank, world):
-    """whisper-medium decoder, Q5_0, 16 windows x 5 beam
-    streams (80 streams; the five streams of a window share its cross K/V),
-    224 fixed steps after a 4-token seeded random prefix, cross-attention
-    over a 1500 x 1024 N(0, 1) encoder output per window.  Each stream is
-    fed its own greedy choice (the beam re-ranking itself is host policy,
-    not part of the step).  Tokens per second of all streams."""
+    """whisper-medium decoder, Q5_0, 16 windows, beam 5
+    (80 streams; the five beams of a window share its cross K/V), 224
+    fixed steps after a seeded random 4-token prompt per window,
+    cross-attention over a 1500 x 1024 N(0, 1) encoder output per window.
+    Every step is the reference's beam step (transcribe.rs:886-990) on the
+    device: the step with its stacked logits projection, log_softmax +
+    top-5 per beam, the per-window ranking of the 25 candidates and the
+    fork of the survivors' self-attention caches.  End-of-text and the
+    other special ids are never chosen, so every beam decodes all 224 steps
+    (the finished-hypothesis bookkeeping is host policy).  Tokens per
+    second of all beams."""
     import torch
     from rusty_whisper_b200 import decoder
     c = DEC_MEDIUM
     n_win, beams, steps, prefix = 16, 5, 224, 4
     S = n_win * beams
+    eot = 50257
     t = synth.decoder_tensors(c["n_vocab"], c["n_ctx"], c["n_state"], c["n_layer"], 6, seed=7, gen_device=dev)
     dec = decoder.Decoder(c["n_vocab"], c["n_ctx"], c["n_state"], c["n_head"], c["n_layer"], t)
     enc = torch.from_numpy(synth.normal(300 + rank, n_win * 1500 * c["n_state"]).reshape(n_win, 1500, c["n_state"]))
     enc = enc.to(dev)
     sw = [w for w in range(n_win) for _ in range(beams)]
-    pre = torch.from_numpy(synth.randint(400 + rank, prefix * S, 0, 50256).astype(np.int32).reshape(prefix, S))
-    pre = pre.to(dev)
+    pre_w = synth.randint(400 + rank, prefix * n_win, 0, 50256).astype(np.int32).reshape(prefix, n_win)
+    pre = torch.from_numpy(np.repeat(pre_w, beams, axis=1).copy()).to(dev)   # a window's beams share its prompt
+    search = decoder.BeamSearch(dec, n_win, beams, limit=eot)
 
     def run(n_steps):
         dec.begin(enc, sw)
+        search.live = 1
         for i in range(prefix - 1):
             dec.step(pre[i], want="none")
-        tok = dec.step(pre[prefix - 1], want="best")
-        for _ in range(n_steps - 1):
-            tok = dec.step(tok, want="best")
+        tok = pre[prefix - 1]
+        for _ in range(n_steps):
+            tok = search.step(tok)
         return tok
 
     run(8)
@@ -446,13 +454,15 @@ def run_decoder_beams(args, dev, hbm_peak, stream, rank, world):
     D, Lr = c["n_state"], c["n_layer"]
     cross_bytes = n_win * Lr * 2 * 1500 * D * 2.0
     res = {"workload": "BASELINE config 4: whisper-medium decoder (24 x d1024/16 heads/FFN 4096, vocab 51865), Q5_0, "
-                       f"{n_win} windows x {beams} beam streams, {steps} steps after a {prefix}-token prefix",
+                       f"{n_win} windows x beam {beams}, {steps} beam steps after a {prefix}-token prompt",
            "tokens_per_s": round(world * S * steps / tt, 1), "ms_per_step": round(tt / (steps + prefix) * 1e3, 3),
            "streams": S,
            "bytes_per_step": {"quantized_weights": round(sum(v[1].nbytes for v in t.values() if isinstance(v, tuple)) / 1e6, 1),
                               "cross_kv_f16_MB": round(cross_bytes / 1e6, 1)},
+           "beam": beams,
            "note": "linears on the tiled integer-MMA GEMV (k_gemv_tile: 80 streams as 32-row tiles, bit-identical "
-                   "to the per-stream GEMV); each stream takes its own greedy id; the step replays from a CUDA graph",
+                   "to the per-stream GEMV); the decoder step replays from a CUDA graph, then k_beam_topk, "
+                   "k_beam_select and k_self_fork (copies only the survivors not kept in their parent's slot)",
            "data": "synthetic (seeded): random-code Q5_0 weights (every block its own draw), encoder output N(0, 1)"}
     if rank == 0 and world == 1 and not args.no_cpu:
         import oracle

@@ -303,6 +303,56 @@ int rwq_decoder_begin(rwq_decoder* d, const float* enc_out, int64_t n_windows, i
  * With both NULL the projection is skipped (prompt positions).  A full
  * context (n_text_ctx positions) returns RWQ_ERR_ARG (decoder.rs:115-120). */
 int rwq_decoder_step(rwq_decoder* d, const int32_t* tokens, float* logits, int32_t* best, int32_t limit, void* stream);
+/* ---- Beam search on the device --------------------------------------
+ * The pieces of one step of the reference's beam search (decode_window_beam,
+ * transcribe.rs:835-1011), so a beam decode stays on the device between
+ * steps: the beams of a window are its streams, stored contiguously
+ * (stream w*B + b is beam b of window w: stream_window = [0]*B + [1]*B + ...
+ * at rwq_decoder_begin).  The host policy around them (timestamp rules,
+ * finished hypotheses, the final ranking) stays with the caller. */
+
+/* `forward_hidden` (decoder.rs:110-206) for every stream: one position,
+ * then the final layernorm; hidden [S][n_state] (device) receives the
+ * states, no projection. */
+int rwq_decoder_step_hidden(rwq_decoder* d, const int32_t* tokens, float* hidden, void* stream);
+
+/* `project_logits` (decoder.rs:315-321): logits[rows][n_vocab] =
+ * hidden[rows][n_state] . token_embedding^T as one stacked projection, as
+ * the reference projects all beams at once (transcribe.rs:970-977).
+ * rows <= the decoder's streams; device pointers, hidden 16-byte aligned.
+ * The same bits as the projection inside rwq_decoder_step. */
+int rwq_decoder_project(rwq_decoder* d, const float* hidden, int64_t rows, float* logits, void* stream);
+
+/* `Decoder::fork` for a whole beam step (decoder.rs:71-79): stream i's
+ * self-attention cache becomes stream src[i]'s (device array [S]).  Only
+ * entries with src[i] != i, src[i] in i's window and src[src[i]] ==
+ * src[i] (the source keeps its own history) are copied, in place; the
+ * others are ignored.  rwq_beam_select's src always qualifies. */
+int rwq_decoder_fork(rwq_decoder* d, const int32_t* src, void* stream);
+
+/* log_softmax (transcribe.rs:482-486) and top_k (:672-685) of each row of
+ * logits[rows][n_vocab] (device): ids >= limit are excluded like
+ * suppressed tokens (limit < 0: none), -inf logits are never chosen; lp
+ * [rows][k] descending with id [rows][k] (-1 / -inf past the choosable
+ * ids); 1 <= k <= 8.  Ties in value are ordered by id. */
+int rwq_beam_topk(const float* logits, int64_t rows, int64_t n_vocab, int32_t limit, int k, float* lp, int32_t* id,
+                  void* stream);
+
+/* The candidate ranking of one beam step for each of n_windows windows of
+ * `beams` streams (transcribe.rs:890-925): the live beams (rank[s] <
+ * n_live; rank NULL: slot order, used with n_live = 1 after the prompt)
+ * each offer their k candidates (lp, id from rwq_beam_topk) scored
+ * sum_lp[s] + max(lp, -30) (sum_lp NULL: 0); a stable sort by score in
+ * the reference's beam order keeps the best `beams`.  Per slot s of the
+ * window: src[s] the stream whose history it continues (for
+ * rwq_decoder_fork), token[s], sum_out[s], step_lp[s] = max(lp, -30),
+ * rank_out[s] its place in the ranking.  A survivor stays in its parent's
+ * slot if it is that parent's first survivor, so only the others are
+ * copied by rwq_decoder_fork.  All arrays device, [n_windows * beams]. */
+int rwq_beam_select(const float* lp, const int32_t* id, int k, const float* sum_lp, const int32_t* rank,
+                    int64_t n_windows, int beams, int n_live, int32_t* src, int32_t* token, float* sum_out,
+                    float* step_lp, int32_t* rank_out, void* stream);
+
 /* `Decoder::reset` (decoder.rs:83-91): positions restart at 0, cross K/V kept. */
 int rwq_decoder_reset(rwq_decoder* d);
 int rwq_decoder_n_past(const rwq_decoder* d, int64_t* n_past);

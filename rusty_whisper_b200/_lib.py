@@ -78,6 +78,11 @@ SIGNATURES = {
     "rwq_decoder_set_quant": (_I, [_P, ctypes.c_char_p, _I, _P, _SZ, _L, _L]),
     "rwq_decoder_begin": (_I, [_P, _P, _L, _L, _P, _L, _P]),
     "rwq_decoder_step": (_I, [_P, _P, _P, _P, ctypes.c_int32, _P]),
+    "rwq_decoder_step_hidden": (_I, [_P, _P, _P, _P]),
+    "rwq_decoder_project": (_I, [_P, _P, _L, _P, _P]),
+    "rwq_decoder_fork": (_I, [_P, _P, _P]),
+    "rwq_beam_topk": (_I, [_P, _L, _L, ctypes.c_int32, _I, _P, _P, _P]),
+    "rwq_beam_select": (_I, [_P, _P, _I, _P, _P, _L, _I, _I, _P, _P, _P, _P, _P, _P]),
     "rwq_decoder_reset": (_I, [_P]),
     "rwq_decoder_n_past": (_I, [_P, ctypes.POINTER(_L)]),
 }

@@ -103,6 +103,8 @@ struct rwq_decoder {
     unsigned* attn_cnt = nullptr;  // per (group, head) split counters, zero between launches
     float *x = nullptr, *tmp = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *att = nullptr, *h = nullptr,
           *logits = nullptr, *qkv = nullptr;
+    float* hid = nullptr;          // final-layernormed states of the last hidden step [S][D]
+    int32_t* win_dev = nullptr;    // stream -> window, on the device (fork checks)
     int32_t* best = nullptr;
     int* dpos = nullptr;           // the decode position, on the device
     int32_t* tok_in = nullptr;     // this step's tokens (graph input)
@@ -197,6 +199,8 @@ size_t layout_state(rwq_decoder* d, int S, int W, int n_audio, int n_groups, int
     d->qkv = reinterpret_cast<float*>(take(S * 3 * D * 4));
     d->h = reinterpret_cast<float*>(take(S * F * 4));
     d->logits = reinterpret_cast<float*>(take(S * size_t(d->n_vocab) * 4));
+    d->hid = reinterpret_cast<float*>(take(S * D * 4));
+    d->win_dev = reinterpret_cast<int32_t*>(take(size_t(S) * 4));
     d->best = reinterpret_cast<int32_t*>(take(size_t(S) * 4));
     d->dpos = reinterpret_cast<int*>(take(4));
     d->tok_in = reinterpret_cast<int32_t*>(take(size_t(S) * 4));
@@ -223,15 +227,16 @@ rwq::ActsView with_k(rwq::ActsView v, int k) {
     return v;
 }
 
-// Row transform + quantize into the layout the linears of this step read.
+// Row transform + quantize into the layout the linears of this step read
+// (quantize false: only the transformed rows into yout).
 int rows(rwq_decoder* d, int mode, const float* x, const float* add, float* xout, const float* w, const float* b, int k,
-         cudaStream_t s) {
+         cudaStream_t s, float* yout = nullptr, bool quantize = true) {
     const int S = d->n_streams;
     const bool gemm = S > rwq::GEMV_FAMILY_MAX_M;
     const rwq::ActsView a = with_k(gemm ? d->gemm : d->gemv, k);
-    DEC_CUDA(rwq::launch_rows_quant_v(mode, x, add, xout, w, b, S, k, gemm ? &a : nullptr, gemm ? nullptr : &a, nullptr,
-                                      s),
-             "decoder row transform");
+    const rwq::ActsView* ga = quantize && gemm ? &a : nullptr;
+    const rwq::ActsView* va = quantize && !gemm ? &a : nullptr;
+    DEC_CUDA(rwq::launch_rows_quant_v(mode, x, add, xout, w, b, S, k, ga, va, yout, s), "decoder row transform");
     return RWQ_OK;
 }
 
@@ -257,7 +262,8 @@ bool graphs_enabled() {
 
 // The kernels of one decode position (decoder.rs:102-206), reading the
 // tokens from d->tok_in and the position from d->dpos; mode bit 0: tied
-// logits into d->logits, bit 1: greedy choice into d->best.
+// logits into d->logits, bit 1: greedy choice into d->best, bit 2: the
+// final-layernormed states into d->hid (forward_hidden, decoder.rs:110).
 int issue_step(rwq_decoder* d, int mode, int32_t limit, cudaStream_t s) {
     const int S = d->n_streams, D = d->n_state, H = d->n_head, F = d->n_ff;
     DEC_CUDA(rwq::launch_embed(rwq::weight_of(d->emb), d->tok_in, S, d->dense["decoder.positional_embedding"], d->dpos,
@@ -321,9 +327,10 @@ int issue_step(rwq_decoder* d, int mode, int32_t limit, cudaStream_t s) {
     }
     if (mode) {
         // final LN (decoder.rs:200-204), tied logits (decoder.rs:315-321)
+        const bool proj = (mode & 3) != 0;
         DEC_RC(rows(d, d->n_layer ? rwq::RQ_ADD_LN : rwq::RQ_LN, d->x, d->tmp, d->x, d->dense["decoder.ln.weight"],
-                    d->dense["decoder.ln.bias"], D, s));
-        DEC_RC(linear(d, d->emb, nullptr, d->logits, s));
+                    d->dense["decoder.ln.bias"], D, s, (mode & 4) ? d->hid : nullptr, proj));
+        if (proj) DEC_RC(linear(d, d->emb, nullptr, d->logits, s));
         if (mode & 2) DEC_CUDA(rwq::launch_argmax(d->logits, S, d->n_vocab, limit, d->best, s), "argmax");
     }
     DEC_CUDA(rwq::launch_pos_advance(d->dpos, s), "position advance");
@@ -577,6 +584,7 @@ int rwq_decoder_begin(rwq_decoder* d, const float* enc_out, int64_t n_windows, i
     DEC_CUDA(cudaMemcpyAsync(d->cross_streams, gst.data(), gst.size() * 4, cudaMemcpyHostToDevice, s), "copy groups");
     DEC_CUDA(cudaMemcpyAsync(d->self_kv, sid.data(), sid.size() * 4, cudaMemcpyHostToDevice, s), "copy groups");
     DEC_CUDA(cudaMemcpyAsync(d->self_off, soff.data(), soff.size() * 4, cudaMemcpyHostToDevice, s), "copy groups");
+    DEC_CUDA(cudaMemcpyAsync(d->win_dev, win.data(), win.size() * 4, cudaMemcpyHostToDevice, s), "copy windows");
     // cross K/V (decoder.rs:41-56): quantize the encoder output once, then
     // two GEMMs per layer, windows in chunks to bound the scratch.
     const int per = std::max(1, int((size_t(1) << 30) / (size_t(T) * D * 14)));
@@ -616,8 +624,58 @@ int rwq_decoder_begin(rwq_decoder* d, const float* enc_out, int64_t n_windows, i
     return RWQ_OK;
 }
 
+namespace {
+int step_impl(rwq_decoder* d, const int32_t* tokens, float* logits, int32_t* best, int32_t limit, float* hidden,
+              void* stream);
+}
+
 int rwq_decoder_step(rwq_decoder* d, const int32_t* tokens, float* logits, int32_t* best, int32_t limit,
                      void* stream) {
+    return step_impl(d, tokens, logits, best, limit, nullptr, stream);
+}
+
+int rwq_decoder_step_hidden(rwq_decoder* d, const int32_t* tokens, float* hidden, void* stream) {
+    if (!hidden) return dfail(RWQ_ERR_ARG, "hidden is null");
+    return step_impl(d, tokens, nullptr, nullptr, -1, hidden, stream);
+}
+
+int rwq_decoder_project(rwq_decoder* d, const float* hidden, int64_t rows_n, float* logits, void* stream) {
+    if (!d) return dfail(RWQ_ERR_ARG, "decoder is null");
+    std::lock_guard<std::mutex> g(d->mu);
+    if (!d->n_streams) return dfail(RWQ_ERR_ARG, "rwq_decoder_begin was not called");
+    if (rows_n < 0 || rows_n > d->n_streams)
+        return dfail(RWQ_ERR_ARG, "project: %lld rows, at most the %d streams", (long long)rows_n, d->n_streams);
+    if (rows_n == 0) return RWQ_OK;
+    if (!hidden || !logits) return dfail(RWQ_ERR_ARG, "null hidden or logits");
+    if (reinterpret_cast<uintptr_t>(hidden) & 15) return dfail(RWQ_ERR_ARG, "hidden must be 16-byte aligned");
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const int R = int(rows_n), D = d->n_state;
+    // The step's own row kernel and linear, on R rows: the same bits as the
+    // projection inside rwq_decoder_step (the GEMV family's results do not
+    // depend on the row count).
+    const bool gemm = d->n_streams > rwq::GEMV_FAMILY_MAX_M;
+    rwq::ActsView a = with_k(gemm ? d->gemm : d->gemv, D);
+    a.m = R;
+    DEC_CUDA(rwq::launch_rows_quant_v(rwq::RQ_PLAIN, hidden, nullptr, nullptr, nullptr, nullptr, R, D,
+                                      gemm ? &a : nullptr, gemm ? nullptr : &a, nullptr, s),
+             "quantize hidden rows");
+    return rwq::linear_acts(a, gemm, d->emb, nullptr, logits, s);
+}
+
+int rwq_decoder_fork(rwq_decoder* d, const int32_t* src, void* stream) {
+    if (!d) return dfail(RWQ_ERR_ARG, "decoder is null");
+    if (!src) return dfail(RWQ_ERR_ARG, "src is null");
+    std::lock_guard<std::mutex> g(d->mu);
+    if (!d->n_streams) return dfail(RWQ_ERR_ARG, "rwq_decoder_begin was not called");
+    DEC_CUDA(rwq::launch_self_fork(src, d->win_dev, d->n_streams, d->n_head, d->n_ctx, d->n_layer, d->dpos,
+                                   d->self_k, d->self_v, static_cast<cudaStream_t>(stream)),
+             "fork");
+    return RWQ_OK;
+}
+
+namespace {
+int step_impl(rwq_decoder* d, const int32_t* tokens, float* logits, int32_t* best, int32_t limit, float* hidden,
+              void* stream) {
     if (!d) return dfail(RWQ_ERR_ARG, "decoder is null");
     if (!tokens) return dfail(RWQ_ERR_ARG, "tokens is null");
     std::lock_guard<std::mutex> g(d->mu);
@@ -629,7 +687,7 @@ int rwq_decoder_step(rwq_decoder* d, const int32_t* tokens, float* logits, int32
     const int S = d->n_streams;
     if (tokens != d->tok_in)
         DEC_CUDA(cudaMemcpyAsync(d->tok_in, tokens, size_t(S) * 4, cudaMemcpyDeviceToDevice, s), "copy tokens");
-    const int mode = (logits ? 1 : 0) | (best ? 2 : 0);
+    const int mode = (logits ? 1 : 0) | (best ? 2 : 0) | (hidden ? 4 : 0);
     DEC_CUDA(cudaEventRecord(d->ev_in, s), "cudaEventRecord");
     DEC_CUDA(cudaStreamWaitEvent(d->gs, d->ev_in, 0), "cudaStreamWaitEvent");
     DEC_RC(run_step(d, mode, limit, d->gs));
@@ -640,8 +698,12 @@ int rwq_decoder_step(rwq_decoder* d, const int32_t* tokens, float* logits, int32
         DEC_CUDA(cudaMemcpyAsync(logits, d->logits, size_t(S) * d->n_vocab * 4, cudaMemcpyDeviceToDevice, s),
                  "copy logits");
     if (best) DEC_CUDA(cudaMemcpyAsync(best, d->best, size_t(S) * 4, cudaMemcpyDeviceToDevice, s), "copy ids");
+    if (hidden && hidden != d->hid)
+        DEC_CUDA(cudaMemcpyAsync(hidden, d->hid, size_t(S) * d->n_state * 4, cudaMemcpyDeviceToDevice, s),
+                 "copy hidden");
     return RWQ_OK;
 }
+}  // namespace
 
 int rwq_decoder_reset(rwq_decoder* d) {
     if (!d) return dfail(RWQ_ERR_ARG, "decoder is null");

@@ -47,6 +47,12 @@ bool attn_dec_quantizes(int max_group);
 // else enough for one CTA per SM, at most 8 splits of at least 128 keys.
 int attn_dec_splits(int H, int n_groups, int max_group, int L, int sms);
 cudaError_t launch_argmax(const float* logits, int rows, int V, int limit, int32_t* best, cudaStream_t s);
+// Decoder::fork for a beam step (rwq_beam.cu): stream i's self-attention
+// cache [layer][S][H][ctx][64] (both K and V, positions 0 .. *dpos) takes
+// stream src[i]'s, for src[i] != i in the same window (win[]) whose own
+// src is itself; other entries are left alone.  Device arrays.
+cudaError_t launch_self_fork(const int32_t* src, const int32_t* win, int S, int H, int ctx, int n_layer,
+                             const int* dpos, __half* kc, __half* vc, cudaStream_t s);
 // x[i] = dequant(w row tokens[i]) + pos[*dpos] (bit-exact dequant,
 // quant.rs:528-537); pos is [ctx][k].
 cudaError_t launch_embed(const Weight& w, const int32_t* tokens, int n, const float* pos, const int* dpos, float* x,

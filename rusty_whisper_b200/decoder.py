@@ -5,9 +5,13 @@
     dec.begin(enc_out, stream_window)     # Decoder::new for every stream
     logits = dec.step(tokens)             # forward(&[token]) for every stream
     best = dec.step(tokens, want="best", limit=eot)   # greedy choice on the device
+    hidden = dec.step(tokens, want="hidden")          # forward_hidden
+    logits = dec.project(hidden)                      # project_logits, stacked
+    dec.fork(src)                          # Decoder::fork for a beam step
 
 Streams step in lockstep; streams that decode the same window (beams)
-share its cross-attention K/V.
+share its cross-attention K/V.  ``BeamSearch`` runs the reference's beam
+step (transcribe.rs:886-990) on the device.
 """
 from __future__ import annotations
 
@@ -70,7 +74,8 @@ class Decoder:
     def step(self, tokens, want: str = "logits", limit: int = -1, out=None):
         """tokens: one id per stream (CUDA int32 tensor, or a host sequence).
         want: "logits" -> [S, n_vocab] f32, "best" -> [S] int32 greedy ids,
-        "none" -> a prompt position, nothing projected."""
+        "hidden" -> [S, n_state] f32 final-layernormed states (no
+        projection), "none" -> a prompt position, nothing projected."""
         torch = _torch()
         if not torch.is_tensor(tokens) or not tokens.is_cuda:
             self._tok.copy_(torch.as_tensor(np.asarray(tokens, np.int32)))
@@ -78,6 +83,11 @@ class Decoder:
         S = self.n_streams
         dev = tokens.device
         lg = best = None
+        if want == "hidden":
+            hid = out if out is not None else torch.empty((S, self.shape[2]), device=dev, dtype=torch.float32)
+            _lib.check(_lib.lib().rwq_decoder_step_hidden(self._h, _ptr(tokens), _ptr(hid),
+                                                          ctypes.c_void_p(_stream_ptr(dev))))
+            return hid
         if want == "logits":
             lg = out if out is not None else torch.empty((S, self.shape[0]), device=dev, dtype=torch.float32)
         elif want == "best":
@@ -86,6 +96,26 @@ class Decoder:
                                                _ptr(best) if best is not None else None, limit,
                                                ctypes.c_void_p(_stream_ptr(dev))))
         return lg if want == "logits" else best
+
+    def project(self, hidden, out=None):
+        """project_logits (decoder.rs:315-321) of stacked hidden rows
+        [rows <= S, n_state] (CUDA f32) -> [rows, n_vocab]."""
+        torch = _torch()
+        hidden = hidden.contiguous()
+        rows = hidden.shape[0]
+        lg = out if out is not None else torch.empty((rows, self.shape[0]), device=hidden.device, dtype=torch.float32)
+        _lib.check(_lib.lib().rwq_decoder_project(self._h, _ptr(hidden), rows, _ptr(lg),
+                                                  ctypes.c_void_p(_stream_ptr(hidden.device))))
+        return lg
+
+    def fork(self, src) -> None:
+        """Decoder::fork for a beam step: stream i continues stream src[i]'s
+        history (CUDA int32 [S], same window; see rwq_decoder_fork)."""
+        torch = _torch()
+        if not torch.is_tensor(src) or not src.is_cuda:
+            src = torch.as_tensor(np.asarray(src, np.int32)).cuda(self.device)
+        src = src.contiguous()
+        _lib.check(_lib.lib().rwq_decoder_fork(self._h, _ptr(src), ctypes.c_void_p(_stream_ptr(src.device))))
 
     def reset(self) -> None:
         _lib.check(_lib.lib().rwq_decoder_reset(self._h))
@@ -106,3 +136,57 @@ class Decoder:
             self.free()
         except Exception:
             pass
+
+
+def beam_topk(logits, k: int, limit: int = -1):
+    """log_softmax + top_k of each row (transcribe.rs:482-486, 672-685) on
+    the device: (lp [rows, k] f32, id [rows, k] int32)."""
+    torch = _torch()
+    logits = logits.contiguous()
+    rows, V = logits.shape
+    lp = torch.empty((rows, k), device=logits.device, dtype=torch.float32)
+    ids = torch.empty((rows, k), device=logits.device, dtype=torch.int32)
+    _lib.check(_lib.lib().rwq_beam_topk(_ptr(logits), rows, V, limit, k, _ptr(lp), _ptr(ids),
+                                        ctypes.c_void_p(_stream_ptr(logits.device))))
+    return lp, ids
+
+
+class BeamSearch:
+    """The reference's beam step (transcribe.rs:886-990) for W windows of B
+    beams on one Decoder, all on the device: per step the stacked logits of
+    every beam, top-k per beam, the per-window ranking of the candidates
+    (rwq_beam_select) and the cache fork, with no host round trip.  Ids
+    >= ``limit`` are never chosen (``limit`` = end-of-text keeps every beam
+    decoding; the finished-hypothesis bookkeeping is the caller's)."""
+
+    def __init__(self, dec: Decoder, n_windows: int, beams: int, limit: int = -1):
+        torch = _torch()
+        self.dec, self.W, self.B, self.limit = dec, n_windows, beams, limit
+        S = n_windows * beams
+        dev = torch.device("cuda", dec.device)
+        z = lambda dt: torch.zeros(S, device=dev, dtype=dt)   # noqa: E731
+        self.sum, self.rank = z(torch.float32), z(torch.int32)
+        self.src, self.tok, self.step_lp = z(torch.int32), z(torch.int32), z(torch.float32)
+        self.sum_next, self.rank_next = z(torch.float32), z(torch.int32)
+        self.lp = torch.empty((S, beams), device=dev, dtype=torch.float32)
+        self.ids = torch.empty((S, beams), device=dev, dtype=torch.int32)
+        self.logits = torch.empty((S, dec.shape[0]), device=dev, dtype=torch.float32)
+        self.live = 1
+
+    def step(self, tokens):
+        """Feed `tokens` (one per stream), rank, fork; returns the next
+        tokens (CUDA int32 [S]), also in ``self.tok``."""
+        L = _lib.lib()
+        st = ctypes.c_void_p(_stream_ptr(self.logits.device))
+        self.dec.step(tokens, want="logits", out=self.logits)
+        _lib.check(L.rwq_beam_topk(_ptr(self.logits), self.logits.shape[0], self.logits.shape[1], self.limit, self.B,
+                                   _ptr(self.lp), _ptr(self.ids), st))
+        first = self.live == 1
+        _lib.check(L.rwq_beam_select(_ptr(self.lp), _ptr(self.ids), self.B, None if first else _ptr(self.sum),
+                                     None if first else _ptr(self.rank), self.W, self.B, self.live, _ptr(self.src),
+                                     _ptr(self.tok), _ptr(self.sum_next), _ptr(self.step_lp), _ptr(self.rank_next), st))
+        self.dec.fork(self.src)
+        self.sum, self.sum_next = self.sum_next, self.sum
+        self.rank, self.rank_next = self.rank_next, self.rank
+        self.live = self.B
+        return self.tok
