@@ -379,7 +379,8 @@ def run_encoder(args, dev, tc_peak, stream, rank, world):
            "gflop_per_window": {"quant_linear": round(lin / 1e9, 2), "attention": round(att / 1e9, 2),
                                 "conv": round(conv / 1e9, 2)},
            "achieved_TFLOPs": round(fl / tb / 1e12, 1), "frac_of_measured_bf16": round(fl / tb / 1e12 / tc_peak, 4),
-           "kernels": "k_rows_quant, k_gemm_fold, k_to_heads, k_attn, cuBLAS SGEMM + k_im2col3/k_bias_gelu (conv)",
+           "kernels": "k_rows_quant, k_gemm_fold, k_to_heads, k_attn; conv stem: k_im2col_split + k_gemm_hl (f16 hi|lo "
+                      "tensor cores) + k_bias_gelu",
            "gpu_launches_per_batch": 4 + 6 * 13 + 1,
            "data": "synthetic (seeded): random-init weights N(0, 0.02) quantized to Q5_1, mel N(-0.5, 0.3)"}
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -483,17 +484,20 @@ def run_decoder_beams(args, dev, hbm_peak, stream, rank, world):
 
 def run_large_v3(args, dev, stream, rank, world):
     """large-v3-shaped end to end, Q4_0: 256 windows of 30 s
-    synthetic audio sharded evenly over the ranks; per rank, host audio ->
-    log-mel (128 mels) -> encoder (32 blocks, d1280) -> decoder (32 blocks,
-    vocab 51866) greedy for 224 tokens after the 4-token start sequence ->
-    token ids back on the host.  Audio-seconds per second of all ranks (time:
-    max over ranks)."""
+    synthetic audio sharded evenly over the ranks through shard.run_sharded
+    (the reference's transcribe_parallel + merge_parallel_results,
+    transcribe.rs:1528-1586); per rank, host audio -> log-mel (128 mels) ->
+    encoder (32 blocks, d1280) -> decoder (32 blocks, vocab 51866) greedy for
+    224 tokens after the 4-token start sequence -> token ids back on the
+    host, then every window's tokens gathered on rank 0 in window order.
+    Audio-seconds per second of all ranks (device time, max over ranks)."""
     import torch
     import torch.distributed as dist
-    from rusty_whisper_b200 import audio, decoder, encoder
+    from rusty_whisper_b200 import audio, decoder, encoder, shard
     c = LARGE_V3
     total_win, steps = 256, 224
-    n_win = total_win // world
+    share = list(shard.window_range(total_win, world, rank))
+    n_win = len(share)
     te = synth.encoder_tensors(c["n_mels"], c["n_audio"], c["n_state"], c["enc_layers"], 2, seed=11, gen_device=dev)
     td = synth.decoder_tensors(c["n_vocab"], c["n_ctx"], c["n_state"], c["dec_layers"], 2, seed=12, gen_device=dev)
     enc = encoder.Encoder(c["n_mels"], c["n_audio"], c["n_state"], c["n_head"], c["enc_layers"], te)
@@ -501,7 +505,7 @@ def run_large_v3(args, dev, stream, rank, world):
     del te, td
     mel_plan = audio.LogMel(audio.mel_filterbank(c["n_mels"]), c["n_mels"])
     distinct = [synth.speechlike_window(900 + 13 * i) for i in range(8)]
-    host = torch.from_numpy(np.stack([distinct[(rank * n_win + i) % 8] for i in range(n_win)])).pin_memory()
+    host = torch.from_numpy(np.stack([distinct[i % 8] for i in share])).pin_memory()
     toks_host = torch.empty((steps, n_win), dtype=torch.int32).pin_memory()
     sot = torch.tensor([50258, 50259, 50360, 50364], dtype=torch.int32)     # sot, lang, transcribe, notimestamps
     prompt = sot.repeat(n_win, 1).t().contiguous().to(dev)
@@ -535,18 +539,28 @@ def run_large_v3(args, dev, stream, rank, world):
     torch.cuda.synchronize()
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    pipeline(steps)
-    e1.record(stream)
-    torch.cuda.synchronize()
+
+    def run_share(batch):
+        assert list(batch) == share
+        e0.record(stream)
+        pipeline(steps)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        return [toks_host[:, j].clone() for j in range(n_win)]
+
+    w0 = time.perf_counter()
+    gathered = shard.run_sharded(list(range(total_win)), run_share, timeout_s=300.0)
+    wall = time.perf_counter() - w0
     from rusty_whisper_b200 import quant
     quant.stream_check()
+    if rank == 0:
+        assert len(gathered) == total_win and all(g.shape == (steps,) for g in gathered)
     tt = e0.elapsed_time(e1) / 1e3
     tmax = tt
     if world > 1:
-        tm = torch.tensor([tt], dtype=torch.float64, device=dev)
+        tm = torch.tensor([tt, wall], dtype=torch.float64, device=dev)
         dist.all_reduce(tm, op=dist.ReduceOp.MAX)
-        tmax = float(tm.item())
+        tmax, wall = float(tm[0].item()), float(tm[1].item())
     stages = {"audio_mel_encoder_s": round(e0.elapsed_time(marks["enc"]) / 1e3, 3),
               "cross_kv_s": round(marks["enc"].elapsed_time(marks["begin"]) / 1e3, 3),
               "decode_s": round(marks["begin"].elapsed_time(e1) / 1e3, 3)}
@@ -556,7 +570,10 @@ def run_large_v3(args, dev, stream, rank, world):
            "rank0_stages": stages, "ms_per_decode_step": round(stages["decode_s"] / (steps + 4) * 1e3, 3),
            "windows_per_rank": n_win, "scaling": "strong (256 windows in total)",
            "h2d_bytes_per_rank": int(host.numel() * 4), "d2h_bytes_per_rank": int(steps * n_win * 4),
-           "timing": "CUDA events around host audio -> tokens on the host, max over ranks",
+           "timing": "CUDA events around host audio -> tokens on the host, max over ranks; the host gather of "
+                     "every window's tokens on rank 0 (shard.run_sharded) follows it",
+           "gather": {"windows_on_rank0": total_win if rank == 0 else None,
+                      "wall_s_incl_gather": round(wall, 3)},
            "data": "synthetic (seeded): band-limited noise at -20 dBFS with 0.2-2 s silences; random-code Q4_0 "
                    "weights (every block its own draw)"}
     if rank == 0 and world == 1 and not args.no_cpu:

@@ -266,6 +266,19 @@ int rwq_encoder_encode_dev(rwq_encoder* e, const float* mel, int64_t n_windows, 
 /* Host buffers (copies inside, synchronous). */
 int rwq_encoder_encode(rwq_encoder* e, const float* mel, int64_t n_windows, float* out);
 
+/* `conv1d` with kernel 3 and padding 1 (tensor.rs:335-370, the encoder's
+ * stem, encoder.rs:196-210) on the tensor cores: x [n_win][in_ch][t_in]
+ * (each window channel-major, as the reference's input), w
+ * [out_ch][in_ch][3], bias [out_ch] (may be NULL), stride 1 or 2; out
+ * [n_win][t_out][out_ch], t_out = (t_in - 1) / stride + 1, is the
+ * reference's [out_ch][t_out] result transposed to time-major (the layout
+ * the encoder continues in, encoder.rs:215-220).  Both operands are split
+ * into f16 hi + lo (about 22 significant bits each), so the sums match an
+ * f32 conv to ~1e-6 of their scale.  Device buffers; scratch from this
+ * stream's workspace. */
+int rwq_conv1d_dev(const float* x, int64_t n_win, int64_t in_ch, int64_t t_in, const float* w, int64_t out_ch,
+                   const float* bias, int stride, float* out, void* stream);
+
 /* Non-causal multi-head attention over projected q, k, v
  * [n_windows][t][n_state] (`multi_head_attention`, src/encoder.rs:107-121,
  * with `mha_split_kv` :48-80): softmax(q k^T / 8) v per head of 64, on f16

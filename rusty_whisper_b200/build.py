@@ -60,7 +60,7 @@ def build(verbose: bool = False, force: bool = False) -> str:
         if p.wait() != 0:
             raise RuntimeError(f"nvcc failed on {src}")
     tmp = LIB + ".tmp"
-    cmd = [NVCC, "-gencode", "arch=compute_100a,code=sm_100a", "-shared", "-o", tmp, *objs, "-lcublas"]
+    cmd = [NVCC, "-gencode", "arch=compute_100a,code=sm_100a", "-shared", "-o", tmp, *objs]
     if verbose:
         print(" ".join(cmd), flush=True)
     subprocess.check_call(cmd)

@@ -4,8 +4,12 @@
 // linear on the quantized tensor-core GEMM.
 //
 // Per batch of W windows (T = n_ctx frames each, M = W*T rows):
-//   conv stem   im2col + cuBLAS SGEMM (dense f32 weights, as the reference
-//               keeps them) + bias/GELU (+ positions) epilogue kernel;
+//   conv stem   the conv weights stay dense f32, as the reference keeps
+//               them (model.rs:231-257); each conv1d (tensor.rs:335-370)
+//               is an im2col GEMM on the tensor cores with both operands
+//               split into f16 hi + lo (k_im2col_split, k_gemm_hl: about
+//               22 significant bits per operand, the accuracy of f32 for
+//               these sums) + bias/GELU (+ positions) epilogue kernel;
 //   per block   [residual add +] LayerNorm + int8 quantize (one kernel)
 //               -> Q, K, V GEMMs sharing the quantized activations
 //               -> f16 heads -> flash attention -> quantize -> out GEMM
@@ -13,7 +17,6 @@
 //               -> GELU + quantize -> fc2 GEMM;
 //   ln_post     fused with the last residual add.
 // The activations stay in HBM between kernels; nothing returns to the host.
-#include <cublas_v2.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <cmath>
@@ -69,7 +72,11 @@ struct rwq_encoder {
     std::map<std::string, float*> dense;       // device copies, by whisper.cpp name
     std::map<std::string, size_t> dense_len;   // expected element counts
     std::vector<Layer> layers;
-    cublasHandle_t blas = nullptr;
+    // conv weights as hi|lo GEMM operands [D][kp/32][64] + column scales,
+    // built from the dense tensors at the first encode after they are set
+    uint16_t *conv1_hl = nullptr, *conv2_hl = nullptr;
+    float *conv1_cs = nullptr, *conv2_cs = nullptr;
+    bool stem_ready = false;
     void* ws = nullptr;                        // batch workspace (grown on demand)
     size_t ws_bytes = 0;
     std::mutex mu;
@@ -122,10 +129,15 @@ rwq_qtensor** quant_slot(rwq_encoder* e, const std::string& name, int64_t* want_
 }
 
 struct Bufs {
-    float *x, *tmp, *q, *k, *v, *h, *att, *a1, *c1, *a2;
+    float *x, *tmp, *q, *k, *v, *h, *att, *c1;
+    uint16_t *a1, *a2;    // conv1 / conv2 im2col rows as hi|lo operands
+    float *rs1, *rs2;     // their row scales
     __half *qh, *kh, *vh;
     rwq::ActsView acts;   // GEMM layout, k up to n_ff
 };
+
+// Columns of conv1's im2col rows: 3 * n_mels rounded up to a 32-block.
+int conv1_kp(const rwq_encoder* e) { return (3 * e->n_mels + 31) / 32 * 32; }
 
 size_t carve(const rwq_encoder* e, int nwin, uint8_t* base, Bufs* b) {
     const size_t T = size_t(e->n_ctx), D = size_t(e->n_state), F = size_t(e->n_ff), M = size_t(nwin) * T;
@@ -144,9 +156,11 @@ size_t carve(const rwq_encoder* e, int nwin, uint8_t* base, Bufs* b) {
     z.v = reinterpret_cast<float*>(take(M * D * 4));
     z.h = reinterpret_cast<float*>(take(M * F * 4));
     z.att = reinterpret_cast<float*>(take(M * D * 4));
-    z.a1 = reinterpret_cast<float*>(take(2 * M * size_t(e->n_mels) * 3 * 4));
+    z.a1 = reinterpret_cast<uint16_t*>(take(2 * M * size_t(conv1_kp(e)) * 4));
+    z.rs1 = reinterpret_cast<float*>(take(2 * M * 4));
     z.c1 = reinterpret_cast<float*>(take(2 * M * D * 4));
-    z.a2 = reinterpret_cast<float*>(take(M * D * 3 * 4));
+    z.a2 = reinterpret_cast<uint16_t*>(take(M * D * 3 * 4));
+    z.rs2 = reinterpret_cast<float*>(take(M * 4));
     z.qh = reinterpret_cast<__half*>(take(M * D * 2));
     z.kh = reinterpret_cast<__half*>(take(M * D * 2));
     z.vh = reinterpret_cast<__half*>(take(M * D * 2));
@@ -177,26 +191,45 @@ rwq::ActsView acts_for(const Bufs& b, int k) {
     return v;
 }
 
+// The conv weights as hi|lo GEMM operands (once per set of weights).
+int ensure_stem(rwq_encoder* e, cudaStream_t s) {
+    if (e->stem_ready) return RWQ_OK;
+    const int D = e->n_state, NM = e->n_mels, k1 = conv1_kp(e);
+    const int n_pad = (D + 255) / 256 * 256;
+    if (!e->conv1_hl) {
+        ENC_CUDA(cudaMalloc(&e->conv1_hl, size_t(D) * k1 * 4), "cudaMalloc(conv1 operand)");
+        ENC_CUDA(cudaMalloc(&e->conv2_hl, size_t(D) * 3 * D * 4), "cudaMalloc(conv2 operand)");
+        ENC_CUDA(cudaMalloc(&e->conv1_cs, size_t(n_pad) * 4), "cudaMalloc(conv1 scales)");
+        ENC_CUDA(cudaMalloc(&e->conv2_cs, size_t(n_pad) * 4), "cudaMalloc(conv2 scales)");
+    }
+    // weight [D][in][3]: row j's column c*3 + kk is the im2col column order
+    ENC_CUDA(rwq::launch_split_dense(e->dense["encoder.conv1.weight"], D, k1, 3 * NM, 3 * NM, n_pad, e->conv1_hl,
+                                     e->conv1_cs, s),
+             "split conv1 weights");
+    ENC_CUDA(rwq::launch_split_dense(e->dense["encoder.conv2.weight"], D, 3 * D, 3 * D, 3 * D, n_pad, e->conv2_hl,
+                                     e->conv2_cs, s),
+             "split conv2 weights");
+    e->stem_ready = true;
+    return RWQ_OK;
+}
+
 // The forward for `nwin` windows (mel [nwin][n_mels][2*n_ctx] on the device).
 int encode_batch(rwq_encoder* e, const Bufs& b, const float* mel, int nwin, float* out, cudaStream_t s) {
     const int T = e->n_ctx, D = e->n_state, F = e->n_ff, H = e->n_head, NM = e->n_mels;
-    const int M = nwin * T, M2 = 2 * M, m_pad = b.acts.m_pad;
+    const int M = nwin * T, M2 = 2 * M, m_pad = b.acts.m_pad, k1 = conv1_kp(e);
     auto W = [&](const std::string& n) { return e->dense[n]; };
-    const float one = 1.f, zero = 0.f;
+    ENC_RC(ensure_stem(e, s));
     // conv1 (stride 1) + GELU: [2T][n_mels*3] x [D][n_mels*3]^T per window
-    ENC_CUDA(rwq::launch_im2col3(mel, nwin, NM, 2 * T, 2 * T, 1, size_t(NM) * 2 * T, size_t(2 * T), 1, b.a1, s),
+    ENC_CUDA(rwq::launch_im2col_split(mel, nwin, NM, 2 * T, 2 * T, 1, size_t(NM) * 2 * T, size_t(2 * T), 1, k1, b.a1,
+                                      b.rs1, s),
              "im2col conv1");
-    if (cublasSetStream(e->blas, s) != CUBLAS_STATUS_SUCCESS) return efail(RWQ_ERR_CUDA, "cublasSetStream");
-    if (cublasSgemm(e->blas, CUBLAS_OP_T, CUBLAS_OP_N, D, M2, NM * 3, &one, W("encoder.conv1.weight"), NM * 3, b.a1,
-                    NM * 3, &zero, b.c1, D) != CUBLAS_STATUS_SUCCESS)
-        return efail(RWQ_ERR_CUDA, "cublasSgemm conv1");
+    ENC_RC(rwq::gemm_hl(b.a1, b.rs1, M2, e->conv1_hl, e->conv1_cs, D, k1 / rwq::QK, nullptr, b.c1, s));
     ENC_CUDA(rwq::launch_bias_gelu(b.c1, size_t(M2), D, W("encoder.conv1.bias"), nullptr, 1, s), "conv1 gelu");
     // conv2 (stride 2) + GELU + positions, written time-major: x [M][D]
-    ENC_CUDA(rwq::launch_im2col3(b.c1, nwin, D, 2 * T, T, 2, size_t(2 * T) * D, 1, size_t(D), b.a2, s),
+    ENC_CUDA(rwq::launch_im2col_split(b.c1, nwin, D, 2 * T, T, 2, size_t(2 * T) * D, 1, size_t(D), 3 * D, b.a2, b.rs2,
+                                      s),
              "im2col conv2");
-    if (cublasSgemm(e->blas, CUBLAS_OP_T, CUBLAS_OP_N, D, M, D * 3, &one, W("encoder.conv2.weight"), D * 3, b.a2,
-                    D * 3, &zero, b.x, D) != CUBLAS_STATUS_SUCCESS)
-        return efail(RWQ_ERR_CUDA, "cublasSgemm conv2");
+    ENC_RC(rwq::gemm_hl(b.a2, b.rs2, M, e->conv2_hl, e->conv2_cs, D, 3 * D / rwq::QK, nullptr, b.x, s));
     ENC_CUDA(rwq::launch_bias_gelu(b.x, size_t(M), D, W("encoder.conv2.bias"), W("encoder.positional_embedding"), T,
                                    s),
              "conv2 gelu");
@@ -266,10 +299,6 @@ int rwq_encoder_new(int n_mels, int n_ctx, int n_state, int n_head, int n_layer,
     e->n_ff = 4 * n_state;
     e->layers.resize(size_t(n_layer));
     expected_dense(e);
-    if (cublasCreate(&e->blas) != CUBLAS_STATUS_SUCCESS) {
-        delete e;
-        return efail(RWQ_ERR_CUDA, "cublasCreate failed");
-    }
     *out = e;
     return RWQ_OK;
 }
@@ -283,7 +312,9 @@ int rwq_encoder_free(rwq_encoder* e) {
     for (auto& L : e->layers)
         for (rwq_qtensor* t : {L.q, L.k, L.v, L.o, L.fc1, L.fc2}) rwq_qtensor_free(t);
     cudaFree(e->ws);
-    if (e->blas) cublasDestroy(e->blas);
+    for (void* p : {static_cast<void*>(e->conv1_hl), static_cast<void*>(e->conv2_hl), static_cast<void*>(e->conv1_cs),
+                    static_cast<void*>(e->conv2_cs)})
+        cudaFree(p);
     if (prev != e->device) cudaSetDevice(prev);
     delete e;
     return RWQ_OK;
@@ -299,7 +330,37 @@ int rwq_encoder_set_dense(rwq_encoder* e, const char* name, const float* data, i
     float*& dst = e->dense[name];
     if (!dst) ENC_CUDA(cudaMalloc(&dst, it->second * 4), "cudaMalloc(dense tensor)");
     ENC_CUDA(cudaMemcpy(dst, data, it->second * 4, cudaMemcpyHostToDevice), "copy dense tensor");
+    if (std::strncmp(name, "encoder.conv", 12) == 0) e->stem_ready = false;   // re-split at the next encode
     return RWQ_OK;
+}
+
+int rwq_conv1d_dev(const float* x, int64_t n_win, int64_t in_ch, int64_t t_in, const float* w, int64_t out_ch,
+                   const float* bias, int stride, float* out, void* stream) {
+    if (n_win < 0 || in_ch <= 0 || t_in <= 0 || out_ch <= 0 || (stride != 1 && stride != 2))
+        return efail(RWQ_ERR_ARG, "conv1d: bad shape (windows %lld, in %lld, t %lld, out %lld, stride %d)",
+                     (long long)n_win, (long long)in_ch, (long long)t_in, (long long)out_ch, stride);
+    if (in_ch > (1 << 20) || out_ch > (1 << 20) || t_in > (1 << 24)) return efail(RWQ_ERR_ARG, "conv1d: too large");
+    if (n_win == 0) return RWQ_OK;
+    if (!x || !w || !out) return efail(RWQ_ERR_ARG, "conv1d: null pointer");
+    const int64_t t_out = (t_in - 1) / stride + 1, rows = n_win * t_out;
+    if (rows > INT32_MAX) return efail(RWQ_ERR_ARG, "conv1d: too many output rows");
+    const int kp = int((3 * in_ch + 31) / 32 * 32), n_pad = int((out_ch + 255) / 256 * 256);
+    const size_t a_b = align_up(size_t(rows) * kp * 4, 256), r_b = align_up(size_t(rows) * 4, 256),
+                 b_b = align_up(size_t(out_ch) * kp * 4, 256), c_b = align_up(size_t(n_pad) * 4, 256);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    return rwq::with_stream_scratch(s, a_b + r_b + b_b + c_b, [&](void* buf) {
+        uint8_t* p = static_cast<uint8_t*>(buf);
+        uint16_t* ahl = reinterpret_cast<uint16_t*>(p);
+        float* rs = reinterpret_cast<float*>(p + a_b);
+        uint16_t* bhl = reinterpret_cast<uint16_t*>(p + a_b + r_b);
+        float* cs = reinterpret_cast<float*>(p + a_b + r_b + b_b);
+        ENC_CUDA(rwq::launch_split_dense(w, int(out_ch), kp, int(3 * in_ch), int(3 * in_ch), n_pad, bhl, cs, s),
+                 "split conv weights");
+        ENC_CUDA(rwq::launch_im2col_split(x, int(n_win), int(in_ch), int(t_in), int(t_out), stride,
+                                          size_t(in_ch) * t_in, size_t(t_in), 1, kp, ahl, rs, s),
+                 "im2col");
+        return rwq::gemm_hl(ahl, rs, int(rows), bhl, cs, int(out_ch), kp / rwq::QK, bias, out, s);
+    });
 }
 
 int rwq_encoder_set_quant(rwq_encoder* e, const char* name, int dtype, const uint8_t* raw, size_t raw_len, int64_t n,

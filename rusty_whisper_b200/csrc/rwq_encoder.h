@@ -24,8 +24,6 @@ cudaError_t launch_rows_quant(int mode, const float* x, const float* add, float*
 cudaError_t launch_rows_quant_v(int mode, const float* x, const float* add, float* xout, const float* lw,
                                 const float* lb, int m, int k, const ActsView* gemm, const ActsView* gemv,
                                 float* yout, cudaStream_t s);
-cudaError_t launch_im2col3(const float* in, int n_win, int c_in, int t_in, int t_out, int stride, size_t sw,
-                           size_t sc, size_t st, float* out, cudaStream_t s);
 cudaError_t launch_bias_gelu(float* y, size_t rows, int cols, const float* bias, const float* pos, int t_per_win,
                              cudaStream_t s);
 cudaError_t launch_to_heads(const float* src, int ld, int col0, int n_win, int T, int H, float scale, __half* dst,
@@ -41,6 +39,12 @@ int gemm_quantized(const ActsView& v, rwq_qtensor* w, const float* bias, float* 
 // Same on either layout: `gemm` false reads the GEMV layout (q8, d, sum, u;
 // integer-MMA GEMV in chunks of 8 rows), true the GEMM layout.
 int linear_acts(const ActsView& v, bool gemm, rwq_qtensor* w, const float* bias, float* out, cudaStream_t s);
+
+// k_gemm_hl on prepared hi|lo operands (launch_split_rows /
+// launch_im2col_split for A, launch_split_dense for a dense B), with this
+// stream's fault flag.  Returns an RWQ_* status.
+int gemm_hl(const uint16_t* ahl, const float* rowscale, int m, const uint16_t* bhl, const float* colscale, int n,
+            int nb, const float* bias, float* out, cudaStream_t s);
 
 // The GEMM kernel path that GEMM-sized matmuls take on this host thread
 // (2 folded-scale, 3 exact-integer, 4 hi|lo; rwq_set_gemm_path), which

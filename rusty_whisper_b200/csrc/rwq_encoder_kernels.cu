@@ -4,7 +4,7 @@
 //     (tensor.rs:274-289) or tanh-GELU (tensor.rs:291-306), then the int8
 //     activation quantizer (quant.rs:690-716) writing the tensor-core
 //     GEMM's operand directly (f16 codes + transposed block scales);
-//   * the conv stem as im2col + GEMM with a bias/GELU/position epilogue;
+//   * the conv stem's bias/GELU/position epilogue (its GEMMs are k_gemm_hl);
 //   * k_to_heads + k_attn: non-causal multi-head attention
 //     (encoder.rs:48-80) as a flash-style kernel on f16 tensor-core MMAs
 //     with f32 accumulation and an online softmax, so the [T, T] score
@@ -209,19 +209,6 @@ __global__ void __launch_bounds__(256) k_rows_quant(const float* x, const float*
 // im2col for a kernel-3, pad-1 conv over windows: out row (w, t) holds
 // in(w, ic, t*stride + j - 1) at column ic*3 + j (zero outside [0, t_in)).
 // in(w, ic, t) = in[w*sw + ic*sc + t*st].
-__global__ void k_im2col3(const float* __restrict__ in, int n_win, int c_in, int t_in, int t_out, int stride,
-                          size_t sw, size_t sc, size_t st, float* __restrict__ out) {
-    const size_t kcols = size_t(c_in) * 3;
-    const size_t total = size_t(n_win) * t_out * kcols;
-    for (size_t i = size_t(blockIdx.x) * blockDim.x + threadIdx.x; i < total; i += size_t(gridDim.x) * blockDim.x) {
-        const size_t col = i % kcols, r = i / kcols;
-        const int t = int(r % t_out), w = int(r / t_out);
-        const int ic = int(col / 3), j = int(col % 3);
-        const int ti = t * stride + j - 1;
-        out[i] = (ti >= 0 && ti < t_in) ? in[size_t(w) * sw + size_t(ic) * sc + size_t(ti) * st] : 0.f;
-    }
-}
-
 // y[r][c] = gelu(y[r][c] + bias[c]) (+ pos[(r % t_per_win)][c] if pos).
 __global__ void k_bias_gelu(float* __restrict__ y, size_t rows, int cols, const float* __restrict__ bias,
                             const float* __restrict__ pos, int t_per_win) {
@@ -498,14 +485,6 @@ cudaError_t launch_rows_quant_v(int mode, const float* x, const float* add, floa
         case RQ_ADD_LN: return rows_quant_mode<RQ_ADD_LN>(x, add, xout, lw, lb, m, k, o, yout, s);
         default: return cudaErrorInvalidValue;
     }
-}
-
-cudaError_t launch_im2col3(const float* in, int n_win, int c_in, int t_in, int t_out, int stride, size_t sw,
-                           size_t sc, size_t st, float* out, cudaStream_t s) {
-    const size_t total = size_t(n_win) * t_out * c_in * 3;
-    if (!total) return cudaSuccess;
-    k_im2col3<<<grid_stride(total, 256), 256, 0, s>>>(in, n_win, c_in, t_in, t_out, stride, sw, sc, st, out);
-    return cudaGetLastError();
 }
 
 cudaError_t launch_bias_gelu(float* y, size_t rows, int cols, const float* bias, const float* pos, int t_per_win,

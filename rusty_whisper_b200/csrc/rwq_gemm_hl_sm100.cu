@@ -401,11 +401,62 @@ __global__ void __launch_bounds__(128) k_split_rows(const float* __restrict__ a,
     if (threadIdx.x == 0) rowscale[row] = ldexpf(1.0f, -ex);
 }
 
-// Dense f32 weight rows [n][ldw] (first k columns used, k % 32 == 0) into
-// the hi|lo operand layout with per-row scales; rows n..n_pad-1 get
-// colscale 0.  One warp per row.
-__global__ void k_split_dense(const float* __restrict__ w, int n, int k, int ldw, int n_pad, uint16_t* __restrict__ bhl,
-                              float* __restrict__ colscale) {
+// The im2col rows of a kernel-3, padding-1 conv1d (tensor.rs:335-370),
+// straight into the hi|lo operand: output row r = (window w, time t) has
+// column j = c*3 + kk (j < 3*c_in) = in[w, c, t*stride + kk - 1] (0 outside
+// [0, t_in)), columns 3*c_in .. kp-1 zero; element (w, c, t) of the input
+// sits at in[w*sw + c*sc + t*st].  One CTA of 128 threads per row: pass 1
+// finds the row's largest |value|, pass 2 writes value*2^e = hi + lo.
+__device__ __forceinline__ float im2col_at(const float* __restrict__ in, int w, int t, int j, int c_in, int t_in,
+                                           int stride, size_t sw, size_t sc, size_t st) {
+    if (j >= 3 * c_in) return 0.f;
+    const int c = j / 3, ti = t * stride + (j - 3 * c) - 1;
+    return (ti >= 0 && ti < t_in) ? __ldg(in + size_t(w) * sw + size_t(c) * sc + size_t(ti) * st) : 0.f;
+}
+
+__global__ void __launch_bounds__(128) k_im2col_split(const float* __restrict__ in, int c_in, int t_in, int t_out,
+                                                      int stride, size_t sw, size_t sc, size_t st, int kp,
+                                                      uint16_t* __restrict__ ahl, float* __restrict__ rowscale) {
+    pdl_trigger();
+    pdl_wait();
+    const int row = blockIdx.x;
+    const int w = row / t_out, t = row % t_out;
+    const int nb = kp / QK;
+    const int bsub = threadIdx.x >> 3, esub = (threadIdx.x & 7) * 4;
+    float mx = 0.f;
+    for (int b = bsub; b < nb; b += 16)
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+            mx = fmaxf(mx, fabsf(im2col_at(in, w, t, b * QK + esub + e, c_in, t_in, stride, sw, sc, st)));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    __shared__ float s_mx[4];
+    if ((threadIdx.x & 31) == 0) s_mx[threadIdx.x >> 5] = mx;
+    __syncthreads();
+    mx = fmaxf(fmaxf(s_mx[0], s_mx[1]), fmaxf(s_mx[2], s_mx[3]));
+    const int ex = hl_row_exp(mx);
+    const float up = ldexpf(1.0f, ex);
+    for (int b = bsub; b < nb; b += 16) {
+        float4 v;
+        v.x = __fmul_rn(im2col_at(in, w, t, b * QK + esub, c_in, t_in, stride, sw, sc, st), up);
+        v.y = __fmul_rn(im2col_at(in, w, t, b * QK + esub + 1, c_in, t_in, stride, sw, sc, st), up);
+        v.z = __fmul_rn(im2col_at(in, w, t, b * QK + esub + 2, c_in, t_in, stride, sw, sc, st), up);
+        v.w = __fmul_rn(im2col_at(in, w, t, b * QK + esub + 3, c_in, t_in, stride, sw, sc, st), up);
+        float4 rest, dummy;
+        const uint2 hi = hl_pack_hi(v, rest);
+        const uint2 lo = hl_pack_hi(rest, dummy);
+        uint16_t* o = ahl + (size_t(row) * nb + b) * 64;
+        *reinterpret_cast<uint2*>(o + esub) = hi;
+        *reinterpret_cast<uint2*>(o + 32 + esub) = lo;
+    }
+    if (threadIdx.x == 0) rowscale[row] = ldexpf(1.0f, -ex);
+}
+
+// Dense f32 weight rows [n][ldw] (first kv columns used, zeros up to k,
+// k % 32 == 0) into the hi|lo operand layout with per-row scales; rows
+// n..n_pad-1 get colscale 0.  One warp per row.
+__global__ void k_split_dense(const float* __restrict__ w, int n, int k, int kv, int ldw, int n_pad,
+                              uint16_t* __restrict__ bhl, float* __restrict__ colscale) {
     const int lane = threadIdx.x & 31;
     const int j = int((size_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5);
     if (j >= n_pad) return;
@@ -415,14 +466,15 @@ __global__ void k_split_dense(const float* __restrict__ w, int n, int k, int ldw
     }
     const float* wr = w + size_t(j) * ldw;
     float mx = 0.f;
-    for (int e = lane; e < k; e += 32) mx = fmaxf(mx, fabsf(wr[e]));
+    for (int e = lane; e < kv; e += 32) mx = fmaxf(mx, fabsf(wr[e]));
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
     const int ex = hl_row_exp(mx);
     const float up = ldexpf(1.0f, ex);
     const int nb = k / QK;
     for (int b = 0; b < nb; ++b) {
-        const float v = __fmul_rn(wr[b * QK + lane], up);
+        const int e = b * QK + lane;
+        const float v = e < kv ? __fmul_rn(wr[e], up) : 0.f;
         const __half h = __float2half_rn(v);
         const __half l = __float2half_rn(__fsub_rn(v, __half2float(h)));
         uint16_t* o = bhl + (size_t(j) * nb + b) * 64;
@@ -580,12 +632,20 @@ cudaError_t launch_split_rows(const float* a, int m, int k, int lda, bool quanti
     return launch_pdl(kern, dim3(unsigned(m)), dim3(128), 0, s, a, m, k, lda, ahl, rowscale);
 }
 
-cudaError_t launch_split_dense(const float* w, int n, int k, int ldw, int n_pad, uint16_t* bhl, float* colscale,
-                               cudaStream_t s) {
+cudaError_t launch_split_dense(const float* w, int n, int k, int kv, int ldw, int n_pad, uint16_t* bhl,
+                               float* colscale, cudaStream_t s) {
     if (n_pad <= 0) return cudaSuccess;
     const size_t threads = size_t(n_pad) * 32;
-    k_split_dense<<<unsigned((threads + 255) / 256), 256, 0, s>>>(w, n, k, ldw, n_pad, bhl, colscale);
+    k_split_dense<<<unsigned((threads + 255) / 256), 256, 0, s>>>(w, n, k, kv, ldw, n_pad, bhl, colscale);
     return cudaGetLastError();
+}
+
+cudaError_t launch_im2col_split(const float* in, int n_win, int c_in, int t_in, int t_out, int stride, size_t sw,
+                                size_t sc, size_t st, int kp, uint16_t* ahl, float* rowscale, cudaStream_t s) {
+    const long rows = long(n_win) * t_out;
+    if (rows <= 0) return cudaSuccess;
+    return launch_pdl(k_im2col_split, dim3(unsigned(rows)), dim3(128), 0, s, in, c_in, t_in, t_out, stride, sw, sc,
+                      st, kp, ahl, rowscale);
 }
 
 int gemm_hl_ksplit(int m, int n, int nb) {

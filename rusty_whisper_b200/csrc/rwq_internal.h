@@ -79,10 +79,16 @@ cudaError_t launch_gemm_fold(const ActsView& v, const Weight& w, const float* bi
 // and the dequantized values d_a*q_a are split, else the f32 values.
 cudaError_t launch_split_rows(const float* a, int m, int k, int lda, bool quantize, uint16_t* ahl, float* rowscale,
                               cudaStream_t s);
-// Dense f32 weight rows w[n][ldw] (first k columns) into the hi|lo
-// operand layout [n][k/32][64] with colscale[n_pad] (n_pad >= round4(n)).
-cudaError_t launch_split_dense(const float* w, int n, int k, int ldw, int n_pad, uint16_t* bhl, float* colscale,
-                               cudaStream_t s);
+// Dense f32 weight rows w[n][ldw] (first kv columns, zeros up to k) into
+// the hi|lo operand layout [n][k/32][64] with colscale[n_pad] (n_pad >=
+// round4(n)).
+cudaError_t launch_split_dense(const float* w, int n, int k, int kv, int ldw, int n_pad, uint16_t* bhl,
+                               float* colscale, cudaStream_t s);
+// im2col rows of a kernel-3, padding-1 conv1d straight into the hi|lo
+// operand: n_win * t_out rows of kp columns (3*c_in used, then zeros),
+// input element (w, c, t) at in[w*sw + c*sc + t*st].
+cudaError_t launch_im2col_split(const float* in, int n_win, int c_in, int t_in, int t_out, int stride, size_t sw,
+                                size_t sc, size_t st, int kp, uint16_t* ahl, float* rowscale, cudaStream_t s);
 // y[m][n] = (A'*2^e_i)(B*2^e_j)^T * 2^-e_i * 2^-e_j (+ bias) on tcgen05 with
 // both operands split into f16 hi + lo, the whole K accumulated in TMEM.
 cudaError_t launch_gemm_hl(const uint16_t* ahl, const float* rowscale, int m, const uint16_t* bhl,

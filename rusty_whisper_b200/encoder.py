@@ -91,3 +91,28 @@ def multi_head_attention(q, k, v, n_head: int):
     _lib.check(_lib.lib().rwq_attention_dev(_ptr(q), _ptr(k), _ptr(v), q.shape[0], q.shape[1], q.shape[2], n_head,
                                             _ptr(out), ctypes.c_void_p(_stream_ptr(q.device))))
     return out[0] if squeeze else out
+
+
+def conv1d(x, w, b, stride: int):
+    """tensor.rs:335-370 conv1d (kernel 3, padding 1) on the tensor cores:
+    x CUDA f32 [n_win, in_ch, t] (or [in_ch, t]), w [out_ch, in_ch, 3], b
+    [out_ch] or None -> [n_win, t_out, out_ch] (time-major: the
+    reference's [out_ch, t_out] transposed)."""
+    torch = _torch()
+    squeeze = x.dim() == 2
+    if squeeze:
+        x = x.unsqueeze(0)
+    x, w = x.contiguous(), w.contiguous()
+    n_win, in_ch, t = x.shape
+    out_ch = w.shape[0]
+    if w.shape != (out_ch, in_ch, 3):
+        raise ValueError("w must be [out_ch, in_ch, 3]")
+    t_out = (t - 1) // stride + 1
+    out = torch.empty((n_win, t_out, out_ch), device=x.device, dtype=torch.float32)
+    bp = None
+    if b is not None:
+        b = b.contiguous()
+        bp = _ptr(b)
+    _lib.check(_lib.lib().rwq_conv1d_dev(_ptr(x), n_win, in_ch, t, _ptr(w), out_ch, bp, stride, _ptr(out),
+                                         ctypes.c_void_p(_stream_ptr(x.device))))
+    return out[0] if squeeze else out

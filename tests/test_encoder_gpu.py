@@ -9,8 +9,10 @@ Bars:
     error <= 2e-2 per window and max |err| <= 0.25 on LayerNorm-scaled
     outputs, against the oracle encoder run on the same tensors;
   * batch composition: a window encodes the same alone or in a batch
-    (within 1e-4 relative RMS; the conv stem's SGEMM may pick
-    size-dependent kernels).
+    (within 1e-4 relative RMS: the tensor-core GEMMs' K splits may differ
+    with the batch's row count);
+  * the conv stem's conv1d on the tensor cores against the reference's f32
+    conv1d.
 """
 import numpy as np
 import pytest
@@ -48,6 +50,27 @@ def test_attention_matches_reference_mha(torch_mod, w, t, n_head):
         ref = oracle.mha(q[i], k[i], v[i], n_head)
         err = np.max(np.abs(got[i] - ref))
         assert err <= 5e-3 * np.max(np.abs(ref)), (i, err)
+
+
+@pytest.mark.parametrize("w,in_ch,t,out_ch,stride", [(1, 80, 3000, 512, 1), (2, 512, 3000, 512, 2),
+                                                     (1, 128, 200, 1280, 1), (3, 7, 33, 20, 2), (1, 3, 1, 5, 1)])
+def test_conv1d_matches_reference(torch_mod, w, in_ch, t, out_ch, stride):
+    """The encoder stem's conv1d (tensor.rs:335-370) on the hi|lo tensor-core
+    GEMM against the reference's f32 conv: within 1e-5 of each output
+    window's scale (f32-level: the two sums round differently by ~2e-6),
+    and the 1e-3 rule (quant.rs:1365)."""
+    import oracle
+    from rusty_whisper_b200 import encoder, synth
+    x = synth.normal(1 + t, w * in_ch * t, -0.5, 0.3).reshape(w, in_ch, t)
+    wt = synth.normal(2 + in_ch, out_ch * in_ch * 3, 0.0, 0.02).reshape(out_ch, in_ch, 3)
+    b = synth.normal(3 + out_ch, out_ch, 0.0, 0.02)
+    got = encoder.conv1d(*(torch_mod.from_numpy(a).cuda() for a in (x, wt, b)), stride).cpu().numpy()
+    for i in range(w):
+        ref = oracle.conv1d(x[i], wt, b, stride).T
+        assert got[i].shape == ref.shape
+        err = np.abs(got[i].astype(np.float64) - ref)
+        assert err.max() <= 1e-5 * np.abs(ref).max(), (i, err.max(), np.abs(ref).max())
+        assert (err / np.maximum(np.abs(ref), 1.0)).max() < 1e-3
 
 
 def _encoder_pair(dtype, n_ctx=100, n_state=256, n_head=4, n_layer=2, n_mels=80, seed=5):
