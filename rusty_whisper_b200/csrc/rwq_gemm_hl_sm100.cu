@@ -37,17 +37,19 @@
 //              D0 (after waiting for D0's drain at a run start), a commit
 //              per stage and one per D0 run;
 //   warps 2-9  epilogue: warp w owns TMEM lanes 32*(w%4).. and half of the
-//              columns; it adds every D0 run into registers, then D1, and
-//              writes the tile to shared memory (the drained stage ring);
-//              then all 320 threads add the K slices' tiles
-//              (clusters of S CTAs, read through distributed shared memory
-//              in slice order), scale, add the bias and store coalesced.
+//              columns; it adds every D0 run into registers, then D1,
+//              scales, adds the bias and writes 32 x 32 boxes into the
+//              drained stage ring for TMA stores.  With the K range split
+//              over a cluster of S CTAs, each leaves its unscaled tile in
+//              shared memory and adds a row slice of all S tiles in slice
+//              order (distributed shared memory).
 // Every wait is bounded (rwq_sm100.cuh); no load uses cluster multicast.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 #include <cuda_fp16.h>
 #include <cstdio>
 #include <cstring>
+#include <map>
 #include <mutex>
 #include "rwq_common.cuh"
 #include "rwq_internal.h"
@@ -64,16 +66,18 @@ constexpr int HL_EPI0 = 2;                  // first epilogue warp
 constexpr int HL_EPI_WARPS = 8;
 constexpr int HL_THREADS = (HL_EPI0 + HL_EPI_WARPS) * 32;
 constexpr int HL_DRAIN = 8;                 // K blocks per D0 run
+// How an unsplit tile reaches Y: TMA stores of 32 x 32 boxes (N % 4 == 0
+// and Y 16-byte aligned), float4 stores, or element stores.
+enum { HL_STORE_TMA = 0, HL_STORE_VEC = 1, HL_STORE_SCALAR = 2 };
 
 template <int BN>
 struct Hl {
     static constexpr int B_BYTES = BN * 128;
     static constexpr int STAGE_BYTES = HL_A_BYTES + B_BYTES;
     static constexpr int STAGES = BN == 256 ? 4 : BN == 128 ? 6 : 8;   // 192 KiB of stages
-    // The f32 tile in shared memory: rows of BN + 4 floats, so the eight
-    // rows a quarter-warp writes at once fall in distinct 16-byte banks.
+    // K-split partial tiles in the drained stages: rows of BN + 4 floats, so
+    // the eight rows a quarter-warp writes at once fall in distinct banks.
     static constexpr int PITCH = BN + 4;
-    static constexpr int PART_BYTES = HL_BM * PITCH * 4;
     static constexpr int TMEM_COLS = 2 * BN;              // D0 at column 0, D1 at column BN
     static constexpr int CPW = BN / 2;                    // columns per epilogue warp
     // kind::f16, D f32, A/B f16, both K-major, N>>3 at bit 17, M>>4 at bit 24.
@@ -82,10 +86,15 @@ struct Hl {
         uint64_t full[STAGES], empty[STAGES], d0_full, d0_empty;
         uint32_t tmem_base;
         int abort;
+        // the tile's row scales, column scales and bias, loaded during the
+        // mainloop so the copy-out reads them from shared memory
+        alignas(16) float rs[HL_BM];
+        alignas(16) float cs[BN];
+        alignas(16) float bs[BN];
     };
     static constexpr int SMEM = STAGES * STAGE_BYTES + int(sizeof(Bars)) + 1024;
     static_assert(SMEM <= 227 * 1024, "shared memory budget");
-    static_assert(PART_BYTES <= STAGES * STAGE_BYTES, "the f32 tile must fit in the drained stages");
+    static_assert(HL_BM * PITCH * 4 <= STAGES * STAGE_BYTES, "the output tile must fit in the drained stages");
     static_assert(BN == 64 || BN == 128 || BN == 256, "tile width");
 };
 
@@ -106,14 +115,16 @@ __device__ __forceinline__ void hl_cluster_sync() {
     asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 
-// grid: x = n_tiles * S (K slice = blockIdx.x % S, clusters of S CTAs along
-// x when S > 1), y = m_tiles.  Slice r covers K blocks [r*kps, min(nb,
-// (r+1)*kps)), never empty (the host picks S so).
+// grid: x = n_tiles * S (K slice = blockIdx.x % S), y = m_tiles.  Slice r
+// covers K blocks [r*kps, min(nb, (r+1)*kps)), never empty (the host picks
+// S so).  S > 1: the S CTAs of a cluster (along x) each leave their
+// unscaled tile in shared memory and add row slices of all S tiles.
 template <int BN>
 __global__ void __launch_bounds__(HL_THREADS, 1)
     k_gemm_hl(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-              const float* __restrict__ rowscale, const float* __restrict__ colscale, const float* __restrict__ bias,
-              float* __restrict__ Y, int M, int N, int nb, int kps, int S, int vec_store, int* __restrict__ err_flag) {
+              const __grid_constant__ CUtensorMap tmY, const float* __restrict__ rowscale,
+              const float* __restrict__ colscale, const float* __restrict__ bias, float* __restrict__ Y, int M, int N,
+              int nb, int kps, int S, int store_mode, int* __restrict__ err_flag) {
     using F = Hl<BN>;
     constexpr int STAGES = F::STAGES, STAGE_BYTES = F::STAGE_BYTES, PITCH = F::PITCH, CPW = F::CPW;
     constexpr uint32_t IDESC = F::IDESC;
@@ -122,7 +133,6 @@ __global__ void __launch_bounds__(HL_THREADS, 1)
     uint8_t* base = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     Bars* bar = reinterpret_cast<Bars*>(base + STAGES * STAGE_BYTES);
     volatile int* abort = &bar->abort;
-    float* part = reinterpret_cast<float*>(base);   // the f32 tile, after the last MMA
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int split = int(blockIdx.x) % S;
@@ -201,6 +211,14 @@ __global__ void __launch_bounds__(HL_THREADS, 1)
         }
         __syncwarp();
     } else {
+        {   // scales and bias of the tile, zero past the edges
+            const int t = int(threadIdx.x) - HL_EPI0 * 32;   // 0 .. 255
+            if (t < HL_BM) bar->rs[t] = m0 + t < M ? __ldg(rowscale + m0 + t) : 0.f;
+            for (int c = t; c < BN; c += HL_EPI_WARPS * 32) {
+                bar->cs[c] = __ldg(colscale + n0 + c);   // padded to a multiple of 256 columns
+                bar->bs[c] = (bias && n0 + c < N) ? __ldg(bias + n0 + c) : 0.f;
+            }
+        }
         // Epilogue: warp w owns TMEM lanes 32*(w%4).. (tile rows) and
         // columns h*CPW .. h*CPW + CPW of D0 and D1.
         const int q = warp & 3, h = (warp - HL_EPI0) >> 2;
@@ -230,20 +248,67 @@ __global__ void __launch_bounds__(HL_THREADS, 1)
             if (lane == 0) mbar_arrive(&bar->d0_empty);
         }
         if (ok) {
-            // The last D0 commit came after every MMA, D1's included.
+            // The last D0 commit came after every MMA, D1's included.  One
+            // 32-column box at a time: sums = D0 runs + D1, then (S == 1)
+            // y = sum * 2^-e_j * 2^-e_i (+ bias) into a 32 x 32 box of the
+            // drained stage ring for a TMA store (128-byte swizzle: 16-byte
+            // chunk k of row r at k ^ (r & 7); box (q, column box cb) at
+            // (q * BN/32 + cb) * 4 KiB), or straight to Y; (S > 1) the
+            // unscaled sums into the drained ring as rows of PITCH floats.
             const int row = q * 32 + lane;
-            float* prow = part + size_t(row) * PITCH;
+            const float rs = bar->rs[row];
 #pragma unroll
-            for (int c = 0; c < CPW; c += 16) {
-                uint32_t v[16];
-                tmem_ld16(tmem + lane_off + uint32_t(BN + h * CPW + c), v);
-                tmem_wait_ld();
+            for (int bx = 0; bx < CPW / 32; ++bx) {
+                const int c0 = bx * 32, cb = h * (CPW / 32) + bx;
+                float v[32];
 #pragma unroll
-                for (int e = 0; e < 16; e += 4)
-                    *reinterpret_cast<float4*>(prow + h * CPW + c + e) = make_float4(
-                        __fadd_rn(acc[c + e], __uint_as_float(v[e])), __fadd_rn(acc[c + e + 1], __uint_as_float(v[e + 1])),
-                        __fadd_rn(acc[c + e + 2], __uint_as_float(v[e + 2])),
-                        __fadd_rn(acc[c + e + 3], __uint_as_float(v[e + 3])));
+                for (int half = 0; half < 2; ++half) {
+                    uint32_t d1[16];
+                    tmem_ld16(tmem + lane_off + uint32_t(BN + h * CPW + c0 + 16 * half), d1);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int e = 0; e < 16; ++e) v[16 * half + e] = __fadd_rn(acc[c0 + 16 * half + e], __uint_as_float(d1[e]));
+                }
+                if (S == 1) {
+#pragma unroll
+                    for (int e = 0; e < 32; ++e) {
+                        const int cc = cb * 32 + e;
+                        float t = __fmul_rn(__fmul_rn(v[e], bar->cs[cc]), rs);
+                        v[e] = bias ? __fadd_rn(t, bar->bs[cc]) : t;
+                    }
+                    if (store_mode == HL_STORE_TMA) {
+                        uint8_t* box = base + (q * (BN / 32) + cb) * 4096 + lane * 128;
+#pragma unroll
+                        for (int k4 = 0; k4 < 8; ++k4)
+                            *reinterpret_cast<float4*>(box + ((k4 ^ (lane & 7)) << 4)) =
+                                make_float4(v[4 * k4], v[4 * k4 + 1], v[4 * k4 + 2], v[4 * k4 + 3]);
+                    } else if (m0 + row < M) {
+                        float* yr = Y + size_t(m0 + row) * N + n0 + cb * 32;
+#pragma unroll
+                        for (int e = 0; e < 32; ++e)
+                            if (n0 + cb * 32 + e < N) yr[e] = v[e];
+                    }
+                } else {
+                    float* pr = reinterpret_cast<float*>(base) + size_t(row) * PITCH + cb * 32;
+#pragma unroll
+                    for (int e = 0; e < 32; e += 4)
+                        *reinterpret_cast<float4*>(pr + e) = make_float4(v[e], v[e + 1], v[e + 2], v[e + 3]);
+                }
+            }
+            if (S == 1 && store_mode == HL_STORE_TMA) {
+                fence_async_smem();
+                __syncwarp();
+                if (lane == 0) {
+#pragma unroll
+                    for (int bx = 0; bx < CPW / 32; ++bx) {
+                        const int cb = h * (CPW / 32) + bx;
+                        if (n0 + cb * 32 < N && m0 + q * 32 < M)
+                            tma_store_2d(&tmY, n0 + cb * 32, m0 + q * 32, base + (q * (BN / 32) + cb) * 4096);
+                    }
+                    bulk_commit();
+                    bulk_wait_read_all();
+                }
+                __syncwarp();
             }
         }
     }
@@ -253,54 +318,60 @@ __global__ void __launch_bounds__(HL_THREADS, 1)
     tc_fence_before();
     if (S > 1) hl_cluster_sync();
     else __syncthreads();
-
-    // Slice `split` adds rows [split*RS, +RS) of the S partial tiles in
-    // slice order, then y = acc * 2^-e_i * 2^-e_j (+ bias).
-    const int RS = HL_BM / S;
-    const int r0 = split * RS;
-    if (!*abort) {
-        const uint32_t part_s = smem_u32(part);
-        constexpr int C4 = BN / 4;
-        for (int idx = threadIdx.x; idx < RS * C4; idx += HL_THREADS) {
-            const int rr = r0 + idx / C4, c = (idx % C4) * 4;
-            const int gi = m0 + rr, gj = n0 + c;
-            if (gi >= M || gj >= N) continue;
-            const uint32_t off = uint32_t((rr * PITCH + c) * 4);
-            float4 acc;
-            if (S == 1) {
-                acc = *reinterpret_cast<const float4*>(part + rr * PITCH + c);
-            } else {
-                acc = hl_ld_cluster4(hl_mapa(part_s + off, 0));
+    if (S > 1 && !*abort) {
+        // Slice `split` adds rows [r0, r1) of the S partial tiles in slice
+        // order (distributed shared memory), scales, adds the bias and
+        // stores; four float4 per thread per round, loads before stores.
+        const int r0 = split * HL_BM / S, r1 = (split + 1) * HL_BM / S;
+        const uint32_t part_s = smem_u32(base);
+        constexpr int C4 = BN / 4, U = 4;
+        const int total = (r1 - r0) * C4;
+        for (int i0 = threadIdx.x; i0 < total; i0 += U * HL_THREADS) {
+            float4 acc[U];
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const int idx = min(i0 + u * HL_THREADS, total - 1);
+                const int rr = r0 + idx / C4, c = (idx % C4) * 4;
+                const uint32_t off = part_s + uint32_t((rr * PITCH + c) * 4);
+                acc[u] = hl_ld_cluster4(hl_mapa(off, 0));
                 for (int s2 = 1; s2 < S; ++s2) {
-                    const float4 t = hl_ld_cluster4(hl_mapa(part_s + off, uint32_t(s2)));
-                    acc.x = __fadd_rn(acc.x, t.x);
-                    acc.y = __fadd_rn(acc.y, t.y);
-                    acc.z = __fadd_rn(acc.z, t.z);
-                    acc.w = __fadd_rn(acc.w, t.w);
+                    const float4 t = hl_ld_cluster4(hl_mapa(off, uint32_t(s2)));
+                    acc[u].x = __fadd_rn(acc[u].x, t.x);
+                    acc[u].y = __fadd_rn(acc[u].y, t.y);
+                    acc[u].z = __fadd_rn(acc[u].z, t.z);
+                    acc[u].w = __fadd_rn(acc[u].w, t.w);
                 }
             }
-            const float rs = __ldg(rowscale + gi);
-            const float4 cs = __ldg(reinterpret_cast<const float4*>(colscale + gj));   // padded, 16-byte aligned
-            float4 v = make_float4(__fmul_rn(__fmul_rn(acc.x, cs.x), rs), __fmul_rn(__fmul_rn(acc.y, cs.y), rs),
-                                   __fmul_rn(__fmul_rn(acc.z, cs.z), rs), __fmul_rn(__fmul_rn(acc.w, cs.w), rs));
-            float* yr = Y + size_t(gi) * N + gj;
-            if (vec_store) {   // N % 4 == 0 and Y 16-byte aligned: gj + 3 < N
-                if (bias) {
-                    v.x = __fadd_rn(v.x, __ldg(bias + gj));
-                    v.y = __fadd_rn(v.y, __ldg(bias + gj + 1));
-                    v.z = __fadd_rn(v.z, __ldg(bias + gj + 2));
-                    v.w = __fadd_rn(v.w, __ldg(bias + gj + 3));
-                }
-                *reinterpret_cast<float4*>(yr) = v;
-            } else {
-                const float vv[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-                for (int e = 0; e < 4; ++e)
-                    if (gj + e < N) yr[e] = bias ? __fadd_rn(vv[e], __ldg(bias + gj + e)) : vv[e];
+            for (int u = 0; u < U; ++u) {
+                const int idx = i0 + u * HL_THREADS;
+                if (idx >= total) break;
+                const int rr = r0 + idx / C4, c = (idx % C4) * 4;
+                const int gi = m0 + rr, gj = n0 + c;
+                if (gi >= M || gj >= N) continue;
+                const float rs = bar->rs[rr];
+                const float4 cs = *reinterpret_cast<const float4*>(bar->cs + c);
+                const float4 bs = *reinterpret_cast<const float4*>(bar->bs + c);
+                float4 v = make_float4(__fmul_rn(__fmul_rn(acc[u].x, cs.x), rs), __fmul_rn(__fmul_rn(acc[u].y, cs.y), rs),
+                                       __fmul_rn(__fmul_rn(acc[u].z, cs.z), rs), __fmul_rn(__fmul_rn(acc[u].w, cs.w), rs));
+                if (bias) {
+                    v.x = __fadd_rn(v.x, bs.x);
+                    v.y = __fadd_rn(v.y, bs.y);
+                    v.z = __fadd_rn(v.z, bs.z);
+                    v.w = __fadd_rn(v.w, bs.w);
+                }
+                float* yr = Y + size_t(gi) * N + gj;
+                if (store_mode != HL_STORE_SCALAR) {   // N % 4 == 0 and Y 16-byte aligned: gj + 3 < N
+                    *reinterpret_cast<float4*>(yr) = v;
+                } else {
+                    const float vv[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+                    for (int e = 0; e < 4; ++e)
+                        if (gj + e < N) yr[e] = vv[e];
+                }
             }
         }
     }
-
     // No CTA leaves (or frees its TMEM) while a peer still reads its tile.
     if (S > 1) hl_cluster_sync();
     else __syncthreads();
@@ -515,9 +586,26 @@ bool encode_map(CUtensorMap* map, const void* ptr, uint64_t inner, uint64_t rows
     return true;
 }
 
+// Y as a 2-D f32 tensor [rows][inner] for 32 x 32 TMA store boxes,
+// 128-byte swizzle (inner * 4 must be a multiple of 16).
+bool encode_map_f32(CUtensorMap* map, const void* ptr, uint64_t inner, uint64_t rows, char* why, size_t why_len) {
+    if (!g_encode) return false;
+    cuuint64_t dims[2] = {inner, rows};
+    cuuint64_t strides[1] = {inner * 4};
+    cuuint32_t box[2] = {32, 32};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+        snprintf(why, why_len, "cuTensorMapEncodeTiled (output) failed (%d)", int(r));
+        return false;
+    }
+    return true;
+}
+
 struct DevInfo {
     int sms = 0;
-    int max_clusters[3][3] = {};   // [BN index][S index: 2, 4] (0 = not queried)
     bool attr[3] = {};
 };
 DevInfo g_dev[64];
@@ -528,14 +616,16 @@ constexpr int bn_index() {
     return BN == 64 ? 0 : BN == 128 ? 1 : 2;
 }
 
+// Active clusters of S CTAs that fit at once (cached per device, BN, S).
+int g_max_clusters[64][3][5];
+
 template <int BN>
 int max_active_clusters(int dev, int S) {
     std::lock_guard<std::mutex> g(g_dev_mu);
-    DevInfo& di = g_dev[dev];
-    int& slot = di.max_clusters[bn_index<BN>()][S == 2 ? 0 : 1];
+    int& slot = g_max_clusters[dev][bn_index<BN>()][S];
     if (slot == 0) {
         cudaLaunchConfig_t cfg = {};
-        cfg.gridDim = dim3(unsigned(S) * 64, 1);
+        cfg.gridDim = dim3(unsigned(S) * 60, 1);
         cfg.blockDim = dim3(HL_THREADS);
         cfg.dynamicSmemBytes = Hl<BN>::SMEM;
         cudaLaunchAttribute attr[1];
@@ -557,6 +647,13 @@ int max_active_clusters(int dev, int S) {
 
 thread_local int t_ksplit_override = 0;
 
+int cur_dev() {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    return dev < 64 ? dev : 63;
+}
+
+
 int sms_of(int dev) {
     std::lock_guard<std::mutex> g(g_dev_mu);
     if (g_dev[dev].sms == 0) cudaDeviceGetAttribute(&g_dev[dev].sms, cudaDevAttrMultiProcessorCount, dev);
@@ -574,51 +671,86 @@ cudaError_t ensure_smem_attr(int dev) {
     return cudaSuccess;
 }
 
-// K slices of an m x n GEMM with nb blocks: double while the CTAs still fit
-// in one wave, every slice keeps at least 4 blocks, and all clusters can be
-// resident at once.  A row's sums depend on m only through this choice.
+// Tile width BN and K slices S of an m x n GEMM with nb blocks, from a
+// cost estimate in units of one 128 x 256 K block of MMAs: per CTA
+// ceil(nb/S) blocks at a BN-dependent cost (narrower MMAs do less work per
+// cycle but are bound by shared-memory bandwidth, not proportionally
+// cheaper) plus fixed costs (prologue, TMEM drain and copy-out; each
+// extra slice adds a partial tile to read through distributed shared
+// memory), times the waves of CTAs.  K-split clusters must all be resident
+// at once.  A row's sums depend on m only through S.
+struct HlCfg {
+    int bn = 256, S = 1;
+};
+
+// Cost in units of one K block of a 128 x 256 tile (~0.47 us measured;
+// a 128 x 128 tile's block takes ~0.45 us: narrow MMAs are not cheaper,
+// so narrow tiles only pay where wide ones leave SMs idle).  Fixed per
+// CTA: prologue (~1.2 us) and writing its output (~4 us for a 128 x 256
+// f32 tile, in proportion); a K split adds the partial tile's round trip
+// through shared memory and a share of the distributed reduction.
 template <int BN>
-int ksplit_bn(int dev, int m, int n, int nb) {
-    if (ensure_smem_attr<BN>(dev) != cudaSuccess) return 1;
-    const int sms = sms_of(dev);
-    const long tiles = long((m + HL_BM - 1) / HL_BM) * ((n + BN - 1) / BN);
-    int S = 1;
-    while (S < 4 && tiles * S * 2 <= sms && nb / (S * 2) >= 4) {
-        const int mc = max_active_clusters<BN>(dev, S * 2);
-        if (mc < 0 || tiles > mc) break;
-        S *= 2;
-    }
-    return S;
+constexpr double hl_block_cost() {
+    return BN == 256 ? 1.0 : BN == 128 ? 0.95 : 0.9;
 }
 
-int cur_dev() {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    return dev < 64 ? dev : 63;
+template <int BN>
+void hl_consider(int dev, int m, int n, int nb, int sms, HlCfg* best, double* best_t) {
+    if (ensure_smem_attr<BN>(dev) != cudaSuccess) return;
+    const long tiles = long((m + HL_BM - 1) / HL_BM) * ((n + BN - 1) / BN);
+    for (int S = 1; S <= 4; ++S) {
+        if (S > 1) {
+            if (nb / S < 4 || tiles * S > sms) break;
+            const int mc = max_active_clusters<BN>(dev, S);
+            if (mc < 0 || tiles > mc) continue;
+        }
+        const long ctas = tiles * S, waves = (ctas + sms - 1) / sms;
+        const double store = 8.5 * BN / 256.0;
+        const double fixed = 2.5 + (S == 1 ? store : 3.0 + store / S);
+        const double t = double(waves) * (double((nb + S - 1) / S) * hl_block_cost<BN>() + fixed);
+        if (t < *best_t - 1e-9) {
+            *best_t = t;
+            best->bn = BN;
+            best->S = S;
+        }
+    }
 }
+
+HlCfg hl_choose(int dev, int m, int n, int nb) {
+    const int sms = sms_of(dev);
+    HlCfg best;
+    double t = 1e300;
+    if (n > 128) hl_consider<256>(dev, m, n, nb, sms, &best, &t);
+    if (n > 64) hl_consider<128>(dev, m, n, nb, sms, &best, &t);
+    hl_consider<64>(dev, m, n, nb, sms, &best, &t);
+    return best;
+}
+
 
 template <int BN>
 cudaError_t launch_hl_bn(const uint16_t* ahl, const float* rowscale, int m, const uint16_t* bhl,
-                         const float* colscale, int n, int nb, const float* bias, float* y, int* err_flag,
+                         const float* colscale, int n, int nb, const float* bias, float* y, int* err_flag, int S,
                          cudaStream_t s, char* why, size_t why_len) {
     const int dev = cur_dev();
     cudaError_t e = ensure_smem_attr<BN>(dev);
     if (e != cudaSuccess) return e;
     const int mt = (m + HL_BM - 1) / HL_BM, nt = (n + BN - 1) / BN;
-    int S = t_ksplit_override > 0 ? t_ksplit_override : ksplit_bn<BN>(dev, m, n, nb);
     // Never an empty slice.
-    while (S > 1 && (S - 1) * ((nb + S - 1) / S) >= nb) S /= 2;
+    while (S > 1 && (S - 1) * ((nb + S - 1) / S) >= nb) --S;
     const int kps = (nb + S - 1) / S;
-    CUtensorMap ma, mb;
+    CUtensorMap ma, mb, my;
     if (!encode_map(&ma, ahl, uint64_t(nb) * 64, uint64_t(m), HL_BM, why, why_len)) return cudaErrorInvalidValue;
     if (!encode_map(&mb, bhl, uint64_t(nb) * 64, uint64_t(n), BN, why, why_len)) return cudaErrorInvalidValue;
-    const int vec = (n % 4 == 0) && (reinterpret_cast<uintptr_t>(y) % 16 == 0);
+    const bool vec = (n % 4 == 0) && (reinterpret_cast<uintptr_t>(y) % 16 == 0);
+    int mode = vec ? HL_STORE_VEC : HL_STORE_SCALAR;
+    memset(&my, 0, sizeof my);
+    if (S == 1 && vec && encode_map_f32(&my, y, uint64_t(n), uint64_t(m), why, why_len)) mode = HL_STORE_TMA;
     dim3 grid(unsigned(nt * S), unsigned(mt));
     if (S == 1)
-        return launch_pdl(k_gemm_hl<BN>, grid, dim3(HL_THREADS), Hl<BN>::SMEM, s, ma, mb, rowscale, colscale, bias, y,
-                          m, n, nb, kps, S, vec, err_flag);
-    return launch_pdl_cluster(k_gemm_hl<BN>, grid, dim3(HL_THREADS), Hl<BN>::SMEM, S, s, ma, mb, rowscale, colscale,
-                              bias, y, m, n, nb, kps, S, vec, err_flag);
+        return launch_pdl(k_gemm_hl<BN>, grid, dim3(HL_THREADS), Hl<BN>::SMEM, s, ma, mb, my, rowscale, colscale, bias,
+                          y, m, n, nb, kps, S, mode, err_flag);
+    return launch_pdl_cluster(k_gemm_hl<BN>, grid, dim3(HL_THREADS), Hl<BN>::SMEM, S, s, ma, mb, my, rowscale, colscale,
+                              bias, y, m, n, nb, kps, S, mode, err_flag);
 }
 
 }  // namespace
@@ -648,22 +780,21 @@ cudaError_t launch_im2col_split(const float* in, int n_win, int c_in, int t_in, 
                       st, kp, ahl, rowscale);
 }
 
-int gemm_hl_ksplit(int m, int n, int nb) {
-    const int dev = cur_dev();
-    if (n > 128) return ksplit_bn<256>(dev, m, n, nb);
-    if (n > 64) return ksplit_bn<128>(dev, m, n, nb);
-    return ksplit_bn<64>(dev, m, n, nb);
-}
+int gemm_hl_ksplit(int m, int n, int nb) { return hl_choose(cur_dev(), m, n, nb).S; }
 
-void set_gemm_hl_ksplit(int S) { t_ksplit_override = (S == 1 || S == 2 || S == 4) ? S : 0; }
+void set_gemm_hl_ksplit(int S) { t_ksplit_override = (S >= 1 && S <= 4) ? S : 0; }
 
 cudaError_t launch_gemm_hl(const uint16_t* ahl, const float* rowscale, int m, const uint16_t* bhl,
                            const float* colscale, int n, int nb, const float* bias, float* y, int* err_flag,
                            cudaStream_t s, char* why, size_t why_len) {
     if (m <= 0 || n <= 0) return cudaSuccess;
-    if (n > 128) return launch_hl_bn<256>(ahl, rowscale, m, bhl, colscale, n, nb, bias, y, err_flag, s, why, why_len);
-    if (n > 64) return launch_hl_bn<128>(ahl, rowscale, m, bhl, colscale, n, nb, bias, y, err_flag, s, why, why_len);
-    return launch_hl_bn<64>(ahl, rowscale, m, bhl, colscale, n, nb, bias, y, err_flag, s, why, why_len);
+    HlCfg c = hl_choose(cur_dev(), m, n, nb);
+    if (t_ksplit_override > 0) c.S = t_ksplit_override;
+    switch (c.bn) {
+        case 256: return launch_hl_bn<256>(ahl, rowscale, m, bhl, colscale, n, nb, bias, y, err_flag, c.S, s, why, why_len);
+        case 128: return launch_hl_bn<128>(ahl, rowscale, m, bhl, colscale, n, nb, bias, y, err_flag, c.S, s, why, why_len);
+        default: return launch_hl_bn<64>(ahl, rowscale, m, bhl, colscale, n, nb, bias, y, err_flag, c.S, s, why, why_len);
+    }
 }
 
 }  // namespace rwq
