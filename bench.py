@@ -714,16 +714,46 @@ def run_gemv(args, dev, quant, w_np, hbm_peak, stream):
             pf[0] += b
             pf[1] += dtm
         gbs = nbytes / t / 1e9
+        # The same launches replayed from one CUDA graph (no host launch
+        # gaps): what the decoder's graph-captured step sees.
+        st = torch.cuda.Stream()
+        st.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(st):   # the stream's workspace exists before capture
+            for key in w_np:
+                qa[(key[1], key[2])].matmul(Wc[0][key], out=ys[key])
+        torch.cuda.synchronize()
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr, stream=st):
+            for key in w_np:
+                for c in range(copies):
+                    qa[(key[1], key[2])].matmul(Wc[c][key], out=ys[key])
+        with torch.cuda.stream(st):
+            gr.replay()
+            torch.cuda._sleep(GATE_CYCLES)
+            g0 = torch.cuda.Event(enable_timing=True)
+            g1 = torch.cuda.Event(enable_timing=True)
+            g0.record(st)
+            gr.replay()
+            g1.record(st)
+        torch.cuda.synchronize()
+        tg = g0.elapsed_time(g1) / 1e3
+        del gr
         res[f"M={mm}"] = {"GB/s": round(gbs, 1), "frac_of_measured_hbm": round(gbs / hbm_peak, 4),
                           "us_per_gemv": round(t / launches * 1e6, 3),
+                          "graph_GB/s": round(nbytes / tg / 1e9, 1),
+                          "graph_us_per_gemv": round(tg / launches * 1e6, 3),
                           "per_format_GBs": {f: round(b / x / 1e9, 1) for f, (b, x) in per_fmt.items()}}
     res["logits_Q5_0_51865x1024"] = gemv_logits(args, dev, quant, hbm_peak, stream)
     res["bound"] = "hbm"
     res["peak_GBs"] = hbm_peak
     res["bytes"] = "N*(K/32)*block_bytes + 4*M*K + 4*M*N per GEMV (algorithmic)"
-    res["timing"] = "back-to-back launches of one GEMV over weight copies, one event pair per batch"
+    res["timing"] = ("back-to-back launches of one GEMV over weight copies, one event pair per batch; graph_*: "
+                     "the same launches of all weights replayed from one CUDA graph")
     res["l2"] = f"{copies} rotating weight copies ({copies * total_w / 1e6:.0f} MB > 126 MB L2)"
     return res
+
+
+GEMV_KERNELS = {1: "k_gemv_i8", 2: "k_gemv_mma", 3: "k_gemv_tile", 4: "k_gemv_rows"}
 
 
 def gemv_logits(args, dev, quant, hbm_peak, stream):
@@ -753,7 +783,7 @@ def gemv_logits(args, dev, quant, hbm_peak, stream):
         t = e0.elapsed_time(e1) / 1e3 / reps
         b = n * (k // QK) * block_bytes(dt) + 4.0 * mm * k + 4.0 * mm * n
         out[f"M={mm}"] = {"GB/s": round(b / t / 1e9, 1), "frac_of_measured_hbm": round(b / t / 1e9 / hbm_peak, 4),
-                          "us": round(t * 1e6, 2)}
+                          "us": round(t * 1e6, 2), "kernel": GEMV_KERNELS[quant.gemv_kernel_for(Wl[0], mm)]}
     return out
 
 

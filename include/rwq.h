@@ -160,19 +160,27 @@ int rwq_matmul_t_q_noalloc(const float* a, int64_t m, int64_t k, const rwq_qtens
 int rwq_set_gemm_path(int path);
 
 /* Force the kernel of the GEMV family (m <= 256, or path 1 above) for
- * testing and benchmarking: 0 = automatic (the integer-MMA kernel for every
- * m, so a row's result does not depend on m), 1 = dp4a kernel (one warp
- * lane per block, lanes per row from k, launches of 8 rows), 2 =
- * integer-MMA kernel (mma.sync m16n8k32: one instruction per block for 16
- * weight rows x 8 activation rows, up to 64 rows per launch sharing each
- * decoded weight fragment), 3 = tiled integer-MMA kernel (the same
- * arithmetic tiled like a GEMM: 32-64 weight rows x 32-64 activation rows
- * per CTA, K streamed through shared memory; automatic from 32 rows on).
- * All compute the reference's per-block formula (quant.rs:349-351,
- * :452-454) with exact integer block dots; 1 differs from the others only
- * in f32 summation order, 0, 2 and 3 give identical bits.  Applies to this
- * host thread. */
+ * testing and benchmarking: 0 = automatic (kernels 4, 2 and 3 by m and
+ * shape; they give identical bits, so a row's result does not depend on
+ * m), 1 = dp4a kernel (one warp lane per block, lanes per row from k,
+ * launches of 8 rows), 2 = integer-MMA kernel (mma.sync m16n8k32: one
+ * instruction per block for 16 weight rows x 8 activation rows, up to 64
+ * rows per launch sharing each decoded weight fragment), 3 = tiled
+ * integer-MMA kernel (the same arithmetic tiled like a GEMM: 32-64 weight
+ * rows x 32-64 activation rows per CTA, K streamed through shared memory;
+ * automatic from 32 rows on), 4 = row-per-lane kernel (one weight row per
+ * warp lane, dp4a block dots, the weight planes staged by TMA; automatic
+ * at 1-2 rows on weights the integer-MMA kernel runs without a K split,
+ * i.e. wide ones such as the logits projection; elsewhere kind 4 runs the
+ * automatic choice).  All compute the reference's per-block formula
+ * (quant.rs:349-351, :452-454) with exact integer block dots; 1 differs
+ * from the others only in f32 summation order, 0, 2, 3 and 4 give
+ * identical bits.  Applies to this host thread. */
 int rwq_set_gemv_kernel(int kind);
+
+/* The GEMV kernel (1-4 as above) this host thread's setting runs for an
+ * m-row call on weight `w` (m <= 256), or a negative status. */
+int rwq_gemv_kernel_for(const rwq_qtensor* w, int64_t m);
 
 /* Synchronize `stream` and report any fault a kernel recorded on it. */
 int rwq_stream_check(void* stream);

@@ -43,6 +43,7 @@ SIGNATURES = {
     "rwq_matmul_t_q_noalloc": (_I, [_P, _L, _L, _P, _P, _P, _P]),
     "rwq_set_gemm_path": (_I, [_I]),
     "rwq_set_gemv_kernel": (_I, [_I]),
+    "rwq_gemv_kernel_for": (_I, [_P, _L]),
     "rwq_stream_check": (_I, [_P]),
     "rwq_mma_peak": (_I, [_I, ctypes.c_longlong, _I, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_double)]),
     "rwq_model_load": (_I, [ctypes.c_char_p, ctypes.POINTER(_P)]),

@@ -240,7 +240,7 @@ int run_quantized(const rwq::ActsView& v, int layout, rwq_qtensor* b, const floa
     const int64_t k = v.k;
     if (layout == rwq::LAYOUT_GEMV) {
         if (k > 8192) return fail(RWQ_ERR_ARG, "k=%lld too large for the GEMV kernels (max 8192)", (long long)k);
-        RWQ_CUDA(rwq::launch_gemv_i8(v, w, bias, out, s), "gemv launch");
+        RWQ_CUDA(rwq::launch_gemv_i8(v, w, bias, out, s, err_flag), "gemv launch");
         return RWQ_OK;
     }
     int rc;
@@ -441,6 +441,7 @@ int qtensor_concat_rows(rwq_qtensor* const* parts, int np, cudaStream_t s, rwq_q
         if (e != cudaSuccess) return cleanup(cuda_fail(e, "copy weight planes"));
         r0 += ri;
     }
+    prepare_gemv_rows(w);
     *out = t;
     return RWQ_OK;
 }
@@ -521,6 +522,7 @@ static int qtensor_new_impl(const void* raw, bool raw_on_device, size_t raw_len,
         if (tmp) cudaFree(tmp);
         if (e != cudaSuccess) return cleanup(cuda_fail(e, "repack"));
     }
+    rwq::prepare_gemv_rows(w);
     *out = t;
     return RWQ_OK;
 }
@@ -735,9 +737,15 @@ int rwq_set_gemm_path(int path) {
 }
 
 int rwq_set_gemv_kernel(int kind) {
-    if (kind < 0 || kind > 3) return fail(RWQ_ERR_ARG, "kind must be 0, 1, 2 or 3");
+    if (kind < 0 || kind > 4) return fail(RWQ_ERR_ARG, "kind must be 0, 1, 2, 3 or 4");
     rwq::set_gemv_kind(kind);
     return RWQ_OK;
+}
+
+int rwq_gemv_kernel_for(const rwq_qtensor* w, int64_t m) {
+    if (!w) return fail(RWQ_ERR_ARG, "weight is null");
+    if (m < 1 || m > rwq::GEMV_FAMILY_MAX_M) return fail(RWQ_ERR_ARG, "m=%lld outside [1, 256]", (long long)m);
+    return rwq::gemv_kernel_for(w->w, int(m));
 }
 
 int rwq_stream_check(void* stream) {

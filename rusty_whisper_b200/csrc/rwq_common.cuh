@@ -115,6 +115,35 @@ __device__ __forceinline__ int dp4a_ss(uint32_t a_s8, uint32_t b_s8, int c) {
     return d;
 }
 
+// The integer dots of the GEMV kernels start from the bits of 1.5*2^23
+// (minus the Q4_0/Q5_0 code offset times sum(q_a)), so for |S| < 2^22 the
+// chain's result read as f32 is 1.5*2^23 + S exactly and S is one FADD.
+constexpr uint32_t MAGIC_BITS = 0x4B400000u;  // 12582912.0f
+constexpr float MAGIC_F = 12582912.0f;
+
+// Start of the s-th K slice (s >= 1) that k_gemv_mma uses for weight tile
+// T, or a value past every group if there is none.  KS > 1: slice s of the
+// group range starts at s*ng/KS.  KS == 1: k_gemv_mma's CTA c owns tiles
+// [c*tiles/gx, (c+1)*tiles/gx) and its 8 warps split the (tile, group)
+// items evenly; a warp range that starts inside tile T splits it there.
+__device__ inline int gemv_slice_start(int T, int s, int ks, int ng, int gx, int tiles) {
+    constexpr int NONE = 1 << 30;
+    if (ks > 1) return s < ks ? s * ng / ks : NONE;
+    if (s != 1 || gx <= 0) return NONE;
+    int c = int(int64_t(T) * gx / tiles);
+    while (c > 0 && int(int64_t(c) * tiles / gx) > T) --c;
+    while (c + 1 < gx && int(int64_t(c + 1) * tiles / gx) <= T) ++c;
+    const int t_lo = int(int64_t(c) * tiles / gx), t_hi = int(int64_t(c + 1) * tiles / gx);
+    const int nt = t_hi - t_lo;
+    if (nt < 8) return NONE;   // whole tiles per warp
+    const int items = nt * ng, local = (T - t_lo) * ng;
+    for (int w = 1; w < 8; ++w) {
+        const int i = w * items / 8;
+        if (i > local && i < local + ng) return i - local;
+    }
+    return NONE;
+}
+
 // Programmatic dependent launch: a kernel launched with
 // launch_pdl() may start while its predecessor on the stream is finishing.
 // It must call pdl_wait() before its first global-memory access (read or

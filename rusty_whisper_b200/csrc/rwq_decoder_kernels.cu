@@ -284,7 +284,7 @@ __global__ void __launch_bounds__(TC_WARPS * 32) k_attn_dec_tc(const float* __re
                        qo.d + size_t(st) * nbq + kb, qo.sum + size_t(st) * nbq + kb, qo.u + size_t(st) * nbq + kb);
         }
     };
-    const int D = H * HD, splits = int(gridDim.z), sp = int(blockIdx.z);
+    const int splits = int(gridDim.z), sp = int(blockIdx.z);
     pdl_wait();
     if (dpos) L = min(*dpos + 1, L);   // self-attention: keys 0..pos (L is the cache capacity)
     const int s0 = grp_off[gr], G = grp_off[gr + 1] - s0;

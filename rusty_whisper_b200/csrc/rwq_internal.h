@@ -27,6 +27,11 @@ struct Weight {
     uint16_t* bhl = nullptr;   // [n][nb][64]
     float* colscale = nullptr;
     bool fold_ready = false;
+    // TMA descriptors (CUtensorMap, 128 bytes each) of the qs, qh, d and m
+    // planes for k_gemv_rows, encoded when the weight is created;
+    // rows_ready is false where the plane layout does not allow them.
+    alignas(64) unsigned char row_maps[4][128] = {};
+    bool rows_ready = false;
 };
 
 // Scratch for one activation quantization (quantize_acts_i8 output).
@@ -60,10 +65,24 @@ cudaError_t launch_build_fold_cache(Weight& w, cudaStream_t s);
 cudaError_t launch_quantize_acts(const float* a, const ActsView& v, bool want_gemm, cudaStream_t s);
 cudaError_t launch_dequant_rows(const Weight& w, const int32_t* rows, int nrows, float* out, cudaStream_t s);
 cudaError_t launch_block_dots(const ActsView& v, const Weight& w, int32_t* S, cudaStream_t s);
-cudaError_t launch_gemv_i8(const ActsView& v, const Weight& w, const float* bias, float* y, cudaStream_t s);
-// GEMV kernel choice for the calling host thread: 0 auto (integer MMA),
-// 1 dp4a, 2 integer MMA.
+// err_flag (may be null) receives a code if a bounded wait of k_gemv_rows
+// expires.
+cudaError_t launch_gemv_i8(const ActsView& v, const Weight& w, const float* bias, float* y, cudaStream_t s,
+                           int* err_flag = nullptr);
+// GEMV kernel choice for the calling host thread: 0 auto, 1 dp4a, 2
+// integer MMA, 3 tiled integer MMA, 4 row-per-lane TMA kernel.
 void set_gemv_kind(int kind);
+// The kernel (1-4) launch_gemv_i8 runs for m rows on w with aligned codes.
+int gemv_kernel_for(const Weight& w, int m);
+// The row-per-lane GEMV (k_gemv_rows, one or two activation rows, weights
+// that k_gemv_mma runs without a K split): encode the plane descriptors
+// at weight creation; whether it can run these activations; the launch
+// (gx = k_gemv_mma's grid, whose tile split it reproduces).
+void prepare_gemv_rows(Weight& w);
+constexpr int GEMV_ROWS_MAX_M = 2;
+bool gemv_rows_fits(const ActsView& v, const Weight& w);
+cudaError_t launch_gemv_rows(const ActsView& v, const Weight& w, const float* bias, float* y, int gx,
+                             int* err_flag, cudaStream_t s);
 cudaError_t launch_gemv_f32(const float* a, int m, const Weight& w, const float* bias, float* y, cudaStream_t s);
 // tcgen05 GEMM.  S_dump (optional, small shapes) receives the per-block
 // integer dots read back from tensor memory.

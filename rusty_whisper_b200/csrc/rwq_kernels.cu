@@ -322,8 +322,6 @@ __device__ __forceinline__ void decode(const RawBlock<DT>& rb, BlockCodes<DT>& b
 //     acc <- fma(d_a*d_b, S, acc);  acc <- fma(d_a*sum(q_a), m_b, acc)
 // then an xor butterfly over the L lanes.  L and BPL depend on K only, so
 // every output row is bit-identical whatever M (quant.rs:1372-1384).
-constexpr uint32_t MAGIC_BITS = 0x4B400000u;  // 12582912.0f
-constexpr float MAGIC_F = 12582912.0f;
 
 template <int DT, int L, int BPL, int MR, int PF, bool REGA>
 __global__ void __launch_bounds__(TPB) k_gemv_i8(const uint8_t* __restrict__ qs, const uint32_t* __restrict__ qh,
@@ -955,29 +953,6 @@ __device__ __forceinline__ void cp_async16z(uint32_t dst, const void* src, bool 
 }
 __device__ __forceinline__ void cp_async4z(uint32_t dst, const void* src, bool ok) {
     asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(dst), "l"(src), "r"(ok ? 4 : 0) : "memory");
-}
-
-// Start of the s-th K slice (s >= 1) that k_gemv_mma uses for weight tile
-// T, or a value past every group if there is none.  KS > 1: slice s of the
-// group range starts at s*ng/KS.  KS == 1: k_gemv_mma's CTA c owns tiles
-// [c*tiles/gx, (c+1)*tiles/gx) and its 8 warps split the (tile, group)
-// items evenly; a warp range that starts inside tile T splits it there.
-__device__ inline int gemv_slice_start(int T, int s, int ks, int ng, int gx, int tiles) {
-    constexpr int NONE = 1 << 30;
-    if (ks > 1) return s < ks ? s * ng / ks : NONE;
-    if (s != 1 || gx <= 0) return NONE;
-    int c = int(int64_t(T) * gx / tiles);
-    while (c > 0 && int(int64_t(c) * tiles / gx) > T) --c;
-    while (c + 1 < gx && int(int64_t(c + 1) * tiles / gx) <= T) ++c;
-    const int t_lo = int(int64_t(c) * tiles / gx), t_hi = int(int64_t(c + 1) * tiles / gx);
-    const int nt = t_hi - t_lo;
-    if (nt < 8) return NONE;   // whole tiles per warp
-    const int items = nt * ng, local = (T - t_lo) * ng;
-    for (int w = 1; w < 8; ++w) {
-        const int i = w * items / 8;
-        if (i > local && i < local + ng) return i - local;
-    }
-    return NONE;
 }
 
 template <int DT, int WN, int NT, bool CL>
@@ -1843,22 +1818,30 @@ int gemv_rows_per_launch(int dtype, int k) {
     return r;
 }
 
-cudaError_t launch_gemv_i8(const ActsView& v, const Weight& w, const float* bias, float* y, cudaStream_t s) {
+// Kernel of one launch of the GEMV family for activations `c` (c.m <= 256):
+// 4 row-per-lane (one or two rows on a weight k_gemv_mma runs without a K
+// split: the wide ones), 3 tiled integer MMA (many rows; needs 16-byte
+// aligned activation codes), 2 integer MMA, 1 dp4a.  2, 3 and 4 give the
+// same bits, so the choice is a speed choice; the MMA kernels address the
+// planes with 32-bit offsets.
+int gemv_choice(const ActsView& c, const Weight& w) {
+    const int forced = t_gemv_kind;
+    if (forced == 1) return 1;
+    if ((forced == 0 || forced == 4) && c.m <= GEMV_ROWS_MAX_M && gemv_mma_ks(w.n, w.nb) == 1 && gemv_rows_fits(c, w))
+        return 4;
+    if (uint64_t(w.n) * uint64_t(round4(w.nb)) * uint64_t(qs_bytes(w.dtype)) >= (uint64_t(1) << 32)) return 1;
+    const bool tile_ok = (reinterpret_cast<uintptr_t>(c.q8) & 15) == 0;
+    if (forced == 3) return tile_ok ? 3 : 2;
+    if (forced == 2) return 2;
+    return tile_ok && c.m >= gemv_tile_min_m(w.n, w.nb) ? 3 : 2;
+}
+
+cudaError_t launch_gemv_i8(const ActsView& v, const Weight& w, const float* bias, float* y, cudaStream_t s,
+                           int* err_flag) {
     if (v.m <= 0 || w.n <= 0) return cudaSuccess;
-    // The integer-MMA kernel serves every m (one instruction per block for
-    // 16 x 8 dots, up to 64 rows per launch), so a row's result never
-    // depends on m; the dp4a kernel (8 rows per launch) is kept as an
-    // alternative (tests, benchmarks).  The MMA kernel addresses the planes
-    // with 32-bit offsets.
-    const int kind = t_gemv_kind ? t_gemv_kind : 2;
-    const bool mma = (kind == 2 || kind == 3) &&
-                     uint64_t(w.n) * uint64_t(round4(w.nb)) * uint64_t(qs_bytes(w.dtype)) < (uint64_t(1) << 32);
-    // The tiled kernel needs 16-byte aligned activation codes; it computes
-    // exactly what k_gemv_mma does, so the switch point is a speed choice.
-    const bool tile_ok = mma && (reinterpret_cast<uintptr_t>(v.q8) & 15) == 0;
-    // The MMA kernel takes all rows in one launch (CTA rows of up to 64
+    // The MMA kernels take up to 256 rows per launch (CTA rows of up to 64
     // activation rows share the weights through L2); dp4a launches 8 rows.
-    const int per = mma ? GEMV_FAMILY_MAX_M : GEMV_MAX_M;
+    const int per = gemv_choice(v, w) == 1 ? GEMV_MAX_M : GEMV_FAMILY_MAX_M;
     for (int m0 = 0; m0 < v.m; m0 += per) {
         ActsView c = v;
         c.m = v.m - m0 < per ? v.m - m0 : per;
@@ -1867,13 +1850,33 @@ cudaError_t launch_gemv_i8(const ActsView& v, const Weight& w, const float* bias
         c.sum = v.sum + size_t(m0) * v.nb;
         c.u = v.u + size_t(m0) * v.nb;
         float* yc = y + size_t(m0) * w.n;
-        const bool tile = tile_ok && (kind == 3 || (t_gemv_kind == 0 && c.m >= gemv_tile_min_m(w.n, w.nb)));
-        const cudaError_t e = tile  ? by_dtype<GemvTileF>(w.dtype, c, w, bias, yc, s)
-                              : mma ? by_dtype<GemvMmaF>(w.dtype, c, w, bias, yc, s)
-                                    : by_dtype<GemvI8F>(w.dtype, c, w, bias, yc, s);
+        cudaError_t e;
+        switch (gemv_choice(c, w)) {
+            case 4: {
+                int dev = 0, sms = 148;
+                dev_sms(&dev, &sms);
+                // k_gemv_mma's grid at KS == 1, whose tile split k_gemv_rows reproduces.
+                int gx = ((w.n + 15) / 16) / (GM_THREADS / 32);
+                gx = gx < 1 ? 1 : (gx > 2 * sms ? 2 * sms : gx);
+                e = launch_gemv_rows(c, w, bias, yc, gx, err_flag, s);
+                break;
+            }
+            case 3: e = by_dtype<GemvTileF>(w.dtype, c, w, bias, yc, s); break;
+            case 2: e = by_dtype<GemvMmaF>(w.dtype, c, w, bias, yc, s); break;
+            default: e = by_dtype<GemvI8F>(w.dtype, c, w, bias, yc, s); break;
+        }
         if (e != cudaSuccess) return e;
     }
     return cudaSuccess;
+}
+
+int gemv_kernel_for(const Weight& w, int m) {
+    ActsView c;
+    c.m = m;
+    c.k = w.k;
+    c.nb = w.nb;
+    c.q8 = reinterpret_cast<int8_t*>(uintptr_t(256));   // library-allocated codes are 256-byte aligned
+    return gemv_choice(c, w);
 }
 
 cudaError_t launch_gemv_f32(const float* a, int m, const Weight& w, const float* bias, float* y, cudaStream_t s) {

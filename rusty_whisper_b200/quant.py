@@ -303,10 +303,20 @@ def set_gemm_path(path: int) -> None:
 
 
 def set_gemv_kernel(kind: int) -> None:
-    """Kernel of the GEMV family (m <= 256): 0 automatic (integer MMA, tiled
-    from 32 rows on), 1 dp4a, 2 integer MMA only, 3 tiled integer MMA only.
-    Kinds 0, 2 and 3 give bit-identical results."""
+    """Kernel of the GEMV family (m <= 256): 0 automatic (row-per-lane at 1-2
+    rows on wide weights, integer MMA, tiled from 32 rows on), 1 dp4a, 2
+    integer MMA only, 3 tiled integer MMA only, 4 row-per-lane where it
+    applies.  Kinds 0, 2, 3 and 4 give bit-identical results."""
     _lib.check(_lib.lib().rwq_set_gemv_kernel(kind))
+
+
+def gemv_kernel_for(w: "QTensor", m: int) -> int:
+    """The GEMV kernel (1-4, as set_gemv_kernel) that an m-row call on `w`
+    runs under this thread's setting."""
+    r = _lib.lib().rwq_gemv_kernel_for(w._h, int(m))
+    if r < 0:
+        _lib.check(r)
+    return r
 
 
 def stream_check(stream=None) -> None:

@@ -189,6 +189,39 @@ def test_gemv_tile_bit_identical_to_mma(rq, dtype, k, n):
 
 
 @pytest.mark.parametrize("dtype", FORMATS)
+@pytest.mark.parametrize("k,n", [(1024, 51865), (1280, 19000), (256, 20001), (224, 19000), (5120, 19200)])
+def test_gemv_rows_bit_identical_to_mma(rq, orc, dtype, k, n):
+    """The row-per-lane GEMV (one weight row per lane, dp4a block dots, the
+    planes staged by TMA) reproduces the integer-MMA GEMV's summation order
+    -- blocks in kb order, and the head/tail split of the 16-row tiles that
+    two of its warps share -- so at one and two rows the two kernels give
+    identical bits; it is the automatic choice there on wide weights
+    (ragged N, pad blocks when K/32 is not a multiple of 4)."""
+    import torch
+    from rusty_whisper_b200 import synth
+    raw = synth.random_blocks(dtype, n, k, 7 * dtype + n + k)
+    w = rq.QTensor([n, k], dtype, raw)
+    bias = torch.from_numpy(synth.normal(5, n)).cuda()
+    a_np = synth.normal(60 + k, 2 * k).reshape(2, k)
+    a = cuda(a_np)
+    assert rq.gemv_kernel_for(w, 1) == 4 and rq.gemv_kernel_for(w, 2) == 4
+    assert rq.gemv_kernel_for(w, 3) == 2
+    try:
+        for m in (1, 2):
+            outs = []
+            for kind in (2, 4, 0):
+                rq.set_gemv_kernel(kind)
+                outs.append(rq.matmul_t_q(a[:m], w, bias=bias if m == 1 else None))
+            rq.stream_check()
+            assert torch.equal(outs[0].view(torch.int32), outs[1].view(torch.int32)), (m, "mma vs rows")
+            assert torch.equal(outs[0].view(torch.int32), outs[2].view(torch.int32)), (m, "mma vs auto")
+    finally:
+        rq.set_gemv_kernel(0)
+    y = host(outs[2])
+    assert close(y, orc.int8_scalar_matmul(a_np, dtype, raw, n)) < TOL
+
+
+@pytest.mark.parametrize("dtype", FORMATS)
 @pytest.mark.parametrize("m,k,n", [(1, 768, 768), (5, 256, 300), (20, 96, 41)])
 def test_matmul_f32_mode_matches_dequant_then_fp(rq, orc, dtype, m, k, n):
     a, raw = _case(dtype, m, k, n, 13 * dtype + m)
