@@ -662,8 +662,13 @@ def run_profile_driver(args):
             enc[w] = torch.from_numpy(synth.normal(300 + w % 8, 1500 * c["n_state"]).reshape(1500, c["n_state"]))
         dec.begin(enc, [w for w in range(n_win) for _ in range(per)])
         tok = torch.zeros(n_win * per, dtype=torch.int32, device=dev)
-        for _ in range(args.steps):
-            tok = dec.step(tok, want="best")
+        if args.only == "beam":   # config 4's benchmarked step: beam 5 (top-k, ranking, fork)
+            bs = decoder.BeamSearch(dec, n_win, per, limit=50257)   # end-of-text, as the benchmarked step
+            for _ in range(args.steps):
+                tok = bs.step(tok)
+        else:
+            for _ in range(args.steps):
+                tok = dec.step(tok, want="best")
     torch.cuda.synchronize()
     quant.stream_check()
     line = {"profile_driver": args.only, "m": args.m, "steps": args.steps}
@@ -903,10 +908,12 @@ def main():
                          "3 exact integer, 4 hi|lo")
     ap.add_argument("--m", type=int, default=1,
                     help="--only logits: activation rows; --only decode: 256 selects config 5's decoder")
-    ap.add_argument("--only", default="all", choices=["all", "gemm", "encoder", "decoder", "large", "logits", "gemv", "decode"],
+    ap.add_argument("--only", default="all", choices=["all", "gemm", "encoder", "decoder", "large", "logits", "gemv", "decode",
+                                                      "beam"],
                     help="gemm: only the config-2 GEMM sweep; encoder / decoder / large: only that leg; "
                          "logits: --steps launches of config 4's tied-logits GEMV at --m rows; decode: --steps "
-                         "config-4 decode steps, graphs off when RWQ_DECODER_GRAPHS=0 (short runs for profiling)")
+                         "config-4 decode steps, graphs off when RWQ_DECODER_GRAPHS=0 (short runs for profiling); "
+                         "beam: the same as config 4's beam-5 steps (top-k, ranking, fork)")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", 1))
@@ -923,7 +930,7 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local_rank))
     try:
-        if args.only in ("logits", "gemv", "decode"):
+        if args.only in ("logits", "gemv", "decode", "beam"):
             run_profile_driver(args)
             return
         if args.only in ("encoder", "decoder", "large"):

@@ -30,112 +30,220 @@ constexpr int TOPK_THREADS = 256;
 // (v, i) ranks before (bv, bi): larger value first, then smaller id.
 __device__ __forceinline__ bool better(float v, int i, float bv, int bi) { return v > bv || (v == bv && i < bi); }
 
-// One CTA per row.  Ids >= n are excluded (suppressed); -inf logits are
-// never chosen (the reference skips lp == -inf); rows with fewer than k
-// choosable ids get id -1 and lp -inf in the remaining places.
-__global__ void __launch_bounds__(TOPK_THREADS) k_beam_topk(const float* __restrict__ logits, int V, int n, int k,
+// Rows are split over a cluster of TOPK_CHUNKS CTAs (one chunk of the
+// first n ids each): every CTA finds its chunk's max m_c, s_c = sum of
+// exp(v - m_c) and top k; CTA 0 of the cluster reads the partials through
+// distributed shared memory, forms lse = M + ln(sum_c s_c exp(m_c - M))
+// (M = max m_c; transcribe.rs:482-486 with the sum split by chunk) and
+// merges the top k.  Ids >= n are excluded (suppressed); -inf and NaN
+// logits are never chosen (the reference skips lp == -inf); rows with
+// fewer than k choosable ids get id -1 and lp -inf in the remaining places.
+constexpr int TOPK_CHUNKS = 8;
+constexpr int NOID = 0x7fffffff;
+
+struct TopkPart {
+    float m, s;
+    float v[BEAM_MAX];
+    int i[BEAM_MAX];
+};
+
+// Pop the best of the lanes' sorted lists (heads tv[0], ti[0]) k times:
+// the result, best first, in every lane's ov/oi.  Ids are distinct, so the
+// butterfly agrees on one winner, whose lane shifts its list.
+template <int K>
+__device__ __forceinline__ void warp_topk(float (&tv)[K], int (&ti)[K], float (&ov)[K], int (&oi)[K]) {
+#pragma unroll
+    for (int r = 0; r < K; ++r) {
+        float bv = tv[0];
+        int bi = ti[0];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float v = __shfl_xor_sync(0xffffffffu, bv, o);
+            const int i = __shfl_xor_sync(0xffffffffu, bi, o);
+            if (i != NOID && (bi == NOID || better(v, i, bv, bi))) {
+                bv = v;
+                bi = i;
+            }
+        }
+        ov[r] = bv;
+        oi[r] = bi;
+        if (bi != NOID && ti[0] == bi) {
+#pragma unroll
+            for (int c = 0; c + 1 < K; ++c) {
+                tv[c] = tv[c + 1];
+                ti[c] = ti[c + 1];
+            }
+            tv[K - 1] = -INFINITY;
+            ti[K - 1] = NOID;
+        }
+    }
+}
+
+__device__ __forceinline__ uint32_t bk_mapa(const void* p, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(uint32_t(__cvta_generic_to_shared(p))), "r"(rank));
+    return r;
+}
+__device__ __forceinline__ float bk_ld_f(uint32_t a) {
+    float v;
+    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(a) : "memory");
+    return v;
+}
+__device__ __forceinline__ int bk_ld_i(uint32_t a) {
+    int v;
+    asm volatile("ld.shared::cluster.s32 %0, [%1];" : "=r"(v) : "r"(a) : "memory");
+    return v;
+}
+__device__ __forceinline__ void bk_cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+template <int K>
+__global__ void __launch_bounds__(TOPK_THREADS) k_beam_topk(const float* __restrict__ logits, int V, int n,
                                                           float* __restrict__ lp_out, int32_t* __restrict__ id_out) {
     pdl_trigger();
     pdl_wait();
-    const float* row = logits + size_t(blockIdx.x) * V;
+    const int c = int(blockIdx.x), r_row = int(blockIdx.y);
+    const float* row = logits + size_t(r_row) * V;
+    const int j0 = int(int64_t(c) * n / TOPK_CHUNKS), j1 = int(int64_t(c + 1) * n / TOPK_CHUNKS);
     const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
-    __shared__ float s_red[TOPK_THREADS / 32];
-    __shared__ float s_v[TOPK_THREADS * BEAM_MAX];
-    __shared__ int s_i[TOPK_THREADS * BEAM_MAX];
+    constexpr int NW = TOPK_THREADS / 32;
+    __shared__ float s_red[NW];
+    __shared__ float s_wv[NW][BEAM_MAX];
+    __shared__ int s_wi[NW][BEAM_MAX];
+    __shared__ TopkPart part;
     // max (NaN ignored, as f32::max folding from -inf)
     float mx = -INFINITY;
-    for (int j = t; j < n; j += TOPK_THREADS) mx = fmaxf(mx, row[j]);
+    for (int j = j0 + t; j < j1; j += TOPK_THREADS) mx = fmaxf(mx, row[j]);
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
     if (lane == 0) s_red[warp] = mx;
     __syncthreads();
     mx = s_red[0];
 #pragma unroll
-    for (int w = 1; w < TOPK_THREADS / 32; ++w) mx = fmaxf(mx, s_red[w]);
+    for (int w = 1; w < NW; ++w) mx = fmaxf(mx, s_red[w]);
     __syncthreads();
-    // sum of exp(v - max), then lse = max + ln(sum) (transcribe.rs:484)
+    // sum of exp(v - m_c) over the chunk (0 for a chunk without a finite max)
     float sum = 0.f;
-    for (int j = t; j < n; j += TOPK_THREADS) sum += expf(__fsub_rn(row[j], mx));
+    if (mx > -INFINITY)
+        for (int j = j0 + t; j < j1; j += TOPK_THREADS) sum += expf(__fsub_rn(row[j], mx));
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
     if (lane == 0) s_red[warp] = sum;
     __syncthreads();
     sum = 0.f;
 #pragma unroll
-    for (int w = 0; w < TOPK_THREADS / 32; ++w) sum += s_red[w];
-    const float lse = __fadd_rn(mx, logf(sum));
-    // this thread's best k, sorted
-    float tv[BEAM_MAX];
-    int ti[BEAM_MAX];
+    for (int w = 0; w < NW; ++w) sum += s_red[w];
+    // this thread's best k, sorted, then the warp's, then the CTA's
+    float tv[K], ov[K];
+    int ti[K], oi[K];
 #pragma unroll
-    for (int c = 0; c < BEAM_MAX; ++c) {
-        tv[c] = -INFINITY;
-        ti[c] = 0x7fffffff;
+    for (int q = 0; q < K; ++q) {
+        tv[q] = -INFINITY;
+        ti[q] = NOID;
     }
-    for (int j = t; j < n; j += TOPK_THREADS) {
-        const float v = row[j];
-        if (!(v > -INFINITY)) continue;   // -inf and NaN are never chosen
-        if (!better(v, j, tv[k - 1], ti[k - 1])) continue;
-        int c = k - 1;
-        while (c > 0 && better(v, j, tv[c - 1], ti[c - 1])) {
-            tv[c] = tv[c - 1];
-            ti[c] = ti[c - 1];
-            --c;
+    auto offer = [&](float v, int j) {
+        if (!(v > -INFINITY)) return;   // -inf and NaN are never chosen
+        if (ti[K - 1] != NOID && !better(v, j, tv[K - 1], ti[K - 1])) return;
+        // insert, keeping tv[0..K) sorted (registers: fixed-index moves)
+        bool placed = false;
+#pragma unroll
+        for (int q = K - 1; q >= 0; --q) {
+            if (placed) continue;
+            const bool above = q > 0 && (ti[q - 1] == NOID || better(v, j, tv[q - 1], ti[q - 1]));
+            if (above) {
+                tv[q] = tv[q - 1];
+                ti[q] = ti[q - 1];
+            } else {
+                tv[q] = v;
+                ti[q] = j;
+                placed = true;
+            }
         }
-        tv[c] = v;
-        ti[c] = j;
-    }
-    for (int c = 0; c < BEAM_MAX; ++c) {
-        s_v[t * BEAM_MAX + c] = c < k ? tv[c] : -INFINITY;
-        s_i[t * BEAM_MAX + c] = c < k ? ti[c] : 0x7fffffff;
-    }
-    __syncthreads();
-    // warp 0 merges: k rounds of a (value, id) arg-max over all lists
-    if (warp == 0) {
-        for (int r = 0; r < k; ++r) {
-            float bv = -INFINITY;
-            int bi = 0x7fffffff, bslot = -1;
-            for (int e = lane; e < TOPK_THREADS * BEAM_MAX; e += 32) {
-                const float v = s_v[e];
-                const int i = s_i[e];
-                if (i != 0x7fffffff && better(v, i, bv, bi)) {
-                    bv = v;
-                    bi = i;
-                    bslot = e;
-                }
-            }
+    };
+    for (int j = j0 + t; j < j1; j += TOPK_THREADS) offer(row[j], j);
+    warp_topk<K>(tv, ti, ov, oi);
+    if (lane == 0)
 #pragma unroll
-            for (int o = 16; o > 0; o >>= 1) {
-                const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-                const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-                const int os = __shfl_xor_sync(0xffffffffu, bslot, o);
-                if ((oi != 0x7fffffff && bi == 0x7fffffff) || (oi != 0x7fffffff && better(ov, oi, bv, bi))) {
-                    bv = ov;
-                    bi = oi;
-                    bslot = os;
-                }
+        for (int q = 0; q < K; ++q) {
+            s_wv[warp][q] = ov[q];
+            s_wi[warp][q] = oi[q];
+        }
+    __syncthreads();
+    if (warp == 0) {
+#pragma unroll
+        for (int q = 0; q < K; ++q) {
+            tv[q] = lane < NW ? s_wv[lane][q] : -INFINITY;
+            ti[q] = lane < NW ? s_wi[lane][q] : NOID;
+        }
+        warp_topk<K>(tv, ti, ov, oi);
+        if (lane == 0) {
+            part.m = mx;
+            part.s = sum;
+#pragma unroll
+            for (int q = 0; q < K; ++q) {
+                part.v[q] = ov[q];
+                part.i[q] = oi[q];
             }
-            if (lane == 0) {
-                const size_t o = size_t(blockIdx.x) * k + r;
-                if (bslot >= 0) {
-                    lp_out[o] = __fsub_rn(bv, lse);
-                    id_out[o] = bi;
-                    s_i[bslot] = 0x7fffffff;   // taken
+        }
+    }
+    bk_cluster_sync();
+    if (c == 0 && warp == 0) {
+        // lane q < TOPK_CHUNKS reads chunk q's partial
+        float m_c = -INFINITY, s_c = 0.f;
+#pragma unroll
+        for (int q = 0; q < K; ++q) {
+            tv[q] = -INFINITY;
+            ti[q] = NOID;
+        }
+        if (lane < TOPK_CHUNKS) {
+            m_c = bk_ld_f(bk_mapa(&part.m, lane));
+            s_c = bk_ld_f(bk_mapa(&part.s, lane));
+#pragma unroll
+            for (int q = 0; q < K; ++q) {
+                tv[q] = bk_ld_f(bk_mapa(&part.v[q], lane));
+                ti[q] = bk_ld_i(bk_mapa(&part.i[q], lane));
+            }
+        }
+        float M = m_c;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+        // sum in chunk order
+        float S = 0.f;
+#pragma unroll
+        for (int q = 0; q < TOPK_CHUNKS; ++q) {
+            const float mq = __shfl_sync(0xffffffffu, m_c, q), sq = __shfl_sync(0xffffffffu, s_c, q);
+            if (sq > 0.f) S = __fadd_rn(S, __fmul_rn(sq, expf(__fsub_rn(mq, M))));
+        }
+        const float lse = __fadd_rn(M, logf(S));
+        warp_topk<K>(tv, ti, ov, oi);
+        if (lane == 0) {
+#pragma unroll
+            for (int q = 0; q < K; ++q) {
+                const size_t o = size_t(r_row) * K + q;
+                if (oi[q] != NOID) {
+                    lp_out[o] = __fsub_rn(ov[q], lse);
+                    id_out[o] = oi[q];
                 } else {
                     lp_out[o] = -INFINITY;
                     id_out[o] = -1;
                 }
             }
-            __syncwarp();
         }
     }
+    bk_cluster_sync();   // the partials stay readable until CTA 0 is done
 }
 
-// One thread per window (<= 64 candidates).  Streams of window w are
-// w*B .. w*B + B - 1; the live beams are the slots whose rank is below
-// n_live, visited in rank order (the reference's beam order), each with
-// its k candidates in top-k order; a stable sort by score keeps that
-// order among equal scores (Rust's sort_by, transcribe.rs:924).
+// One warp per window (<= 64 candidates: beams x k <= 8 x 8, two per
+// lane).  Streams of window w are w*B .. w*B + B - 1; the live beams are
+// the slots whose rank is below n_live, visited in rank order (the
+// reference's beam order), each with its k candidates in top-k order;
+// candidate e = (beam order q)*k + j.  A candidate's place in the stable
+// sort by score (Rust's sort_by, transcribe.rs:924) is the number of valid
+// candidates with a higher score or an equal score and a smaller e.
+// Survivors take stream slots: the best survivor of each parent stays in
+// the parent's slot; the others take, in survivor order, the slots no
+// survivor descends from, in slot order.
 __global__ void k_beam_select(const float* __restrict__ lp, const int32_t* __restrict__ id, int k,
                               const float* __restrict__ sum_in, const int32_t* __restrict__ rank_in, int W, int B,
                               int n_live, int32_t* __restrict__ src, int32_t* __restrict__ tok,
@@ -143,88 +251,158 @@ __global__ void k_beam_select(const float* __restrict__ lp, const int32_t* __res
                               int32_t* __restrict__ rank_out) {
     pdl_trigger();
     pdl_wait();
-    const int w = blockIdx.x * blockDim.x + threadIdx.x;
-    if (w >= W) return;
+    const int lane = threadIdx.x & 31;
+    const int w = int(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (w >= W) return;   // whole warps leave together
     const int s0 = w * B;
-    int order[BEAM_MAX];
-    int nb = 0;
-    for (int r = 0; r < n_live; ++r)
+    // slot of beam-order position q (lanes q < n_live), broadcast below
+    int slot_q = -1;
+    if (lane < n_live)
         for (int b = 0; b < B; ++b)
-            if ((rank_in ? rank_in[s0 + b] : b) == r) {
-                order[nb++] = b;
+            if ((rank_in ? rank_in[s0 + b] : b) == lane) {
+                slot_q = b;
                 break;
             }
-    float score[BEAM_MAX * BEAM_MAX], slp[BEAM_MAX * BEAM_MAX];
-    int par[BEAM_MAX * BEAM_MAX], cid[BEAM_MAX * BEAM_MAX];
-    int nc = 0;
-    for (int q = 0; q < nb; ++q) {
-        const int b = order[q];
-        for (int j = 0; j < k; ++j) {
-            const int i = id[size_t(s0 + b) * k + j];
-            if (i < 0) continue;
-            const float st = fmaxf(lp[size_t(s0 + b) * k + j], -30.0f);
-            const float sc = __fadd_rn(sum_in ? sum_in[s0 + b] : 0.f, st);
-            int c = nc++;
-            while (c > 0 && score[c - 1] < sc) {   // stable: equal scores keep their order
-                score[c] = score[c - 1];
-                slp[c] = slp[c - 1];
-                par[c] = par[c - 1];
-                cid[c] = cid[c - 1];
-                --c;
+    // two candidates per lane: e = lane and e = lane + 32
+    float sc[2], st[2];
+    int par[2], cid[2];
+    bool ok[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        const int e = lane + 32 * h, q = e / k, jj = e % k;
+        const int b = __shfl_sync(0xffffffffu, slot_q, q < 32 ? q : 0);
+        ok[h] = e < n_live * k && q < n_live && b >= 0;
+        sc[h] = st[h] = 0.f;
+        par[h] = cid[h] = 0;
+        if (ok[h]) {
+            const int i = id[size_t(s0 + b) * k + jj];
+            ok[h] = i >= 0;
+            st[h] = fmaxf(lp[size_t(s0 + b) * k + jj], -30.0f);
+            sc[h] = __fadd_rn(sum_in ? sum_in[s0 + b] : 0.f, st[h]);
+            par[h] = b;
+            cid[h] = i;
+        }
+    }
+    // stable rank among the valid candidates
+    int rk[2] = {0, 0};
+#pragma unroll
+    for (int h2 = 0; h2 < 2; ++h2) {
+        for (int l2 = 0; l2 < 32; ++l2) {
+            const float o_sc = __shfl_sync(0xffffffffu, sc[h2], l2);
+            const bool o_ok = __shfl_sync(0xffffffffu, ok[h2] ? 1 : 0, l2) != 0;
+            const int oe = l2 + 32 * h2;
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const int e = lane + 32 * h;
+                if (o_ok && (o_sc > sc[h] || (o_sc == sc[h] && oe < e))) ++rk[h];
             }
-            score[c] = sc;
-            slp[c] = st;
-            par[c] = b;
-            cid[c] = i;
         }
     }
-    const int nsel = nc < B ? nc : B;
-    // Slots: the first survivor of each parent stays in the parent's slot;
-    // the others take the slots no survivor descends from.
-    int slot_of[BEAM_MAX];
-    bool used[BEAM_MAX], parent[BEAM_MAX];
-    for (int b = 0; b < B; ++b) used[b] = parent[b] = false;
-    for (int c = 0; c < nsel; ++c) parent[par[c]] = true;
-    for (int c = 0; c < nsel; ++c) {
-        slot_of[c] = -1;
-        if (!used[par[c]]) {
-            slot_of[c] = par[c];
-            used[par[c]] = true;
+    const int nvalid = __popc(__ballot_sync(0xffffffffu, ok[0])) + __popc(__ballot_sync(0xffffffffu, ok[1]));
+    const int nsel = nvalid < B ? nvalid : B;
+    // survivors' parents; keepers: no better survivor of the same parent
+    unsigned parent_mask = 0;
+    bool surv[2], keep[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) surv[h] = ok[h] && rk[h] < nsel;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        unsigned m = __ballot_sync(0xffffffffu, surv[h]);
+        for (unsigned mm = m; mm; mm &= mm - 1) parent_mask |= 1u << __shfl_sync(0xffffffffu, par[h], __ffs(mm) - 1);
+    }
+#pragma unroll
+    for (int h = 0; h < 2; ++h) keep[h] = surv[h];
+#pragma unroll
+    for (int h2 = 0; h2 < 2; ++h2)
+        for (int l2 = 0; l2 < 32; ++l2) {
+            const bool o_s = __shfl_sync(0xffffffffu, surv[h2] ? 1 : 0, l2) != 0;
+            const int o_p = __shfl_sync(0xffffffffu, par[h2], l2), o_r = __shfl_sync(0xffffffffu, rk[h2], l2);
+#pragma unroll
+            for (int h = 0; h < 2; ++h)
+                if (o_s && o_p == par[h] && o_r < rk[h]) keep[h] = false;
         }
+    const unsigned all = (1u << B) - 1u;
+    const unsigned free_mask = all & ~parent_mask;
+    // keepers stay in their parent's slot; the m-th non-keeper (by rank)
+    // takes the m-th free slot
+    int slot[2] = {-1, -1}, m_nk[2] = {0, 0};
+    unsigned used = 0;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        if (keep[h]) slot[h] = par[h];
+        const unsigned km = __ballot_sync(0xffffffffu, keep[h]);
+        for (unsigned mm = km; mm; mm &= mm - 1) used |= 1u << __shfl_sync(0xffffffffu, par[h], __ffs(mm) - 1);
     }
-    int next_free = 0;
-    for (int c = 0; c < nsel; ++c) {
-        if (slot_of[c] >= 0) continue;
-        while (next_free < B && (used[next_free] || parent[next_free])) ++next_free;
-        slot_of[c] = next_free;
-        used[next_free] = true;
+#pragma unroll
+    for (int h2 = 0; h2 < 2; ++h2)
+        for (int l2 = 0; l2 < 32; ++l2) {
+            const bool o_nk = __shfl_sync(0xffffffffu, (surv[h2] && !keep[h2]) ? 1 : 0, l2) != 0;
+            const int o_r = __shfl_sync(0xffffffffu, rk[h2], l2);
+#pragma unroll
+            for (int h = 0; h < 2; ++h)
+                if (o_nk && o_r < rk[h]) ++m_nk[h];
+        }
+#pragma unroll
+    for (int h = 0; h < 2; ++h)
+        if (surv[h] && !keep[h]) {
+            unsigned fm = free_mask;
+            for (int q = 0; q < m_nk[h]; ++q) fm &= fm - 1;
+            slot[h] = __ffs(fm) - 1;
+        }
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        const unsigned nm = __ballot_sync(0xffffffffu, surv[h] && !keep[h]);
+        for (unsigned mm = nm; mm; mm &= mm - 1) used |= 1u << __shfl_sync(0xffffffffu, slot[h], __ffs(mm) - 1);
     }
-    for (int c = 0; c < nsel; ++c) {
-        const int s = s0 + slot_of[c];
-        src[s] = s0 + par[c];
-        tok[s] = cid[c];
-        sum_out[s] = score[c];
-        step_out[s] = slp[c];
-        rank_out[s] = c;
-    }
+#pragma unroll
+    for (int h = 0; h < 2; ++h)
+        if (surv[h]) {
+            const int sI = s0 + slot[h];
+            src[sI] = s0 + par[h];
+            tok[sI] = cid[h];
+            sum_out[sI] = sc[h];
+            step_out[sI] = st[h];
+            rank_out[sI] = rk[h];
+        }
     // Fewer candidates than beams (a row with fewer than k choosable ids):
     // the remaining slots repeat the best survivor, ranked last.
-    int extra = nsel;
-    for (int b = 0; b < B; ++b) {
-        if (used[b]) continue;
-        const int s = s0 + b;
-        if (nsel == 0) {
-            src[s] = s;
-            tok[s] = 0;
-            sum_out[s] = -INFINITY;
-            step_out[s] = -INFINITY;
-        } else {
-            src[s] = s0 + par[0];
-            tok[s] = cid[0];
-            sum_out[s] = score[0];
-            step_out[s] = slp[0];
+    if (nsel < B) {
+        int best_lane = -1, best_h = 0;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const unsigned bm = __ballot_sync(0xffffffffu, surv[h] && rk[h] == 0);
+            if (bm) {
+                best_lane = __ffs(bm) - 1;
+                best_h = h;
+            }
         }
-        rank_out[s] = extra++;
+        float b_sc = -INFINITY, b_st = -INFINITY;
+        int b_par = 0, b_cid = 0;
+        if (best_lane >= 0) {
+            b_sc = __shfl_sync(0xffffffffu, best_h ? sc[1] : sc[0], best_lane);
+            b_st = __shfl_sync(0xffffffffu, best_h ? st[1] : st[0], best_lane);
+            b_par = __shfl_sync(0xffffffffu, best_h ? par[1] : par[0], best_lane);
+            b_cid = __shfl_sync(0xffffffffu, best_h ? cid[1] : cid[0], best_lane);
+        }
+        if (lane == 0) {
+            int extra = nsel;
+            for (int b = 0; b < B; ++b) {
+                if (used & (1u << b)) continue;
+                const int sI = s0 + b;
+                if (nsel == 0) {
+                    src[sI] = sI;
+                    tok[sI] = 0;
+                    sum_out[sI] = -INFINITY;
+                    step_out[sI] = -INFINITY;
+                } else {
+                    src[sI] = s0 + b_par;
+                    tok[sI] = b_cid;
+                    sum_out[sI] = b_sc;
+                    step_out[sI] = b_st;
+                }
+                rank_out[sI] = extra++;
+            }
+        }
     }
 }
 
@@ -280,10 +458,24 @@ int rwq_beam_topk(const float* logits, int64_t rows, int64_t n_vocab, int32_t li
                           (long long)n_vocab, k, rwq::BEAM_MAX);
     if (rows == 0) return RWQ_OK;
     if (!logits || !lp || !id) return rwq::bfail(RWQ_ERR_ARG, "rwq_beam_topk: null pointer");
-    if (rows > (1 << 24)) return rwq::bfail(RWQ_ERR_ARG, "rwq_beam_topk: too many rows");
     const int n = (limit >= 0 && limit < n_vocab) ? int(limit) : int(n_vocab);
-    cudaError_t e = rwq::launch_pdl(rwq::k_beam_topk, dim3(unsigned(rows)), dim3(rwq::TOPK_THREADS), 0,
-                                    static_cast<cudaStream_t>(stream), logits, int(n_vocab), n, k, lp, id);
+    if (rows > 65535) return rwq::bfail(RWQ_ERR_ARG, "rwq_beam_topk: too many rows");
+    auto go = [&](auto kern) {
+        return rwq::launch_pdl_cluster(kern, dim3(rwq::TOPK_CHUNKS, unsigned(rows)), dim3(rwq::TOPK_THREADS), 0,
+                                       rwq::TOPK_CHUNKS, static_cast<cudaStream_t>(stream), logits, int(n_vocab), n,
+                                       lp, id);
+    };
+    cudaError_t e;
+    switch (k) {
+        case 1: e = go(rwq::k_beam_topk<1>); break;
+        case 2: e = go(rwq::k_beam_topk<2>); break;
+        case 3: e = go(rwq::k_beam_topk<3>); break;
+        case 4: e = go(rwq::k_beam_topk<4>); break;
+        case 5: e = go(rwq::k_beam_topk<5>); break;
+        case 6: e = go(rwq::k_beam_topk<6>); break;
+        case 7: e = go(rwq::k_beam_topk<7>); break;
+        default: e = go(rwq::k_beam_topk<8>); break;
+    }
     if (e != cudaSuccess) return rwq::bfail(RWQ_ERR_CUDA, "rwq_beam_topk: %s", cudaGetErrorString(e));
     return RWQ_OK;
 }
@@ -298,8 +490,8 @@ int rwq_beam_select(const float* lp, const int32_t* id, int k, const float* sum_
     if (n_windows == 0) return RWQ_OK;
     if (!lp || !id || !src || !token || !sum_out || !step_lp || !rank_out)
         return rwq::bfail(RWQ_ERR_ARG, "rwq_beam_select: null pointer");
-    const unsigned blocks = unsigned((n_windows + 63) / 64);
-    cudaError_t e = rwq::launch_pdl(rwq::k_beam_select, dim3(blocks), dim3(64), 0, static_cast<cudaStream_t>(stream),
+    const unsigned blocks = unsigned((n_windows + 3) / 4);   // a warp per window
+    cudaError_t e = rwq::launch_pdl(rwq::k_beam_select, dim3(blocks), dim3(128), 0, static_cast<cudaStream_t>(stream),
                                     lp, id, k, sum_lp, rank, int(n_windows), beams, n_live, src, token, sum_out,
                                     step_lp, rank_out);
     if (e != cudaSuccess) return rwq::bfail(RWQ_ERR_CUDA, "rwq_beam_select: %s", cudaGetErrorString(e));

@@ -132,6 +132,116 @@ def test_topk_matches_reference(torch_mod):
             assert all(ids[r, len(want):] == -1) and all(np.isneginf(lp[r, len(want):]))
 
 
+def test_topk_vocab_rows_chunk_ties(torch_mod):
+    """Rows of a whisper vocabulary (split over the kernel's chunks), with
+    the maximum repeated across chunk boundaries: equal values rank by the
+    smaller id, as the reference's stable sort does."""
+    from rusty_whisper_b200 import decoder, synth
+    n_v = 51865
+    lg = synth.normal(6, 5 * n_v).reshape(5, n_v) * np.float32(3.0)
+    lg[1, ::997] = np.float32(40.0)          # 53 equal maxima spread over every chunk
+    lg[3, 6400:6560] = np.float32(30.0)      # a run of ties straddling a chunk boundary
+    lg[4, :] = np.float32(1.0)               # all equal
+    for k, limit in ((5, 50257), (8, -1), (3, 6500)):
+        lp, ids = decoder.beam_topk(torch_mod.from_numpy(lg).cuda(), k, limit)
+        lp, ids = lp.cpu().numpy(), ids.cpu().numpy()
+        for r in range(5):
+            row = lg[r, :limit] if limit >= 0 else lg[r]
+            want = _top_k(_log_softmax(row), k)
+            assert [int(i) for i in ids[r, :len(want)]] == [i for _, i in want], (k, r)
+            assert np.allclose(lp[r, :len(want)], [v for v, _ in want], rtol=0, atol=2e-5)
+
+
+def _select_ref(lp, ids, k, sum_in, rank_in, W, B, n_live):
+    """transcribe.rs:890-925 for each window (candidates of the live beams
+    in rank order, each beam's in top-k order, scored sum + max(lp, -30),
+    stable sort, best B kept), with the slot rule of rwq_beam_select: the
+    best survivor of each parent keeps the parent's slot, the others take
+    the slots no survivor descends from in slot order, and slots left over
+    repeat the best survivor ranked last."""
+    S = W * B
+    src, tok = np.zeros(S, np.int64), np.zeros(S, np.int64)
+    sm, stp, rk = np.zeros(S, np.float32), np.zeros(S, np.float32), np.zeros(S, np.int64)
+    for w in range(W):
+        s0 = w * B
+        order = []
+        for r in range(n_live):
+            for b in range(B):
+                if (rank_in[s0 + b] if rank_in is not None else b) == r:
+                    order.append(b)
+                    break
+        cands = []
+        for b in order:
+            for j in range(k):
+                i = int(ids[s0 + b, j])
+                if i < 0:
+                    continue
+                st = np.float32(max(np.float32(lp[s0 + b, j]), np.float32(-30.0)))
+                sc = np.float32(np.float32(sum_in[s0 + b] if sum_in is not None else 0.0) + st)
+                cands.append((sc, st, b, i))
+        cands.sort(key=lambda c: -float(c[0]))
+        sel = cands[:B]
+        parents = {c[2] for c in sel}
+        used, slots = set(), []
+        for c in sel:
+            if c[2] not in used:
+                slots.append(c[2])
+                used.add(c[2])
+            else:
+                slots.append(None)
+        free = [b for b in range(B) if b not in parents]
+        for n, c in enumerate(sel):
+            if slots[n] is None:
+                slots[n] = free.pop(0)
+                used.add(slots[n])
+        for n, (c, b) in enumerate(zip(sel, slots)):
+            src[s0 + b], tok[s0 + b], sm[s0 + b], stp[s0 + b], rk[s0 + b] = s0 + c[2], c[3], c[0], c[1], n
+        extra = len(sel)
+        for b in range(B):
+            if b in used:
+                continue
+            if sel:
+                c = sel[0]
+                src[s0 + b], tok[s0 + b], sm[s0 + b], stp[s0 + b] = s0 + c[2], c[3], c[0], c[1]
+            else:
+                src[s0 + b], tok[s0 + b], sm[s0 + b], stp[s0 + b] = s0 + b, 0, -np.inf, -np.inf
+            rk[s0 + b] = extra
+            extra += 1
+    return src, tok, sm, stp, rk
+
+
+@pytest.mark.parametrize("W,B,k,n_live", [(16, 5, 5, 5), (3, 8, 8, 8), (4, 3, 1, 2), (5, 5, 5, 1), (2, 6, 4, 6)])
+def test_beam_select_matches_reference(torch_mod, W, B, k, n_live):
+    """rwq_beam_select against the reference's ranking on crafted
+    candidates: tied scores (stable order), invalid ids (-1: fewer
+    candidates than beams), permuted beam ranks, -30 clamping."""
+    import ctypes
+    from rusty_whisper_b200 import _lib
+    torch = torch_mod
+    rng = np.random.default_rng(W * 100 + B * 10 + k)
+    S = W * B
+    lp = np.round(rng.normal(-3, 2, (S, k)) * 4) / np.float32(4)          # many exact ties
+    lp[rng.random((S, k)) < 0.1] = np.float32(-45.0)                       # clamped to -30
+    ids = rng.integers(0, 50000, (S, k)).astype(np.int32)
+    ids[rng.random((S, k)) < 0.15] = -1
+    if W > 2:
+        ids[2 * B:3 * B] = -1                                              # a window with no candidate
+    sum_in = (np.round(rng.normal(-10, 3, S) * 2) / 2).astype(np.float32)
+    rank_in = np.concatenate([rng.permutation(B) for _ in range(W)]).astype(np.int32)
+    lp = np.ascontiguousarray(lp.astype(np.float32))
+    dev = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()     # noqa: E731
+    g_lp, g_id, g_sum, g_rank = dev(lp), dev(ids), dev(sum_in), dev(rank_in)
+    outs = [torch.zeros(S, dtype=dt, device="cuda") for dt in (torch.int32, torch.int32, torch.float32,
+                                                              torch.float32, torch.int32)]
+    p = lambda t: ctypes.c_void_p(t.data_ptr())                            # noqa: E731
+    _lib.check(_lib.lib().rwq_beam_select(p(g_lp), p(g_id), k, p(g_sum), p(g_rank), W, B, n_live,
+                                          *[p(o) for o in outs], ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)))
+    got = [o.cpu().numpy() for o in outs]
+    want = _select_ref(lp, ids, k, sum_in, rank_in, W, B, n_live)
+    for g, wv, name in zip(got, want, ("src", "tok", "sum", "step_lp", "rank")):
+        assert np.array_equal(g.astype(np.float64), np.asarray(wv, np.float64)), name
+
+
 def test_beam_search_device_matches_reference_algorithm(torch_mod):
     from rusty_whisper_b200 import decoder
     W, B, steps, limit = 2, 3, 12, 1990
