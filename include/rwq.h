@@ -355,7 +355,7 @@ int rwq_decoder_fork(rwq_decoder* d, const int32_t* src, void* stream);
  * logits[rows][n_vocab] (device): ids >= limit are excluded like
  * suppressed tokens (limit < 0: none), -inf logits are never chosen; lp
  * [rows][k] descending with id [rows][k] (-1 / -inf past the choosable
- * ids); 1 <= k <= 8.  Ties in value are ordered by id. */
+ * ids); 1 <= k <= 8, rows <= 65535.  Ties in value are ordered by id. */
 int rwq_beam_topk(const float* logits, int64_t rows, int64_t n_vocab, int32_t limit, int k, float* lp, int32_t* id,
                   void* stream);
 
