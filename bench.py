@@ -237,6 +237,7 @@ def run_ours(args, rank, world, local_rank):
         by_fmt[NAMES[dt]][1] += a.elapsed_time(b) / r / 1e3
     by_fmt = {f: round(o / t / 1e12, 2) for f, (o, t) in by_fmt.items()}
 
+    config1 = run_config1(args, dev, quant, stream, rank, world) if args.only == "all" else None
     gemv = run_gemv(args, dev, quant, w_np, hbm_peak, stream) if args.only == "all" else None
     e2e = run_e2e(args, dev, quant, W, acts_np, world) if args.only == "all" else None
     frontend = run_frontend(args, dev, hbm_peak, stream, rank, world) if args.only == "all" else None
@@ -265,6 +266,7 @@ def run_ours(args, rank, world, local_rank):
             "traffic_launch": "ncu, Q4_0 M=1500 K=768 N=3072 launch (profiles/)",
             "per_format_tops": by_fmt,
         },
+        "config1": config1,
         "gemv": gemv,
         "frontend": frontend,
         "encoder": enc,
@@ -789,6 +791,81 @@ def gemv_logits(args, dev, quant, hbm_peak, stream):
         b = n * (k // QK) * block_bytes(dt) + 4.0 * mm * k + 4.0 * mm * n
         out[f"M={mm}"] = {"GB/s": round(b / t / 1e9, 1), "frac_of_measured_hbm": round(b / t / 1e9 / hbm_peak, 4),
                           "us": round(t * 1e6, 2), "kernel": GEMV_KERNELS[quant.gemv_kernel_for(Wl[0], mm)]}
+    return out
+
+
+def run_config1(args, dev, quant, stream, rank, world):
+    """BASELINE config 1 on its own seed-0 inputs: Q8_0 W[1536x384],
+    X[1500x384] ~ N(0,1), one matmul_t_q (quantizer + tensor-core GEMM).
+    Device-resident: R back-to-back calls between one event pair, L2
+    flushed before each batch; end to end: the host-buffer entry point
+    (pinned X in, Y out)."""
+    import torch
+    import torch.distributed as dist
+    x_np, raw = synth.config1_inputs(0)
+    m, k, n = 1500, 384, 1536
+    w = quant.QTensor([n, k], 8, raw)
+    w.prepare_gemm()
+    x = torch.from_numpy(x_np).to(dev)
+    y = torch.empty((m, n), dtype=torch.float32, device=dev)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    R = 20
+    for _ in range(5):
+        quant.matmul_t_q(x, w, out=y)
+    torch.cuda.synchronize()
+    times = []
+    for _ in range(max(args.steps // 4, 3)):
+        flush.zero_()
+        torch.cuda._sleep(GATE_CYCLES)
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(R):
+            quant.matmul_t_q(x, w, out=y)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        times.append(e0.elapsed_time(e1) / 1e3 / R)
+    quant.stream_check()
+    t = statistics.median(times)
+    ops = 2.0 * m * n * k
+    # end to end through the host-buffer call
+    xp = torch.from_numpy(x_np).pin_memory()
+    yp = torch.empty((m, n), dtype=torch.float32).pin_memory()
+    for _ in range(3):
+        quant.matmul_t_q(xp.numpy(), w, out=yp.numpy())
+    reps = 20
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        quant.matmul_t_q(xp.numpy(), w, out=yp.numpy())
+    te = (time.perf_counter() - t0) / reps
+    if world > 1:
+        tt = torch.tensor([t, te], dtype=torch.float64, device=dev)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        t, te = (float(v) for v in tt.tolist())
+    out = {"workload": "BASELINE config 1: Q8_0 W[1536x384] (d~U(0.001,0.02), q~U[-127,127]), X[1500x384] ~ N(0,1), "
+                       "seed 0; one matmul_t_q (int8 activation quantizer + GEMM)",
+           "TOPS": round(world * ops / t / 1e12, 2), "us_per_matmul": round(t * 1e6, 2),
+           "e2e": {"TOPS": round(world * ops / te / 1e12, 3), "us_per_call": round(te * 1e6, 1),
+                   "h2d_bytes": m * k * 4, "d2h_bytes": m * n * 4,
+                   "api": "rwq_matmul_t_q (pinned host buffers, synchronous)"},
+           "kernels": "k_quantize + k_gemm_fold", "gpu_launches_per_matmul": 2,
+           "l2": "256 MiB written before every batch of 20 calls"}
+    if rank == 0 and world == 1 and not args.no_cpu:
+        import oracle
+        oracle.lib()
+        threads = oracle.default_threads()
+        oracle.matmul_t_q(x_np, 8, raw, n, tier=oracle.TIER_AUTO, threads=threads, packed=False)
+        reps, t0 = 0, time.perf_counter()
+        while reps < 3 or time.perf_counter() - t0 < 3.0:
+            oracle.matmul_t_q(x_np, 8, raw, n, tier=oracle.TIER_AUTO, threads=threads, packed=False)
+            reps += 1
+            if reps >= 50:
+                break
+        tc = (time.perf_counter() - t0) / reps
+        out["cpu_baseline"] = {"TOPS": round(ops / tc / 1e12, 4), "ms_per_matmul": round(tc * 1e3, 2),
+                               "cores": threads, "kind": "port",
+                               "tier": oracle.TIER_NAMES[oracle.dispatch_tier()],
+                               "sample": f"{reps} calls of the same matmul (reference's first-call path)"}
     return out
 
 

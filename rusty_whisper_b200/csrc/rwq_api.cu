@@ -597,8 +597,8 @@ int rwq_matmul_t_q(const float* a, int64_t m, int64_t k, const rwq_qtensor* b, c
     // GEMM-family calls (m > 256 and no forced path) run in row chunks of
     // more than 256 rows, so every chunk stays in the family and the results
     // are those of one call (each output row's sum does not depend on which
-    // other rows share the GEMM as long as the K split is the same; the
-    // K split is picked from the chunk's tile count, see k_gemm_hl): the upload of chunk c+1, the matmul of chunk c
+    // other rows share the GEMM as long as the kernel and its K split are
+    // the same; both are picked from the tile count): the upload of chunk c+1, the matmul of chunk c
     // and the download of chunk c-1 overlap (PCIe is full duplex).  With
     // pageable host buffers the copies still work, without the overlap.
     const int chunks = (t_gemm_path == 0) ? int(std::min<int64_t>(6, m / 257)) : 1;
@@ -610,12 +610,19 @@ int rwq_matmul_t_q(const float* a, int64_t m, int64_t k, const rwq_qtensor* b, c
     } else {
         CopyPipe* cp = nullptr;
         if ((rc = copy_pipe(&cp))) return rc;
-        // Every chunk runs with the K split of the whole call, so the
-        // chunks give the bits of one device call.
+        // Every chunk runs with the kernel and K split of the whole call,
+        // so the chunks give the bits of one device call.
         struct KsplitGuard {
-            explicit KsplitGuard(int S) { rwq::set_gemm_hl_ksplit(S); }
-            ~KsplitGuard() { rwq::set_gemm_hl_ksplit(0); }
-        } ks_guard(rwq::gemm_hl_ksplit(int(m), int(n), int(k / rwq::QK)));
+            KsplitGuard(int S, int fold) {
+                rwq::set_gemm_hl_ksplit(S);
+                rwq::set_gemm_fold_config(fold);
+            }
+            ~KsplitGuard() {
+                rwq::set_gemm_hl_ksplit(0);
+                rwq::set_gemm_fold_config(0);
+            }
+        } ks_guard(rwq::gemm_hl_ksplit(int(m), int(n), int(k / rwq::QK)),
+                   rwq::gemm_fold_config(int(m), int(n), int(k / rwq::QK)));
         RWQ_CUDA(cudaEventRecord(cp->ev_in, s), "event");
         RWQ_CUDA(cudaStreamWaitEvent(cp->up, cp->ev_in, 0), "event wait");
         RWQ_CUDA(cudaStreamWaitEvent(cp->down, cp->ev_in, 0), "event wait");

@@ -300,6 +300,273 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
 }
 
+// ------------------------------------------------------------- wide tiles
+// k_gemm_fold_w: the same arithmetic on 128 x 256 output tiles.
+//
+// Measured on the 128 x 128 kernel above: a block takes ~0.35 us against
+// 0.14 us of MMA, and neither the operand stream (3 and 4 stages run
+// alike), nor the tensor-memory read rate (16 epilogue warps run like 8)
+// sets that.  What a wider tile changes: an N = 256 MMA reads its A and B
+// operands from shared memory at 96 B/clock instead of the 128 B/clock
+// (the whole shared-memory read rate) of an N = 128 one, so the
+// epilogue's tensor-memory loads and the TMA writes no longer contend
+// with the MMAs for it; each A tile feeds twice the columns; and a
+// whisper-small N = 3072 GEMM at M = 1500 is 144 tiles, one wave, where
+// 128-wide tiles needed two.
+//
+// Roles (608 threads): warp 0 the TMA producer (one 40 KiB stage per
+// block: A 128 x 32 f16 with the 64-byte swizzle, B 256 rows x 64 f16 hi|lo
+// with the 128-byte swizzle; d_a 16 blocks at a time); warps 1-2 issue the
+// MMAs of even / odd blocks (four N = 256 MMAs per block into one of two
+// 256-column TMEM buffers); warps 3-18 the epilogue, four warps per TMEM
+// lane quarter, each 64 columns (acc <- fma(d_a, T, acc) in registers,
+// 16 columns per tensor-memory load).
+//
+// A K split over a cluster of CTAs (partial tiles added through distributed
+// shared memory) was measured and dropped: moving a 128 x 256 f32 partial
+// between CTAs ran at ~25-30 GB/s per SM, by per-thread remote stores and
+// by bulk shared::cluster copies alike, so the reduction cost more than the
+// split saved on the N = 768 shapes, which stay on the 64-column kernel.
+namespace wide {
+constexpr int BN = 256;
+constexpr int EW = 16;                                   // epilogue warps
+constexpr int THREADS = (EPI0 + EW) * 32;                // 608
+constexpr int CPW = BN / 4;                              // columns per epilogue warp
+constexpr int A_BYTES = BM * 32 * 2;                     // 8 KiB, 64-byte rows
+constexpr int B_BYTES = BN * 64 * 2;                     // 32 KiB, 128-byte rows
+constexpr int STAGE_BYTES = A_BYTES + B_BYTES;           // 40 KiB
+constexpr int STAGES = 5;
+constexpr int NBUF = 2;                                  // 2 x 256 TMEM columns
+constexpr int DA_SLOTS = 2;
+constexpr uint32_t IDESC = (1u << 4) | (uint32_t(BN >> 3) << 17) | (uint32_t(BM >> 4) << 24);
+struct Bars {
+    uint64_t full[STAGES], empty[STAGES], acc_full[NBUF], acc_empty[NBUF], da_full[DA_SLOTS], da_empty[DA_SLOTS];
+    uint32_t tmem_base;
+    int abort;
+};
+constexpr int SMEM = STAGES * STAGE_BYTES + DA_SLOTS * DA_BYTES + int(sizeof(Bars)) + 1024;
+static_assert(SMEM <= 227 * 1024, "shared memory budget");
+static_assert(EW * 32 * CPW * 4 <= STAGES * STAGE_BYTES, "output staging must fit in the stages");
+static_assert(STAGE_BYTES % 1024 == 0, "stages keep the 1024-byte swizzle alignment");
+}  // namespace wide
+
+// Shared-memory matrix descriptor: K-major, 64-byte swizzle (8-row groups
+// 512 bytes apart), layout type 4 = SWIZZLE_64B.
+__device__ __forceinline__ uint64_t sw64_desc(uint32_t saddr) {
+    uint64_t d = uint64_t((saddr & 0x3FFFFu) >> 4);
+    d |= uint64_t(16 >> 4) << 16;
+    d |= uint64_t(512 >> 4) << 32;
+    d |= uint64_t(1) << 46;
+    d |= uint64_t(4) << 61;
+    return d;
+}
+
+// tcgen05.wait::ld with the 16 loaded registers as operands, so no use of
+// them can be scheduled before the wait.
+__device__ __forceinline__ void tmem_wait_ld16(uint32_t* r) {
+    asm volatile("tcgen05.wait::ld.sync.aligned;"
+                 : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                   "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]),
+                   "+r"(r[15])
+                 :
+                 : "memory");
+}
+
+__global__ void __launch_bounds__(wide::THREADS, 1)
+    k_gemm_fold_w(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                  const __grid_constant__ CUtensorMap tmY, const __grid_constant__ CUtensorMap tmD, int use_tma_store,
+                  const float* __restrict__ colscale, const float* __restrict__ bias, float* __restrict__ Y, int M,
+                  int N, int nb, int* __restrict__ err_flag) {
+    constexpr int BN = wide::BN, EW = wide::EW, CPW = wide::CPW;
+    constexpr int A_BYTES = wide::A_BYTES, STAGE_BYTES = wide::STAGE_BYTES, STAGES = wide::STAGES;
+    constexpr int NBUF = wide::NBUF, DA_SLOTS = wide::DA_SLOTS;
+    constexpr uint32_t IDESC = wide::IDESC;
+    using Bars = wide::Bars;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* base = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+    float* ring = reinterpret_cast<float*>(base + STAGES * STAGE_BYTES);
+    Bars* bar = reinterpret_cast<Bars*>(reinterpret_cast<uint8_t*>(ring) + DA_SLOTS * DA_BYTES);
+    volatile int* abort = &bar->abort;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int n0 = int(blockIdx.x) * BN, m0 = int(blockIdx.y) * BM;
+    const int nblk = nb;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(&bar->full[s], 1);
+            mbar_init(&bar->empty[s], 1);
+        }
+        for (int b = 0; b < NBUF; ++b) {
+            mbar_init(&bar->acc_full[b], 1);
+            mbar_init(&bar->acc_empty[b], EW);
+        }
+        for (int c = 0; c < DA_SLOTS; ++c) {
+            mbar_init(&bar->da_full[c], 1);
+            mbar_init(&bar->da_empty[c], EW);
+        }
+        bar->abort = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    }
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                         smem_u32(&bar->tmem_base)),
+                     "r"(TMEM_COLS)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    if (threadIdx.x == 32) {
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmA)) : "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmB)) : "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmD)) : "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = bar->tmem_base;
+    // Set-up above overlaps the previous kernel; global memory only below.
+    pdl_trigger();
+    pdl_wait();
+
+    if (warp == 0) {
+        if (lane == 0) {
+            for (int i = 0; i < nblk; ++i) {
+                const int s = i % STAGES;
+                if (i % DA_GROUP == 0) {
+                    // d_a rows of blocks i .. i+15 (rows past nb read as 0).
+                    const int g = i / DA_GROUP, c = g % DA_SLOTS;
+                    if (!mbar_wait(&bar->da_empty[c], ((g / DA_SLOTS) & 1) ^ 1, abort, err_flag, 5)) break;
+                    mbar_expect_tx(&bar->da_full[c], DA_BYTES);
+                    tma_load_2d(ring + c * (DA_BYTES / 4), &tmD, m0, i, &bar->da_full[c]);
+                }
+                if (!mbar_wait(&bar->empty[s], ((i / STAGES) & 1) ^ 1, abort, err_flag, 1)) break;
+                uint8_t* st = base + s * STAGE_BYTES;
+                mbar_expect_tx(&bar->full[s], STAGE_BYTES);
+                tma_load_2d(st, &tmA, i * 32, m0, &bar->full[s]);
+                tma_load_2d(st + A_BYTES, &tmB, i * 64, n0, &bar->full[s]);
+            }
+        }
+    } else if (warp == 1 || warp == 2) {
+        // Warp 1 issues the even blocks (TMEM buffer 0), warp 2 the odd ones
+        // (buffer 1); each commit tracks the issuing thread's own MMAs.
+        if (lane == 0) {
+            const int u = warp - 1;
+            const uint32_t d = tmem + uint32_t(u * BN);
+            for (int i = u; i < nblk; i += 2) {
+                const int s = i % STAGES;
+                if (!mbar_spin(&bar->full[s], (i / STAGES) & 1, abort, err_flag, 2)) break;
+                if (!mbar_spin(&bar->acc_empty[u], ((i / NBUF) & 1) ^ 1, abort, err_flag, 3)) break;
+                tc_fence_after();
+                const uint32_t a = smem_u32(base + s * STAGE_BYTES);
+                const uint32_t b = a + uint32_t(A_BYTES);
+                // K half 0: A bytes +0..31, B hi +0..31, lo +64..95;
+                // K half 1: A bytes +32..63, B hi +32..63, lo +96..127.
+                mma_f16_id(d, sw64_desc(a), sw128_desc(b), IDESC, 0);
+                mma_f16_id(d, sw64_desc(a), sw128_desc(b + 64), IDESC, 1);
+                mma_f16_id(d, sw64_desc(a + 32), sw128_desc(b + 32), IDESC, 1);
+                mma_f16_id(d, sw64_desc(a + 32), sw128_desc(b + 96), IDESC, 1);
+                mma_commit(&bar->acc_full[u]);
+                mma_commit(&bar->empty[s]);
+            }
+        }
+    } else {
+        const int q = warp & 3, h = (warp - EPI0) >> 2;   // TMEM lane quarter, column quarter
+        float2 acc[CPW / 2];
+#pragma unroll
+        for (int c = 0; c < CPW / 2; ++c) acc[c] = make_float2(0.f, 0.f);
+        const uint32_t lane_off = uint32_t(q * 32) << 16;
+        for (int i = 0; i < nblk; ++i) {
+            const int u = i % NBUF, g = i / DA_GROUP, c = g % DA_SLOTS;
+            const bool got = (i % DA_GROUP != 0 || mbar_wait(&bar->da_full[c], (g / DA_SLOTS) & 1, abort, err_flag, 6)) &&
+                             mbar_spin(&bar->acc_full[u], (i / NBUF) & 1, abort, err_flag, 4);
+            if (!__all_sync(0xffffffffu, got)) break;
+            tc_fence_after();
+            const float da = ring[c * (DA_BYTES / 4) + (i % DA_GROUP) * BM + q * 32 + lane];
+            const float2 da2 = make_float2(da, da);
+            const uint32_t taddr = tmem + lane_off + uint32_t(u * BN + h * CPW);
+#pragma unroll
+            for (int cc = 0; cc < CPW / 16; ++cc) {
+                uint32_t r[16];
+                tmem_ld16(taddr + uint32_t(cc * 16), r);
+                tmem_wait_ld16(r);
+#pragma unroll
+                for (int e = 0; e < 8; ++e)
+                    acc[cc * 8 + e] = __ffma2_rn(da2, make_float2(__uint_as_float(r[2 * e]), __uint_as_float(r[2 * e + 1])),
+                                                 acc[cc * 8 + e]);
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) {
+                mbar_arrive(&bar->acc_empty[u]);
+                if (i % DA_GROUP == DA_GROUP - 1 || i == nblk - 1) mbar_arrive(&bar->da_empty[c]);
+            }
+        }
+        const int col0 = n0 + h * CPW;
+        const int row = m0 + q * 32 + lane;
+        if (!*abort) {
+            const bool bias_vec = (reinterpret_cast<uintptr_t>(bias) & 15) == 0;
+            if (use_tma_store) {
+                // Staging for this warp: CPW/32 boxes of 32 rows x 128 bytes,
+                // 128-byte swizzle (16-byte chunk c of row r at c ^ (r & 7)).
+                uint8_t* stg = base + (warp - EPI0) * (32 * CPW * 4);
+#pragma unroll
+                for (int b = 0; b < CPW / 32; ++b) {
+                    uint8_t* box = stg + b * 4096 + lane * 128;
+#pragma unroll
+                    for (int c4 = 0; c4 < 8; ++c4) {
+                        const int col = col0 + b * 32 + c4 * 4;   // < n0 + BN <= padded width
+                        const float4 cs = __ldg(reinterpret_cast<const float4*>(colscale + col));
+                        const float2 a01 = acc[b * 16 + c4 * 2], a23 = acc[b * 16 + c4 * 2 + 1];
+                        float4 v = make_float4(__fmul_rn(a01.x, cs.x), __fmul_rn(a01.y, cs.y),
+                                               __fmul_rn(a23.x, cs.z), __fmul_rn(a23.y, cs.w));
+                        if (bias && col < N) {  // N % 4 == 0 on this path
+                            const float4 bb = bias_vec ? __ldg(reinterpret_cast<const float4*>(bias + col))
+                                                       : make_float4(__ldg(bias + col), __ldg(bias + col + 1),
+                                                                     __ldg(bias + col + 2), __ldg(bias + col + 3));
+                            v.x = __fadd_rn(v.x, bb.x); v.y = __fadd_rn(v.y, bb.y);
+                            v.z = __fadd_rn(v.z, bb.z); v.w = __fadd_rn(v.w, bb.w);
+                        }
+                        *reinterpret_cast<float4*>(box + ((c4 ^ (lane & 7)) << 4)) = v;
+                    }
+                }
+                fence_async_smem();
+                __syncwarp();
+                if (lane == 0) {
+#pragma unroll
+                    for (int b = 0; b < CPW / 32; ++b)
+                        if (col0 + b * 32 < N && m0 + q * 32 < M)
+                            tma_store_2d(&tmY, col0 + b * 32, m0 + q * 32, stg + b * 4096);
+                    bulk_commit();
+                    bulk_wait_read_all();
+                }
+                __syncwarp();
+            } else if (row < M) {
+                float* yr = Y + size_t(row) * N;
+#pragma unroll
+                for (int cc = 0; cc < CPW / 2; ++cc) {
+                    const int col = col0 + 2 * cc;
+                    if (col < N) {
+                        const float v = __fmul_rn(acc[cc].x, __ldg(colscale + col));
+                        yr[col] = bias ? __fadd_rn(v, __ldg(bias + col)) : v;
+                    }
+                    if (col + 1 < N) {
+                        const float v = __fmul_rn(acc[cc].y, __ldg(colscale + col + 1));
+                        yr[col + 1] = bias ? __fadd_rn(v, __ldg(bias + col + 1)) : v;
+                    }
+                }
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 0) {
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
+    }
+}
+
 // ------------------------------------------------------------- host side
 PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 std::once_flag g_once;
@@ -364,17 +631,84 @@ cudaError_t launch_fold_bn(const ActsView& v, const Weight& w, const float* bias
                       v.m, w.n, w.nb, err_flag);
 }
 
-cudaError_t launch_fold(const ActsView& v, const Weight& w, const float* bias, float* y, int* err_flag,
-                        cudaStream_t s, char* why, size_t why_len) {
-    static int sm_count[64] = {};
+std::mutex g_dev_mu;
+int g_sms[64];
+int g_wide_attr[64];
+
+int cur_dev() {
     int dev = 0;
     cudaGetDevice(&dev);
-    if (dev < 64 && sm_count[dev] == 0) cudaDeviceGetAttribute(&sm_count[dev], cudaDevAttrMultiProcessorCount, dev);
-    const int sms = dev < 64 ? sm_count[dev] : 148;
+    return dev < 64 ? dev : 63;
+}
+
+int sms_of(int dev) {
+    std::lock_guard<std::mutex> g(g_dev_mu);
+    if (g_sms[dev] == 0 && cudaDeviceGetAttribute(&g_sms[dev], cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+        g_sms[dev] = 148;
+    return g_sms[dev];
+}
+
+cudaError_t wide_smem_attr(int dev) {
+    std::lock_guard<std::mutex> g(g_dev_mu);
+    if (g_wide_attr[dev]) return cudaSuccess;
+    cudaError_t e = cudaFuncSetAttribute(k_gemm_fold_w, cudaFuncAttributeMaxDynamicSharedMemorySize, wide::SMEM);
+    if (e == cudaSuccess) g_wide_attr[dev] = 1;
+    return e;
+}
+
+// Tile width.  Per-CTA time is modelled from measured per-block costs
+// (128 x 64: 0.24 us, 128 x 128: 0.35 us, 128 x 256: 0.5 us) plus fixed
+// costs (prologue and output write: ~3.5 us, ~5.5 us for the 128 x 256
+// tile's 128 KiB), times the waves of CTAs.  Returns true for 256.
+thread_local int t_fold_override = 0;
+
+bool fold_wide(int dev, int m, int n, int nb) {
+    const int sms = sms_of(dev);
+    const long mt = (m + BM - 1) / BM;
+    const long tiles128 = long((n + 127) / 128) * mt;
+    const bool bn64 = 2 * tiles128 <= sms;
+    const long narrow_tiles = bn64 ? 2 * tiles128 : tiles128;
+    const double narrow = double((narrow_tiles + sms - 1) / sms) * (3.5 + nb * (bn64 ? 0.24 : 0.35));
+    const long wide_tiles = long((n + wide::BN - 1) / wide::BN) * mt;
+    const double wide_t = double((wide_tiles + sms - 1) / sms) * (5.5 + nb * 0.5);
+    return wide_t < narrow;
+}
+
+cudaError_t launch_fold_wide(const ActsView& v, const Weight& w, const float* bias, float* y, int* err_flag,
+                             cudaStream_t s, char* why, size_t why_len) {
+    const int dev = cur_dev();
+    cudaError_t e = wide_smem_attr(dev);
+    if (e != cudaSuccess) return e;
+    CUtensorMap ma, mb, my, md;
+    if (!encode_map(&ma, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, v.q16, uint64_t(v.k), uint64_t(v.m), 32, BM,
+                    CU_TENSOR_MAP_SWIZZLE_64B, why, why_len))
+        return cudaErrorInvalidValue;
+    if (!encode_map(&mb, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, w.bhl, uint64_t(w.nb) * 64, uint64_t(w.n), 64, wide::BN,
+                    CU_TENSOR_MAP_SWIZZLE_128B, why, why_len))
+        return cudaErrorInvalidValue;
+    if (!encode_map(&md, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, v.dT, uint64_t(v.m_pad), uint64_t(w.nb), BM, DA_GROUP,
+                    CU_TENSOR_MAP_SWIZZLE_NONE, why, why_len))
+        return cudaErrorInvalidValue;
+    int use_tma_store = (w.n % 4 == 0) && (reinterpret_cast<uintptr_t>(y) % 16 == 0);
+    if (use_tma_store && !encode_map(&my, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, y, uint64_t(w.n), uint64_t(v.m), 32, 32,
+                                     CU_TENSOR_MAP_SWIZZLE_128B, why, why_len))
+        use_tma_store = 0;
+    if (!use_tma_store) memset(&my, 0, sizeof my);
+    const int nt = (w.n + wide::BN - 1) / wide::BN, mt = (v.m + BM - 1) / BM;
+    const dim3 grid(static_cast<unsigned>(nt), static_cast<unsigned>(mt));
+    return launch_pdl(k_gemm_fold_w, grid, dim3(wide::THREADS), wide::SMEM, s, ma, mb, my, md, use_tma_store,
+                      w.colscale, bias, y, v.m, w.n, w.nb, err_flag);
+}
+
+cudaError_t launch_fold(const ActsView& v, const Weight& w, const float* bias, float* y, int* err_flag,
+                        cudaStream_t s, char* why, size_t why_len) {
+    const int dev = cur_dev();
+    const bool wide_tiles = t_fold_override ? t_fold_override == 2 : fold_wide(dev, v.m, w.n, w.nb);
+    if (wide_tiles) return launch_fold_wide(v, w, bias, y, err_flag, s, why, why_len);
     const long tiles128 = long((w.n + 127) / 128) * ((v.m + BM - 1) / BM);
     // 64-wide tiles when they still fit in one wave and 128-wide ones
     // would leave at least half the SMs idle.
-    if (2 * tiles128 <= sms) return launch_fold_bn<64>(v, w, bias, y, err_flag, s, why, why_len);
+    if (2 * tiles128 <= sms_of(dev)) return launch_fold_bn<64>(v, w, bias, y, err_flag, s, why, why_len);
     return launch_fold_bn<128>(v, w, bias, y, err_flag, s, why, why_len);
 }
 
@@ -385,5 +719,9 @@ cudaError_t launch_gemm_fold(const ActsView& v, const Weight& w, const float* bi
     if (v.m <= 0 || w.n <= 0) return cudaSuccess;
     return launch_fold(v, w, bias, y, err_flag, s, why, why_len);
 }
+
+int gemm_fold_config(int m, int n, int nb) { return fold_wide(cur_dev(), m, n, nb) ? 2 : 1; }
+
+void set_gemm_fold_config(int code) { t_fold_override = (code == 1 || code == 2) ? code : 0; }
 
 }  // namespace rwq

@@ -92,6 +92,13 @@ cudaError_t launch_gemm_tc(const ActsView& v, const Weight& w, const float* bias
 // tcgen05 GEMM with the weight scales folded into the B operand.
 cudaError_t launch_gemm_fold(const ActsView& v, const Weight& w, const float* bias, float* y, int* err_flag,
                              cudaStream_t s, char* why, size_t why_len);
+// The tile width k_gemm_fold picks for an m x n GEMM of nb blocks on the
+// current device: 1 = 128- or 64-column tiles, 2 = 128 x 256 tiles.
+int gemm_fold_config(int m, int n, int nb);
+// Force that choice for this host thread (1 or 2; anything else:
+// automatic).  The host-buffer entry point runs row chunks with the choice
+// of the whole call.
+void set_gemm_fold_config(int code);
 
 // Rows of activations a[m][lda] (first k columns) into the hi|lo operand
 // of k_gemm_hl: with `quantize` the reference's int8 quantizer runs first
