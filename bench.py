@@ -259,11 +259,13 @@ def run_ours(args, rank, world, local_rank):
                    "l2": "256 MiB buffer written before every timed step (L2 126 MB)"},
         "gpu_launches": 18 * args.steps,
         "roofline": {
-            "bound": "tensor", "kernel": "k_gemm_fold (tcgen05 kind::f16, scales folded into an f16 hi|lo weight operand)",
+            "bound": "tensor",
+            "kernel": "k_gemm_fold_w (N=3072: 128x256 tiles) + k_gemm_fold<64> (N=768) (tcgen05 kind::f16, "
+                      "weight scales folded into an f16 hi|lo operand)",
             "achieved": round(gemm_tops, 2), "peak": tc_peak, "unit": "TFLOP/s",
             "frac": round(gemm_tops / tc_peak, 4), "peak_kind": f"{peak_kind} dense bf16 (burst)",
-            "traffic": profile_traffic("k_gemm_fold_config2_768x3072.md"),
-            "traffic_launch": "ncu, Q4_0 M=1500 K=768 N=3072 launch (profiles/)",
+            "traffic": profile_traffic("k_gemm_fold_w_config2_768x3072.md"),
+            "traffic_launch": "ncu, k_gemm_fold_w Q4_0 M=1500 K=768 N=3072 launch (profiles/)",
             "per_format_tops": by_fmt,
         },
         "config1": config1,
