@@ -618,7 +618,7 @@ def run_profile_driver(args):
     `logits` -- config 4's tied-logits GEMV (Q5_0 51865 x 1024, four weight
     copies) at --m rows, --steps back-to-back launches; `gemv` -- the same
     for config 5's decoder projection (Q4_0 1280 x 1280, eight copies);
-    `decode` -- the config-4 decoder (80 streams; config 5's with --m 256),
+    `decode` -- the config-4 decoder (80 streams; config 5's with --m 32..256 windows),
     begin then --steps greedy steps."""
     import torch
     from rusty_whisper_b200 import quant
@@ -654,9 +654,9 @@ def run_profile_driver(args):
         del gr
     else:
         from rusty_whisper_b200 import decoder
-        if args.m == 256:   # config 5's decoder: large-v3 shape, Q4_0, 256 windows, one stream each
+        if args.m in (32, 64, 128, 256):   # config 5's decoder: large-v3 shape, Q4_0, m windows (256 / ranks)
             c = dict(n_vocab=LARGE_V3["n_vocab"], n_ctx=448, n_state=1280, n_head=20, n_layer=32)
-            n_win, per, dt = 256, 1, 2
+            n_win, per, dt = args.m, 1, 2
         else:               # config 4: whisper-medium, Q5_0, 16 windows x 5 streams
             c, n_win, per, dt = DEC_MEDIUM, 16, 5, 6
         t = synth.decoder_tensors(c["n_vocab"], c["n_ctx"], c["n_state"], c["n_layer"], dt, seed=7, gen_device=dev)
@@ -986,7 +986,8 @@ def main():
                     help="GEMM kernel path of the sweep (rwq_set_gemm_path): 0 automatic (folded-scale), 2 folded-scale, "
                          "3 exact integer, 4 hi|lo")
     ap.add_argument("--m", type=int, default=1,
-                    help="--only logits: activation rows; --only decode: 256 selects config 5's decoder")
+                    help="--only logits: activation rows; --only decode: 32, 64, 128 or 256 select config 5's "
+                         "decoder with that many windows (one rank's share at 8, 4, 2, 1 GPUs)")
     ap.add_argument("--only", default="all", choices=["all", "gemm", "encoder", "decoder", "large", "logits", "gemv", "decode",
                                                       "beam"],
                     help="gemm: only the config-2 GEMM sweep; encoder / decoder / large: only that leg; "
