@@ -267,6 +267,11 @@ def run_ours(args, rank, world, local_rank):
             "traffic": profile_traffic("k_gemm_fold_w_config2_768x3072.md"),
             "traffic_launch": "ncu, k_gemm_fold_w Q4_0 M=1500 K=768 N=3072 launch (profiles/)",
             "per_format_tops": by_fmt,
+            # The int8 tier's block scaling costs two f16 MMAs per unit of
+            # work (the weight operand as hi + lo): what the tensor pipe
+            # actually issues, against the same peak.
+            "issued_mma_tflops": round(2 * gemm_tops, 2),
+            "issued_mma_frac": round(2 * gemm_tops / tc_peak, 4),
         },
         "config1": config1,
         "gemv": gemv,
