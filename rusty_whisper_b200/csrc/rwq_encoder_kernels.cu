@@ -101,13 +101,27 @@ __global__ void __launch_bounds__(256) k_rows_quant(const float* x, const float*
                                                     const float* __restrict__ lw, const float* __restrict__ lb,
                                                     int m, int k, QOut o, float* __restrict__ yout, int slice_len) {
     constexpr bool LN = MODE == RQ_LN || MODE == RQ_ADD_LN;
-    pdl_trigger();
-    pdl_wait();
     const int lane = threadIdx.x & 31;
     const int nb = k / QK, nch = k / 128;
     const int wpr = LN ? RQ_WPR : (nch + slice_len - 1) / slice_len;   // warps per row
     const size_t wg = (size_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
     const int row = int(wg / wpr), wr = int(wg % wpr);
+    // The LayerNorm's weight and bias are never written by a kernel that
+    // runs as a programmatic dependent: read them before the wait, while
+    // the predecessor finishes.
+    float4 lwv[LN ? NV : 1], lbv[LN ? NV : 1];
+    if constexpr (LN) {
+#pragma unroll
+        for (int j = 0; j < NV; ++j) {
+            const int c = wr + RQ_WPR * j;
+            if (c < nch) {
+                lwv[j] = __ldg(reinterpret_cast<const float4*>(lw + c * 128 + lane * 4));
+                lbv[j] = __ldg(reinterpret_cast<const float4*>(lb + c * 128 + lane * 4));
+            }
+        }
+    }
+    pdl_trigger();
+    pdl_wait();
     const int rows = o.q16 ? o.m_pad : m;
     const bool live = row < m;
     if (!LN && !live) {
@@ -193,9 +207,7 @@ __global__ void __launch_bounds__(256) k_rows_quant(const float* x, const float*
         for (int j = 0; j < NV; ++j) {
             const int c = wr + RQ_WPR * j;
             if (c < nch) {
-                const int e = c * 128 + lane * 4;
-                const float4 w = __ldg(reinterpret_cast<const float4*>(lw + e));
-                const float4 b = __ldg(reinterpret_cast<const float4*>(lb + e));
+                const float4 w = lwv[j], b = lbv[j];
                 auto f = [&](float xv, float wv, float bv) {
                     return __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(xv, mean), inv), wv), bv);
                 };
