@@ -285,8 +285,14 @@ __global__ void __launch_bounds__(TC_WARPS * 32) k_attn_dec_tc(const float* __re
         }
     };
     const int splits = int(gridDim.z), sp = int(blockIdx.z);
-    pdl_wait();
-    if (dpos) L = min(*dpos + 1, L);   // self-attention: keys 0..pos (L is the cache capacity)
+    // Cross-attention (no position): its K/V and group maps are written once
+    // when the decode begins, so its first K/V tile is requested before the
+    // wait for the predecessor (which produces the queries).
+    const bool early = dpos == nullptr;
+    if (!early) {
+        pdl_wait();
+        L = min(*dpos + 1, L);   // self-attention: keys 0..pos (L is the cache capacity)
+    }
     const int s0 = grp_off[gr], G = grp_off[gr + 1] - s0;
     if (G <= 0) return;
     const int k_lo = int(int64_t(sp) * L / splits), k_hi = int(int64_t(sp + 1) * L / splits);
@@ -306,6 +312,12 @@ __global__ void __launch_bounds__(TC_WARPS * 32) k_attn_dec_tc(const float* __re
             tc_cp16(dv + tc_swz(row, ch), V + o, ok);
         }
     };
+    const int ntiles = (k_hi - k_lo + TC_KEYS - 1) / TC_KEYS;
+    if (early) {
+        if (warp < ntiles) load(warp, 0);
+        asm volatile("cp.async.commit_group;" ::: "memory");
+        pdl_wait();
+    }
     // A fragments of the queries (scaled by log2(e)/8): row g = hi, g+8 = lo.
     const float L2E = 1.4426950408889634f;
     uint32_t qa[4][4];
@@ -321,13 +333,14 @@ __global__ void __launch_bounds__(TC_WARPS * 32) k_attn_dec_tc(const float* __re
                 tc_split2(__fmul_rn(v.x, 0.125f) * L2E, __fmul_rn(v.y, 0.125f) * L2E, qa[kk][2 * u], qa[kk][2 * u + 1]);
             }
     }
-    const int ntiles = (k_hi - k_lo + TC_KEYS - 1) / TC_KEYS;
     float o[8][4];
 #pragma unroll
     for (int i = 0; i < 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
     float m = -INFINITY, l = 0.f;   // query g (the four lanes of one g agree on m)
-    if (warp < ntiles) load(warp, 0);
-    asm volatile("cp.async.commit_group;" ::: "memory");
+    if (!early) {
+        if (warp < ntiles) load(warp, 0);
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    }
     for (int t = warp, it = 0; t < ntiles; t += TC_WARPS, ++it) {
         const int st = it & 1;
         if (t + TC_WARPS < ntiles) load(t + TC_WARPS, st ^ 1);
