@@ -82,6 +82,8 @@ struct Fold {
     // kind::f16, D f32, A/B f16, K-major, N>>3 at bit 17, M>>4 at bit 24.
     static constexpr uint32_t IDESC = (1u << 4) | (uint32_t(BN >> 3) << 17) | (uint32_t(BM >> 4) << 24);
     struct Bars {
+        alignas(16) float cs[BN];   // the tile's column scales and bias, read once early
+        alignas(16) float bs[BN];
         uint64_t full[STAGES], empty[STAGES], acc_full[NBUF], acc_empty[NBUF], da_full[DA_SLOTS], da_empty[DA_SLOTS];
         uint32_t tmem_base;
         int abort;
@@ -210,6 +212,12 @@ __global__ void __launch_bounds__(THREADS, 1)
         float2 acc[CPW / 2];
 #pragma unroll
         for (int c = 0; c < CPW / 2; ++c) acc[c] = make_float2(0.f, 0.f);
+        // The tile's column scales and bias into shared memory now, so the
+        // final scaling does not wait on their loads.
+        for (int c = int(threadIdx.x) - EPI0 * 32; c < BN; c += EPI_WARPS * 32) {
+            bar->cs[c] = __ldg(colscale + n0 + c);   // padded width
+            bar->bs[c] = bias && n0 + c < N ? __ldg(bias + n0 + c) : 0.f;
+        }
         for (int blk = 0; blk < nb; ++blk) {
             const int u = blk % NBUF, g = blk / DA_GROUP, c = g % DA_SLOTS;
             const bool got = (blk % DA_GROUP != 0 || mbar_wait(&bar->da_full[c], (g / DA_SLOTS) & 1, abort, err_flag, 6)) &&
@@ -236,7 +244,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         // y = acc * 2^-e_j (+ bias), written through shared memory.
         const int col0 = n0 + h * CPW;
         const int row = m0 + q * 32 + lane;
-        const bool bias_vec = (reinterpret_cast<uintptr_t>(bias) & 15) == 0;
+        asm volatile("bar.sync 1, %0;" ::"r"(EPI_WARPS * 32) : "memory");   // scales and bias in place
         if (!*abort) {
             if (use_tma_store) {
                 // Staging for this warp (in the drained stage ring): CPW/32
@@ -249,14 +257,12 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
                     for (int c4 = 0; c4 < 8; ++c4) {
                         const int col = col0 + b * 32 + c4 * 4;   // < n0 + BN <= padded width
-                        const float4 cs = __ldg(reinterpret_cast<const float4*>(colscale + col));
+                        const float4 cs = *reinterpret_cast<const float4*>(bar->cs + (col - n0));
                         const float2 a01 = acc[b * 16 + c4 * 2], a23 = acc[b * 16 + c4 * 2 + 1];
                         float4 v = make_float4(__fmul_rn(a01.x, cs.x), __fmul_rn(a01.y, cs.y),
                                                __fmul_rn(a23.x, cs.z), __fmul_rn(a23.y, cs.w));
                         if (bias && col < N) {  // N % 4 == 0 on this path
-                            const float4 bb = bias_vec ? __ldg(reinterpret_cast<const float4*>(bias + col))
-                                                       : make_float4(__ldg(bias + col), __ldg(bias + col + 1),
-                                                                     __ldg(bias + col + 2), __ldg(bias + col + 3));
+                            const float4 bb = *reinterpret_cast<const float4*>(bar->bs + (col - n0));
                             v.x = __fadd_rn(v.x, bb.x); v.y = __fadd_rn(v.y, bb.y);
                             v.z = __fadd_rn(v.z, bb.z); v.w = __fadd_rn(v.w, bb.w);
                         }
@@ -340,6 +346,8 @@ constexpr int NBUF = 2;                                  // 2 x 256 TMEM columns
 constexpr int DA_SLOTS = 2;
 constexpr uint32_t IDESC = (1u << 4) | (uint32_t(BN >> 3) << 17) | (uint32_t(BM >> 4) << 24);
 struct Bars {
+    alignas(16) float cs[BN];   // the tile's column scales and bias, read once early
+    alignas(16) float bs[BN];
     uint64_t full[STAGES], empty[STAGES], acc_full[NBUF], acc_empty[NBUF], da_full[DA_SLOTS], da_empty[DA_SLOTS];
     uint32_t tmem_base;
     int abort;
@@ -475,6 +483,12 @@ __global__ void __launch_bounds__(wide::THREADS, 1)
         float2 acc[CPW / 2];
 #pragma unroll
         for (int c = 0; c < CPW / 2; ++c) acc[c] = make_float2(0.f, 0.f);
+        // The tile's column scales and bias into shared memory now, so the
+        // final scaling does not wait on their loads.
+        for (int c = int(threadIdx.x) - EPI0 * 32; c < BN; c += EW * 32) {
+            bar->cs[c] = __ldg(colscale + n0 + c);   // padded width
+            bar->bs[c] = bias && n0 + c < N ? __ldg(bias + n0 + c) : 0.f;
+        }
         const uint32_t lane_off = uint32_t(q * 32) << 16;
         for (int i = 0; i < nblk; ++i) {
             const int u = i % NBUF, g = i / DA_GROUP, c = g % DA_SLOTS;
@@ -504,8 +518,8 @@ __global__ void __launch_bounds__(wide::THREADS, 1)
         }
         const int col0 = n0 + h * CPW;
         const int row = m0 + q * 32 + lane;
+        asm volatile("bar.sync 1, %0;" ::"r"(EW * 32) : "memory");   // scales and bias in place
         if (!*abort) {
-            const bool bias_vec = (reinterpret_cast<uintptr_t>(bias) & 15) == 0;
             if (use_tma_store) {
                 // Staging for this warp: CPW/32 boxes of 32 rows x 128 bytes,
                 // 128-byte swizzle (16-byte chunk c of row r at c ^ (r & 7)).
@@ -516,14 +530,12 @@ __global__ void __launch_bounds__(wide::THREADS, 1)
 #pragma unroll
                     for (int c4 = 0; c4 < 8; ++c4) {
                         const int col = col0 + b * 32 + c4 * 4;   // < n0 + BN <= padded width
-                        const float4 cs = __ldg(reinterpret_cast<const float4*>(colscale + col));
+                        const float4 cs = *reinterpret_cast<const float4*>(bar->cs + (col - n0));
                         const float2 a01 = acc[b * 16 + c4 * 2], a23 = acc[b * 16 + c4 * 2 + 1];
                         float4 v = make_float4(__fmul_rn(a01.x, cs.x), __fmul_rn(a01.y, cs.y),
                                                __fmul_rn(a23.x, cs.z), __fmul_rn(a23.y, cs.w));
                         if (bias && col < N) {  // N % 4 == 0 on this path
-                            const float4 bb = bias_vec ? __ldg(reinterpret_cast<const float4*>(bias + col))
-                                                       : make_float4(__ldg(bias + col), __ldg(bias + col + 1),
-                                                                     __ldg(bias + col + 2), __ldg(bias + col + 3));
+                            const float4 bb = *reinterpret_cast<const float4*>(bar->bs + (col - n0));
                             v.x = __fadd_rn(v.x, bb.x); v.y = __fadd_rn(v.y, bb.y);
                             v.z = __fadd_rn(v.z, bb.z); v.w = __fadd_rn(v.w, bb.w);
                         }
