@@ -366,6 +366,23 @@ int rwq::gemm_quantized(const ActsView& v, rwq_qtensor* w, const float* bias, fl
     return run_quantized(v, v.ahl ? LAYOUT_HL : LAYOUT_FOLD, w, bias, out, s, nullptr, ws->err);
 }
 
+bool rwq::gemm_gelu_quantized_fits(const ActsView& v, rwq_qtensor* w, const ActsView& out) {
+    return w && t_gemm_path != 3 && !v.ahl && v.k == w->w.k && rwq::gemm_fold_gelu_fits(v, w->w, out);
+}
+
+int rwq::gemm_gelu_quantized(const ActsView& v, rwq_qtensor* w, const float* bias, const ActsView& out,
+                             cudaStream_t s) {
+    if (!gemm_gelu_quantized_fits(v, w, out)) return fail(RWQ_ERR_ARG, "fused GELU GEMM does not apply here");
+    Workspace* ws = nullptr;
+    int rc = get_workspace(s, &ws);
+    if (rc) return rc;
+    if ((rc = weight_fold_cache(w, s))) return rc;
+    char why[256] = {0};
+    cudaError_t e = rwq::launch_gemm_fold_gelu(v, w->w, bias, out, ws->err, s, why, sizeof why);
+    if (e != cudaSuccess) return fail(RWQ_ERR_CUDA, "gemm launch: %s %s", cudaGetErrorString(e), why);
+    return RWQ_OK;
+}
+
 int rwq::linear_acts(const ActsView& v, bool gemm, rwq_qtensor* w, const float* bias, float* out, cudaStream_t s) {
     Workspace* ws = nullptr;
     int rc = get_workspace(s, &ws);

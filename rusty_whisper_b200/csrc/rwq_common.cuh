@@ -30,6 +30,14 @@ namespace rwq {
 
 constexpr int QK = 32;
 
+// GELU as tensor.rs:291-306 computes it, same operation order:
+//   0.5 * t * (1 + tanh(C * (t + 0.044715 * t * t * t)))
+__device__ __forceinline__ float gelu_ref(float t) {
+    const float C = 0.7978846f;
+    const float cube = __fmul_rn(__fmul_rn(__fmul_rn(0.044715f, t), t), t);
+    return __fmul_rn(__fmul_rn(0.5f, t), __fadd_rn(1.0f, tanhf(__fmul_rn(C, __fadd_rn(t, cube)))));
+}
+
 enum Dtype : int { Q4_0 = 2, Q4_1 = 3, Q5_0 = 6, Q5_1 = 7, Q8_0 = 8 };
 
 __host__ __device__ constexpr int block_bytes(int dt) {

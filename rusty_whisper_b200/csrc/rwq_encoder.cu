@@ -234,6 +234,17 @@ int encode_batch(rwq_encoder* e, const Bufs& b, const float* mel, int nwin, floa
                                    s),
              "conv2 gelu");
     const rwq::ActsView aD = acts_for(b, D), aF = acts_for(b, F);
+    // fc2's operand in b.h's memory (f16 codes [M][F], then d_a and
+    // d_a*sum(q_a) [F/32][m_pad]): the fused fc1 writes it while its own
+    // operand (b.acts) is still being read.
+    rwq::ActsView aH = aF;
+    aH.q16 = reinterpret_cast<uint16_t*>(b.h);
+    aH.dT = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(b.h) + align_up(size_t(M) * F * 2, 256));
+    aH.uT = aH.dT + size_t(F / rwq::QK) * m_pad;
+    aH.q8 = nullptr;
+    aH.d = nullptr;
+    aH.sum = nullptr;
+    aH.u = nullptr;
     const float qscale = 1.0f / std::sqrt(float(D / H));   // 1/8 for head dim 64: exact
     for (int l = 0; l < e->n_layer; ++l) {
         const Layer& L = e->layers[size_t(l)];
@@ -255,11 +266,18 @@ int encode_batch(rwq_encoder* e, const Bufs& b, const float* mel, int nwin, floa
         ENC_CUDA(rwq::launch_rows_quant(rwq::RQ_ADD_LN, b.x, b.tmp, b.x, W(lname(l, "mlp_ln.weight")),
                                         W(lname(l, "mlp_ln.bias")), M, D, m_pad, aD.q16, aD.dT, aD.uT, nullptr, s),
                  "mlp_ln");
-        ENC_RC(rwq::gemm_quantized(aD, L.fc1, W(lname(l, "mlp.0.bias")), b.h, s));
-        ENC_CUDA(rwq::launch_rows_quant(rwq::RQ_GELU, b.h, nullptr, nullptr, nullptr, nullptr, M, F, m_pad, aF.q16,
-                                        aF.dT, aF.uT, nullptr, s),
-                 "gelu quantize");
-        ENC_RC(rwq::gemm_quantized(aF, L.fc2, W(lname(l, "mlp.2.bias")), b.tmp, s));
+        if (rwq::gemm_gelu_quantized_fits(aD, L.fc1, aH)) {
+            // fc1 with GELU and the quantizer in its epilogue, into fc2's
+            // operand (carved from b.h, which the f32 output would use)
+            ENC_RC(rwq::gemm_gelu_quantized(aD, L.fc1, W(lname(l, "mlp.0.bias")), aH, s));
+            ENC_RC(rwq::gemm_quantized(aH, L.fc2, W(lname(l, "mlp.2.bias")), b.tmp, s));
+        } else {
+            ENC_RC(rwq::gemm_quantized(aD, L.fc1, W(lname(l, "mlp.0.bias")), b.h, s));
+            ENC_CUDA(rwq::launch_rows_quant(rwq::RQ_GELU, b.h, nullptr, nullptr, nullptr, nullptr, M, F, m_pad,
+                                            aF.q16, aF.dT, aF.uT, nullptr, s),
+                     "gelu quantize");
+            ENC_RC(rwq::gemm_quantized(aF, L.fc2, W(lname(l, "mlp.2.bias")), b.tmp, s));
+        }
     }
     // [x += last mlp out;] ln_post -> out
     ENC_CUDA(rwq::launch_rows_quant(e->n_layer ? rwq::RQ_ADD_LN : rwq::RQ_LN, b.x, b.tmp, b.x,

@@ -36,6 +36,15 @@ cudaError_t launch_attention(const __half* Qh, const __half* Kh, const __half* V
 // first use.  Returns an RWQ_* status (error text set).
 int gemm_quantized(const ActsView& v, rwq_qtensor* w, const float* bias, float* out, cudaStream_t s);
 
+// Same GEMM with GELU and the int8 quantizer fused into its epilogue: the
+// output goes straight into `out`'s GEMM-layout operand (q16, dT, uT) for
+// the next GEMM (the encoder's fc1 -> fc2).  `out` must not share memory
+// with `v`.  gemm_gelu_quantized_fits says whether this call can run
+// fused (w.n a multiple of 256, the default tensor-core path); otherwise
+// the caller runs gemm_quantized and the GELU row kernel.
+bool gemm_gelu_quantized_fits(const ActsView& v, rwq_qtensor* w, const ActsView& out);
+int gemm_gelu_quantized(const ActsView& v, rwq_qtensor* w, const float* bias, const ActsView& out, cudaStream_t s);
+
 // Same on either layout: `gemm` false reads the GEMV layout (q8, d, sum, u;
 // integer-MMA GEMV in chunks of 8 rows), true the GEMM layout.
 int linear_acts(const ActsView& v, bool gemm, rwq_qtensor* w, const float* bias, float* out, cudaStream_t s);

@@ -18,14 +18,6 @@ namespace rwq {
 
 namespace {
 
-// tensor.rs:291-306, same operation order:
-//   0.5 * t * (1 + tanh(C * (t + 0.044715 * t * t * t)))
-__device__ __forceinline__ float gelu_ref(float t) {
-    const float C = 0.7978846f;
-    const float cube = __fmul_rn(__fmul_rn(__fmul_rn(0.044715f, t), t), t);
-    return __fmul_rn(__fmul_rn(0.5f, t), __fadd_rn(1.0f, tanhf(__fmul_rn(C, __fadd_rn(t, cube)))));
-}
-
 // One 32-element block held as 4 values by each of 8 consecutive lanes
 // (lane & 7 = position): the reference quantizer (quant.rs:690-716), as
 // k_quantize does it -- d = amax/127, inv = 1/d or 0, q = round(x*inv)

@@ -32,6 +32,7 @@
 //              which clip the ragged M and N edges.
 // Every wait is bounded (see rwq_sm100.cuh).
 #include <cuda.h>
+#include <cuda_fp16.h>
 #include <cudaTypedefs.h>
 #include <cstdio>
 #include <cstring>
@@ -384,7 +385,8 @@ __global__ void __launch_bounds__(wide::THREADS, 1)
     k_gemm_fold_w(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                   const __grid_constant__ CUtensorMap tmY, const __grid_constant__ CUtensorMap tmD, int use_tma_store,
                   const float* __restrict__ colscale, const float* __restrict__ bias, float* __restrict__ Y, int M,
-                  int N, int nb, int* __restrict__ err_flag) {
+                  int N, int nb, int* __restrict__ err_flag, const __grid_constant__ CUtensorMap tmQ,
+                  float* __restrict__ qdT, float* __restrict__ quT, int q_m_pad) {
     constexpr int BN = wide::BN, EW = wide::EW, CPW = wide::CPW;
     constexpr int A_BYTES = wide::A_BYTES, STAGE_BYTES = wide::STAGE_BYTES, STAGES = wide::STAGES;
     constexpr int NBUF = wide::NBUF, DA_SLOTS = wide::DA_SLOTS;
@@ -519,7 +521,67 @@ __global__ void __launch_bounds__(wide::THREADS, 1)
         const int col0 = n0 + h * CPW;
         const int row = m0 + q * 32 + lane;
         asm volatile("bar.sync 1, %0;" ::"r"(EW * 32) : "memory");   // scales and bias in place
-        if (!*abort) {
+        if (!*abort && q_m_pad > 0) {
+            // GELU, then the reference's int8 quantizer per 32-column block,
+            // straight into the next GEMM's operand: f16 codes through the
+            // staging boxes (tmQ, 64 f16 x 32 rows, 128-byte swizzle), d_a and
+            // d_a*sum(q_a) transposed [block][m_pad].  Each thread holds one
+            // row's whole blocks, so the values and their order are those of
+            // a GEMM writing y and the GELU row kernel quantizing it.
+            uint8_t* box = base + (warp - EPI0) * 4096 + lane * 128;
+#pragma unroll
+            for (int j = 0; j < CPW / 32; ++j) {
+                float amax = 0.f;
+#pragma unroll
+                for (int i = 0; i < 16; ++i) {
+                    const int col = col0 + j * 32 + 2 * i;   // < n0 + BN <= N on this path
+                    float2 v = make_float2(__fmul_rn(acc[j * 16 + i].x, bar->cs[col - n0]),
+                                           __fmul_rn(acc[j * 16 + i].y, bar->cs[col - n0 + 1]));
+                    if (bias) {
+                        v.x = __fadd_rn(v.x, bar->bs[col - n0]);
+                        v.y = __fadd_rn(v.y, bar->bs[col - n0 + 1]);
+                    }
+                    v = make_float2(gelu_ref(v.x), gelu_ref(v.y));
+                    acc[j * 16 + i] = v;
+                    const float ax = fabsf(v.x), ay = fabsf(v.y);
+                    amax = fmaxf(amax, fmaxf(isnan(ax) ? 0.f : ax, isnan(ay) ? 0.f : ay));
+                }
+                const float d = __fdiv_rn(amax, 127.0f);
+                const float inv = d > 0.f ? __fdiv_rn(1.0f, d) : 0.f;
+                auto code = [inv](float v) {
+                    const float r = roundf(__fmul_rn(v, inv));
+                    return isnan(r) ? 0 : int(fminf(127.f, fmaxf(-127.f, r)));
+                };
+                int sum = 0;
+#pragma unroll
+                for (int ch = 0; ch < 4; ++ch) {   // 8 codes = one 16-byte chunk of the row
+                    uint32_t w[4];
+#pragma unroll
+                    for (int p2 = 0; p2 < 4; ++p2) {
+                        const float2 v = acc[j * 16 + ch * 4 + p2];
+                        const int c0 = code(v.x), c1 = code(v.y);
+                        sum += c0 + c1;
+                        w[p2] = uint32_t(__half_as_ushort(__int2half_rn(c0))) |
+                                (uint32_t(__half_as_ushort(__int2half_rn(c1))) << 16);
+                    }
+                    const int chunk = j * 4 + ch;
+                    *reinterpret_cast<uint4*>(box + ((chunk ^ (lane & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+                }
+                if (row < q_m_pad) {
+                    const size_t bl = size_t((col0 + j * 32) / QK);
+                    qdT[bl * q_m_pad + row] = row < M ? d : 0.f;
+                    quT[bl * q_m_pad + row] = row < M ? __fmul_rn(d, float(sum)) : 0.f;
+                }
+            }
+            fence_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+                if (m0 + q * 32 < M) tma_store_2d(&tmQ, col0, m0 + q * 32, base + (warp - EPI0) * 4096);
+                bulk_commit();
+                bulk_wait_read_all();
+            }
+            __syncwarp();
+        } else if (!*abort) {
             if (use_tma_store) {
                 // Staging for this warp: CPW/32 boxes of 32 rows x 128 bytes,
                 // 128-byte swizzle (16-byte chunk c of row r at c ^ (r & 7)).
@@ -686,8 +748,10 @@ bool fold_wide(int dev, int m, int n, int nb) {
     return wide_t < narrow;
 }
 
+// qout (optional): instead of y, GELU of the output quantized into this
+// GEMM-layout operand (q16, dT, uT, m_pad; k = w.n).
 cudaError_t launch_fold_wide(const ActsView& v, const Weight& w, const float* bias, float* y, int* err_flag,
-                             cudaStream_t s, char* why, size_t why_len) {
+                             cudaStream_t s, char* why, size_t why_len, const ActsView* qout = nullptr) {
     const int dev = cur_dev();
     cudaError_t e = wide_smem_attr(dev);
     if (e != cudaSuccess) return e;
@@ -701,15 +765,21 @@ cudaError_t launch_fold_wide(const ActsView& v, const Weight& w, const float* bi
     if (!encode_map(&md, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, v.dT, uint64_t(v.m_pad), uint64_t(w.nb), BM, DA_GROUP,
                     CU_TENSOR_MAP_SWIZZLE_NONE, why, why_len))
         return cudaErrorInvalidValue;
-    int use_tma_store = (w.n % 4 == 0) && (reinterpret_cast<uintptr_t>(y) % 16 == 0);
+    int use_tma_store = !qout && (w.n % 4 == 0) && (reinterpret_cast<uintptr_t>(y) % 16 == 0);
     if (use_tma_store && !encode_map(&my, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, y, uint64_t(w.n), uint64_t(v.m), 32, 32,
                                      CU_TENSOR_MAP_SWIZZLE_128B, why, why_len))
         use_tma_store = 0;
     if (!use_tma_store) memset(&my, 0, sizeof my);
+    CUtensorMap mq;
+    memset(&mq, 0, sizeof mq);
+    if (qout && !encode_map(&mq, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, qout->q16, uint64_t(w.n), uint64_t(v.m), 64, 32,
+                            CU_TENSOR_MAP_SWIZZLE_128B, why, why_len))
+        return cudaErrorInvalidValue;
     const int nt = (w.n + wide::BN - 1) / wide::BN, mt = (v.m + BM - 1) / BM;
     const dim3 grid(static_cast<unsigned>(nt), static_cast<unsigned>(mt));
     return launch_pdl(k_gemm_fold_w, grid, dim3(wide::THREADS), wide::SMEM, s, ma, mb, my, md, use_tma_store,
-                      w.colscale, bias, y, v.m, w.n, w.nb, err_flag);
+                      w.colscale, bias, y, v.m, w.n, w.nb, err_flag, mq, qout ? qout->dT : nullptr,
+                      qout ? qout->uT : nullptr, qout ? qout->m_pad : 0);
 }
 
 cudaError_t launch_fold(const ActsView& v, const Weight& w, const float* bias, float* y, int* err_flag,
@@ -730,6 +800,18 @@ cudaError_t launch_gemm_fold(const ActsView& v, const Weight& w, const float* bi
                              cudaStream_t s, char* why, size_t why_len) {
     if (v.m <= 0 || w.n <= 0) return cudaSuccess;
     return launch_fold(v, w, bias, y, err_flag, s, why, why_len);
+}
+
+bool gemm_fold_gelu_fits(const ActsView& v, const Weight& w, const ActsView& out) {
+    auto al = [](const void* p, uintptr_t a) { return p && (reinterpret_cast<uintptr_t>(p) % a) == 0; };
+    return v.m > 0 && w.n % wide::BN == 0 && out.k == w.n && out.m_pad >= v.m && al(out.q16, 16) && al(out.dT, 4) &&
+           al(out.uT, 4);
+}
+
+cudaError_t launch_gemm_fold_gelu(const ActsView& v, const Weight& w, const float* bias, const ActsView& out,
+                                  int* err_flag, cudaStream_t s, char* why, size_t why_len) {
+    if (!gemm_fold_gelu_fits(v, w, out)) return cudaErrorInvalidValue;
+    return launch_fold_wide(v, w, bias, nullptr, err_flag, s, why, why_len, &out);
 }
 
 int gemm_fold_config(int m, int n, int nb) { return fold_wide(cur_dev(), m, n, nb) ? 2 : 1; }

@@ -92,6 +92,14 @@ cudaError_t launch_gemm_tc(const ActsView& v, const Weight& w, const float* bias
 // tcgen05 GEMM with the weight scales folded into the B operand.
 cudaError_t launch_gemm_fold(const ActsView& v, const Weight& w, const float* bias, float* y, int* err_flag,
                              cudaStream_t s, char* why, size_t why_len);
+// k_gemm_fold on 128 x 256 tiles whose epilogue applies GELU to y (with
+// bias) and quantizes it, per 32-column block as the reference's int8
+// quantizer does, straight into `out`'s GEMM-layout operand (q16, dT, uT;
+// out.k == w.n, a multiple of 256): the encoder's fc1 without its f32
+// output and the row kernel that would read it back.
+bool gemm_fold_gelu_fits(const ActsView& v, const Weight& w, const ActsView& out);
+cudaError_t launch_gemm_fold_gelu(const ActsView& v, const Weight& w, const float* bias, const ActsView& out,
+                                  int* err_flag, cudaStream_t s, char* why, size_t why_len);
 // The tile width k_gemm_fold picks for an m x n GEMM of nb blocks on the
 // current device: 1 = 128- or 64-column tiles, 2 = 128 x 256 tiles.
 int gemm_fold_config(int m, int n, int nb);
