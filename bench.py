@@ -388,10 +388,11 @@ def run_encoder(args, dev, tc_peak, stream, rank, world):
            "gflop_per_window": {"quant_linear": round(lin / 1e9, 2), "attention": round(att / 1e9, 2),
                                 "conv": round(conv / 1e9, 2)},
            "achieved_TFLOPs": round(fl / tb / 1e12, 1), "frac_of_measured_bf16": round(fl / tb / 1e12 / tc_peak, 4),
-           "kernels": "k_rows_quant, k_gemm_fold(_w) (fc1 with GELU + quantize in its epilogue), k_to_heads, k_attn; "
+           "kernels": "k_rows_quant, k_gemm_fold_w (Q/K/V writing f16 heads, fc1 with GELU + quantize in its "
+                      "epilogue), k_gemm_fold, k_attn; "
                       "conv stem: k_im2col_split + k_gemm_hl (f16 hi|lo "
                       "tensor cores) + k_bias_gelu",
-           "gpu_launches_per_batch": 4 + 6 * 12 + 1,   # fc1 quantizes its GELU output for fc2 itself
+           "gpu_launches_per_batch": 4 + 6 * 9 + 1,   # Q/K/V write heads, fc1 quantizes its GELU output itself
            "data": "synthetic (seeded): random-init weights N(0, 0.02) quantized to Q5_1, mel N(-0.5, 0.3)"}
     if rank == 0 and world == 1 and not args.no_cpu:
         import oracle

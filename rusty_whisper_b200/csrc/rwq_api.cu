@@ -383,6 +383,23 @@ int rwq::gemm_gelu_quantized(const ActsView& v, rwq_qtensor* w, const float* bia
     return RWQ_OK;
 }
 
+bool rwq::gemm_heads_fits(const ActsView& v, rwq_qtensor* w, int n_win, int T, int H, const __half* dst) {
+    return w && t_gemm_path != 3 && !v.ahl && v.k == w->w.k && rwq::gemm_fold_heads_fits(v, w->w, n_win, T, H, dst);
+}
+
+int rwq::gemm_heads(const ActsView& v, rwq_qtensor* w, const float* bias, __half* dst, int n_win, int T, int H,
+                    float scale, cudaStream_t s) {
+    if (!gemm_heads_fits(v, w, n_win, T, H, dst)) return fail(RWQ_ERR_ARG, "fused heads GEMM does not apply here");
+    Workspace* ws = nullptr;
+    int rc = get_workspace(s, &ws);
+    if (rc) return rc;
+    if ((rc = weight_fold_cache(w, s))) return rc;
+    char why[256] = {0};
+    cudaError_t e = rwq::launch_gemm_fold_heads(v, w->w, bias, dst, n_win, T, H, scale, ws->err, s, why, sizeof why);
+    if (e != cudaSuccess) return fail(RWQ_ERR_CUDA, "gemm launch: %s %s", cudaGetErrorString(e), why);
+    return RWQ_OK;
+}
+
 int rwq::linear_acts(const ActsView& v, bool gemm, rwq_qtensor* w, const float* bias, float* out, cudaStream_t s) {
     Workspace* ws = nullptr;
     int rc = get_workspace(s, &ws);

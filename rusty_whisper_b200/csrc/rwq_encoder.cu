@@ -252,12 +252,20 @@ int encode_batch(rwq_encoder* e, const Bufs& b, const float* mel, int nwin, floa
         ENC_CUDA(rwq::launch_rows_quant(l ? rwq::RQ_ADD_LN : rwq::RQ_LN, b.x, b.tmp, b.x, W(lname(l, "attn_ln.weight")),
                                         W(lname(l, "attn_ln.bias")), M, D, m_pad, aD.q16, aD.dT, aD.uT, nullptr, s),
                  "attn_ln");
-        ENC_RC(rwq::gemm_quantized(aD, L.q, W(lname(l, "attn.query.bias")), b.q, s));
-        ENC_RC(rwq::gemm_quantized(aD, L.k, nullptr, b.k, s));   // whisper's key projection has no bias
-        ENC_RC(rwq::gemm_quantized(aD, L.v, W(lname(l, "attn.value.bias")), b.v, s));
-        ENC_CUDA(rwq::launch_to_heads(b.q, D, 0, nwin, T, H, qscale, b.qh, s), "q heads");
-        ENC_CUDA(rwq::launch_to_heads(b.k, D, 0, nwin, T, H, 1.0f, b.kh, s), "k heads");
-        ENC_CUDA(rwq::launch_to_heads(b.v, D, 0, nwin, T, H, 1.0f, b.vh, s), "v heads");
+        if (rwq::gemm_heads_fits(aD, L.q, nwin, T, H, b.qh) && rwq::gemm_heads_fits(aD, L.k, nwin, T, H, b.kh) &&
+            rwq::gemm_heads_fits(aD, L.v, nwin, T, H, b.vh)) {
+            // the projections write their f16 heads themselves
+            ENC_RC(rwq::gemm_heads(aD, L.q, W(lname(l, "attn.query.bias")), b.qh, nwin, T, H, qscale, s));
+            ENC_RC(rwq::gemm_heads(aD, L.k, nullptr, b.kh, nwin, T, H, 1.0f, s));   // no key bias in whisper
+            ENC_RC(rwq::gemm_heads(aD, L.v, W(lname(l, "attn.value.bias")), b.vh, nwin, T, H, 1.0f, s));
+        } else {
+            ENC_RC(rwq::gemm_quantized(aD, L.q, W(lname(l, "attn.query.bias")), b.q, s));
+            ENC_RC(rwq::gemm_quantized(aD, L.k, nullptr, b.k, s));   // whisper's key projection has no bias
+            ENC_RC(rwq::gemm_quantized(aD, L.v, W(lname(l, "attn.value.bias")), b.v, s));
+            ENC_CUDA(rwq::launch_to_heads(b.q, D, 0, nwin, T, H, qscale, b.qh, s), "q heads");
+            ENC_CUDA(rwq::launch_to_heads(b.k, D, 0, nwin, T, H, 1.0f, b.kh, s), "k heads");
+            ENC_CUDA(rwq::launch_to_heads(b.v, D, 0, nwin, T, H, 1.0f, b.vh, s), "v heads");
+        }
         ENC_CUDA(rwq::launch_attention(b.qh, b.kh, b.vh, nwin, T, H, b.att, s), "attention");
         ENC_CUDA(rwq::launch_rows_quant(rwq::RQ_PLAIN, b.att, nullptr, nullptr, nullptr, nullptr, M, D, m_pad, aD.q16,
                                         aD.dT, aD.uT, nullptr, s),

@@ -43,6 +43,13 @@ int gemm_quantized(const ActsView& v, rwq_qtensor* w, const float* bias, float* 
 // fused (w.n a multiple of 256, the default tensor-core path); otherwise
 // the caller runs gemm_quantized and the GELU row kernel.
 bool gemm_gelu_quantized_fits(const ActsView& v, rwq_qtensor* w, const ActsView& out);
+// Same GEMM writing f16 attention heads [n_win][H][T][64] of (A W^T + bias)
+// * scale directly (the encoder's Q, K and V: no f32 output, no
+// launch_to_heads); the _fits predicate as above (w.n == H * 64, a multiple
+// of 256).
+bool gemm_heads_fits(const ActsView& v, rwq_qtensor* w, int n_win, int T, int H, const __half* dst);
+int gemm_heads(const ActsView& v, rwq_qtensor* w, const float* bias, __half* dst, int n_win, int T, int H, float scale,
+               cudaStream_t s);
 int gemm_gelu_quantized(const ActsView& v, rwq_qtensor* w, const float* bias, const ActsView& out, cudaStream_t s);
 
 // Same on either layout: `gemm` false reads the GEMV layout (q8, d, sum, u;

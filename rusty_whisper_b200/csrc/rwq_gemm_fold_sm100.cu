@@ -386,7 +386,8 @@ __global__ void __launch_bounds__(wide::THREADS, 1)
                   const __grid_constant__ CUtensorMap tmY, const __grid_constant__ CUtensorMap tmD, int use_tma_store,
                   const float* __restrict__ colscale, const float* __restrict__ bias, float* __restrict__ Y, int M,
                   int N, int nb, int* __restrict__ err_flag, const __grid_constant__ CUtensorMap tmQ,
-                  float* __restrict__ qdT, float* __restrict__ quT, int q_m_pad) {
+                  float* __restrict__ qdT, float* __restrict__ quT, int q_m_pad, __half* __restrict__ hdst,
+                  int hT, int hH, float hscale) {
     constexpr int BN = wide::BN, EW = wide::EW, CPW = wide::CPW;
     constexpr int A_BYTES = wide::A_BYTES, STAGE_BYTES = wide::STAGE_BYTES, STAGES = wide::STAGES;
     constexpr int NBUF = wide::NBUF, DA_SLOTS = wide::DA_SLOTS;
@@ -581,6 +582,47 @@ __global__ void __launch_bounds__(wide::THREADS, 1)
                 bulk_wait_read_all();
             }
             __syncwarp();
+        } else if (!*abort && hdst) {
+            // Attention heads: f16(y * hscale) of row (window w, frame t) and
+            // head c/64 at hdst[((w*H + c/64)*T + t)*64 + c%64] -- a warp's
+            // 64 columns are one head.  Rows of one window go out as one
+            // 32 x 64 f16 TMA box (tmQ over [W*H*T][64]); a warp whose rows
+            // cross a window boundary stores its rows itself.
+            uint8_t* box = base + (warp - EPI0) * 4096 + lane * 128;
+#pragma unroll
+            for (int ch = 0; ch < 8; ++ch) {
+                uint32_t wv[4];
+#pragma unroll
+                for (int p2 = 0; p2 < 4; ++p2) {
+                    const int i = ch * 4 + p2, col = col0 + 2 * i;
+                    float2 v = make_float2(__fmul_rn(acc[i].x, bar->cs[col - n0]),
+                                           __fmul_rn(acc[i].y, bar->cs[col - n0 + 1]));
+                    if (bias) {
+                        v.x = __fadd_rn(v.x, bar->bs[col - n0]);
+                        v.y = __fadd_rn(v.y, bar->bs[col - n0 + 1]);
+                    }
+                    const __half2 hv = __floats2half2_rn(__fmul_rn(v.x, hscale), __fmul_rn(v.y, hscale));
+                    wv[p2] = *reinterpret_cast<const uint32_t*>(&hv);
+                }
+                *reinterpret_cast<uint4*>(box + ((ch ^ (lane & 7)) << 4)) = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+            }
+            fence_async_smem();
+            __syncwarp();
+            const int r0 = m0 + q * 32, hd = col0 / 64;
+            const int w0 = r0 / hT, t0 = r0 - w0 * hT;
+            if (t0 + 32 <= hT) {
+                if (lane == 0) {
+                    if (r0 < M) tma_store_2d(&tmQ, 0, (w0 * hH + hd) * hT + t0, base + (warp - EPI0) * 4096);
+                    bulk_commit();
+                    bulk_wait_read_all();
+                }
+            } else if (row < M) {
+                const int w = row / hT, t = row - w * hT;
+                uint4* dst = reinterpret_cast<uint4*>(hdst + ((size_t(w) * hH + hd) * hT + t) * 64);
+#pragma unroll
+                for (int ch = 0; ch < 8; ++ch) dst[ch] = *reinterpret_cast<const uint4*>(box + ((ch ^ (lane & 7)) << 4));
+            }
+            __syncwarp();
         } else if (!*abort) {
             if (use_tma_store) {
                 // Staging for this warp: CPW/32 boxes of 32 rows x 128 bytes,
@@ -750,8 +792,16 @@ bool fold_wide(int dev, int m, int n, int nb) {
 
 // qout (optional): instead of y, GELU of the output quantized into this
 // GEMM-layout operand (q16, dT, uT, m_pad; k = w.n).
+// heads (optional): instead of y, f16 attention heads [n_win][H][T][64] of
+// y * scale (v.m == n_win * T, w.n == H * 64).
+struct HeadsOut {
+    __half* dst;
+    int n_win, T, H;
+    float scale;
+};
 cudaError_t launch_fold_wide(const ActsView& v, const Weight& w, const float* bias, float* y, int* err_flag,
-                             cudaStream_t s, char* why, size_t why_len, const ActsView* qout = nullptr) {
+                             cudaStream_t s, char* why, size_t why_len, const ActsView* qout = nullptr,
+                             const HeadsOut* heads = nullptr) {
     const int dev = cur_dev();
     cudaError_t e = wide_smem_attr(dev);
     if (e != cudaSuccess) return e;
@@ -765,7 +815,7 @@ cudaError_t launch_fold_wide(const ActsView& v, const Weight& w, const float* bi
     if (!encode_map(&md, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, v.dT, uint64_t(v.m_pad), uint64_t(w.nb), BM, DA_GROUP,
                     CU_TENSOR_MAP_SWIZZLE_NONE, why, why_len))
         return cudaErrorInvalidValue;
-    int use_tma_store = !qout && (w.n % 4 == 0) && (reinterpret_cast<uintptr_t>(y) % 16 == 0);
+    int use_tma_store = !qout && !heads && (w.n % 4 == 0) && (reinterpret_cast<uintptr_t>(y) % 16 == 0);
     if (use_tma_store && !encode_map(&my, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, y, uint64_t(w.n), uint64_t(v.m), 32, 32,
                                      CU_TENSOR_MAP_SWIZZLE_128B, why, why_len))
         use_tma_store = 0;
@@ -775,11 +825,16 @@ cudaError_t launch_fold_wide(const ActsView& v, const Weight& w, const float* bi
     if (qout && !encode_map(&mq, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, qout->q16, uint64_t(w.n), uint64_t(v.m), 64, 32,
                             CU_TENSOR_MAP_SWIZZLE_128B, why, why_len))
         return cudaErrorInvalidValue;
+    if (heads && !encode_map(&mq, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, heads->dst, 64,
+                             uint64_t(heads->n_win) * heads->H * heads->T, 64, 32, CU_TENSOR_MAP_SWIZZLE_128B, why,
+                             why_len))
+        return cudaErrorInvalidValue;
     const int nt = (w.n + wide::BN - 1) / wide::BN, mt = (v.m + BM - 1) / BM;
     const dim3 grid(static_cast<unsigned>(nt), static_cast<unsigned>(mt));
     return launch_pdl(k_gemm_fold_w, grid, dim3(wide::THREADS), wide::SMEM, s, ma, mb, my, md, use_tma_store,
                       w.colscale, bias, y, v.m, w.n, w.nb, err_flag, mq, qout ? qout->dT : nullptr,
-                      qout ? qout->uT : nullptr, qout ? qout->m_pad : 0);
+                      qout ? qout->uT : nullptr, qout ? qout->m_pad : 0, heads ? heads->dst : nullptr,
+                      heads ? heads->T : 1, heads ? heads->H : 1, heads ? heads->scale : 1.0f);
 }
 
 cudaError_t launch_fold(const ActsView& v, const Weight& w, const float* bias, float* y, int* err_flag,
@@ -812,6 +867,19 @@ cudaError_t launch_gemm_fold_gelu(const ActsView& v, const Weight& w, const floa
                                   int* err_flag, cudaStream_t s, char* why, size_t why_len) {
     if (!gemm_fold_gelu_fits(v, w, out)) return cudaErrorInvalidValue;
     return launch_fold_wide(v, w, bias, nullptr, err_flag, s, why, why_len, &out);
+}
+
+bool gemm_fold_heads_fits(const ActsView& v, const Weight& w, int n_win, int T, int H, const __half* dst) {
+    return v.m > 0 && v.m == n_win * T && T >= 32 && w.n == H * 64 && w.n % wide::BN == 0 && dst &&
+           (reinterpret_cast<uintptr_t>(dst) % 16) == 0;
+}
+
+cudaError_t launch_gemm_fold_heads(const ActsView& v, const Weight& w, const float* bias, __half* dst, int n_win,
+                                   int T, int H, float scale, int* err_flag, cudaStream_t s, char* why,
+                                   size_t why_len) {
+    if (!gemm_fold_heads_fits(v, w, n_win, T, H, dst)) return cudaErrorInvalidValue;
+    const HeadsOut ho{dst, n_win, T, H, scale};
+    return launch_fold_wide(v, w, bias, nullptr, err_flag, s, why, why_len, nullptr, &ho);
 }
 
 int gemm_fold_config(int m, int n, int nb) { return fold_wide(cur_dev(), m, n, nb) ? 2 : 1; }

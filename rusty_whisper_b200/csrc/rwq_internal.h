@@ -3,6 +3,7 @@
 #pragma once
 #include <cstddef>
 #include <cstdint>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 namespace rwq {
@@ -100,6 +101,14 @@ cudaError_t launch_gemm_fold(const ActsView& v, const Weight& w, const float* bi
 bool gemm_fold_gelu_fits(const ActsView& v, const Weight& w, const ActsView& out);
 cudaError_t launch_gemm_fold_gelu(const ActsView& v, const Weight& w, const float* bias, const ActsView& out,
                                   int* err_flag, cudaStream_t s, char* why, size_t why_len);
+// k_gemm_fold on 128 x 256 tiles writing f16 attention heads
+// [n_win][H][T][64] of y * scale (v.m == n_win * T, w.n == H * 64, a
+// multiple of 256): the encoder's Q, K and V projections without their f32
+// outputs and the conversion kernel that would read them back.
+bool gemm_fold_heads_fits(const ActsView& v, const Weight& w, int n_win, int T, int H, const __half* dst);
+cudaError_t launch_gemm_fold_heads(const ActsView& v, const Weight& w, const float* bias, __half* dst, int n_win,
+                                   int T, int H, float scale, int* err_flag, cudaStream_t s, char* why,
+                                   size_t why_len);
 // The tile width k_gemm_fold picks for an m x n GEMM of nb blocks on the
 // current device: 1 = 128- or 64-column tiles, 2 = 128 x 256 tiles.
 int gemm_fold_config(int m, int n, int nb);
