@@ -266,10 +266,9 @@ int encode_batch(rwq_encoder* e, const Bufs& b, const float* mel, int nwin, floa
             ENC_CUDA(rwq::launch_to_heads(b.k, D, 0, nwin, T, H, 1.0f, b.kh, s), "k heads");
             ENC_CUDA(rwq::launch_to_heads(b.v, D, 0, nwin, T, H, 1.0f, b.vh, s), "v heads");
         }
-        ENC_CUDA(rwq::launch_attention(b.qh, b.kh, b.vh, nwin, T, H, b.att, s), "attention");
-        ENC_CUDA(rwq::launch_rows_quant(rwq::RQ_PLAIN, b.att, nullptr, nullptr, nullptr, nullptr, M, D, m_pad, aD.q16,
-                                        aD.dT, aD.uT, nullptr, s),
-                 "quantize attention");
+        // attention output rows quantized by the attention kernel itself
+        ENC_CUDA(rwq::launch_attention(b.qh, b.kh, b.vh, nwin, T, H, b.att, s, aD.q16, aD.dT, aD.uT, m_pad),
+                 "attention");
         ENC_RC(rwq::gemm_quantized(aD, L.o, W(lname(l, "attn.out.bias")), b.tmp, s));
         ENC_CUDA(rwq::launch_rows_quant(rwq::RQ_ADD_LN, b.x, b.tmp, b.x, W(lname(l, "mlp_ln.weight")),
                                         W(lname(l, "mlp_ln.bias")), M, D, m_pad, aD.q16, aD.dT, aD.uT, nullptr, s),

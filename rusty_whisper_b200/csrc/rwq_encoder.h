@@ -28,8 +28,11 @@ cudaError_t launch_bias_gelu(float* y, size_t rows, int cols, const float* bias,
                              cudaStream_t s);
 cudaError_t launch_to_heads(const float* src, int ld, int col0, int n_win, int T, int H, float scale, __half* dst,
                             cudaStream_t s);
+// With q16 set, the output rows go quantized into that GEMM-layout operand
+// (q16 [n_win*T][H*64], dT and uT [H*2][m_pad]) instead of f32 into `out`.
 cudaError_t launch_attention(const __half* Qh, const __half* Kh, const __half* Vh, int n_win, int T, int H,
-                             float* out, cudaStream_t s);
+                             float* out, cudaStream_t s, uint16_t* q16 = nullptr, float* dT = nullptr,
+                             float* uT = nullptr, int m_pad = 0);
 
 // The tensor-core GEMM on activations already quantized into `v` (GEMM
 // layout): out = A W^T (+ bias).  Builds the weight's operand cache on

@@ -278,9 +278,13 @@ __device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
     return *reinterpret_cast<const uint32_t*>(&h);
 }
 
+// QOUT: the output rows quantized straight into the GEMM-layout operand of
+// the next linear (o.q16, o.dT, o.uT), as the quantizer row kernel would
+// write them, instead of f32 rows into `out`.
+template <bool QOUT>
 __global__ void __launch_bounds__(AT_THREADS) k_attn(const __half* __restrict__ Qh, const __half* __restrict__ Kh,
                                                      const __half* __restrict__ Vh, int T, int H,
-                                                     float* __restrict__ out) {
+                                                     float* __restrict__ out, QOut qo) {
     pdl_trigger();
     __shared__ __align__(128) uint8_t sQ[AT_Q * 128];
     __shared__ __align__(128) uint8_t sK[2][AT_K * 128];
@@ -412,12 +416,58 @@ __global__ void __launch_bounds__(AT_THREADS) k_attn(const __half* __restrict__ 
 #pragma unroll
     for (int r = 0; r < 2; ++r) {
         const int t = q0 + warp * 16 + g + r * 8;
-        if (t >= T) continue;
         const float inv = 1.0f / lrow[r];
-        float* dst = out + (size_t(w) * T + t) * D + h * AT_D;
+        if constexpr (QOUT) {
+            // Two 32-column blocks per row of this head (columns 0-31: n-tiles
+            // 0-3, 32-63: 4-7), spread over the quad's four lanes: the
+            // reference quantizer with the block's amax and code sum over the
+            // quad (every lane runs the shuffles; rows past T write nothing).
+            const size_t row = size_t(w) * T + t;
 #pragma unroll
-        for (int nt = 0; nt < 8; ++nt)
-            *reinterpret_cast<float2*>(dst + nt * 8 + tig * 2) = make_float2(o[nt][2 * r] * inv, o[nt][2 * r + 1] * inv);
+            for (int hb = 0; hb < 2; ++hb) {
+                float v[8], amax = 0.f;
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    v[2 * j] = o[hb * 4 + j][2 * r] * inv;
+                    v[2 * j + 1] = o[hb * 4 + j][2 * r + 1] * inv;
+                    const float a0 = fabsf(v[2 * j]), a1 = fabsf(v[2 * j + 1]);
+                    amax = fmaxf(amax, fmaxf(isnan(a0) ? 0.f : a0, isnan(a1) ? 0.f : a1));
+                }
+                amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+                amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+                const float d = __fdiv_rn(amax, 127.0f);
+                const float qinv = d > 0.f ? __fdiv_rn(1.0f, d) : 0.f;
+                int c[8], sum = 0;
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                    const float rr = roundf(__fmul_rn(v[e], qinv));
+                    c[e] = isnan(rr) ? 0 : int(fminf(127.f, fmaxf(-127.f, rr)));
+                    sum += c[e];
+                }
+                sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+                sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+                if (t < T) {
+                    uint16_t* dst = qo.q16 + row * D + h * AT_D + hb * 32;
+#pragma unroll
+                    for (int j = 0; j < 4; ++j)
+                        *reinterpret_cast<uint32_t*>(dst + j * 8 + tig * 2) =
+                            uint32_t(__half_as_ushort(__int2half_rn(c[2 * j]))) |
+                            (uint32_t(__half_as_ushort(__int2half_rn(c[2 * j + 1]))) << 16);
+                    if (tig == 0) {
+                        const size_t bl = size_t(h) * 2 + hb;
+                        qo.dT[bl * qo.m_pad + row] = d;
+                        qo.uT[bl * qo.m_pad + row] = __fmul_rn(d, float(sum));
+                    }
+                }
+            }
+        } else {
+            if (t >= T) continue;
+            float* dst = out + (size_t(w) * T + t) * D + h * AT_D;
+#pragma unroll
+            for (int nt = 0; nt < 8; ++nt)
+                *reinterpret_cast<float2*>(dst + nt * 8 + tig * 2) =
+                    make_float2(o[nt][2 * r] * inv, o[nt][2 * r + 1] * inv);
+        }
     }
 }
 
@@ -508,10 +558,18 @@ cudaError_t launch_to_heads(const float* src, int ld, int col0, int n_win, int T
 }
 
 cudaError_t launch_attention(const __half* Qh, const __half* Kh, const __half* Vh, int n_win, int T, int H,
-                             float* out, cudaStream_t s) {
+                             float* out, cudaStream_t s, uint16_t* q16, float* dT, float* uT, int m_pad) {
     if (!n_win || !T || !H) return cudaSuccess;
     dim3 grid((T + AT_Q - 1) / AT_Q, H, n_win);
-    return launch_pdl(k_attn, grid, dim3(AT_THREADS), 0, s, Qh, Kh, Vh, T, H, out);
+    QOut qo{};
+    if (q16) {
+        qo.q16 = q16;
+        qo.dT = dT;
+        qo.uT = uT;
+        qo.m_pad = m_pad;
+        return launch_pdl(k_attn<true>, grid, dim3(AT_THREADS), 0, s, Qh, Kh, Vh, T, H, out, qo);
+    }
+    return launch_pdl(k_attn<false>, grid, dim3(AT_THREADS), 0, s, Qh, Kh, Vh, T, H, out, qo);
 }
 
 }  // namespace rwq
