@@ -611,11 +611,19 @@ int rwq_decoder_begin(rwq_decoder* d, const float* enc_out, int64_t n_windows, i
                      "quantize encoder output");
             for (int l = 0; l < d->n_layer; ++l) {
                 const DLayer& L = d->layers[size_t(l)];
-                DEC_RC(rwq::gemm_quantized(a, L.xk, nullptr, kt, s));
-                DEC_RC(rwq::gemm_quantized(a, L.xv, d->dense[lname(l, "cross_attn.value.bias")], vt, s));
                 const size_t lo = (size_t(l) * W + w0) * H * size_t(T) * 64;
-                DEC_CUDA(rwq::launch_to_heads(kt, D, 0, nw, T, H, 1.0f, d->cross_k + lo, s), "cross k heads");
-                DEC_CUDA(rwq::launch_to_heads(vt, D, 0, nw, T, H, 1.0f, d->cross_v + lo, s), "cross v heads");
+                const float* vb = d->dense[lname(l, "cross_attn.value.bias")];
+                if (rwq::gemm_heads_fits(a, L.xk, nw, T, H, d->cross_k + lo) &&
+                    rwq::gemm_heads_fits(a, L.xv, nw, T, H, d->cross_v + lo)) {
+                    // the projections write their f16 heads themselves
+                    DEC_RC(rwq::gemm_heads(a, L.xk, nullptr, d->cross_k + lo, nw, T, H, 1.0f, s));
+                    DEC_RC(rwq::gemm_heads(a, L.xv, vb, d->cross_v + lo, nw, T, H, 1.0f, s));
+                } else {
+                    DEC_RC(rwq::gemm_quantized(a, L.xk, nullptr, kt, s));
+                    DEC_RC(rwq::gemm_quantized(a, L.xv, vb, vt, s));
+                    DEC_CUDA(rwq::launch_to_heads(kt, D, 0, nw, T, H, 1.0f, d->cross_k + lo, s), "cross k heads");
+                    DEC_CUDA(rwq::launch_to_heads(vt, D, 0, nw, T, H, 1.0f, d->cross_v + lo, s), "cross v heads");
+                }
             }
             return int(RWQ_OK);
         });
