@@ -282,7 +282,7 @@ __device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
 // the next linear (o.q16, o.dT, o.uT), as the quantizer row kernel would
 // write them, instead of f32 rows into `out`.
 template <bool QOUT>
-__global__ void __launch_bounds__(AT_THREADS) k_attn(const __half* __restrict__ Qh, const __half* __restrict__ Kh,
+__global__ void __launch_bounds__(AT_THREADS, 4) k_attn(const __half* __restrict__ Qh, const __half* __restrict__ Kh,
                                                      const __half* __restrict__ Vh, int T, int H,
                                                      float* __restrict__ out, QOut qo) {
     pdl_trigger();
