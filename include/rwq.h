@@ -294,6 +294,18 @@ int rwq_conv1d_dev(const float* x, int64_t n_win, int64_t in_ch, int64_t t_in, c
 int rwq_attention_dev(const float* q, const float* k, const float* v, int64_t n_windows, int64_t t, int64_t n_state,
                       int64_t n_head, float* out, void* stream);
 
+/* The encoder's and decoder's row transform: with `add` non-NULL first
+ * x_out = x + add (x_out may be x: the residual stream in place), then the
+ * LayerNorm of each of the m rows of k (`layer_norm`, src/tensor.rs:274-289,
+ * eps 1e-5) into y[m, k] and/or, quantized by `quantize_acts_i8`
+ * (quant.rs:690-716), into q[m, k] int8, d[m, k/32] f32, sum[m, k/32]
+ * int32 -- the operand the next quantized linear reads.  y or q may be
+ * NULL (not both); q, d and sum go together.  k % 128 == 0; x, add, x_out,
+ * y, weight and bias 16-byte aligned; device pointers.  A row's result is
+ * the same bits whatever m is. */
+int rwq_layer_norm_dev(const float* x, const float* add, float* x_out, const float* weight, const float* bias,
+                       int64_t m, int64_t k, float* y, int8_t* q, float* d, int32_t* sum, void* stream);
+
 /* ---- Decoder ---------------------------------------------------------------
  * Replaces the KV-cached `decoder::Decoder` (reference src/decoder.rs:36-321)
  * for S decode streams stepping in lockstep on the device.  A stream decodes

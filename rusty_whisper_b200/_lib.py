@@ -74,6 +74,7 @@ SIGNATURES = {
     "rwq_encoder_encode": (_I, [_P, _P, _L, _P]),
     "rwq_attention_dev": (_I, [_P, _P, _P, _L, _L, _L, _L, _P, _P]),
     "rwq_conv1d_dev": (_I, [_P, _L, _L, _L, _P, _L, _P, _I, _P, _P]),
+    "rwq_layer_norm_dev": (_I, [_P, _P, _P, _P, _P, _L, _L, _P, _P, _P, _P, _P]),
     "rwq_decoder_new": (_I, [_I, _I, _I, _I, _I, ctypes.POINTER(_P)]),
     "rwq_decoder_free": (_I, [_P]),
     "rwq_decoder_set_dense": (_I, [_P, ctypes.c_char_p, _P, _L]),

@@ -21,6 +21,7 @@
 #include <cuda_runtime.h>
 #include <cmath>
 #include <cstdarg>
+#include <cstdint>
 #include <cstdio>
 #include <cstring>
 #include <map>
@@ -487,6 +488,42 @@ int rwq_attention_dev(const float* q, const float* k, const float* v, int64_t n_
         ENC_CUDA(rwq::launch_to_heads(k, D, 0, W, T, H, 1.0f, kh, s), "k heads");
         ENC_CUDA(rwq::launch_to_heads(v, D, 0, W, T, H, 1.0f, vh, s), "v heads");
         ENC_CUDA(rwq::launch_attention(qh, kh, vh, W, T, H, out, s), "attention");
+        return int(RWQ_OK);
+    });
+}
+
+int rwq_layer_norm_dev(const float* x, const float* add, float* x_out, const float* weight, const float* bias,
+                       int64_t m, int64_t k, float* y, int8_t* q, float* d, int32_t* sum, void* stream) {
+    if (m < 0 || k <= 0 || k % 128 || k > 2048) return efail(RWQ_ERR_ARG, "bad shape (k %% 128 == 0, k <= 2048)");
+    if (m > INT32_MAX / k) return efail(RWQ_ERR_ARG, "too many rows");
+    if (m == 0) return RWQ_OK;
+    if (!x || !weight || !bias || (add && !x_out)) return efail(RWQ_ERR_ARG, "null pointer");
+    if (!y && !q) return efail(RWQ_ERR_ARG, "no output (y and q both NULL)");
+    if (q && (!d || !sum)) return efail(RWQ_ERR_ARG, "q, d and sum go together");
+    if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(add) | reinterpret_cast<uintptr_t>(x_out) |
+         reinterpret_cast<uintptr_t>(y) | reinterpret_cast<uintptr_t>(weight) | reinterpret_cast<uintptr_t>(bias)) &
+        15)
+        return efail(RWQ_ERR_ARG, "layer_norm operands must be 16-byte aligned");
+    if (reinterpret_cast<uintptr_t>(q) & 3) return efail(RWQ_ERR_ARG, "q must be 4-byte aligned");
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const int mode = add ? rwq::RQ_ADD_LN : rwq::RQ_LN;
+    const int M = int(m), K = int(k);
+    if (!q) {
+        ENC_CUDA(rwq::launch_rows_quant_v(mode, x, add, x_out, weight, bias, M, K, nullptr, nullptr, y, s),
+                 "layer_norm");
+        return RWQ_OK;
+    }
+    return rwq::with_stream_scratch(s, size_t(m) * (k / 32) * 4, [&](void* buf) {
+        rwq::ActsView v;
+        v.m = M;
+        v.k = K;
+        v.nb = K / 32;
+        v.m_pad = M;
+        v.q8 = q;
+        v.d = d;
+        v.sum = sum;
+        v.u = static_cast<float*>(buf);
+        ENC_CUDA(rwq::launch_rows_quant_v(mode, x, add, x_out, weight, bias, M, K, nullptr, &v, y, s), "layer_norm");
         return int(RWQ_OK);
     });
 }

@@ -210,6 +210,106 @@ __global__ void __launch_bounds__(256) k_rows_quant(const float* x, const float*
     }
 }
 
+// The LayerNorm modes of k_rows_quant with one warp per row, for encoder-
+// sized batches: each lane holds all the row's chunks (c = 0 .. nch-1, at
+// most NV), so a warp has NV loads in flight and needs no CTA barrier.  The
+// statistics are added in exactly k_rows_quant's order -- per lane the
+// chunks c = w, w + RQ_WPR, ... for each of the RQ_WPR chunk classes w, one
+// xor tree per class, then the classes in order -- so both kernels give the
+// same bits and the choice between them depends on the row count only.
+template <int MODE, int NV>
+__global__ void __launch_bounds__(128) k_ln_rows_warp(const float* x, const float* __restrict__ add, float* xout,
+                                                      const float* __restrict__ lw, const float* __restrict__ lb,
+                                                      int m, int k, QOut o, float* __restrict__ yout) {
+    static_assert(MODE == RQ_LN || MODE == RQ_ADD_LN, "LayerNorm modes only");
+    constexpr bool PRE = NV <= 4;   // LayerNorm weights held in registers across the wait
+    const int lane = threadIdx.x & 31;
+    const int nb = k / QK, nch = k / 128;
+    const int row = int((size_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5);
+    float4 lwv[PRE ? NV : 1], lbv[PRE ? NV : 1];
+    if constexpr (PRE) {
+#pragma unroll
+        for (int c = 0; c < NV; ++c)
+            if (c < nch) {
+                lwv[c] = __ldg(reinterpret_cast<const float4*>(lw + c * 128 + lane * 4));
+                lbv[c] = __ldg(reinterpret_cast<const float4*>(lb + c * 128 + lane * 4));
+            }
+    }
+    pdl_trigger();
+    pdl_wait();
+    const int rows = o.q16 ? o.m_pad : m;
+    if (row >= rows) return;
+    if (row >= m) {
+        for (int bl = lane; bl < nb; bl += 32) {
+            o.dT[size_t(bl) * o.m_pad + row] = 0.f;
+            o.uT[size_t(bl) * o.m_pad + row] = 0.f;
+        }
+        return;
+    }
+    const float4* xr = reinterpret_cast<const float4*>(x + size_t(row) * k);
+    float4 v[NV];
+#pragma unroll
+    for (int c = 0; c < NV; ++c)
+        if (c < nch) v[c] = xr[c * 32 + lane];
+    if (MODE == RQ_ADD_LN) {
+        const float4* ar = reinterpret_cast<const float4*>(add + size_t(row) * k);
+        float4* xo = reinterpret_cast<float4*>(xout + size_t(row) * k);
+#pragma unroll
+        for (int c = 0; c < NV; ++c)
+            if (c < nch) {
+                const float4 a = __ldg(ar + c * 32 + lane);
+                v[c] = make_float4(__fadd_rn(v[c].x, a.x), __fadd_rn(v[c].y, a.y), __fadd_rn(v[c].z, a.z),
+                                   __fadd_rn(v[c].w, a.w));
+                xo[c * 32 + lane] = v[c];
+            }
+    }
+    // Sum of one chunk class w over this lane, then over the warp.
+    auto class_sum = [&](int w, auto term) {
+        float s = 0.f;
+#pragma unroll
+        for (int c = 0; c < NV; ++c)
+            if (c % RQ_WPR == w && c < nch) s += term(v[c]);
+#pragma unroll
+        for (int o2 = 16; o2 > 0; o2 >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o2);
+        return s;
+    };
+    auto plain = [](float4 a) { return (a.x + a.y) + (a.z + a.w); };
+    float tot = class_sum(0, plain);
+#pragma unroll
+    for (int w = 1; w < RQ_WPR; ++w) tot = __fadd_rn(tot, class_sum(w, plain));
+    const float mean = __fdiv_rn(tot, float(k));
+    auto sq = [mean](float4 a) {
+        const float p = __fsub_rn(a.x, mean), q = __fsub_rn(a.y, mean), r = __fsub_rn(a.z, mean),
+                    t = __fsub_rn(a.w, mean);
+        return (__fmul_rn(p, p) + __fmul_rn(q, q)) + (__fmul_rn(r, r) + __fmul_rn(t, t));
+    };
+    float qt = class_sum(0, sq);
+#pragma unroll
+    for (int w = 1; w < RQ_WPR; ++w) qt = __fadd_rn(qt, class_sum(w, sq));
+    const float var = __fdiv_rn(qt, float(k));
+    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, 1e-5f)));
+#pragma unroll
+    for (int c = 0; c < NV; ++c)
+        if (c < nch) {
+            float4 w, b;
+            if constexpr (PRE) {
+                w = lwv[c];
+                b = lbv[c];
+            } else {
+                w = __ldg(reinterpret_cast<const float4*>(lw + c * 128 + lane * 4));
+                b = __ldg(reinterpret_cast<const float4*>(lb + c * 128 + lane * 4));
+            }
+            auto f = [&](float xv, float wv, float bv) {
+                return __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(xv, mean), inv), wv), bv);
+            };
+            const float4 y = make_float4(f(v[c].x, w.x, b.x), f(v[c].y, w.y, b.y), f(v[c].z, w.z, b.z),
+                                         f(v[c].w, w.w, b.w));
+            const int e = c * 128 + lane * 4;
+            if (o.q16 || o.q8) quant_block4(y, row, k, e, o);
+            if (yout) *reinterpret_cast<float4*>(yout + size_t(row) * k + e) = y;
+        }
+}
+
 // im2col for a kernel-3, pad-1 conv over windows: out row (w, t) holds
 // in(w, ic, t*stride + j - 1) at column ic*3 + j (zero outside [0, t_in)).
 // in(w, ic, t) = in[w*sw + ic*sc + t*st].
@@ -481,7 +581,7 @@ cudaError_t rows_quant_mode(const float* x, const float* add, float* xout, const
                             int k, const QOut& o, float* yout, cudaStream_t s) {
     const int rows = o.q16 ? o.m_pad : m;
     const int nch = k / 128;
-    if (MODE == RQ_PLAIN || MODE == RQ_GELU) {
+    if constexpr (MODE == RQ_PLAIN || MODE == RQ_GELU) {
         // One chunk per warp for decoder-sized batches (latency), four for
         // encoder-sized ones; the result does not depend on the split.
         const int slice = size_t(rows) * nch >= size_t(1) << 16 ? 4 : 1;
@@ -489,16 +589,32 @@ cudaError_t rows_quant_mode(const float* x, const float* add, float* xout, const
         const unsigned grid = unsigned((size_t(rows) * wpr * 32 + 255) / 256);
         return launch_pdl(k_rows_quant<MODE, 1>, dim3(grid), dim3(256), 0, s, x, add, xout, lw, lb, m, k, o, yout,
                           slice);
+    } else {
+        // Encoder-sized batches: one warp per row (k_ln_rows_warp); the result
+        // is the same bits as the RQ_WPR-warp kernel's.
+        if (rows >= 2048 && nch <= 16) {
+            const unsigned grid = unsigned((size_t(rows) * 32 + 127) / 128);
+            if (nch <= 4)
+                return launch_pdl(k_ln_rows_warp<MODE, 4>, dim3(grid), dim3(128), 0, s, x, add, xout, lw, lb, m, k, o,
+                                  yout);
+            if (nch <= 8)
+                return launch_pdl(k_ln_rows_warp<MODE, 8>, dim3(grid), dim3(128), 0, s, x, add, xout, lw, lb, m, k, o,
+                                  yout);
+            if (nch <= 12)
+                return launch_pdl(k_ln_rows_warp<MODE, 12>, dim3(grid), dim3(128), 0, s, x, add, xout, lw, lb, m, k, o,
+                                  yout);
+            return launch_pdl(k_ln_rows_warp<MODE, 16>, dim3(grid), dim3(128), 0, s, x, add, xout, lw, lb, m, k, o, yout);
+        }
+        // Decoder-sized batches: one row (RQ_WPR warps) per CTA, to spread
+        // the few rows over the SMs.
+        const int tpb = RQ_WPR * 32;
+        const unsigned grid = unsigned((size_t(rows) * RQ_WPR * 32 + tpb - 1) / tpb);
+        if (nch <= RQ_WPR * 2)
+            return launch_pdl(k_rows_quant<MODE, 2>, dim3(grid), dim3(tpb), 0, s, x, add, xout, lw, lb, m, k, o, yout, 1);
+        if (nch <= RQ_WPR * 4)
+            return launch_pdl(k_rows_quant<MODE, 4>, dim3(grid), dim3(tpb), 0, s, x, add, xout, lw, lb, m, k, o, yout, 1);
+        return cudaErrorInvalidValue;
     }
-    // One row per CTA for decoder-sized batches (twice the CTAs to spread
-    // over the SMs), two for encoder-sized ones; the result is the same.
-    const int tpb = rows < 2048 ? RQ_WPR * 32 : 2 * RQ_WPR * 32;
-    const unsigned grid = unsigned((size_t(rows) * RQ_WPR * 32 + tpb - 1) / tpb);
-    if (nch <= RQ_WPR * 2)
-        return launch_pdl(k_rows_quant<MODE, 2>, dim3(grid), dim3(tpb), 0, s, x, add, xout, lw, lb, m, k, o, yout, 1);
-    if (nch <= RQ_WPR * 4)
-        return launch_pdl(k_rows_quant<MODE, 4>, dim3(grid), dim3(tpb), 0, s, x, add, xout, lw, lb, m, k, o, yout, 1);
-    return cudaErrorInvalidValue;
 }
 
 }  // namespace

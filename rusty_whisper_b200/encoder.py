@@ -93,6 +93,39 @@ def multi_head_attention(q, k, v, n_head: int):
     return out[0] if squeeze else out
 
 
+def layer_norm(x, w, b, add=None, quantize: bool = False, want_y: bool = True):
+    """tensor.rs:274-289 LayerNorm (eps 1e-5) over the rows of CUDA f32
+    x [m, k] (k % 128 == 0), as the encoder and decoder run it: with
+    ``add``, x is first replaced in place by x + add (the residual stream);
+    with ``quantize`` the rows are also quantized by quant.rs:690-716.
+    Returns ``y`` ([m, k] f32, None when not ``want_y``) and, with
+    ``quantize``, ``(y, (q, d, sum))``."""
+    torch = _torch()
+    if not (isinstance(x, torch.Tensor) and x.is_cuda and x.dtype == torch.float32 and x.dim() == 2
+            and x.is_contiguous()):
+        raise TypeError("layer_norm takes a contiguous 2-D CUDA float32 tensor")
+    m, k = x.shape
+    w, b = (t.contiguous() for t in (w, b))
+    if add is not None:
+        add = add.contiguous()
+        if add.shape != x.shape:
+            raise ValueError("add must have x's shape")
+    out = torch.empty_like(x) if want_y else None
+    q = d = s = None
+    if quantize:
+        q = torch.empty((m, k), dtype=torch.int8, device=x.device)
+        d = torch.empty((m, k // 32), dtype=torch.float32, device=x.device)
+        s = torch.empty((m, k // 32), dtype=torch.int32, device=x.device)
+    def p(t):
+        return _ptr(t) if t is not None else None
+
+    with torch.cuda.device(x.device):
+        _lib.check(_lib.lib().rwq_layer_norm_dev(_ptr(x), p(add), _ptr(x) if add is not None else None, _ptr(w),
+                                                 _ptr(b), m, k, p(out), p(q), p(d), p(s),
+                                                 ctypes.c_void_p(_stream_ptr(x.device))))
+    return (out, (q, d, s)) if quantize else out
+
+
 def conv1d(x, w, b, stride: int):
     """tensor.rs:335-370 conv1d (kernel 3, padding 1) on the tensor cores:
     x CUDA f32 [n_win, in_ch, t] (or [in_ch, t]), w [out_ch, in_ch, 3], b

@@ -73,6 +73,79 @@ def test_conv1d_matches_reference(torch_mod, w, in_ch, t, out_ch, stride):
         assert (err / np.maximum(np.abs(ref), 1.0)).max() < 1e-3
 
 
+def _ln_inputs(m, k, seed):
+    from rusty_whisper_b200 import synth
+    x = synth.normal(seed, m * k, 0.3, 1.5).reshape(m, k)
+    add = synth.normal(seed + 1, m * k, -0.1, 0.7).reshape(m, k)
+    w = synth.normal(seed + 2, k, 1.0, 0.02)
+    b = synth.normal(seed + 3, k, 0.0, 0.02)
+    return x, add, w, b
+
+
+@pytest.mark.parametrize("m,k", [(1, 512), (37, 384), (2500, 512), (2048, 1280), (3000, 2048), (4099, 128)])
+def test_layer_norm_matches_reference(torch_mod, m, k):
+    """The encoder's row transform (residual add + LayerNorm, tensor.rs:
+    274-289, + the int8 quantizer, quant.rs:690-716) against the oracle:
+    x + add bit-exact (one f32 add), the LayerNorm within 1e-5 of each
+    row's scale (the row sums are added in another order), and the codes,
+    scales and sums bit-exact against the oracle quantizer run on the
+    kernel's own LayerNorm rows.  m >= 2048 runs the one-warp-per-row
+    kernel, smaller m the four-warp one."""
+    import oracle
+    from rusty_whisper_b200 import encoder
+    x, add, w, b = _ln_inputs(m, k, 40 + m + k)
+    dx, da, dw, db = (torch_mod.from_numpy(a).cuda() for a in (x, add, w, b))
+    y, (q, d, s) = encoder.layer_norm(dx, dw, db, add=da, quantize=True)
+    xs = x + add
+    assert np.array_equal(dx.cpu().numpy(), xs)
+    got = y.cpu().numpy()
+    ref = oracle.layernorm(xs, w, b)
+    err = np.abs(got.astype(np.float64) - ref).max(axis=1)
+    assert np.all(err <= 1e-5 * np.abs(ref).max(axis=1)), err.max()
+    rq, rd, rs = oracle.quantize_acts_i8(got)
+    assert np.array_equal(q.cpu().numpy(), rq)
+    assert np.array_equal(d.cpu().numpy(), rd)
+    assert np.array_equal(s.cpu().numpy(), rs)
+    y2 = encoder.layer_norm(torch_mod.from_numpy(xs).cuda(), dw, db)   # no add, no codes
+    assert np.array_equal(y2.cpu().numpy(), got)
+
+
+@pytest.mark.parametrize("k", [384, 512, 1280, 2048])
+def test_layer_norm_rows_independent_of_batch(torch_mod, k):
+    """A row's LayerNorm and codes are the same bits alone in a small batch
+    (four warps per row) and inside an encoder-sized one (one warp per row):
+    the decoder's stream-count invariance and the encoder's batch
+    composition rest on it."""
+    from rusty_whisper_b200 import encoder
+    x, _, w, b = _ln_inputs(3000, k, 7 + k)
+    dw, db = torch_mod.from_numpy(w).cuda(), torch_mod.from_numpy(b).cuda()
+    big_y, big_q = encoder.layer_norm(torch_mod.from_numpy(x).cuda(), dw, db, quantize=True)
+    for r0, r1 in [(0, 1), (5, 300), (2990, 3000)]:
+        y, q = encoder.layer_norm(torch_mod.from_numpy(np.ascontiguousarray(x[r0:r1])).cuda(), dw, db,
+                                  quantize=True)
+        assert np.array_equal(y.cpu().numpy(), big_y[r0:r1].cpu().numpy()), (k, r0)
+        for a, c in zip(q, big_q):
+            assert np.array_equal(a.cpu().numpy(), c[r0:r1].cpu().numpy()), (k, r0)
+
+
+def test_layer_norm_errors(torch_mod):
+    from rusty_whisper_b200 import encoder
+    x = torch_mod.zeros((4, 100), device="cuda")
+    w = torch_mod.ones(100, device="cuda")
+    with pytest.raises(ValueError):
+        encoder.layer_norm(x, w, w)                          # k % 128 != 0
+    x = torch_mod.zeros((4, 128), device="cuda")
+    w = torch_mod.ones(128, device="cuda")
+    with pytest.raises(ValueError):
+        encoder.layer_norm(x, w, w, want_y=False)            # no output
+    with pytest.raises(ValueError):
+        encoder.layer_norm(x, w, w, add=torch_mod.zeros((3, 128), device="cuda"))
+    with pytest.raises(TypeError):
+        encoder.layer_norm(x.double(), w, w)
+    y = encoder.layer_norm(torch_mod.zeros((0, 128), device="cuda"), w, w)
+    assert y.shape == (0, 128)
+
+
 def _encoder_pair(dtype, n_ctx=100, n_state=256, n_head=4, n_layer=2, n_mels=80, seed=5):
     import oracle
     from rusty_whisper_b200 import encoder, synth
