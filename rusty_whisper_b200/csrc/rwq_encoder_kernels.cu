@@ -373,6 +373,13 @@ __device__ __forceinline__ void mma16816(float (&c)[4], const uint32_t (&a)[4], 
                  : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
                  : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
+// 2^x by the MUFU.EX2 unit (PTX ex2.approx.ftz.f32: relative error about
+// 2^-22, below the f16 rounding of the probabilities that use it; 2^-inf = 0).
+__device__ __forceinline__ float ex2_approx(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
 __device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
     const __half2 h = __floats2half2_rn(lo, hi);
     return *reinterpret_cast<const uint32_t*>(&h);
@@ -452,39 +459,49 @@ __global__ void __launch_bounds__(AT_THREADS, 4) k_attn(const __half* __restrict
                 mma16816(s[2 * np + 1], qf[kk], b[2], b[3]);
             }
         }
-        // mask keys past T, then the online softmax (log2 domain)
+        // mask keys past T (last tile only), then the online softmax:
+        // p = 2^(s*log2e - m*log2e), one FFMA and one MUFU.EX2 per score
         const int kbase = j * AT_K;
+        if (kbase + AT_K > T) {
+#pragma unroll
+            for (int nt = 0; nt < 8; ++nt)
+#pragma unroll
+                for (int e = 0; e < 4; ++e)
+                    if (kbase + nt * 8 + tig * 2 + (e & 1) >= T) s[nt][e] = -INFINITY;
+        }
         float mx[2] = {mrow[0], mrow[1]};
 #pragma unroll
         for (int nt = 0; nt < 8; ++nt) {
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const int key = kbase + nt * 8 + tig * 2 + (e & 1);
-                float v = key < T ? s[nt][e] * L2E : -INFINITY;
-                s[nt][e] = v;
-                mx[e >> 1] = fmaxf(mx[e >> 1], v);
-            }
+            for (int e = 0; e < 4; ++e) mx[e >> 1] = fmaxf(mx[e >> 1], s[nt][e]);
         }
 #pragma unroll
         for (int r = 0; r < 2; ++r) {
             mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 1));
             mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 2));
         }
-        float alpha[2];
+        float alpha[2], nmx[2];
 #pragma unroll
         for (int r = 0; r < 2; ++r) {
-            alpha[r] = exp2f(mrow[r] - mx[r]);
+            alpha[r] = ex2_approx(__fmul_rn(__fsub_rn(mrow[r], mx[r]), L2E));
+            nmx[r] = -__fmul_rn(mx[r], L2E);
             mrow[r] = mx[r];
             lrow[r] *= alpha[r];
+        }
+        // Once the row maxima settle alpha is 1 and the rescale a no-op.
+        if (__any_sync(0xffffffffu, alpha[0] != 1.f || alpha[1] != 1.f)) {
+#pragma unroll
+            for (int nt = 0; nt < 8; ++nt)
+#pragma unroll
+                for (int e = 0; e < 4; ++e) o[nt][e] *= alpha[e >> 1];
         }
 #pragma unroll
         for (int nt = 0; nt < 8; ++nt) {
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
-                const float p = exp2f(s[nt][e] - mx[e >> 1]);
+                const float p = ex2_approx(fmaf(s[nt][e], L2E, nmx[e >> 1]));
                 s[nt][e] = p;
                 lrow[e >> 1] += p;
-                o[nt][e] *= alpha[e >> 1];
             }
         }
         // O += P V
