@@ -10,6 +10,7 @@
 //     with f32 accumulation and an online softmax, so the [T, T] score
 //     matrix never leaves the SM.
 #include <cuda_fp16.h>
+#include <atomic>
 #include <cstdint>
 #include "rwq_common.cuh"
 #include "rwq_encoder.h"
@@ -346,10 +347,11 @@ __global__ void k_to_heads(const float* __restrict__ src, int ld, int col0, int 
 
 // ------------------------------------------------------------ attention
 // Flash-style attention, head dim 64.  CTA: 4 warps x 16 query rows; K/V
-// tiles of 64 keys double-buffered in shared memory by cp.async; f16
+// tiles of 64 keys in a three-stage cp.async ring in shared memory; f16
 // m16n8k16 MMAs with f32 accumulators; 128-byte rows swizzled by 16-byte
 // chunk (chunk ^ (row & 7)) so ldmatrix is conflict-free.
-constexpr int AT_Q = 64, AT_K = 64, AT_D = 64, AT_THREADS = 128;
+constexpr int AT_Q = 64, AT_K = 64, AT_D = 64, AT_THREADS = 128, AT_STAGES = 3;
+constexpr int AT_SMEM = AT_Q * 128 + AT_STAGES * 2 * AT_K * 128;   // 56 KB: four CTAs per SM
 
 __device__ __forceinline__ uint32_t swz(int row, int chunk) { return uint32_t(row * 128 + ((chunk ^ (row & 7)) << 4)); }
 
@@ -393,18 +395,16 @@ __global__ void __launch_bounds__(AT_THREADS, 4) k_attn(const __half* __restrict
                                                      const __half* __restrict__ Vh, int T, int H,
                                                      float* __restrict__ out, QOut qo) {
     pdl_trigger();
-    __shared__ __align__(128) uint8_t sQ[AT_Q * 128];
-    __shared__ __align__(128) uint8_t sK[2][AT_K * 128];
-    __shared__ __align__(128) uint8_t sV[2][AT_K * 128];
+    extern __shared__ __align__(128) uint8_t at_smem[];   // Q tile, then AT_STAGES x (K tile, V tile)
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, g = lane >> 2, tig = lane & 3;
     const int w = blockIdx.z, h = blockIdx.y, q0 = blockIdx.x * AT_Q;
     const size_t head = (size_t(w) * H + h) * size_t(T) * AT_D;
     const __half* Qb = Qh + head;
     const __half* Kb = Kh + head;
     const __half* Vb = Vh + head;
-    const uint32_t sQa = uint32_t(__cvta_generic_to_shared(sQ));
-    const uint32_t sKa[2] = {uint32_t(__cvta_generic_to_shared(sK[0])), uint32_t(__cvta_generic_to_shared(sK[1]))};
-    const uint32_t sVa[2] = {uint32_t(__cvta_generic_to_shared(sV[0])), uint32_t(__cvta_generic_to_shared(sV[1]))};
+    const uint32_t sQa = uint32_t(__cvta_generic_to_shared(at_smem));
+    auto sKa = [sQa](int st) { return sQa + uint32_t(AT_Q * 128 + st * 2 * AT_K * 128); };
+    auto sVa = [sQa](int st) { return sQa + uint32_t(AT_Q * 128 + st * 2 * AT_K * 128 + AT_K * 128); };
 
     auto load_tile = [&](const __half* base, int r0, uint32_t dst) {
 #pragma unroll
@@ -415,12 +415,19 @@ __global__ void __launch_bounds__(AT_THREADS, 4) k_attn(const __half* __restrict
         }
     };
     pdl_wait();
-    load_tile(Qb, q0, sQa);
-    load_tile(Kb, 0, sKa[0]);
-    load_tile(Vb, 0, sVa[0]);
-    asm volatile("cp.async.commit_group;" ::: "memory");
-
     const int nkv = (T + AT_K - 1) / AT_K;
+    // cp.async group g holds K/V tile g (group 0 the Q tile too); tiles
+    // 0 .. AT_STAGES-2 are in flight before the loop.
+    load_tile(Qb, q0, sQa);
+#pragma unroll
+    for (int t = 0; t < AT_STAGES - 1; ++t) {
+        if (t < nkv) {
+            load_tile(Kb, t * AT_K, sKa(t));
+            load_tile(Vb, t * AT_K, sVa(t));
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    }
+
     float o[8][4];
 #pragma unroll
     for (int i = 0; i < 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
@@ -429,14 +436,20 @@ __global__ void __launch_bounds__(AT_THREADS, 4) k_attn(const __half* __restrict
     const float L2E = 1.4426950408889634f;
 
     for (int j = 0; j < nkv; ++j) {
-        const int st = j & 1;
-        if (j + 1 < nkv) {
-            load_tile(Kb, (j + 1) * AT_K, sKa[st ^ 1]);
-            load_tile(Vb, (j + 1) * AT_K, sVa[st ^ 1]);
-        }
-        asm volatile("cp.async.commit_group;" ::: "memory");
-        asm volatile("cp.async.wait_group 1;" ::: "memory");
+        // Tile j has landed (at most AT_STAGES-2 younger groups pending);
+        // after the barrier every warp is done with tile j-1, whose stage
+        // the load of tile j + AT_STAGES - 1 reuses: one barrier per tile.
+        const int st = j % AT_STAGES;
+        asm volatile("cp.async.wait_group %0;" ::"n"(AT_STAGES - 2) : "memory");
         __syncthreads();
+        {
+            const int jn = j + AT_STAGES - 1;
+            if (jn < nkv) {
+                load_tile(Kb, jn * AT_K, sKa(jn % AT_STAGES));
+                load_tile(Vb, jn * AT_K, sVa(jn % AT_STAGES));
+            }
+            asm volatile("cp.async.commit_group;" ::: "memory");
+        }
         if (j == 0) {
 #pragma unroll
             for (int kk = 0; kk < 4; ++kk) {
@@ -454,7 +467,7 @@ __global__ void __launch_bounds__(AT_THREADS, 4) k_attn(const __half* __restrict
             for (int np = 0; np < 4; ++np) {
                 uint32_t b[4];
                 const int mi = lane >> 3, key = np * 16 + (lane & 7) + (mi >> 1) * 8, ch = kk * 2 + (mi & 1);
-                ldm_x4(sKa[st] + swz(key, ch), b);
+                ldm_x4(sKa(st) + swz(key, ch), b);
                 mma16816(s[2 * np], qf[kk], b[0], b[1]);
                 mma16816(s[2 * np + 1], qf[kk], b[2], b[3]);
             }
@@ -469,11 +482,18 @@ __global__ void __launch_bounds__(AT_THREADS, 4) k_attn(const __half* __restrict
                 for (int e = 0; e < 4; ++e)
                     if (kbase + nt * 8 + tig * 2 + (e & 1) >= T) s[nt][e] = -INFINITY;
         }
-        float mx[2] = {mrow[0], mrow[1]};
+        // row maxima and sums as trees (short dependency chains)
+        float mx[2];
 #pragma unroll
-        for (int nt = 0; nt < 8; ++nt) {
+        for (int r = 0; r < 2; ++r) {
+            float t[8];
 #pragma unroll
-            for (int e = 0; e < 4; ++e) mx[e >> 1] = fmaxf(mx[e >> 1], s[nt][e]);
+            for (int nt = 0; nt < 8; ++nt) t[nt] = fmaxf(s[nt][2 * r], s[nt][2 * r + 1]);
+#pragma unroll
+            for (int w2 = 4; w2 > 0; w2 >>= 1)
+#pragma unroll
+                for (int i = 0; i < w2; ++i) t[i] = fmaxf(t[i], t[i + w2]);
+            mx[r] = fmaxf(mrow[r], t[0]);
         }
 #pragma unroll
         for (int r = 0; r < 2; ++r) {
@@ -496,13 +516,19 @@ __global__ void __launch_bounds__(AT_THREADS, 4) k_attn(const __half* __restrict
                 for (int e = 0; e < 4; ++e) o[nt][e] *= alpha[e >> 1];
         }
 #pragma unroll
-        for (int nt = 0; nt < 8; ++nt) {
+        for (int nt = 0; nt < 8; ++nt)
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const float p = ex2_approx(fmaf(s[nt][e], L2E, nmx[e >> 1]));
-                s[nt][e] = p;
-                lrow[e >> 1] += p;
-            }
+            for (int e = 0; e < 4; ++e) s[nt][e] = ex2_approx(fmaf(s[nt][e], L2E, nmx[e >> 1]));
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+            float t[8];
+#pragma unroll
+            for (int nt = 0; nt < 8; ++nt) t[nt] = s[nt][2 * r] + s[nt][2 * r + 1];
+#pragma unroll
+            for (int w2 = 4; w2 > 0; w2 >>= 1)
+#pragma unroll
+                for (int i = 0; i < w2; ++i) t[i] += t[i + w2];
+            lrow[r] += t[0];
         }
         // O += P V
 #pragma unroll
@@ -516,12 +542,11 @@ __global__ void __launch_bounds__(AT_THREADS, 4) k_attn(const __half* __restrict
             for (int np = 0; np < 4; ++np) {
                 uint32_t b[4];
                 const int mi = lane >> 3, key = kk * 16 + (lane & 7) + (mi & 1) * 8, ch = np * 2 + (mi >> 1);
-                ldm_x4_t(sVa[st] + swz(key, ch), b);
+                ldm_x4_t(sVa(st) + swz(key, ch), b);
                 mma16816(o[2 * np], a, b[0], b[1]);
                 mma16816(o[2 * np + 1], a, b[2], b[3]);
             }
         }
-        __syncthreads();
     }
     asm volatile("cp.async.wait_group 0;" ::: "memory");
 #pragma unroll
@@ -690,6 +715,23 @@ cudaError_t launch_to_heads(const float* src, int ld, int col0, int n_win, int T
     return cudaGetLastError();
 }
 
+// The dynamic shared-memory limit of k_attn<QOUT> (variant v), raised once
+// per device, with the whole carveout as shared memory (four 57 KB CTAs).
+cudaError_t attn_smem_attr(void (*kern)(const __half*, const __half*, const __half*, int, int, float*, QOut), int v) {
+    static std::atomic<uint64_t> done{0};
+    int dev = 0;
+    if (const cudaError_t e = cudaGetDevice(&dev)) return e;
+    const uint64_t bit = uint64_t(1) << ((dev & 31) * 2 + v);
+    if (done.load(std::memory_order_acquire) & bit) return cudaSuccess;
+    if (const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, AT_SMEM))
+        return e;
+    if (const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                                   int(cudaSharedmemCarveoutMaxShared)))
+        return e;
+    done.fetch_or(bit, std::memory_order_acq_rel);
+    return cudaSuccess;
+}
+
 cudaError_t launch_attention(const __half* Qh, const __half* Kh, const __half* Vh, int n_win, int T, int H,
                              float* out, cudaStream_t s, uint16_t* q16, float* dT, float* uT, int m_pad) {
     if (!n_win || !T || !H) return cudaSuccess;
@@ -700,9 +742,11 @@ cudaError_t launch_attention(const __half* Qh, const __half* Kh, const __half* V
         qo.dT = dT;
         qo.uT = uT;
         qo.m_pad = m_pad;
-        return launch_pdl(k_attn<true>, grid, dim3(AT_THREADS), 0, s, Qh, Kh, Vh, T, H, out, qo);
+        if (const cudaError_t e = attn_smem_attr(k_attn<true>, 0)) return e;
+        return launch_pdl(k_attn<true>, grid, dim3(AT_THREADS), size_t(AT_SMEM), s, Qh, Kh, Vh, T, H, out, qo);
     }
-    return launch_pdl(k_attn<false>, grid, dim3(AT_THREADS), 0, s, Qh, Kh, Vh, T, H, out, qo);
+    if (const cudaError_t e = attn_smem_attr(k_attn<false>, 1)) return e;
+    return launch_pdl(k_attn<false>, grid, dim3(AT_THREADS), size_t(AT_SMEM), s, Qh, Kh, Vh, T, H, out, qo);
 }
 
 }  // namespace rwq
