@@ -391,8 +391,10 @@ def run_encoder(args, dev, tc_peak, stream, rank, world):
            "kernels": "k_rows_quant, k_gemm_fold_w (Q/K/V writing f16 heads, fc1 with GELU + quantize in its "
                       "epilogue), k_gemm_fold, k_attn (its output rows quantized in the kernel); "
                       "conv stem: k_im2col_split + k_gemm_hl (f16 hi|lo "
-                      "tensor cores) + k_bias_gelu",
-           "gpu_launches_per_batch": 4 + 6 * 8 + 1,   # Q/K/V write heads; attention, fc1 quantize their outputs
+                      "tensor cores, bias + GELU (+ positions) in its epilogue)",
+           # stem 2 x (im2col, GEMM); per block 6 GEMMs (Q/K/V write heads, fc1
+           # quantizes its output), attention, 2 LayerNorms; ln_post
+           "gpu_launches_per_batch": 4 + 6 * 9 + 1,
            "data": "synthetic (seeded): random-init weights N(0, 0.02) quantized to Q5_1, mel N(-0.5, 0.3)"}
     if rank == 0 and world == 1 and not args.no_cpu:
         import oracle

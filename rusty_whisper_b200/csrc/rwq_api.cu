@@ -411,12 +411,12 @@ int rwq::linear_acts(const ActsView& v, bool gemm, rwq_qtensor* w, const float* 
 int rwq::gemm_path() { return pick_path(GEMV_FAMILY_MAX_M + 1, 0); }
 
 int rwq::gemm_hl(const uint16_t* ahl, const float* rowscale, int m, const uint16_t* bhl, const float* colscale, int n,
-                 int nb, const float* bias, float* out, cudaStream_t s) {
+                 int nb, const float* bias, float* out, cudaStream_t s, const HlEpilogue* epi) {
     Workspace* ws = nullptr;
     int rc = get_workspace(s, &ws);
     if (rc) return rc;
     char why[256] = {0};
-    cudaError_t e = launch_gemm_hl(ahl, rowscale, m, bhl, colscale, n, nb, bias, out, ws->err, s, why, sizeof why);
+    cudaError_t e = launch_gemm_hl(ahl, rowscale, m, bhl, colscale, n, nb, bias, out, ws->err, s, why, sizeof why, epi);
     if (e != cudaSuccess) return fail(RWQ_ERR_CUDA, "gemm launch: %s %s", cudaGetErrorString(e), why);
     return RWQ_OK;
 }

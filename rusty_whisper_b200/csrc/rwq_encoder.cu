@@ -9,7 +9,7 @@
 //               is an im2col GEMM on the tensor cores with both operands
 //               split into f16 hi + lo (k_im2col_split, k_gemm_hl: about
 //               22 significant bits per operand, the accuracy of f32 for
-//               these sums) + bias/GELU (+ positions) epilogue kernel;
+//               these sums), bias/GELU (+ positions) in the GEMM epilogue;
 //   per block   [residual add +] LayerNorm + int8 quantize (one kernel)
 //               -> Q, K, V GEMMs sharing the quantized activations
 //               -> f16 heads -> flash attention -> quantize -> out GEMM
@@ -220,20 +220,23 @@ int encode_batch(rwq_encoder* e, const Bufs& b, const float* mel, int nwin, floa
     const int M = nwin * T, M2 = 2 * M, m_pad = b.acts.m_pad, k1 = conv1_kp(e);
     auto W = [&](const std::string& n) { return e->dense[n]; };
     ENC_RC(ensure_stem(e, s));
-    // conv1 (stride 1) + GELU: [2T][n_mels*3] x [D][n_mels*3]^T per window
+    // conv1 (stride 1) + bias + GELU in the GEMM's epilogue:
+    // [2T][n_mels*3] x [D][n_mels*3]^T per window
     ENC_CUDA(rwq::launch_im2col_split(mel, nwin, NM, 2 * T, 2 * T, 1, size_t(NM) * 2 * T, size_t(2 * T), 1, k1, b.a1,
                                       b.rs1, s),
              "im2col conv1");
-    ENC_RC(rwq::gemm_hl(b.a1, b.rs1, M2, e->conv1_hl, e->conv1_cs, D, k1 / rwq::QK, nullptr, b.c1, s));
-    ENC_CUDA(rwq::launch_bias_gelu(b.c1, size_t(M2), D, W("encoder.conv1.bias"), nullptr, 1, s), "conv1 gelu");
-    // conv2 (stride 2) + GELU + positions, written time-major: x [M][D]
+    rwq::HlEpilogue epi;
+    epi.gelu = true;
+    ENC_RC(rwq::gemm_hl(b.a1, b.rs1, M2, e->conv1_hl, e->conv1_cs, D, k1 / rwq::QK, W("encoder.conv1.bias"), b.c1, s,
+                        &epi));
+    // conv2 (stride 2) + bias + GELU + positions, written time-major: x [M][D]
     ENC_CUDA(rwq::launch_im2col_split(b.c1, nwin, D, 2 * T, T, 2, size_t(2 * T) * D, 1, size_t(D), 3 * D, b.a2, b.rs2,
                                       s),
              "im2col conv2");
-    ENC_RC(rwq::gemm_hl(b.a2, b.rs2, M, e->conv2_hl, e->conv2_cs, D, 3 * D / rwq::QK, nullptr, b.x, s));
-    ENC_CUDA(rwq::launch_bias_gelu(b.x, size_t(M), D, W("encoder.conv2.bias"), W("encoder.positional_embedding"), T,
-                                   s),
-             "conv2 gelu");
+    epi.pos = W("encoder.positional_embedding");
+    epi.pos_period = T;
+    ENC_RC(rwq::gemm_hl(b.a2, b.rs2, M, e->conv2_hl, e->conv2_cs, D, 3 * D / rwq::QK, W("encoder.conv2.bias"), b.x, s,
+                        &epi));
     const rwq::ActsView aD = acts_for(b, D), aF = acts_for(b, F);
     // fc2's operand in b.h's memory (f16 codes [M][F], then d_a and
     // d_a*sum(q_a) [F/32][m_pad]): the fused fc1 writes it while its own

@@ -24,8 +24,6 @@ cudaError_t launch_rows_quant(int mode, const float* x, const float* add, float*
 cudaError_t launch_rows_quant_v(int mode, const float* x, const float* add, float* xout, const float* lw,
                                 const float* lb, int m, int k, const ActsView* gemm, const ActsView* gemv,
                                 float* yout, cudaStream_t s);
-cudaError_t launch_bias_gelu(float* y, size_t rows, int cols, const float* bias, const float* pos, int t_per_win,
-                             cudaStream_t s);
 cudaError_t launch_to_heads(const float* src, int ld, int col0, int n_win, int T, int H, float scale, __half* dst,
                             cudaStream_t s);
 // With q16 set, the output rows go quantized into that GEMM-layout operand
@@ -63,7 +61,7 @@ int linear_acts(const ActsView& v, bool gemm, rwq_qtensor* w, const float* bias,
 // launch_im2col_split for A, launch_split_dense for a dense B), with this
 // stream's fault flag.  Returns an RWQ_* status.
 int gemm_hl(const uint16_t* ahl, const float* rowscale, int m, const uint16_t* bhl, const float* colscale, int n,
-            int nb, const float* bias, float* out, cudaStream_t s);
+            int nb, const float* bias, float* out, cudaStream_t s, const HlEpilogue* epi = nullptr);
 
 // The GEMM kernel path that GEMM-sized matmuls take on this host thread
 // (2 folded-scale, 3 exact-integer, 4 hi|lo; rwq_set_gemm_path), which

@@ -4,7 +4,6 @@
 //     (tensor.rs:274-289) or tanh-GELU (tensor.rs:291-306), then the int8
 //     activation quantizer (quant.rs:690-716) writing the tensor-core
 //     GEMM's operand directly (f16 codes + transposed block scales);
-//   * the conv stem's bias/GELU/position epilogue (its GEMMs are k_gemm_hl);
 //   * k_to_heads + k_attn: non-causal multi-head attention
 //     (encoder.rs:48-80) as a flash-style kernel on f16 tensor-core MMAs
 //     with f32 accumulation and an online softmax, so the [T, T] score
@@ -314,18 +313,6 @@ __global__ void __launch_bounds__(128) k_ln_rows_warp(const float* x, const floa
 // im2col for a kernel-3, pad-1 conv over windows: out row (w, t) holds
 // in(w, ic, t*stride + j - 1) at column ic*3 + j (zero outside [0, t_in)).
 // in(w, ic, t) = in[w*sw + ic*sc + t*st].
-// y[r][c] = gelu(y[r][c] + bias[c]) (+ pos[(r % t_per_win)][c] if pos).
-__global__ void k_bias_gelu(float* __restrict__ y, size_t rows, int cols, const float* __restrict__ bias,
-                            const float* __restrict__ pos, int t_per_win) {
-    const size_t total = rows * size_t(cols);
-    for (size_t i = size_t(blockIdx.x) * blockDim.x + threadIdx.x; i < total; i += size_t(gridDim.x) * blockDim.x) {
-        const int c = int(i % cols);
-        float v = gelu_ref(__fadd_rn(y[i], bias[c]));
-        if (pos) v = __fadd_rn(v, pos[size_t((i / cols) % t_per_win) * cols + c]);
-        y[i] = v;
-    }
-}
-
 // f32 [n_win*T][ld] (head h = columns col0 + h*64 ..) -> f16 [n_win][H][T][64],
 // multiplied by `scale` (a power of two: exact).
 __global__ void k_to_heads(const float* __restrict__ src, int ld, int col0, int n_win, int T, int H, float scale,
@@ -697,14 +684,6 @@ cudaError_t launch_rows_quant_v(int mode, const float* x, const float* add, floa
         case RQ_ADD_LN: return rows_quant_mode<RQ_ADD_LN>(x, add, xout, lw, lb, m, k, o, yout, s);
         default: return cudaErrorInvalidValue;
     }
-}
-
-cudaError_t launch_bias_gelu(float* y, size_t rows, int cols, const float* bias, const float* pos, int t_per_win,
-                             cudaStream_t s) {
-    const size_t total = rows * size_t(cols);
-    if (!total) return cudaSuccess;
-    k_bias_gelu<<<grid_stride(total, 256), 256, 0, s>>>(y, rows, cols, bias, pos, t_per_win);
-    return cudaGetLastError();
 }
 
 cudaError_t launch_to_heads(const float* src, int ld, int col0, int n_win, int T, int H, float scale, __half* dst,

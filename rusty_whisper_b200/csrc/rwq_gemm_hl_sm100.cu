@@ -124,7 +124,8 @@ __global__ void __launch_bounds__(HL_THREADS, 1)
     k_gemm_hl(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
               const __grid_constant__ CUtensorMap tmY, const float* __restrict__ rowscale,
               const float* __restrict__ colscale, const float* __restrict__ bias, float* __restrict__ Y, int M, int N,
-              int nb, int kps, int S, int store_mode, int* __restrict__ err_flag) {
+              int nb, int kps, int S, int store_mode, int* __restrict__ err_flag, int gelu,
+              const float* __restrict__ epos, int epos_period) {
     using F = Hl<BN>;
     constexpr int STAGES = F::STAGES, STAGE_BYTES = F::STAGE_BYTES, PITCH = F::PITCH, CPW = F::CPW;
     constexpr uint32_t IDESC = F::IDESC;
@@ -276,6 +277,27 @@ __global__ void __launch_bounds__(HL_THREADS, 1)
                         float t = __fmul_rn(__fmul_rn(v[e], bar->cs[cc]), rs);
                         v[e] = bias ? __fadd_rn(t, bar->bs[cc]) : t;
                     }
+                    if (gelu) {
+#pragma unroll
+                        for (int e = 0; e < 32; ++e) v[e] = gelu_ref(v[e]);
+                    }
+                    if (epos && m0 + row < M && n0 + cb * 32 + 32 <= N) {   // rows of N floats, N % 4 == 0
+                        const float4* pr = reinterpret_cast<const float4*>(
+                            epos + size_t((m0 + row) % epos_period) * N + n0 + cb * 32);
+#pragma unroll
+                        for (int k4 = 0; k4 < 8; ++k4) {
+                            const float4 pv = __ldg(pr + k4);
+                            v[4 * k4] = __fadd_rn(v[4 * k4], pv.x);
+                            v[4 * k4 + 1] = __fadd_rn(v[4 * k4 + 1], pv.y);
+                            v[4 * k4 + 2] = __fadd_rn(v[4 * k4 + 2], pv.z);
+                            v[4 * k4 + 3] = __fadd_rn(v[4 * k4 + 3], pv.w);
+                        }
+                    } else if (epos && m0 + row < M) {
+#pragma unroll
+                        for (int e = 0; e < 32; ++e)
+                            if (n0 + cb * 32 + e < N)
+                                v[e] = __fadd_rn(v[e], epos[size_t((m0 + row) % epos_period) * N + n0 + cb * 32 + e]);
+                    }
                     if (store_mode == HL_STORE_TMA) {
                         uint8_t* box = base + (q * (BN / 32) + cb) * 4096 + lane * 128;
 #pragma unroll
@@ -359,6 +381,14 @@ __global__ void __launch_bounds__(HL_THREADS, 1)
                     v.y = __fadd_rn(v.y, bs.y);
                     v.z = __fadd_rn(v.z, bs.z);
                     v.w = __fadd_rn(v.w, bs.w);
+                }
+                if (gelu) v = make_float4(gelu_ref(v.x), gelu_ref(v.y), gelu_ref(v.z), gelu_ref(v.w));
+                if (epos) {
+                    const float* pr = epos + size_t(gi % epos_period) * N + gj;
+                    v.x = __fadd_rn(v.x, pr[0]);
+                    if (gj + 1 < N) v.y = __fadd_rn(v.y, pr[1]);
+                    if (gj + 2 < N) v.z = __fadd_rn(v.z, pr[2]);
+                    if (gj + 3 < N) v.w = __fadd_rn(v.w, pr[3]);
                 }
                 float* yr = Y + size_t(gi) * N + gj;
                 if (store_mode != HL_STORE_SCALAR) {   // N % 4 == 0 and Y 16-byte aligned: gj + 3 < N
@@ -730,7 +760,7 @@ HlCfg hl_choose(int dev, int m, int n, int nb) {
 template <int BN>
 cudaError_t launch_hl_bn(const uint16_t* ahl, const float* rowscale, int m, const uint16_t* bhl,
                          const float* colscale, int n, int nb, const float* bias, float* y, int* err_flag, int S,
-                         cudaStream_t s, char* why, size_t why_len) {
+                         cudaStream_t s, char* why, size_t why_len, const HlEpilogue& epi) {
     const int dev = cur_dev();
     cudaError_t e = ensure_smem_attr<BN>(dev);
     if (e != cudaSuccess) return e;
@@ -748,9 +778,9 @@ cudaError_t launch_hl_bn(const uint16_t* ahl, const float* rowscale, int m, cons
     dim3 grid(unsigned(nt * S), unsigned(mt));
     if (S == 1)
         return launch_pdl(k_gemm_hl<BN>, grid, dim3(HL_THREADS), Hl<BN>::SMEM, s, ma, mb, my, rowscale, colscale, bias,
-                          y, m, n, nb, kps, S, mode, err_flag);
+                          y, m, n, nb, kps, S, mode, err_flag, int(epi.gelu), epi.pos, epi.pos_period);
     return launch_pdl_cluster(k_gemm_hl<BN>, grid, dim3(HL_THREADS), Hl<BN>::SMEM, S, s, ma, mb, my, rowscale, colscale,
-                              bias, y, m, n, nb, kps, S, mode, err_flag);
+                              bias, y, m, n, nb, kps, S, mode, err_flag, int(epi.gelu), epi.pos, epi.pos_period);
 }
 
 }  // namespace
@@ -786,14 +816,17 @@ void set_gemm_hl_ksplit(int S) { t_ksplit_override = (S >= 1 && S <= 4) ? S : 0;
 
 cudaError_t launch_gemm_hl(const uint16_t* ahl, const float* rowscale, int m, const uint16_t* bhl,
                            const float* colscale, int n, int nb, const float* bias, float* y, int* err_flag,
-                           cudaStream_t s, char* why, size_t why_len) {
+                           cudaStream_t s, char* why, size_t why_len, const HlEpilogue* epi) {
     if (m <= 0 || n <= 0) return cudaSuccess;
+    const HlEpilogue none;
+    const HlEpilogue& ep = epi ? *epi : none;
+    if (ep.pos && ep.pos_period <= 0) return cudaErrorInvalidValue;
     HlCfg c = hl_choose(cur_dev(), m, n, nb);
     if (t_ksplit_override > 0) c.S = t_ksplit_override;
     switch (c.bn) {
-        case 256: return launch_hl_bn<256>(ahl, rowscale, m, bhl, colscale, n, nb, bias, y, err_flag, c.S, s, why, why_len);
-        case 128: return launch_hl_bn<128>(ahl, rowscale, m, bhl, colscale, n, nb, bias, y, err_flag, c.S, s, why, why_len);
-        default: return launch_hl_bn<64>(ahl, rowscale, m, bhl, colscale, n, nb, bias, y, err_flag, c.S, s, why, why_len);
+        case 256: return launch_hl_bn<256>(ahl, rowscale, m, bhl, colscale, n, nb, bias, y, err_flag, c.S, s, why, why_len, ep);
+        case 128: return launch_hl_bn<128>(ahl, rowscale, m, bhl, colscale, n, nb, bias, y, err_flag, c.S, s, why, why_len, ep);
+        default: return launch_hl_bn<64>(ahl, rowscale, m, bhl, colscale, n, nb, bias, y, err_flag, c.S, s, why, why_len, ep);
     }
 }
 

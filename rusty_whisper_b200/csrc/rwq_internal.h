@@ -132,11 +132,19 @@ cudaError_t launch_split_dense(const float* w, int n, int k, int kv, int ldw, in
 // input element (w, c, t) at in[w*sw + c*sc + t*st].
 cudaError_t launch_im2col_split(const float* in, int n_win, int c_in, int t_in, int t_out, int stride, size_t sw,
                                 size_t sc, size_t st, int kp, uint16_t* ahl, float* rowscale, cudaStream_t s);
+// Optional element-wise tail of k_gemm_hl's epilogue, after the bias:
+// y = gelu(y) (tanh form) and then y += pos[(row % pos_period)][col] (pos
+// has n columns) -- the conv stem's bias/GELU/position step.
+struct HlEpilogue {
+    bool gelu = false;
+    const float* pos = nullptr;
+    int pos_period = 1;
+};
 // y[m][n] = (A'*2^e_i)(B*2^e_j)^T * 2^-e_i * 2^-e_j (+ bias) on tcgen05 with
 // both operands split into f16 hi + lo, the whole K accumulated in TMEM.
 cudaError_t launch_gemm_hl(const uint16_t* ahl, const float* rowscale, int m, const uint16_t* bhl,
                            const float* colscale, int n, int nb, const float* bias, float* y, int* err_flag,
-                           cudaStream_t s, char* why, size_t why_len);
+                           cudaStream_t s, char* why, size_t why_len, const HlEpilogue* epi = nullptr);
 // The K split (1, 2 or 4 CTAs per output tile) k_gemm_hl picks for an
 // m x n GEMM of nb blocks on the current device.
 int gemm_hl_ksplit(int m, int n, int nb);
