@@ -628,7 +628,9 @@ def run_profile_driver(args):
     copies) at --m rows, --steps back-to-back launches; `gemv` -- the same
     for config 5's decoder projection (Q4_0 1280 x 1280, eight copies);
     `decode` -- the config-4 decoder (80 streams; config 5's with --m 32..256 windows),
-    begin then --steps greedy steps."""
+    begin then --steps greedy steps; `attention` -- --steps calls of the
+    encoder's attention (rwq_attention_dev) at config 3's shape, 8 windows
+    x 1500 frames x 8 heads of 64."""
     import torch
     from rusty_whisper_b200 import quant
     quant.init(0)
@@ -661,6 +663,21 @@ def run_profile_driver(args):
         torch.cuda.synchronize()
         us_per_launch = e0.elapsed_time(e1) * 1e3 / max(args.steps, 1)
         del gr
+    elif args.only == "attention":
+        from rusty_whisper_b200 import encoder
+        nw, t_ctx, d, heads = 8, 1500, 512, 8
+        q, k, v = (torch.from_numpy(synth.normal(40 + i, nw * t_ctx * d).reshape(nw, t_ctx, d)).to(dev)
+                   for i in range(3))
+        encoder.multi_head_attention(q, k, v, heads)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            encoder.multi_head_attention(q, k, v, heads)
+        e1.record()
+        torch.cuda.synchronize()
+        us_per_call = e0.elapsed_time(e1) * 1e3 / max(args.steps, 1)
+        attn_flop = 4.0 * nw * heads * t_ctx * t_ctx * 64
     else:
         from rusty_whisper_b200 import decoder
         if args.m in (32, 64, 128, 256):   # config 5's decoder: large-v3 shape, Q4_0, m windows (256 / ranks)
@@ -687,6 +704,8 @@ def run_profile_driver(args):
     line = {"profile_driver": args.only, "m": args.m, "steps": args.steps}
     if args.only in ("logits", "gemv"):
         line.update(us_per_launch=round(us_per_launch, 2), tops=round(2 * args.m * n * k / us_per_launch / 1e6, 1))
+    if args.only == "attention":   # a call: three f16 head conversions + k_attn
+        line.update(us_per_call=round(us_per_call, 1), tflops=round(attn_flop / us_per_call / 1e6, 1))
     print(json.dumps(line), flush=True)
 
 
@@ -998,11 +1017,12 @@ def main():
                     help="--only logits: activation rows; --only decode: 32, 64, 128 or 256 select config 5's "
                          "decoder with that many windows (one rank's share at 8, 4, 2, 1 GPUs)")
     ap.add_argument("--only", default="all", choices=["all", "gemm", "encoder", "decoder", "large", "logits", "gemv", "decode",
-                                                      "beam"],
+                                                      "beam", "attention"],
                     help="gemm: only the config-2 GEMM sweep; encoder / decoder / large: only that leg; "
                          "logits: --steps launches of config 4's tied-logits GEMV at --m rows; decode: --steps "
                          "config-4 decode steps, graphs off when RWQ_DECODER_GRAPHS=0 (short runs for profiling); "
-                         "beam: the same as config 4's beam-5 steps (top-k, ranking, fork)")
+                         "beam: the same as config 4's beam-5 steps (top-k, ranking, fork); attention: --steps "
+                         "calls of the encoder attention at config 3's shape")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", 1))
@@ -1019,7 +1039,7 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local_rank))
     try:
-        if args.only in ("logits", "gemv", "decode", "beam"):
+        if args.only in ("logits", "gemv", "decode", "beam", "attention"):
             run_profile_driver(args)
             return
         if args.only in ("encoder", "decoder", "large"):

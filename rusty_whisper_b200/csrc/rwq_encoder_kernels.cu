@@ -222,19 +222,9 @@ __global__ void __launch_bounds__(128) k_ln_rows_warp(const float* x, const floa
                                                       const float* __restrict__ lw, const float* __restrict__ lb,
                                                       int m, int k, QOut o, float* __restrict__ yout) {
     static_assert(MODE == RQ_LN || MODE == RQ_ADD_LN, "LayerNorm modes only");
-    constexpr bool PRE = NV <= 4;   // LayerNorm weights held in registers across the wait
     const int lane = threadIdx.x & 31;
     const int nb = k / QK, nch = k / 128;
     const int row = int((size_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5);
-    float4 lwv[PRE ? NV : 1], lbv[PRE ? NV : 1];
-    if constexpr (PRE) {
-#pragma unroll
-        for (int c = 0; c < NV; ++c)
-            if (c < nch) {
-                lwv[c] = __ldg(reinterpret_cast<const float4*>(lw + c * 128 + lane * 4));
-                lbv[c] = __ldg(reinterpret_cast<const float4*>(lb + c * 128 + lane * 4));
-            }
-    }
     pdl_trigger();
     pdl_wait();
     const int rows = o.q16 ? o.m_pad : m;
@@ -291,14 +281,11 @@ __global__ void __launch_bounds__(128) k_ln_rows_warp(const float* x, const floa
 #pragma unroll
     for (int c = 0; c < NV; ++c)
         if (c < nch) {
-            float4 w, b;
-            if constexpr (PRE) {
-                w = lwv[c];
-                b = lbv[c];
-            } else {
-                w = __ldg(reinterpret_cast<const float4*>(lw + c * 128 + lane * 4));
-                b = __ldg(reinterpret_cast<const float4*>(lb + c * 128 + lane * 4));
-            }
+            // LayerNorm weights read here (L1 hits after the first rows):
+            // holding them across the wait cost 30 registers and a third of
+            // the resident warps
+            const float4 w = __ldg(reinterpret_cast<const float4*>(lw + c * 128 + lane * 4));
+            const float4 b = __ldg(reinterpret_cast<const float4*>(lb + c * 128 + lane * 4));
             auto f = [&](float xv, float wv, float bv) {
                 return __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(xv, mean), inv), wv), bv);
             };
